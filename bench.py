@@ -1,0 +1,184 @@
+"""Headline benchmark: decode tok/s + p50 TTFT of the Qwen3-235B-A22B-shaped 4-bit MoE
+(94 layers, hidden 4096, 64/4 heads x 128, 128 experts top-8, expert FFN 1536, vocab
+151936), batch 32, prompt 1024, on N B200s, synthetic uniform-random prompts and
+random-init N(0, 0.02) weights quantised to 4-bit blocks.
+
+    python bench.py [--gpus N --steps K --warmup W]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (N > 1)
+    python bench.py --impl reference                       (reference arm)
+
+`value` is whole-job decode tokens/s, device-timed with CUDA events around the decode
+steps (max over ranks); `e2e` is the same metric through the public engine API
+(LLMEngine.step), including the per-step host->device step-descriptor copy and the
+device->host read of the sampled tokens.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s + p50 TTFT, Qwen3-235B-A22B-shape 4-bit, 1/2/4/8 B200, max over ranks"
+
+
+def reference_arm(args):
+    # The reference is a Rust workspace with no Python package, no GPU kernels and no
+    # end-to-end forward; it cannot be installed or run here.
+    print(json.dumps({"impl": "reference", "unavailable":
+                      "reference is a pre-alpha Rust workspace (no GPU kernels, no end-to-end forward, no cargo "
+                      "toolchain on the box); pip install of /root/reference fails: no setup.py/pyproject.toml"}))
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit())
+        mx = max(float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[3 + i].lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="syntropy", choices=["syntropy", "reference"])
+    ap.add_argument("--model", default="qwen3-235b-a22b")
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--prompt", type=int, default=1024)
+    ap.add_argument("--decode", type=int, default=256)
+    ap.add_argument("--layers", type=int, default=0, help="dev only: override layer count (invalid headline)")
+    ap.add_argument("--seed", type=int, default=0)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    import torch
+
+    from syntropy_b200.models.config import get_config
+    from syntropy_b200.models.transformer import prepare_weights
+    from syntropy_b200.runtime.engine import LLMEngine, SamplingParams
+    from syntropy_b200.runtime.runner import ModelRunner
+    from syntropy_b200 import ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    if world > 1:
+        raise SystemExit("multi-GPU bench path not built yet")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cfg = get_config(args.model)
+    if args.layers:
+        cfg = cfg.replace(n_layers=args.layers)
+    t0 = time.time()
+    mw = prepare_weights(cfg, dev, seed=args.seed, max_pos=args.prompt + args.decode + 16)
+    torch.cuda.synchronize()
+    t_weights = time.time() - t0
+    B = args.batch
+    max_len = args.prompt + args.decode
+    runner = ModelRunner(mw, max_batch=B, max_seq_len=max_len + 16)
+    eng = LLMEngine(runner, max_prefill_tokens=8192)
+    g = torch.Generator().manual_seed(1234 + rank)
+    prompts = [torch.randint(0, cfg.vocab, (args.prompt,), generator=g).tolist() for _ in range(B)]
+    # ---- prefill: TTFT of each request (all submitted at t0) ----
+    total_steps = args.warmup + args.steps
+    assert total_steps + 1 <= args.decode, "warmup + steps must fit in the decode length"
+    ids = [eng.add_request(p, SamplingParams(max_tokens=args.decode, temperature=0.0)) for p in prompts]
+    t_sub = time.perf_counter()
+    while eng.waiting:
+        eng.step()
+    torch.cuda.synchronize()
+    seqs = {s.seq_id: s for s in eng.running}
+    ttft = sorted(seqs[i].t_first_token - t_sub for i in ids)
+    p50_ttft_ms = 1e3 * ttft[len(ttft) // 2]
+    # ---- decode: warm-up then timed steps ----
+    for _ in range(args.warmup):
+        eng.step()
+    torch.cuda.synchronize()
+    # launch count of one decode step (eager count of the captured sequence)
+    n_launch = ops.count_launches(lambda: runner.decode_forward(B)) if hasattr(ops, "count_launches") else None
+    # timed decode steps through the engine: device time = sum of CUDA-event-bracketed
+    # graph replays; e2e = wall time of the same steps (descriptor H2D + tokens D2H)
+    runner.time_events = []
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        te = time.perf_counter()
+        for _ in range(args.steps):
+            eng.step()
+        torch.cuda.synchronize()
+        e2e_s = time.perf_counter() - te
+    dev_ms = sum(a.elapsed_time(b) for a, b in runner.time_events)
+    assert len(runner.time_events) == args.steps
+    ms_step = dev_ms / args.steps
+    value = B * 1e3 / ms_step
+    e2e_value = B * args.steps / e2e_s
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16 activations, 4-bit block weights (32-elem, fp16 scale+min)",
+        "data": "synthetic uniform-random prompts, random-init N(0,0.02) weights quantised to 4-bit",
+        "p50_ttft_ms": round(p50_ttft_ms, 2),
+        "config": {"model": args.model if not args.layers else f"{args.model}[layers={args.layers}] (DEV, not headline)",
+                   "global_batch": B, "seq_len": args.prompt, "decode_len": args.decode,
+                   "parallelism": f"ep{world}" if world > 1 else "single-gpu",
+                   "expert_cache_frac": 1.0, "l2": "inputs larger than L2 (weights 140+ GB streamed per step)",
+                   "weights_gb": round(mw.nbytes() / 1e9, 2), "weight_build_s": round(t_weights, 1)},
+        "clocks": clk.summary(),
+        "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": runner.desc.nbytes,
+                "d2h_bytes_per_step": 4 * B},
+        "gpu_launches": (n_launch * args.steps) if n_launch else None,
+        "impl": "syntropy",
+    }
+    if rank == 0:
+        print(json.dumps(out))
+
+
+if __name__ == "__main__":
+    main()

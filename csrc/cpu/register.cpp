@@ -1,0 +1,28 @@
+// Registration of every exported function (one place, so the surface is easy to audit).
+#include "ops.h"
+
+namespace syn {
+
+void register_all(pybind11::module& m) {
+  m.def("q4_quantize_rows_cpu", &q4_quantize_rows_cpu);
+  m.def("q4_dequant_rows_cpu", &q4_dequant_rows_cpu);
+  m.def("q4_rows_to_tiled_cpu", &q4_rows_to_tiled_cpu);
+  m.def("q4_quantize", &q4_quantize);
+  m.def("q4_rows_to_tiled", &q4_rows_to_tiled);
+  m.def("q4_tiled_to_rows", &q4_tiled_to_rows);
+  m.def("q4t_dequant", &q4t_dequant);
+  m.def("q4_gemv", &q4_gemv);
+  m.def("rmsnorm", &rmsnorm);
+  m.def("moe_combine_rmsnorm", &moe_combine_rmsnorm);
+  m.def("qk_rope_kv_write", &qk_rope_kv_write);
+  m.def("embed", &embed);
+  m.def("attn_decode", &attn_decode);
+  m.def("router_logits", &router_logits);
+  m.def("moe_topk", &moe_topk);
+  m.def("argmax", &argmax);
+  m.def("sample", &sample);
+  m.def("philox", &philox);
+  m.def("philox_cpu", &philox_cpu);
+}
+
+}  // namespace syn

@@ -1,0 +1,42 @@
+// Declarations of every function exported by syntropy_b200._C.
+#pragma once
+#include <torch/extension.h>
+#include <vector>
+
+namespace syn {
+// q4 format (CPU oracle)
+torch::Tensor q4_quantize_rows_cpu(torch::Tensor w);
+torch::Tensor q4_dequant_rows_cpu(torch::Tensor rows, int64_t N, int64_t K);
+std::vector<torch::Tensor> q4_rows_to_tiled_cpu(torch::Tensor rows, int64_t N, int64_t K);
+// q4 format (device)
+std::vector<torch::Tensor> q4_quantize(torch::Tensor w);
+std::vector<torch::Tensor> q4_rows_to_tiled(torch::Tensor rows, int64_t N, int64_t K);
+torch::Tensor q4_tiled_to_rows(torch::Tensor qw, torch::Tensor sm, int64_t N, int64_t K);
+torch::Tensor q4t_dequant(torch::Tensor qw, torch::Tensor sm, int64_t N, int64_t K);
+void q4_gemv(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
+             torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor res, torch::Tensor out,
+             int64_t N, int64_t K, int64_t mode);
+
+void rmsnorm(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor out);
+void moe_combine_rmsnorm(torch::Tensor x, torch::Tensor yp, torch::Tensor pair_of, torch::Tensor shared,
+                         torch::Tensor w, torch::Tensor out, double eps);
+void qk_rope_kv_write(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t D, torch::Tensor qn, torch::Tensor kn,
+                      double eps, torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t, torch::Tensor slot,
+                      torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache);
+void embed(torch::Tensor table, torch::Tensor ids, torch::Tensor out);
+void attn_decode(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor block_tables,
+                 torch::Tensor ctx_lens, torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor out,
+                 int64_t pages_per_split, double scale);
+void router_logits(torch::Tensor h, torch::Tensor W, torch::Tensor logits);
+void moe_topk(torch::Tensor logits, torch::Tensor bias, int64_t E, int64_t k, int64_t scoring, int64_t n_groups,
+              int64_t topk_groups, bool norm, double scaling, bool pred, torch::Tensor topk_ids, torch::Tensor topk_w,
+              torch::Tensor tok_off, torch::Tensor tok_idx, torch::Tensor pair_w, torch::Tensor pair_of,
+              torch::Tensor pred_mask);
+void argmax(torch::Tensor logits, torch::Tensor out);
+void sample(torch::Tensor logits, torch::Tensor temperature, torch::Tensor top_k, torch::Tensor top_p,
+            torch::Tensor seed, torch::Tensor stream, torch::Tensor counter, torch::Tensor out);
+torch::Tensor philox(int64_t seed, int64_t stream, int64_t counter0, int64_t n, torch::Tensor like);
+torch::Tensor philox_cpu(int64_t seed, int64_t stream, int64_t counter0, int64_t n);
+
+void register_all(pybind11::module& m);
+}  // namespace syn

@@ -1,0 +1,83 @@
+// Raw-pointer launchers for every CUDA kernel.  The .cu files include no torch header
+// (fast builds); csrc/torch_ops*.cpp validate tensors and call these.  Every launcher
+// returns the cudaError_t of its launch.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace syn {
+
+// ---- q4 format ----
+cudaError_t launch_q4_quantize(const void* w, bool is_bf16, int64_t N, int64_t K, uint32_t* qw, void* sm,
+                               cudaStream_t s);
+cudaError_t launch_q4_rows_to_tiled(const uint8_t* rows, int64_t N, int64_t K, uint32_t* qw, void* sm,
+                                    cudaStream_t s);
+cudaError_t launch_q4_tiled_to_rows(const uint32_t* qw, const void* sm, int64_t N, int64_t K, uint8_t* rows,
+                                    cudaStream_t s);
+cudaError_t launch_q4t_dequant(const uint32_t* qw, const void* sm, int64_t N, int64_t K, void* out_bf16,
+                               cudaStream_t s);
+
+// ---- decode GEMV over 4-bit tiled weights ----
+struct GemvArgs {
+  const void* x;               // bf16 [rows, ldx]
+  const int64_t* qw_ptrs;      // [E] device pointers
+  const int64_t* sm_ptrs;      // [E] device pointers
+  const int32_t* tok_off;      // [E+1]
+  const int32_t* tok_idx;      // [P] or nullptr (identity)
+  const float* route_w;        // [P] (mode 2)
+  const void* res;             // bf16 [P, N] (mode 3)
+  void* out;
+  int N, K, ldx;
+  int mode;
+  int E;
+};
+cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s);
+
+// ---- norms, RoPE, KV writes, embedding ----
+cudaError_t launch_rmsnorm(const void* x, bool x_bf16, const float* w, void* y, int T, int H, float eps,
+                           cudaStream_t s);
+cudaError_t launch_moe_combine_rmsnorm(float* x, const float* yp, const int32_t* pair_of, int top_k,
+                                       const float* shared, const float* w, void* y, int T, int H, float eps,
+                                       cudaStream_t s);
+cudaError_t launch_qk_rope_kv_write(const void* qkv, int T, int Hq, int Hkv, int D, const float* qn, const float* kn,
+                                    float eps, const int32_t* pos, const float* cos_t, const float* sin_t,
+                                    const int64_t* slot, void* q_out, void* k_cache, void* v_cache, int block_size,
+                                    cudaStream_t s);
+cudaError_t launch_embed(const void* table, const int32_t* ids, float* out, int T, int H, cudaStream_t s);
+
+// ---- paged decode attention ----
+cudaError_t launch_attn_decode(const void* q, const void* kc, const void* vc, const int32_t* block_tables,
+                               const int32_t* ctx_lens, float* part_o, float* part_ml, void* out, int T, int Hq,
+                               int Hkv, int D, int max_blocks, int pages_per_split, int n_splits, float scale,
+                               cudaStream_t s);
+
+// ---- MoE routing ----
+cudaError_t launch_router_logits(const void* h, const void* W, float* logits, int T, int H, int E_rows,
+                                 cudaStream_t s);
+struct TopkArgs {
+  const float* logits;   // [T, E_rows]
+  const float* bias;     // [E] selection bias (sigmoid routing) or null
+  int T, E, E_rows, k;
+  int scoring;           // 0 softmax, 1 sigmoid
+  int n_groups, topk_groups;
+  int norm;              // renormalise the k weights
+  float scaling;
+  int pred;              // also top-k of logits[:, E:2E] (next-layer prediction)
+  int32_t* topk_ids;     // [T, k]
+  float* topk_w;         // [T, k]
+  int32_t* tok_off;      // [E+1]
+  int32_t* tok_idx;      // [T*k] token of each pair (pairs sorted by expert, then token)
+  float* pair_w;         // [T*k]
+  int32_t* pair_of;      // [T, k] pair index of each choice, choices sorted by expert
+  int32_t* pred_mask;    // [E] 1 if any token is predicted to use expert e at the next layer
+};
+cudaError_t launch_moe_topk(const TopkArgs& a, cudaStream_t s);
+
+// ---- sampling ----
+cudaError_t launch_argmax(const float* logits, int T, int V, int32_t* out, cudaStream_t s);
+cudaError_t launch_sample(const float* logits, int T, int V, const float* temperature, const int32_t* top_k,
+                          const float* top_p, const int64_t* seed, const int64_t* stream, int64_t* counter,
+                          int32_t* out, cudaStream_t s);
+cudaError_t launch_philox(uint64_t seed, uint64_t stream, uint64_t counter0, int n, uint32_t* out, cudaStream_t s);
+
+}  // namespace syn

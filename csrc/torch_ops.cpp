@@ -1,0 +1,287 @@
+// Tensor-level wrappers: validate shapes, dtypes and devices, then call the raw-pointer
+// launchers of syn/launch.h on the current CUDA stream.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "ops.h"
+#include "syn/launch.h"
+
+#define SYN_CHECK_CUDA(expr)                                                              \
+  do {                                                                                    \
+    cudaError_t _e = (expr);                                                              \
+    TORCH_CHECK(_e == cudaSuccess, "CUDA error ", cudaGetErrorString(_e), " at ", __FILE__, \
+                ":", __LINE__);                                                           \
+  } while (0)
+
+#define SYN_CHECK_INPUT(x)                                   \
+  TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor");   \
+  TORCH_CHECK((x).is_contiguous(), #x " must be contiguous")
+
+namespace syn {
+
+static inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream(); }
+
+std::vector<torch::Tensor> q4_quantize(torch::Tensor w) {
+  SYN_CHECK_INPUT(w);
+  TORCH_CHECK(w.dim() == 2, "q4_quantize expects [N, K]");
+  const int64_t N = w.size(0), K = w.size(1);
+  TORCH_CHECK(N % 16 == 0 && K % 64 == 0, "q4 tiled layout needs N%16==0 and K%64==0");
+  TORCH_CHECK(w.scalar_type() == torch::kFloat32 || w.scalar_type() == torch::kBFloat16,
+              "q4_quantize: float32 or bfloat16");
+  const at::cuda::CUDAGuard guard(w.device());
+  auto qw = torch::empty({N * K / 8}, w.options().dtype(torch::kInt32));
+  auto sm = torch::empty({N * K / 16}, w.options().dtype(torch::kFloat16));
+  SYN_CHECK_CUDA(launch_q4_quantize(w.data_ptr(), w.scalar_type() == torch::kBFloat16, N, K,
+                                    reinterpret_cast<uint32_t*>(qw.data_ptr()), sm.data_ptr(), cur_stream()));
+  return {qw, sm};
+}
+
+std::vector<torch::Tensor> q4_rows_to_tiled(torch::Tensor rows, int64_t N, int64_t K) {
+  SYN_CHECK_INPUT(rows);
+  TORCH_CHECK(N % 16 == 0 && K % 64 == 0, "q4 tiled layout needs N%16==0 and K%64==0");
+  TORCH_CHECK(rows.numel() == N * K / 32 * 20, "q4 rows: wrong byte count");
+  const at::cuda::CUDAGuard guard(rows.device());
+  auto qw = torch::empty({N * K / 8}, rows.options().dtype(torch::kInt32));
+  auto sm = torch::empty({N * K / 16}, rows.options().dtype(torch::kFloat16));
+  SYN_CHECK_CUDA(launch_q4_rows_to_tiled(rows.data_ptr<uint8_t>(), N, K, reinterpret_cast<uint32_t*>(qw.data_ptr()),
+                                         sm.data_ptr(), cur_stream()));
+  return {qw, sm};
+}
+
+torch::Tensor q4_tiled_to_rows(torch::Tensor qw, torch::Tensor sm, int64_t N, int64_t K) {
+  SYN_CHECK_INPUT(qw);
+  SYN_CHECK_INPUT(sm);
+  TORCH_CHECK(qw.numel() * 8 == N * K && sm.numel() * 16 == N * K, "q4_tiled_to_rows: sizes");
+  const at::cuda::CUDAGuard guard(qw.device());
+  auto rows = torch::empty({N * K / 32 * 20}, qw.options().dtype(torch::kUInt8));
+  SYN_CHECK_CUDA(launch_q4_tiled_to_rows(reinterpret_cast<const uint32_t*>(qw.data_ptr()), sm.data_ptr(), N, K,
+                                         rows.data_ptr<uint8_t>(), cur_stream()));
+  return rows;
+}
+
+torch::Tensor q4t_dequant(torch::Tensor qw, torch::Tensor sm, int64_t N, int64_t K) {
+  SYN_CHECK_INPUT(qw);
+  SYN_CHECK_INPUT(sm);
+  TORCH_CHECK(qw.numel() * 8 == N * K && sm.numel() * 16 == N * K, "q4t_dequant: sizes");
+  const at::cuda::CUDAGuard guard(qw.device());
+  auto out = torch::empty({N, K}, qw.options().dtype(torch::kBFloat16));
+  SYN_CHECK_CUDA(launch_q4t_dequant(reinterpret_cast<const uint32_t*>(qw.data_ptr()), sm.data_ptr(), N, K,
+                                    out.data_ptr(), cur_stream()));
+  return out;
+}
+
+void q4_gemv(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
+             torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor res, torch::Tensor out, int64_t N,
+             int64_t K, int64_t mode) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16, "x must be cuda bf16");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be [rows, K] with unit inner stride");
+  TORCH_CHECK(N % 16 == 0 && K % 64 == 0, "q4_gemv: N%16, K%64");
+  TORCH_CHECK(x.size(1) == K, "q4_gemv: x width != K");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(x.data_ptr()) & 3) == 0 && x.stride(0) % 2 == 0,
+              "q4_gemv: x rows must be 4-byte aligned");
+  TORCH_CHECK(qw_ptrs.is_cuda() && sm_ptrs.is_cuda() && tok_off.is_cuda(), "index arrays must be on the device");
+  TORCH_CHECK(qw_ptrs.scalar_type() == torch::kInt64 && sm_ptrs.scalar_type() == torch::kInt64, "ptr arrays int64");
+  TORCH_CHECK(tok_off.scalar_type() == torch::kInt32, "tok_off int32");
+  const int E = (int)qw_ptrs.numel();
+  TORCH_CHECK(sm_ptrs.numel() == E && tok_off.numel() == E + 1, "tok_off must have E+1 entries");
+  TORCH_CHECK(out.is_cuda() && out.is_contiguous(), "out must be contiguous cuda");
+  GemvArgs a;
+  a.x = x.data_ptr();
+  a.qw_ptrs = qw_ptrs.data_ptr<int64_t>();
+  a.sm_ptrs = sm_ptrs.data_ptr<int64_t>();
+  a.tok_off = tok_off.data_ptr<int32_t>();
+  a.tok_idx = tok_idx.numel() ? tok_idx.data_ptr<int32_t>() : nullptr;
+  a.route_w = route_w.numel() ? route_w.data_ptr<float>() : nullptr;
+  a.res = res.numel() ? res.data_ptr() : nullptr;
+  a.out = out.data_ptr();
+  a.N = (int)N;
+  a.K = (int)K;
+  a.ldx = (int)x.stride(0);
+  a.mode = (int)mode;
+  a.E = E;
+  if (mode == 0) TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.size(-1) == N, "out bf16 [P, N]");
+  if (mode == 3) TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.size(-1) == N, "out f32 [P, N]");
+  if (mode == 1) TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.size(-1) == N / 2, "out bf16 [P, N/2]");
+  if (mode == 2) TORCH_CHECK(a.route_w && out.scalar_type() == torch::kFloat32 && out.size(-1) == N, "mode 2: route_w, fp32 [P, N]");
+  TORCH_CHECK(mode >= 0 && mode <= 3, "q4_gemv: bad mode");
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_q4_gemv(a, cur_stream()));
+}
+
+
+static inline const float* fptr_or_null(const torch::Tensor& t) {
+  if (!t.defined() || t.numel() == 0) return nullptr;
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == torch::kFloat32 && t.is_contiguous(), "expected contiguous cuda f32");
+  return t.data_ptr<float>();
+}
+
+void rmsnorm(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor out) {
+  SYN_CHECK_INPUT(x);
+  SYN_CHECK_INPUT(out);
+  TORCH_CHECK(x.dim() == 2 && out.sizes() == x.sizes() && out.scalar_type() == torch::kBFloat16, "rmsnorm shapes");
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 || x.scalar_type() == torch::kBFloat16, "rmsnorm x dtype");
+  TORCH_CHECK(w.numel() == x.size(1), "rmsnorm weight size");
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_rmsnorm(x.data_ptr(), x.scalar_type() == torch::kBFloat16, fptr_or_null(w), out.data_ptr(),
+                                (int)x.size(0), (int)x.size(1), (float)eps, cur_stream()));
+}
+
+void moe_combine_rmsnorm(torch::Tensor x, torch::Tensor yp, torch::Tensor pair_of, torch::Tensor shared,
+                         torch::Tensor w, torch::Tensor out, double eps) {
+  SYN_CHECK_INPUT(x);
+  SYN_CHECK_INPUT(yp);
+  SYN_CHECK_INPUT(pair_of);
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 && yp.scalar_type() == torch::kFloat32, "f32 x, yp");
+  TORCH_CHECK(pair_of.scalar_type() == torch::kInt32 && pair_of.dim() == 2 && pair_of.size(0) == x.size(0), "pair_of");
+  TORCH_CHECK(yp.size(-1) == x.size(1), "yp width");
+  const float* wp = fptr_or_null(w);
+  if (wp) TORCH_CHECK(out.is_cuda() && out.scalar_type() == torch::kBFloat16 && out.sizes() == x.sizes(), "out");
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_moe_combine_rmsnorm(x.data_ptr<float>(), yp.data_ptr<float>(), pair_of.data_ptr<int32_t>(),
+                                            (int)pair_of.size(1), fptr_or_null(shared), wp,
+                                            wp ? out.data_ptr() : nullptr, (int)x.size(0), (int)x.size(1),
+                                            (float)eps, cur_stream()));
+}
+
+void qk_rope_kv_write(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t D, torch::Tensor qn, torch::Tensor kn,
+                      double eps, torch::Tensor pos, torch::Tensor cos_t, torch::Tensor sin_t, torch::Tensor slot,
+                      torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache) {
+  SYN_CHECK_INPUT(qkv);
+  SYN_CHECK_INPUT(pos);
+  SYN_CHECK_INPUT(slot);
+  SYN_CHECK_INPUT(q_out);
+  SYN_CHECK_INPUT(k_cache);
+  SYN_CHECK_INPUT(v_cache);
+  TORCH_CHECK(qkv.scalar_type() == torch::kBFloat16 && qkv.size(-1) == (Hq + 2 * Hkv) * D, "qkv shape");
+  const int64_t T = qkv.size(0);
+  TORCH_CHECK(pos.numel() == T && pos.scalar_type() == torch::kInt32, "pos");
+  TORCH_CHECK(slot.numel() == T && slot.scalar_type() == torch::kInt64, "slot");
+  TORCH_CHECK(q_out.numel() == T * Hq * D && q_out.scalar_type() == torch::kBFloat16, "q_out");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(1) == Hkv && k_cache.size(3) == D, "k_cache [nb, Hkv, bs, D]");
+  TORCH_CHECK(cos_t.size(-1) == D / 2 && sin_t.size(-1) == D / 2, "rope table");
+  const at::cuda::CUDAGuard guard(qkv.device());
+  SYN_CHECK_CUDA(launch_qk_rope_kv_write(qkv.data_ptr(), (int)T, (int)Hq, (int)Hkv, (int)D, fptr_or_null(qn),
+                                         fptr_or_null(kn), (float)eps, pos.data_ptr<int32_t>(),
+                                         cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), slot.data_ptr<int64_t>(),
+                                         q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                         (int)k_cache.size(2), cur_stream()));
+}
+
+void embed(torch::Tensor table, torch::Tensor ids, torch::Tensor out) {
+  SYN_CHECK_INPUT(table);
+  SYN_CHECK_INPUT(ids);
+  SYN_CHECK_INPUT(out);
+  TORCH_CHECK(table.scalar_type() == torch::kBFloat16 && ids.scalar_type() == torch::kInt32 &&
+                  out.scalar_type() == torch::kFloat32, "embed dtypes");
+  const at::cuda::CUDAGuard guard(table.device());
+  SYN_CHECK_CUDA(launch_embed(table.data_ptr(), ids.data_ptr<int32_t>(), out.data_ptr<float>(), (int)ids.numel(),
+                              (int)table.size(1), cur_stream()));
+}
+
+void attn_decode(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor block_tables,
+                 torch::Tensor ctx_lens, torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor out,
+                 int64_t pages_per_split, double scale) {
+  SYN_CHECK_INPUT(q);
+  SYN_CHECK_INPUT(kc);
+  SYN_CHECK_INPUT(vc);
+  SYN_CHECK_INPUT(block_tables);
+  SYN_CHECK_INPUT(ctx_lens);
+  SYN_CHECK_INPUT(part_o);
+  SYN_CHECK_INPUT(part_ml);
+  SYN_CHECK_INPUT(out);
+  TORCH_CHECK(q.dim() == 3 && q.scalar_type() == torch::kBFloat16, "q [T, Hq, D] bf16");
+  TORCH_CHECK(kc.dim() == 4 && kc.size(2) == 16 && kc.scalar_type() == torch::kBFloat16, "cache [nb, Hkv, 16, D] bf16");
+  const int64_t T = q.size(0), Hq = q.size(1), D = q.size(2), Hkv = kc.size(1);
+  TORCH_CHECK(block_tables.dim() == 2 && block_tables.size(0) >= T && block_tables.scalar_type() == torch::kInt32, "block_tables");
+  const int64_t max_blocks = block_tables.size(1);
+  const int64_t n_splits = (max_blocks + pages_per_split - 1) / pages_per_split;
+  TORCH_CHECK(part_o.numel() >= T * Hkv * n_splits * 16 * D, "part_o too small");
+  TORCH_CHECK(part_ml.numel() >= T * Hkv * n_splits * 16 * 2, "part_ml too small");
+  TORCH_CHECK(out.numel() == T * Hq * D && out.scalar_type() == torch::kBFloat16, "out");
+  const at::cuda::CUDAGuard guard(q.device());
+  SYN_CHECK_CUDA(launch_attn_decode(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), block_tables.data_ptr<int32_t>(),
+                                    ctx_lens.data_ptr<int32_t>(), part_o.data_ptr<float>(), part_ml.data_ptr<float>(),
+                                    out.data_ptr(), (int)T, (int)Hq, (int)Hkv, (int)D, (int)max_blocks,
+                                    (int)pages_per_split, (int)n_splits, (float)scale, cur_stream()));
+}
+
+void router_logits(torch::Tensor h, torch::Tensor W, torch::Tensor logits) {
+  SYN_CHECK_INPUT(h);
+  SYN_CHECK_INPUT(W);
+  SYN_CHECK_INPUT(logits);
+  TORCH_CHECK(h.scalar_type() == torch::kBFloat16 && W.scalar_type() == torch::kBFloat16, "bf16 h, W");
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.size(0) == h.size(0) && logits.size(1) == W.size(0), "logits");
+  const at::cuda::CUDAGuard guard(h.device());
+  SYN_CHECK_CUDA(launch_router_logits(h.data_ptr(), W.data_ptr(), logits.data_ptr<float>(), (int)h.size(0),
+                                      (int)h.size(1), (int)W.size(0), cur_stream()));
+}
+
+void moe_topk(torch::Tensor logits, torch::Tensor bias, int64_t E, int64_t k, int64_t scoring, int64_t n_groups,
+              int64_t topk_groups, bool norm, double scaling, bool pred, torch::Tensor topk_ids, torch::Tensor topk_w,
+              torch::Tensor tok_off, torch::Tensor tok_idx, torch::Tensor pair_w, torch::Tensor pair_of,
+              torch::Tensor pred_mask) {
+  SYN_CHECK_INPUT(logits);
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32, "logits f32");
+  const int64_t T = logits.size(0);
+  TORCH_CHECK(logits.size(1) == (pred ? 2 * E : E), "logits width");
+  TORCH_CHECK(topk_ids.numel() >= T * k && topk_w.numel() >= T * k && tok_idx.numel() >= T * k &&
+                  pair_w.numel() >= T * k && pair_of.numel() >= T * k && tok_off.numel() >= E + 1, "topk outputs");
+  TopkArgs a;
+  a.logits = logits.data_ptr<float>();
+  a.bias = fptr_or_null(bias);
+  a.T = (int)T;
+  a.E = (int)E;
+  a.E_rows = (int)logits.size(1);
+  a.k = (int)k;
+  a.scoring = (int)scoring;
+  a.n_groups = (int)n_groups;
+  a.topk_groups = (int)topk_groups;
+  a.norm = norm ? 1 : 0;
+  a.scaling = (float)scaling;
+  a.pred = pred ? 1 : 0;
+  a.topk_ids = topk_ids.data_ptr<int32_t>();
+  a.topk_w = topk_w.data_ptr<float>();
+  a.tok_off = tok_off.data_ptr<int32_t>();
+  a.tok_idx = tok_idx.data_ptr<int32_t>();
+  a.pair_w = pair_w.data_ptr<float>();
+  a.pair_of = pair_of.data_ptr<int32_t>();
+  a.pred_mask = pred_mask.numel() ? pred_mask.data_ptr<int32_t>() : nullptr;
+  const at::cuda::CUDAGuard guard(logits.device());
+  SYN_CHECK_CUDA(launch_moe_topk(a, cur_stream()));
+}
+
+void argmax(torch::Tensor logits, torch::Tensor out) {
+  SYN_CHECK_INPUT(logits);
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.dim() == 2, "logits f32 [T, V]");
+  TORCH_CHECK(out.scalar_type() == torch::kInt32 && out.numel() >= logits.size(0), "out int32");
+  const at::cuda::CUDAGuard guard(logits.device());
+  SYN_CHECK_CUDA(launch_argmax(logits.data_ptr<float>(), (int)logits.size(0), (int)logits.size(1),
+                               out.data_ptr<int32_t>(), cur_stream()));
+}
+
+void sample(torch::Tensor logits, torch::Tensor temperature, torch::Tensor top_k, torch::Tensor top_p,
+            torch::Tensor seed, torch::Tensor stream, torch::Tensor counter, torch::Tensor out) {
+  SYN_CHECK_INPUT(logits);
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.dim() == 2, "logits f32 [T, V]");
+  const int64_t T = logits.size(0);
+  TORCH_CHECK(temperature.numel() >= T && top_k.numel() >= T && top_p.numel() >= T && seed.numel() >= T &&
+                  stream.numel() >= T && counter.numel() >= T && out.numel() >= T, "sample params");
+  TORCH_CHECK(seed.scalar_type() == torch::kInt64 && stream.scalar_type() == torch::kInt64 &&
+                  counter.scalar_type() == torch::kInt64, "seed/stream/counter int64");
+  const at::cuda::CUDAGuard guard(logits.device());
+  SYN_CHECK_CUDA(launch_sample(logits.data_ptr<float>(), (int)T, (int)logits.size(1), temperature.data_ptr<float>(),
+                               top_k.data_ptr<int32_t>(), top_p.data_ptr<float>(), seed.data_ptr<int64_t>(),
+                               stream.data_ptr<int64_t>(), counter.data_ptr<int64_t>(), out.data_ptr<int32_t>(),
+                               cur_stream()));
+}
+
+torch::Tensor philox(int64_t seed, int64_t stream, int64_t counter0, int64_t n, torch::Tensor like) {
+  const at::cuda::CUDAGuard guard(like.device());
+  auto out = torch::empty({n}, like.options().dtype(torch::kInt32));
+  SYN_CHECK_CUDA(launch_philox((uint64_t)seed, (uint64_t)stream, (uint64_t)counter0, (int)n,
+                               reinterpret_cast<uint32_t*>(out.data_ptr()), cur_stream()));
+  return out;
+}
+
+}  // namespace syn

@@ -1,0 +1,51 @@
+"""Builds the native extension ``syntropy_b200._C`` in-tree.
+
+One shared object holds the C++ runtime (quantisers, Philox, MoE split rule, rings,
+format parsers, I/O pool, metrics) and every CUDA kernel.  CUDA code is compiled for
+sm_100a only: the ``-gencode`` flag below also stops torch from adding its own arch list.
+
+    python setup.py build_ext --inplace
+"""
+import glob
+import os
+
+from setuptools import setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+
+def _sources():
+    pats = ["csrc/cpu/*.cpp", "csrc/cuda/*.cu", "csrc/*.cpp"]
+    out = []
+    for p in pats:
+        out += sorted(glob.glob(os.path.join(ROOT, p)))
+    return [os.path.relpath(s, ROOT) for s in out]
+
+
+CXX_FLAGS = ["-O3", "-std=c++17", "-fno-strict-aliasing", "-Wno-unused-function"]
+NVCC_FLAGS = [
+    "-O3",
+    "-std=c++17",
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-lineinfo",
+    "--expt-relaxed-constexpr",
+    "-Xptxas", "-v",
+    "-U__CUDA_NO_HALF_OPERATORS__",
+    "-U__CUDA_NO_HALF_CONVERSIONS__",
+    "-U__CUDA_NO_BFLOAT16_CONVERSIONS__",
+    "-U__CUDA_NO_HALF2_OPERATORS__",
+]
+
+setup(
+    name="syntropy_b200",
+    ext_modules=[
+        CUDAExtension(
+            name="syntropy_b200._C",
+            sources=_sources(),
+            include_dirs=[os.path.join(ROOT, "csrc", "include"), os.path.join(ROOT, "csrc")],
+            extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
+        )
+    ],
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)

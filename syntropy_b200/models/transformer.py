@@ -1,0 +1,219 @@
+"""Engine forward for the ``llama`` and ``qwen_moe`` families (GQA attention, dense SwiGLU
+or top-k MoE FFN), over paged KV.
+
+Per-layer decode sequence (each line one kernel on CUDA):
+    qkv   = gemv(h, Wqkv)                         q4 GEMV
+    q     = qk_norm + rope(qkv); k, v -> pages    fused RmsNorm+Rope+KvWrite
+    o     = paged_attention(q, pages)             split-KV decode attention + merge
+    x    += gemv(o, Wo)                           q4 GEMV, f32 residual epilogue
+    h     = rmsnorm(x)
+  dense:  a = swiglu(gemv(h, Wgu)); x += gemv(a, Wd)
+  MoE:    logits = router(h [, next router]); top-k + CSR
+          a  = swiglu(grouped_gemv(h, Wgu[e]))   one weight read per active expert
+          yp = w * grouped_gemv(a, Wd[e])
+          x += sum_j yp (ascending expert);  h = rmsnorm_next(x)   fused combine
+Block structure follows crates/graph/src/blocks/snapshots/{gqa_fused,dense_ffn,moe}.txt.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+
+from .. import ops
+from ..formats.q4 import Q4Weight
+from .config import ModelConfig
+from .reference import rope_table
+from .weights import expert_tensor, make_tensor, layer_shapes
+
+
+@dataclass
+class ExpertBank:
+    """Stacked per-expert matrices [E][N, K].  On CUDA: q4 tiled storage + pointer tables
+    (the pointer of expert e may point into the VRAM bank, a cache slot or host memory)."""
+
+    E: int
+    N: int
+    K: int
+    qw: torch.Tensor | None = None    # int32 [E, N*K/8]
+    sm: torch.Tensor | None = None    # fp16 [E, N*K/16]
+    w: torch.Tensor | None = None     # CPU/dense: [E, N, K]
+    qw_ptrs: torch.Tensor | None = None  # int64 [E] device
+    sm_ptrs: torch.Tensor | None = None
+
+    def weight(self, e: int) -> torch.Tensor:
+        if self.w is not None:
+            return self.w[e]
+        return Q4Weight(self.N, self.K, self.qw[e], self.sm[e]).dequant()
+
+    def build_ptrs(self):
+        if self.qw is None:
+            return
+        dev = self.qw.device
+        qb, sb = self.qw.data_ptr(), self.sm.data_ptr()
+        qs, ss = self.qw.stride(0) * 4, self.sm.stride(0) * 2
+        self.qw_ptrs = torch.tensor([qb + e * qs for e in range(self.E)], dtype=torch.int64, device=dev)
+        self.sm_ptrs = torch.tensor([sb + e * ss for e in range(self.E)], dtype=torch.int64, device=dev)
+
+    @property
+    def expert_nbytes(self) -> int:
+        return self.N * self.K // 32 * 20
+
+
+@dataclass
+class LayerWeights:
+    attn_norm: torch.Tensor
+    ffn_norm: torch.Tensor
+    qkv: object
+    o: object
+    q_norm: torch.Tensor | None = None
+    k_norm: torch.Tensor | None = None
+    gate_up: object = None
+    down: object = None
+    router: torch.Tensor | None = None      # [E, H] (bf16 on CUDA)
+    router_cat: torch.Tensor | None = None  # [2E, H]: this layer's rows then the next layer's
+    router_bias: torch.Tensor | None = None
+    experts_gu: ExpertBank | None = None
+    experts_down: ExpertBank | None = None
+    is_moe: bool = False
+
+
+@dataclass
+class ModelWeights:
+    cfg: ModelConfig
+    device: torch.device
+    embed: torch.Tensor
+    final_norm: torch.Tensor
+    lm_head: object
+    layers: list = field(default_factory=list)
+    rope_cos: torch.Tensor | None = None
+    rope_sin: torch.Tensor | None = None
+
+    def nbytes(self) -> int:
+        tot = 0
+        seen = set()
+
+        def add(t):
+            nonlocal tot
+            if t is None:
+                return
+            if isinstance(t, Q4Weight):
+                tot += t.nbytes
+            elif isinstance(t, ExpertBank):
+                for x in (t.qw, t.sm, t.w):
+                    if x is not None and x.data_ptr() not in seen:
+                        seen.add(x.data_ptr())
+                        tot += x.numel() * x.element_size()
+            elif isinstance(t, torch.Tensor):
+                tot += t.numel() * t.element_size()
+
+        add(self.embed)
+        add(self.lm_head)
+        for L in self.layers:
+            for v in L.__dict__.values():
+                add(v)
+        return tot
+
+
+def _linear_weight(w: torch.Tensor, quant: str, device):
+    if device.type == "cuda":
+        if quant == "q4":
+            return Q4Weight.quantize(w.to(device))
+        return w.to(device=device, dtype=torch.bfloat16)
+    return w.float()
+
+
+def prepare_weights(cfg: ModelConfig, device="cpu", seed: int = 0, quant: str | None = None,
+                    state_dict: dict | None = None, max_pos: int = 8192,
+                    expert_range: tuple[int, int] | None = None, dense_dtype=None) -> ModelWeights:
+    """Builds engine-ready weights from ``state_dict`` (canonical names) or synthetic ones
+    generated directly on ``device``.  ``expert_range`` limits MoE experts to [a, b)
+    (expert parallelism); other experts' pointers are left at zero."""
+    device = torch.device(device)
+    quant = quant or cfg.weight_quant
+    is_cuda = device.type == "cuda"
+    gen_dev = device if is_cuda else "cpu"
+
+    def get(name, shape):
+        if state_dict is not None:
+            return state_dict[name].to(gen_dev).float()
+        return make_tensor(cfg, name, shape, seed=seed, device=gen_dev)
+
+    ea, eb = expert_range if expert_range else (0, cfg.n_experts)
+    shapes_g = {"embed": (cfg.vocab, cfg.hidden), "final_norm": (cfg.hidden,), "lm_head": (cfg.vocab, cfg.hidden)}
+    emb = get("embed", shapes_g["embed"])
+    mw = ModelWeights(
+        cfg=cfg, device=device,
+        embed=emb.to(torch.bfloat16) if is_cuda else emb,
+        final_norm=get("final_norm", shapes_g["final_norm"]).float(),
+        lm_head=_linear_weight(emb if cfg.tie_embeddings else get("lm_head", shapes_g["lm_head"]), quant, device),
+    )
+    del emb
+    for i in range(cfg.n_layers):
+        pre = f"layers.{i}."
+        sh = layer_shapes(cfg, i)
+        qkv = torch.cat([get(pre + "q_proj", sh["q_proj"]), get(pre + "k_proj", sh["k_proj"]),
+                         get(pre + "v_proj", sh["v_proj"])], 0)
+        L = LayerWeights(
+            attn_norm=get(pre + "attn_norm", sh["attn_norm"]).float(),
+            ffn_norm=get(pre + "ffn_norm", sh["ffn_norm"]).float(),
+            qkv=_linear_weight(qkv, quant, device),
+            o=_linear_weight(get(pre + "o_proj", sh["o_proj"]), quant, device),
+        )
+        del qkv
+        if cfg.qk_norm:
+            L.q_norm = get(pre + "q_norm", sh["q_norm"]).float()
+            L.k_norm = get(pre + "k_norm", sh["k_norm"]).float()
+        if cfg.layer_is_moe(i):
+            L.is_moe = True
+            r = get(pre + "router", sh["router"])
+            L.router = r.to(torch.bfloat16) if is_cuda else r
+            E, f, H = cfg.n_experts, cfg.moe_ffn, cfg.hidden
+            gu = ExpertBank(E, 2 * f, H)
+            dn = ExpertBank(E, H, f)
+            if is_cuda and quant == "q4":
+                gu.qw = torch.zeros(E, 2 * f * H // 8, dtype=torch.int32, device=device)
+                gu.sm = torch.zeros(E, 2 * f * H // 16, dtype=torch.float16, device=device)
+                dn.qw = torch.zeros(E, H * f // 8, dtype=torch.int32, device=device)
+                dn.sm = torch.zeros(E, H * f // 16, dtype=torch.float16, device=device)
+                for e in range(ea, eb):
+                    if state_dict is not None:
+                        g = state_dict[pre + "experts.gate"][e].to(gen_dev).float()
+                        u = state_dict[pre + "experts.up"][e].to(gen_dev).float()
+                        d = state_dict[pre + "experts.down"][e].to(gen_dev).float()
+                    else:
+                        g = expert_tensor(cfg, pre + "experts.gate", e, (f, H), seed=seed, device=gen_dev)
+                        u = expert_tensor(cfg, pre + "experts.up", e, (f, H), seed=seed, device=gen_dev)
+                        d = expert_tensor(cfg, pre + "experts.down", e, (H, f), seed=seed, device=gen_dev)
+                    q = Q4Weight.quantize(ops.interleave_gate_up(g, u))
+                    gu.qw[e].copy_(q.qw)
+                    gu.sm[e].copy_(q.sm)
+                    q = Q4Weight.quantize(d)
+                    dn.qw[e].copy_(q.qw)
+                    dn.sm[e].copy_(q.sm)
+                gu.build_ptrs()
+                dn.build_ptrs()
+            else:
+                g = get(pre + "experts.gate", sh["experts.gate"])
+                u = get(pre + "experts.up", sh["experts.up"])
+                gu.w = torch.stack([ops.interleave_gate_up(g[e], u[e]) for e in range(E)])
+                dn.w = get(pre + "experts.down", sh["experts.down"])
+                if is_cuda:
+                    gu.w = gu.w.to(device=device, dtype=torch.bfloat16)
+                    dn.w = dn.w.to(device=device, dtype=torch.bfloat16)
+            L.experts_gu, L.experts_down = gu, dn
+            if "router_bias" in sh:
+                L.router_bias = get(pre + "router_bias", sh["router_bias"]).float()
+        else:
+            gu = ops.interleave_gate_up(get(pre + "gate", sh["gate"]), get(pre + "up", sh["up"]))
+            L.gate_up = _linear_weight(gu, quant, device)
+            L.down = _linear_weight(get(pre + "down", sh["down"]), quant, device)
+        mw.layers.append(L)
+    # next-layer router rows appended for prediction (the last MoE layer predicts nothing)
+    for i, L in enumerate(mw.layers):
+        if L.is_moe and i + 1 < cfg.n_layers and mw.layers[i + 1].is_moe:
+            L.router_cat = torch.cat([L.router, mw.layers[i + 1].router], 0).contiguous()
+    cos, sin = rope_table(cfg.head_dim, cfg.rope_theta, max_pos, device)
+    mw.rope_cos, mw.rope_sin = cos.contiguous(), sin.contiguous()
+    return mw

@@ -1,0 +1,366 @@
+"""Device-dispatched ops (CUDA kernel or CPU f32 torch)."""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from .._ext import ext
+from ..formats.q4 import Q4Weight
+
+__all__ = [
+    "GEMV_STORE", "GEMV_SWIGLU", "GEMV_SCALED_F32", "GEMV_ADD_F32",
+    "rms_norm", "embed", "linear", "linear_grouped", "qk_rope_kv_write", "attn_decode",
+    "attn_prefill", "router_logits", "moe_topk", "moe_combine_rmsnorm", "argmax", "sample",
+    "swiglu_interleaved_ref", "interleave_gate_up", "count_launches",
+]
+
+GEMV_STORE, GEMV_SWIGLU, GEMV_SCALED_F32, GEMV_ADD_F32 = 0, 1, 2, 3
+DECODE_ROWS_MAX = 64  # above this a linear runs as a GEMM
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """[f, K] x2 -> [2f, K] with 8-row gate/up chunks: rows 16c..16c+7 = gate[8c..8c+7],
+    rows 16c+8..16c+15 = up[8c..8c+7] (the layout the SWIGLU GEMV epilogue reads)."""
+    f, K = gate.shape
+    assert f % 8 == 0
+    return torch.stack([gate.reshape(f // 8, 8, K), up.reshape(f // 8, 8, K)], dim=1).reshape(2 * f, K)
+
+
+def swiglu_interleaved_ref(gu: torch.Tensor) -> torch.Tensor:
+    T, n2 = gu.shape
+    g = gu.reshape(T, n2 // 16, 2, 8)
+    return (F.silu(g[:, :, 0].float()) * g[:, :, 1].float()).reshape(T, n2 // 2)
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    if x.is_cuda:
+        if out is None:
+            out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+        ext().rmsnorm(x, w, eps, out)
+        _launched()
+        return out
+    x32 = x.float()
+    y = x32 * torch.rsqrt(x32.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
+
+
+def embed(table: torch.Tensor, ids: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    if table.is_cuda:
+        ext().embed(table, ids, out)
+        _launched()
+    else:
+        out.copy_(table.float()[ids.long()])
+    return out
+
+
+_LAUNCHES = {"count": None}
+
+
+def count_launches(fn) -> int:
+    """Runs ``fn`` eagerly and returns how many of this package's kernels it launched."""
+    _LAUNCHES["count"] = 0
+    try:
+        fn()
+    finally:
+        n = _LAUNCHES["count"]
+        _LAUNCHES["count"] = None
+    return n
+
+
+def _launched(n: int = 1):
+    if _LAUNCHES["count"] is not None:
+        _LAUNCHES["count"] += n
+
+
+def _dense_weight(W) -> torch.Tensor:
+    return W.dequant() if isinstance(W, Q4Weight) else W
+
+
+def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: torch.Tensor | None = None):
+    """out = x @ W^T with an epilogue:
+    STORE: out = y; SWIGLU: out = silu(gate) * up (interleaved rows); ADD_F32: out += y (f32)."""
+    if not x.is_cuda:
+        y = x.float() @ W.float().t()
+        if mode == GEMV_SWIGLU:
+            out.copy_(swiglu_interleaved_ref(y))
+        elif mode == GEMV_ADD_F32:
+            out.add_(y)
+        else:
+            out.copy_(y)
+        return out
+    T = x.shape[0]
+    if isinstance(W, Q4Weight) and T <= DECODE_ROWS_MAX:
+        ptrs = _ptrs(W)
+        kmode = {GEMV_STORE: 0, GEMV_SWIGLU: 1, GEMV_ADD_F32: 3}[mode]
+        ext().q4_gemv(x, ptrs[0], ptrs[1], _identity_off(T, x.device), _EMPTY_I32(x.device), _EMPTY_F32(x.device),
+                      _EMPTY_BF16(x.device), out, W.N, W.K, kmode)
+        _launched()
+        return out
+    # GEMM path (prefill): dequantised tile + library matmul until the tcgen05 GEMM lands
+    Wd = _dense_weight(W)
+    y = x.to(Wd.dtype) @ Wd.t()
+    if mode == GEMV_SWIGLU:
+        out.copy_(swiglu_interleaved_ref(y))
+    elif mode == GEMV_ADD_F32:
+        out.add_(y.float())
+    else:
+        out.copy_(y)
+    return out
+
+
+_PTR_CACHE: dict = {}
+_OFF_CACHE: dict = {}
+_EMPTY: dict = {}
+
+
+def _ptrs(W: Q4Weight):
+    key = (W.qw.data_ptr(), W.sm.data_ptr())
+    p = _PTR_CACHE.get(key)
+    if p is None:
+        dev = W.qw.device
+        p = (torch.tensor([W.qw.data_ptr()], dtype=torch.int64, device=dev),
+             torch.tensor([W.sm.data_ptr()], dtype=torch.int64, device=dev))
+        _PTR_CACHE[key] = p
+    return p
+
+
+def _identity_off(T: int, dev):
+    key = (T, str(dev))
+    t = _OFF_CACHE.get(key)
+    if t is None:
+        t = torch.tensor([0, T], dtype=torch.int32, device=dev)
+        _OFF_CACHE[key] = t
+    return t
+
+
+def _empty(dtype, dev):
+    key = (dtype, str(dev))
+    t = _EMPTY.get(key)
+    if t is None:
+        t = torch.empty(0, dtype=dtype, device=dev)
+        _EMPTY[key] = t
+    return t
+
+
+def _EMPTY_I32(dev):
+    return _empty(torch.int32, dev)
+
+
+def _EMPTY_F32(dev):
+    return _empty(torch.float32, dev)
+
+
+def _EMPTY_BF16(dev):
+    return _empty(torch.bfloat16, dev)
+
+
+def linear_grouped(x: torch.Tensor, bank, tok_off: torch.Tensor, tok_idx: torch.Tensor | None,
+                   out: torch.Tensor, mode: int, route_w: torch.Tensor | None = None,
+                   qw_ptrs: torch.Tensor | None = None, sm_ptrs: torch.Tensor | None = None):
+    """Grouped (per-expert) linear over CSR pair lists.  bank: ExpertLinear (N, K, tensors)."""
+    if x.is_cuda:
+        e = ext()
+        kmode = {GEMV_STORE: 0, GEMV_SWIGLU: 1, GEMV_SCALED_F32: 2}[mode]
+        e.q4_gemv(x, qw_ptrs, sm_ptrs, tok_off,
+                  tok_idx if tok_idx is not None else _EMPTY_I32(x.device),
+                  route_w if route_w is not None else _EMPTY_F32(x.device),
+                  _EMPTY_BF16(x.device), out, bank.N, bank.K, kmode)
+        _launched()
+        return out
+    # CPU reference: loop over experts in ascending order
+    off = tok_off.tolist()
+    for eidx in range(len(off) - 1):
+        a, b = off[eidx], off[eidx + 1]
+        if a == b:
+            continue
+        rows = tok_idx[a:b].long() if tok_idx is not None else torch.arange(a, b)
+        y = x[rows].float() @ bank.weight(eidx).float().t()
+        if mode == GEMV_SWIGLU:
+            out[a:b] = swiglu_interleaved_ref(y)
+        elif mode == GEMV_SCALED_F32:
+            out[a:b] = route_w[a:b, None] * y
+        else:
+            out[a:b] = y
+    return out
+
+
+def qk_rope_kv_write(qkv, Hq, Hkv, D, q_norm, k_norm, eps, pos, cos_t, sin_t, slot, q_out, k_cache, v_cache):
+    if qkv.is_cuda:
+        ext().qk_rope_kv_write(qkv, Hq, Hkv, D, q_norm if q_norm is not None else _EMPTY_F32(qkv.device),
+                               k_norm if k_norm is not None else _EMPTY_F32(qkv.device), eps, pos, cos_t, sin_t,
+                               slot, q_out, k_cache, v_cache)
+        _launched()
+        return
+    T = qkv.shape[0]
+    x = qkv.float().reshape(T, Hq + 2 * Hkv, D)
+    q, k, v = x[:, :Hq], x[:, Hq:Hq + Hkv], x[:, Hq + Hkv:]
+
+    def _n(t, w):
+        return t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+
+    if q_norm is not None:
+        q = _n(q, q_norm)
+        k = _n(k, k_norm)
+    p = pos.long()
+    c = cos_t[p][:, None, :]
+    s = sin_t[p][:, None, :]
+
+    def _r(t):
+        a, b = t[..., : D // 2], t[..., D // 2:]
+        return torch.cat([a * c - b * s, b * c + a * s], -1)
+
+    q, k = _r(q), _r(k)
+    q_out.copy_(q.reshape(q_out.shape))
+    bs = k_cache.shape[2]
+    for i in range(T):
+        sl = int(slot[i])
+        if sl < 0:
+            continue
+        k_cache[sl // bs, :, sl % bs] = k[i]
+        v_cache[sl // bs, :, sl % bs] = v[i]
+
+
+def attn_decode(q, k_cache, v_cache, block_tables, ctx_lens, out, scale, part_o=None, part_ml=None,
+                pages_per_split=16):
+    """q: [T, Hq, D]; one query row per sequence, attending to ctx_lens[t] cached tokens."""
+    if q.is_cuda:
+        ext().attn_decode(q, k_cache, v_cache, block_tables, ctx_lens, part_o, part_ml, out, pages_per_split, scale)
+        _launched(2)
+        return out
+    T, Hq, D = q.shape
+    Hkv = k_cache.shape[1]
+    bs = k_cache.shape[2]
+    for t in range(T):
+        n = int(ctx_lens[t])
+        nb = (n + bs - 1) // bs
+        blocks = block_tables[t, :nb].long()
+        k = k_cache[blocks].permute(0, 2, 1, 3).reshape(nb * bs, Hkv, D)[:n]
+        v = v_cache[blocks].permute(0, 2, 1, 3).reshape(nb * bs, Hkv, D)[:n]
+        g = Hq // Hkv
+        kk = k.repeat_interleave(g, 1).float()
+        vv = v.repeat_interleave(g, 1).float()
+        s = torch.einsum("hd,khd->hk", q[t].float(), kk) * scale
+        p = torch.softmax(s, -1)
+        out[t] = torch.einsum("hk,khd->hd", p, vv).to(out.dtype)
+    return out
+
+
+def attn_prefill(q, k, v, cu_seqlens: list[int], out, scale):
+    """Causal attention over freshly prefilled sequences (no cached prefix).
+    q: [T, Hq, D], k/v: [T, Hkv, D] (rotated), out: [T, Hq, D]."""
+    Hq, Hkv = q.shape[1], k.shape[1]
+    for i in range(len(cu_seqlens) - 1):
+        a, b = cu_seqlens[i], cu_seqlens[i + 1]
+        qq = q[a:b].transpose(0, 1)[None]
+        kk = k[a:b].transpose(0, 1)[None]
+        vv = v[a:b].transpose(0, 1)[None]
+        if not q.is_cuda:
+            qq, kk, vv = qq.float(), kk.float(), vv.float()
+        o = F.scaled_dot_product_attention(qq, kk, vv, is_causal=True, scale=scale, enable_gqa=(Hq != Hkv))
+        out[a:b] = o[0].transpose(0, 1).to(out.dtype)
+    return out
+
+
+def router_logits(h, W, out):
+    if h.is_cuda:
+        ext().router_logits(h, W, out)
+        _launched()
+    else:
+        out.copy_(h.float() @ W.float().t())
+    return out
+
+
+def moe_topk(logits, cfg, bias, pred: bool, bufs: dict):
+    """Top-k routing + CSR.  bufs: topk_ids, topk_w, tok_off, tok_idx, pair_w, pair_of, pred_mask."""
+    E, k = cfg.n_experts, cfg.top_k
+    scoring = 0 if cfg.router_scoring == "softmax" else 1
+    if logits.is_cuda:
+        ext().moe_topk(logits, bias if bias is not None else _EMPTY_F32(logits.device), E, k, scoring, cfg.n_groups,
+                       cfg.topk_groups, cfg.norm_topk_prob, cfg.routed_scaling, pred, bufs["topk_ids"],
+                       bufs["topk_w"], bufs["tok_off"], bufs["tok_idx"], bufs["pair_w"], bufs["pair_of"],
+                       bufs["pred_mask"] if pred else _EMPTY_I32(logits.device))
+        _launched()
+        return
+    from ..models.reference import topk_stable
+    T = logits.shape[0]
+    lg = logits[:, :E].float()
+    if scoring == 0:
+        scores = torch.softmax(lg, -1)
+        sel = scores.clone()
+    else:
+        scores = torch.sigmoid(lg)
+        sel = scores + (bias.float() if bias is not None else 0)
+    if cfg.n_groups > 1:
+        gs = sel.view(T, cfg.n_groups, E // cfg.n_groups)
+        gscore = gs.topk(2, -1).values.sum(-1) if scoring == 1 else gs.max(-1).values
+        _, gi = topk_stable(gscore, cfg.topk_groups)
+        gm = torch.zeros_like(gscore).scatter_(1, gi, 1.0)
+        sel = sel.masked_fill(gm[:, :, None].expand_as(gs).reshape(T, E) == 0, float("-inf"))
+    _, ids = topk_stable(sel, k)
+    w = torch.gather(scores, -1, ids)
+    if cfg.norm_topk_prob:
+        w = w / w.sum(-1, keepdim=True)
+    w = w * cfg.routed_scaling
+    bufs["topk_ids"][:T] = ids.int()
+    bufs["topk_w"][:T] = w
+    counts = torch.bincount(ids.reshape(-1), minlength=E)
+    off = torch.zeros(E + 1, dtype=torch.int64)
+    off[1:] = torch.cumsum(counts, 0)
+    bufs["tok_off"][: E + 1] = off.int()
+    fill = off[:-1].clone()
+    pair_of = torch.empty(T, k, dtype=torch.int32)
+    for e in range(E):
+        pass
+    for t in range(T):
+        order = torch.argsort(ids[t])
+        for slot, j in enumerate(order.tolist()):
+            e = int(ids[t, j])
+            p = int(fill[e])
+            fill[e] += 1
+            bufs["tok_idx"][p] = t
+            bufs["pair_w"][p] = w[t, j]
+            pair_of[t, slot] = p
+    # pairs of one expert are in token order because tokens are visited in order
+    bufs["pair_of"][:T] = pair_of
+
+
+def moe_combine_rmsnorm(x, yp, pair_of, shared, w, out, eps):
+    if x.is_cuda:
+        ext().moe_combine_rmsnorm(x, yp, pair_of, shared if shared is not None else _EMPTY_F32(x.device),
+                                  w if w is not None else _EMPTY_F32(x.device),
+                                  out if out is not None else _EMPTY_BF16(x.device), eps)
+        _launched()
+        return
+    T, k = pair_of.shape
+    acc = torch.zeros_like(x)
+    for j in range(k):
+        acc += yp[pair_of[:, j].long()]
+    if shared is not None:
+        acc += shared
+    x.add_(acc)
+    if w is not None:
+        out.copy_(rms_norm(x, w, eps))
+
+
+def argmax(logits, out):
+    if logits.is_cuda:
+        ext().argmax(logits, out)
+        _launched()
+    else:
+        out.copy_(torch.argmax(logits, -1).int())
+    return out
+
+
+def sample(logits, temperature, top_k, top_p, seed, stream, counter, out):
+    if logits.is_cuda:
+        ext().sample(logits, temperature, top_k, top_p, seed, stream, counter, out)
+        _launched()
+        return out
+    from ..runtime.sampling_ref import sample_ref
+    out.copy_(sample_ref(logits, temperature, top_k, top_p, seed, stream, counter))
+    return out

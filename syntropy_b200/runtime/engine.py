@@ -1,0 +1,246 @@
+"""LLM engine: request intake, continuous batching, prefill/decode steps, sampling state.
+
+Scheduling (reference design: plan/rfcs/RFC-0012-execution-scheduler.md): FCFS admission
+while KV pages last; a step is either a prefill batch (whole prompts up to a token budget)
+or one decode step over every running sequence.  Each sequence carries its sampling key
+(seed, stream) and ``rng_counter`` (plan/decisions/ADR-0107-counter-based-sampling-rng.md).
+"""
+from __future__ import annotations
+
+import itertools
+import random
+import time
+from collections import deque
+from dataclasses import dataclass, field
+
+import torch
+
+from .. import ops
+from .runner import ModelRunner
+
+
+@dataclass
+class SamplingParams:
+    max_tokens: int = 16
+    temperature: float = 0.0
+    top_k: int = 0
+    top_p: float = 1.0
+    seed: int | None = None
+    stop_token_ids: tuple = ()
+    ignore_eos: bool = True
+
+
+@dataclass
+class Sequence:
+    seq_id: int
+    prompt: list
+    params: SamplingParams
+    output: list = field(default_factory=list)
+    blocks: list = field(default_factory=list)
+    status: str = "waiting"  # waiting | running | finished
+    finish_reason: str | None = None
+    seed: int = 0
+    stream: int = 0
+    rng_counter: int = 0
+    t_arrival: float = 0.0
+    t_first_token: float | None = None
+    t_finished: float | None = None
+
+    @property
+    def n_tokens(self) -> int:
+        return len(self.prompt) + len(self.output)
+
+
+@dataclass
+class StepOutput:
+    seq_id: int
+    new_tokens: list
+    finished: bool
+    finish_reason: str | None = None
+
+
+class LLMEngine:
+    def __init__(self, runner: ModelRunner, max_prefill_tokens: int = 8192, eos_token_id: int | None = None):
+        self.runner = runner
+        self.cfg = runner.cfg
+        self.max_prefill_tokens = max_prefill_tokens
+        self.eos = eos_token_id
+        self.waiting: deque[Sequence] = deque()
+        self.running: list[Sequence] = []
+        self.finished: dict[int, Sequence] = {}
+        self._ids = itertools.count()
+        self._boot_seed = random.getrandbits(63)
+        self.stats = {"prefill_steps": 0, "decode_steps": 0, "decode_tokens": 0, "prefill_tokens": 0}
+
+    # ------------------------------------------------------------------ intake
+    def add_request(self, prompt: list[int], params: SamplingParams | None = None, choice_index: int = 0) -> int:
+        params = params or SamplingParams()
+        if not prompt:
+            raise ValueError("empty prompt")
+        for t in prompt:
+            if not 0 <= t < self.cfg.vocab:
+                raise ValueError(f"token id {t} out of range [0, {self.cfg.vocab})")
+        if len(prompt) + params.max_tokens > self.runner.max_seq_len:
+            raise ValueError("prompt + max_tokens exceeds max_seq_len")
+        sid = next(self._ids)
+        s = Sequence(sid, list(prompt), params, t_arrival=time.perf_counter())
+        if params.seed is not None:  # client seed: key (seed, choice index)
+            s.seed, s.stream = params.seed, choice_index
+        else:  # generated seed: key (seed, sequence id)
+            s.seed, s.stream = self._boot_seed ^ sid, sid
+        self.waiting.append(s)
+        return sid
+
+    def abort(self, seq_id: int):
+        for s in list(self.waiting):
+            if s.seq_id == seq_id:
+                self.waiting.remove(s)
+                self._finish(s, "cancelled")
+                return
+        for s in self.running:
+            if s.seq_id == seq_id:
+                self._finish(s, "cancelled")
+                self.running.remove(s)
+                return
+
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    # ------------------------------------------------------------------ steps
+    def step(self) -> list[StepOutput]:
+        batch = self._admit()
+        if batch:
+            return self._prefill(batch)
+        if self.running:
+            return self._decode()
+        return []
+
+    def _admit(self) -> list[Sequence]:
+        kv = self.runner.kv
+        batch, tokens = [], 0
+        while self.waiting and len(self.running) + len(batch) < self.runner.max_batch:
+            s = self.waiting[0]
+            need = kv.blocks_needed(len(s.prompt) + 1)
+            if kv.alloc.num_free < need or (batch and tokens + len(s.prompt) > self.max_prefill_tokens):
+                break
+            self.waiting.popleft()
+            kv.ensure(s.blocks, len(s.prompt))
+            batch.append(s)
+            tokens += len(s.prompt)
+        return batch
+
+    def _prefill(self, batch: list[Sequence]) -> list[StepOutput]:
+        kv = self.runner.kv
+        toks, pos, slots, cu = [], [], [], [0]
+        for s in batch:
+            toks += s.prompt
+            pos += list(range(len(s.prompt)))
+            slots += [kv.slot(s.blocks, p) for p in range(len(s.prompt))]
+            cu.append(cu[-1] + len(s.prompt))
+        logits = self.runner.prefill(torch.tensor(toks), torch.tensor(pos), torch.tensor(slots), cu)
+        nxt = self._sample_rows(logits, batch)
+        self.stats["prefill_steps"] += 1
+        self.stats["prefill_tokens"] += cu[-1]
+        now = time.perf_counter()
+        outs = []
+        for s, t in zip(batch, nxt):
+            s.t_first_token = now
+            s.status = "running"
+            self.running.append(s)
+            outs.append(self._append(s, t))
+        self._reap()
+        return outs
+
+    def _sample_rows(self, logits: torch.Tensor, seqs: list[Sequence]) -> list[int]:
+        n = len(seqs)
+        dev = logits.device
+        temp = torch.tensor([s.params.temperature for s in seqs], dtype=torch.float32, device=dev)
+        topk = torch.tensor([s.params.top_k for s in seqs], dtype=torch.int32, device=dev)
+        topp = torch.tensor([s.params.top_p for s in seqs], dtype=torch.float32, device=dev)
+        seed = torch.tensor([s.seed for s in seqs], dtype=torch.int64, device=dev)
+        stream = torch.tensor([s.stream for s in seqs], dtype=torch.int64, device=dev)
+        ctr = torch.tensor([s.rng_counter for s in seqs], dtype=torch.int64, device=dev)
+        out = torch.empty(n, dtype=torch.int32, device=dev)
+        ops.sample(logits.contiguous(), temp, topk, topp, seed, stream, ctr, out)
+        ctr_h = ctr.cpu().tolist()
+        for s, c in zip(seqs, ctr_h):
+            s.rng_counter = int(c)
+        return out.cpu().tolist()
+
+    def _decode(self) -> list[StepOutput]:
+        r = self.runner
+        kv = r.kv
+        seqs = self.running
+        B = len(seqs)
+        d = r.desc.h
+        for i, s in enumerate(seqs):
+            p = s.n_tokens - 1
+            kv.ensure(s.blocks, p + 1)
+            d["tokens"][i] = s.output[-1]
+            d["pos"][i] = p
+            d["ctx_len"][i] = p + 1
+            d["slot"][i] = kv.slot(s.blocks, p)
+            bt = d["block_tables"][i]
+            bt[: len(s.blocks)] = torch.tensor(s.blocks, dtype=torch.int32)
+            d["temperature"][i] = s.params.temperature
+            d["top_k"][i] = s.params.top_k
+            d["top_p"][i] = s.params.top_p
+            d["seed"][i] = s.seed
+            d["stream"][i] = s.stream
+            d["counter"][i] = s.rng_counter
+        if r.use_graphs:  # padding rows of the bucket
+            from .runner import bucket_for
+            bb = bucket_for(B)
+            for i in range(B, bb):
+                d["tokens"][i] = 0
+                d["pos"][i] = 0
+                d["ctx_len"][i] = 1
+                d["slot"][i] = -1
+                d["block_tables"][i, 0] = 0
+                d["temperature"][i] = 0.0
+        nxt = r.decode(B).cpu().tolist()
+        # greedy rows take no draw; sampled rows take exactly one
+        for s in seqs:
+            if s.params.temperature > 0:
+                s.rng_counter += 1
+        self.stats["decode_steps"] += 1
+        self.stats["decode_tokens"] += B
+        outs = [self._append(s, t) for s, t in zip(seqs, nxt)]
+        self._reap()
+        return outs
+
+    def _append(self, s: Sequence, tok: int) -> StepOutput:
+        s.output.append(int(tok))
+        reason = None
+        if len(s.output) >= s.params.max_tokens:
+            reason = "length"
+        elif tok in s.params.stop_token_ids or (not s.params.ignore_eos and self.eos is not None and tok == self.eos):
+            reason = "stop"
+        if reason:
+            s.finish_reason = reason
+            s.status = "finished"
+        return StepOutput(s.seq_id, [int(tok)], reason is not None, reason)
+
+    def _finish(self, s: Sequence, reason: str):
+        s.status = "finished"
+        s.finish_reason = s.finish_reason or reason
+        s.t_finished = time.perf_counter()
+        self.runner.kv.release(s.blocks)
+        self.finished[s.seq_id] = s
+
+    def _reap(self):
+        keep = []
+        for s in self.running:
+            if s.status == "finished":
+                self._finish(s, s.finish_reason or "length")
+            else:
+                keep.append(s)
+        self.running = keep
+
+    # ------------------------------------------------------------------ convenience
+    def generate(self, prompts: list[list[int]], params: SamplingParams | list[SamplingParams]) -> list[list[int]]:
+        plist = params if isinstance(params, list) else [params] * len(prompts)
+        ids = [self.add_request(p, sp) for p, sp in zip(prompts, plist)]
+        while self.has_work():
+            self.step()
+        return [self.finished[i].output for i in ids]

@@ -1,0 +1,407 @@
+"""Model runner: static device buffers, the decode forward (captured in one CUDA graph per
+batch bucket) and the eager prefill forward.
+
+Step inputs travel as ONE packed step descriptor (int64 words) copied host->device per
+step, mirroring the reference's StepDesc-first graph design (crates/kernels/include/
+syntropy/step_desc.h; plan/rfcs/RFC-0040-kernel-providers-and-backends.md:425-461).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from .. import ops
+from ..formats.q4 import Q4Weight
+from ..kv.paged import PagedKVCache
+from ..models.transformer import ModelWeights
+
+BUCKETS = (1, 2, 4, 8, 16, 32, 48, 64)
+
+
+def bucket_for(n: int, buckets=BUCKETS) -> int:
+    for b in buckets:
+        if n <= b:
+            return b
+    raise ValueError(f"batch {n} exceeds the largest bucket {buckets[-1]}")
+
+
+class StepDesc:
+    """Packed per-step inputs.  Fields (rows = max_batch):
+    tokens, pos, ctx_len, top_k : int32-valued; slot, seed, stream, counter : int64;
+    temperature, top_p : f32 (bit-cast); block_tables [rows, max_blocks] int32."""
+
+    INT_FIELDS = ("tokens", "pos", "ctx_len", "top_k")
+    LONG_FIELDS = ("slot", "seed", "stream", "counter")
+    F_FIELDS = ("temperature", "top_p")
+
+    def __init__(self, rows: int, max_blocks: int, device):
+        self.rows, self.max_blocks = rows, max_blocks
+        n_i32 = rows * (len(self.INT_FIELDS) + len(self.F_FIELDS)) + rows * max_blocks
+        n_i32 += (-n_i32) % 2
+        n_i64 = rows * len(self.LONG_FIELDS)
+        self.nbytes = n_i32 * 4 + n_i64 * 8
+        pin = device.type == "cuda"
+        self.host = torch.zeros(self.nbytes, dtype=torch.uint8, pin_memory=pin)
+        self.dev = torch.zeros(self.nbytes, dtype=torch.uint8, device=device)
+        self.h, self.d = self._views(self.host), self._views(self.dev)
+
+    def _views(self, buf):
+        rows, mb = self.rows, self.max_blocks
+        n_i32 = rows * (len(self.INT_FIELDS) + len(self.F_FIELDS)) + rows * mb
+        n_i32 += (-n_i32) % 2
+        i32 = buf[: n_i32 * 4].view(torch.int32)
+        i64 = buf[n_i32 * 4:].view(torch.int64)
+        v = {}
+        o = 0
+        for f in self.INT_FIELDS:
+            v[f] = i32[o:o + rows]
+            o += rows
+        for f in self.F_FIELDS:
+            v[f] = i32[o:o + rows].view(torch.float32)
+            o += rows
+        v["block_tables"] = i32[o:o + rows * mb].view(rows, mb)
+        o = 0
+        for f in self.LONG_FIELDS:
+            v[f] = i64[o:o + rows]
+            o += rows
+        return v
+
+    def upload(self):
+        self.dev.copy_(self.host, non_blocking=True)
+
+
+class ModelRunner:
+    def __init__(self, mw: ModelWeights, max_batch: int = 64, max_seq_len: int = 4096, num_blocks: int | None = None,
+                 kv_dtype=None, use_graphs: bool = True, kv_budget_bytes: int | None = None):
+        cfg = mw.cfg
+        self.mw, self.cfg = mw, cfg
+        self.device = mw.device
+        self.is_cuda = self.device.type == "cuda"
+        self.max_batch = max_batch
+        self.max_seq_len = max_seq_len
+        self.block_size = 16
+        self.max_blocks = (max_seq_len + self.block_size - 1) // self.block_size
+        kv_dtype = kv_dtype or (torch.bfloat16 if self.is_cuda else torch.float32)
+        if num_blocks is None:
+            per = PagedKVCache.bytes_per_block(cfg.n_layers, cfg.n_kv_heads, cfg.head_dim, self.block_size,
+                                               torch.tensor([], dtype=kv_dtype).element_size())
+            if kv_budget_bytes is None:
+                num_blocks = max_batch * self.max_blocks + 1
+            else:
+                num_blocks = max(2, kv_budget_bytes // per)
+        self.kv = PagedKVCache(cfg.n_layers, num_blocks, cfg.n_kv_heads, cfg.head_dim, self.block_size, kv_dtype,
+                               self.device)
+        self.desc = StepDesc(max_batch, self.max_blocks, self.device)
+        self.use_graphs = use_graphs and self.is_cuda
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.time_events: list | None = None  # when a list: (start, end) CUDA events per decode
+        self._alloc_buffers()
+        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+
+    # ------------------------------------------------------------------ buffers
+    def _alloc_buffers(self):
+        cfg, B, dev = self.cfg, self.max_batch, self.device
+        act = torch.bfloat16 if self.is_cuda else torch.float32
+        H = cfg.hidden
+        qkv_dim = cfg.q_dim + 2 * cfg.kv_dim
+        b = {}
+        b["x"] = torch.zeros(B, H, dtype=torch.float32, device=dev)
+        b["h"] = torch.zeros(B, H, dtype=act, device=dev)
+        b["qkv"] = torch.zeros(B, qkv_dim, dtype=act, device=dev)
+        b["q"] = torch.zeros(B, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
+        b["attn"] = torch.zeros(B, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
+        b["logits"] = torch.zeros(B, cfg.vocab, dtype=torch.float32, device=dev)
+        b["next"] = torch.zeros(B, dtype=torch.int32, device=dev)
+        if any(not L.is_moe for L in self.mw.layers):
+            b["ffn_mid"] = torch.zeros(B, cfg.ffn, dtype=act, device=dev)
+        if cfg.is_moe:
+            E, k = cfg.n_experts, cfg.top_k
+            b["rlogits"] = torch.zeros(B, 2 * E, dtype=torch.float32, device=dev)
+            b["topk_ids"] = torch.zeros(B, k, dtype=torch.int32, device=dev)
+            b["topk_w"] = torch.zeros(B, k, dtype=torch.float32, device=dev)
+            b["tok_off"] = torch.zeros(E + 1, dtype=torch.int32, device=dev)
+            b["tok_idx"] = torch.zeros(B * k, dtype=torch.int32, device=dev)
+            b["pair_w"] = torch.zeros(B * k, dtype=torch.float32, device=dev)
+            b["pair_of"] = torch.zeros(B, k, dtype=torch.int32, device=dev)
+            b["pred_mask"] = torch.zeros(E, dtype=torch.int32, device=dev)
+            b["moe_mid"] = torch.zeros(B * k, cfg.moe_ffn, dtype=act, device=dev)
+            b["moe_out"] = torch.zeros(B * k, H, dtype=torch.float32, device=dev)
+        # split-KV workspace sized for the largest split count
+        self.pages_per_split = 16
+        n_splits = (self.max_blocks + self.pages_per_split - 1) // self.pages_per_split
+        if self.is_cuda:
+            b["part_o"] = torch.zeros(B * cfg.n_kv_heads * n_splits * 16 * cfg.head_dim, dtype=torch.float32,
+                                      device=dev)
+            b["part_ml"] = torch.zeros(B * cfg.n_kv_heads * n_splits * 16 * 2, dtype=torch.float32, device=dev)
+        self.buf = b
+
+    # ------------------------------------------------------------------ decode
+    def _moe_bufs(self, B):
+        b = self.buf
+        k = self.cfg.top_k
+        return {"topk_ids": b["topk_ids"][:B], "topk_w": b["topk_w"][:B], "tok_off": b["tok_off"],
+                "tok_idx": b["tok_idx"][:B * k], "pair_w": b["pair_w"][:B * k], "pair_of": b["pair_of"][:B],
+                "pred_mask": b["pred_mask"]}
+
+    def decode_forward(self, B: int):
+        """Forward of the first B rows of the step descriptor; writes logits and next tokens."""
+        cfg, mw, b, d = self.cfg, self.mw, self.buf, self.desc.d
+        x, h = b["x"][:B], b["h"][:B]
+        ops.embed(mw.embed, d["tokens"][:B], x)
+        n_layers = cfg.n_layers
+        first = mw.layers[0]
+        ops.rms_norm(x, first.attn_norm, cfg.rms_eps, out=h)
+        for i, L in enumerate(mw.layers):
+            nxt = mw.layers[i + 1] if i + 1 < n_layers else None
+            self._attention_decode(L, B, i)
+            if L.is_moe:
+                self._moe_decode(L, nxt, B)
+            else:
+                ops.rms_norm(x, L.ffn_norm, cfg.rms_eps, out=h)
+                mid = b["ffn_mid"][:B]
+                ops.linear(h, L.gate_up, mid, ops.GEMV_SWIGLU)
+                ops.linear(mid, L.down, x, ops.GEMV_ADD_F32)
+                ops.rms_norm(x, nxt.attn_norm if nxt else mw.final_norm, cfg.rms_eps, out=h)
+        logits = b["logits"][:B]
+        ops.linear(h, mw.lm_head, logits, ops.GEMV_STORE)
+        ops.sample(logits, d["temperature"][:B], d["top_k"][:B], d["top_p"][:B], d["seed"][:B], d["stream"][:B],
+                   d["counter"][:B], b["next"][:B])
+        return logits
+
+    def _attention_decode(self, L, B, i):
+        cfg, b, d = self.cfg, self.buf, self.desc.d
+        h = b["h"][:B]
+        qkv = b["qkv"][:B]
+        ops.linear(h, L.qkv, qkv, ops.GEMV_STORE)
+        q = b["q"][:B]
+        ops.qk_rope_kv_write(qkv, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, L.q_norm, L.k_norm, cfg.rms_eps,
+                             d["pos"][:B], self.mw.rope_cos, self.mw.rope_sin, d["slot"][:B], q, self.kv.k[i],
+                             self.kv.v[i])
+        attn = b["attn"][:B]
+        ops.attn_decode(q, self.kv.k[i], self.kv.v[i], d["block_tables"][:B], d["ctx_len"][:B], attn, self.scale,
+                        b.get("part_o"), b.get("part_ml"), self.pages_per_split)
+        ops.linear(attn.view(B, -1), L.o, b["x"][:B], ops.GEMV_ADD_F32)
+
+    def _moe_decode(self, L, nxt, B):
+        cfg, mw, b = self.cfg, self.mw, self.buf
+        x, h = b["x"][:B], b["h"][:B]
+        ops.rms_norm(x, L.ffn_norm, cfg.rms_eps, out=h)
+        pred = L.router_cat is not None
+        rw = L.router_cat if pred else L.router
+        E = cfg.n_experts
+        rl = b["rlogits"][:B, : (2 * E if pred else E)]
+        ops.router_logits(h, rw, rl)
+        mb = self._moe_bufs(B)
+        ops.moe_topk(rl, cfg, L.router_bias, pred, mb)
+        k = cfg.top_k
+        mid = b["moe_mid"][:B * k]
+        yp = b["moe_out"][:B * k]
+        gu, dn = L.experts_gu, L.experts_down
+        ops.linear_grouped(h, gu, mb["tok_off"], mb["tok_idx"], mid, ops.GEMV_SWIGLU,
+                           qw_ptrs=gu.qw_ptrs, sm_ptrs=gu.sm_ptrs)
+        ops.linear_grouped(mid, dn, mb["tok_off"], None, yp, ops.GEMV_SCALED_F32, route_w=mb["pair_w"],
+                           qw_ptrs=dn.qw_ptrs, sm_ptrs=dn.sm_ptrs)
+        nw = nxt.attn_norm if nxt else mw.final_norm
+        ops.moe_combine_rmsnorm(x, yp, mb["pair_of"], None, nw, h, cfg.rms_eps)
+
+    def decode(self, B: int):
+        """Run one decode step for the first B rows (descriptor already filled on the host)."""
+        self.desc.upload()
+        if self.use_graphs:
+            bb = bucket_for(B)
+            g = self.graphs.get(bb)
+            if g is None:
+                g = self.capture(bb)
+            ev = self._ev0()
+            g.replay()
+            self._ev1(ev)
+        else:
+            ev = self._ev0()
+            self.decode_forward(B)
+            self._ev1(ev)
+        return self.buf["next"][:B]
+
+    def _ev0(self):
+        if self.time_events is None or not self.is_cuda:
+            return None
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        return (e0, e1)
+
+    def _ev1(self, ev):
+        if ev is not None:
+            ev[1].record()
+            self.time_events.append(ev)
+
+    def capture(self, bb: int) -> "torch.cuda.CUDAGraph":
+        """Capture the decode forward for bucket size bb (rows beyond the live batch are
+        padding: null page, slot -1, greedy)."""
+        d = self.desc.h
+        saved = {k: v.clone() for k, v in d.items()}
+        d["tokens"][:bb] = 0
+        d["pos"][:bb] = 0
+        d["ctx_len"][:bb] = 1
+        d["slot"][:bb] = -1
+        d["block_tables"][:bb] = 0
+        d["temperature"][:bb] = 0
+        d["top_k"][:bb] = 0
+        d["top_p"][:bb] = 1
+        self.desc.upload()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.decode_forward(bb)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.decode_forward(bb)
+        torch.cuda.synchronize()
+        for k, v in saved.items():
+            d[k].copy_(v)
+        self.graphs[bb] = g
+        return g
+
+    # ------------------------------------------------------------------ prefill
+    @torch.no_grad()
+    def prefill(self, tokens: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor, cu_seqlens: list[int]):
+        """Eager prefill of freshly started sequences (positions from 0).  Returns the
+        last-token logits of each sequence [n_seq, vocab] (f32)."""
+        cfg, mw, dev = self.cfg, self.mw, self.device
+        T = tokens.numel()
+        act = torch.bfloat16 if self.is_cuda else torch.float32
+        tokens = tokens.to(dev, torch.int32)
+        positions = positions.to(dev, torch.int32)
+        slots = slots.to(dev, torch.int64)
+        x = torch.empty(T, cfg.hidden, dtype=torch.float32, device=dev)
+        ops.embed(mw.embed, tokens, x)
+        h = torch.empty(T, cfg.hidden, dtype=act, device=dev)
+        qkv = torch.empty(T, cfg.q_dim + 2 * cfg.kv_dim, dtype=act, device=dev)
+        q = torch.empty(T, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
+        attn = torch.empty(T, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
+        for i, L in enumerate(mw.layers):
+            ops.rms_norm(x, L.attn_norm, cfg.rms_eps, out=h)
+            ops.linear(h, L.qkv, qkv, ops.GEMV_STORE)
+            ops.qk_rope_kv_write(qkv, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, L.q_norm, L.k_norm, cfg.rms_eps,
+                                 positions, mw.rope_cos, mw.rope_sin, slots, q, self.kv.k[i], self.kv.v[i])
+            kc = self.kv.k[i].permute(0, 2, 1, 3).reshape(-1, cfg.n_kv_heads, cfg.head_dim)[slots]
+            vc = self.kv.v[i].permute(0, 2, 1, 3).reshape(-1, cfg.n_kv_heads, cfg.head_dim)[slots]
+            ops.attn_prefill(q, kc, vc, cu_seqlens, attn, self.scale)
+            ops.linear(attn.view(T, -1), L.o, x, ops.GEMV_ADD_F32)
+            ops.rms_norm(x, L.ffn_norm, cfg.rms_eps, out=h)
+            if L.is_moe:
+                self._moe_prefill(L, h, x)
+            else:
+                mid = torch.empty(T, cfg.ffn, dtype=act, device=dev)
+                ops.linear(h, L.gate_up, mid, ops.GEMV_SWIGLU)
+                ops.linear(mid, L.down, x, ops.GEMV_ADD_F32)
+        last = torch.tensor([c - 1 for c in cu_seqlens[1:]], device=dev, dtype=torch.long)
+        hl = ops.rms_norm(x[last].contiguous(), mw.final_norm, cfg.rms_eps)
+        logits = torch.empty(last.numel(), cfg.vocab, dtype=torch.float32, device=dev)
+        ops.linear(hl, mw.lm_head, logits, ops.GEMV_STORE)
+        return logits
+
+    def _moe_prefill(self, L, h, x):
+        """MoE FFN for a prefill chunk: routing on the device, then one GEMM pair per active
+        expert over its gathered rows, combined in ascending expert order."""
+        cfg = self.cfg
+        T = h.shape[0]
+        E, k = cfg.n_experts, cfg.top_k
+        dev = h.device
+        if T <= 256 and self.is_cuda:
+            logits = torch.empty(T, E, dtype=torch.float32, device=dev)
+            ops.router_logits(h, L.router, logits)
+            mb = {"topk_ids": torch.empty(T, k, dtype=torch.int32, device=dev),
+                  "topk_w": torch.empty(T, k, dtype=torch.float32, device=dev),
+                  "tok_off": torch.empty(E + 1, dtype=torch.int32, device=dev),
+                  "tok_idx": torch.empty(T * k, dtype=torch.int32, device=dev),
+                  "pair_w": torch.empty(T * k, dtype=torch.float32, device=dev),
+                  "pair_of": torch.empty(T, k, dtype=torch.int32, device=dev), "pred_mask": None}
+            ops.moe_topk(logits, cfg, L.router_bias, False, mb)
+        else:
+            logits = h.float() @ L.router.float().t()
+            mb = {"topk_ids": torch.empty(T, k, dtype=torch.int32, device=dev),
+                  "topk_w": torch.empty(T, k, dtype=torch.float32, device=dev),
+                  "tok_off": torch.empty(E + 1, dtype=torch.int32, device=dev),
+                  "tok_idx": torch.empty(T * k, dtype=torch.int32, device=dev),
+                  "pair_w": torch.empty(T * k, dtype=torch.float32, device=dev),
+                  "pair_of": torch.empty(T, k, dtype=torch.int32, device=dev)}
+            _route_torch(logits, cfg, L.router_bias, mb)
+        off = mb["tok_off"].tolist()
+        yp = torch.zeros(T * k, cfg.hidden, dtype=torch.float32, device=dev)
+        tok_idx = mb["tok_idx"].long()
+        gu, dn = L.experts_gu, L.experts_down
+        for e in range(E):
+            a, b = off[e], off[e + 1]
+            if a == b:
+                continue
+            rows = h[tok_idx[a:b]]
+            if self.is_cuda and rows.shape[0] <= ops.DECODE_ROWS_MAX and gu.qw is not None:
+                mid = torch.empty(b - a, cfg.moe_ffn, dtype=h.dtype, device=dev)
+                ops.linear_grouped(rows, gu, _off1(b - a, dev), None, mid, ops.GEMV_SWIGLU,
+                                   qw_ptrs=gu.qw_ptrs[e:e + 1], sm_ptrs=gu.sm_ptrs[e:e + 1])
+                ops.linear_grouped(mid, dn, _off1(b - a, dev), None, yp[a:b], ops.GEMV_SCALED_F32,
+                                   route_w=mb["pair_w"][a:b], qw_ptrs=dn.qw_ptrs[e:e + 1],
+                                   sm_ptrs=dn.sm_ptrs[e:e + 1])
+                continue
+            wg = gu.weight(e)
+            wd = dn.weight(e)
+            y = rows.to(wg.dtype) @ wg.t()
+            mid = ops.swiglu_interleaved_ref(y).to(wd.dtype)
+            yp[a:b] = mb["pair_w"][a:b, None] * (mid @ wd.t()).float()
+        ops.moe_combine_rmsnorm(x, yp, mb["pair_of"], None, None, None, cfg.rms_eps)
+
+
+_OFF1: dict = {}
+
+
+def _off1(n, dev):
+    key = (n, str(dev))
+    t = _OFF1.get(key)
+    if t is None:
+        t = torch.tensor([0, n], dtype=torch.int32, device=dev)
+        _OFF1[key] = t
+    return t
+
+
+def _route_torch(logits, cfg, bias, mb):
+    """Large-T routing with torch ops (same rule as the kernel: ties to the lower index)."""
+    T = logits.shape[0]
+    E, k = cfg.n_experts, cfg.top_k
+    dev = logits.device
+    if cfg.router_scoring == "softmax":
+        scores = torch.softmax(logits.float(), -1)
+        sel = scores
+    else:
+        scores = torch.sigmoid(logits.float())
+        sel = scores + (bias if bias is not None else 0)
+    if cfg.n_groups > 1:
+        gs = sel.view(T, cfg.n_groups, E // cfg.n_groups)
+        gscore = gs.topk(2, -1).values.sum(-1) if cfg.router_scoring == "sigmoid" else gs.max(-1).values
+        gi = torch.sort(-gscore, dim=-1, stable=True).indices[:, : cfg.topk_groups]
+        gm = torch.zeros_like(gscore).scatter_(1, gi, 1.0)
+        sel = sel.masked_fill(gm[:, :, None].expand_as(gs).reshape(T, E) == 0, float("-inf"))
+    ids = torch.sort(-sel, dim=-1, stable=True).indices[:, :k]
+    w = torch.gather(scores, -1, ids)
+    if cfg.norm_topk_prob:
+        w = w / w.sum(-1, keepdim=True)
+    w = w * cfg.routed_scaling
+    # pairs sorted by (expert, token); per token choices sorted by expert
+    ids_sorted, order = torch.sort(ids, dim=-1)
+    w_sorted = torch.gather(w, -1, order)
+    flat_e = ids_sorted.reshape(-1)
+    key = flat_e.long() * T + torch.arange(T, device=dev).repeat_interleave(k)
+    perm = torch.argsort(key)
+    counts = torch.bincount(flat_e, minlength=E)
+    mb["tok_off"][0] = 0
+    mb["tok_off"][1:] = torch.cumsum(counts, 0).int()
+    mb["tok_idx"].copy_((perm // k).int())
+    mb["pair_w"].copy_(w_sorted.reshape(-1)[perm])
+    pair_of = torch.empty(T * k, dtype=torch.int32, device=dev)
+    pair_of[perm] = torch.arange(T * k, device=dev, dtype=torch.int32)
+    mb["pair_of"].copy_(pair_of.view(T, k))
+    mb["topk_ids"].copy_(ids.int())
+    mb["topk_w"].copy_(w)

@@ -1,0 +1,77 @@
+"""CPU oracle of the device sampler (csrc/cuda/sampler.cu): same Philox4x32-10 draw
+contract, same fixed-point inverse-CDF selection, same top-k/top-p thresholds."""
+from __future__ import annotations
+
+import math
+
+import torch
+
+M0, M1 = 0xD2511F53, 0xCD9E8D57
+W0, W1 = 0x9E3779B9, 0xBB67AE85
+MASK = 0xFFFFFFFF
+
+
+def philox4x32_10(ctr: list[int], k0: int, k1: int) -> list[int]:
+    """Philox4x32-10 from Salmon et al., SC'11 (pure Python)."""
+    c = list(ctr)
+    for r in range(10):
+        if r:
+            k0 = (k0 + W0) & MASK
+            k1 = (k1 + W1) & MASK
+        p0 = M0 * c[0]
+        p1 = M1 * c[2]
+        hi0, lo0 = p0 >> 32, p0 & MASK
+        hi1, lo1 = p1 >> 32, p1 & MASK
+        c = [hi1 ^ c[1] ^ k0, lo1, hi0 ^ c[3] ^ k1, lo0]
+    return c
+
+
+def philox_draw(seed: int, stream: int, counter: int) -> int:
+    seed &= (1 << 64) - 1
+    stream &= (1 << 64) - 1
+    counter &= (1 << 64) - 1
+    c = philox4x32_10([counter & MASK, counter >> 32, stream & MASK, stream >> 32], seed & MASK, seed >> 32)
+    return c[0]
+
+
+def sample_row(logits: torch.Tensor, temperature: float, top_k: int, top_p: float, seed: int, stream: int,
+               counter: int) -> tuple[int, int]:
+    """Returns (token, new_counter)."""
+    lg = logits.double() if False else logits.float()
+    if not temperature > 0:
+        return int(torch.argmax(lg).item()), counter
+    z = lg / temperature
+    mx = z.max()
+    V = z.numel()
+    keep = torch.ones(V, dtype=torch.bool)
+    if 0 < top_k < V:
+        kth = torch.sort(z, descending=True).values[top_k - 1]
+        keep &= z >= kth
+    mass = torch.where(keep, torch.floor(torch.exp(z - mx).double() * 4294967296.0), torch.zeros(V, dtype=torch.float64))
+    mass = mass.to(torch.int64)
+    if top_p < 1.0:
+        total = int(mass.sum())
+        need = int(top_p * total)
+        vals = torch.sort(mass, descending=True).values
+        cum = torch.cumsum(vals, 0)
+        idx = int(torch.searchsorted(cum, torch.tensor(need)).item())
+        idx = min(idx, V - 1)
+        floor = int(vals[idx])
+        mass = torch.where(mass >= floor, mass, torch.zeros_like(mass))
+    total = int(mass.sum())
+    x0 = philox_draw(seed, stream, counter)
+    target = (x0 * total) >> 32
+    cum = torch.cumsum(mass, 0)
+    tok = int(torch.searchsorted(cum, torch.tensor(target), right=True).item())
+    return min(tok, V - 1), counter + 1
+
+
+def sample_ref(logits, temperature, top_k, top_p, seed, stream, counter) -> torch.Tensor:
+    T = logits.shape[0]
+    out = torch.empty(T, dtype=torch.int32)
+    for t in range(T):
+        tok, c = sample_row(logits[t], float(temperature[t]), int(top_k[t]), float(top_p[t]), int(seed[t]),
+                            int(stream[t]), int(counter[t]))
+        out[t] = tok
+        counter[t] = c
+    return out

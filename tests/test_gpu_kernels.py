@@ -1,0 +1,213 @@
+"""sm_100a kernels against plain f32 PyTorch references of the same op."""
+import math
+
+import pytest
+import torch
+
+from syntropy_b200 import ops
+from syntropy_b200._ext import ext
+from syntropy_b200.formats.q4 import Q4Weight, dequant_rows_ref
+from syntropy_b200.models.config import get_config
+from syntropy_b200.runtime.sampling_ref import sample_ref
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
+
+
+def test_q4_quantize_matches_cpu_oracle(cuda):
+    w = torch.randn(128, 512) * 0.02
+    rows_cpu = ext().q4_quantize_rows_cpu(w)
+    q = Q4Weight.quantize(w.to(cuda))
+    assert torch.equal(q.to_rows().cpu(), rows_cpu)
+    deq = q.dequant().float().cpu()
+    ref = dequant_rows_ref(rows_cpu, 128, 512)
+    assert torch.allclose(deq, ref.to(torch.bfloat16).float(), atol=0, rtol=0)
+    q2 = Q4Weight.from_rows(rows_cpu.to(cuda), 128, 512)
+    assert torch.equal(q2.qw, q.qw) and torch.equal(q2.sm, q.sm)
+
+
+@pytest.mark.parametrize("T,N,K", [(1, 256, 512), (5, 512, 1024), (8, 4096, 4096), (32, 1024, 4096),
+                                   (64, 256, 1536), (3, 9216, 4096)])
+def test_q4_gemv_dense(cuda, T, N, K):
+    torch.manual_seed(0)
+    w = torch.randn(N, K, device=cuda) * 0.02
+    q = Q4Weight.quantize(w)
+    wd = ext().q4t_dequant(q.qw, q.sm, N, K)  # bf16 (exact for these magnitudes? compare vs f32 dequant below)
+    rows = q.to_rows().cpu()
+    wf = dequant_rows_ref(rows, N, K).to(cuda)
+    x = (torch.randn(T, K, device=cuda)).to(torch.bfloat16)
+    out = torch.empty(T, N, dtype=torch.bfloat16, device=cuda)
+    ops.linear(x, q, out, ops.GEMV_STORE)
+    ref = x.float() @ wf.t()
+    assert _rel(out, ref) < 4e-3
+    # f32 residual epilogue
+    res = torch.randn(T, N, device=cuda)
+    r0 = res.clone()
+    ops.linear(x, q, res, ops.GEMV_ADD_F32)
+    assert _rel(res - r0, ref) < 1e-4
+    del wd
+
+
+def test_q4_gemv_grouped_swiglu_and_scaled(cuda):
+    torch.manual_seed(1)
+    E, f, H, T, k = 8, 256, 512, 6, 3
+    g = torch.randn(E, f, H, device=cuda) * 0.02
+    u = torch.randn(E, f, H, device=cuda) * 0.02
+    d = torch.randn(E, H, f, device=cuda) * 0.02
+    from syntropy_b200.models.transformer import ExpertBank
+    gu = ExpertBank(E, 2 * f, H)
+    dn = ExpertBank(E, H, f)
+    gu.qw = torch.zeros(E, 2 * f * H // 8, dtype=torch.int32, device=cuda)
+    gu.sm = torch.zeros(E, 2 * f * H // 16, dtype=torch.float16, device=cuda)
+    dn.qw = torch.zeros(E, H * f // 8, dtype=torch.int32, device=cuda)
+    dn.sm = torch.zeros(E, H * f // 16, dtype=torch.float16, device=cuda)
+    for e in range(E):
+        q = Q4Weight.quantize(ops.interleave_gate_up(g[e], u[e]))
+        gu.qw[e].copy_(q.qw); gu.sm[e].copy_(q.sm)
+        q = Q4Weight.quantize(d[e])
+        dn.qw[e].copy_(q.qw); dn.sm[e].copy_(q.sm)
+    gu.build_ptrs(); dn.build_ptrs()
+    cfg = get_config("tiny-qwen-moe").replace(n_experts=E, top_k=k, hidden=H, moe_ffn=f)
+    h = torch.randn(T, H, device=cuda).to(torch.bfloat16)
+    logits = torch.randn(T, E, device=cuda)
+    bufs = {"topk_ids": torch.zeros(T, k, dtype=torch.int32, device=cuda),
+            "topk_w": torch.zeros(T, k, device=cuda), "tok_off": torch.zeros(E + 1, dtype=torch.int32, device=cuda),
+            "tok_idx": torch.zeros(T * k, dtype=torch.int32, device=cuda), "pair_w": torch.zeros(T * k, device=cuda),
+            "pair_of": torch.zeros(T, k, dtype=torch.int32, device=cuda), "pred_mask": None}
+    ops.moe_topk(logits, cfg, None, False, bufs)
+    mid = torch.empty(T * k, f, dtype=torch.bfloat16, device=cuda)
+    ops.linear_grouped(h, gu, bufs["tok_off"], bufs["tok_idx"], mid, ops.GEMV_SWIGLU, qw_ptrs=gu.qw_ptrs,
+                       sm_ptrs=gu.sm_ptrs)
+    yp = torch.empty(T * k, H, device=cuda)
+    ops.linear_grouped(mid, dn, bufs["tok_off"], None, yp, ops.GEMV_SCALED_F32, route_w=bufs["pair_w"],
+                       qw_ptrs=dn.qw_ptrs, sm_ptrs=dn.sm_ptrs)
+    x = torch.zeros(T, H, device=cuda)
+    ops.moe_combine_rmsnorm(x, yp, bufs["pair_of"], None, None, None, 1e-6)
+    # reference in f32 with dequantised weights
+    ref = torch.zeros(T, H, device=cuda)
+    for t in range(T):
+        for j in range(k):
+            e = int(bufs["topk_ids"][t, j])
+            wg = gu.weight(e).float()
+            a = ops.swiglu_interleaved_ref(h[t:t + 1].float() @ wg.t())
+            ref[t] += bufs["topk_w"][t, j] * (a.to(torch.bfloat16).float() @ dn.weight(e).float().t())[0]
+    assert _rel(x, ref) < 1e-2
+
+
+def test_moe_topk_matches_cpu(cuda):
+    torch.manual_seed(2)
+    cfg = get_config("qwen3-235b-a22b")
+    E, k, T = cfg.n_experts, cfg.top_k, 32
+    logits = torch.randn(T, 2 * E)
+
+    def bufs(dev):
+        return {"topk_ids": torch.zeros(T, k, dtype=torch.int32, device=dev),
+                "topk_w": torch.zeros(T, k, device=dev), "tok_off": torch.zeros(E + 1, dtype=torch.int32, device=dev),
+                "tok_idx": torch.zeros(T * k, dtype=torch.int32, device=dev), "pair_w": torch.zeros(T * k, device=dev),
+                "pair_of": torch.zeros(T, k, dtype=torch.int32, device=dev),
+                "pred_mask": torch.zeros(E, dtype=torch.int32, device=dev)}
+
+    bc, bg = bufs("cpu"), bufs(cuda)
+    ops.moe_topk(logits[:, :E].contiguous(), cfg, None, False, bc)
+    ops.moe_topk(logits.to(cuda), cfg, None, True, bg)
+    for key in ("topk_ids", "tok_off", "tok_idx", "pair_of"):
+        assert torch.equal(bc[key], bg[key].cpu()), key
+    assert torch.allclose(bc["topk_w"], bg["topk_w"].cpu(), rtol=1e-5, atol=1e-6)
+    # prediction mask = union of the next layer's top-k
+    pred = torch.zeros(E, dtype=torch.int32)
+    pred[torch.sort(-torch.softmax(logits[:, E:], -1), dim=-1, stable=True).indices[:, :k].reshape(-1)] = 1
+    assert torch.equal(pred, bg["pred_mask"].cpu())
+
+
+def test_deepseek_group_routing_matches_cpu(cuda):
+    torch.manual_seed(3)
+    cfg = get_config("deepseek-v3")
+    E, k, T = cfg.n_experts, cfg.top_k, 16
+    logits = torch.randn(T, E)
+    bias = torch.randn(E) * 0.1
+
+    def bufs(dev):
+        return {"topk_ids": torch.zeros(T, k, dtype=torch.int32, device=dev),
+                "topk_w": torch.zeros(T, k, device=dev), "tok_off": torch.zeros(E + 1, dtype=torch.int32, device=dev),
+                "tok_idx": torch.zeros(T * k, dtype=torch.int32, device=dev), "pair_w": torch.zeros(T * k, device=dev),
+                "pair_of": torch.zeros(T, k, dtype=torch.int32, device=dev), "pred_mask": None}
+
+    bc, bg = bufs("cpu"), bufs(cuda)
+    ops.moe_topk(logits, cfg, bias, False, bc)
+    ops.moe_topk(logits.to(cuda), cfg, bias.to(cuda), False, bg)
+    assert torch.equal(torch.sort(bc["topk_ids"], -1).values, torch.sort(bg["topk_ids"].cpu(), -1).values)
+    assert torch.allclose(bc["topk_w"].sort(-1).values, bg["topk_w"].cpu().sort(-1).values, rtol=1e-4, atol=1e-6)
+
+
+@pytest.mark.parametrize("G,D,ctx", [(16, 128, [1, 17, 300, 1025]), (4, 128, [33, 64, 5]), (8, 128, [700])])
+def test_attn_decode(cuda, G, D, ctx):
+    torch.manual_seed(4)
+    Hkv = 2
+    Hq = G * Hkv
+    T = len(ctx)
+    bs = 16
+    maxb = max((c + bs - 1) // bs for c in ctx)
+    nblocks = T * maxb + 1
+    kc = torch.randn(nblocks, Hkv, bs, D, device=cuda).to(torch.bfloat16)
+    vc = torch.randn(nblocks, Hkv, bs, D, device=cuda).to(torch.bfloat16)
+    perm = torch.randperm(nblocks - 1) + 1
+    bt = perm[: T * maxb].view(T, maxb).to(torch.int32).to(cuda)
+    q = torch.randn(T, Hq, D, device=cuda).to(torch.bfloat16)
+    cl = torch.tensor(ctx, dtype=torch.int32, device=cuda)
+    out = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=cuda)
+    pps = 4
+    ns = (maxb + pps - 1) // pps
+    po = torch.empty(T * Hkv * ns * 16 * D, device=cuda)
+    pml = torch.empty(T * Hkv * ns * 16 * 2, device=cuda)
+    ops.attn_decode(q, kc, vc, bt, cl, out, 1 / math.sqrt(D), po, pml, pps)
+    ref = torch.empty(T, Hq, D)
+    ops.attn_decode(q.cpu().float(), kc.cpu().float(), vc.cpu().float(), bt.cpu(), cl.cpu(), ref, 1 / math.sqrt(D))
+    assert _rel(out.cpu(), ref) < 1e-2
+
+
+def test_qk_rope_kv_write(cuda):
+    torch.manual_seed(5)
+    Hq, Hkv, D, T = 8, 2, 128, 7
+    from syntropy_b200.models.reference import rope_table
+    cos, sin = rope_table(D, 1e6, 4096)
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D).to(torch.bfloat16)
+    pos = torch.tensor([0, 1, 5, 100, 2000, 3, 4095], dtype=torch.int32)
+    slot = torch.tensor([16, 17, 40, 3, 90, -1, 5], dtype=torch.int64)
+    qn, kn = torch.rand(D) + 0.5, torch.rand(D) + 0.5
+    kc = torch.zeros(8, Hkv, 16, D)
+    vc = torch.zeros(8, Hkv, 16, D)
+    qo = torch.zeros(T, Hq, D)
+    ops.qk_rope_kv_write(qkv.float(), Hq, Hkv, D, qn, kn, 1e-6, pos, cos, sin, slot, qo, kc, vc)
+    kg, vg = kc.to(torch.bfloat16).to(cuda) * 0, vc.to(torch.bfloat16).to(cuda) * 0
+    qg = torch.zeros(T, Hq, D, dtype=torch.bfloat16, device=cuda)
+    ops.qk_rope_kv_write(qkv.to(cuda), Hq, Hkv, D, qn.to(cuda), kn.to(cuda), 1e-6, pos.to(cuda), cos.to(cuda),
+                         sin.to(cuda), slot.to(cuda), qg, kg, vg)
+    assert _rel(qg.cpu(), qo) < 5e-3
+    assert _rel(kg.cpu(), kc) < 5e-3
+    assert _rel(vg.cpu(), vc) < 5e-3
+
+
+def test_sampler(cuda):
+    torch.manual_seed(6)
+    T, V = 16, 151936
+    logits = torch.randn(T, V) * 3
+    # Philox device == host
+    assert torch.equal(ext().philox(123, 7, 1000, 4096, logits.to(cuda)).cpu(), ext().philox_cpu(123, 7, 1000, 4096))
+    temp = torch.tensor([0.0] * 4 + [1.0] * 12)
+    topk = torch.tensor([0] * 8 + [50] * 4 + [0] * 4, dtype=torch.int32)
+    topp = torch.tensor([1.0] * 12 + [0.9] * 4)
+    seed = torch.arange(T, dtype=torch.int64) * 7919
+    stream = torch.arange(T, dtype=torch.int64)
+    ctr = torch.zeros(T, dtype=torch.int64)
+    out = torch.empty(T, dtype=torch.int32, device=cuda)
+    ctr_g = ctr.to(cuda)
+    ops.sample(logits.to(cuda), temp.to(cuda), topk.to(cuda), topp.to(cuda), seed.to(cuda), stream.to(cuda), ctr_g,
+               out)
+    ref = sample_ref(logits, temp, topk, topp, seed, stream, ctr.clone())
+    assert torch.equal(out.cpu()[:4], torch.argmax(logits[:4], -1).int())
+    agree = (out.cpu() == ref).float().mean().item()
+    assert agree >= 0.9, (out.cpu(), ref)
+    assert torch.equal(ctr_g.cpu(), (temp > 0).long())
