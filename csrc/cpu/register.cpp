@@ -23,6 +23,15 @@ void register_all(pybind11::module& m) {
   m.def("sample", &sample);
   m.def("philox", &philox);
   m.def("philox_cpu", &philox_cpu);
+  m.def("symm_alloc", &symm_alloc);
+  m.def("symm_open", &symm_open);
+  m.def("symm_close", &symm_close);
+  m.def("p2p_access", &p2p_access);
+  m.def("ep_step_begin", &ep_step_begin);
+  m.def("ep_dispatch", &ep_dispatch);
+  m.def("ep_build", &ep_build);
+  m.def("ep_combine", &ep_combine);
+  m.def("q4_gemv_ep", &q4_gemv_ep);
 }
 
 }  // namespace syn

@@ -18,6 +18,7 @@
 //    order (deterministic); one CTA per (16-row tile, expert).
 #include "common.cuh"
 #include "syn/q4.h"
+#include "sync.cuh"
 
 namespace syn {
 
@@ -29,6 +30,8 @@ enum GemvMode : int {
   GEMV_SWIGLU = 1,       // rows interleaved in 8-row gate/up chunks -> out_bf16[p][n/2]
   GEMV_SCALED_F32 = 2,   // out_f32[p][n] = route_w[p] * y
   GEMV_ADD_F32 = 3,      // out_f32[p][n] += y (residual stream kept in f32)
+  GEMV_SCALED_F32_PTR = 4,  // ((float*)out_ptrs[p])[n] = route_w[p] * y (peer memory allowed)
+  GEMV_STORE_F32 = 5,    // out_f32[p][n] = y (logits)
 };
 
 __global__ void __launch_bounds__(GEMV_WARPS * 32)
@@ -37,7 +40,6 @@ q4_gemv_kernel(GemvArgs a) {
   const int e = blockIdx.y;
   const int p0 = a.tok_off[e];
   const int cnt = a.tok_off[e + 1] - p0;
-  if (cnt <= 0) return;
   const uint4* __restrict__ qw = reinterpret_cast<const uint4*>(a.qw_ptrs[e]);
   const uint2* __restrict__ sm = reinterpret_cast<const uint2*>(a.sm_ptrs[e]);
 
@@ -147,6 +149,10 @@ q4_gemv_kernel(GemvArgs a) {
         reinterpret_cast<float*>(a.out)[(int64_t)p * a.N + n] = a.route_w[p] * v;
       } else if (a.mode == GEMV_ADD_F32) {
         reinterpret_cast<float*>(a.out)[(int64_t)p * a.N + n] += v;
+      } else if (a.mode == GEMV_STORE_F32) {
+        reinterpret_cast<float*>(a.out)[(int64_t)p * a.N + n] = v;
+      } else if (a.mode == GEMV_SCALED_F32_PTR) {
+        reinterpret_cast<float*>(a.out_ptrs[p])[n] = a.route_w[p] * v;
       }
     }
     if (a.mode == GEMV_SWIGLU) {
@@ -168,6 +174,23 @@ q4_gemv_kernel(GemvArgs a) {
       }
     }
     __syncthreads();
+  }
+  if (a.done_ctr != nullptr) {
+    // Completion of the whole grid: every CTA publishes its stores, the last one raises
+    // the peers' flags (counter reset for the next launch before the release).
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned total = gridDim.x * gridDim.y;
+      const unsigned prev = atomicAdd(a.done_ctr, 1u);
+      if (prev == total - 1) {
+        *a.done_ctr = 0u;
+        __threadfence_system();
+        const uint32_t seq = (*a.step_ctr) * (uint32_t)a.n_layers + (uint32_t)a.layer + 1u;
+        for (int q = 0; q < a.sig_n; ++q)
+          st_release_sys(reinterpret_cast<uint32_t*>(a.sig_peers[q] + a.sig_off) + a.sig_rank, seq);
+      }
+    }
   }
 }
 

@@ -38,5 +38,26 @@ void sample(torch::Tensor logits, torch::Tensor temperature, torch::Tensor top_k
 torch::Tensor philox(int64_t seed, int64_t stream, int64_t counter0, int64_t n, torch::Tensor like);
 torch::Tensor philox_cpu(int64_t seed, int64_t stream, int64_t counter0, int64_t n);
 
+std::vector<torch::Tensor> symm_alloc(int64_t nbytes);
+int64_t symm_open(torch::Tensor handle);
+void symm_close(int64_t ptr);
+bool p2p_access(int64_t a, int64_t b);
+void ep_step_begin(torch::Tensor step_ctr);
+void ep_dispatch(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, int64_t H, int64_t k, int64_t E_loc,
+                 std::vector<int64_t> offs, torch::Tensor step_ctr, int64_t n_layers, int64_t layer,
+                 int64_t timeout_ns, torch::Tensor status, torch::Tensor h, torch::Tensor ids, torch::Tensor w);
+void ep_build(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, int64_t H, int64_t k, int64_t E_loc,
+              std::vector<int64_t> offs, torch::Tensor step_ctr, int64_t n_layers, int64_t layer, int64_t timeout_ns,
+              torch::Tensor status, torch::Tensor tok_off, torch::Tensor tok_idx, torch::Tensor pair_w,
+              torch::Tensor pair_dst);
+void ep_combine(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, int64_t H, int64_t k, int64_t E_loc,
+                std::vector<int64_t> offs, torch::Tensor step_ctr, int64_t n_layers, int64_t layer,
+                int64_t timeout_ns, torch::Tensor status, torch::Tensor x, torch::Tensor wn, torch::Tensor hout,
+                double eps);
+void q4_gemv_ep(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
+                torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor out_ptrs, int64_t N, int64_t K,
+                torch::Tensor done_ctr, torch::Tensor peers, int64_t sig_off, int64_t sig_rank,
+                torch::Tensor step_ctr, int64_t n_layers, int64_t layer);
+
 void register_all(pybind11::module& m);
 }  // namespace syn

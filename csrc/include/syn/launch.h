@@ -30,7 +30,34 @@ struct GemvArgs {
   int N, K, ldx;
   int mode;
   int E;
+  // mode 4 (GEMV_SCALED_F32_PTR): row p goes to (float*)out_ptrs[p]
+  const int64_t* out_ptrs;
+  // completion signal (optional): the last CTA stores seq into every peer's flag array
+  unsigned* done_ctr;
+  const int64_t* sig_peers;   // [sig_n] symmetric-region bases
+  int64_t sig_off;            // byte offset of the flag array in the region
+  int sig_n, sig_rank;
+  const uint32_t* step_ctr;
+  int n_layers, layer;
 };
+
+// ---- expert parallelism over NVLink peer memory ----
+struct EpArgs {
+  const int64_t* peers;  // device array [N] of symmetric-region bases (own included)
+  int N, rank, cap, H, k, E_loc;
+  int64_t off_x, off_meta, off_cnt, off_flag_disp, off_comb, off_flag_comb;
+  const uint32_t* step_ctr;
+  int n_layers, layer;
+  uint64_t timeout_ns;
+  int* status;
+};
+cudaError_t launch_ep_step_begin(uint32_t* step_ctr, cudaStream_t s);
+cudaError_t launch_ep_dispatch(const EpArgs& a, const void* h, const int32_t* ids, const float* w, int T,
+                               cudaStream_t s);
+cudaError_t launch_ep_build(const EpArgs& a, int32_t* tok_off, int32_t* tok_idx, float* pair_w, int64_t* pair_dst,
+                            cudaStream_t s);
+cudaError_t launch_ep_combine(const EpArgs& a, float* x, const float* wn, void* hout, float eps, int T,
+                              cudaStream_t s);
 cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s);
 
 // ---- norms, RoPE, KV writes, embedding ----

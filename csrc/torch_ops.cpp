@@ -100,11 +100,20 @@ void q4_gemv(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torc
   a.ldx = (int)x.stride(0);
   a.mode = (int)mode;
   a.E = E;
+  a.out_ptrs = nullptr;
+  a.done_ctr = nullptr;
+  a.sig_peers = nullptr;
+  a.sig_off = 0;
+  a.sig_n = 0;
+  a.sig_rank = 0;
+  a.step_ctr = nullptr;
+  a.n_layers = 0;
+  a.layer = 0;
   if (mode == 0) TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.size(-1) == N, "out bf16 [P, N]");
-  if (mode == 3) TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.size(-1) == N, "out f32 [P, N]");
+  if (mode == 3 || mode == 5) TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.size(-1) == N, "out f32 [P, N]");
   if (mode == 1) TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.size(-1) == N / 2, "out bf16 [P, N/2]");
   if (mode == 2) TORCH_CHECK(a.route_w && out.scalar_type() == torch::kFloat32 && out.size(-1) == N, "mode 2: route_w, fp32 [P, N]");
-  TORCH_CHECK(mode >= 0 && mode <= 3, "q4_gemv: bad mode");
+  TORCH_CHECK(mode >= 0 && mode <= 5 && mode != 4, "q4_gemv: bad mode (mode 4 goes through q4_gemv_ep)");
   const at::cuda::CUDAGuard guard(x.device());
   SYN_CHECK_CUDA(launch_q4_gemv(a, cur_stream()));
 }
@@ -282,6 +291,116 @@ torch::Tensor philox(int64_t seed, int64_t stream, int64_t counter0, int64_t n, 
   SYN_CHECK_CUDA(launch_philox((uint64_t)seed, (uint64_t)stream, (uint64_t)counter0, (int)n,
                                reinterpret_cast<uint32_t*>(out.data_ptr()), cur_stream()));
   return out;
+}
+
+
+static EpArgs make_ep_args(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, int64_t H, int64_t k,
+                           int64_t E_loc, std::vector<int64_t> offs, torch::Tensor step_ctr, int64_t n_layers,
+                           int64_t layer, int64_t timeout_ns, torch::Tensor status) {
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == torch::kInt64 && peers.numel() == N, "peers: cuda int64 [N]");
+  TORCH_CHECK(offs.size() == 6, "6 region offsets");
+  TORCH_CHECK(step_ctr.is_cuda() && step_ctr.scalar_type() == torch::kInt32, "step_ctr cuda int32");
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == torch::kInt32, "status cuda int32");
+  EpArgs a;
+  a.peers = peers.data_ptr<int64_t>();
+  a.N = (int)N;
+  a.rank = (int)rank;
+  a.cap = (int)cap;
+  a.H = (int)H;
+  a.k = (int)k;
+  a.E_loc = (int)E_loc;
+  a.off_x = offs[0];
+  a.off_meta = offs[1];
+  a.off_cnt = offs[2];
+  a.off_flag_disp = offs[3];
+  a.off_comb = offs[4];
+  a.off_flag_comb = offs[5];
+  a.step_ctr = reinterpret_cast<const uint32_t*>(step_ctr.data_ptr());
+  a.n_layers = (int)n_layers;
+  a.layer = (int)layer;
+  a.timeout_ns = (uint64_t)timeout_ns;
+  a.status = status.data_ptr<int32_t>();
+  return a;
+}
+
+void ep_step_begin(torch::Tensor step_ctr) {
+  TORCH_CHECK(step_ctr.is_cuda() && step_ctr.scalar_type() == torch::kInt32, "step_ctr");
+  const at::cuda::CUDAGuard guard(step_ctr.device());
+  SYN_CHECK_CUDA(launch_ep_step_begin(reinterpret_cast<uint32_t*>(step_ctr.data_ptr()), cur_stream()));
+}
+
+void ep_dispatch(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, int64_t H, int64_t k, int64_t E_loc,
+                 std::vector<int64_t> offs, torch::Tensor step_ctr, int64_t n_layers, int64_t layer,
+                 int64_t timeout_ns, torch::Tensor status, torch::Tensor h, torch::Tensor ids, torch::Tensor w) {
+  auto a = make_ep_args(peers, N, rank, cap, H, k, E_loc, offs, step_ctr, n_layers, layer, timeout_ns, status);
+  TORCH_CHECK(h.is_cuda() && h.scalar_type() == torch::kBFloat16 && h.size(1) == H, "h bf16 [T, H]");
+  TORCH_CHECK(h.size(0) <= cap, "ep_dispatch: more local rows than capacity");
+  TORCH_CHECK(ids.scalar_type() == torch::kInt32 && w.scalar_type() == torch::kFloat32, "ids int32, w f32");
+  const at::cuda::CUDAGuard guard(h.device());
+  SYN_CHECK_CUDA(launch_ep_dispatch(a, h.data_ptr(), ids.data_ptr<int32_t>(), w.data_ptr<float>(), (int)h.size(0),
+                                    cur_stream()));
+}
+
+void ep_build(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, int64_t H, int64_t k, int64_t E_loc,
+              std::vector<int64_t> offs, torch::Tensor step_ctr, int64_t n_layers, int64_t layer, int64_t timeout_ns,
+              torch::Tensor status, torch::Tensor tok_off, torch::Tensor tok_idx, torch::Tensor pair_w,
+              torch::Tensor pair_dst) {
+  auto a = make_ep_args(peers, N, rank, cap, H, k, E_loc, offs, step_ctr, n_layers, layer, timeout_ns, status);
+  TORCH_CHECK(tok_off.numel() >= E_loc + 1 && tok_idx.numel() >= N * cap * k && pair_w.numel() >= N * cap * k &&
+                  pair_dst.numel() >= N * cap * k, "ep_build outputs too small");
+  const at::cuda::CUDAGuard guard(tok_off.device());
+  SYN_CHECK_CUDA(launch_ep_build(a, tok_off.data_ptr<int32_t>(), tok_idx.data_ptr<int32_t>(), pair_w.data_ptr<float>(),
+                                 pair_dst.data_ptr<int64_t>(), cur_stream()));
+}
+
+void ep_combine(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, int64_t H, int64_t k, int64_t E_loc,
+                std::vector<int64_t> offs, torch::Tensor step_ctr, int64_t n_layers, int64_t layer,
+                int64_t timeout_ns, torch::Tensor status, torch::Tensor x, torch::Tensor wn, torch::Tensor hout,
+                double eps) {
+  auto a = make_ep_args(peers, N, rank, cap, H, k, E_loc, offs, step_ctr, n_layers, layer, timeout_ns, status);
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kFloat32 && x.size(1) == H, "x f32 [T, H]");
+  const float* wp = fptr_or_null(wn);
+  if (wp) TORCH_CHECK(hout.scalar_type() == torch::kBFloat16 && hout.sizes() == x.sizes(), "hout");
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_ep_combine(a, x.data_ptr<float>(), wp, wp ? hout.data_ptr() : nullptr, (float)eps,
+                                   (int)x.size(0), cur_stream()));
+}
+
+// Grouped GEMV whose epilogue stores row p to out_ptrs[p] (peer memory allowed) and whose
+// last CTA raises flag `sig_rank` in every peer's flag array at byte offset sig_off.
+void q4_gemv_ep(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
+                torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor out_ptrs, int64_t N, int64_t K,
+                torch::Tensor done_ctr, torch::Tensor peers, int64_t sig_off, int64_t sig_rank,
+                torch::Tensor step_ctr, int64_t n_layers, int64_t layer) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x");
+  TORCH_CHECK(N % 16 == 0 && K % 64 == 0 && x.size(1) == K, "q4_gemv_ep shapes");
+  TORCH_CHECK(done_ctr.is_cuda() && done_ctr.scalar_type() == torch::kInt32, "done_ctr cuda int32");
+  GemvArgs a;
+  a.x = x.data_ptr();
+  a.qw_ptrs = qw_ptrs.data_ptr<int64_t>();
+  a.sm_ptrs = sm_ptrs.data_ptr<int64_t>();
+  a.tok_off = tok_off.data_ptr<int32_t>();
+  a.tok_idx = tok_idx.numel() ? tok_idx.data_ptr<int32_t>() : nullptr;
+  a.route_w = route_w.data_ptr<float>();
+  a.res = nullptr;
+  a.out = nullptr;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.ldx = (int)x.stride(0);
+  a.mode = 4;
+  a.E = (int)qw_ptrs.numel();
+  a.out_ptrs = out_ptrs.data_ptr<int64_t>();
+  a.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr());
+  a.sig_peers = peers.data_ptr<int64_t>();
+  a.sig_off = sig_off;
+  a.sig_n = (int)peers.numel();
+  a.sig_rank = (int)sig_rank;
+  a.step_ctr = reinterpret_cast<const uint32_t*>(step_ctr.data_ptr());
+  a.n_layers = (int)n_layers;
+  a.layer = (int)layer;
+  TORCH_CHECK(tok_off.numel() == a.E + 1, "tok_off E+1");
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_q4_gemv(a, cur_stream()));
 }
 
 }  // namespace syn

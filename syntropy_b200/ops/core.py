@@ -13,7 +13,7 @@ __all__ = [
     "GEMV_STORE", "GEMV_SWIGLU", "GEMV_SCALED_F32", "GEMV_ADD_F32",
     "rms_norm", "embed", "linear", "linear_grouped", "qk_rope_kv_write", "attn_decode",
     "attn_prefill", "router_logits", "moe_topk", "moe_combine_rmsnorm", "argmax", "sample",
-    "swiglu_interleaved_ref", "interleave_gate_up", "count_launches",
+    "swiglu_interleaved_ref", "interleave_gate_up", "count_launches", "DECODE_ROWS_MAX",
 ]
 
 GEMV_STORE, GEMV_SWIGLU, GEMV_SCALED_F32, GEMV_ADD_F32 = 0, 1, 2, 3
@@ -97,6 +97,8 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
     if isinstance(W, Q4Weight) and T <= DECODE_ROWS_MAX:
         ptrs = _ptrs(W)
         kmode = {GEMV_STORE: 0, GEMV_SWIGLU: 1, GEMV_ADD_F32: 3}[mode]
+        if kmode == 0 and out.dtype == torch.float32:
+            kmode = 5
         ext().q4_gemv(x, ptrs[0], ptrs[1], _identity_off(T, x.device), _EMPTY_I32(x.device), _EMPTY_F32(x.device),
                       _EMPTY_BF16(x.device), out, W.N, W.K, kmode)
         _launched()
