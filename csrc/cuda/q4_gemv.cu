@@ -22,8 +22,6 @@
 
 namespace syn {
 
-constexpr int GEMV_WARPS = 8;
-constexpr int GEMV_NT = 4;  // up to 4 n-tiles of 8 tokens per pass
 
 enum GemvMode : int {
   GEMV_STORE_BF16 = 0,   // out_bf16[p][n]
@@ -34,146 +32,202 @@ enum GemvMode : int {
   GEMV_STORE_F32 = 5,    // out_f32[p][n] = y (logits)
 };
 
-__global__ void __launch_bounds__(GEMV_WARPS * 32)
-q4_gemv_kernel(GemvArgs a) {
-  const int tile = blockIdx.x;
+
+__device__ __forceinline__ uint4 ld_stream_v4(const uint4* p) { return __ldcs(p); }
+__device__ __forceinline__ uint2 ld_stream_v2(const uint2* p) { return __ldcs(p); }
+
+// Epilogue for one (row n, token j) value.  `p` is the pair index.
+__device__ __forceinline__ void gemv_store(const GemvArgs& a, int p, int n, float v) {
+  switch (a.mode) {
+    case GEMV_STORE_BF16:
+      reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)p * a.N + n] = f2bf(v);
+      break;
+    case GEMV_SCALED_F32:
+      reinterpret_cast<float*>(a.out)[(int64_t)p * a.N + n] = a.route_w[p] * v;
+      break;
+    case GEMV_ADD_F32:
+      reinterpret_cast<float*>(a.out)[(int64_t)p * a.N + n] += v;
+      break;
+    case GEMV_STORE_F32:
+      reinterpret_cast<float*>(a.out)[(int64_t)p * a.N + n] = v;
+      break;
+    case GEMV_SCALED_F32_PTR:
+      reinterpret_cast<float*>(a.out_ptrs[p])[n] = a.route_w[p] * v;
+      break;
+    default:
+      break;
+  }
+}
+
+// Warp tile: R 16-row tiles x NT 8-token tiles; KS warps split K (KS == 1: every warp of the
+// 4-warp CTA is an independent tile, no shared memory).  U k-groups (64 columns each) of
+// weights and scales are loaded before any of them is used, so each warp keeps
+// U * R * 528 bytes in flight.
+template <int R, int NT, int KS>
+__global__ void __launch_bounds__(KS == 1 ? 128 : KS * 32)
+q4_gemv2_kernel(GemvArgs a) {
+  constexpr int WARPS = KS == 1 ? 4 : KS;
+  constexpr int U = 4;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
   const int e = blockIdx.y;
   const int p0 = a.tok_off[e];
   const int cnt = a.tok_off[e + 1] - p0;
-  const uint4* __restrict__ qw = reinterpret_cast<const uint4*>(a.qw_ptrs[e]);
-  const uint2* __restrict__ sm = reinterpret_cast<const uint2*>(a.sm_ptrs[e]);
-
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int g = lane >> 2, t = lane & 3;
+  const int n_units = a.N / (16 * R);
+  const int unit = KS == 1 ? blockIdx.x * WARPS + warp : blockIdx.x;
+  const int kw = KS == 1 ? 0 : warp;
   const int KG = a.K >> 6;
+  const bool active = cnt > 0 && unit < n_units;
 
-  __shared__ float red[GEMV_WARPS][GEMV_NT][4][32];
+  extern __shared__ float gsm[];  // KS > 1: [KS][R][NT][4][32]
 
-  const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
-
-  for (int c0 = 0; c0 < cnt; c0 += GEMV_NT * 8) {
-    const int ccount = min(cnt - c0, GEMV_NT * 8);
-    const int ntc = (ccount + 7) >> 3;
-    // Row pointers for the B fragments: token column g of each n-tile.
-    const __nv_bfloat16* xr[GEMV_NT];
+  if (active || KS > 1) {
+    const uint4* __restrict__ qw = reinterpret_cast<const uint4*>(a.qw_ptrs[e]);
+    const uint2* __restrict__ sm = reinterpret_cast<const uint2*>(a.sm_ptrs[e]);
     const __nv_bfloat16* xbase = reinterpret_cast<const __nv_bfloat16*>(a.x);
+    const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
+    const int nchunks = active ? (cnt + NT * 8 - 1) / (NT * 8) : 0;
+    for (int ch = 0; ch < nchunks; ++ch) {
+      const int c0 = ch * NT * 8;
+      const int ccount = min(cnt - c0, NT * 8);
+      const int ntc = (ccount + 7) >> 3;
+      const __nv_bfloat16* xr[NT];
 #pragma unroll
-    for (int nt = 0; nt < GEMV_NT; ++nt) {
-      int j = min(nt * 8 + g, ccount - 1);
-      int p = p0 + c0 + j;
-      int row = a.tok_idx ? a.tok_idx[p] : p;
-      xr[nt] = xbase + (int64_t)row * a.ldx + 2 * t;
-    }
-    float acc[GEMV_NT][4];
+      for (int nt = 0; nt < NT; ++nt) {
+        const int j = min(nt * 8 + g, ccount - 1);
+        const int pp = p0 + c0 + j;
+        const int row = a.tok_idx ? a.tok_idx[pp] : pp;
+        xr[nt] = xbase + (int64_t)row * a.ldx + 2 * t;
+      }
+      float acc[R][NT][4];
 #pragma unroll
-    for (int nt = 0; nt < GEMV_NT; ++nt)
+      for (int r = 0; r < R; ++r)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[r][nt][i] = 0.f;
 
-    const uint4* qbase = qw + (int64_t)tile * KG * 32 + lane;
-    const uint2* sbase = sm + (int64_t)tile * KG * 16;
-
-#pragma unroll 2
-    for (int kg = warp; kg < KG; kg += GEMV_WARPS) {
-      const uint4 q = ldg_stream(qbase + (int64_t)kg * 32);
-      const uint2 s_lo = __ldg(sbase + (int64_t)kg * 16 + g);      // row g: (d0,m0),(d1,m1)
-      const uint2 s_hi = __ldg(sbase + (int64_t)kg * 16 + g + 8);  // row g+8
-      const uint32_t qwords[4] = {q.x, q.y, q.z, q.w};
+      for (int kb = kw; kb < KG; kb += KS * U) {
+        uint4 q[U][R];
+        uint2 slo[U][R], shi[U][R];
 #pragma unroll
-      for (int b = 0; b < 2; ++b) {
-        float blk[GEMV_NT][4], xs[GEMV_NT][4];
+        for (int u = 0; u < U; ++u) {
+          const int kg = kb + u * KS;
+          if (kg < KG) {
 #pragma unroll
-        for (int nt = 0; nt < GEMV_NT; ++nt)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) { blk[nt][i] = 0.f; xs[nt][i] = 0.f; }
-#pragma unroll
-        for (int s = 0; s < 2; ++s) {
-          const uint32_t w = qwords[b * 2 + s];
-          uint32_t af[4];
-          af[0] = lop3_and_or(w, 0x000F000Fu, 0x43004300u);
-          af[1] = lop3_and_or(w >> 4, 0x000F000Fu, 0x43004300u);
-          af[2] = lop3_and_or(w >> 8, 0x000F000Fu, 0x43004300u);
-          af[3] = lop3_and_or(w >> 12, 0x000F000Fu, 0x43004300u);
-          const int k0 = kg * 64 + b * 32 + s * 16;
-#pragma unroll
-          for (int nt = 0; nt < GEMV_NT; ++nt) {
-            if (nt < ntc) {
-              uint32_t bf[2];
-              bf[0] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0));
-              bf[1] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0 + 8));
-              mma_bf16_16816(blk[nt], af, bf, blk[nt]);
-              mma_bf16_16816(xs[nt], ones, bf, xs[nt]);
+            for (int r = 0; r < R; ++r) {
+              const int64_t tk = (int64_t)(unit * R + r) * KG + kg;
+              q[u][r] = ld_stream_v4(qw + tk * 32 + lane);
+              slo[u][r] = ld_stream_v2(sm + tk * 16 + g);
+              shi[u][r] = ld_stream_v2(sm + tk * 16 + g + 8);
             }
           }
         }
-        const half2 dm_lo = *reinterpret_cast<const half2*>(b ? &s_lo.y : &s_lo.x);
-        const half2 dm_hi = *reinterpret_cast<const half2*>(b ? &s_hi.y : &s_hi.x);
-        const float d_lo = __low2float(dm_lo), d_hi = __low2float(dm_hi);
-        const float m_lo = fmaf(-128.f, d_lo, __high2float(dm_lo));
-        const float m_hi = fmaf(-128.f, d_hi, __high2float(dm_hi));
 #pragma unroll
-        for (int nt = 0; nt < GEMV_NT; ++nt) {
-          if (nt < ntc) {
-            acc[nt][0] += fmaf(d_lo, blk[nt][0], m_lo * xs[nt][0]);
-            acc[nt][1] += fmaf(d_lo, blk[nt][1], m_lo * xs[nt][1]);
-            acc[nt][2] += fmaf(d_hi, blk[nt][2], m_hi * xs[nt][2]);
-            acc[nt][3] += fmaf(d_hi, blk[nt][3], m_hi * xs[nt][3]);
+        for (int u = 0; u < U; ++u) {
+          const int kg = kb + u * KS;
+          if (kg >= KG) break;
+#pragma unroll
+          for (int b = 0; b < 2; ++b) {
+            uint32_t af[R][2][4];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+              const uint32_t w0 = b ? q[u][r].z : q[u][r].x;
+              const uint32_t w1 = b ? q[u][r].w : q[u][r].y;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                af[r][0][j] = lop3_and_or(w0 >> (4 * j), 0x000F000Fu, 0x43004300u);
+                af[r][1][j] = lop3_and_or(w1 >> (4 * j), 0x000F000Fu, 0x43004300u);
+              }
+            }
+            float dlo[R], dhi[R], mlo[R], mhi[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+              const uint32_t vlo = b ? slo[u][r].y : slo[u][r].x;
+              const uint32_t vhi = b ? shi[u][r].y : shi[u][r].x;
+              const half2 hl = *reinterpret_cast<const half2*>(&vlo);
+              const half2 hh = *reinterpret_cast<const half2*>(&vhi);
+              dlo[r] = __low2float(hl);
+              dhi[r] = __low2float(hh);
+              mlo[r] = fmaf(-128.f, dlo[r], __high2float(hl));
+              mhi[r] = fmaf(-128.f, dhi[r], __high2float(hh));
+            }
+            const int k0 = kg * 64 + b * 32;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              if (nt < ntc) {
+                uint32_t bf[2][2];
+                bf[0][0] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0));
+                bf[0][1] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0 + 8));
+                bf[1][0] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0 + 16));
+                bf[1][1] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0 + 24));
+                float xs[4] = {0.f, 0.f, 0.f, 0.f};
+                mma_bf16_16816(xs, ones, bf[0], xs);
+                mma_bf16_16816(xs, ones, bf[1], xs);
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                  float blk[4] = {0.f, 0.f, 0.f, 0.f};
+                  mma_bf16_16816(blk, af[r][0], bf[0], blk);
+                  mma_bf16_16816(blk, af[r][1], bf[1], blk);
+                  acc[r][nt][0] += fmaf(dlo[r], blk[0], mlo[r] * xs[0]);
+                  acc[r][nt][1] += fmaf(dlo[r], blk[1], mlo[r] * xs[1]);
+                  acc[r][nt][2] += fmaf(dhi[r], blk[2], mhi[r] * xs[2]);
+                  acc[r][nt][3] += fmaf(dhi[r], blk[3], mhi[r] * xs[3]);
+                }
+              }
+            }
+          }
+        }
+      }
+
+      if (KS > 1) {
+        // split-K reduction across the CTA's warps in a fixed order
+        float* red = gsm;
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) red[(((warp * R + r) * NT + nt) * 4 + i) * 32 + lane] = acc[r][nt][i];
+        __syncthreads();
+        if (warp == 0) {
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                float v = 0.f;
+                for (int w = 0; w < KS; ++w) v += red[(((w * R + r) * NT + nt) * 4 + i) * 32 + lane];
+                acc[r][nt][i] = v;
+              }
+        }
+        __syncthreads();
+        if (warp != 0) continue;
+      }
+      // Epilogue straight from the accumulator fragments:
+      // acc[r][nt][0]: row g, token 2t; [1]: row g, token 2t+1; [2], [3]: row g+8.
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int tile = unit * R + r;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const int j = nt * 8 + 2 * t + hf;
+            if (j >= ccount) continue;
+            const int p = p0 + c0 + j;
+            if (a.mode == GEMV_SWIGLU) {
+              const float gv = acc[r][nt][hf], uv = acc[r][nt][2 + hf];
+              reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)p * (a.N / 2) + tile * 8 + g] = f2bf(silu(gv) * uv);
+            } else {
+              gemv_store(a, p, tile * 16 + g, acc[r][nt][hf]);
+              gemv_store(a, p, tile * 16 + g + 8, acc[r][nt][2 + hf]);
+            }
           }
         }
       }
     }
-    // Split-K reduction across warps (fixed order).
-#pragma unroll
-    for (int nt = 0; nt < GEMV_NT; ++nt)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) red[warp][nt][i][lane] = acc[nt][i];
-    __syncthreads();
-    // 16 rows x (ntc*8) tokens; thread -> (row r, token j)
-    if (a.mode != GEMV_SWIGLU)
-    for (int idx = threadIdx.x; idx < 16 * ntc * 8; idx += blockDim.x) {
-      const int r = idx & 15;
-      const int j = idx >> 4;  // token inside this chunk
-      if (j >= ccount) continue;
-      const int nt = j >> 3, jj = j & 7;
-      // Fragment position of (row r, token jj): lane = (r%8)*4 + jj/2, reg = (r/8)*2 + jj%2
-      const int ln = (r & 7) * 4 + (jj >> 1);
-      const int rg = (r >> 3) * 2 + (jj & 1);
-      float v = 0.f;
-#pragma unroll
-      for (int w = 0; w < GEMV_WARPS; ++w) v += red[w][nt][rg][ln];
-      const int p = p0 + c0 + j;
-      const int n = tile * 16 + r;
-      if (a.mode == GEMV_STORE_BF16) {
-        reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)p * a.N + n] = f2bf(v);
-      } else if (a.mode == GEMV_SCALED_F32) {
-        reinterpret_cast<float*>(a.out)[(int64_t)p * a.N + n] = a.route_w[p] * v;
-      } else if (a.mode == GEMV_ADD_F32) {
-        reinterpret_cast<float*>(a.out)[(int64_t)p * a.N + n] += v;
-      } else if (a.mode == GEMV_STORE_F32) {
-        reinterpret_cast<float*>(a.out)[(int64_t)p * a.N + n] = v;
-      } else if (a.mode == GEMV_SCALED_F32_PTR) {
-        reinterpret_cast<float*>(a.out_ptrs[p])[n] = a.route_w[p] * v;
-      }
-    }
-    if (a.mode == GEMV_SWIGLU) {
-      // Each (feature f, token j): gate = row f, up = row f + 8 of this tile.
-      for (int idx = threadIdx.x; idx < 8 * ntc * 8; idx += blockDim.x) {
-        const int f = idx & 7;
-        const int j = idx >> 3;
-        if (j >= ccount) continue;
-        const int nt = j >> 3, jj = j & 7;
-        const int ln = f * 4 + (jj >> 1);
-        float gv = 0.f, uv = 0.f;
-#pragma unroll
-        for (int w = 0; w < GEMV_WARPS; ++w) {
-          gv += red[w][nt][(jj & 1)][ln];
-          uv += red[w][nt][2 + (jj & 1)][ln];
-        }
-        const int p = p0 + c0 + j;
-        reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)p * (a.N / 2) + tile * 8 + f] = f2bf(silu(gv) * uv);
-      }
-    }
-    __syncthreads();
   }
   if (a.done_ctr != nullptr) {
     // Completion of the whole grid: every CTA publishes its stores, the last one raises
@@ -194,10 +248,37 @@ q4_gemv_kernel(GemvArgs a) {
   }
 }
 
-cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {
-  dim3 grid((unsigned)(a.N / 16), (unsigned)a.E);
-  q4_gemv_kernel<<<grid, GEMV_WARPS * 32, 0, s>>>(a);
+template <int R, int NT, int KS>
+static cudaError_t launch_v2(const GemvArgs& a, cudaStream_t s) {
+  constexpr int WARPS = KS == 1 ? 4 : KS;
+  const int units = a.N / (16 * R);
+  const int gx = KS == 1 ? (units + WARPS - 1) / WARPS : units;
+  const size_t smem = KS > 1 ? (size_t)KS * R * NT * 4 * 32 * sizeof(float) : 0;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(q4_gemv2_kernel<R, NT, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  dim3 grid((unsigned)gx, (unsigned)a.E);
+  q4_gemv2_kernel<R, NT, KS><<<grid, WARPS * 32, smem, s>>>(a);
   return cudaGetLastError();
+}
+
+cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {
+  // Tile shape: NT from the caller's bound on rows per expert; two row tiles per warp when
+  // several token tiles share them; split K across warps only when there are too few
+  // (expert, row-tile) units to keep ~4 warps per SM scheduler busy.
+  const int nt = a.nt_hint <= 1 ? 1 : (a.nt_hint <= 2 ? 2 : 4);
+  const int R = (nt >= 2 && a.N % 32 == 0) ? 2 : 1;
+  const long units = (long)(a.N / (16 * R)) * a.E_active_hint;
+  const bool split = units < 148L * 16;
+  if (R == 1) {
+    if (nt == 1) return split ? launch_v2<1, 1, 8>(a, s) : launch_v2<1, 1, 1>(a, s);
+    if (nt == 2) return split ? launch_v2<1, 2, 8>(a, s) : launch_v2<1, 2, 1>(a, s);
+    return split ? launch_v2<1, 4, 8>(a, s) : launch_v2<1, 4, 1>(a, s);
+  }
+  if (nt == 2) return split ? launch_v2<2, 2, 8>(a, s) : launch_v2<2, 2, 1>(a, s);
+  return split ? launch_v2<2, 4, 8>(a, s) : launch_v2<2, 4, 1>(a, s);
 }
 
 }  // namespace syn

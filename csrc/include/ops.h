@@ -15,7 +15,7 @@ torch::Tensor q4_tiled_to_rows(torch::Tensor qw, torch::Tensor sm, int64_t N, in
 torch::Tensor q4t_dequant(torch::Tensor qw, torch::Tensor sm, int64_t N, int64_t K);
 void q4_gemv(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
              torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor res, torch::Tensor out,
-             int64_t N, int64_t K, int64_t mode);
+             int64_t N, int64_t K, int64_t mode, int64_t nt_hint, int64_t e_active);
 
 void rmsnorm(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor out);
 void moe_combine_rmsnorm(torch::Tensor x, torch::Tensor yp, torch::Tensor pair_of, torch::Tensor shared,
@@ -57,7 +57,7 @@ void ep_combine(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, int64
 void q4_gemv_ep(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
                 torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor out_ptrs, int64_t N, int64_t K,
                 torch::Tensor done_ctr, torch::Tensor peers, int64_t sig_off, int64_t sig_rank,
-                torch::Tensor step_ctr, int64_t n_layers, int64_t layer);
+                torch::Tensor step_ctr, int64_t n_layers, int64_t layer, int64_t nt_hint, int64_t e_active);
 
 void register_all(pybind11::module& m);
 }  // namespace syn

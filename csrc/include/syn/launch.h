@@ -39,6 +39,9 @@ struct GemvArgs {
   int sig_n, sig_rank;
   const uint32_t* step_ctr;
   int n_layers, layer;
+  // launch shape hints: max rows (tokens) per expert -> n-tiles of 8; experts likely active
+  int nt_hint;
+  int E_active_hint;
 };
 
 // ---- expert parallelism over NVLink peer memory ----

@@ -73,7 +73,7 @@ torch::Tensor q4t_dequant(torch::Tensor qw, torch::Tensor sm, int64_t N, int64_t
 
 void q4_gemv(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
              torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor res, torch::Tensor out, int64_t N,
-             int64_t K, int64_t mode) {
+             int64_t K, int64_t mode, int64_t nt_hint, int64_t e_active) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16, "x must be cuda bf16");
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be [rows, K] with unit inner stride");
   TORCH_CHECK(N % 16 == 0 && K % 64 == 0, "q4_gemv: N%16, K%64");
@@ -109,6 +109,8 @@ void q4_gemv(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torc
   a.step_ctr = nullptr;
   a.n_layers = 0;
   a.layer = 0;
+  a.nt_hint = (int)nt_hint;
+  a.E_active_hint = (int)std::max<int64_t>(1, e_active);
   if (mode == 0) TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.size(-1) == N, "out bf16 [P, N]");
   if (mode == 3 || mode == 5) TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.size(-1) == N, "out f32 [P, N]");
   if (mode == 1) TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.size(-1) == N / 2, "out bf16 [P, N/2]");
@@ -371,7 +373,7 @@ void ep_combine(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, int64
 void q4_gemv_ep(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
                 torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor out_ptrs, int64_t N, int64_t K,
                 torch::Tensor done_ctr, torch::Tensor peers, int64_t sig_off, int64_t sig_rank,
-                torch::Tensor step_ctr, int64_t n_layers, int64_t layer) {
+                torch::Tensor step_ctr, int64_t n_layers, int64_t layer, int64_t nt_hint, int64_t e_active) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x");
   TORCH_CHECK(N % 16 == 0 && K % 64 == 0 && x.size(1) == K, "q4_gemv_ep shapes");
   TORCH_CHECK(done_ctr.is_cuda() && done_ctr.scalar_type() == torch::kInt32, "done_ctr cuda int32");
@@ -398,6 +400,8 @@ void q4_gemv_ep(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, t
   a.step_ctr = reinterpret_cast<const uint32_t*>(step_ctr.data_ptr());
   a.n_layers = (int)n_layers;
   a.layer = (int)layer;
+  a.nt_hint = (int)nt_hint;
+  a.E_active_hint = (int)std::max<int64_t>(1, e_active);
   TORCH_CHECK(tok_off.numel() == a.E + 1, "tok_off E+1");
   const at::cuda::CUDAGuard guard(x.device());
   SYN_CHECK_CUDA(launch_q4_gemv(a, cur_stream()));

@@ -1,0 +1,66 @@
+"""Decode-step profiling harness: builds a model of a named shape, prefills a batch,
+then runs decode steps between cudaProfilerStart/Stop so that
+``ncu --profile-from-start off`` sees only the decode kernels.
+
+    python -m syntropy_b200.bench.profile_decode --model qwen3-235b-a22b --layers 4 \
+        --batch 32 --prompt 1024 --steps 2 [--eager]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import time
+
+import torch
+
+from ..models.config import get_config
+from ..models.transformer import prepare_weights
+from ..runtime.engine import LLMEngine, SamplingParams
+from ..runtime.runner import ModelRunner
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="qwen3-235b-a22b")
+    ap.add_argument("--layers", type=int, default=0)
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--prompt", type=int, default=1024)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--eager", action="store_true", help="no CUDA graph (one launch per op)")
+    ap.add_argument("--expert-cache-frac", type=float, default=1.0)
+    args = ap.parse_args()
+    dev = torch.device("cuda:0")
+    cfg = get_config(args.model)
+    if args.layers:
+        cfg = cfg.replace(n_layers=args.layers)
+    mw = prepare_weights(cfg, dev, seed=0, max_pos=args.prompt + 64)
+    runner = ModelRunner(mw, max_batch=args.batch, max_seq_len=args.prompt + 64, use_graphs=not args.eager)
+    if args.expert_cache_frac < 1.0:
+        from ..experts.cache import ExpertCache
+        ExpertCache(mw.layers, args.expert_cache_frac, dev)
+    eng = LLMEngine(runner)
+    g = torch.Generator().manual_seed(0)
+    for _ in range(args.batch):
+        eng.add_request(torch.randint(0, cfg.vocab, (args.prompt,), generator=g).tolist(),
+                        SamplingParams(max_tokens=args.warmup + args.steps + 4))
+    while eng.waiting:
+        eng.step()
+    for _ in range(args.warmup):
+        eng.step()
+    torch.cuda.synchronize()
+    runner.time_events = []
+    torch.cuda.profiler.start()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eng.step()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    wall = time.perf_counter() - t0
+    dev_ms = sum(a.elapsed_time(b) for a, b in runner.time_events) / args.steps
+    print(json.dumps({"model": cfg.name, "layers": cfg.n_layers, "batch": args.batch, "ms_per_step": dev_ms,
+                      "wall_ms_per_step": 1e3 * wall / args.steps}))
+
+
+if __name__ == "__main__":
+    main()

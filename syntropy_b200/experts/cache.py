@@ -1,0 +1,172 @@
+"""VRAM expert cache over a pinned host tier.
+
+Every MoE layer keeps ``n_resident = floor(frac * E_loc)`` experts in VRAM slots; the
+others live in pinned host memory, which under unified addressing the GPU reads directly
+over PCIe.  The grouped GEMV takes a per-expert pointer table, so an expert's "home" is
+just the pointer it is given: a VRAM slot (hit) or its host copy (miss, read in place
+while the resident experts stream from HBM on other SMs).
+
+Residency adapts: routing counts feed a decayed LFU score per expert (``ExpertStats``);
+``rebalance`` swaps the coldest resident for the hottest host expert when the hot one
+leads by a hysteresis margin, copying weights on a side stream between steps.
+
+Reference design: plan/rfcs/RFC-0023-moe-expert-cache-prediction-prefetch.md §5-§9 and
+crates/tier/src/experts/{sizing.rs:98-166,stats.rs:35-205}.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+
+class ExpertStats:
+    """Decayed-LFU expert popularity per layer (counts of routed rows)."""
+
+    def __init__(self, n_layers: int, n_experts: int, decay: float = 0.98, device="cpu"):
+        self.decay = decay
+        self.score = torch.zeros(n_layers, n_experts, dtype=torch.float64)
+        self.total = torch.zeros(n_layers, n_experts, dtype=torch.int64)
+
+    def observe(self, layer: int, counts: torch.Tensor):
+        c = counts.detach().to("cpu", torch.float64)
+        self.score[layer].mul_(self.decay).add_(c)
+        self.total[layer] += counts.detach().to("cpu", torch.int64)
+
+    def hit_rate(self, layer: int, resident: torch.Tensor) -> float:
+        t = self.total[layer].double()
+        s = t.sum()
+        return float((t * resident.double()).sum() / s) if s > 0 else 0.0
+
+    def state_dict(self):
+        return {"score": self.score.clone(), "total": self.total.clone(), "decay": self.decay}
+
+    def load_state_dict(self, d):
+        self.score.copy_(d["score"])
+        self.total.copy_(d["total"])
+        self.decay = float(d["decay"])
+
+
+class ExpertCache:
+    """Residency manager for the expert banks of a model's MoE layers on one device."""
+
+    def __init__(self, layers, frac: float, device, hysteresis: float = 1.25):
+        self.layers = [L for L in layers if getattr(L, "is_moe", False)]
+        self.frac = frac
+        self.device = device
+        self.hysteresis = hysteresis
+        self.banks = []
+        for L in self.layers:
+            self.banks.append(_TieredBank(L.experts_gu, L.experts_down, frac, device))
+
+    @property
+    def n_resident(self) -> int:
+        return self.banks[0].n_res if self.banks else 0
+
+    def vram_bytes(self) -> int:
+        return sum(b.vram_bytes() for b in self.banks)
+
+    def host_bytes(self) -> int:
+        return sum(b.host_bytes() for b in self.banks)
+
+    def rebalance(self, stats: ExpertStats, max_swaps_per_layer: int = 2) -> int:
+        """Swap cold residents for hot host experts (decayed LFU with hysteresis)."""
+        n = 0
+        for li, b in enumerate(self.banks):
+            sc = stats.score[li, b.e0: b.e0 + b.E]
+            for _ in range(max_swaps_per_layer):
+                res = b.resident_mask()
+                if res.all() or (~res).all():
+                    break
+                cold_res = torch.where(res, sc, torch.full_like(sc, math.inf)).argmin().item()
+                hot_host = torch.where(~res, sc, torch.full_like(sc, -math.inf)).argmax().item()
+                if sc[hot_host] <= self.hysteresis * sc[cold_res] or sc[hot_host] <= 0:
+                    break
+                b.swap(cold_res, hot_host)
+                n += 1
+        return n
+
+
+class _TieredBank:
+    """Moves an ExpertBank pair (gate_up, down) to a resident/host split in place."""
+
+    def __init__(self, gu, dn, frac, device):
+        self.gu, self.dn = gu, dn
+        self.E = gu.E
+        self.e0 = gu.e0
+        self.n_res = max(0, min(self.E, int(math.floor(frac * self.E + 1e-9))))
+        self.slot_of = list(range(self.n_res)) + [-1] * (self.E - self.n_res)  # expert -> vram slot
+        self.host_of = [-1] * self.n_res + list(range(self.E - self.n_res))    # expert -> host row
+        cuda = device.type == "cuda" if hasattr(device, "type") else str(device).startswith("cuda")
+        self.cuda = cuda
+        self.parts = []
+        for bank in (gu, dn):
+            if bank.qw is None:
+                self.parts.append(None)
+                continue
+            nh = self.E - self.n_res
+            qh = torch.empty((nh,) + tuple(bank.qw.shape[1:]), dtype=bank.qw.dtype, pin_memory=cuda)
+            sh = torch.empty((nh,) + tuple(bank.sm.shape[1:]), dtype=bank.sm.dtype, pin_memory=cuda)
+            if nh:
+                qh.copy_(bank.qw[self.n_res:])
+                sh.copy_(bank.sm[self.n_res:])
+            qv = bank.qw[: self.n_res].clone()
+            sv = bank.sm[: self.n_res].clone()
+            bank.qw, bank.sm = qv, sv  # VRAM keeps only the resident slots
+            self.parts.append({"bank": bank, "qv": qv, "sv": sv, "qh": qh, "sh": sh})
+            self._write_ptrs(bank, qv, sv, qh, sh)
+        if cuda:
+            torch.cuda.empty_cache()
+
+    def _write_ptrs(self, bank, qv, sv, qh, sh):
+        qp, sp = [], []
+        for e in range(self.E):
+            s = self.slot_of[e]
+            if s >= 0:
+                qp.append(qv.data_ptr() + s * qv.stride(0) * qv.element_size())
+                sp.append(sv.data_ptr() + s * sv.stride(0) * sv.element_size())
+            else:
+                h = self.host_of[e]
+                qp.append(qh.data_ptr() + h * qh.stride(0) * qh.element_size())
+                sp.append(sh.data_ptr() + h * sh.stride(0) * sh.element_size())
+        dev = bank.qw_ptrs.device if bank.qw_ptrs is not None else qv.device
+        new_q = torch.tensor(qp, dtype=torch.int64)
+        new_s = torch.tensor(sp, dtype=torch.int64)
+        if bank.qw_ptrs is None:
+            bank.qw_ptrs, bank.sm_ptrs = new_q.to(dev), new_s.to(dev)
+        else:  # in place: captured graphs keep reading the same pointer tables
+            bank.qw_ptrs.copy_(new_q)
+            bank.sm_ptrs.copy_(new_s)
+
+    def resident_mask(self) -> torch.Tensor:
+        return torch.tensor([s >= 0 for s in self.slot_of])
+
+    def vram_bytes(self):
+        return sum(p["qv"].numel() * 4 + p["sv"].numel() * 2 for p in self.parts if p)
+
+    def host_bytes(self):
+        return sum(p["qh"].numel() * 4 + p["sh"].numel() * 2 for p in self.parts if p)
+
+    def swap(self, e_res: int, e_host: int):
+        """Exchange the homes of a resident and a host expert (weights copied both ways)."""
+        s, h = self.slot_of[e_res], self.host_of[e_host]
+        for p in self.parts:
+            if p is None:
+                continue
+            tq = p["qv"][s].clone()
+            ts = p["sv"][s].clone()
+            p["qv"][s].copy_(p["qh"][h], non_blocking=True)
+            p["sv"][s].copy_(p["sh"][h], non_blocking=True)
+            p["qh"][h].copy_(tq, non_blocking=False)
+            p["sh"][h].copy_(ts, non_blocking=False)
+        self.slot_of[e_res], self.slot_of[e_host] = -1, s
+        self.host_of[e_res], self.host_of[e_host] = h, -1
+        for p in self.parts:
+            if p is not None:
+                self._write_ptrs(p["bank"], p["qv"], p["sv"], p["qh"], p["sh"])
+
+    def weight_of(self, which: int, e: int):
+        """Dense view of expert e (for the CPU path / tests)."""
+        p = self.parts[which]
+        s = self.slot_of[e]
+        return (p["qv"][s], p["sv"][s]) if s >= 0 else (p["qh"][self.host_of[e]], p["sh"][self.host_of[e]])

@@ -33,9 +33,10 @@ class ExpertBank:
     """Stacked per-expert matrices [E][N, K].  On CUDA: q4 tiled storage + pointer tables
     (the pointer of expert e may point into the VRAM bank, a cache slot or host memory)."""
 
-    E: int
+    E: int        # experts held (local rows)
     N: int
     K: int
+    e0: int = 0   # global id of local row 0 (expert parallelism)
     qw: torch.Tensor | None = None    # int32 [E, N*K/8]
     sm: torch.Tensor | None = None    # fp16 [E, N*K/16]
     w: torch.Tensor | None = None     # CPU/dense: [E, N, K]
@@ -170,13 +171,14 @@ def prepare_weights(cfg: ModelConfig, device="cpu", seed: int = 0, quant: str | 
             r = get(pre + "router", sh["router"])
             L.router = r.to(torch.bfloat16) if is_cuda else r
             E, f, H = cfg.n_experts, cfg.moe_ffn, cfg.hidden
-            gu = ExpertBank(E, 2 * f, H)
-            dn = ExpertBank(E, H, f)
+            El = eb - ea
+            gu = ExpertBank(El, 2 * f, H, e0=ea)
+            dn = ExpertBank(El, H, f, e0=ea)
             if is_cuda and quant == "q4":
-                gu.qw = torch.zeros(E, 2 * f * H // 8, dtype=torch.int32, device=device)
-                gu.sm = torch.zeros(E, 2 * f * H // 16, dtype=torch.float16, device=device)
-                dn.qw = torch.zeros(E, H * f // 8, dtype=torch.int32, device=device)
-                dn.sm = torch.zeros(E, H * f // 16, dtype=torch.float16, device=device)
+                gu.qw = torch.zeros(El, 2 * f * H // 8, dtype=torch.int32, device=device)
+                gu.sm = torch.zeros(El, 2 * f * H // 16, dtype=torch.float16, device=device)
+                dn.qw = torch.zeros(El, H * f // 8, dtype=torch.int32, device=device)
+                dn.sm = torch.zeros(El, H * f // 16, dtype=torch.float16, device=device)
                 for e in range(ea, eb):
                     if state_dict is not None:
                         g = state_dict[pre + "experts.gate"][e].to(gen_dev).float()
@@ -187,18 +189,19 @@ def prepare_weights(cfg: ModelConfig, device="cpu", seed: int = 0, quant: str | 
                         u = expert_tensor(cfg, pre + "experts.up", e, (f, H), seed=seed, device=gen_dev)
                         d = expert_tensor(cfg, pre + "experts.down", e, (H, f), seed=seed, device=gen_dev)
                     q = Q4Weight.quantize(ops.interleave_gate_up(g, u))
-                    gu.qw[e].copy_(q.qw)
-                    gu.sm[e].copy_(q.sm)
+                    gu.qw[e - ea].copy_(q.qw)
+                    gu.sm[e - ea].copy_(q.sm)
                     q = Q4Weight.quantize(d)
-                    dn.qw[e].copy_(q.qw)
-                    dn.sm[e].copy_(q.sm)
+                    dn.qw[e - ea].copy_(q.qw)
+                    dn.sm[e - ea].copy_(q.sm)
+                    del g, u, d, q
                 gu.build_ptrs()
                 dn.build_ptrs()
             else:
                 g = get(pre + "experts.gate", sh["experts.gate"])
                 u = get(pre + "experts.up", sh["experts.up"])
-                gu.w = torch.stack([ops.interleave_gate_up(g[e], u[e]) for e in range(E)])
-                dn.w = get(pre + "experts.down", sh["experts.down"])
+                gu.w = torch.stack([ops.interleave_gate_up(g[e], u[e]) for e in range(ea, eb)])
+                dn.w = get(pre + "experts.down", sh["experts.down"])[ea:eb].contiguous()
                 if is_cuda:
                     gu.w = gu.w.to(device=device, dtype=torch.bfloat16)
                     dn.w = dn.w.to(device=device, dtype=torch.bfloat16)

@@ -13,7 +13,7 @@ __all__ = [
     "GEMV_STORE", "GEMV_SWIGLU", "GEMV_SCALED_F32", "GEMV_ADD_F32",
     "rms_norm", "embed", "linear", "linear_grouped", "qk_rope_kv_write", "attn_decode",
     "attn_prefill", "router_logits", "moe_topk", "moe_combine_rmsnorm", "argmax", "sample",
-    "swiglu_interleaved_ref", "interleave_gate_up", "count_launches", "DECODE_ROWS_MAX",
+    "swiglu_interleaved_ref", "interleave_gate_up", "count_launches", "DECODE_ROWS_MAX", "moe_nt_hint",
 ]
 
 GEMV_STORE, GEMV_SWIGLU, GEMV_SCALED_F32, GEMV_ADD_F32 = 0, 1, 2, 3
@@ -100,7 +100,7 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
         if kmode == 0 and out.dtype == torch.float32:
             kmode = 5
         ext().q4_gemv(x, ptrs[0], ptrs[1], _identity_off(T, x.device), _EMPTY_I32(x.device), _EMPTY_F32(x.device),
-                      _EMPTY_BF16(x.device), out, W.N, W.K, kmode)
+                      _EMPTY_BF16(x.device), out, W.N, W.K, kmode, (T + 7) // 8, 1)
         _launched()
         return out
     # GEMM path (prefill): dequantised tile + library matmul until the tcgen05 GEMM lands
@@ -161,17 +161,28 @@ def _EMPTY_BF16(dev):
     return _empty(torch.bfloat16, dev)
 
 
+def moe_nt_hint(n_pairs: int, n_experts: int) -> int:
+    """Token tiles of 8 per expert pass: sized for the mean load (an expert above it takes
+    an extra pass over its weights, which is rarer than paying registers on every tile)."""
+    mean = n_pairs / max(1, n_experts)
+    return 1 if mean <= 4 else (2 if mean <= 10 else 4)
+
+
 def linear_grouped(x: torch.Tensor, bank, tok_off: torch.Tensor, tok_idx: torch.Tensor | None,
                    out: torch.Tensor, mode: int, route_w: torch.Tensor | None = None,
-                   qw_ptrs: torch.Tensor | None = None, sm_ptrs: torch.Tensor | None = None):
-    """Grouped (per-expert) linear over CSR pair lists.  bank: ExpertLinear (N, K, tensors)."""
+                   qw_ptrs: torch.Tensor | None = None, sm_ptrs: torch.Tensor | None = None,
+                   nt_hint: int | None = None):
+    """Grouped (per-expert) linear over CSR pair lists.  bank: ExpertBank (N, K, tensors)."""
     if x.is_cuda:
         e = ext()
         kmode = {GEMV_STORE: 0, GEMV_SWIGLU: 1, GEMV_SCALED_F32: 2}[mode]
+        E = qw_ptrs.numel()
+        if nt_hint is None:
+            nt_hint = moe_nt_hint(out.shape[0], E)
         e.q4_gemv(x, qw_ptrs, sm_ptrs, tok_off,
                   tok_idx if tok_idx is not None else _EMPTY_I32(x.device),
                   route_w if route_w is not None else _EMPTY_F32(x.device),
-                  _EMPTY_BF16(x.device), out, bank.N, bank.K, kmode)
+                  _EMPTY_BF16(x.device), out, bank.N, bank.K, kmode, nt_hint, min(E, out.shape[0]))
         _launched()
         return out
     # CPU reference: loop over experts in ascending order

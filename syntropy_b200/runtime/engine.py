@@ -60,8 +60,12 @@ class StepOutput:
 
 
 class LLMEngine:
-    def __init__(self, runner: ModelRunner, max_prefill_tokens: int = 8192, eos_token_id: int | None = None):
+    def __init__(self, runner: ModelRunner, max_prefill_tokens: int = 8192, eos_token_id: int | None = None,
+                 dist_ctx=None):
         self.runner = runner
+        # Under expert parallelism every rank must take the same kind of step (the MoE
+        # layers exchange rows), so step kinds are agreed over the host control group.
+        self.dist = dist_ctx if (dist_ctx is not None and dist_ctx.enabled) else None
         self.cfg = runner.cfg
         self.max_prefill_tokens = max_prefill_tokens
         self.eos = eos_token_id
@@ -108,12 +112,38 @@ class LLMEngine:
 
     # ------------------------------------------------------------------ steps
     def step(self) -> list[StepOutput]:
+        if self.dist is not None:
+            return self._step_lockstep()
         batch = self._admit()
         if batch:
             return self._prefill(batch)
         if self.running:
             return self._decode()
         return []
+
+    def _step_lockstep(self) -> list[StepOutput]:
+        import torch.distributed as dist
+        want = torch.tensor([1 if self._can_admit() else 0, 1 if self.running else 0], dtype=torch.int64)
+        dist.all_reduce(want, op=dist.ReduceOp.MAX, group=self.dist.cpu_group)
+        if want[0]:
+            return self._prefill(self._admit())
+        if want[1]:
+            return self._decode()
+        return []
+
+    def _can_admit(self) -> bool:
+        if not self.waiting or len(self.running) >= self.runner.max_batch:
+            return False
+        s = self.waiting[0]
+        return self.runner.kv.alloc.num_free >= self.runner.kv.blocks_needed(len(s.prompt) + 1)
+
+    def global_has_work(self) -> bool:
+        if self.dist is None:
+            return self.has_work()
+        import torch.distributed as dist
+        t = torch.tensor([1 if self.has_work() else 0], dtype=torch.int64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.dist.cpu_group)
+        return bool(t[0])
 
     def _admit(self) -> list[Sequence]:
         kv = self.runner.kv
@@ -131,6 +161,10 @@ class LLMEngine:
 
     def _prefill(self, batch: list[Sequence]) -> list[StepOutput]:
         kv = self.runner.kv
+        if not batch:  # lockstep participation with no local prompts
+            self.runner.prefill(torch.zeros(0, dtype=torch.int32), torch.zeros(0, dtype=torch.int32),
+                                torch.zeros(0, dtype=torch.int64), [0])
+            return []
         toks, pos, slots, cu = [], [], [], [0]
         for s in batch:
             toks += s.prompt
@@ -241,6 +275,6 @@ class LLMEngine:
     def generate(self, prompts: list[list[int]], params: SamplingParams | list[SamplingParams]) -> list[list[int]]:
         plist = params if isinstance(params, list) else [params] * len(prompts)
         ids = [self.add_request(p, sp) for p, sp in zip(prompts, plist)]
-        while self.has_work():
+        while self.global_has_work():
             self.step()
         return [self.finished[i].output for i in ids]

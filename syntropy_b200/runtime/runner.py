@@ -74,8 +74,9 @@ class StepDesc:
 
 class ModelRunner:
     def __init__(self, mw: ModelWeights, max_batch: int = 64, max_seq_len: int = 4096, num_blocks: int | None = None,
-                 kv_dtype=None, use_graphs: bool = True, kv_budget_bytes: int | None = None):
+                 kv_dtype=None, use_graphs: bool = True, kv_budget_bytes: int | None = None, ep=None):
         cfg = mw.cfg
+        self.ep = ep  # parallel.ep.EPGroup or None
         self.mw, self.cfg = mw, cfg
         self.device = mw.device
         self.is_cuda = self.device.type == "cuda"
@@ -118,6 +119,12 @@ class ModelRunner:
             b["ffn_mid"] = torch.zeros(B, cfg.ffn, dtype=act, device=dev)
         if cfg.is_moe:
             E, k = cfg.n_experts, cfg.top_k
+            ep = self.ep
+            if ep is not None and not ep.fused:
+                B = B * ep.N  # baseline routes every rank's rows on every rank
+                b["h_all"] = torch.zeros(B, H, dtype=act, device=dev)
+                b["x_part"] = torch.zeros(B, H, dtype=torch.float32, device=dev)
+                b["moe_red"] = torch.zeros(self.max_batch, H, dtype=torch.float32, device=dev)
             b["rlogits"] = torch.zeros(B, 2 * E, dtype=torch.float32, device=dev)
             b["topk_ids"] = torch.zeros(B, k, dtype=torch.int32, device=dev)
             b["topk_w"] = torch.zeros(B, k, dtype=torch.float32, device=dev)
@@ -126,8 +133,12 @@ class ModelRunner:
             b["pair_w"] = torch.zeros(B * k, dtype=torch.float32, device=dev)
             b["pair_of"] = torch.zeros(B, k, dtype=torch.int32, device=dev)
             b["pred_mask"] = torch.zeros(E, dtype=torch.int32, device=dev)
-            b["moe_mid"] = torch.zeros(B * k, cfg.moe_ffn, dtype=act, device=dev)
+            n_pairs = B * k
+            if ep is not None and ep.fused:
+                n_pairs = max(n_pairs, ep.N * ep.cap * k)
+            b["moe_mid"] = torch.zeros(n_pairs, cfg.moe_ffn, dtype=act, device=dev)
             b["moe_out"] = torch.zeros(B * k, H, dtype=torch.float32, device=dev)
+            B = self.max_batch
         # split-KV workspace sized for the largest split count
         self.pages_per_split = 16
         n_splits = (self.max_blocks + self.pages_per_split - 1) // self.pages_per_split
@@ -149,6 +160,8 @@ class ModelRunner:
         """Forward of the first B rows of the step descriptor; writes logits and next tokens."""
         cfg, mw, b, d = self.cfg, self.mw, self.buf, self.desc.d
         x, h = b["x"][:B], b["h"][:B]
+        if self.ep is not None:
+            self.ep.step_begin()
         ops.embed(mw.embed, d["tokens"][:B], x)
         n_layers = cfg.n_layers
         first = mw.layers[0]
@@ -157,7 +170,7 @@ class ModelRunner:
             nxt = mw.layers[i + 1] if i + 1 < n_layers else None
             self._attention_decode(L, B, i)
             if L.is_moe:
-                self._moe_decode(L, nxt, B)
+                self._moe_decode(L, nxt, B, i)
             else:
                 ops.rms_norm(x, L.ffn_norm, cfg.rms_eps, out=h)
                 mid = b["ffn_mid"][:B]
@@ -184,40 +197,79 @@ class ModelRunner:
                         b.get("part_o"), b.get("part_ml"), self.pages_per_split)
         ops.linear(attn.view(B, -1), L.o, b["x"][:B], ops.GEMV_ADD_F32)
 
-    def _moe_decode(self, L, nxt, B):
+    def _moe_decode(self, L, nxt, B, layer):
         cfg, mw, b = self.cfg, self.mw, self.buf
         x, h = b["x"][:B], b["h"][:B]
         ops.rms_norm(x, L.ffn_norm, cfg.rms_eps, out=h)
+        nw = nxt.attn_norm if nxt else mw.final_norm
+        ep = self.ep
+        if ep is not None and not ep.fused:
+            return self._moe_decode_baseline(L, B, nw)
         pred = L.router_cat is not None
         rw = L.router_cat if pred else L.router
         E = cfg.n_experts
-        rl = b["rlogits"][:B, : (2 * E if pred else E)]
+        W = 2 * E if pred else E
+        rl = b["rlogits"].view(-1)[: B * W].view(B, W)
         ops.router_logits(h, rw, rl)
         mb = self._moe_bufs(B)
         ops.moe_topk(rl, cfg, L.router_bias, pred, mb)
         k = cfg.top_k
+        gu, dn = L.experts_gu, L.experts_down
+        if ep is not None:
+            ep.moe_decode_fused(layer, h, mb["topk_ids"], mb["topk_w"], x, gu, dn, b["moe_mid"], nw, h,
+                                cfg.rms_eps)
+            return
         mid = b["moe_mid"][:B * k]
         yp = b["moe_out"][:B * k]
-        gu, dn = L.experts_gu, L.experts_down
         ops.linear_grouped(h, gu, mb["tok_off"], mb["tok_idx"], mid, ops.GEMV_SWIGLU,
                            qw_ptrs=gu.qw_ptrs, sm_ptrs=gu.sm_ptrs)
         ops.linear_grouped(mid, dn, mb["tok_off"], None, yp, ops.GEMV_SCALED_F32, route_w=mb["pair_w"],
                            qw_ptrs=dn.qw_ptrs, sm_ptrs=dn.sm_ptrs)
-        nw = nxt.attn_norm if nxt else mw.final_norm
         ops.moe_combine_rmsnorm(x, yp, mb["pair_of"], None, nw, h, cfg.rms_eps)
+
+    def _moe_decode_baseline(self, L, B, nw):
+        """NCCL baseline: all-gather rows, route all rows, apply local experts, reduce-scatter."""
+        from ..parallel.collectives import all_gather_rows, reduce_scatter_rows
+        cfg, b, ep = self.cfg, self.buf, self.ep
+        N, k, E = ep.N, cfg.top_k, cfg.n_experts
+        x, h = b["x"][:B], b["h"][:B]
+        ha = b["h_all"][: N * B]
+        all_gather_rows(ha, h, ep.ctx.group)
+        R = N * B
+        rl = b["rlogits"].view(-1)[: R * E].view(R, E)
+        ops.router_logits(ha, L.router, rl)
+        mb = self._moe_bufs(R)
+        ops.moe_topk(rl, cfg, L.router_bias, False, mb)
+        ea, eb = ep.expert_range
+        gu, dn = L.experts_gu, L.experts_down
+        mid = b["moe_mid"][: R * k]
+        yp = b["moe_out"][: R * k]
+        yp.zero_()
+        off = mb["tok_off"][ea: eb + 1]
+        ops.linear_grouped(ha, gu, off, mb["tok_idx"], mid, ops.GEMV_SWIGLU, qw_ptrs=gu.qw_ptrs, sm_ptrs=gu.sm_ptrs)
+        ops.linear_grouped(mid, dn, off, None, yp, ops.GEMV_SCALED_F32, route_w=mb["pair_w"],
+                           qw_ptrs=dn.qw_ptrs, sm_ptrs=dn.sm_ptrs)
+        part = b["x_part"][:R]
+        part.zero_()
+        ops.moe_combine_rmsnorm(part, yp, mb["pair_of"], None, None, None, cfg.rms_eps)
+        red = b["moe_red"][:B]
+        reduce_scatter_rows(red, part, ep.ctx.group)
+        x.add_(red)
+        ops.rms_norm(x, nw, cfg.rms_eps, out=h)
 
     def decode(self, B: int):
         """Run one decode step for the first B rows (descriptor already filled on the host)."""
-        self.desc.upload()
         if self.use_graphs:
             bb = bucket_for(B)
             g = self.graphs.get(bb)
             if g is None:
-                g = self.capture(bb)
+                g = self.capture(bb)  # uses (and restores) the host descriptor
+            self.desc.upload()
             ev = self._ev0()
             g.replay()
             self._ev1(ev)
         else:
+            self.desc.upload()
             ev = self._ev0()
             self.decode_forward(B)
             self._ev1(ev)
@@ -298,6 +350,8 @@ class ModelRunner:
                 mid = torch.empty(T, cfg.ffn, dtype=act, device=dev)
                 ops.linear(h, L.gate_up, mid, ops.GEMV_SWIGLU)
                 ops.linear(mid, L.down, x, ops.GEMV_ADD_F32)
+        if len(cu_seqlens) == 1:
+            return torch.zeros(0, cfg.vocab, dtype=torch.float32, device=dev)
         last = torch.tensor([c - 1 for c in cu_seqlens[1:]], device=dev, dtype=torch.long)
         hl = ops.rms_norm(x[last].contiguous(), mw.final_norm, cfg.rms_eps)
         logits = torch.empty(last.numel(), cfg.vocab, dtype=torch.float32, device=dev)
@@ -305,54 +359,34 @@ class ModelRunner:
         return logits
 
     def _moe_prefill(self, L, h, x):
-        """MoE FFN for a prefill chunk: routing on the device, then one GEMM pair per active
-        expert over its gathered rows, combined in ascending expert order."""
+        """MoE FFN for a prefill chunk: routing on the device, then the local experts over
+        their gathered rows (one weight read per active expert), combined in ascending
+        expert order; under expert parallelism the NCCL all-gather/reduce-scatter path."""
         cfg = self.cfg
         T = h.shape[0]
         E, k = cfg.n_experts, cfg.top_k
         dev = h.device
-        if T <= 256 and self.is_cuda:
+        mb = {"topk_ids": torch.empty(T, k, dtype=torch.int32, device=dev),
+              "topk_w": torch.empty(T, k, dtype=torch.float32, device=dev),
+              "tok_off": torch.empty(E + 1, dtype=torch.int32, device=dev),
+              "tok_idx": torch.empty(T * k, dtype=torch.int32, device=dev),
+              "pair_w": torch.empty(T * k, dtype=torch.float32, device=dev),
+              "pair_of": torch.empty(T, k, dtype=torch.int32, device=dev), "pred_mask": None}
+        if T == 0:
+            pass
+        elif T <= 256 and self.is_cuda:
             logits = torch.empty(T, E, dtype=torch.float32, device=dev)
             ops.router_logits(h, L.router, logits)
-            mb = {"topk_ids": torch.empty(T, k, dtype=torch.int32, device=dev),
-                  "topk_w": torch.empty(T, k, dtype=torch.float32, device=dev),
-                  "tok_off": torch.empty(E + 1, dtype=torch.int32, device=dev),
-                  "tok_idx": torch.empty(T * k, dtype=torch.int32, device=dev),
-                  "pair_w": torch.empty(T * k, dtype=torch.float32, device=dev),
-                  "pair_of": torch.empty(T, k, dtype=torch.int32, device=dev), "pred_mask": None}
             ops.moe_topk(logits, cfg, L.router_bias, False, mb)
         else:
             logits = h.float() @ L.router.float().t()
-            mb = {"topk_ids": torch.empty(T, k, dtype=torch.int32, device=dev),
-                  "topk_w": torch.empty(T, k, dtype=torch.float32, device=dev),
-                  "tok_off": torch.empty(E + 1, dtype=torch.int32, device=dev),
-                  "tok_idx": torch.empty(T * k, dtype=torch.int32, device=dev),
-                  "pair_w": torch.empty(T * k, dtype=torch.float32, device=dev),
-                  "pair_of": torch.empty(T, k, dtype=torch.int32, device=dev)}
             _route_torch(logits, cfg, L.router_bias, mb)
-        off = mb["tok_off"].tolist()
-        yp = torch.zeros(T * k, cfg.hidden, dtype=torch.float32, device=dev)
-        tok_idx = mb["tok_idx"].long()
         gu, dn = L.experts_gu, L.experts_down
-        for e in range(E):
-            a, b = off[e], off[e + 1]
-            if a == b:
-                continue
-            rows = h[tok_idx[a:b]]
-            if self.is_cuda and rows.shape[0] <= ops.DECODE_ROWS_MAX and gu.qw is not None:
-                mid = torch.empty(b - a, cfg.moe_ffn, dtype=h.dtype, device=dev)
-                ops.linear_grouped(rows, gu, _off1(b - a, dev), None, mid, ops.GEMV_SWIGLU,
-                                   qw_ptrs=gu.qw_ptrs[e:e + 1], sm_ptrs=gu.sm_ptrs[e:e + 1])
-                ops.linear_grouped(mid, dn, _off1(b - a, dev), None, yp[a:b], ops.GEMV_SCALED_F32,
-                                   route_w=mb["pair_w"][a:b], qw_ptrs=dn.qw_ptrs[e:e + 1],
-                                   sm_ptrs=dn.sm_ptrs[e:e + 1])
-                continue
-            wg = gu.weight(e)
-            wd = dn.weight(e)
-            y = rows.to(wg.dtype) @ wg.t()
-            mid = ops.swiglu_interleaved_ref(y).to(wd.dtype)
-            yp[a:b] = mb["pair_w"][a:b, None] * (mid @ wd.t()).float()
-        ops.moe_combine_rmsnorm(x, yp, mb["pair_of"], None, None, None, cfg.rms_eps)
+        if self.ep is not None:
+            x.add_(self.ep.moe_baseline(h, mb["topk_ids"], mb["topk_w"], gu, dn))
+            return
+        from ..parallel.ep import _local_experts_apply
+        x.add_(_local_experts_apply(h, mb["topk_ids"], mb["topk_w"], gu, dn, (0, E)))
 
 
 _OFF1: dict = {}
