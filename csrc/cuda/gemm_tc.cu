@@ -1,0 +1,378 @@
+// Prefill GEMM on the 5th-generation tensor cores: C = X * W^T with bf16 activations X
+// and 4-bit tiled weights W (syn/q4.h), grouped over experts.
+//
+// One CTA computes a 128 x BN output tile (BN = 128 or 256) with its accumulator in TMEM:
+//   warp 0      TMA producer: X tiles (128 rows x 64 bf16, SWIZZLE_128B) -> smem stage
+//   warp 1      TMEM allocator and MMA issuer: one elected thread issues tcgen05.mma
+//               (kind::f16, M=128, N=BN, K=16, bf16 x bf16 -> f32) per 16 columns and
+//               tcgen05.commit's to the stage's "empty" barrier
+//   warps 4..7  B producers during the main loop: 4-bit weights -> bf16 (d*q+m, f32 math,
+//               one rounding) written straight into the UMMA K-major SWIZZLE_128B layout,
+//               then fence.proxy.async; afterwards the epilogue: tcgen05.ld 32x32b of their
+//               TMEM lane quarter, fused epilogue, global stores
+// Stages are tracked with mbarriers; every wait is bounded (the kernel records an error
+// bit and bails out instead of hanging).  Reference op: `Gemm` (crates/kernels/src/op/
+// kind.rs; f32 reference crates/kernels/src/reference/linear.rs:71).
+#include <cuda.h>
+
+#include "common.cuh"
+#include "sync.cuh"
+#include "syn/q4.h"
+
+namespace syn {
+
+constexpr int TC_BM = 128;
+constexpr int TC_BK = 64;
+constexpr int TC_STAGES = 4;
+constexpr uint64_t TC_WAIT_NS = 2000000000ull;  // 2 s: far above any legitimate stage wait
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(b)), "r"(n));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait on an mbarrier phase; false (with an error bit) after TC_WAIT_NS.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* status, volatile int* abort) {
+  if (mbar_test(b, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_test(b, parity)) {
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > TC_WAIT_NS) {
+      *abort = 1;
+      if (status) atomicOr(status, 1 << 4);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// K-major, SWIZZLE_128B smem matrix descriptor (rows of 128 bytes, 8-row atoms 1024 B apart).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1 << 16;            // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset: next 8-row group
+  d |= (uint64_t)1 << 46;            // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;            // SWIZZLE_128B
+  return d;
+}
+
+template <int BN>
+__device__ __forceinline__ constexpr uint32_t idesc_bf16_f32() {
+  return (1u << 4)                 // D: f32
+         | (1u << 7)               // A: bf16
+         | (1u << 10)              // B: bf16
+         | ((uint32_t)(BN >> 3) << 17)
+         | ((uint32_t)(TC_BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+
+struct TcGemmArgs {
+  const int64_t* qw_ptrs;   // [G] tiled 4-bit weights per group
+  const int64_t* sm_ptrs;   // [G]
+  const int32_t* row_off;   // [G+1] rows of A per group (contiguous)
+  const float* route_w;     // [M] (mode SCALED)
+  void* out;
+  int G, M, N, K;
+  int mode;                 // 0 store bf16, 1 swiglu bf16 [M, N/2], 2 scaled f32, 3 add f32, 5 store f32
+  int* status;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(256, 1) tc_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                                            TcGemmArgs a) {
+  constexpr int A_BYTES = TC_BM * TC_BK * 2;   // 16 KB
+  constexpr int B_BYTES = BN * TC_BK * 2;      // 16 / 32 KB
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + TC_STAGES * A_BYTES;
+  __shared__ __align__(8) uint64_t full_a[TC_STAGES], full_b[TC_STAGES], empty[TC_STAGES], done_bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ int s_group, s_mtile;
+  __shared__ volatile int s_abort;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ntile = blockIdx.y;
+
+  // ---- find this CTA's (group, m-tile) ----
+  if (threadIdx.x == 0) {
+    int acc = 0, grp = -1, mt = 0;
+    for (int g = 0; g < a.G; ++g) {
+      const int cnt = a.row_off[g + 1] - a.row_off[g];
+      const int nt = (cnt + TC_BM - 1) / TC_BM;
+      if ((int)blockIdx.x < acc + nt) { grp = g; mt = blockIdx.x - acc; break; }
+      acc += nt;
+    }
+    s_group = grp;
+    s_mtile = mt;
+    s_abort = 0;
+  }
+  __syncthreads();
+  const int grp = s_group;
+  if (grp < 0) return;  // uniform: beyond the last tile
+  const int row0 = a.row_off[grp] + s_mtile * TC_BM;
+  const int row_end = a.row_off[grp + 1];
+  const int KB = a.K / TC_BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_STAGES; ++s) {
+      mbar_init(&full_a[s], 1);
+      mbar_init(&full_b[s], 128);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(&tmem_base)),
+                 "r"(BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (A) ----------------
+    if (lane == 0) {
+      for (int kb = 0; kb < KB; ++kb) {
+        const int s = kb % TC_STAGES;
+        const uint32_t ph = (kb / TC_STAGES) & 1;
+        if (kb >= TC_STAGES && !mbar_wait(&empty[s], ph ^ 1, a.status, &s_abort)) break;
+        mbar_expect_tx(&full_a[s], A_BYTES);
+        tma_load_2d(sA + s * A_BYTES, &tmap_a, kb * TC_BK, row0, &full_a[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32<BN>();
+      for (int kb = 0; kb < KB; ++kb) {
+        const int s = kb % TC_STAGES;
+        const uint32_t ph = (kb / TC_STAGES) & 1;
+        if (!mbar_wait(&full_a[s], ph, a.status, &s_abort)) break;
+        if (!mbar_wait(&full_b[s], ph, a.status, &s_abort)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+        const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < TC_BK / 16; ++kk)
+          umma_bf16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), idesc, (kb | kk) != 0);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(&done_bar);
+    }
+  } else if (warp >= 4) {
+    // ---------------- B producers: 4-bit -> bf16 in SWIZZLE_128B layout ----------------
+    const int pw = warp - 4;
+    const int g = lane >> 2, t = lane & 3;
+    const uint4* qw = reinterpret_cast<const uint4*>(a.qw_ptrs[grp]);
+    const uint2* sm = reinterpret_cast<const uint2*>(a.sm_ptrs[grp]);
+    const int KG = a.K >> 6;
+    const int tile0 = ntile * (BN / 16);
+    for (int kb = 0; kb < KB; ++kb) {
+      const int s = kb % TC_STAGES;
+      const uint32_t ph = (kb / TC_STAGES) & 1;
+      // prefetch this stage's weights before waiting for the slot
+      uint4 q[BN / 64];
+      uint2 slo[BN / 64], shi[BN / 64];
+#pragma unroll
+      for (int i = 0; i < BN / 64; ++i) {
+        const int64_t tk = (int64_t)(tile0 + pw + 4 * i) * KG + kb;
+        q[i] = __ldcs(qw + tk * 32 + lane);
+        slo[i] = __ldcs(sm + tk * 16 + g);
+        shi[i] = __ldcs(sm + tk * 16 + g + 8);
+      }
+      if (kb >= TC_STAGES && !mbar_wait(&empty[s], ph ^ 1, a.status, &s_abort)) break;
+      uint8_t* B = sB + s * B_BYTES;
+#pragma unroll
+      for (int i = 0; i < BN / 64; ++i) {
+        const int rt = pw + 4 * i;  // 16-row tile inside the BN rows
+        const uint32_t words[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
+#pragma unroll
+        for (int blk = 0; blk < 2; ++blk) {
+          const half2 dl = *reinterpret_cast<const half2*>(blk ? &slo[i].y : &slo[i].x);
+          const half2 dh = *reinterpret_cast<const half2*>(blk ? &shi[i].y : &shi[i].x);
+          const float d_lo = __low2float(dl), m_lo = __high2float(dl);
+          const float d_hi = __low2float(dh), m_hi = __high2float(dh);
+#pragma unroll
+          for (int st = 0; st < 2; ++st) {
+            const uint32_t w = words[blk * 2 + st];
+#pragma unroll
+            for (int reg = 0; reg < 4; ++reg) {
+              const int hi_row = reg & 1, hi_col = reg >> 1;
+              const float q0 = (float)((w >> (4 * reg)) & 15u);
+              const float q1 = (float)((w >> (4 * (reg + 4))) & 15u);
+              const float d = hi_row ? d_hi : d_lo, m = hi_row ? m_hi : m_lo;
+              const uint32_t v = pack_bf16x2(fmaf(d, q0, m), fmaf(d, q1, m));
+              const int row = rt * 16 + g + 8 * hi_row;
+              const int k = blk * 32 + st * 16 + 2 * t + 8 * hi_col;  // even
+              const int byte = k * 2;
+              const int off = row * 128 + ((((byte >> 4) ^ (row & 7)) << 4) | (byte & 15));
+              *reinterpret_cast<uint32_t*>(B + off) = v;
+            }
+          }
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      mbar_arrive(&full_b[s]);
+    }
+    // ---------------- epilogue ----------------
+    const bool ok = mbar_wait(&done_bar, 0, a.status, &s_abort);
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+    const int row = row0 + pw * 32 + lane;  // TMEM lane quarter of this warp
+    const bool live = ok && row < row_end && row < a.M;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld32(tmem + ((uint32_t)(pw * 32) << 16) + c0, r);
+      if (!live) continue;
+      const int n0 = ntile * BN + c0;
+      if (a.mode == 1) {  // SwiGLU over 8-column gate/up chunks
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.out) + (int64_t)row * (a.N / 2) + n0 / 2;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int gi = (j / 8) * 16 + (j % 8);
+          const float gv = __uint_as_float(r[gi]), uv = __uint_as_float(r[gi + 8]);
+          o[j] = f2bf(silu(gv) * uv);
+        }
+      } else if (a.mode == 0) {
+        uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out) + (int64_t)row * a.N + n0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 v;
+          v.x = pack_bf16x2(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1]));
+          v.y = pack_bf16x2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]));
+          v.z = pack_bf16x2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]));
+          v.w = pack_bf16x2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]));
+          o[j] = v;
+        }
+      } else {
+        float* o = reinterpret_cast<float*>(a.out) + (int64_t)row * a.N + n0;
+        const float sc = a.mode == 2 ? a.route_w[row] : 1.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float v = __uint_as_float(r[j]);
+          if (a.mode == 3)
+            o[j] += v;
+          else
+            o[j] = sc * v;
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(BN));
+  }
+}
+
+// ---- host side ----
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode() {
+  static PFN_encodeTiled fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  }
+  return fn;
+}
+
+cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, const int64_t* sm_ptrs,
+                              const int32_t* row_off, int G, int M, int N, int K, int mode, const float* route_w,
+                              void* out, int* status, int max_mtiles, cudaStream_t s) {
+  if (K % TC_BK != 0 || N % 128 != 0 || M <= 0) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || (ldx * 2) % 16 != 0) return cudaErrorInvalidValue;
+  PFN_encodeTiled enc = get_encode();
+  if (!enc) return cudaErrorNotSupported;
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  const cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)TC_BM};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  TcGemmArgs a{qw_ptrs, sm_ptrs, row_off, route_w, out, G, M, N, K, mode, status};
+  const bool wide = (N % 256 == 0);
+  const int BN = wide ? 256 : 128;
+  const size_t smem = 1024 + (size_t)TC_STAGES * (TC_BM * TC_BK * 2 + BN * TC_BK * 2);
+  dim3 grid((unsigned)max_mtiles, (unsigned)(N / BN));
+  if (wide) {
+    static bool set = false;
+    if (!set) {
+      cudaError_t e = cudaFuncSetAttribute(tc_gemm_q4_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem);
+      if (e != cudaSuccess) return e;
+      set = true;
+    }
+    tc_gemm_q4_kernel<256><<<grid, 256, smem, s>>>(map, a);
+  } else {
+    static bool set = false;
+    if (!set) {
+      cudaError_t e = cudaFuncSetAttribute(tc_gemm_q4_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)smem);
+      if (e != cudaSuccess) return e;
+      set = true;
+    }
+    tc_gemm_q4_kernel<128><<<grid, 256, smem, s>>>(map, a);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace syn

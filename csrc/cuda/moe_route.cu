@@ -10,34 +10,46 @@
 
 namespace syn {
 
-// logits[t][e] = dot(h[t], W[e]); one warp per (expert row), looping over tokens.
-// W: bf16 [E_rows, H]; h: bf16 [T, H]; H % 256 == 0.
+// logits[t][e] = dot(h[t], W[e]).  One warp per (expert row, group of 8 tokens): the
+// warp keeps its slice of the weight row in registers and reuses it for the 8 tokens.
+// W: bf16 [E_rows, H]; h: bf16 [T, H]; H % 256 == 0 and H <= 8192.
+template <int CH>  // 16-byte chunks per lane = H / 256
 __global__ void router_logits_kernel(const __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ W,
                                      float* __restrict__ logits, int T, int H, int E_rows) {
   const int lane = threadIdx.x & 31;
-  const int e = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int tg_count = (T + 7) / 8;
+  const int e = gw / tg_count, tg = gw % tg_count;
   if (e >= E_rows) return;
   const uint4* wr = reinterpret_cast<const uint4*>(W + (int64_t)e * H);
-  const int nchunk = H / 8;  // 16-byte chunks
-  for (int t = 0; t < T; ++t) {
+  float2 wf[CH][4];
+#pragma unroll
+  for (int i = 0; i < CH; ++i) {
+    const uint4 v = __ldg(wr + i * 32 + lane);
+    wf[i][0] = unpack_bf16x2(v.x);
+    wf[i][1] = unpack_bf16x2(v.y);
+    wf[i][2] = unpack_bf16x2(v.z);
+    wf[i][3] = unpack_bf16x2(v.w);
+  }
+  const int t1 = min(T, tg * 8 + 8);
+  for (int t = tg * 8; t < t1; ++t) {
     const uint4* hr = reinterpret_cast<const uint4*>(h + (int64_t)t * H);
     float acc = 0.f;
-    for (int c = lane; c < nchunk; c += 32) {
-      const uint4 wv = __ldg(wr + c), hv = __ldg(hr + c);
-      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, hh[4] = {hv.x, hv.y, hv.z, hv.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 a = unpack_bf16x2(ww[i]), b = unpack_bf16x2(hh[i]);
-        acc = fmaf(a.x, b.x, acc);
-        acc = fmaf(a.y, b.y, acc);
+    for (int i = 0; i < CH; ++i) {
+      const uint4 v = __ldg(hr + i * 32 + lane);
+      const uint32_t hh[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 b = unpack_bf16x2(hh[j]);
+        acc = fmaf(wf[i][j].x, b.x, acc);
+        acc = fmaf(wf[i][j].y, b.y, acc);
       }
     }
     acc = warp_sum(acc);
     if (lane == 0) logits[(int64_t)t * E_rows + e] = acc;
   }
 }
-
-
 
 constexpr int TOPK_MAX_E = 512;
 constexpr int TOPK_MAX_K = 16;
@@ -214,10 +226,22 @@ __global__ void __launch_bounds__(1024) moe_topk_kernel(TopkArgs a) {
 cudaError_t launch_router_logits(const void* h, const void* W, float* logits, int T, int H, int E_rows,
                                  cudaStream_t s) {
   if (T == 0) return cudaSuccess;
-  if (H % 8 != 0) return cudaErrorInvalidValue;
+  if (H % 256 != 0 || H > 8192) return cudaErrorInvalidValue;
   const int warps = 8;
-  router_logits_kernel<<<(E_rows + warps - 1) / warps, warps * 32, 0, s>>>(
-      reinterpret_cast<const __nv_bfloat16*>(h), reinterpret_cast<const __nv_bfloat16*>(W), logits, T, H, E_rows);
+  const long n_warps = (long)E_rows * ((T + 7) / 8);
+  const unsigned grid = (unsigned)((n_warps + warps - 1) / warps);
+  auto hp = reinterpret_cast<const __nv_bfloat16*>(h);
+  auto wp = reinterpret_cast<const __nv_bfloat16*>(W);
+  switch (H / 256) {
+    case 1: router_logits_kernel<1><<<grid, warps * 32, 0, s>>>(hp, wp, logits, T, H, E_rows); break;
+    case 2: router_logits_kernel<2><<<grid, warps * 32, 0, s>>>(hp, wp, logits, T, H, E_rows); break;
+    case 4: router_logits_kernel<4><<<grid, warps * 32, 0, s>>>(hp, wp, logits, T, H, E_rows); break;
+    case 8: router_logits_kernel<8><<<grid, warps * 32, 0, s>>>(hp, wp, logits, T, H, E_rows); break;
+    case 16: router_logits_kernel<16><<<grid, warps * 32, 0, s>>>(hp, wp, logits, T, H, E_rows); break;
+    case 28: router_logits_kernel<28><<<grid, warps * 32, 0, s>>>(hp, wp, logits, T, H, E_rows); break;
+    case 32: router_logits_kernel<32><<<grid, warps * 32, 0, s>>>(hp, wp, logits, T, H, E_rows); break;
+    default: return cudaErrorInvalidValue;
+  }
   return cudaGetLastError();
 }
 

@@ -59,5 +59,9 @@ void q4_gemv_ep(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, t
                 torch::Tensor done_ctr, torch::Tensor peers, int64_t sig_off, int64_t sig_rank,
                 torch::Tensor step_ctr, int64_t n_layers, int64_t layer, int64_t nt_hint, int64_t e_active);
 
+void tc_gemm_q4(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor row_off, int64_t N,
+                int64_t K, int64_t mode, torch::Tensor route_w, torch::Tensor out, torch::Tensor status,
+                int64_t max_mtiles);
+
 void register_all(pybind11::module& m);
 }  // namespace syn

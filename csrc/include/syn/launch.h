@@ -44,6 +44,11 @@ struct GemvArgs {
   int E_active_hint;
 };
 
+// ---- prefill GEMM on tcgen05 (4-bit weights, grouped) ----
+cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, const int64_t* sm_ptrs,
+                              const int32_t* row_off, int G, int M, int N, int K, int mode, const float* route_w,
+                              void* out, int* status, int max_mtiles, cudaStream_t s);
+
 // ---- expert parallelism over NVLink peer memory ----
 struct EpArgs {
   const int64_t* peers;  // device array [N] of symmetric-region bases (own included)

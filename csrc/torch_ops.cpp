@@ -407,4 +407,32 @@ void q4_gemv_ep(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, t
   SYN_CHECK_CUDA(launch_q4_gemv(a, cur_stream()));
 }
 
+
+// C = X W^T on tcgen05 with 4-bit weights, grouped over contiguous row ranges.
+//   x: bf16 [M, K]; row_off: int32 [G+1] (device); qw/sm ptrs: int64 [G]
+//   mode 0: out bf16 [M, N]; 1: SwiGLU out bf16 [M, N/2]; 2: out f32 [M, N] * route_w[m];
+//   3: out f32 [M, N] += ; 5: out f32 [M, N]
+void tc_gemm_q4(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor row_off, int64_t N,
+                int64_t K, int64_t mode, torch::Tensor route_w, torch::Tensor out, torch::Tensor status,
+                int64_t max_mtiles) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x bf16 [M, K]");
+  TORCH_CHECK(x.size(1) == K && K % 64 == 0 && N % 128 == 0, "tc_gemm_q4 shapes (K%64, N%128)");
+  TORCH_CHECK(row_off.is_cuda() && row_off.scalar_type() == torch::kInt32 && row_off.numel() == qw_ptrs.numel() + 1,
+              "row_off int32 [G+1]");
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == torch::kInt32, "status int32");
+  const int64_t M = x.size(0);
+  if (mode == 1) TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.size(-1) == N / 2 && out.size(0) >= M, "out swiglu");
+  if (mode == 0) TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.size(-1) == N && out.size(0) >= M, "out bf16");
+  if (mode == 2 || mode == 3 || mode == 5)
+    TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.size(-1) == N && out.size(0) >= M, "out f32");
+  if (mode == 2) TORCH_CHECK(route_w.numel() >= M, "route_w");
+  TORCH_CHECK(out.is_contiguous(), "out contiguous");
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_tc_gemm_q4(x.data_ptr(), (int)x.stride(0), qw_ptrs.data_ptr<int64_t>(), sm_ptrs.data_ptr<int64_t>(),
+                                   row_off.data_ptr<int32_t>(), (int)qw_ptrs.numel(), (int)M, (int)N, (int)K, (int)mode,
+                                   mode == 2 ? route_w.data_ptr<float>() : nullptr, out.data_ptr(),
+                                   status.data_ptr<int32_t>(), (int)max_mtiles, cur_stream()));
+}
+
 }  // namespace syn

@@ -1,0 +1,171 @@
+"""Kernel microbenchmarks at the flagship shapes (Qwen3-235B-A22B, batch 32 decode and
+8192-token prefill).  Each kernel is timed with CUDA events after warm-up; inputs exceed
+L2 (126 MB) wherever the kernel streams weights.  Reports achieved bandwidth / FLOP rate
+as a fraction of the measured peaks in MEASURED_PEAKS.json (copy bandwidth, cuBLAS bf16).
+
+    python -m syntropy_b200.bench.kernels [--only name,...]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+from .. import ops
+from .._ext import ext
+from ..formats.q4 import Q4Weight
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def timeit(fn, iters=20, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / iters  # us
+
+
+def bank(E, N, K, dev):
+    from ..models.transformer import ExpertBank
+    b = ExpertBank(E, N, K)
+    b.qw = torch.empty(E, N * K // 8, dtype=torch.int32, device=dev)
+    b.sm = torch.empty(E, N * K // 16, dtype=torch.float16, device=dev)
+    for e in range(E):
+        q = Q4Weight.quantize(torch.randn(N, K, device=dev) * 0.02)
+        b.qw[e].copy_(q.qw)
+        b.sm[e].copy_(q.sm)
+    b.build_ptrs()
+    return b
+
+
+def routing(T, E, k, dev, seed=0):
+    from ..models.config import get_config
+    cfg = get_config("qwen3-235b-a22b").replace(n_experts=E, top_k=k)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    logits = torch.randn(T, E, device=dev, generator=g)
+    bufs = {"topk_ids": torch.zeros(T, k, dtype=torch.int32, device=dev),
+            "topk_w": torch.zeros(T, k, device=dev), "tok_off": torch.zeros(E + 1, dtype=torch.int32, device=dev),
+            "tok_idx": torch.zeros(T * k, dtype=torch.int32, device=dev), "pair_w": torch.zeros(T * k, device=dev),
+            "pair_of": torch.zeros(T, k, dtype=torch.int32, device=dev), "pred_mask": None}
+    ops.moe_topk(logits, cfg, None, False, bufs)
+    return cfg, bufs
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default="")
+    ap.add_argument("--batch", type=int, default=32)
+    args = ap.parse_args()
+    only = set(x for x in args.only.split(",") if x)
+    dev = torch.device("cuda:0")
+    hbm, tf, src = peaks()
+    res = []
+    T = args.batch
+
+    def report(name, us, nbytes=None, flops=None, extra=None):
+        r = {"kernel": name, "us": round(us, 2)}
+        if nbytes:
+            r["GB/s"] = round(nbytes / us / 1e3, 1)
+            r["frac_hbm"] = round(nbytes / us / 1e3 / hbm, 3)
+        if flops:
+            r["TFLOP/s"] = round(flops / us / 1e6, 1)
+            r["frac_bf16"] = round(flops / us / 1e6 / tf, 3)
+        if extra:
+            r.update(extra)
+        r["peak_source"] = src
+        res.append(r)
+        print(json.dumps(r), flush=True)
+
+    want = lambda n: not only or n in only  # noqa: E731
+    H, f, E, k = 4096, 1536, 128, 8
+    if want("moe_gate_up") or want("moe_down"):
+        cfg, b = routing(T, E, k, dev)
+        gu = bank(E, 2 * f, H, dev)
+        dn = bank(E, H, f, dev)
+        h = torch.randn(T, H, device=dev).to(torch.bfloat16)
+        mid = torch.empty(T * k, f, dtype=torch.bfloat16, device=dev)
+        yp = torch.empty(T * k, H, dtype=torch.float32, device=dev)
+        active = int((b["tok_off"][1:] - b["tok_off"][:-1] > 0).sum())
+        fn = lambda: ops.linear_grouped(h, gu, b["tok_off"], b["tok_idx"], mid, ops.GEMV_SWIGLU,  # noqa: E731
+                                        qw_ptrs=gu.qw_ptrs, sm_ptrs=gu.sm_ptrs)
+        report("moe_gate_up_gemv", timeit(fn), active * gu.N * gu.K * 5 // 8, extra={"active_experts": active})
+        fn = lambda: ops.linear_grouped(mid, dn, b["tok_off"], None, yp, ops.GEMV_SCALED_F32,  # noqa: E731
+                                        route_w=b["pair_w"], qw_ptrs=dn.qw_ptrs, sm_ptrs=dn.sm_ptrs)
+        report("moe_down_gemv", timeit(fn), active * dn.N * dn.K * 5 // 8, extra={"active_experts": active})
+        del gu, dn
+    for name, N, K in (("qkv_gemv", 9216, 4096), ("o_gemv", 4096, 8192), ("lm_head_gemv", 151936, 4096)):
+        if not want(name):
+            continue
+        reps = max(1, int(math.ceil(300e6 / (N * K * 5 / 8))))  # rotate copies to exceed L2
+        ws = [Q4Weight.quantize(torch.randn(N, K, device=dev) * 0.02) for _ in range(reps)]
+        x = torch.randn(T, K, device=dev).to(torch.bfloat16)
+        out = torch.empty(T, N, dtype=torch.float32 if name == "lm_head_gemv" else torch.bfloat16, device=dev)
+        i = [0]
+
+        def fn():
+            ops.linear(x, ws[i[0] % reps], out, ops.GEMV_STORE)
+            i[0] += 1
+        report(name, timeit(fn), N * K * 5 // 8)
+        del ws
+    if want("router"):
+        W = (torch.randn(2 * E, H, device=dev) * 0.02).to(torch.bfloat16)
+        h = torch.randn(T, H, device=dev).to(torch.bfloat16)
+        lg = torch.empty(T, 2 * E, device=dev)
+        report("router_logits", timeit(lambda: ops.router_logits(h, W, lg)), W.numel() * 2)
+        cfg, b = routing(T, E, k, dev)
+        b["pred_mask"] = torch.zeros(E, dtype=torch.int32, device=dev)
+        report("moe_topk", timeit(lambda: ops.moe_topk(lg, cfg, None, True, b)))
+    if want("attn"):
+        from ..kv.paged import PagedKVCache
+        ctx, Hq, Hkv, D = 1024, 64, 4, 128
+        nb = T * (ctx // 16) + 1
+        kc = torch.randn(nb, Hkv, 16, D, device=dev).to(torch.bfloat16)
+        vc = torch.randn(nb, Hkv, 16, D, device=dev).to(torch.bfloat16)
+        bt = (torch.randperm(nb - 1, device=dev)[: T * (ctx // 16)] + 1).int().view(T, -1)
+        cl = torch.full((T,), ctx, dtype=torch.int32, device=dev)
+        q = torch.randn(T, Hq, D, device=dev).to(torch.bfloat16)
+        out = torch.empty_like(q)
+        pps = 16
+        ns = (bt.shape[1] + pps - 1) // pps
+        po = torch.empty(T * Hkv * ns * 16 * D, device=dev)
+        pml = torch.empty(T * Hkv * ns * 16 * 2, device=dev)
+        fn = lambda: ops.attn_decode(q, kc, vc, bt, cl, out, 1 / math.sqrt(D), po, pml, pps)  # noqa: E731
+        report("attn_decode", timeit(fn), T * ctx * Hkv * D * 2 * 2)
+    if want("gemm_tc"):
+        for M, N, K in ((8192, 9216, 4096), (8192, 4096, 8192)):
+            w = Q4Weight.quantize(torch.randn(N, K, device=dev) * 0.02)
+            x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+            out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+            st = torch.zeros(1, dtype=torch.int32, device=dev)
+            qp = torch.tensor([w.qw.data_ptr()], device=dev)
+            sp = torch.tensor([w.sm.data_ptr()], device=dev)
+            off = torch.tensor([0, M], dtype=torch.int32, device=dev)
+            fn = lambda: ext().tc_gemm_q4(x, qp, sp, off, N, K, 0, torch.empty(0, device=dev), out, st,  # noqa: E731
+                                          M // 128 + 1)
+            report(f"tc_gemm_q4_{M}x{N}x{K}", timeit(fn, iters=10), flops=2 * M * N * K,
+                   extra={"status": int(st.item())})
+            wd = w.dequant()
+            report(f"cublas_bf16_{M}x{N}x{K}(reference)", timeit(lambda: x @ wd.t(), iters=10), flops=2 * M * N * K)
+    print(json.dumps({"summary": res}))
+
+
+if __name__ == "__main__":
+    main()
