@@ -33,6 +33,7 @@ void register_all(pybind11::module& m) {
   m.def("ep_combine", &ep_combine);
   m.def("q4_gemv_ep", &q4_gemv_ep);
   m.def("tc_gemm_q4", &tc_gemm_q4);
+  register_runtime(m);
 }
 
 }  // namespace syn

@@ -1,0 +1,335 @@
+// Host-side native runtime exposed to Python: SPSC rings (in-process or in a POSIX shared
+// memory region), the data-plane frame codec, the MoE split rule, an O_DIRECT pread pool
+// into pinned buffers, and lock-free metric counters / log-linear histograms.
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <atomic>
+#include <chrono>
+#include <condition_variable>
+#include <cstdlib>
+#include <cstring>
+#include <deque>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include <torch/extension.h>
+
+#include "syn/frame.h"
+#include "syn/moe_assign.h"
+#include "syn/spsc.h"
+
+namespace py = pybind11;
+
+namespace syn {
+
+// ------------------------------------------------------------------ shared memory region
+// A named POSIX shm object holding a header and any number of SPSC rings (the daemon <->
+// runner "local plane"; reference crates/ipc/src/shm.rs:75-468).
+class ShmRegion {
+ public:
+  ShmRegion(const std::string& name, int64_t nbytes, bool create) : name_(name), size_(nbytes), owner_(create) {
+    int fd = shm_open(name.c_str(), create ? (O_CREAT | O_RDWR | O_EXCL) : O_RDWR, 0600);
+    TORCH_CHECK(fd >= 0, "shm_open(", name, ") failed: ", strerror(errno));
+    if (create) TORCH_CHECK(ftruncate(fd, nbytes) == 0, "ftruncate failed");
+    base_ = mmap(nullptr, (size_t)nbytes, PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+    close(fd);
+    TORCH_CHECK(base_ != MAP_FAILED, "mmap failed");
+  }
+  ~ShmRegion() {
+    if (base_ && base_ != MAP_FAILED) munmap(base_, (size_t)size_);
+    if (owner_) shm_unlink(name_.c_str());
+  }
+  int64_t address() const { return (int64_t)(uintptr_t)base_; }
+  int64_t size() const { return size_; }
+
+ private:
+  std::string name_;
+  int64_t size_;
+  bool owner_;
+  void* base_ = nullptr;
+};
+
+// ------------------------------------------------------------------ SPSC ring wrapper
+class Ring {
+ public:
+  // Own memory (in-process ring).
+  Ring(int64_t capacity, int64_t slot_bytes) {
+    TORCH_CHECK(capacity > 0 && (capacity & (capacity - 1)) == 0, "capacity must be a power of two");
+    own_.resize(SpscRing::bytes_needed(capacity, (uint32_t)slot_bytes) + 64);
+    void* p = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(own_.data()) + 63) & ~uintptr_t(63));
+    r_ = SpscRing::init(p, (uint64_t)capacity, (uint32_t)slot_bytes);
+    buf_.resize(slot_bytes);
+  }
+  // Ring at an address (e.g. inside a ShmRegion); init=true formats it.
+  Ring(int64_t address, int64_t capacity, int64_t slot_bytes, bool init) {
+    void* p = (void*)(uintptr_t)address;
+    TORCH_CHECK((address & 63) == 0, "ring address must be 64-byte aligned");
+    r_ = init ? SpscRing::init(p, (uint64_t)capacity, (uint32_t)slot_bytes) : SpscRing::attach(p);
+    TORCH_CHECK(r_ != nullptr, "no ring at this address");
+    buf_.resize(r_->hdr()->slot_bytes);
+  }
+  static int64_t bytes_needed(int64_t capacity, int64_t slot_bytes) {
+    return (int64_t)SpscRing::bytes_needed((uint64_t)capacity, (uint32_t)slot_bytes);
+  }
+  bool push(py::bytes b) {
+    std::string s = b;
+    return r_->push(s.data(), (uint32_t)s.size());
+  }
+  py::object pop() {
+    const int64_t n = r_->pop(buf_.data(), (uint32_t)buf_.size());
+    if (n < 0) return py::none();
+    return py::bytes(reinterpret_cast<const char*>(buf_.data()), (size_t)n);
+  }
+  int64_t size() { return (int64_t)r_->size(); }
+  int64_t capacity() { return (int64_t)r_->capacity(); }
+
+ private:
+  std::vector<uint8_t> own_;
+  std::vector<uint8_t> buf_;
+  SpscRing* r_ = nullptr;
+};
+
+// ------------------------------------------------------------------ frames
+py::bytes frame_encode_py(int64_t ftype, int64_t flags, int64_t instance, int64_t term, int64_t seq, int64_t step,
+                          int64_t chan_seq, py::bytes ext, py::bytes payload) {
+  std::string e = ext, p = payload;
+  FrameSpec s;
+  s.ftype = (uint8_t)ftype;
+  s.flags = (uint16_t)flags;
+  s.instance = (uint64_t)instance;
+  s.epoch_term = (uint64_t)term;
+  s.epoch_seq = (uint64_t)seq;
+  s.step = (uint64_t)step;
+  s.chan_seq = (uint64_t)chan_seq;
+  std::string out(frame_len(e.size(), p.size()), '\0');
+  frame_encode(s, reinterpret_cast<const uint8_t*>(e.data()), e.size(), reinterpret_cast<const uint8_t*>(p.data()),
+               p.size(), reinterpret_cast<uint8_t*>(&out[0]));
+  return py::bytes(out);
+}
+
+py::tuple frame_decode_py(py::bytes buf) {
+  std::string b = buf;
+  FrameSpec s;
+  size_t eo, el, po, pl;
+  const int rc = frame_decode(reinterpret_cast<const uint8_t*>(b.data()), b.size(), &s, &eo, &el, &po, &pl);
+  if (rc != FRAME_OK) return py::make_tuple(rc, py::none(), py::none(), py::none());
+  py::dict spec;
+  spec["wire_minor"] = s.wire_minor;
+  spec["ftype"] = s.ftype;
+  spec["flags"] = s.flags;
+  spec["instance"] = s.instance;
+  spec["epoch_term"] = s.epoch_term;
+  spec["epoch_seq"] = s.epoch_seq;
+  spec["step"] = s.step;
+  spec["chan_seq"] = s.chan_seq;
+  return py::make_tuple(0, spec, py::bytes(b.data() + eo, el), py::bytes(b.data() + po, pl));
+}
+
+int64_t crc32c_py(py::bytes b) {
+  std::string s = b;
+  return crc32c(reinterpret_cast<const uint8_t*>(s.data()), s.size());
+}
+
+// ------------------------------------------------------------------ MoE split rule
+// route: int64 [n, 3] (expert, tokens, cache_slot); eligible: int32 bitmap words.
+torch::Tensor moe_assign_py(torch::Tensor route, torch::Tensor eligible, int64_t n_experts, int64_t b_copy,
+                            int64_t expert_bytes, int64_t copy_slots) {
+  route = route.to(torch::kInt64).contiguous();
+  eligible = eligible.to(torch::kInt32).contiguous();
+  const int64_t n = route.size(0);
+  std::vector<syn_route_slot> r(n);
+  auto ra = route.accessor<int64_t, 2>();
+  for (int64_t i = 0; i < n; ++i) {
+    r[i].expert = (uint16_t)ra[i][0];
+    r[i].tokens = (uint16_t)ra[i][1];
+    r[i].cache_slot = (uint32_t)ra[i][2];
+  }
+  std::vector<uint32_t> order(n), out(n);
+  syn_moe_assign(r.data(), (uint32_t)n, reinterpret_cast<const uint32_t*>(eligible.data_ptr()), (uint32_t)n_experts,
+                 (uint32_t)b_copy, (uint64_t)expert_bytes, (uint32_t)copy_slots, order.data(), out.data());
+  auto t = torch::empty({n}, torch::kInt64);
+  for (int64_t i = 0; i < n; ++i) t[i] = (int64_t)out[i];
+  return t;
+}
+
+// ------------------------------------------------------------------ I/O pool
+// Reads (fd, offset, length) extents into caller buffers (pinned host memory for the
+// host->VRAM weight path) with N worker threads using pread; files opened with O_DIRECT
+// when the extent and buffer alignments allow (reference: crates/io/src/pool/linux.rs).
+class IoPool {
+ public:
+  explicit IoPool(int threads) {
+    for (int i = 0; i < threads; ++i) workers_.emplace_back([this] { run(); });
+  }
+  ~IoPool() {
+    {
+      std::lock_guard<std::mutex> g(mu_);
+      stop_ = true;
+    }
+    cv_.notify_all();
+    for (auto& t : workers_) t.join();
+  }
+  // Submit a read; returns a ticket.  dst is a host address with room for `len` bytes.
+  int64_t submit(const std::string& path, int64_t offset, int64_t len, int64_t dst) {
+    std::lock_guard<std::mutex> g(mu_);
+    const int64_t id = next_++;
+    q_.push_back({id, path, offset, len, dst});
+    pending_++;
+    cv_.notify_one();
+    return id;
+  }
+  // Wait for all submitted reads; returns total bytes read (negative errno of the first failure).
+  int64_t wait_all() {
+    std::unique_lock<std::mutex> g(mu_);
+    done_cv_.wait(g, [this] { return pending_ == 0; });
+    const int64_t r = first_error_ ? first_error_ : bytes_;
+    bytes_ = 0;
+    first_error_ = 0;
+    return r;
+  }
+
+ private:
+  struct Job {
+    int64_t id;
+    std::string path;
+    int64_t offset, len, dst;
+  };
+  void run() {
+    for (;;) {
+      Job j;
+      {
+        std::unique_lock<std::mutex> g(mu_);
+        cv_.wait(g, [this] { return stop_ || !q_.empty(); });
+        if (stop_ && q_.empty()) return;
+        j = q_.front();
+        q_.pop_front();
+      }
+      int64_t got = do_read(j);
+      {
+        std::lock_guard<std::mutex> g(mu_);
+        if (got < 0 && !first_error_) first_error_ = got;
+        if (got > 0) bytes_ += got;
+        if (--pending_ == 0) done_cv_.notify_all();
+      }
+    }
+  }
+  static int64_t do_read(const Job& j) {
+    const bool aligned = (j.offset % 4096 == 0) && (j.len % 4096 == 0) && (j.dst % 4096 == 0);
+    int fd = open(j.path.c_str(), O_RDONLY | (aligned ? O_DIRECT : 0));
+    if (fd < 0 && aligned) fd = open(j.path.c_str(), O_RDONLY);
+    if (fd < 0) return -errno;
+    int64_t done = 0;
+    while (done < j.len) {
+      const ssize_t n = pread(fd, (char*)(uintptr_t)j.dst + done, (size_t)(j.len - done), (off_t)(j.offset + done));
+      if (n < 0) {
+        if (errno == EINTR) continue;
+        const int64_t e = -errno;
+        close(fd);
+        return e;
+      }
+      if (n == 0) break;
+      done += n;
+    }
+    close(fd);
+    return done;
+  }
+  std::vector<std::thread> workers_;
+  std::deque<Job> q_;
+  std::mutex mu_;
+  std::condition_variable cv_, done_cv_;
+  bool stop_ = false;
+  int64_t next_ = 0, pending_ = 0, bytes_ = 0, first_error_ = 0;
+};
+
+// ------------------------------------------------------------------ metrics
+// Counters and log-linear histograms with relaxed atomics (hot-thread safe; reference
+// crates/obs/src/metrics/{registry.rs,histogram.rs}).  Histogram buckets: 8 linear
+// sub-buckets per power of two from 1 unit to 2^40 units.
+class Histogram {
+ public:
+  static constexpr int kSub = 8, kPow = 41, kBuckets = kSub * kPow;
+  Histogram() {
+    for (auto& b : b_) b.store(0, std::memory_order_relaxed);
+  }
+  static int bucket(uint64_t v) {
+    if (v < kSub) return (int)v;
+    const int p = 63 - __builtin_clzll(v);  // floor(log2 v) >= 3
+    const int sub = (int)((v >> (p - 3)) & (kSub - 1));
+    const int idx = (p - 2) * kSub + sub;
+    return idx < kBuckets ? idx : kBuckets - 1;
+  }
+  static double lower(int idx) {
+    if (idx < kSub) return idx;
+    const int p = idx / kSub + 2, sub = idx % kSub;
+    return std::ldexp(1.0 + sub / (double)kSub, p);
+  }
+  void record(int64_t v) {
+    b_[bucket(v < 0 ? 0 : (uint64_t)v)].fetch_add(1, std::memory_order_relaxed);
+    n_.fetch_add(1, std::memory_order_relaxed);
+    sum_.fetch_add(v, std::memory_order_relaxed);
+  }
+  double quantile(double q) {
+    const uint64_t n = n_.load(std::memory_order_relaxed);
+    if (!n) return 0.0;
+    const uint64_t target = (uint64_t)std::ceil(q * n);
+    uint64_t acc = 0;
+    for (int i = 0; i < kBuckets; ++i) {
+      acc += b_[i].load(std::memory_order_relaxed);
+      if (acc >= target) return lower(i);
+    }
+    return lower(kBuckets - 1);
+  }
+  int64_t count() { return (int64_t)n_.load(); }
+  int64_t sum() { return (int64_t)sum_.load(); }
+
+ private:
+  std::atomic<uint64_t> b_[kBuckets];
+  std::atomic<uint64_t> n_{0};
+  std::atomic<int64_t> sum_{0};
+};
+
+class Counter {
+ public:
+  void add(int64_t v) { v_.fetch_add(v, std::memory_order_relaxed); }
+  int64_t get() { return v_.load(std::memory_order_relaxed); }
+
+ private:
+  std::atomic<int64_t> v_{0};
+};
+
+void register_runtime(py::module& m) {
+  py::class_<ShmRegion>(m, "ShmRegion")
+      .def(py::init<const std::string&, int64_t, bool>())
+      .def("address", &ShmRegion::address)
+      .def("size", &ShmRegion::size);
+  py::class_<Ring>(m, "SpscRing")
+      .def(py::init<int64_t, int64_t>())
+      .def(py::init<int64_t, int64_t, int64_t, bool>())
+      .def_static("bytes_needed", &Ring::bytes_needed)
+      .def("push", &Ring::push)
+      .def("pop", &Ring::pop)
+      .def("size", &Ring::size)
+      .def("capacity", &Ring::capacity);
+  m.def("frame_encode", &frame_encode_py);
+  m.def("frame_decode", &frame_decode_py);
+  m.def("crc32c", &crc32c_py);
+  m.def("moe_assign", &moe_assign_py);
+  py::class_<IoPool>(m, "IoPool")
+      .def(py::init<int>())
+      .def("submit", &IoPool::submit)
+      .def("wait_all", &IoPool::wait_all, py::call_guard<py::gil_scoped_release>());
+  py::class_<Histogram>(m, "Histogram")
+      .def(py::init<>())
+      .def("record", &Histogram::record)
+      .def("quantile", &Histogram::quantile)
+      .def("count", &Histogram::count)
+      .def("sum", &Histogram::sum);
+  py::class_<Counter>(m, "Counter").def(py::init<>()).def("add", &Counter::add).def("get", &Counter::get);
+}
+
+}  // namespace syn

@@ -3,6 +3,8 @@
 //
 // One CTA computes a 128 x BN output tile (BN = 128 or 256) with its accumulator in TMEM:
 //   warp 0      TMA producer: X tiles (128 rows x 64 bf16, SWIZZLE_128B) -> smem stage
+//   warp 2      raw-weight loader: bulk async copies (cp.async.bulk) of the packed 4-bit
+//               tiles and their scales, TC_RAW stages ahead of the dequantisers
 //   warp 1      TMEM allocator and MMA issuer: one elected thread issues tcgen05.mma
 //               (kind::f16, M=128, N=BN, K=16, bf16 x bf16 -> f32) per 16 columns and
 //               tcgen05.commit's to the stage's "empty" barrier
@@ -23,7 +25,8 @@ namespace syn {
 
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 64;
-constexpr int TC_STAGES = 4;
+constexpr int TC_RAW = 6;     // packed-weight stages (deep: they hide HBM latency)
+constexpr int TC_TILE_RAW = 640;  // bytes per 16-row x 64-col packed tile: 512 nibbles + 128 scales
 constexpr uint64_t TC_WAIT_NS = 2000000000ull;  // 2 s: far above any legitimate stage wait
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -59,6 +62,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* sta
     }
   }
   return true;
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
@@ -125,15 +135,28 @@ struct TcGemmArgs {
 };
 
 template <int BN>
+struct TcCfg {
+  static constexpr int STAGES = BN == 256 ? 3 : 4;
+  static constexpr int A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
+  static constexpr int B_BYTES = BN * TC_BK * 2;     // 16 / 32 KB
+  static constexpr int RAW_BYTES = (BN / 16) * TC_TILE_RAW;
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * (A_BYTES + B_BYTES) + (size_t)TC_RAW * RAW_BYTES;
+};
+
+template <int BN>
 __global__ void __launch_bounds__(256, 1) tc_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                             TcGemmArgs a) {
-  constexpr int A_BYTES = TC_BM * TC_BK * 2;   // 16 KB
-  constexpr int B_BYTES = BN * TC_BK * 2;      // 16 / 32 KB
+  constexpr int TC_STAGES = TcCfg<BN>::STAGES;
+  constexpr int A_BYTES = TcCfg<BN>::A_BYTES;
+  constexpr int B_BYTES = TcCfg<BN>::B_BYTES;
+  constexpr int RAW_BYTES = TcCfg<BN>::RAW_BYTES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + TC_STAGES * A_BYTES;
+  uint8_t* sR = sB + TC_STAGES * B_BYTES;
   __shared__ __align__(8) uint64_t full_a[TC_STAGES], full_b[TC_STAGES], empty[TC_STAGES], done_bar;
+  __shared__ __align__(8) uint64_t raw_full[TC_RAW], raw_empty[TC_RAW];
   __shared__ uint32_t tmem_base;
   __shared__ int s_group, s_mtile;
   __shared__ volatile int s_abort;
@@ -167,6 +190,10 @@ __global__ void __launch_bounds__(256, 1) tc_gemm_q4_kernel(const __grid_constan
       mbar_init(&full_b[s], 128);
       mbar_init(&empty[s], 1);
     }
+    for (int r = 0; r < TC_RAW; ++r) {
+      mbar_init(&raw_full[r], 1);
+      mbar_init(&raw_empty[r], 128);
+    }
     mbar_init(&done_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
@@ -191,6 +218,27 @@ __global__ void __launch_bounds__(256, 1) tc_gemm_q4_kernel(const __grid_constan
         tma_load_2d(sA + s * A_BYTES, &tmap_a, kb * TC_BK, row0, &full_a[s]);
       }
     }
+  } else if (warp == 2) {
+    // ---------------- raw 4-bit weight loader ----------------
+    if (lane == 0) {
+      const uint8_t* qw = reinterpret_cast<const uint8_t*>(a.qw_ptrs[grp]);
+      const uint8_t* sm = reinterpret_cast<const uint8_t*>(a.sm_ptrs[grp]);
+      const int KG = a.K >> 6;
+      const int tile0 = ntile * (BN / 16);
+      for (int kb = 0; kb < KB; ++kb) {
+        const int r = kb % TC_RAW;
+        const uint32_t ph = (kb / TC_RAW) & 1;
+        if (kb >= TC_RAW && !mbar_wait(&raw_empty[r], ph ^ 1, a.status, &s_abort)) break;
+        mbar_expect_tx(&raw_full[r], RAW_BYTES);
+        uint8_t* dst = sR + r * RAW_BYTES;
+#pragma unroll 4
+        for (int i = 0; i < BN / 16; ++i) {
+          const int64_t tk = (int64_t)(tile0 + i) * KG + kb;
+          bulk_load(dst + i * TC_TILE_RAW, qw + tk * 512, 512, &raw_full[r]);
+          bulk_load(dst + i * TC_TILE_RAW + 512, sm + tk * 128, 128, &raw_full[r]);
+        }
+      }
+    }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
@@ -213,23 +261,22 @@ __global__ void __launch_bounds__(256, 1) tc_gemm_q4_kernel(const __grid_constan
     // ---------------- B producers: 4-bit -> bf16 in SWIZZLE_128B layout ----------------
     const int pw = warp - 4;
     const int g = lane >> 2, t = lane & 3;
-    const uint4* qw = reinterpret_cast<const uint4*>(a.qw_ptrs[grp]);
-    const uint2* sm = reinterpret_cast<const uint2*>(a.sm_ptrs[grp]);
-    const int KG = a.K >> 6;
-    const int tile0 = ntile * (BN / 16);
     for (int kb = 0; kb < KB; ++kb) {
       const int s = kb % TC_STAGES;
       const uint32_t ph = (kb / TC_STAGES) & 1;
-      // prefetch this stage's weights before waiting for the slot
+      const int rr = kb % TC_RAW;
+      if (!mbar_wait(&raw_full[rr], (kb / TC_RAW) & 1, a.status, &s_abort)) break;
       uint4 q[BN / 64];
       uint2 slo[BN / 64], shi[BN / 64];
+      const uint8_t* R = sR + rr * RAW_BYTES;
 #pragma unroll
       for (int i = 0; i < BN / 64; ++i) {
-        const int64_t tk = (int64_t)(tile0 + pw + 4 * i) * KG + kb;
-        q[i] = __ldcs(qw + tk * 32 + lane);
-        slo[i] = __ldcs(sm + tk * 16 + g);
-        shi[i] = __ldcs(sm + tk * 16 + g + 8);
+        const uint8_t* tb = R + (pw + 4 * i) * TC_TILE_RAW;
+        q[i] = *reinterpret_cast<const uint4*>(tb + lane * 16);
+        slo[i] = *reinterpret_cast<const uint2*>(tb + 512 + g * 8);
+        shi[i] = *reinterpret_cast<const uint2*>(tb + 512 + (g + 8) * 8);
       }
+      mbar_arrive(&raw_empty[rr]);
       if (kb >= TC_STAGES && !mbar_wait(&empty[s], ph ^ 1, a.status, &s_abort)) break;
       uint8_t* B = sB + s * B_BYTES;
 #pragma unroll
@@ -351,7 +398,7 @@ cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, co
   TcGemmArgs a{qw_ptrs, sm_ptrs, row_off, route_w, out, G, M, N, K, mode, status};
   const bool wide = (N % 256 == 0);
   const int BN = wide ? 256 : 128;
-  const size_t smem = 1024 + (size_t)TC_STAGES * (TC_BM * TC_BK * 2 + BN * TC_BK * 2);
+  const size_t smem = wide ? TcCfg<256>::SMEM : TcCfg<128>::SMEM;
   dim3 grid((unsigned)max_mtiles, (unsigned)(N / BN));
   if (wide) {
     static bool set = false;

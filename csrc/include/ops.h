@@ -64,4 +64,5 @@ void tc_gemm_q4(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, t
                 int64_t max_mtiles);
 
 void register_all(pybind11::module& m);
+void register_runtime(pybind11::module& m);
 }  // namespace syn

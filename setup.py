@@ -24,6 +24,7 @@ def _sources():
 
 
 CXX_FLAGS = ["-O3", "-std=c++17", "-fno-strict-aliasing", "-Wno-unused-function"]
+LIBS = ["rt"]
 NVCC_FLAGS = [
     "-O3",
     "-std=c++17",
@@ -45,6 +46,7 @@ setup(
             sources=_sources(),
             include_dirs=[os.path.join(ROOT, "csrc", "include"), os.path.join(ROOT, "csrc")],
             extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
+            libraries=LIBS,
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},

@@ -30,17 +30,34 @@ def peaks():
         return 6650.0, 1590.0, "fallback"
 
 
-def timeit(fn, iters=20, warmup=3):
-    for _ in range(warmup):
-        fn()
+def timeit(fn, iters=20, warmup=3, graph=True):
+    """Device time per call (us).  The timed calls are captured in one CUDA graph and
+    replayed, so host launch overhead does not show up in the number."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(warmup):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(iters):
-        fn()
-    e1.record()
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(iters):
+                fn()
+        g.replay()  # warm
+        torch.cuda.synchronize()
+        e0.record()
+        g.replay()
+        e1.record()
+    else:
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
     torch.cuda.synchronize()
-    return e0.elapsed_time(e1) * 1e3 / iters  # us
+    return e0.elapsed_time(e1) * 1e3 / iters
 
 
 def bank(E, N, K, dev):

@@ -13,7 +13,7 @@ __all__ = [
     "GEMV_STORE", "GEMV_SWIGLU", "GEMV_SCALED_F32", "GEMV_ADD_F32",
     "rms_norm", "embed", "linear", "linear_grouped", "qk_rope_kv_write", "attn_decode",
     "attn_prefill", "router_logits", "moe_topk", "moe_combine_rmsnorm", "argmax", "sample",
-    "swiglu_interleaved_ref", "interleave_gate_up", "count_launches", "DECODE_ROWS_MAX", "moe_nt_hint",
+    "swiglu_interleaved_ref", "interleave_gate_up", "count_launches", "DECODE_ROWS_MAX", "moe_nt_hint", "gemm_grouped", "gemm_status",
 ]
 
 GEMV_STORE, GEMV_SWIGLU, GEMV_SCALED_F32, GEMV_ADD_F32 = 0, 1, 2, 3
@@ -103,7 +103,12 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
                       _EMPTY_BF16(x.device), out, W.N, W.K, kmode, (T + 7) // 8, 1)
         _launched()
         return out
-    # GEMM path (prefill): dequantised tile + library matmul until the tcgen05 GEMM lands
+    # GEMM path (prefill): tcgen05 kernel with fused dequant and epilogue
+    if isinstance(W, Q4Weight) and W.N % 128 == 0 and W.K % 64 == 0:
+        ptrs = _ptrs(W)
+        gm = {GEMV_STORE: 0 if out.dtype == torch.bfloat16 else 5, GEMV_SWIGLU: 1, GEMV_ADD_F32: 3}[mode]
+        gemm_grouped(x, ptrs[0], ptrs[1], _identity_off(T, x.device), W.N, W.K, gm, None, out, 1)
+        return out
     Wd = _dense_weight(W)
     y = x.to(Wd.dtype) @ Wd.t()
     if mode == GEMV_SWIGLU:
@@ -166,6 +171,33 @@ def moe_nt_hint(n_pairs: int, n_experts: int) -> int:
     an extra pass over its weights, which is rarer than paying registers on every tile)."""
     mean = n_pairs / max(1, n_experts)
     return 1 if mean <= 4 else (2 if mean <= 10 else 4)
+
+
+_STATUS: dict = {}
+
+
+def gemm_status(dev) -> torch.Tensor:
+    """Per-device int32 error word of the tcgen05 GEMM (bit 4: a pipeline wait timed out)."""
+    key = str(dev)
+    t = _STATUS.get(key)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=dev)
+        _STATUS[key] = t
+    return t
+
+
+def gemm_grouped(x, qw_ptrs, sm_ptrs, row_off, N, K, mode, route_w, out, G, max_rows_per_group=None):
+    """tcgen05 GEMM over G contiguous row groups of x (bf16 [M, K]) with 4-bit weights.
+    mode: 0 bf16 store, 1 SwiGLU, 2 f32 * route_w[row], 3 f32 +=, 5 f32 store."""
+    M = x.shape[0]
+    if M == 0:
+        return out
+    max_mtiles = (M + 127) // 128 + G
+    ext().tc_gemm_q4(x, qw_ptrs, sm_ptrs, row_off, N, K, mode,
+                     route_w if route_w is not None else _EMPTY_F32(x.device), out, gemm_status(x.device),
+                     max_mtiles)
+    _launched()
+    return out
 
 
 def linear_grouped(x: torch.Tensor, bank, tok_off: torch.Tensor, tok_idx: torch.Tensor | None,

@@ -159,7 +159,14 @@ def _local_experts_apply(rows, ids, w, gu, dn, erange) -> torch.Tensor:
     tok_idx = tok.int().contiguous()
     P = sel.numel()
     f = gu.N // 2
-    if rows.is_cuda and gu.qw is not None and int(counts.max()) <= 256:
+    if rows.is_cuda and gu.qw is not None and P > 256 and gu.N % 128 == 0 and dn.N % 128 == 0:
+        # prefill-sized: gather rows per expert, then grouped tcgen05 GEMMs
+        a_rows = rows.index_select(0, tok.long()).contiguous()
+        mid = torch.empty(P, f, dtype=rows.dtype, device=dev)
+        ops.gemm_grouped(a_rows, gu.qw_ptrs, gu.sm_ptrs, tok_off, gu.N, gu.K, 1, None, mid, eb - ea)
+        yp = torch.empty(P, H, dtype=torch.float32, device=dev)
+        ops.gemm_grouped(mid, dn.qw_ptrs, dn.sm_ptrs, tok_off, dn.N, dn.K, 2, pw, yp, eb - ea)
+    elif rows.is_cuda and gu.qw is not None and int(counts.max()) <= 256:
         mid = torch.empty(P, f, dtype=rows.dtype, device=dev)
         ops.linear_grouped(rows, gu, tok_off, tok_idx, mid, ops.GEMV_SWIGLU, qw_ptrs=gu.qw_ptrs, sm_ptrs=gu.sm_ptrs)
         yp = torch.empty(P, H, dtype=torch.float32, device=dev)

@@ -1,0 +1,129 @@
+"""Native host runtime: SPSC rings (in-process and shared memory across processes), the
+data-plane frame codec (byte layout + CRC32C), the MoE split rule against a direct
+transcription of its definition, the pread I/O pool and the metric histograms."""
+import multiprocessing as mp
+import os
+import random
+
+import torch
+
+from syntropy_b200._ext import ext
+
+
+def test_spsc_ring_fifo_and_full():
+    r = ext().SpscRing(8, 64)
+    for i in range(8):
+        assert r.push(bytes([i]) * (i + 1))
+    assert not r.push(b"x")  # full
+    for i in range(8):
+        assert r.pop() == bytes([i]) * (i + 1)
+    assert r.pop() is None
+
+
+def _consumer(name, size, n, q):
+    e = ext()
+    reg = e.ShmRegion(name, size, False)
+    r = e.SpscRing(reg.address(), 0, 0, False)
+    got = []
+    while len(got) < n:
+        m = r.pop()
+        if m is not None:
+            got.append(int.from_bytes(m, "little"))
+    q.put(got)
+
+
+def test_spsc_ring_across_processes():
+    e = ext()
+    name = f"/syn_test_{os.getpid()}"
+    size = e.SpscRing.bytes_needed(64, 16) + 4096
+    reg = e.ShmRegion(name, size, True)
+    r = e.SpscRing(reg.address(), 64, 16, True)
+    ctx = mp.get_context("fork")
+    q = ctx.Queue()
+    p = ctx.Process(target=_consumer, args=(name, size, 1000, q))
+    p.start()
+    i = 0
+    while i < 1000:
+        if r.push(i.to_bytes(8, "little")):
+            i += 1
+    assert q.get(timeout=60) == list(range(1000))
+    p.join(timeout=30)
+
+
+def test_frame_roundtrip_and_layout():
+    e = ext()
+    ext_b, pay = b"abc", bytes(range(200))
+    f = e.frame_encode(0x01, 0x8, 7, 3, 4, 99, 5, ext_b, pay)
+    assert f[:4] == b"SYNF" and f[4] == 1 and f[5] == 0x01
+    assert len(f) == 64 + 64 + 200
+    assert int.from_bytes(f[48:52], "little") == 64 and int.from_bytes(f[52:56], "little") == 200
+    assert int.from_bytes(f[56:60], "little") == e.crc32c(pay)
+    rc, spec, x, p = e.frame_decode(f)
+    assert rc == 0 and spec["step"] == 99 and spec["chan_seq"] == 5 and spec["instance"] == 7
+    assert x[:3] == ext_b and p == pay
+    bad = bytearray(f)
+    bad[100] ^= 1
+    assert e.frame_decode(bytes(bad))[0] == 3  # header CRC covers the extension
+    bad = bytearray(f)
+    bad[-1] ^= 1
+    assert e.frame_decode(bytes(bad))[0] == 4
+
+
+def test_crc32c_known_value():
+    # RFC 3720 (iSCSI) check value for "123456789"
+    assert ext().crc32c(b"123456789") == 0xE3069283
+
+
+def _assign_by_definition(route, eligible, n_experts, b_copy, expert_bytes, copy_slots):
+    MISS, HIT, CPU = 0xFFFFFFFF, 0xFFFFFFFF, 0xFFFFFFFE
+    out = []
+    elig = lambda e: e < n_experts and (eligible[e >> 5] >> (e & 31)) & 1  # noqa: E731
+    for i, (e, t, slot) in enumerate(route):
+        if slot != MISS:
+            out.append(HIT)
+        elif elig(e):
+            c = sum(1 for j, (f, u, s2) in enumerate(route)
+                    if s2 == MISS and elig(f) and (u > t or (u == t and (f < e or (f == e and j < i)))))
+            ok = c < copy_slots and expert_bytes <= b_copy and (c + 1) * expert_bytes <= b_copy
+            out.append(c if ok else CPU)
+        else:
+            out.append(CPU)
+    return out
+
+
+def test_moe_assign_matches_definition():
+    rng = random.Random(0)
+    for _ in range(200):
+        n_exp = rng.choice([8, 64, 128, 256])
+        n = rng.randint(1, 40)
+        route = [(rng.randrange(n_exp), rng.randint(1, 9), rng.choice([0xFFFFFFFF, 0xFFFFFFFF, 3])) for _ in range(n)]
+        eligible = [rng.getrandbits(32) for _ in range((n_exp + 31) // 32)]
+        b_copy, eb, cs = rng.randint(0, 10) * 100, rng.choice([50, 100, 300]), rng.randint(0, 6)
+        got = ext().moe_assign(torch.tensor(route, dtype=torch.int64), torch.tensor(
+            [x - (1 << 32) if x >= (1 << 31) else x for x in eligible], dtype=torch.int32), n_exp, b_copy, eb, cs)
+        assert got.tolist() == _assign_by_definition(route, eligible, n_exp, b_copy, eb, cs)
+
+
+def test_io_pool_reads_extents(tmp_path):
+    data = os.urandom(3 * 4096 + 123)
+    p = tmp_path / "blob.bin"
+    p.write_bytes(data)
+    buf = torch.zeros(len(data), dtype=torch.uint8)
+    pool = ext().IoPool(3)
+    pool.submit(str(p), 0, 4096, buf.data_ptr())
+    pool.submit(str(p), 4096, 2 * 4096 + 123, buf.data_ptr() + 4096)
+    assert pool.wait_all() == len(data)
+    assert bytes(buf.numpy()) == data
+
+
+def test_histogram_quantiles():
+    h = ext().Histogram()
+    for v in range(1, 10001):
+        h.record(v)
+    assert h.count() == 10000
+    q50 = h.quantile(0.5)
+    assert 0.85 * 5000 <= q50 <= 5000 * 1.01
+    c = ext().Counter()
+    c.add(5)
+    c.add(7)
+    assert c.get() == 12
