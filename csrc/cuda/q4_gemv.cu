@@ -264,6 +264,221 @@ static cudaError_t launch_v2(const GemvArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+
+__device__ __forceinline__ void cp_async16_g(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+               "l"(gmem));
+}
+__device__ __forceinline__ void cp_async8_g(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+               "l"(gmem));
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+// v3: per-warp cp.async ring of packed weight groups (no registers held by loads in
+// flight) and per-CTA block sums of x in shared memory (no extra MMAs for the min term).
+// Warp tile: R 16-row tiles x NT 8-token tiles over the full K; CTA = 4 warps = 4 tiles
+// of the same expert.  S ring slots per warp, D groups prefetched ahead.
+template <int R, int NT>
+struct GemvV3 {
+  static constexpr int WARPS = 4;
+  static constexpr int S = 8;        // ring slots per warp
+  static constexpr int D = 6;        // groups in flight ahead of the consumer
+  static constexpr int SLOT = R * 640;  // bytes per slot: R x (512 B nibbles + 128 B scales)
+  static size_t smem(int K) { return (size_t)WARPS * S * SLOT + (size_t)NT * 8 * (K / 32) * 4; }
+};
+
+template <int R, int NT>
+__global__ void __launch_bounds__(128) q4_gemv3_kernel(GemvArgs a) {
+  using C = GemvV3<R, NT>;
+  extern __shared__ __align__(16) uint8_t gsm3[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int e = blockIdx.y;
+  const int p0 = a.tok_off[e];
+  const int cnt = a.tok_off[e + 1] - p0;
+  const int n_units = a.N / (16 * R);
+  const int unit = blockIdx.x * C::WARPS + warp;
+  const int KG = a.K >> 6, KB32 = a.K >> 5;
+  uint8_t* ring = gsm3 + warp * C::S * C::SLOT;
+  float* xsum = reinterpret_cast<float*>(gsm3 + C::WARPS * C::S * C::SLOT);  // [NT*8][KB32]
+  const bool cta_active = cnt > 0 && blockIdx.x * C::WARPS < n_units;
+
+  if (cta_active) {
+    const uint8_t* qw = reinterpret_cast<const uint8_t*>(a.qw_ptrs[e]);
+    const uint8_t* smw = reinterpret_cast<const uint8_t*>(a.sm_ptrs[e]);
+    const __nv_bfloat16* xbase = reinterpret_cast<const __nv_bfloat16*>(a.x);
+    const bool active = unit < n_units;
+    for (int c0 = 0; c0 < cnt; c0 += NT * 8) {
+      const int ccount = min(cnt - c0, NT * 8);
+      const int ntc = (ccount + 7) >> 3;
+      // ---- per-CTA block sums of x for this chunk's tokens (fixed order) ----
+      __syncthreads();
+      for (int idx = threadIdx.x; idx < ntc * 8 * KB32; idx += blockDim.x) {
+        const int j = idx / KB32, kb = idx % KB32;
+        float sacc = 0.f;
+        if (j < ccount) {
+          const int pp = p0 + c0 + j;
+          const int row = a.tok_idx ? a.tok_idx[pp] : pp;
+          const uint4* xp = reinterpret_cast<const uint4*>(xbase + (int64_t)row * a.ldx + kb * 32);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint4 v = __ldg(xp + c);
+            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float2 f = unpack_bf16x2(w4[i]);
+              sacc += f.x + f.y;
+            }
+          }
+        }
+        xsum[j * KB32 + kb] = sacc;
+      }
+      __syncthreads();
+      if (!active) continue;
+      const __nv_bfloat16* xr[NT];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int j = min(nt * 8 + g, ccount - 1);
+        const int pp = p0 + c0 + j;
+        const int row = a.tok_idx ? a.tok_idx[pp] : pp;
+        xr[nt] = xbase + (int64_t)row * a.ldx + 2 * t;
+      }
+      float acc[R][NT][4];
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[r][nt][i] = 0.f;
+
+      auto issue = [&](int kg) {
+        uint8_t* slot = ring + (kg % C::S) * C::SLOT;
+        if (kg < KG) {
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const int64_t tk = (int64_t)(unit * R + r) * KG + kg;
+            cp_async16_g(slot + r * 640 + lane * 16, qw + tk * 512 + lane * 16);
+            if (lane < 8) cp_async16_g(slot + r * 640 + 512 + lane * 16, smw + tk * 128 + lane * 16);
+          }
+        }
+        cp_commit();  // empty groups keep the wait_group arithmetic uniform
+      };
+#pragma unroll
+      for (int i = 0; i < C::D; ++i) issue(i);
+      for (int kg = 0; kg < KG; ++kg) {
+        issue(kg + C::D);
+        cp_wait<C::D>();
+        __syncwarp();
+        const uint8_t* slot = ring + (kg % C::S) * C::SLOT;
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          uint32_t af[R][2][4];
+          float dlo[R], dhi[R], mlo[R], mhi[R];
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const uint4 q = *reinterpret_cast<const uint4*>(slot + r * 640 + lane * 16);
+            const uint32_t w0 = b ? q.z : q.x;
+            const uint32_t w1 = b ? q.w : q.y;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              af[r][0][j] = lop3_and_or(w0 >> (4 * j), 0x000F000Fu, 0x43004300u);
+              af[r][1][j] = lop3_and_or(w1 >> (4 * j), 0x000F000Fu, 0x43004300u);
+            }
+            const half2 hl = *reinterpret_cast<const half2*>(slot + r * 640 + 512 + g * 8 + b * 4);
+            const half2 hh = *reinterpret_cast<const half2*>(slot + r * 640 + 512 + (g + 8) * 8 + b * 4);
+            dlo[r] = __low2float(hl);
+            dhi[r] = __low2float(hh);
+            mlo[r] = fmaf(-128.f, dlo[r], __high2float(hl));
+            mhi[r] = fmaf(-128.f, dhi[r], __high2float(hh));
+          }
+          const int k0 = kg * 64 + b * 32;
+          const int kb32 = kg * 2 + b;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            if (nt < ntc) {
+              uint32_t bf[2][2];
+              bf[0][0] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0));
+              bf[0][1] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0 + 8));
+              bf[1][0] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0 + 16));
+              bf[1][1] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0 + 24));
+              const float xs0 = xsum[(nt * 8 + 2 * t) * KB32 + kb32];
+              const float xs1 = xsum[(nt * 8 + 2 * t + 1) * KB32 + kb32];
+#pragma unroll
+              for (int r = 0; r < R; ++r) {
+                float blk[4] = {0.f, 0.f, 0.f, 0.f};
+                mma_bf16_16816(blk, af[r][0], bf[0], blk);
+                mma_bf16_16816(blk, af[r][1], bf[1], blk);
+                acc[r][nt][0] += fmaf(dlo[r], blk[0], mlo[r] * xs0);
+                acc[r][nt][1] += fmaf(dlo[r], blk[1], mlo[r] * xs1);
+                acc[r][nt][2] += fmaf(dhi[r], blk[2], mhi[r] * xs0);
+                acc[r][nt][3] += fmaf(dhi[r], blk[3], mhi[r] * xs1);
+              }
+            }
+          }
+        }
+        __syncwarp();
+      }
+      cp_wait<0>();
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int tile = unit * R + r;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const int j = nt * 8 + 2 * t + hf;
+            if (j >= ccount) continue;
+            const int p = p0 + c0 + j;
+            if (a.mode == GEMV_SWIGLU) {
+              const float gv = acc[r][nt][hf], uv = acc[r][nt][2 + hf];
+              reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)p * (a.N / 2) + tile * 8 + g] = f2bf(silu(gv) * uv);
+            } else {
+              gemv_store(a, p, tile * 16 + g, acc[r][nt][hf]);
+              gemv_store(a, p, tile * 16 + g + 8, acc[r][nt][2 + hf]);
+            }
+          }
+        }
+      }
+    }
+  }
+  if (a.done_ctr != nullptr) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned total = gridDim.x * gridDim.y;
+      const unsigned prev = atomicAdd(a.done_ctr, 1u);
+      if (prev == total - 1) {
+        *a.done_ctr = 0u;
+        __threadfence_system();
+        const uint32_t seq = (*a.step_ctr) * (uint32_t)a.n_layers + (uint32_t)a.layer + 1u;
+        for (int q = 0; q < a.sig_n; ++q)
+          st_release_sys(reinterpret_cast<uint32_t*>(a.sig_peers[q] + a.sig_off) + a.sig_rank, seq);
+      }
+    }
+  }
+}
+
+template <int R, int NT>
+static cudaError_t launch_v3(const GemvArgs& a, cudaStream_t s) {
+  using C = GemvV3<R, NT>;
+  const int units = a.N / (16 * R);
+  const int gx = (units + C::WARPS - 1) / C::WARPS;
+  const size_t smem = C::smem(a.K);
+  static size_t set_for = 0;
+  if (smem > 48 * 1024 && smem > set_for) {
+    cudaError_t e = cudaFuncSetAttribute(q4_gemv3_kernel<R, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    set_for = smem;
+  }
+  dim3 grid((unsigned)gx, (unsigned)a.E);
+  q4_gemv3_kernel<R, NT><<<grid, C::WARPS * 32, smem, s>>>(a);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {
   // Tile shape: NT from the caller's bound on rows per expert; two row tiles per warp when
   // several token tiles share them; split K across warps only when there are too few
@@ -273,12 +488,12 @@ cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {
   const long units = (long)(a.N / (16 * R)) * a.E_active_hint;
   const bool split = units < 148L * 16;
   if (R == 1) {
-    if (nt == 1) return split ? launch_v2<1, 1, 8>(a, s) : launch_v2<1, 1, 1>(a, s);
-    if (nt == 2) return split ? launch_v2<1, 2, 8>(a, s) : launch_v2<1, 2, 1>(a, s);
-    return split ? launch_v2<1, 4, 8>(a, s) : launch_v2<1, 4, 1>(a, s);
+    if (nt == 1) return split ? launch_v2<1, 1, 8>(a, s) : launch_v3<1, 1>(a, s);
+    if (nt == 2) return split ? launch_v2<1, 2, 8>(a, s) : launch_v3<1, 2>(a, s);
+    return split ? launch_v2<1, 4, 8>(a, s) : launch_v3<1, 4>(a, s);
   }
-  if (nt == 2) return split ? launch_v2<2, 2, 8>(a, s) : launch_v2<2, 2, 1>(a, s);
-  return split ? launch_v2<2, 4, 8>(a, s) : launch_v2<2, 4, 1>(a, s);
+  if (nt == 2) return split ? launch_v2<2, 2, 8>(a, s) : launch_v3<2, 2>(a, s);
+  return split ? launch_v2<2, 4, 8>(a, s) : launch_v3<2, 4>(a, s);
 }
 
 }  // namespace syn
