@@ -18,6 +18,8 @@
 //    order (deterministic); one CTA per (16-row tile, expert).
 #include "common.cuh"
 #include "syn/q4.h"
+#include <cstdlib>
+
 #include "sync.cuh"
 
 namespace syn {
@@ -287,7 +289,9 @@ struct GemvV3 {
   static constexpr int S = 8;        // ring slots per warp
   static constexpr int D = 6;        // groups in flight ahead of the consumer
   static constexpr int SLOT = R * 640;  // bytes per slot: R x (512 B nibbles + 128 B scales)
-  static size_t smem(int K) { return (size_t)WARPS * S * SLOT + (size_t)NT * 8 * (K / 32) * 4; }
+  static size_t smem(int K, bool xsum_global) {
+    return (size_t)WARPS * S * SLOT + (xsum_global ? 0 : (size_t)NT * 8 * (K / 32) * 4);
+  }
 };
 
 template <int R, int NT>
@@ -311,40 +315,73 @@ __global__ void __launch_bounds__(128) q4_gemv3_kernel(GemvArgs a) {
     const uint8_t* smw = reinterpret_cast<const uint8_t*>(a.sm_ptrs[e]);
     const __nv_bfloat16* xbase = reinterpret_cast<const __nv_bfloat16*>(a.x);
     const bool active = unit < n_units;
+    auto issue = [&](int kg) {
+      uint8_t* slot = ring + (kg % C::S) * C::SLOT;
+      if (active && kg < KG) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const int64_t tk = (int64_t)(unit * R + r) * KG + kg;
+          cp_async16_g(slot + r * 640 + lane * 16, qw + tk * 512 + lane * 16);
+          if (lane < 8) cp_async16_g(slot + r * 640 + 512 + lane * 16, smw + tk * 128 + lane * 16);
+        }
+      }
+      cp_commit();  // empty groups keep the wait_group arithmetic uniform
+    };
     for (int c0 = 0; c0 < cnt; c0 += NT * 8) {
       const int ccount = min(cnt - c0, NT * 8);
       const int ntc = (ccount + 7) >> 3;
-      // ---- per-CTA block sums of x for this chunk's tokens (fixed order) ----
-      __syncthreads();
-      for (int idx = threadIdx.x; idx < ntc * 8 * KB32; idx += blockDim.x) {
-        const int j = idx / KB32, kb = idx % KB32;
-        float sacc = 0.f;
-        if (j < ccount) {
-          const int pp = p0 + c0 + j;
-          const int row = a.tok_idx ? a.tok_idx[pp] : pp;
-          const uint4* xp = reinterpret_cast<const uint4*>(xbase + (int64_t)row * a.ldx + kb * 32);
+      // weights start streaming before the block sums are formed
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint4 v = __ldg(xp + c);
-            const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+      for (int i = 0; i < C::D; ++i) issue(i);
+      // ---- block sums of x for this chunk's tokens (fixed order) ----
+      const float* xsg = a.xsum;  // optional precomputed [rows][K/32]
+      if (xsg == nullptr) {
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < ntc * 8 * KB32; idx += blockDim.x) {
+          const int j = idx / KB32, kb = idx % KB32;
+          float sacc = 0.f;
+          if (j < ccount) {
+            const int pp = p0 + c0 + j;
+            const int row = a.tok_idx ? a.tok_idx[pp] : pp;
+            const uint4* xp = reinterpret_cast<const uint4*>(xbase + (int64_t)row * a.ldx + kb * 32);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float2 f = unpack_bf16x2(w4[i]);
-              sacc += f.x + f.y;
+            for (int c = 0; c < 4; ++c) {
+              const uint4 v = __ldg(xp + c);
+              const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float2 f = unpack_bf16x2(w4[i]);
+                sacc += f.x + f.y;
+              }
             }
           }
+          xsum[j * KB32 + kb] = sacc;
         }
-        xsum[j * KB32 + kb] = sacc;
+        __syncthreads();
       }
-      __syncthreads();
-      if (!active) continue;
+      if (!active) {
+        cp_wait<0>();
+        continue;
+      }
       const __nv_bfloat16* xr[NT];
+      const float* xsr[NT][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const int j = min(nt * 8 + g, ccount - 1);
         const int pp = p0 + c0 + j;
         const int row = a.tok_idx ? a.tok_idx[pp] : pp;
         xr[nt] = xbase + (int64_t)row * a.ldx + 2 * t;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int jj = min(nt * 8 + 2 * t + hf, ccount - 1);
+          if (xsg) {
+            const int pj = p0 + c0 + jj;
+            const int rj = a.tok_idx ? a.tok_idx[pj] : pj;
+            xsr[nt][hf] = xsg + (int64_t)rj * KB32;
+          } else {
+            xsr[nt][hf] = xsum + (nt * 8 + 2 * t + hf) * KB32;
+          }
+        }
       }
       float acc[R][NT][4];
 #pragma unroll
@@ -354,20 +391,6 @@ __global__ void __launch_bounds__(128) q4_gemv3_kernel(GemvArgs a) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) acc[r][nt][i] = 0.f;
 
-      auto issue = [&](int kg) {
-        uint8_t* slot = ring + (kg % C::S) * C::SLOT;
-        if (kg < KG) {
-#pragma unroll
-          for (int r = 0; r < R; ++r) {
-            const int64_t tk = (int64_t)(unit * R + r) * KG + kg;
-            cp_async16_g(slot + r * 640 + lane * 16, qw + tk * 512 + lane * 16);
-            if (lane < 8) cp_async16_g(slot + r * 640 + 512 + lane * 16, smw + tk * 128 + lane * 16);
-          }
-        }
-        cp_commit();  // empty groups keep the wait_group arithmetic uniform
-      };
-#pragma unroll
-      for (int i = 0; i < C::D; ++i) issue(i);
       for (int kg = 0; kg < KG; ++kg) {
         issue(kg + C::D);
         cp_wait<C::D>();
@@ -404,8 +427,8 @@ __global__ void __launch_bounds__(128) q4_gemv3_kernel(GemvArgs a) {
               bf[0][1] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0 + 8));
               bf[1][0] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0 + 16));
               bf[1][1] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0 + 24));
-              const float xs0 = xsum[(nt * 8 + 2 * t) * KB32 + kb32];
-              const float xs1 = xsum[(nt * 8 + 2 * t + 1) * KB32 + kb32];
+              const float xs0 = xsr[nt][0][kb32];
+              const float xs1 = xsr[nt][1][kb32];
 #pragma unroll
               for (int r = 0; r < R; ++r) {
                 float blk[4] = {0.f, 0.f, 0.f, 0.f};
@@ -466,7 +489,7 @@ static cudaError_t launch_v3(const GemvArgs& a, cudaStream_t s) {
   using C = GemvV3<R, NT>;
   const int units = a.N / (16 * R);
   const int gx = (units + C::WARPS - 1) / C::WARPS;
-  const size_t smem = C::smem(a.K);
+  const size_t smem = C::smem(a.K, a.xsum != nullptr);
   static size_t set_for = 0;
   if (smem > 48 * 1024 && smem > set_for) {
     cudaError_t e = cudaFuncSetAttribute(q4_gemv3_kernel<R, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -479,6 +502,36 @@ static cudaError_t launch_v3(const GemvArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+// Block sums of x: out[r][b] = sum_{i<32} x[r][32 b + i] in f32 (fixed order).
+__global__ void block_sums_kernel(const __nv_bfloat16* __restrict__ x, int rows, int K, int ldx,
+                                  float* __restrict__ out) {
+  const int KB32 = K / 32;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)rows * KB32) return;
+  const int r = (int)(idx / KB32), b = (int)(idx % KB32);
+  const uint4* xp = reinterpret_cast<const uint4*>(x + (int64_t)r * ldx + b * 32);
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint4 v = __ldg(xp + c);
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = unpack_bf16x2(w4[i]);
+      s += f.x + f.y;
+    }
+  }
+  out[idx] = s;
+}
+
+cudaError_t launch_block_sums(const void* x, int rows, int K, int ldx, float* out, cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  const int64_t n = (int64_t)rows * (K / 32);
+  block_sums_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), rows, K,
+                                                                 ldx, out);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {
   // Tile shape: NT from the caller's bound on rows per expert; two row tiles per warp when
   // several token tiles share them; split K across warps only when there are too few
@@ -487,6 +540,20 @@ cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {
   const int R = (nt >= 2 && a.N % 32 == 0) ? 2 : 1;
   const long units = (long)(a.N / (16 * R)) * a.E_active_hint;
   const bool split = units < 148L * 16;
+  static int env_variant = -1;
+  if (env_variant < 0) {
+    const char* v = getenv("SYN_GEMV_VARIANT");
+    env_variant = v ? atoi(v) : 0;
+  }
+  const int variant = a.variant ? a.variant : env_variant;
+  if (!split && variant == 2) {
+    if (R == 1) {
+      if (nt == 1) return launch_v2<1, 1, 1>(a, s);
+      if (nt == 2) return launch_v2<1, 2, 1>(a, s);
+      return launch_v2<1, 4, 1>(a, s);
+    }
+    return nt == 2 ? launch_v2<2, 2, 1>(a, s) : launch_v2<2, 4, 1>(a, s);
+  }
   if (R == 1) {
     if (nt == 1) return split ? launch_v2<1, 1, 8>(a, s) : launch_v3<1, 1>(a, s);
     if (nt == 2) return split ? launch_v2<1, 2, 8>(a, s) : launch_v3<1, 2>(a, s);

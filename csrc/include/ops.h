@@ -15,7 +15,8 @@ torch::Tensor q4_tiled_to_rows(torch::Tensor qw, torch::Tensor sm, int64_t N, in
 torch::Tensor q4t_dequant(torch::Tensor qw, torch::Tensor sm, int64_t N, int64_t K);
 void q4_gemv(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
              torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor res, torch::Tensor out,
-             int64_t N, int64_t K, int64_t mode, int64_t nt_hint, int64_t e_active);
+             int64_t N, int64_t K, int64_t mode, int64_t nt_hint, int64_t e_active, torch::Tensor xsum);
+void block_sums(torch::Tensor x, torch::Tensor out);
 
 void rmsnorm(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor out);
 void moe_combine_rmsnorm(torch::Tensor x, torch::Tensor yp, torch::Tensor pair_of, torch::Tensor shared,

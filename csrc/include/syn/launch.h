@@ -42,7 +42,11 @@ struct GemvArgs {
   // launch shape hints: max rows (tokens) per expert -> n-tiles of 8; experts likely active
   int nt_hint;
   int E_active_hint;
+  // optional precomputed block sums of x: f32 [rows][K/32] (nullptr: computed per CTA)
+  const float* xsum;
+  int variant;  // 0 auto; 2 force v2 (register pipeline); 3 force v3 (cp.async ring)
 };
+cudaError_t launch_block_sums(const void* x, int rows, int K, int ldx, float* out, cudaStream_t s);
 
 // ---- prefill GEMM on tcgen05 (4-bit weights, grouped) ----
 cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, const int64_t* sm_ptrs,

@@ -73,7 +73,7 @@ torch::Tensor q4t_dequant(torch::Tensor qw, torch::Tensor sm, int64_t N, int64_t
 
 void q4_gemv(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
              torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor res, torch::Tensor out, int64_t N,
-             int64_t K, int64_t mode, int64_t nt_hint, int64_t e_active) {
+             int64_t K, int64_t mode, int64_t nt_hint, int64_t e_active, torch::Tensor xsum) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16, "x must be cuda bf16");
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be [rows, K] with unit inner stride");
   TORCH_CHECK(N % 16 == 0 && K % 64 == 0, "q4_gemv: N%16, K%64");
@@ -111,6 +111,12 @@ void q4_gemv(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torc
   a.layer = 0;
   a.nt_hint = (int)nt_hint;
   a.E_active_hint = (int)std::max<int64_t>(1, e_active);
+  a.xsum = nullptr;
+  a.variant = 0;
+  if (xsum.defined() && xsum.numel() > 0) {
+    TORCH_CHECK(xsum.is_cuda() && xsum.scalar_type() == torch::kFloat32 && xsum.size(-1) == K / 32, "xsum f32 [rows, K/32]");
+    a.xsum = xsum.data_ptr<float>();
+  }
   if (mode == 0) TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.size(-1) == N, "out bf16 [P, N]");
   if (mode == 3 || mode == 5) TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.size(-1) == N, "out f32 [P, N]");
   if (mode == 1) TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.size(-1) == N / 2, "out bf16 [P, N/2]");
@@ -402,6 +408,8 @@ void q4_gemv_ep(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, t
   a.layer = (int)layer;
   a.nt_hint = (int)nt_hint;
   a.E_active_hint = (int)std::max<int64_t>(1, e_active);
+  a.xsum = nullptr;
+  a.variant = 0;
   TORCH_CHECK(tok_off.numel() == a.E + 1, "tok_off E+1");
   const at::cuda::CUDAGuard guard(x.device());
   SYN_CHECK_CUDA(launch_q4_gemv(a, cur_stream()));
@@ -433,6 +441,17 @@ void tc_gemm_q4(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, t
                                    row_off.data_ptr<int32_t>(), (int)qw_ptrs.numel(), (int)M, (int)N, (int)K, (int)mode,
                                    mode == 2 ? route_w.data_ptr<float>() : nullptr, out.data_ptr(),
                                    status.data_ptr<int32_t>(), (int)max_mtiles, cur_stream()));
+}
+
+
+void block_sums(torch::Tensor x, torch::Tensor out) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x bf16 [rows, K]");
+  TORCH_CHECK(x.size(1) % 32 == 0, "K % 32");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == torch::kFloat32 && out.is_contiguous() &&
+                  out.numel() >= x.size(0) * (x.size(1) / 32), "out f32 [rows, K/32]");
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_block_sums(x.data_ptr(), (int)x.size(0), (int)x.size(1), (int)x.stride(0),
+                                   out.data_ptr<float>(), cur_stream()));
 }
 
 }  // namespace syn

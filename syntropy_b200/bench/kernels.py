@@ -124,6 +124,13 @@ def main():
         fn = lambda: ops.linear_grouped(h, gu, b["tok_off"], b["tok_idx"], mid, ops.GEMV_SWIGLU,  # noqa: E731
                                         qw_ptrs=gu.qw_ptrs, sm_ptrs=gu.sm_ptrs)
         report("moe_gate_up_gemv", timeit(fn), active * gu.N * gu.K * 5 // 8, extra={"active_experts": active})
+        xs = torch.empty(T, H // 32, device=dev)
+
+        def fn_pre():
+            ops.block_sums(h, xs)
+            ops.linear_grouped(h, gu, b["tok_off"], b["tok_idx"], mid, ops.GEMV_SWIGLU, qw_ptrs=gu.qw_ptrs,
+                               sm_ptrs=gu.sm_ptrs, xsum=xs)
+        report("moe_gate_up_gemv+block_sums", timeit(fn_pre), active * gu.N * gu.K * 5 // 8)
         fn = lambda: ops.linear_grouped(mid, dn, b["tok_off"], None, yp, ops.GEMV_SCALED_F32,  # noqa: E731
                                         route_w=b["pair_w"], qw_ptrs=dn.qw_ptrs, sm_ptrs=dn.sm_ptrs)
         report("moe_down_gemv", timeit(fn), active * dn.N * dn.K * 5 // 8, extra={"active_experts": active})
@@ -140,7 +147,7 @@ def main():
         def fn():
             ops.linear(x, ws[i[0] % reps], out, ops.GEMV_STORE)
             i[0] += 1
-        report(name, timeit(fn), N * K * 5 // 8)
+        report(name, timeit(fn, warmup=max(3, reps)), N * K * 5 // 8)
         del ws
     if want("router"):
         W = (torch.randn(2 * E, H, device=dev) * 0.02).to(torch.bfloat16)

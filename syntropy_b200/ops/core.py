@@ -13,7 +13,7 @@ __all__ = [
     "GEMV_STORE", "GEMV_SWIGLU", "GEMV_SCALED_F32", "GEMV_ADD_F32",
     "rms_norm", "embed", "linear", "linear_grouped", "qk_rope_kv_write", "attn_decode",
     "attn_prefill", "router_logits", "moe_topk", "moe_combine_rmsnorm", "argmax", "sample",
-    "swiglu_interleaved_ref", "interleave_gate_up", "count_launches", "DECODE_ROWS_MAX", "moe_nt_hint", "gemm_grouped", "gemm_status",
+    "swiglu_interleaved_ref", "interleave_gate_up", "count_launches", "DECODE_ROWS_MAX", "moe_nt_hint", "gemm_grouped", "gemm_status", "block_sums",
 ]
 
 GEMV_STORE, GEMV_SWIGLU, GEMV_SCALED_F32, GEMV_ADD_F32 = 0, 1, 2, 3
@@ -100,7 +100,7 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
         if kmode == 0 and out.dtype == torch.float32:
             kmode = 5
         ext().q4_gemv(x, ptrs[0], ptrs[1], _identity_off(T, x.device), _EMPTY_I32(x.device), _EMPTY_F32(x.device),
-                      _EMPTY_BF16(x.device), out, W.N, W.K, kmode, (T + 7) // 8, 1)
+                      _EMPTY_BF16(x.device), out, W.N, W.K, kmode, (T + 7) // 8, 1, _EMPTY_F32(x.device))
         _launched()
         return out
     # GEMM path (prefill): tcgen05 kernel with fused dequant and epilogue
@@ -166,6 +166,13 @@ def _EMPTY_BF16(dev):
     return _empty(torch.bfloat16, dev)
 
 
+def block_sums(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """f32 sums of every 32-element block of each row of x (the min term of 4-bit GEMVs)."""
+    ext().block_sums(x, out)
+    _launched()
+    return out
+
+
 def moe_nt_hint(n_pairs: int, n_experts: int) -> int:
     """Token tiles of 8 per expert pass: sized for the mean load (an expert above it takes
     an extra pass over its weights, which is rarer than paying registers on every tile)."""
@@ -203,7 +210,7 @@ def gemm_grouped(x, qw_ptrs, sm_ptrs, row_off, N, K, mode, route_w, out, G, max_
 def linear_grouped(x: torch.Tensor, bank, tok_off: torch.Tensor, tok_idx: torch.Tensor | None,
                    out: torch.Tensor, mode: int, route_w: torch.Tensor | None = None,
                    qw_ptrs: torch.Tensor | None = None, sm_ptrs: torch.Tensor | None = None,
-                   nt_hint: int | None = None):
+                   nt_hint: int | None = None, xsum: torch.Tensor | None = None):
     """Grouped (per-expert) linear over CSR pair lists.  bank: ExpertBank (N, K, tensors)."""
     if x.is_cuda:
         e = ext()
@@ -214,7 +221,8 @@ def linear_grouped(x: torch.Tensor, bank, tok_off: torch.Tensor, tok_idx: torch.
         e.q4_gemv(x, qw_ptrs, sm_ptrs, tok_off,
                   tok_idx if tok_idx is not None else _EMPTY_I32(x.device),
                   route_w if route_w is not None else _EMPTY_F32(x.device),
-                  _EMPTY_BF16(x.device), out, bank.N, bank.K, kmode, nt_hint, min(E, out.shape[0]))
+                  _EMPTY_BF16(x.device), out, bank.N, bank.K, kmode, nt_hint, min(E, out.shape[0]),
+                  xsum if xsum is not None else _EMPTY_F32(x.device))
         _launched()
         return out
     # CPU reference: loop over experts in ascending order
