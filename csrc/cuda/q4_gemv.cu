@@ -65,11 +65,10 @@ __device__ __forceinline__ void gemv_store(const GemvArgs& a, int p, int n, floa
 // 4-warp CTA is an independent tile, no shared memory).  U k-groups (64 columns each) of
 // weights and scales are loaded before any of them is used, so each warp keeps
 // U * R * 528 bytes in flight.
-template <int R, int NT, int KS>
-__global__ void __launch_bounds__(KS == 1 ? 128 : KS * 32)
+template <int R, int NT, int KS, int U = 4, int MINB = 1>
+__global__ void __launch_bounds__(KS == 1 ? 128 : KS * 32, MINB)
 q4_gemv2_kernel(GemvArgs a) {
   constexpr int WARPS = KS == 1 ? 4 : KS;
-  constexpr int U = 4;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int e = blockIdx.y;
@@ -250,19 +249,19 @@ q4_gemv2_kernel(GemvArgs a) {
   }
 }
 
-template <int R, int NT, int KS>
+template <int R, int NT, int KS, int U = 4, int MINB = 1>
 static cudaError_t launch_v2(const GemvArgs& a, cudaStream_t s) {
   constexpr int WARPS = KS == 1 ? 4 : KS;
   const int units = a.N / (16 * R);
   const int gx = KS == 1 ? (units + WARPS - 1) / WARPS : units;
   const size_t smem = KS > 1 ? (size_t)KS * R * NT * 4 * 32 * sizeof(float) : 0;
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(q4_gemv2_kernel<R, NT, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(q4_gemv2_kernel<R, NT, KS, U, MINB>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
   dim3 grid((unsigned)gx, (unsigned)a.E);
-  q4_gemv2_kernel<R, NT, KS><<<grid, WARPS * 32, smem, s>>>(a);
+  q4_gemv2_kernel<R, NT, KS, U, MINB><<<grid, WARPS * 32, smem, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -546,6 +545,11 @@ cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {
     env_variant = v ? atoi(v) : 0;
   }
   const int variant = a.variant ? a.variant : env_variant;
+  if (!split && R == 1 && nt == 1) {
+    if (variant == 21) return launch_v2<1, 1, 1, 8>(a, s);
+    if (variant == 22) return launch_v2<1, 1, 1, 4, 8>(a, s);
+    if (variant == 23) return launch_v2<1, 1, 1, 6, 6>(a, s);
+  }
   if (!split && variant == 2) {
     if (R == 1) {
       if (nt == 1) return launch_v2<1, 1, 1>(a, s);

@@ -1,0 +1,85 @@
+"""HTTP surfaces on CPU with the tiny model: native NDJSON generate, OpenAI completions and
+chat (plain and SSE), Anthropic messages, health/models/metrics, error shapes."""
+import json
+
+import pytest
+import torch
+
+pytest.importorskip("fastapi")
+from fastapi.testclient import TestClient  # noqa: E402
+
+from syntropy_b200.api import build_app  # noqa: E402
+from syntropy_b200.models.config import get_config  # noqa: E402
+from syntropy_b200.models.transformer import prepare_weights  # noqa: E402
+from syntropy_b200.runtime.async_engine import AsyncEngine  # noqa: E402
+from syntropy_b200.runtime.engine import LLMEngine  # noqa: E402
+from syntropy_b200.runtime.runner import ModelRunner  # noqa: E402
+from syntropy_b200.text.tokenizer import ByteTokenizer  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def client():
+    cfg = get_config("tiny-llama")
+    mw = prepare_weights(cfg, "cpu", seed=0)
+    aeng = AsyncEngine(LLMEngine(ModelRunner(mw, max_batch=4, max_seq_len=256)))
+    app = build_app(aeng, ByteTokenizer(cfg.vocab), model_id="tiny")
+    with TestClient(app) as c:
+        yield c
+    aeng.close()
+
+
+def test_health_models_version(client):
+    assert client.get("/healthz").json()["status"] == "ok"
+    assert client.get("/v1/models").json()["data"][0]["id"] == "tiny"
+    assert "version" in client.get("/v1/syntropy/version").json()
+
+
+def test_native_generate_ndjson(client):
+    r = client.post("/v1/syntropy/generate", json={"model": "tiny", "tokens": [5, 6, 7, 8],
+                                                   "sampling": {"max_tokens": 5}, "return_tokens": True})
+    lines = [json.loads(x) for x in r.text.strip().splitlines()]
+    assert lines[0]["event"] == "started" and lines[-1]["event"] == "done"
+    toks = [t for x in lines if x["event"] == "text" for t in x["tokens"]]
+    assert len(toks) == 5 and lines[-1]["usage"]["completion_tokens"] == 5
+    assert [x["id"].split(":")[1] for x in lines] == [str(i) for i in range(len(lines))]
+
+
+def test_native_generate_range_check(client):
+    r = client.post("/v1/syntropy/generate", json={"model": "tiny", "tokens": [1, 99999]})
+    assert r.status_code == 400 and r.json()["error"]["type"] == "token_id_out_of_range"
+    r = client.post("/v1/syntropy/generate", json={"model": "tiny", "tokens": [1], "bogus": 1})
+    assert r.status_code == 400
+
+
+def test_openai_completions_and_chat(client):
+    r = client.post("/v1/completions", json={"model": "tiny", "prompt": "hello", "max_tokens": 4, "temperature": 0})
+    j = r.json()
+    assert j["object"] == "text_completion" and j["usage"]["completion_tokens"] == 4
+    r = client.post("/v1/chat/completions", json={"model": "tiny", "messages": [{"role": "user", "content": "hi"}],
+                                                  "max_tokens": 3, "temperature": 0})
+    j = r.json()
+    assert j["choices"][0]["message"]["role"] == "assistant" and j["usage"]["completion_tokens"] == 3
+    r = client.post("/v1/chat/completions", json={"model": "tiny", "messages": [{"role": "user", "content": "hi"}],
+                                                  "max_tokens": 3, "stream": True, "temperature": 0.7, "seed": 1})
+    events = [x for x in r.text.split("\n\n") if x.startswith("data: ")]
+    assert events[-1] == "data: [DONE]"
+    assert json.loads(events[-2][6:])["choices"][0]["finish_reason"] == "length"
+
+
+def test_anthropic_messages(client):
+    r = client.post("/v1/messages", json={"model": "tiny", "max_tokens": 3,
+                                          "messages": [{"role": "user", "content": "hi"}]})
+    j = r.json()
+    assert j["type"] == "message" and j["usage"]["output_tokens"] == 3 and j["stop_reason"] == "max_tokens"
+    r = client.post("/v1/messages", json={"model": "tiny", "messages": [{"role": "user", "content": "x"}]})
+    assert r.status_code == 400
+    r = client.post("/v1/messages", json={"model": "tiny", "max_tokens": 2, "stream": True,
+                                          "messages": [{"role": "user", "content": "hi"}]})
+    kinds = [x.split("\n")[0] for x in r.text.strip().split("\n\n")]
+    assert kinds[0] == "event: message_start" and kinds[-1] == "event: message_stop"
+
+
+def test_metrics_exposed(client):
+    client.post("/v1/completions", json={"model": "tiny", "prompt": [1, 2, 3], "max_tokens": 2})
+    m = client.get("/metrics").text
+    assert "syntropy_requests_total" in m and "syntropy_generated_tokens_total" in m
