@@ -279,10 +279,9 @@ __global__ void __launch_bounds__(256, 1) tc_gemm_q4_kernel(const __grid_constan
       mbar_arrive(&raw_empty[rr]);
       if (kb >= TC_STAGES && !mbar_wait(&empty[s], ph ^ 1, a.status, &s_abort)) break;
       uint8_t* B = sB + s * B_BYTES;
-      // Dequantise to bf16 pairs: (128+q) via LOP3, minus 128 (exact), then d*q+m in one
-      // bf16x2 FMA.  Each register is two adjacent k of one row: one 4-byte store into the
-      // K-major SWIZZLE_128B tile (chunk index XOR row%8, and row%8 == g here).
-      const __nv_bfloat162 c128 = __floats2bfloat162_rn(128.f, 128.f);
+      // Dequantise: value = bf16(fma(d, q, m)) in f32 (one rounding, the reference's
+      // dequantised value), stored as pairs of adjacent k into the K-major SWIZZLE_128B tile
+      // (16-byte chunk index XOR row%8; row%8 == g for every row this thread writes).
 #pragma unroll
       for (int i = 0; i < BN / 64; ++i) {
         const int rt = pw + 4 * i;  // 16-row tile inside the BN rows
@@ -291,21 +290,20 @@ __global__ void __launch_bounds__(256, 1) tc_gemm_q4_kernel(const __grid_constan
         for (int blk = 0; blk < 2; ++blk) {
           const half2 dl = *reinterpret_cast<const half2*>(blk ? &slo[i].y : &slo[i].x);
           const half2 dh = *reinterpret_cast<const half2*>(blk ? &shi[i].y : &shi[i].x);
-          const __nv_bfloat162 d2[2] = {__float2bfloat162_rn(__low2float(dl)), __float2bfloat162_rn(__low2float(dh))};
-          const __nv_bfloat162 m2[2] = {__float2bfloat162_rn(__high2float(dl)),
-                                        __float2bfloat162_rn(__high2float(dh))};
+          const float dd[2] = {__low2float(dl), __low2float(dh)};
+          const float mm[2] = {__high2float(dl), __high2float(dh)};
 #pragma unroll
           for (int st = 0; st < 2; ++st) {
             const uint32_t w = words[blk * 2 + st];
 #pragma unroll
             for (int reg = 0; reg < 4; ++reg) {
               const int hi_row = reg & 1, hi_col = reg >> 1;
-              uint32_t qq = lop3_and_or(w >> (4 * reg), 0x000F000Fu, 0x43004300u);
-              __nv_bfloat162 v = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&qq), c128);
-              v = __hfma2(v, d2[hi_row], m2[hi_row]);
+              const float q0 = (float)((w >> (4 * reg)) & 15u);
+              const float q1 = (float)((w >> (4 * (reg + 4))) & 15u);
+              const uint32_t v = pack_bf16x2(fmaf(dd[hi_row], q0, mm[hi_row]), fmaf(dd[hi_row], q1, mm[hi_row]));
               const int row = rt * 16 + g + 8 * hi_row;
               const int chunk = (blk * 4 + st * 2 + hi_col) ^ g;
-              *reinterpret_cast<__nv_bfloat162*>(B + row * 128 + chunk * 16 + 4 * t) = v;
+              *reinterpret_cast<uint32_t*>(B + row * 128 + chunk * 16 + 4 * t) = v;
             }
           }
         }

@@ -549,6 +549,10 @@ cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {
     if (variant == 21) return launch_v2<1, 1, 1, 8>(a, s);
     if (variant == 22) return launch_v2<1, 1, 1, 4, 8>(a, s);
     if (variant == 23) return launch_v2<1, 1, 1, 6, 6>(a, s);
+    if (variant == 24) return launch_v2<1, 1, 1, 4, 10>(a, s);
+    if (variant == 25) return launch_v2<1, 1, 1, 2, 12>(a, s);
+    if (variant == 26) return launch_v2<1, 1, 1, 3, 10>(a, s);
+    if (variant == 0 || variant == 22) return launch_v2<1, 1, 1, 4, 8>(a, s);
   }
   if (!split && variant == 2) {
     if (R == 1) {

@@ -18,6 +18,7 @@ def ext():
     if _mod is not None:
         return _mod
     try:
+        import torch  # noqa: F401  (loads libc10/libtorch that the extension links against)
         _mod = importlib.import_module("syntropy_b200._C")
     except Exception as e:  # pragma: no cover - depends on the build state
         _err = e

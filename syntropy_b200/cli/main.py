@@ -1,0 +1,129 @@
+"""syntropy_b200 CLI: serve, run, plan, bench, probe, doctor, config, version."""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+
+def _engine_from_config(cfg, device: str):
+    import torch
+
+    from ..models.config import get_config
+    from ..models.transformer import prepare_weights
+    from ..runtime.engine import LLMEngine
+    from ..runtime.runner import ModelRunner
+    mcfg = get_config(cfg.model.name)
+    if cfg.model.quant:
+        mcfg = mcfg.replace(weight_quant=cfg.model.quant)
+    dev = torch.device(device)
+    sd = None
+    if cfg.model.path:
+        from ..formats.safetensors import load_state_dict
+        sd = load_state_dict(cfg.model.path)
+    mw = prepare_weights(mcfg, dev, seed=cfg.model.seed, state_dict=sd, max_pos=cfg.model.max_seq_len + 16)
+    if cfg.tier.expert_cache_frac < 1.0 and mcfg.is_moe and dev.type == "cuda":
+        from ..experts.cache import ExpertCache
+        ExpertCache(mw.layers, cfg.tier.expert_cache_frac, dev)
+    runner = ModelRunner(mw, max_batch=cfg.sched.max_batch, max_seq_len=cfg.model.max_seq_len,
+                         use_graphs=cfg.sched.cuda_graphs and cfg.feature("cuda_graph"))
+    return LLMEngine(runner, max_prefill_tokens=cfg.sched.max_prefill_tokens), mcfg
+
+
+def cmd_version(args, cfg):
+    from .. import __version__
+    print(json.dumps({"version": __version__, "arch": "sm_100a"}))
+
+
+def cmd_config(args, cfg):
+    print(json.dumps({"config": cfg.to_dict(), "origin": cfg.origin}, indent=2))
+
+
+def cmd_plan(args, cfg):
+    from ..models.config import get_config
+    from ..planner import plan_placement
+    p = plan_placement(get_config(cfg.model.name), args.gpus, args.batch, args.ctx,
+                       cache_frac=args.expert_cache_frac, fused=cfg.parallel.fused_collectives)
+    print(p.describe() if args.explain else json.dumps({"mode": p.stages[0].mode.value,
+                                                        "expert_cache_frac": p.expert_cache_frac,
+                                                        "predicted_step_ms": p.predicted_step_ms}))
+
+
+def cmd_run(args, cfg):
+    from ..runtime.engine import SamplingParams
+    from ..text.tokenizer import load_tokenizer
+    eng, mcfg = _engine_from_config(cfg, args.device)
+    tok = load_tokenizer(cfg.model.path or None, mcfg.vocab)
+    ids = [int(x) for x in args.tokens.split(",")] if args.tokens else tok.encode(args.prompt)
+    out = eng.generate([ids], SamplingParams(max_tokens=args.max_tokens, temperature=args.temperature,
+                                             seed=args.seed))[0]
+    print(json.dumps({"tokens": out, "text": tok.decode(out)}))
+
+
+def cmd_serve(args, cfg):
+    import uvicorn
+
+    from ..api import build_app
+    from ..runtime.async_engine import AsyncEngine
+    from ..text.tokenizer import load_tokenizer
+    eng, mcfg = _engine_from_config(cfg, args.device)
+    aeng = AsyncEngine(eng)
+    app = build_app(aeng, load_tokenizer(cfg.model.path or None, mcfg.vocab), model_id=cfg.api.model_id,
+                    bench_api=cfg.debug.bench_api)
+    uvicorn.run(app, host=cfg.api.host, port=cfg.api.port, log_level="warning")
+
+
+def cmd_probe(args, cfg):
+    from ..probe import probe_all
+    print(json.dumps(probe_all(quick=not args.full), indent=2))
+
+
+def cmd_doctor(args, cfg):
+    from ..probe import doctor
+    rep = doctor()
+    print(json.dumps(rep, indent=2))
+    sys.exit(0 if all(c["ok"] for c in rep["checks"]) else 1)
+
+
+def cmd_bench(args, cfg):
+    root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    os.execv(sys.executable, [sys.executable, os.path.join(root, "bench.py")] + args.rest)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(prog="syntropy_b200")
+    ap.add_argument("--config", default=None, help="TOML config file")
+    ap.add_argument("-o", "--set", action="append", default=[], help="section.key=value override")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    sub.add_parser("version")
+    sub.add_parser("config")
+    p = sub.add_parser("plan")
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--batch", type=int, default=32)
+    p.add_argument("--ctx", type=int, default=2048)
+    p.add_argument("--expert-cache-frac", type=float, default=None)
+    p.add_argument("--explain", action="store_true")
+    p = sub.add_parser("run")
+    p.add_argument("--prompt", default="Hello")
+    p.add_argument("--tokens", default="")
+    p.add_argument("--max-tokens", type=int, default=16)
+    p.add_argument("--temperature", type=float, default=0.0)
+    p.add_argument("--seed", type=int, default=None)
+    p.add_argument("--device", default="cuda:0")
+    p = sub.add_parser("serve")
+    p.add_argument("--device", default="cuda:0")
+    p = sub.add_parser("probe")
+    p.add_argument("--full", action="store_true")
+    sub.add_parser("doctor")
+    p = sub.add_parser("bench")
+    p.add_argument("rest", nargs=argparse.REMAINDER)
+    args = ap.parse_args(argv)
+    from ..config import load_config
+    cfg = load_config(args.config, overrides=args.set)
+    {"version": cmd_version, "config": cmd_config, "plan": cmd_plan, "run": cmd_run, "serve": cmd_serve,
+     "probe": cmd_probe, "doctor": cmd_doctor, "bench": cmd_bench}[args.cmd](args, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,146 @@
+"""Cost-model planner: picks tensor / expert / pipeline parallelism and the expert-cache
+share for 1, 2, 4 or 8 B200s, pricing each candidate's decode step from measured
+bandwidths.
+
+Decode is priced term by term (the reference's CostTerm idea, crates/obs/src/cost_term.rs):
+  weights  = bytes streamed per step / (HBM bandwidth * kernel efficiency)
+  kv       = KV bytes read per step / HBM bandwidth
+  host     = cold-expert bytes read over PCIe / PCIe bandwidth
+  collect  = per-layer collective latency (alpha) + bytes / NVLink bandwidth (beta)
+  launch   = kernels per step * graph-launch gap
+The collective model follows crates/solver/src/collective.rs:236-333 (one-shot vs ring).
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+from dataclasses import dataclass
+
+from ..core.plan import CollectiveAlgo, ExpertOwnerMap, ParallelismMode, PlacementPlan, StagePlan, TpSplit
+from ..models.config import ModelConfig
+
+
+@dataclass
+class HardwareModel:
+    hbm_gbs: float = 6446.6        # measured copy bandwidth
+    hbm_eff: float = 0.55          # achieved fraction for 4-bit GEMV streams (measured)
+    nvlink_gbs: float = 770.0      # peer copy per direction
+    nvlink_alpha_us: float = 6.0   # one fused flag round trip
+    nccl_alpha_us: float = 18.0    # small NCCL collective latency
+    pcie_gbs: float = 55.5         # pinned H2D (measured on the B200 box)
+    vram_gb: float = 178.0
+    launch_gap_us: float = 1.2     # per kernel inside a CUDA graph
+    tflops: float = 1422.0         # sustained bf16
+
+    @classmethod
+    def from_measured(cls, path: str | None = None) -> "HardwareModel":
+        hw = cls()
+        path = path or os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
+        try:
+            with open(path) as f:
+                d = json.load(f)
+            hw.hbm_gbs = float(d.get("hbm_gbs", hw.hbm_gbs))
+            hw.tflops = float(d.get("bf16_tflops_sustained", hw.tflops))
+        except (OSError, ValueError):
+            pass
+        return hw
+
+
+def _weight_bytes(cfg: ModelConfig) -> tuple[float, float, float]:
+    """(attention+dense bytes per layer, one expert's bytes, lm_head bytes) at 5 bits/weight."""
+    bpw = 5.0 / 8 if cfg.weight_quant == "q4" else (1.0 if cfg.weight_quant == "fp8" else 2.0)
+    h = cfg.hidden
+    attn = (h * (cfg.q_dim + 2 * cfg.kv_dim) + cfg.q_dim * h) * bpw
+    expert = 3 * h * cfg.moe_ffn * bpw if cfg.is_moe else 0.0
+    head = cfg.vocab * h * bpw
+    return attn, expert, head
+
+
+def price_decode(cfg: ModelConfig, n_gpu: int, batch: int, ctx: int, mode: ParallelismMode, cache_frac: float,
+                 hw: HardwareModel, fused: bool = True) -> dict:
+    attn_b, exp_b, head_b = _weight_bytes(cfg)
+    L = cfg.n_layers
+    terms = {}
+    if cfg.is_moe:
+        E, k = cfg.n_experts, cfg.top_k
+        per_rank_tokens = batch / n_gpu if mode == ParallelismMode.EP else batch
+        # expected active experts per layer given `batch` tokens routed uniformly
+        p_active = 1.0 - (1.0 - k / E) ** batch
+        e_local = E / (n_gpu if mode == ParallelismMode.EP else 1)
+        active_local = e_local * p_active
+        hot = active_local * cache_frac
+        cold = active_local * (1.0 - cache_frac)
+        attn_rank = attn_b / (n_gpu if mode == ParallelismMode.INTRA_NODE_TP else 1)
+        terms["weights"] = L * (hot * exp_b + attn_rank) / (hw.hbm_gbs * 1e9 * hw.hbm_eff) * 1e3
+        terms["host_tier"] = L * cold * exp_b / (hw.pcie_gbs * 1e9) * 1e3
+        kv_tok = 2 * cfg.kv_dim * 2 * L
+        terms["kv"] = per_rank_tokens * ctx * kv_tok / (hw.hbm_gbs * 1e9 * 0.45) * 1e3
+        if n_gpu > 1:
+            alpha = hw.nvlink_alpha_us if fused else hw.nccl_alpha_us
+            msg = per_rank_tokens * cfg.hidden * (2 + 4 * k / n_gpu)
+            terms["collectives"] = L * 2 * (alpha * 1e-3 + msg / (hw.nvlink_gbs * 1e9) * 1e3)
+        terms["launch"] = L * 11 * hw.launch_gap_us * 1e-3
+    else:
+        tp = n_gpu if mode == ParallelismMode.INTRA_NODE_TP else 1
+        ffn_b = 3 * cfg.hidden * cfg.ffn * (5.0 / 8 if cfg.weight_quant == "q4" else 2.0)
+        terms["weights"] = L * (attn_b + ffn_b) / tp / (hw.hbm_gbs * 1e9 * hw.hbm_eff) * 1e3
+        kv_tok = 2 * cfg.kv_dim * 2 * L
+        terms["kv"] = batch * ctx * kv_tok / tp / (hw.hbm_gbs * 1e9 * 0.45) * 1e3
+        if tp > 1:
+            alpha = hw.nvlink_alpha_us if fused else hw.nccl_alpha_us
+            msg = batch * cfg.hidden * 4
+            terms["collectives"] = L * 2 * (alpha * 1e-3 + msg / (hw.nvlink_gbs * 1e9) * 1e3)
+        terms["launch"] = L * 8 * hw.launch_gap_us * 1e-3
+    terms["lm_head"] = head_b / (hw.hbm_gbs * 1e9 * 0.5) * 1e3
+    terms["total"] = sum(v for kk, v in terms.items() if kk != "total")
+    return terms
+
+
+def fits(cfg: ModelConfig, n_gpu: int, mode: ParallelismMode, cache_frac: float, hw: HardwareModel,
+         batch: int, ctx: int) -> bool:
+    attn_b, exp_b, head_b = _weight_bytes(cfg)
+    L = cfg.n_layers
+    per_gpu = head_b + 2 * cfg.vocab * cfg.hidden  # head + bf16 embedding
+    if cfg.is_moe:
+        e_local = cfg.n_experts / (n_gpu if mode == ParallelismMode.EP else 1)
+        per_gpu += L * (attn_b + e_local * exp_b * cache_frac)
+    else:
+        tp = n_gpu if mode == ParallelismMode.INTRA_NODE_TP else 1
+        per_gpu += L * (attn_b + 3 * cfg.hidden * cfg.ffn * 5 / 8) / tp
+    kv = batch * ctx * 2 * cfg.kv_dim * 2 * L / (n_gpu if mode != ParallelismMode.LOCAL else 1)
+    return (per_gpu + kv) / 1e9 < hw.vram_gb * 0.95
+
+
+def plan_placement(cfg: ModelConfig, n_gpu: int, batch: int = 32, ctx: int = 2048,
+                   cache_frac: float | None = None, hw: HardwareModel | None = None,
+                   fused: bool = True) -> PlacementPlan:
+    hw = hw or HardwareModel.from_measured()
+    cands = []
+    modes = [ParallelismMode.LOCAL] if n_gpu == 1 else [ParallelismMode.EP, ParallelismMode.INTRA_NODE_TP,
+                                                       ParallelismMode.DP]
+    if not cfg.is_moe and n_gpu > 1:
+        modes = [ParallelismMode.INTRA_NODE_TP, ParallelismMode.DP]
+    fracs = [cache_frac] if cache_frac is not None else [1.0, 0.8, 0.6, 0.4]
+    for mode in modes:
+        for fr in fracs:
+            if not fits(cfg, n_gpu, mode, fr, hw, batch, ctx):
+                continue
+            if mode == ParallelismMode.DP:
+                t = price_decode(cfg, 1, max(1, batch // n_gpu), ctx, ParallelismMode.LOCAL, fr, hw)
+            else:
+                t = price_decode(cfg, n_gpu, batch, ctx, mode, fr, hw, fused)
+            cands.append((t["total"], mode, fr, t))
+    if not cands:
+        raise ValueError(f"{cfg.name} does not fit on {n_gpu} GPU(s) at batch {batch}, ctx {ctx}")
+    cands.sort(key=lambda c: (c[0], -c[2]))
+    total, mode, fr, terms = cands[0]
+    devices = list(range(n_gpu))
+    stage = StagePlan(layers=(0, cfg.n_layers), devices=devices, mode=mode,
+                      collective=CollectiveAlgo.FUSED if fused else CollectiveAlgo.NCCL)
+    if mode == ParallelismMode.EP:
+        stage.experts = ExpertOwnerMap.contiguous(cfg.n_layers, cfg.n_experts, n_gpu)
+    if mode == ParallelismMode.INTRA_NODE_TP:
+        stage.tp = TpSplit([1.0 / n_gpu] * n_gpu)
+    return PlacementPlan(model=cfg.name, stages=[stage], expert_cache_frac=fr, max_batch=batch,
+                         predicted_step_ms=total, cost_terms={k: v for k, v in terms.items() if k != "total"})

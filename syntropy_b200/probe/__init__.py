@@ -1,0 +1,110 @@
+"""Hardware probes (HBM copy bandwidth, pinned H2D, NVLink peer copy, graph launch cost)
+and `doctor` checks.  Feed the planner's HardwareModel (reference: crates/probe)."""
+from __future__ import annotations
+
+import os
+import platform
+import time
+
+
+def _time_cuda(fn, iters=5):
+    import torch
+    fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = float("inf")
+    for _ in range(iters):
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    return best * 1e-3
+
+
+def probe_host() -> dict:
+    info = {"platform": platform.platform(), "cpus": os.cpu_count()}
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemTotal"):
+                    info["mem_gb"] = round(int(line.split()[1]) / 1e6, 1)
+        with open("/proc/cpuinfo") as f:
+            flags = next((ln for ln in f if ln.startswith("flags")), "")
+        info["avx512"] = "avx512f" in flags
+        info["amx"] = "amx_tile" in flags
+    except OSError:
+        pass
+    return info
+
+
+def probe_gpu(quick: bool = True) -> dict:
+    import torch
+    if not torch.cuda.is_available():
+        return {"available": False}
+    dev = torch.device("cuda:0")
+    p = torch.cuda.get_device_properties(dev)
+    out = {"available": True, "name": p.name, "sms": p.multi_processor_count,
+           "mem_gb": round(p.total_memory / 1e9, 1), "cc": f"{p.major}.{p.minor}", "count": torch.cuda.device_count()}
+    n = (256 if quick else 1024) << 20
+    a = torch.empty(n, dtype=torch.uint8, device=dev)
+    b = torch.empty_like(a)
+    t = _time_cuda(lambda: b.copy_(a))
+    out["hbm_copy_gbs"] = round(2 * n / t / 1e9, 1)
+    h = torch.empty(n, dtype=torch.uint8, pin_memory=True)
+    t = _time_cuda(lambda: a.copy_(h, non_blocking=True))
+    out["h2d_gbs"] = round(n / t / 1e9, 1)
+    g = torch.cuda.CUDAGraph()
+    x = torch.zeros(1, device=dev)
+    with torch.cuda.graph(g):
+        for _ in range(100):
+            x.add_(1)
+    t = _time_cuda(g.replay)
+    out["graph_kernel_gap_us"] = round(t / 100 * 1e6, 2)
+    if torch.cuda.device_count() > 1:
+        try:
+            c = torch.empty(n, dtype=torch.uint8, device="cuda:1")
+            t = _time_cuda(lambda: c.copy_(a))
+            out["peer_copy_gbs"] = round(n / t / 1e9, 1)
+        except Exception as e:  # pragma: no cover
+            out["peer_copy_error"] = str(e)
+    return out
+
+
+def probe_all(quick: bool = True) -> dict:
+    return {"host": probe_host(), "gpu": probe_gpu(quick), "time": time.time()}
+
+
+def doctor() -> dict:
+    checks = []
+
+    def chk(name, fn):
+        try:
+            r = fn()
+            checks.append({"check": name, "ok": bool(r[0]), "detail": r[1]})
+        except Exception as e:
+            checks.append({"check": name, "ok": False, "detail": str(e)})
+
+    def ext_loaded():
+        from .._ext import ext
+        m = ext()
+        return True, m.__file__
+
+    def torch_cuda():
+        import torch
+        return True, f"torch {torch.__version__}, cuda available={torch.cuda.is_available()}"
+
+    def memlock():
+        import resource
+        soft, hard = resource.getrlimit(resource.RLIMIT_MEMLOCK)
+        return True, f"RLIMIT_MEMLOCK soft={soft} hard={hard}"
+
+    def nccl():
+        import torch.distributed as d
+        return d.is_nccl_available(), "nccl available" if d.is_nccl_available() else "nccl missing"
+
+    chk("native extension", ext_loaded)
+    chk("torch", torch_cuda)
+    chk("memlock", memlock)
+    chk("nccl", nccl)
+    return {"checks": checks}
