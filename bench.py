@@ -93,6 +93,7 @@ def main():
     ap.add_argument("--decode", type=int, default=256)
     ap.add_argument("--layers", type=int, default=0, help="dev only: override layer count (invalid headline)")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--baseline", action="store_true", help="NCCL all-gather/reduce-scatter MoE data plane")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -105,38 +106,60 @@ def main():
     from syntropy_b200.runtime.runner import ModelRunner
     from syntropy_b200 import ops
 
+    from syntropy_b200.parallel.dist import init_distributed, max_over_ranks, shutdown
+
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
-    if world > 1:
-        raise SystemExit("multi-GPU bench path not built yet")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+    ctx = init_distributed(timeout_s=300)
+    rank, local = ctx.rank, ctx.local_rank
+    dev = ctx.device
     cfg = get_config(args.model)
     if args.layers:
         cfg = cfg.replace(n_layers=args.layers)
+    if args.batch % world:
+        raise SystemExit("global batch must divide over the GPUs")
+    B = args.batch // world  # data-parallel attention: each rank serves its share of sequences
+    ep = None
+    if world > 1:
+        from syntropy_b200.parallel.ep import EPGroup
+        ep = EPGroup(ctx, cfg.n_experts, cfg.top_k, cfg.hidden, cap=B, n_layers=cfg.n_layers,
+                     fused=not args.baseline)
     t0 = time.time()
-    mw = prepare_weights(cfg, dev, seed=args.seed, max_pos=args.prompt + args.decode + 16)
+    mw = prepare_weights(cfg, dev, seed=args.seed, max_pos=args.prompt + args.decode + 16,
+                         expert_range=ep.expert_range if ep else None)
     torch.cuda.synchronize()
     t_weights = time.time() - t0
-    B = args.batch
     max_len = args.prompt + args.decode
-    runner = ModelRunner(mw, max_batch=B, max_seq_len=max_len + 16)
-    eng = LLMEngine(runner, max_prefill_tokens=8192)
-    g = torch.Generator().manual_seed(1234 + rank)
-    prompts = [torch.randint(0, cfg.vocab, (args.prompt,), generator=g).tolist() for _ in range(B)]
+    runner = ModelRunner(mw, max_batch=B, max_seq_len=max_len + 16, ep=ep,
+                         use_graphs=not (ep is not None and not ep.fused))
+    eng = LLMEngine(runner, max_prefill_tokens=8192, dist_ctx=ctx)
+    g = torch.Generator().manual_seed(1234)
+    all_prompts = [torch.randint(0, cfg.vocab, (args.prompt,), generator=g).tolist() for _ in range(args.batch)]
+    prompts = all_prompts[rank::world]
     # ---- prefill: TTFT of each request (all submitted at t0) ----
     total_steps = args.warmup + args.steps
     assert total_steps + 1 <= args.decode, "warmup + steps must fit in the decode length"
     ids = [eng.add_request(p, SamplingParams(max_tokens=args.decode, temperature=0.0)) for p in prompts]
+    if ctx.enabled:
+        import torch.distributed as dist
+        dist.barrier(group=ctx.cpu_group)
     t_sub = time.perf_counter()
-    while eng.waiting:
-        eng.step()
+    if ctx.enabled:
+        while _any_waiting(ctx, eng):
+            eng.step()
+    else:
+        while eng.waiting:
+            eng.step()
     torch.cuda.synchronize()
     seqs = {s.seq_id: s for s in eng.running}
-    ttft = sorted(seqs[i].t_first_token - t_sub for i in ids)
+    my_ttft = [seqs[i].t_first_token - t_sub for i in ids]
+    if ctx.enabled:
+        import torch.distributed as dist
+        gathered = [None] * world
+        dist.all_gather_object(gathered, my_ttft, group=ctx.cpu_group)
+        my_ttft = [x for part in gathered for x in part]
+    ttft = sorted(my_ttft)
     p50_ttft_ms = 1e3 * ttft[len(ttft) // 2]
     # ---- decode: warm-up then timed steps ----
     for _ in range(args.warmup):
@@ -156,9 +179,12 @@ def main():
         e2e_s = time.perf_counter() - te
     dev_ms = sum(a.elapsed_time(b) for a, b in runner.time_events)
     assert len(runner.time_events) == args.steps
+    dev_ms = max_over_ranks(ctx, dev_ms)
+    e2e_s = max_over_ranks(ctx, e2e_s)
+    status = ep.check_status() if ep is not None else 0
     ms_step = dev_ms / args.steps
-    value = B * 1e3 / ms_step
-    e2e_value = B * args.steps / e2e_s
+    value = args.batch * 1e3 / ms_step          # whole-job tokens/s over all ranks
+    e2e_value = args.batch * args.steps / e2e_s
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
@@ -167,7 +193,8 @@ def main():
         "p50_ttft_ms": round(p50_ttft_ms, 2),
         "config": {"model": args.model if not args.layers else f"{args.model}[layers={args.layers}] (DEV, not headline)",
                    "global_batch": B, "seq_len": args.prompt, "decode_len": args.decode,
-                   "parallelism": f"ep{world}" if world > 1 else "single-gpu",
+                   "parallelism": (f"ep{world}+dp-attention" + ("" if ep is None or ep.fused else " (nccl baseline)"))
+                   if world > 1 else "single-gpu",
                    "expert_cache_frac": 1.0, "l2": "inputs larger than L2 (weights 140+ GB streamed per step)",
                    "weights_gb": round(mw.nbytes() / 1e9, 2), "weight_build_s": round(t_weights, 1)},
         "clocks": clk.summary(),
@@ -175,9 +202,20 @@ def main():
                 "d2h_bytes_per_step": 4 * B},
         "gpu_launches": (n_launch * args.steps) if n_launch else None,
         "impl": "syntropy",
+        "device_status": status,
     }
     if rank == 0:
         print(json.dumps(out))
+    runner.graphs.clear()
+    shutdown(ctx)
+
+
+def _any_waiting(ctx, eng) -> bool:
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([1 if eng.waiting else 0], dtype=torch.int64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=ctx.cpu_group)
+    return bool(t[0])
 
 
 if __name__ == "__main__":

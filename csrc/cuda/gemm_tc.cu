@@ -8,10 +8,11 @@
 //   warp 1      TMEM allocator and MMA issuer: one elected thread issues tcgen05.mma
 //               (kind::f16, M=128, N=BN, K=16, bf16 x bf16 -> f32) per 16 columns and
 //               tcgen05.commit's to the stage's "empty" barrier
-//   warps 4..7  B producers during the main loop: 4-bit weights -> bf16 (d*q+m, f32 math,
-//               one rounding) written straight into the UMMA K-major SWIZZLE_128B layout,
-//               then fence.proxy.async; afterwards the epilogue: tcgen05.ld 32x32b of their
-//               TMEM lane quarter, fused epilogue, global stores
+//   warps 4..11 B producers during the main loop (two per scheduler, so dequantisation
+//               latency hides): 4-bit weights -> bf16 (d*q+m, f32 math, one rounding)
+//               written straight into the UMMA K-major SWIZZLE_128B layout, then
+//               fence.proxy.async; afterwards the epilogue: tcgen05.ld 32x32b of their TMEM
+//               lane quarter (warp % 4) and column half, fused epilogue, global stores
 // Stages are tracked with mbarriers; every wait is bounded (the kernel records an error
 // bit and bails out instead of hanging).  Reference op: `Gemm` (crates/kernels/src/op/
 // kind.rs; f32 reference crates/kernels/src/reference/linear.rs:71).
@@ -143,8 +144,11 @@ struct TcCfg {
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * (A_BYTES + B_BYTES) + (size_t)TC_RAW * RAW_BYTES;
 };
 
+constexpr int TC_THREADS = 384;
+constexpr int TC_PRODUCERS = 8;  // warps 4..11
+
 template <int BN>
-__global__ void __launch_bounds__(256, 1) tc_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmap_a,
+__global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                             TcGemmArgs a) {
   constexpr int TC_STAGES = TcCfg<BN>::STAGES;
   constexpr int A_BYTES = TcCfg<BN>::A_BYTES;
@@ -187,12 +191,12 @@ __global__ void __launch_bounds__(256, 1) tc_gemm_q4_kernel(const __grid_constan
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) {
       mbar_init(&full_a[s], 1);
-      mbar_init(&full_b[s], 128);
+      mbar_init(&full_b[s], TC_PRODUCERS * 32);
       mbar_init(&empty[s], 1);
     }
     for (int r = 0; r < TC_RAW; ++r) {
       mbar_init(&raw_full[r], 1);
-      mbar_init(&raw_empty[r], 128);
+      mbar_init(&raw_empty[r], TC_PRODUCERS * 32);
     }
     mbar_init(&done_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -257,21 +261,22 @@ __global__ void __launch_bounds__(256, 1) tc_gemm_q4_kernel(const __grid_constan
       }
       umma_commit(&done_bar);
     }
-  } else if (warp >= 4) {
+  } else if (warp >= 4 && warp < 4 + TC_PRODUCERS) {
     // ---------------- B producers: 4-bit -> bf16 in SWIZZLE_128B layout ----------------
-    const int pw = warp - 4;
+    const int pw = warp - 4;  // 0..7
     const int g = lane >> 2, t = lane & 3;
+    constexpr int TPW = BN / 16 / TC_PRODUCERS;  // 16-row tiles per producer warp
     for (int kb = 0; kb < KB; ++kb) {
       const int s = kb % TC_STAGES;
       const uint32_t ph = (kb / TC_STAGES) & 1;
       const int rr = kb % TC_RAW;
       if (!mbar_wait(&raw_full[rr], (kb / TC_RAW) & 1, a.status, &s_abort)) break;
-      uint4 q[BN / 64];
-      uint2 slo[BN / 64], shi[BN / 64];
+      uint4 q[TPW];
+      uint2 slo[TPW], shi[TPW];
       const uint8_t* R = sR + rr * RAW_BYTES;
 #pragma unroll
-      for (int i = 0; i < BN / 64; ++i) {
-        const uint8_t* tb = R + (pw + 4 * i) * TC_TILE_RAW;
+      for (int i = 0; i < TPW; ++i) {
+        const uint8_t* tb = R + (pw + TC_PRODUCERS * i) * TC_TILE_RAW;
         q[i] = *reinterpret_cast<const uint4*>(tb + lane * 16);
         slo[i] = *reinterpret_cast<const uint2*>(tb + 512 + g * 8);
         shi[i] = *reinterpret_cast<const uint2*>(tb + 512 + (g + 8) * 8);
@@ -283,8 +288,8 @@ __global__ void __launch_bounds__(256, 1) tc_gemm_q4_kernel(const __grid_constan
       // dequantised value), stored as pairs of adjacent k into the K-major SWIZZLE_128B tile
       // (16-byte chunk index XOR row%8; row%8 == g for every row this thread writes).
 #pragma unroll
-      for (int i = 0; i < BN / 64; ++i) {
-        const int rt = pw + 4 * i;  // 16-row tile inside the BN rows
+      for (int i = 0; i < TPW; ++i) {
+        const int rt = pw + TC_PRODUCERS * i;  // 16-row tile inside the BN rows
         const uint32_t words[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
 #pragma unroll
         for (int blk = 0; blk < 2; ++blk) {
@@ -314,12 +319,14 @@ __global__ void __launch_bounds__(256, 1) tc_gemm_q4_kernel(const __grid_constan
     // ---------------- epilogue ----------------
     const bool ok = mbar_wait(&done_bar, 0, a.status, &s_abort);
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-    const int row = row0 + pw * 32 + lane;  // TMEM lane quarter of this warp
+    const int quarter = warp & 3;       // TMEM lanes this warp may read
+    const int half = (warp - 4) >> 2;   // which half of the columns it stores
+    const int row = row0 + quarter * 32 + lane;
     const bool live = ok && row < row_end && row < a.M;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
+    for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
       uint32_t r[32];
-      tmem_ld32(tmem + ((uint32_t)(pw * 32) << 16) + c0, r);
+      tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + c0, r);
       if (!live) continue;
       const int n0 = ntile * BN + c0;
       if (a.mode == 1) {  // SwiGLU over 8-column gate/up chunks
@@ -408,7 +415,7 @@ cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, co
       if (e != cudaSuccess) return e;
       set = true;
     }
-    tc_gemm_q4_kernel<256><<<grid, 256, smem, s>>>(map, a);
+    tc_gemm_q4_kernel<256><<<grid, TC_THREADS, smem, s>>>(map, a);
   } else {
     static bool set = false;
     if (!set) {
@@ -417,7 +424,7 @@ cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, co
       if (e != cudaSuccess) return e;
       set = true;
     }
-    tc_gemm_q4_kernel<128><<<grid, 256, smem, s>>>(map, a);
+    tc_gemm_q4_kernel<128><<<grid, TC_THREADS, smem, s>>>(map, a);
   }
   return cudaGetLastError();
 }

@@ -1,0 +1,81 @@
+"""Expert parallelism over NVLink on 2 GPUs: the fused dispatch/combine data plane gives
+the same greedy tokens as the NCCL baseline data plane and as one GPU holding every expert.
+Runs as two child processes (one per GPU); skipped with fewer than 2 GPUs."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+WORKER = r"""
+import json, os, sys, torch
+sys.path.insert(0, os.environ["ROOT"])
+from syntropy_b200.models.config import get_config
+from syntropy_b200.models.transformer import prepare_weights
+from syntropy_b200.runtime.engine import LLMEngine, SamplingParams
+from syntropy_b200.runtime.runner import ModelRunner
+from syntropy_b200.parallel.dist import init_distributed, shutdown
+from syntropy_b200.parallel.ep import EPGroup
+fused = os.environ["FUSED"] == "1"
+ctx = init_distributed(timeout_s=60)
+cfg = get_config("small-qwen-moe")
+ep = EPGroup(ctx, cfg.n_experts, cfg.top_k, cfg.hidden, cap=4, n_layers=cfg.n_layers, fused=fused)
+mw = prepare_weights(cfg, ctx.device, seed=7, expert_range=ep.expert_range)
+runner = ModelRunner(mw, max_batch=4, max_seq_len=256, ep=ep, use_graphs=fused)
+eng = LLMEngine(runner, dist_ctx=ctx)
+g = torch.Generator().manual_seed(3)
+prompts = [torch.randint(0, cfg.vocab, (n,), generator=g).tolist() for n in (11, 30, 7, 19)]
+outs = eng.generate(prompts[ctx.rank::ctx.world], SamplingParams(max_tokens=8))
+st = ep.check_status()
+runner.graphs.clear()
+print("RESULT " + json.dumps({"rank": ctx.rank, "outs": outs, "status": st}), flush=True)
+shutdown(ctx)
+"""
+
+
+def _run(fused: bool):
+    port = 29611 if fused else 29612
+    procs = []
+    for r in range(2):
+        env = dict(os.environ, ROOT=ROOT, FUSED="1" if fused else "0", RANK=str(r), WORLD_SIZE="2",
+                   LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        procs.append(subprocess.Popen([sys.executable, "-c", WORKER], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.STDOUT, text=True))
+    res = {}
+    for p in procs:
+        out, _ = p.communicate(timeout=600)
+        assert p.returncode == 0, out[-3000:]
+        line = [x for x in out.splitlines() if x.startswith("RESULT ")][-1]
+        d = json.loads(line[7:])
+        res[d["rank"]] = d
+    return res
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_fused_matches_baseline_and_single_gpu():
+    from syntropy_b200.models.config import get_config
+    from syntropy_b200.models.transformer import prepare_weights
+    from syntropy_b200.runtime.engine import LLMEngine, SamplingParams
+    from syntropy_b200.runtime.runner import ModelRunner
+    fused = _run(True)
+    base = _run(False)
+    same = 0
+    for r in (0, 1):
+        assert fused[r]["status"] == 0
+        same += sum(a == b for a, b in zip(fused[r]["outs"], base[r]["outs"]))
+    # fused sums the k expert rows per token; the baseline sums per-rank partials first:
+    # the f32 association differs, so a near-tie argmax may flip on a random-weight model
+    assert same >= 3
+    cfg = get_config("small-qwen-moe")
+    mw = prepare_weights(cfg, torch.device("cuda:0"), seed=7)
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, cfg.vocab, (n,), generator=g).tolist() for n in (11, 30, 7, 19)]
+    single = LLMEngine(ModelRunner(mw, max_batch=4, max_seq_len=256)).generate(prompts, SamplingParams(max_tokens=8))
+    agree = sum(a == b for r in (0, 1) for a, b in zip(fused[r]["outs"], single[r::2]))
+    assert agree >= 3  # different f32 summation association (per-rank partials) may flip a near-tie
