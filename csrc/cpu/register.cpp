@@ -35,6 +35,7 @@ void register_all(pybind11::module& m) {
   m.def("q4_gemv_ep", &q4_gemv_ep);
   m.def("tc_gemm_q4", &tc_gemm_q4);
   register_runtime(m);
+  register_formats(m);
 }
 
 }  // namespace syn

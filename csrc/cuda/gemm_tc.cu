@@ -72,6 +72,15 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
@@ -125,11 +134,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
 }
 
 struct TcGemmArgs {
+  int raw_tma;              // 1: packed weights come from the 4-D tensor maps (one bank)
   const int64_t* qw_ptrs;   // [G] tiled 4-bit weights per group
   const int64_t* sm_ptrs;   // [G]
   const int32_t* row_off;   // [G+1] rows of A per group (contiguous)
   const float* route_w;     // [M] (mode SCALED)
   void* out;
+  int group_base;           // expert index of group 0 inside the bank (raw_tma)
   int G, M, N, K;
   int mode;                 // 0 store bf16, 1 swiglu bf16 [M, N/2], 2 scaled f32, 3 add f32, 5 store f32
   int* status;
@@ -149,6 +160,8 @@ constexpr int TC_PRODUCERS = 8;  // warps 4..11
 
 template <int BN>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                                            const __grid_constant__ CUtensorMap tmap_q,
+                                                            const __grid_constant__ CUtensorMap tmap_s,
                                                             TcGemmArgs a) {
   constexpr int TC_STAGES = TcCfg<BN>::STAGES;
   constexpr int A_BYTES = TcCfg<BN>::A_BYTES;
@@ -235,11 +248,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
         if (kb >= TC_RAW && !mbar_wait(&raw_empty[r], ph ^ 1, a.status, &s_abort)) break;
         mbar_expect_tx(&raw_full[r], RAW_BYTES);
         uint8_t* dst = sR + r * RAW_BYTES;
+        if (a.raw_tma) {
+          // [BN/16 tiles x 512 B] of nibbles, then [BN/16 x 128 B] of scales: two copies
+          tma_load_4d(dst, &tmap_q, 0, kb, tile0, a.group_base + grp, &raw_full[r]);
+          tma_load_4d(dst + (BN / 16) * 512, &tmap_s, 0, kb, tile0, a.group_base + grp, &raw_full[r]);
+        } else {
 #pragma unroll 4
-        for (int i = 0; i < BN / 16; ++i) {
-          const int64_t tk = (int64_t)(tile0 + i) * KG + kb;
-          bulk_load(dst + i * TC_TILE_RAW, qw + tk * 512, 512, &raw_full[r]);
-          bulk_load(dst + i * TC_TILE_RAW + 512, sm + tk * 128, 128, &raw_full[r]);
+          for (int i = 0; i < BN / 16; ++i) {
+            const int64_t tk = (int64_t)(tile0 + i) * KG + kb;
+            bulk_load(dst + i * 512, qw + tk * 512, 512, &raw_full[r]);
+            bulk_load(dst + (BN / 16) * 512 + i * 128, sm + tk * 128, 128, &raw_full[r]);
+          }
         }
       }
     }
@@ -276,10 +295,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
       const uint8_t* R = sR + rr * RAW_BYTES;
 #pragma unroll
       for (int i = 0; i < TPW; ++i) {
-        const uint8_t* tb = R + (pw + TC_PRODUCERS * i) * TC_TILE_RAW;
-        q[i] = *reinterpret_cast<const uint4*>(tb + lane * 16);
-        slo[i] = *reinterpret_cast<const uint2*>(tb + 512 + g * 8);
-        shi[i] = *reinterpret_cast<const uint2*>(tb + 512 + (g + 8) * 8);
+        const int ti = pw + TC_PRODUCERS * i;
+        q[i] = *reinterpret_cast<const uint4*>(R + ti * 512 + lane * 16);
+        const uint8_t* sb = R + (BN / 16) * 512 + ti * 128;
+        slo[i] = *reinterpret_cast<const uint2*>(sb + g * 8);
+        shi[i] = *reinterpret_cast<const uint2*>(sb + (g + 8) * 8);
       }
       mbar_arrive(&raw_empty[rr]);
       if (kb >= TC_STAGES && !mbar_wait(&empty[s], ph ^ 1, a.status, &s_abort)) break;
@@ -386,25 +406,55 @@ static PFN_encodeTiled get_encode() {
   return fn;
 }
 
+// bank_qw/bank_sm: base of a contiguous expert bank (or of one matrix) and the number
+// of experts in it; when given (non-null), the packed weights stream with two 4-D TMA copies
+// per stage instead of 2 * BN/16 bulk copies.
 cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, const int64_t* sm_ptrs,
                               const int32_t* row_off, int G, int M, int N, int K, int mode, const float* route_w,
-                              void* out, int* status, int max_mtiles, cudaStream_t s) {
+                              void* out, int* status, int max_mtiles, const void* bank_qw, const void* bank_sm,
+                              int bank_experts, int group_base, cudaStream_t s) {
   if (K % TC_BK != 0 || N % 128 != 0 || M <= 0) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || (ldx * 2) % 16 != 0) return cudaErrorInvalidValue;
   PFN_encodeTiled enc = get_encode();
   if (!enc) return cudaErrorNotSupported;
-  CUtensorMap map;
-  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
-  const cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)TC_BM};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
-  TcGemmArgs a{qw_ptrs, sm_ptrs, row_off, route_w, out, G, M, N, K, mode, status};
+  CUtensorMap map, mq, ms;
+  memset(&mq, 0, sizeof(mq));
+  memset(&ms, 0, sizeof(ms));
+  {
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+    const cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)TC_BM};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  }
   const bool wide = (N % 256 == 0);
   const int BN = wide ? 256 : 128;
+  const int raw_tma = bank_qw != nullptr && bank_sm != nullptr &&
+                      (reinterpret_cast<uintptr_t>(bank_qw) & 15) == 0 && (reinterpret_cast<uintptr_t>(bank_sm) & 15) == 0;
+  if (raw_tma) {
+    const cuuint64_t KG = (cuuint64_t)(K / 64), NT = (cuuint64_t)(N / 16);
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    // nibbles: [expert][tile][kg][128 x u32]
+    const cuuint64_t dq[4] = {128, KG, NT, (cuuint64_t)bank_experts};
+    const cuuint64_t sq[3] = {512, 512 * KG, 512 * KG * NT};
+    const cuuint32_t bq[4] = {128, 1, (cuuint32_t)(BN / 16), 1};
+    CUresult r = enc(&mq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, const_cast<void*>(bank_qw), dq, sq, bq, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    // scales: [expert][tile][kg][32 x u32]
+    const cuuint64_t ds[4] = {32, KG, NT, (cuuint64_t)bank_experts};
+    const cuuint64_t ss[3] = {128, 128 * KG, 128 * KG * NT};
+    const cuuint32_t bs[4] = {32, 1, (cuuint32_t)(BN / 16), 1};
+    r = enc(&ms, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, const_cast<void*>(bank_sm), ds, ss, bs, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  }
+  TcGemmArgs a{raw_tma, qw_ptrs, sm_ptrs, row_off, route_w, out, group_base, G, M, N, K, mode, status};
   const size_t smem = wide ? TcCfg<256>::SMEM : TcCfg<128>::SMEM;
   dim3 grid((unsigned)max_mtiles, (unsigned)(N / BN));
   if (wide) {
@@ -415,7 +465,7 @@ cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, co
       if (e != cudaSuccess) return e;
       set = true;
     }
-    tc_gemm_q4_kernel<256><<<grid, TC_THREADS, smem, s>>>(map, a);
+    tc_gemm_q4_kernel<256><<<grid, TC_THREADS, smem, s>>>(map, mq, ms, a);
   } else {
     static bool set = false;
     if (!set) {
@@ -424,7 +474,7 @@ cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, co
       if (e != cudaSuccess) return e;
       set = true;
     }
-    tc_gemm_q4_kernel<128><<<grid, TC_THREADS, smem, s>>>(map, a);
+    tc_gemm_q4_kernel<128><<<grid, TC_THREADS, smem, s>>>(map, mq, ms, a);
   }
   return cudaGetLastError();
 }

@@ -62,8 +62,9 @@ void q4_gemv_ep(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, t
 
 void tc_gemm_q4(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor row_off, int64_t N,
                 int64_t K, int64_t mode, torch::Tensor route_w, torch::Tensor out, torch::Tensor status,
-                int64_t max_mtiles);
+                int64_t max_mtiles, torch::Tensor bank_qw, torch::Tensor bank_sm, int64_t group_base);
 
 void register_all(pybind11::module& m);
 void register_runtime(pybind11::module& m);
+void register_formats(pybind11::module& m);
 }  // namespace syn

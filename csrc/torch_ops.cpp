@@ -422,7 +422,7 @@ void q4_gemv_ep(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, t
 //   3: out f32 [M, N] += ; 5: out f32 [M, N]
 void tc_gemm_q4(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor row_off, int64_t N,
                 int64_t K, int64_t mode, torch::Tensor route_w, torch::Tensor out, torch::Tensor status,
-                int64_t max_mtiles) {
+                int64_t max_mtiles, torch::Tensor bank_qw, torch::Tensor bank_sm, int64_t group_base) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x bf16 [M, K]");
   TORCH_CHECK(x.size(1) == K && K % 64 == 0 && N % 128 == 0, "tc_gemm_q4 shapes (K%64, N%128)");
   TORCH_CHECK(row_off.is_cuda() && row_off.scalar_type() == torch::kInt32 && row_off.numel() == qw_ptrs.numel() + 1,
@@ -440,7 +440,11 @@ void tc_gemm_q4(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, t
   SYN_CHECK_CUDA(launch_tc_gemm_q4(x.data_ptr(), (int)x.stride(0), qw_ptrs.data_ptr<int64_t>(), sm_ptrs.data_ptr<int64_t>(),
                                    row_off.data_ptr<int32_t>(), (int)qw_ptrs.numel(), (int)M, (int)N, (int)K, (int)mode,
                                    mode == 2 ? route_w.data_ptr<float>() : nullptr, out.data_ptr(),
-                                   status.data_ptr<int32_t>(), (int)max_mtiles, cur_stream()));
+                                   status.data_ptr<int32_t>(), (int)max_mtiles,
+                                   bank_qw.numel() ? bank_qw.data_ptr() : nullptr,
+                                   bank_sm.numel() ? bank_sm.data_ptr() : nullptr,
+                                   bank_qw.numel() ? (int)(bank_qw.dim() == 2 ? bank_qw.size(0) : 1) : 0,
+                                   (int)group_base, cur_stream()));
 }
 
 

@@ -183,7 +183,7 @@ def main():
             sp = torch.tensor([w.sm.data_ptr()], device=dev)
             off = torch.tensor([0, M], dtype=torch.int32, device=dev)
             fn = lambda: ext().tc_gemm_q4(x, qp, sp, off, N, K, 0, torch.empty(0, device=dev), out, st,  # noqa: E731
-                                          M // 128 + 1)
+                                          M // 128 + 1, w.qw, w.sm, 0)
             report(f"tc_gemm_q4_{M}x{N}x{K}", timeit(fn, iters=10), flops=2 * M * N * K,
                    extra={"status": int(st.item())})
             wd = w.dequant()

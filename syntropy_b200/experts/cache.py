@@ -113,6 +113,7 @@ class _TieredBank:
             qv = bank.qw[: self.n_res].clone()
             sv = bank.sm[: self.n_res].clone()
             bank.qw, bank.sm = qv, sv  # VRAM keeps only the resident slots
+            bank.bank_contiguous = False
             self.parts.append({"bank": bank, "qv": qv, "sv": sv, "qh": qh, "sh": sh})
             self._write_ptrs(bank, qv, sv, qh, sh)
         if cuda:

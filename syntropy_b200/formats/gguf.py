@@ -1,0 +1,97 @@
+"""GGUF reading (native header parser): metadata, tensor infos, and Q4_1 / F16 / F32 / BF16
+tensor data.  Q4_1 blocks map 1:1 onto this framework's 4-bit interchange layout.
+Reference: crates/manifest/src/gguf.rs:75-335."""
+from __future__ import annotations
+
+import mmap
+
+import numpy as np
+import torch
+
+from .._ext import ext
+
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q4_1, GGML_Q8_0, GGML_BF16 = 0, 1, 2, 3, 8, 30
+_BLOCK = {GGML_F32: (1, 4), GGML_F16: (1, 2), GGML_Q4_0: (32, 18), GGML_Q4_1: (32, 20), GGML_Q8_0: (32, 34),
+          GGML_BF16: (1, 2)}
+
+
+class GGUFFile:
+    def __init__(self, path: str):
+        self.path = path
+        self.version, meta, tensors, self.data_start = ext().gguf_header(path)
+        self.meta = dict(meta)
+        self.tensors = {n: (t, tuple(int(d) for d in dims), int(off)) for n, t, dims, off in tensors}
+        self._f = open(path, "rb")
+        self._mm = mmap.mmap(self._f.fileno(), 0, access=mmap.ACCESS_READ)
+
+    def nbytes(self, name: str) -> int:
+        t, dims, _ = self.tensors[name]
+        n = int(np.prod(dims))
+        bs, bb = _BLOCK[t]
+        return n // bs * bb
+
+    def raw(self, name: str) -> torch.Tensor:
+        t, dims, off = self.tensors[name]
+        b = self.data_start + off
+        return torch.frombuffer(memoryview(self._mm)[b: b + self.nbytes(name)], dtype=torch.uint8).clone()
+
+    def get(self, name: str) -> torch.Tensor:
+        """Dense f32 tensor with torch shape (GGUF dims are innermost-first)."""
+        t, dims, _ = self.tensors[name]
+        shape = tuple(reversed(dims))
+        r = self.raw(name)
+        if t == GGML_F32:
+            return r.view(torch.float32).reshape(shape)
+        if t == GGML_F16:
+            return r.view(torch.float16).float().reshape(shape)
+        if t == GGML_BF16:
+            return r.view(torch.bfloat16).float().reshape(shape)
+        if t == GGML_Q4_1:
+            from .q4 import dequant_rows_ref
+            N = int(np.prod(shape[:-1]))
+            return dequant_rows_ref(r, N, shape[-1]).reshape(shape)
+        raise NotImplementedError(f"GGML type {t} for {name}")
+
+    def close(self):
+        self._mm.close()
+        self._f.close()
+
+
+def write_gguf(path: str, tensors: dict, meta: dict | None = None, alignment: int = 32):
+    """Minimal GGUF v3 writer (F32 tensors and Q4_1 row blocks) for fixtures."""
+    import struct
+
+    def s(x: str) -> bytes:
+        b = x.encode()
+        return struct.pack("<Q", len(b)) + b
+
+    meta = dict(meta or {})
+    meta["general.alignment"] = alignment
+    out = bytearray(b"GGUF" + struct.pack("<I", 3) + struct.pack("<QQ", len(tensors), len(meta)))
+    for k, v in meta.items():
+        out += s(k)
+        if isinstance(v, bool):
+            out += struct.pack("<IB", 7, int(v))
+        elif isinstance(v, int):
+            out += struct.pack("<IQ", 10, v) if v >= 0 else struct.pack("<Iq", 11, v)
+        elif isinstance(v, float):
+            out += struct.pack("<Id", 12, v)
+        else:
+            out += struct.pack("<I", 8) + s(str(v))
+    blobs, off = [], 0
+    for n, (kind, t) in tensors.items():
+        if kind == "q4_1":
+            rows, shape = t
+            raw, gtype = rows.numpy().tobytes(), GGML_Q4_1
+        else:
+            shape, raw, gtype = tuple(t.shape), t.float().contiguous().numpy().tobytes(), GGML_F32
+        out += s(n) + struct.pack("<I", len(shape)) + b"".join(struct.pack("<Q", d) for d in reversed(shape))
+        out += struct.pack("<IQ", gtype, off)
+        pad = (-len(raw)) % alignment
+        blobs.append(raw + b"\0" * pad)
+        off += len(raw) + pad
+    out += b"\0" * ((-len(out)) % alignment)
+    with open(path, "wb") as f:
+        f.write(out)
+        for b in blobs:
+            f.write(b)

@@ -42,6 +42,7 @@ class ExpertBank:
     w: torch.Tensor | None = None     # CPU/dense: [E, N, K]
     qw_ptrs: torch.Tensor | None = None  # int64 [E] device
     sm_ptrs: torch.Tensor | None = None
+    bank_contiguous: bool = False  # qw/sm hold every expert in order (TMA-streamable bank)
 
     def weight(self, e: int) -> torch.Tensor:
         if self.w is not None:
@@ -51,6 +52,7 @@ class ExpertBank:
     def build_ptrs(self):
         if self.qw is None:
             return
+        self.bank_contiguous = True
         dev = self.qw.device
         qb, sb = self.qw.data_ptr(), self.sm.data_ptr()
         qs, ss = self.qw.stride(0) * 4, self.sm.stride(0) * 2

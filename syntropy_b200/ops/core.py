@@ -107,7 +107,7 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
     if isinstance(W, Q4Weight) and W.N % 128 == 0 and W.K % 64 == 0:
         ptrs = _ptrs(W)
         gm = {GEMV_STORE: 0 if out.dtype == torch.bfloat16 else 5, GEMV_SWIGLU: 1, GEMV_ADD_F32: 3}[mode]
-        gemm_grouped(x, ptrs[0], ptrs[1], _identity_off(T, x.device), W.N, W.K, gm, None, out, 1)
+        gemm_grouped(x, ptrs[0], ptrs[1], _identity_off(T, x.device), W.N, W.K, gm, None, out, 1, W.qw, W.sm)
         return out
     Wd = _dense_weight(W)
     y = x.to(Wd.dtype) @ Wd.t()
@@ -193,16 +193,19 @@ def gemm_status(dev) -> torch.Tensor:
     return t
 
 
-def gemm_grouped(x, qw_ptrs, sm_ptrs, row_off, N, K, mode, route_w, out, G, max_rows_per_group=None):
+def gemm_grouped(x, qw_ptrs, sm_ptrs, row_off, N, K, mode, route_w, out, G, bank_qw=None, bank_sm=None):
     """tcgen05 GEMM over G contiguous row groups of x (bf16 [M, K]) with 4-bit weights.
-    mode: 0 bf16 store, 1 SwiGLU, 2 f32 * route_w[row], 3 f32 +=, 5 f32 store."""
+    mode: 0 bf16 store, 1 SwiGLU, 2 f32 * route_w[row], 3 f32 +=, 5 f32 store.
+    bank_qw/bank_sm: the contiguous weight bank (one matrix, or [G, ...] experts in group
+    order) lets the kernel stream packed weights with 4-D TMA copies."""
     M = x.shape[0]
     if M == 0:
         return out
     max_mtiles = (M + 127) // 128 + G
+    e = _EMPTY_I32(x.device)
     ext().tc_gemm_q4(x, qw_ptrs, sm_ptrs, row_off, N, K, mode,
                      route_w if route_w is not None else _EMPTY_F32(x.device), out, gemm_status(x.device),
-                     max_mtiles)
+                     max_mtiles, bank_qw if bank_qw is not None else e, bank_sm if bank_sm is not None else e, 0)
     _launched()
     return out
 

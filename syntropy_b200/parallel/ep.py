@@ -163,9 +163,12 @@ def _local_experts_apply(rows, ids, w, gu, dn, erange) -> torch.Tensor:
         # prefill-sized: gather rows per expert, then grouped tcgen05 GEMMs
         a_rows = rows.index_select(0, tok.long()).contiguous()
         mid = torch.empty(P, f, dtype=rows.dtype, device=dev)
-        ops.gemm_grouped(a_rows, gu.qw_ptrs, gu.sm_ptrs, tok_off, gu.N, gu.K, 1, None, mid, eb - ea)
+        bk = getattr(gu, "bank_contiguous", False)
+        ops.gemm_grouped(a_rows, gu.qw_ptrs, gu.sm_ptrs, tok_off, gu.N, gu.K, 1, None, mid, eb - ea,
+                         gu.qw if bk else None, gu.sm if bk else None)
         yp = torch.empty(P, H, dtype=torch.float32, device=dev)
-        ops.gemm_grouped(mid, dn.qw_ptrs, dn.sm_ptrs, tok_off, dn.N, dn.K, 2, pw, yp, eb - ea)
+        ops.gemm_grouped(mid, dn.qw_ptrs, dn.sm_ptrs, tok_off, dn.N, dn.K, 2, pw, yp, eb - ea,
+                         dn.qw if bk else None, dn.sm if bk else None)
     elif rows.is_cuda and gu.qw is not None and int(counts.max()) <= 256:
         mid = torch.empty(P, f, dtype=rows.dtype, device=dev)
         ops.linear_grouped(rows, gu, tok_off, tok_idx, mid, ops.GEMV_SWIGLU, qw_ptrs=gu.qw_ptrs, sm_ptrs=gu.sm_ptrs)

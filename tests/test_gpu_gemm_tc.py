@@ -25,14 +25,23 @@ def test_tc_gemm_dense(cuda, M, N, K):
     out = torch.zeros(M, N, dtype=torch.float32, device=cuda)
     ptrs = (torch.tensor([q.qw.data_ptr()], device=cuda), torch.tensor([q.sm.data_ptr()], device=cuda))
     off = torch.tensor([0, M], dtype=torch.int32, device=cuda)
-    ext().tc_gemm_q4(x, ptrs[0], ptrs[1], off, N, K, 5, torch.empty(0, device=cuda), out, status, (M + 127) // 128 + 1)
+    e = torch.empty(0, dtype=torch.int32, device=cuda)
+    ext().tc_gemm_q4(x, ptrs[0], ptrs[1], off, N, K, 5, torch.empty(0, device=cuda), out, status, (M + 127) // 128 + 1,
+                     e, e, 0)
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     ref = x.float() @ wd.t()
     assert _rel(out, ref) < 2e-3
     ob = torch.zeros(M, N, dtype=torch.bfloat16, device=cuda)
-    ext().tc_gemm_q4(x, ptrs[0], ptrs[1], off, N, K, 0, torch.empty(0, device=cuda), ob, status, (M + 127) // 128 + 1)
+    ext().tc_gemm_q4(x, ptrs[0], ptrs[1], off, N, K, 0, torch.empty(0, device=cuda), ob, status, (M + 127) // 128 + 1,
+                     q.qw, q.sm, 0)
     assert _rel(ob, ref) < 5e-3
+    # TMA-streamed weights give the same result as the bulk-copy path
+    ot = torch.zeros(M, N, dtype=torch.float32, device=cuda)
+    ext().tc_gemm_q4(x, ptrs[0], ptrs[1], off, N, K, 5, torch.empty(0, device=cuda), ot, status, (M + 127) // 128 + 1,
+                     q.qw, q.sm, 0)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0 and torch.equal(ot, out)
 
 
 def test_tc_gemm_grouped_swiglu_scaled(cuda):
@@ -49,10 +58,15 @@ def test_tc_gemm_grouped_swiglu_scaled(cuda):
     sp = torch.tensor([q.sm.data_ptr() for q in qs], device=cuda)
     status = torch.zeros(1, dtype=torch.int32, device=cuda)
     mid = torch.zeros(M, f, dtype=torch.bfloat16, device=cuda)
-    ext().tc_gemm_q4(x, qp, sp, off, 2 * f, H, 1, torch.empty(0, device=cuda), mid, status, M // 128 + G + 1)
+    e = torch.empty(0, dtype=torch.int32, device=cuda)
+    ext().tc_gemm_q4(x, qp, sp, off, 2 * f, H, 1, torch.empty(0, device=cuda), mid, status, M // 128 + G + 1, e, e, 0)
     rw = torch.rand(M, device=cuda)
     y = torch.zeros(M, 2 * f, dtype=torch.float32, device=cuda)
-    ext().tc_gemm_q4(x, qp, sp, off, 2 * f, H, 2, rw, y, status, M // 128 + G + 1)
+    bq = torch.stack([q.qw for q in qs])
+    bs = torch.stack([q.sm for q in qs])
+    qp2 = torch.tensor([bq[i].data_ptr() for i in range(G)], device=cuda)
+    sp2 = torch.tensor([bs[i].data_ptr() for i in range(G)], device=cuda)
+    ext().tc_gemm_q4(x, qp2, sp2, off, 2 * f, H, 2, rw, y, status, M // 128 + G + 1, bq, bs, 0)
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     offs = off.tolist()
