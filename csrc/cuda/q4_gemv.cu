@@ -554,6 +554,17 @@ cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {
     if (variant == 26) return launch_v2<1, 1, 1, 3, 10>(a, s);
     if (variant == 0 || variant == 22) return launch_v2<1, 1, 1, 4, 8>(a, s);
   }
+  if (split && nt == 4) {
+    static int dense_variant = -1;
+    if (dense_variant < 0) {
+      const char* v = getenv("SYN_GEMV_DENSE");
+      dense_variant = v ? atoi(v) : 0;
+    }
+    if (dense_variant == 1) return launch_v2<1, 4, 8, 2, 1>(a, s);
+    if (dense_variant == 2) return launch_v2<1, 4, 4, 2, 1>(a, s);
+    if (dense_variant == 3) return launch_v2<2, 4, 8, 2, 1>(a, s);
+    if (dense_variant == 4) return launch_v2<1, 4, 2, 2, 2>(a, s);
+  }
   if (!split && variant == 2) {
     if (R == 1) {
       if (nt == 1) return launch_v2<1, 1, 1>(a, s);

@@ -94,6 +94,16 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
             out.copy_(y)
         return out
     T = x.shape[0]
+    if isinstance(W, Q4Weight) and T <= DECODE_ROWS_MAX and T > 8 and _DENSE_AS_GROUPS[0]:
+        # token groups of 8 over shared weights: one HBM pass, the other groups hit L2
+        kmode = {GEMV_STORE: 0, GEMV_SWIGLU: 1, GEMV_ADD_F32: 3}[mode]
+        if kmode == 0 and out.dtype == torch.float32:
+            kmode = 5
+        qp, sp, off = _group_ptrs(W, T)
+        ext().q4_gemv(x, qp, sp, off, _EMPTY_I32(x.device), _EMPTY_F32(x.device), _EMPTY_BF16(x.device), out, W.N,
+                      W.K, kmode, 1, qp.numel(), _EMPTY_F32(x.device))
+        _launched()
+        return out
     if isinstance(W, Q4Weight) and T <= DECODE_ROWS_MAX:
         ptrs = _ptrs(W)
         kmode = {GEMV_STORE: 0, GEMV_SWIGLU: 1, GEMV_ADD_F32: 3}[mode]
@@ -121,6 +131,21 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
 
 
 _PTR_CACHE: dict = {}
+_GROUP_CACHE: dict = {}
+_DENSE_AS_GROUPS = [__import__("os").environ.get("SYN_DENSE_GROUPS", "0") == "1"]
+
+
+def _group_ptrs(W: Q4Weight, T: int):
+    key = (W.qw.data_ptr(), T)
+    v = _GROUP_CACHE.get(key)
+    if v is None:
+        G = (T + 7) // 8
+        dev = W.qw.device
+        v = (torch.tensor([W.qw.data_ptr()] * G, dtype=torch.int64, device=dev),
+             torch.tensor([W.sm.data_ptr()] * G, dtype=torch.int64, device=dev),
+             torch.tensor([min(8 * g, T) for g in range(G + 1)], dtype=torch.int32, device=dev))
+        _GROUP_CACHE[key] = v
+    return v
 _OFF_CACHE: dict = {}
 _EMPTY: dict = {}
 
