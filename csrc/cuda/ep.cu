@@ -196,6 +196,47 @@ __global__ void ep_combine_kernel(EpArgs a, float* __restrict__ x, const float* 
   for (int i = threadIdx.x; i < a.H; i += blockDim.x) hout[(int64_t)t * a.H + i] = f2bf(xr[i] * r * wn[i]);
 }
 
+// TP one-shot all-reduce, receive side: every rank pushed its f32 partial rows into slot
+// [src][row] of this rank's receive area; sum them in rank order (identical bits on every
+// rank), add to the residual, and apply the next RMSNorm.  grid = T, block = 256.
+__global__ void tp_reduce_norm_kernel(EpArgs a, int64_t off_recv, int64_t off_flag, float* __restrict__ x,
+                                      const float* __restrict__ wn, __nv_bfloat16* __restrict__ hout, float eps) {
+  __shared__ float red[32];
+  __shared__ int s_ok;
+  const int t = blockIdx.x;
+  uint8_t* mine = reinterpret_cast<uint8_t*>(a.peers[a.rank]);
+  const uint32_t seq = ep_seq(a.step_ctr, a.n_layers, a.layer);
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  if (threadIdx.x < a.N) {
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(mine + off_flag) + threadIdx.x;
+    if (!wait_flag(f, seq, a.timeout_ns, a.status, 2)) s_ok = 0;
+  }
+  __syncthreads();
+  const float* recv = reinterpret_cast<const float*>(mine + off_recv);
+  float* xr = x + (int64_t)t * a.H;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
+    float acc = 0.f;
+    if (s_ok)
+      for (int r = 0; r < a.N; ++r) acc += recv[((int64_t)r * a.cap + t) * a.H + i];
+    const float v = xr[i] + acc;
+    xr[i] = v;
+    ss += v * v;
+  }
+  if (wn == nullptr) return;
+  ss = block_sum(ss, red);
+  const float rr = rsqrtf(ss / (float)a.H + eps);
+  for (int i = threadIdx.x; i < a.H; i += blockDim.x) hout[(int64_t)t * a.H + i] = f2bf(xr[i] * rr * wn[i]);
+}
+
+cudaError_t launch_tp_reduce_norm(const EpArgs& a, int64_t off_recv, int64_t off_flag, float* x, const float* wn,
+                                  void* hout, float eps, int T, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  tp_reduce_norm_kernel<<<T, 256, 0, s>>>(a, off_recv, off_flag, x, wn, reinterpret_cast<__nv_bfloat16*>(hout), eps);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_ep_dispatch(const EpArgs& a, const void* h, const int32_t* ids, const float* w, int T,
                                cudaStream_t s) {
   if (T > 256) return cudaErrorInvalidValue;

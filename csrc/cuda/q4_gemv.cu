@@ -32,6 +32,7 @@ enum GemvMode : int {
   GEMV_ADD_F32 = 3,      // out_f32[p][n] += y (residual stream kept in f32)
   GEMV_SCALED_F32_PTR = 4,  // ((float*)out_ptrs[p])[n] = route_w[p] * y (peer memory allowed)
   GEMV_STORE_F32 = 5,    // out_f32[p][n] = y (logits)
+  GEMV_PEERS_F32 = 6,    // y -> every TP peer's receive slot (one-shot all-reduce push)
 };
 
 
@@ -55,6 +56,10 @@ __device__ __forceinline__ void gemv_store(const GemvArgs& a, int p, int n, floa
       break;
     case GEMV_SCALED_F32_PTR:
       reinterpret_cast<float*>(a.out_ptrs[p])[n] = a.route_w[p] * v;
+      break;
+    case GEMV_PEERS_F32:
+      for (int q = 0; q < a.sig_n; ++q)
+        reinterpret_cast<float*>(a.sig_peers[q] + a.peer_off)[((int64_t)a.sig_rank * a.peer_cap + p) * a.N + n] = v;
       break;
     default:
       break;
@@ -531,6 +536,215 @@ cudaError_t launch_block_sums(const void* x, int rows, int K, int ldx, float* ou
   return cudaGetLastError();
 }
 
+
+// ---------------------------------------------------------------------------------------
+// v4: TMA-fed GEMV.  A row tile's packed nibbles (K/64 x 512 B) and scales (K/64 x 128 B)
+// are contiguous in the tiled layout, so one elected lane per warp streams them with
+// cp.async.bulk in 8-group chunks (5 KB) into a 3-stage per-warp ring.  Bytes in flight
+// no longer cost registers (15 KB per warp), so a warp streams a whole K without split-K.
+// Same fragment math and epilogues as v2.
+template <int NT>
+struct GemvV4 {
+  static constexpr int WARPS = 4;
+  static constexpr int CG = 8;      // groups per chunk
+  static constexpr int STAGES = 3;
+  static constexpr int QB = CG * 512, SB = CG * 128;
+  static constexpr int STAGE_BYTES = QB + SB;
+  static constexpr size_t SMEM = (size_t)WARPS * STAGES * STAGE_BYTES;
+};
+
+__device__ __forceinline__ uint32_t smem_addr_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+template <int NT>
+__global__ void __launch_bounds__(128) q4_gemv4_kernel(GemvArgs a) {
+  using C = GemvV4<NT>;
+  extern __shared__ __align__(128) uint8_t gsm4[];
+  __shared__ __align__(8) uint64_t bars[C::WARPS][C::STAGES];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int e = blockIdx.y;
+  const int p0 = a.tok_off[e];
+  const int cnt = a.tok_off[e + 1] - p0;
+  const int n_units = a.N / 16;
+  const int unit = blockIdx.x * C::WARPS + warp;
+  const int KG = a.K >> 6;
+  const int n_chunks = (KG + C::CG - 1) / C::CG;
+  uint8_t* ring = gsm4 + warp * C::STAGES * C::STAGE_BYTES;
+  const bool active = cnt > 0 && unit < n_units;
+  if (lane == 0) {
+    for (int s = 0; s < C::STAGES; ++s)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(smem_addr_u32(&bars[warp][s])));
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncwarp();
+  if (active) {
+    const uint8_t* qw = reinterpret_cast<const uint8_t*>(a.qw_ptrs[e]) + (int64_t)unit * KG * 512;
+    const uint8_t* smw = reinterpret_cast<const uint8_t*>(a.sm_ptrs[e]) + (int64_t)unit * KG * 128;
+    const __nv_bfloat16* xbase = reinterpret_cast<const __nv_bfloat16*>(a.x);
+    const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
+    uint32_t phase_bits = 0;  // bit s: parity to wait for on stage s
+    auto issue = [&](int c) {
+      if (lane == 0 && c < n_chunks) {
+        const int s = c % C::STAGES;
+        const int ng = min(C::CG, KG - c * C::CG);
+        uint64_t* bar = &bars[warp][s];
+        const uint32_t bytes = (uint32_t)ng * 640u;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr_u32(bar)),
+                     "r"(bytes)
+                     : "memory");
+        uint8_t* dst = ring + s * C::STAGE_BYTES;
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                         smem_addr_u32(dst)),
+                     "l"(qw + (int64_t)c * C::CG * 512), "r"((uint32_t)ng * 512u), "r"(smem_addr_u32(bar))
+                     : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                         smem_addr_u32(dst + C::QB)),
+                     "l"(smw + (int64_t)c * C::CG * 128), "r"((uint32_t)ng * 128u), "r"(smem_addr_u32(bar))
+                     : "memory");
+      }
+    };
+    for (int c0 = 0; c0 < cnt; c0 += NT * 8) {
+      const int ccount = min(cnt - c0, NT * 8);
+      const int ntc = (ccount + 7) >> 3;
+      const __nv_bfloat16* xr[NT];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int j = min(nt * 8 + g, ccount - 1);
+        const int pp = p0 + c0 + j;
+        const int row = a.tok_idx ? a.tok_idx[pp] : pp;
+        xr[nt] = xbase + (int64_t)row * a.ldx + 2 * t;
+      }
+      float acc[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
+#pragma unroll
+      for (int i = 0; i < C::STAGES; ++i) issue(i);
+      bool ok = true;
+      for (int c = 0; c < n_chunks && ok; ++c) {
+        const int s = c % C::STAGES;
+        const uint32_t par = (phase_bits >> s) & 1u;
+        {  // bounded wait on this chunk's bytes
+          uint32_t done = 0;
+          const uint64_t t0 = globaltimer_ns();
+          while (true) {
+            asm volatile(
+                "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+                : "=r"(done)
+                : "r"(smem_addr_u32(&bars[warp][s])), "r"(par)
+                : "memory");
+            if (done) break;
+            if (globaltimer_ns() - t0 > 2000000000ull) {
+              if (a.status) atomicOr(a.status, 1 << 5);
+              ok = false;
+              break;
+            }
+          }
+        }
+        if (!ok) break;
+        phase_bits ^= 1u << s;
+        const uint8_t* stq = ring + s * C::STAGE_BYTES;
+        const uint8_t* sts = stq + C::QB;
+        const int ng = min(C::CG, KG - c * C::CG);
+        for (int gi = 0; gi < ng; ++gi) {
+          const int kg = c * C::CG + gi;
+          const uint4 q = *reinterpret_cast<const uint4*>(stq + gi * 512 + lane * 16);
+          const uint2 slo = *reinterpret_cast<const uint2*>(sts + gi * 128 + g * 8);
+          const uint2 shi = *reinterpret_cast<const uint2*>(sts + gi * 128 + (g + 8) * 8);
+#pragma unroll
+          for (int b = 0; b < 2; ++b) {
+            const uint32_t w0 = b ? q.z : q.x;
+            const uint32_t w1 = b ? q.w : q.y;
+            uint32_t af[2][4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              af[0][j] = lop3_and_or(w0 >> (4 * j), 0x000F000Fu, 0x43004300u);
+              af[1][j] = lop3_and_or(w1 >> (4 * j), 0x000F000Fu, 0x43004300u);
+            }
+            const uint32_t vlo = b ? slo.y : slo.x, vhi = b ? shi.y : shi.x;
+            const half2 hl = *reinterpret_cast<const half2*>(&vlo);
+            const half2 hh = *reinterpret_cast<const half2*>(&vhi);
+            const float dlo = __low2float(hl), dhi = __low2float(hh);
+            const float mlo = fmaf(-128.f, dlo, __high2float(hl)), mhi = fmaf(-128.f, dhi, __high2float(hh));
+            const int k0 = kg * 64 + b * 32;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              if (nt < ntc) {
+                uint32_t bf[2][2];
+                bf[0][0] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0));
+                bf[0][1] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0 + 8));
+                bf[1][0] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0 + 16));
+                bf[1][1] = __ldg(reinterpret_cast<const uint32_t*>(xr[nt] + k0 + 24));
+                float xs[4] = {0.f, 0.f, 0.f, 0.f}, blk[4] = {0.f, 0.f, 0.f, 0.f};
+                mma_bf16_16816(xs, ones, bf[0], xs);
+                mma_bf16_16816(xs, ones, bf[1], xs);
+                mma_bf16_16816(blk, af[0], bf[0], blk);
+                mma_bf16_16816(blk, af[1], bf[1], blk);
+                acc[nt][0] += fmaf(dlo, blk[0], mlo * xs[0]);
+                acc[nt][1] += fmaf(dlo, blk[1], mlo * xs[1]);
+                acc[nt][2] += fmaf(dhi, blk[2], mhi * xs[2]);
+                acc[nt][3] += fmaf(dhi, blk[3], mhi * xs[3]);
+              }
+            }
+          }
+        }
+        __syncwarp();
+        issue(c + C::STAGES);
+      }
+      if (!ok) break;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int j = nt * 8 + 2 * t + hf;
+          if (j >= ccount) continue;
+          const int p = p0 + c0 + j;
+          if (a.mode == GEMV_SWIGLU) {
+            reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)p * (a.N / 2) + unit * 8 + g] =
+                f2bf(silu(acc[nt][hf]) * acc[nt][2 + hf]);
+          } else {
+            gemv_store(a, p, unit * 16 + g, acc[nt][hf]);
+            gemv_store(a, p, unit * 16 + g + 8, acc[nt][2 + hf]);
+          }
+        }
+      }
+    }
+  }
+  if (a.done_ctr != nullptr) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned total = gridDim.x * gridDim.y;
+      const unsigned prev = atomicAdd(a.done_ctr, 1u);
+      if (prev == total - 1) {
+        *a.done_ctr = 0u;
+        __threadfence_system();
+        const uint32_t seq = (*a.step_ctr) * (uint32_t)a.n_layers + (uint32_t)a.layer + 1u;
+        for (int q = 0; q < a.sig_n; ++q)
+          st_release_sys(reinterpret_cast<uint32_t*>(a.sig_peers[q] + a.sig_off) + a.sig_rank, seq);
+      }
+    }
+  }
+}
+
+template <int NT>
+static cudaError_t launch_v4(const GemvArgs& a, cudaStream_t s) {
+  using C = GemvV4<NT>;
+  const int units = a.N / 16;
+  const int gx = (units + C::WARPS - 1) / C::WARPS;
+  static bool set = false;
+  if (!set) {
+    cudaError_t e = cudaFuncSetAttribute(q4_gemv4_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)C::SMEM);
+    if (e != cudaSuccess) return e;
+    set = true;
+  }
+  dim3 grid((unsigned)gx, (unsigned)a.E);
+  q4_gemv4_kernel<NT><<<grid, C::WARPS * 32, C::SMEM, s>>>(a);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {
   // Tile shape: NT from the caller's bound on rows per expert; two row tiles per warp when
   // several token tiles share them; split K across warps only when there are too few
@@ -545,6 +759,12 @@ cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {
     env_variant = v ? atoi(v) : 0;
   }
   const int variant = a.variant ? a.variant : env_variant;
+  // TMA-fed path: weights in device memory only (bulk copies are not pointed at host memory)
+  if (a.weights_in_vram && (variant == 0 || variant == 4)) {
+    if (nt == 1) return launch_v4<1>(a, s);
+    if (nt == 2) return launch_v4<2>(a, s);
+    return launch_v4<4>(a, s);
+  }
   if (!split && R == 1 && nt == 1) {
     if (variant == 21) return launch_v2<1, 1, 1, 8>(a, s);
     if (variant == 22) return launch_v2<1, 1, 1, 4, 8>(a, s);

@@ -15,7 +15,8 @@ torch::Tensor q4_tiled_to_rows(torch::Tensor qw, torch::Tensor sm, int64_t N, in
 torch::Tensor q4t_dequant(torch::Tensor qw, torch::Tensor sm, int64_t N, int64_t K);
 void q4_gemv(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
              torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor res, torch::Tensor out,
-             int64_t N, int64_t K, int64_t mode, int64_t nt_hint, int64_t e_active, torch::Tensor xsum);
+             int64_t N, int64_t K, int64_t mode, int64_t nt_hint, int64_t e_active, torch::Tensor xsum,
+             bool in_vram);
 void block_sums(torch::Tensor x, torch::Tensor out);
 
 void rmsnorm(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor out);
@@ -58,12 +59,20 @@ void ep_combine(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, int64
 void q4_gemv_ep(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
                 torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor out_ptrs, int64_t N, int64_t K,
                 torch::Tensor done_ctr, torch::Tensor peers, int64_t sig_off, int64_t sig_rank,
-                torch::Tensor step_ctr, int64_t n_layers, int64_t layer, int64_t nt_hint, int64_t e_active);
+                torch::Tensor step_ctr, int64_t n_layers, int64_t layer, int64_t nt_hint, int64_t e_active,
+                bool in_vram);
 
 void tc_gemm_q4(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor row_off, int64_t N,
                 int64_t K, int64_t mode, torch::Tensor route_w, torch::Tensor out, torch::Tensor status,
                 int64_t max_mtiles, torch::Tensor bank_qw, torch::Tensor bank_sm, int64_t group_base);
 
+void q4_gemv_tp(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off, int64_t N,
+                int64_t K, torch::Tensor done_ctr, torch::Tensor peers, int64_t peer_off, int64_t peer_cap,
+                int64_t sig_off, int64_t rank, torch::Tensor step_ctr, int64_t n_layers, int64_t layer);
+void tp_reduce_norm(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, int64_t H, std::vector<int64_t> offs,
+                    torch::Tensor step_ctr, int64_t n_layers, int64_t layer, int64_t timeout_ns, torch::Tensor status,
+                    int64_t off_recv, int64_t off_flag, torch::Tensor x, torch::Tensor wn, torch::Tensor hout,
+                    double eps);
 void register_all(pybind11::module& m);
 void register_runtime(pybind11::module& m);
 void register_formats(pybind11::module& m);

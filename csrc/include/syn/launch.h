@@ -39,12 +39,18 @@ struct GemvArgs {
   int sig_n, sig_rank;
   const uint32_t* step_ctr;
   int n_layers, layer;
+  // mode 6 (GEMV_PEERS_F32): every output row p goes to slot [sig_rank][p] of each peer's
+  // receive area at byte offset peer_off (rows of N floats, peer_cap rows per source)
+  int64_t peer_off;
+  int peer_cap;
   // launch shape hints: max rows (tokens) per expert -> n-tiles of 8; experts likely active
   int nt_hint;
   int E_active_hint;
   // optional precomputed block sums of x: f32 [rows][K/32] (nullptr: computed per CTA)
   const float* xsum;
-  int variant;  // 0 auto; 2 force v2 (register pipeline); 3 force v3 (cp.async ring)
+  int variant;  // 0 auto; 2 force v2 (register pipeline); 3 force v3 (cp.async ring); 4 TMA-fed
+  int* status;  // error bits of bounded waits (v4), may be null
+  int weights_in_vram;  // 1: every weight pointer is device memory (bulk-copy path allowed)
 };
 cudaError_t launch_block_sums(const void* x, int rows, int K, int ldx, float* out, cudaStream_t s);
 
@@ -69,6 +75,8 @@ cudaError_t launch_ep_dispatch(const EpArgs& a, const void* h, const int32_t* id
                                cudaStream_t s);
 cudaError_t launch_ep_build(const EpArgs& a, int32_t* tok_off, int32_t* tok_idx, float* pair_w, int64_t* pair_dst,
                             cudaStream_t s);
+cudaError_t launch_tp_reduce_norm(const EpArgs& a, int64_t off_recv, int64_t off_flag, float* x, const float* wn,
+                                  void* hout, float eps, int T, cudaStream_t s);
 cudaError_t launch_ep_combine(const EpArgs& a, float* x, const float* wn, void* hout, float eps, int T,
                               cudaStream_t s);
 cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s);

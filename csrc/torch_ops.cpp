@@ -73,7 +73,7 @@ torch::Tensor q4t_dequant(torch::Tensor qw, torch::Tensor sm, int64_t N, int64_t
 
 void q4_gemv(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
              torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor res, torch::Tensor out, int64_t N,
-             int64_t K, int64_t mode, int64_t nt_hint, int64_t e_active, torch::Tensor xsum) {
+             int64_t K, int64_t mode, int64_t nt_hint, int64_t e_active, torch::Tensor xsum, bool in_vram) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16, "x must be cuda bf16");
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be [rows, K] with unit inner stride");
   TORCH_CHECK(N % 16 == 0 && K % 64 == 0, "q4_gemv: N%16, K%64");
@@ -113,6 +113,10 @@ void q4_gemv(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torc
   a.E_active_hint = (int)std::max<int64_t>(1, e_active);
   a.xsum = nullptr;
   a.variant = 0;
+  a.peer_off = 0;
+  a.peer_cap = 0;
+  a.status = nullptr;
+  a.weights_in_vram = in_vram ? 1 : 0;
   if (xsum.defined() && xsum.numel() > 0) {
     TORCH_CHECK(xsum.is_cuda() && xsum.scalar_type() == torch::kFloat32 && xsum.size(-1) == K / 32, "xsum f32 [rows, K/32]");
     a.xsum = xsum.data_ptr<float>();
@@ -379,7 +383,8 @@ void ep_combine(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, int64
 void q4_gemv_ep(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
                 torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor out_ptrs, int64_t N, int64_t K,
                 torch::Tensor done_ctr, torch::Tensor peers, int64_t sig_off, int64_t sig_rank,
-                torch::Tensor step_ctr, int64_t n_layers, int64_t layer, int64_t nt_hint, int64_t e_active) {
+                torch::Tensor step_ctr, int64_t n_layers, int64_t layer, int64_t nt_hint, int64_t e_active,
+                bool in_vram) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x");
   TORCH_CHECK(N % 16 == 0 && K % 64 == 0 && x.size(1) == K, "q4_gemv_ep shapes");
   TORCH_CHECK(done_ctr.is_cuda() && done_ctr.scalar_type() == torch::kInt32, "done_ctr cuda int32");
@@ -410,6 +415,10 @@ void q4_gemv_ep(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, t
   a.E_active_hint = (int)std::max<int64_t>(1, e_active);
   a.xsum = nullptr;
   a.variant = 0;
+  a.peer_off = 0;
+  a.peer_cap = 0;
+  a.status = nullptr;
+  a.weights_in_vram = in_vram ? 1 : 0;
   TORCH_CHECK(tok_off.numel() == a.E + 1, "tok_off E+1");
   const at::cuda::CUDAGuard guard(x.device());
   SYN_CHECK_CUDA(launch_q4_gemv(a, cur_stream()));
@@ -456,6 +465,55 @@ void block_sums(torch::Tensor x, torch::Tensor out) {
   const at::cuda::CUDAGuard guard(x.device());
   SYN_CHECK_CUDA(launch_block_sums(x.data_ptr(), (int)x.size(0), (int)x.size(1), (int)x.stride(0),
                                    out.data_ptr<float>(), cur_stream()));
+}
+
+
+// TP row-parallel GEMV whose epilogue pushes the f32 partial rows into every peer's receive
+// slot (one-shot all-reduce); the last CTA raises flag `rank` in every peer's flag array.
+void q4_gemv_tp(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off, int64_t N,
+                int64_t K, torch::Tensor done_ctr, torch::Tensor peers, int64_t peer_off, int64_t peer_cap,
+                int64_t sig_off, int64_t rank, torch::Tensor step_ctr, int64_t n_layers, int64_t layer) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x");
+  TORCH_CHECK(N % 16 == 0 && K % 64 == 0 && x.size(1) == K, "q4_gemv_tp shapes");
+  TORCH_CHECK(x.size(0) <= peer_cap, "more rows than the receive capacity");
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.x = x.data_ptr();
+  a.qw_ptrs = qw_ptrs.data_ptr<int64_t>();
+  a.sm_ptrs = sm_ptrs.data_ptr<int64_t>();
+  a.tok_off = tok_off.data_ptr<int32_t>();
+  a.N = (int)N;
+  a.K = (int)K;
+  a.ldx = (int)x.stride(0);
+  a.mode = 6;
+  a.E = (int)qw_ptrs.numel();
+  a.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr());
+  a.sig_peers = peers.data_ptr<int64_t>();
+  a.sig_off = sig_off;
+  a.sig_n = (int)peers.numel();
+  a.sig_rank = (int)rank;
+  a.step_ctr = reinterpret_cast<const uint32_t*>(step_ctr.data_ptr());
+  a.n_layers = (int)n_layers;
+  a.layer = (int)layer;
+  a.peer_off = peer_off;
+  a.peer_cap = (int)peer_cap;
+  a.nt_hint = (int)((x.size(0) + 7) / 8);
+  a.E_active_hint = 1;
+  a.weights_in_vram = 1;
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_q4_gemv(a, cur_stream()));
+}
+
+void tp_reduce_norm(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, int64_t H, std::vector<int64_t> offs,
+                    torch::Tensor step_ctr, int64_t n_layers, int64_t layer, int64_t timeout_ns, torch::Tensor status,
+                    int64_t off_recv, int64_t off_flag, torch::Tensor x, torch::Tensor wn, torch::Tensor hout,
+                    double eps) {
+  auto a = make_ep_args(peers, N, rank, cap, H, 1, 1, offs, step_ctr, n_layers, layer, timeout_ns, status);
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kFloat32 && x.size(1) == H, "x f32 [T, H]");
+  const float* wp = fptr_or_null(wn);
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_tp_reduce_norm(a, off_recv, off_flag, x.data_ptr<float>(), wp, wp ? hout.data_ptr() : nullptr,
+                                       (float)eps, (int)x.size(0), cur_stream()));
 }
 
 }  // namespace syn

@@ -119,6 +119,40 @@ class ModelWeights:
         return tot
 
 
+class _LazyState(dict):
+    """Canonical state dict whose tensors are generated on first access."""
+
+    def __init__(self, cfg, seed, device):
+        super().__init__()
+        self.cfg, self.seed, self.device = cfg, seed, device
+        from .weights import iter_names
+        self.shapes = dict(iter_names(cfg))
+
+    def __getitem__(self, name):
+        return make_tensor(self.cfg, name, self.shapes[name], seed=self.seed, device=self.device)
+
+    def __contains__(self, name):
+        return name in self.shapes
+
+    def items(self):
+        return ((n, self[n]) for n in self.shapes)
+
+
+class _LazyShard(dict):
+    """TP shard of a lazily generated state dict."""
+
+    def __init__(self, full, cfg, rank, size):
+        super().__init__()
+        self.full, self.cfg, self.rank, self.size = full, cfg, rank, size
+
+    def __getitem__(self, name):
+        from ..parallel.tp import shard_state
+        return shard_state(self.cfg, {name: self.full[name]}, self.rank, self.size)[name]
+
+    def __contains__(self, name):
+        return name in self.full
+
+
 def _linear_weight(w: torch.Tensor, quant: str, device):
     if device.type == "cuda":
         if quant == "q4":
@@ -129,11 +163,25 @@ def _linear_weight(w: torch.Tensor, quant: str, device):
 
 def prepare_weights(cfg: ModelConfig, device="cpu", seed: int = 0, quant: str | None = None,
                     state_dict: dict | None = None, max_pos: int = 8192,
-                    expert_range: tuple[int, int] | None = None, dense_dtype=None) -> ModelWeights:
+                    expert_range: tuple[int, int] | None = None, dense_dtype=None,
+                    tp: tuple[int, int] | None = None) -> ModelWeights:
     """Builds engine-ready weights from ``state_dict`` (canonical names) or synthetic ones
     generated directly on ``device``.  ``expert_range`` limits MoE experts to [a, b)
-    (expert parallelism); other experts' pointers are left at zero."""
+    (expert parallelism).  ``tp=(rank, size)`` keeps this rank's tensor-parallel shard
+    (whole heads / FFN columns) and returns weights whose cfg has the local head counts."""
     device = torch.device(device)
+    if tp is not None and tp[1] > 1:
+        from ..parallel.tp import local_config, shard_state
+        from .weights import synthetic_state_dict
+        full = state_dict if state_dict is not None else None
+        if full is None:
+            # generate each tensor on the device, then keep this rank's slice
+            full = _LazyState(cfg, seed, device if device.type == "cuda" else "cpu")
+        sd_local = shard_state(cfg, full, tp[0], tp[1]) if not isinstance(full, _LazyState) else \
+            _LazyShard(full, cfg, tp[0], tp[1])
+        mw = prepare_weights(local_config(cfg, tp[1]), device, seed, quant, sd_local, max_pos, expert_range,
+                             dense_dtype, None)
+        return mw
     quant = quant or cfg.weight_quant
     is_cuda = device.type == "cuda"
     gen_dev = device if is_cuda else "cpu"

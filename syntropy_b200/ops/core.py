@@ -101,7 +101,7 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
             kmode = 5
         qp, sp, off = _group_ptrs(W, T)
         ext().q4_gemv(x, qp, sp, off, _EMPTY_I32(x.device), _EMPTY_F32(x.device), _EMPTY_BF16(x.device), out, W.N,
-                      W.K, kmode, 1, qp.numel(), _EMPTY_F32(x.device))
+                      W.K, kmode, 1, qp.numel(), _EMPTY_F32(x.device), True)
         _launched()
         return out
     if isinstance(W, Q4Weight) and T <= DECODE_ROWS_MAX:
@@ -110,7 +110,7 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
         if kmode == 0 and out.dtype == torch.float32:
             kmode = 5
         ext().q4_gemv(x, ptrs[0], ptrs[1], _identity_off(T, x.device), _EMPTY_I32(x.device), _EMPTY_F32(x.device),
-                      _EMPTY_BF16(x.device), out, W.N, W.K, kmode, (T + 7) // 8, 1, _EMPTY_F32(x.device))
+                      _EMPTY_BF16(x.device), out, W.N, W.K, kmode, (T + 7) // 8, 1, _EMPTY_F32(x.device), True)
         _launched()
         return out
     # GEMM path (prefill): tcgen05 kernel with fused dequant and epilogue
@@ -250,7 +250,7 @@ def linear_grouped(x: torch.Tensor, bank, tok_off: torch.Tensor, tok_idx: torch.
                   tok_idx if tok_idx is not None else _EMPTY_I32(x.device),
                   route_w if route_w is not None else _EMPTY_F32(x.device),
                   _EMPTY_BF16(x.device), out, bank.N, bank.K, kmode, nt_hint, min(E, out.shape[0]),
-                  xsum if xsum is not None else _EMPTY_F32(x.device))
+                  xsum if xsum is not None else _EMPTY_F32(x.device), bool(getattr(bank, "bank_contiguous", False)))
         _launched()
         return out
     # CPU reference: loop over experts in ascending order

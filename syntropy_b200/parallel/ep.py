@@ -94,7 +94,8 @@ class EPGroup:
         e.q4_gemv_ep(mid[:P], dn.qw_ptrs, dn.sm_ptrs, self.tok_off, torch.empty(0, dtype=torch.int32, device=h.device),
                      self.pair_w, self.pair_dst, dn.N, dn.K, self.done_ctr[layer:layer + 1], self.region.peers,
                      self.off_flag_comb, self.rank, self.step_ctr, self.n_layers, layer,
-                     ops.moe_nt_hint(self.N * h.shape[0] * self.k // self.N, self.E_loc), self.E_loc)
+                     ops.moe_nt_hint(self.N * h.shape[0] * self.k // self.N, self.E_loc), self.E_loc,
+                     bool(getattr(dn, "bank_contiguous", False)))
         e.ep_combine(*c, x, next_norm if next_norm is not None else torch.empty(0, device=h.device), h_out, eps)
         ops.core._launched(5)
 

@@ -1,0 +1,112 @@
+"""Intra-node tensor parallelism (Megatron column/row split over NVLink).
+
+Column-parallel: qkv (whole KV heads per rank) and gate/up; row-parallel: o_proj and down.
+The row-parallel products are reduced by a fused path on GPUs: the GEMV epilogue pushes its
+f32 partial rows straight into every peer's receive slot over NVLink and the last CTA raises
+a flag; the receive kernel sums the N partials in rank order (so every rank holds bitwise
+identical residuals, the reference's member-order rule), adds the residual and applies the
+next RMSNorm.  The NCCL all-reduce path is the baseline (and the CPU/gloo path).
+
+Reference: plan/rfcs/RFC-0032-distributed-execution.md:372-396 (TP layer, member-order f32
+reduction), crates/solver/src/collective.rs:256-333 (one-shot vs ring).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from .._ext import ext
+from .dist import DistContext
+from .symm import SymmetricRegion
+
+
+def _align(n, a=256):
+    return (n + a - 1) // a * a
+
+
+class TPGroup:
+    def __init__(self, ctx: DistContext, hidden: int, cap: int, n_layers: int, timeout_s: float = 2.0,
+                 fused: bool = True):
+        self.ctx = ctx
+        self.N, self.rank, self.H, self.cap = ctx.world, ctx.rank, hidden, cap
+        self.n_layers = n_layers
+        self.fused = fused and ctx.device.type == "cuda"
+        self.timeout_ns = int(timeout_s * 1e9)
+        if self.fused:
+            area = self.N * cap * hidden * 4
+            self.off_recv = [0, _align(area)]
+            self.off_flag = [2 * _align(area), 2 * _align(area) + 256]
+            self.region = SymmetricRegion(ctx, 2 * _align(area) + 512)
+            dev = ctx.device
+            self.step_ctr = torch.zeros(1, dtype=torch.int32, device=dev)
+            self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+            self.done_ctr = torch.zeros(2 * n_layers, dtype=torch.int32, device=dev)
+            self._off1 = {}
+
+    def step_begin(self):
+        if self.fused:
+            ext().ep_step_begin(self.step_ctr)
+
+    def _tok_off(self, T, dev):
+        t = self._off1.get(T)
+        if t is None:
+            t = torch.tensor([0, T], dtype=torch.int32, device=dev)
+            self._off1[T] = t
+        return t
+
+    def row_parallel_reduce(self, which: int, layer: int, x_in, W, x_res, next_norm, h_out, eps):
+        """x_res += all_reduce(x_in @ W^T) across ranks; h_out = rmsnorm(x_res) (if next_norm).
+        which: 0 = attention output projection, 1 = FFN down projection."""
+        T = x_in.shape[0]
+        if self.fused:
+            from ..ops.core import _ptrs
+            qp, sp = _ptrs(W)
+            seq_layer = 2 * layer + which
+            ext().q4_gemv_tp(x_in, qp, sp, self._tok_off(T, x_in.device), W.N, W.K,
+                             self.done_ctr[seq_layer:seq_layer + 1], self.region.peers, self.off_recv[which],
+                             self.cap, self.off_flag[which], self.rank, self.step_ctr, 2 * self.n_layers, seq_layer)
+            ext().tp_reduce_norm(self.region.peers, self.N, self.rank, self.cap, self.H, [0] * 6, self.step_ctr,
+                                 2 * self.n_layers, seq_layer, self.timeout_ns, self.status, self.off_recv[which],
+                                 self.off_flag[which], x_res,
+                                 next_norm if next_norm is not None else torch.empty(0, device=x_in.device),
+                                 h_out, eps)
+            ops.core._launched(2)
+            return
+        part = torch.zeros(T, W.N if hasattr(W, "N") else W.shape[0], dtype=torch.float32, device=x_in.device)
+        ops.linear(x_in, W, part, ops.GEMV_ADD_F32)
+        dist.all_reduce(part, group=self.ctx.group)
+        x_res.add_(part)
+        if next_norm is not None:
+            ops.rms_norm(x_res, next_norm, eps, out=h_out)
+
+    def check_status(self) -> int:
+        return int(self.status.item()) if self.fused else 0
+
+
+def shard_state(cfg, sd: dict, rank: int, size: int) -> dict:
+    """Slices a canonical (llama-family) state dict for TP rank `rank` of `size`."""
+    hq, hk, d = cfg.n_heads // size, cfg.n_kv_heads // size, cfg.head_dim
+    f = cfg.ffn // size
+    out = {}
+    for n, t in sd.items():
+        leaf = n.split(".")[-1]
+        if leaf == "q_proj":
+            out[n] = t[rank * hq * d:(rank + 1) * hq * d]
+        elif leaf in ("k_proj", "v_proj"):
+            out[n] = t[rank * hk * d:(rank + 1) * hk * d]
+        elif leaf == "o_proj":
+            out[n] = t[:, rank * hq * d:(rank + 1) * hq * d]
+        elif leaf in ("gate", "up"):
+            out[n] = t[rank * f:(rank + 1) * f]
+        elif leaf == "down":
+            out[n] = t[:, rank * f:(rank + 1) * f]
+        else:
+            out[n] = t
+    return out
+
+
+def local_config(cfg, size: int):
+    assert cfg.n_heads % size == 0 and cfg.n_kv_heads % size == 0 and cfg.ffn % size == 0, \
+        "heads, KV heads and FFN width must divide by the TP size"
+    return cfg.replace(n_heads=cfg.n_heads // size, n_kv_heads=cfg.n_kv_heads // size, ffn=cfg.ffn // size)

@@ -74,9 +74,10 @@ class StepDesc:
 
 class ModelRunner:
     def __init__(self, mw: ModelWeights, max_batch: int = 64, max_seq_len: int = 4096, num_blocks: int | None = None,
-                 kv_dtype=None, use_graphs: bool = True, kv_budget_bytes: int | None = None, ep=None):
+                 kv_dtype=None, use_graphs: bool = True, kv_budget_bytes: int | None = None, ep=None, tp=None):
         cfg = mw.cfg
         self.ep = ep  # parallel.ep.EPGroup or None
+        self.tp = tp  # parallel.tp.TPGroup or None
         self.mw, self.cfg = mw, cfg
         self.device = mw.device
         self.is_cuda = self.device.type == "cuda"
@@ -162,6 +163,8 @@ class ModelRunner:
         x, h = b["x"][:B], b["h"][:B]
         if self.ep is not None:
             self.ep.step_begin()
+        if self.tp is not None:
+            self.tp.step_begin()
         ops.embed(mw.embed, d["tokens"][:B], x)
         n_layers = cfg.n_layers
         first = mw.layers[0]
@@ -172,11 +175,16 @@ class ModelRunner:
             if L.is_moe:
                 self._moe_decode(L, nxt, B, i)
             else:
-                ops.rms_norm(x, L.ffn_norm, cfg.rms_eps, out=h)
+                nw = nxt.attn_norm if nxt else mw.final_norm
+                if self.tp is None:
+                    ops.rms_norm(x, L.ffn_norm, cfg.rms_eps, out=h)
                 mid = b["ffn_mid"][:B]
                 ops.linear(h, L.gate_up, mid, ops.GEMV_SWIGLU)
-                ops.linear(mid, L.down, x, ops.GEMV_ADD_F32)
-                ops.rms_norm(x, nxt.attn_norm if nxt else mw.final_norm, cfg.rms_eps, out=h)
+                if self.tp is not None:
+                    self.tp.row_parallel_reduce(1, i, mid, L.down, x, nw, h, cfg.rms_eps)
+                else:
+                    ops.linear(mid, L.down, x, ops.GEMV_ADD_F32)
+                    ops.rms_norm(x, nw, cfg.rms_eps, out=h)
         logits = b["logits"][:B]
         ops.linear(h, mw.lm_head, logits, ops.GEMV_STORE)
         ops.sample(logits, d["temperature"][:B], d["top_k"][:B], d["top_p"][:B], d["seed"][:B], d["stream"][:B],
@@ -195,7 +203,10 @@ class ModelRunner:
         attn = b["attn"][:B]
         ops.attn_decode(q, self.kv.k[i], self.kv.v[i], d["block_tables"][:B], d["ctx_len"][:B], attn, self.scale,
                         b.get("part_o"), b.get("part_ml"), self.pages_per_split)
-        ops.linear(attn.view(B, -1), L.o, b["x"][:B], ops.GEMV_ADD_F32)
+        if self.tp is not None:  # o_proj partials reduced over NVLink; h = ffn_norm(x)
+            self.tp.row_parallel_reduce(0, i, attn.view(B, -1), L.o, b["x"][:B], L.ffn_norm, b["h"][:B], cfg.rms_eps)
+        else:
+            ops.linear(attn.view(B, -1), L.o, b["x"][:B], ops.GEMV_ADD_F32)
 
     def _moe_decode(self, L, nxt, B, layer):
         cfg, mw, b = self.cfg, self.mw, self.buf
@@ -342,14 +353,14 @@ class ModelRunner:
             kc = self.kv.k[i].permute(0, 2, 1, 3).reshape(-1, cfg.n_kv_heads, cfg.head_dim)[slots]
             vc = self.kv.v[i].permute(0, 2, 1, 3).reshape(-1, cfg.n_kv_heads, cfg.head_dim)[slots]
             ops.attn_prefill(q, kc, vc, cu_seqlens, attn, self.scale)
-            ops.linear(attn.view(T, -1), L.o, x, ops.GEMV_ADD_F32)
+            self._row_parallel(attn.view(T, -1), L.o, x)
             ops.rms_norm(x, L.ffn_norm, cfg.rms_eps, out=h)
             if L.is_moe:
                 self._moe_prefill(L, h, x)
             else:
                 mid = torch.empty(T, cfg.ffn, dtype=act, device=dev)
                 ops.linear(h, L.gate_up, mid, ops.GEMV_SWIGLU)
-                ops.linear(mid, L.down, x, ops.GEMV_ADD_F32)
+                self._row_parallel(mid, L.down, x)
         if len(cu_seqlens) == 1:
             return torch.zeros(0, cfg.vocab, dtype=torch.float32, device=dev)
         last = torch.tensor([c - 1 for c in cu_seqlens[1:]], device=dev, dtype=torch.long)
@@ -357,6 +368,17 @@ class ModelRunner:
         logits = torch.empty(last.numel(), cfg.vocab, dtype=torch.float32, device=dev)
         ops.linear(hl, mw.lm_head, logits, ops.GEMV_STORE)
         return logits
+
+    def _row_parallel(self, a, W, x):
+        """x += a @ W^T, summed over TP ranks with NCCL (prefill)."""
+        if self.tp is None:
+            ops.linear(a, W, x, ops.GEMV_ADD_F32)
+            return
+        import torch.distributed as dist
+        part = torch.zeros_like(x)
+        ops.linear(a, W, part, ops.GEMV_ADD_F32)
+        dist.all_reduce(part, group=self.tp.ctx.group)
+        x.add_(part)
 
     def _moe_prefill(self, L, h, x):
         """MoE FFN for a prefill chunk: routing on the device, then the local experts over
