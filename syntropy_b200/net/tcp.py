@@ -1,0 +1,124 @@
+"""Framed TCP channel: frames are encoded/verified by the native codec; data frames carry a
+channel sequence number (from 1) checked for continuity; the receiver grants credits so a
+sender never has more than `window` unacknowledged data frames in flight."""
+from __future__ import annotations
+
+import enum
+import socket
+import struct
+import threading
+
+from .._ext import ext
+from ..obs.faults import fault_point
+
+
+class FrameType(enum.IntEnum):
+    ACTIVATION = 0x01
+    TOKEN = 0x02
+    SEQ_CONTROL = 0x03
+    CREDIT = 0x04
+    KV_CHUNK = 0x05
+    COLLECTIVE = 0x08
+    STEP_DESCRIPTOR = 0x09
+    HELLO = 0x0A
+    HELLO_ACK = 0x0B
+    CLOSE = 0x0C
+    EP_DISPATCH = 0x0E
+    EP_COMBINE = 0x0F
+    PING = 0x10
+
+
+CONTROL = {FrameType.HELLO, FrameType.HELLO_ACK, FrameType.CREDIT, FrameType.PING, FrameType.CLOSE}
+
+
+def _recv_exact(sock, n):
+    buf = bytearray()
+    while len(buf) < n:
+        b = sock.recv(n - len(buf))
+        if not b:
+            raise ConnectionError("peer closed")
+        buf += b
+    return bytes(buf)
+
+
+class TcpChannel:
+    def __init__(self, sock: socket.socket, instance: int = 0, window: int = 64):
+        self.sock = sock
+        self.sock.setsockopt(socket.IPPROTO_TCP, socket.TCP_NODELAY, 1)
+        self.instance = instance
+        self.window = window
+        self.send_seq = 0
+        self.recv_seq = 0
+        self.credits = window
+        self._cv = threading.Condition()
+        self._lock = threading.Lock()
+
+    @classmethod
+    def connect(cls, host: str, port: int, **kw) -> "TcpChannel":
+        return cls(socket.create_connection((host, port)), **kw)
+
+    def _write(self, ftype, payload: bytes, ext_b: bytes = b"", step: int = 0, seq: int = 0):
+        f = ext().frame_encode(int(ftype), 0, self.instance, 0, 0, step, seq, ext_b, payload)
+        with self._lock:
+            self.sock.sendall(f)
+
+    def send(self, ftype: FrameType, payload: bytes, ext_b: bytes = b"", step: int = 0, timeout: float = 30.0):
+        """Send a data frame; blocks while the receiver has granted no credit."""
+        with self._cv:
+            if not self._cv.wait_for(lambda: self.credits > 0, timeout=timeout):
+                raise TimeoutError("no credit from receiver")
+            self.credits -= 1
+            self.send_seq += 1
+            seq = self.send_seq
+        if fault_point("net.tcp.send"):
+            return seq  # dropped by a fault plan (the receiver sees a sequence gap)
+        self._write(ftype, payload, ext_b, step, seq)
+        return seq
+
+    def recv(self):
+        """Next data frame as (ftype, spec, ext, payload); credit frames are consumed here."""
+        while True:
+            hdr = _recv_exact(self.sock, 64)
+            ext_len, pay_len = struct.unpack_from("<II", hdr, 48)
+            body = _recv_exact(self.sock, ext_len + pay_len)
+            rc, spec, x, p = ext().frame_decode(hdr + body)
+            if rc != 0:
+                raise ValueError(f"bad frame (code {rc})")
+            ft = FrameType(spec["ftype"])
+            if ft == FrameType.CREDIT:
+                with self._cv:
+                    self.credits += int.from_bytes(p[:4], "little")
+                    self._cv.notify_all()
+                continue
+            if ft in CONTROL:
+                return ft, spec, x, p
+            if spec["chan_seq"] != self.recv_seq + 1:
+                raise ValueError(f"sequence gap: expected {self.recv_seq + 1}, got {spec['chan_seq']}")
+            self.recv_seq = spec["chan_seq"]
+            return ft, spec, x, p
+
+    def grant(self, n: int = 1):
+        self._write(FrameType.CREDIT, int(n).to_bytes(4, "little"))
+
+    def close(self):
+        try:
+            self._write(FrameType.CLOSE, b"")
+        except OSError:
+            pass
+        self.sock.close()
+
+
+class TcpListener:
+    def __init__(self, host: str = "127.0.0.1", port: int = 0):
+        self.sock = socket.socket()
+        self.sock.setsockopt(socket.SOL_SOCKET, socket.SO_REUSEADDR, 1)
+        self.sock.bind((host, port))
+        self.sock.listen(8)
+        self.port = self.sock.getsockname()[1]
+
+    def accept(self, **kw) -> TcpChannel:
+        s, _ = self.sock.accept()
+        return TcpChannel(s, **kw)
+
+    def close(self):
+        self.sock.close()

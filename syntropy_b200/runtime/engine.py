@@ -38,6 +38,7 @@ class Sequence:
     output: list = field(default_factory=list)
     blocks: list = field(default_factory=list)
     status: str = "waiting"  # waiting | running | finished
+    cached_tokens: int = 0   # prompt tokens served from the prefix cache
     finish_reason: str | None = None
     seed: int = 0
     stream: int = 0
@@ -61,8 +62,12 @@ class StepOutput:
 
 class LLMEngine:
     def __init__(self, runner: ModelRunner, max_prefill_tokens: int = 8192, eos_token_id: int | None = None,
-                 dist_ctx=None):
+                 dist_ctx=None, prefix_cache: bool = False):
         self.runner = runner
+        self.prefix = None
+        if prefix_cache:
+            from ..kv.prefix import PrefixCache
+            self.prefix = PrefixCache(runner.kv.alloc, runner.kv.block_size)
         # Under expert parallelism every rank must take the same kind of step (the MoE
         # layers exchange rows), so step kinds are agreed over the host control group.
         self.dist = dist_ctx if (dist_ctx is not None and dist_ctx.enabled) else None
@@ -151,12 +156,16 @@ class LLMEngine:
         while self.waiting and len(self.running) + len(batch) < self.runner.max_batch:
             s = self.waiting[0]
             need = kv.blocks_needed(len(s.prompt) + 1)
+            if kv.alloc.num_free < need and self.prefix is not None:
+                self.prefix.evict(need - kv.alloc.num_free)
             if kv.alloc.num_free < need or (batch and tokens + len(s.prompt) > self.max_prefill_tokens):
                 break
             self.waiting.popleft()
+            if self.prefix is not None:
+                s.blocks, s.cached_tokens = self.prefix.match(s.prompt)
             kv.ensure(s.blocks, len(s.prompt))
             batch.append(s)
-            tokens += len(s.prompt)
+            tokens += len(s.prompt) - s.cached_tokens
         return batch
 
     def _prefill(self, batch: list[Sequence]) -> list[StepOutput]:
@@ -165,13 +174,16 @@ class LLMEngine:
             self.runner.prefill(torch.zeros(0, dtype=torch.int32), torch.zeros(0, dtype=torch.int32),
                                 torch.zeros(0, dtype=torch.int64), [0])
             return []
-        toks, pos, slots, cu = [], [], [], [0]
+        toks, pos, slots, cu, prefix = [], [], [], [0], []
         for s in batch:
-            toks += s.prompt
-            pos += list(range(len(s.prompt)))
-            slots += [kv.slot(s.blocks, p) for p in range(len(s.prompt))]
-            cu.append(cu[-1] + len(s.prompt))
-        logits = self.runner.prefill(torch.tensor(toks), torch.tensor(pos), torch.tensor(slots), cu)
+            st = s.cached_tokens
+            toks += s.prompt[st:]
+            pos += list(range(st, len(s.prompt)))
+            slots += [kv.slot(s.blocks, p) for p in range(st, len(s.prompt))]
+            cu.append(cu[-1] + len(s.prompt) - st)
+            prefix.append((list(s.blocks), st))
+        logits = self.runner.prefill(torch.tensor(toks), torch.tensor(pos), torch.tensor(slots), cu,
+                                     prefix if any(p[1] for p in prefix) else None)
         nxt = self._sample_rows(logits, batch)
         self.stats["prefill_steps"] += 1
         self.stats["prefill_tokens"] += cu[-1]
@@ -259,6 +271,9 @@ class LLMEngine:
         s.status = "finished"
         s.finish_reason = s.finish_reason or reason
         s.t_finished = time.perf_counter()
+        if self.prefix is not None and s.blocks:
+            # KV holds every token but the last sampled one
+            self.prefix.insert((s.prompt + s.output)[: s.n_tokens - 1], s.blocks)
         self.runner.kv.release(s.blocks)
         self.finished[s.seq_id] = s
 

@@ -330,7 +330,8 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()
-    def prefill(self, tokens: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor, cu_seqlens: list[int]):
+    def prefill(self, tokens: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor, cu_seqlens: list[int],
+                prefix: list | None = None):
         """Eager prefill of freshly started sequences (positions from 0).  Returns the
         last-token logits of each sequence [n_seq, vocab] (f32)."""
         cfg, mw, dev = self.cfg, self.mw, self.device
@@ -350,9 +351,12 @@ class ModelRunner:
             ops.linear(h, L.qkv, qkv, ops.GEMV_STORE)
             ops.qk_rope_kv_write(qkv, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, L.q_norm, L.k_norm, cfg.rms_eps,
                                  positions, mw.rope_cos, mw.rope_sin, slots, q, self.kv.k[i], self.kv.v[i])
-            kc = self.kv.k[i].permute(0, 2, 1, 3).reshape(-1, cfg.n_kv_heads, cfg.head_dim)[slots]
-            vc = self.kv.v[i].permute(0, 2, 1, 3).reshape(-1, cfg.n_kv_heads, cfg.head_dim)[slots]
-            ops.attn_prefill(q, kc, vc, cu_seqlens, attn, self.scale)
+            if prefix is None or not any(p[1] for p in prefix):
+                kc = self.kv.k[i].permute(0, 2, 1, 3).reshape(-1, cfg.n_kv_heads, cfg.head_dim)[slots]
+                vc = self.kv.v[i].permute(0, 2, 1, 3).reshape(-1, cfg.n_kv_heads, cfg.head_dim)[slots]
+                ops.attn_prefill(q, kc, vc, cu_seqlens, attn, self.scale)
+            else:
+                self._prefill_attn_with_prefix(i, q, attn, cu_seqlens, prefix)
             self._row_parallel(attn.view(T, -1), L.o, x)
             ops.rms_norm(x, L.ffn_norm, cfg.rms_eps, out=h)
             if L.is_moe:
@@ -368,6 +372,31 @@ class ModelRunner:
         logits = torch.empty(last.numel(), cfg.vocab, dtype=torch.float32, device=dev)
         ops.linear(hl, mw.lm_head, logits, ops.GEMV_STORE)
         return logits
+
+    def _prefill_attn_with_prefix(self, i, q, attn, cu_seqlens, prefix):
+        """Prefill attention for chunks that continue a cached prefix: queries are the new
+        tokens, keys/values are every position of the sequence read from its pages."""
+        import torch.nn.functional as F
+        cfg = self.cfg
+        kflat = self.kv.k[i].permute(0, 2, 1, 3).reshape(-1, cfg.n_kv_heads, cfg.head_dim)
+        vflat = self.kv.v[i].permute(0, 2, 1, 3).reshape(-1, cfg.n_kv_heads, cfg.head_dim)
+        for s_idx, (blocks, start) in enumerate(prefix):
+            a, b = cu_seqlens[s_idx], cu_seqlens[s_idx + 1]
+            n_new = b - a
+            total = start + n_new
+            pos = torch.arange(total, device=q.device)
+            bt = torch.tensor(blocks, device=q.device, dtype=torch.long)
+            sl = bt[pos // self.block_size] * self.block_size + pos % self.block_size
+            kk = kflat[sl].transpose(0, 1)[None]
+            vv = vflat[sl].transpose(0, 1)[None]
+            qq = q[a:b].transpose(0, 1)[None]
+            if not q.is_cuda:
+                qq, kk, vv = qq.float(), kk.float(), vv.float()
+            mask = (torch.arange(total, device=q.device)[None, :] <=
+                    (torch.arange(n_new, device=q.device)[:, None] + start))
+            o = F.scaled_dot_product_attention(qq, kk.to(qq.dtype), vv.to(qq.dtype), attn_mask=mask,
+                                               scale=self.scale, enable_gqa=(cfg.n_heads != cfg.n_kv_heads))
+            attn[a:b] = o[0].transpose(0, 1).to(attn.dtype)
 
     def _row_parallel(self, a, W, x):
         """x += a @ W^T, summed over TP ranks with NCCL (prefill)."""
