@@ -746,60 +746,59 @@ static cudaError_t launch_v4(const GemvArgs& a, cudaStream_t s) {
 }
 
 cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {
-  // Tile shape: NT from the caller's bound on rows per expert; two row tiles per warp when
-  // several token tiles share them; split K across warps only when there are too few
-  // (expert, row-tile) units to keep ~4 warps per SM scheduler busy.
+  // Tile shapes measured on B200 (kernel microbenchmarks at the Qwen3-235B decode shapes):
+  //  * one token tile (MoE experts, token groups of dense layers): register pipeline, U=4,
+  //    eight 4-warp CTAs per SM (v2<1,1,1,4,8>), ~60% of HBM bandwidth on expert streams;
+  //  * few row tiles (dense layers): split K over the warps of a CTA.
+  // An explicit variant (a.variant or SYN_GEMV_VARIANT) overrides the choice.
   const int nt = a.nt_hint <= 1 ? 1 : (a.nt_hint <= 2 ? 2 : 4);
-  const int R = (nt >= 2 && a.N % 32 == 0) ? 2 : 1;
-  const long units = (long)(a.N / (16 * R)) * a.E_active_hint;
-  const bool split = units < 148L * 16;
   static int env_variant = -1;
   if (env_variant < 0) {
     const char* v = getenv("SYN_GEMV_VARIANT");
     env_variant = v ? atoi(v) : 0;
   }
   const int variant = a.variant ? a.variant : env_variant;
-  // TMA-fed path: weights in device memory only (bulk copies are not pointed at host memory)
-  if (a.weights_in_vram && (variant == 0 || variant == 4)) {
+  if (variant == 4 && a.weights_in_vram) {
     if (nt == 1) return launch_v4<1>(a, s);
     if (nt == 2) return launch_v4<2>(a, s);
     return launch_v4<4>(a, s);
   }
-  if (!split && R == 1 && nt == 1) {
-    if (variant == 21) return launch_v2<1, 1, 1, 8>(a, s);
-    if (variant == 22) return launch_v2<1, 1, 1, 4, 8>(a, s);
-    if (variant == 23) return launch_v2<1, 1, 1, 6, 6>(a, s);
-    if (variant == 24) return launch_v2<1, 1, 1, 4, 10>(a, s);
-    if (variant == 25) return launch_v2<1, 1, 1, 2, 12>(a, s);
-    if (variant == 26) return launch_v2<1, 1, 1, 3, 10>(a, s);
-    if (variant == 0 || variant == 22) return launch_v2<1, 1, 1, 4, 8>(a, s);
+  if (variant == 3) {
+    if (nt == 1) return launch_v3<1, 1>(a, s);
+    if (nt == 2) return launch_v3<1, 2>(a, s);
+    return launch_v3<1, 4>(a, s);
   }
-  if (split && nt == 4) {
-    static int dense_variant = -1;
-    if (dense_variant < 0) {
-      const char* v = getenv("SYN_GEMV_DENSE");
-      dense_variant = v ? atoi(v) : 0;
+  if (nt == 1) {
+    switch (variant) {
+      case 21: return launch_v2<1, 1, 1, 8>(a, s);
+      case 23: return launch_v2<1, 1, 1, 6, 6>(a, s);
+      case 24: return launch_v2<1, 1, 1, 4, 10>(a, s);
+      case 25: return launch_v2<1, 1, 1, 2, 12>(a, s);
+      case 26: return launch_v2<1, 1, 1, 3, 10>(a, s);
+      case 27: return launch_v2<1, 1, 8, 4, 1>(a, s);
+      case 28: return launch_v2<1, 1, 4, 4, 2>(a, s);
+      case 29: return launch_v2<1, 1, 2, 4, 4>(a, s);
+      default: break;
     }
-    if (dense_variant == 1) return launch_v2<1, 4, 8, 2, 1>(a, s);
-    if (dense_variant == 2) return launch_v2<1, 4, 4, 2, 1>(a, s);
-    if (dense_variant == 3) return launch_v2<2, 4, 8, 2, 1>(a, s);
-    if (dense_variant == 4) return launch_v2<1, 4, 2, 2, 2>(a, s);
+    const long units = (long)(a.N / 16) * a.E_active_hint;
+    if (units < 148L * 8) return launch_v2<1, 1, 4, 4, 2>(a, s);  // few tiles: split K by 4
+    return launch_v2<1, 1, 1, 4, 8>(a, s);
   }
-  if (!split && variant == 2) {
-    if (R == 1) {
-      if (nt == 1) return launch_v2<1, 1, 1>(a, s);
-      if (nt == 2) return launch_v2<1, 2, 1>(a, s);
-      return launch_v2<1, 4, 1>(a, s);
-    }
-    return nt == 2 ? launch_v2<2, 2, 1>(a, s) : launch_v2<2, 4, 1>(a, s);
+  switch (variant) {
+    case 11: return launch_v2<1, 4, 8, 2, 1>(a, s);
+    case 12: return launch_v2<1, 4, 4, 2, 1>(a, s);
+    case 13: return launch_v2<2, 4, 8, 2, 1>(a, s);
+    case 14: return launch_v2<1, 4, 8, 8, 1>(a, s);
+    default: break;
   }
-  if (R == 1) {
-    if (nt == 1) return split ? launch_v2<1, 1, 8>(a, s) : launch_v3<1, 1>(a, s);
-    if (nt == 2) return split ? launch_v2<1, 2, 8>(a, s) : launch_v3<1, 2>(a, s);
-    return split ? launch_v2<1, 4, 8>(a, s) : launch_v3<1, 4>(a, s);
+  const bool r2 = a.N % 32 == 0;
+  const long units = (long)(a.N / (16 * (r2 ? 2 : 1))) * a.E_active_hint;
+  if (units < 148L * 16) {
+    if (nt == 2) return r2 ? launch_v2<2, 2, 8>(a, s) : launch_v2<1, 2, 8>(a, s);
+    return r2 ? launch_v2<2, 4, 8>(a, s) : launch_v2<1, 4, 8>(a, s);
   }
-  if (nt == 2) return split ? launch_v2<2, 2, 8>(a, s) : launch_v3<2, 2>(a, s);
-  return split ? launch_v2<2, 4, 8>(a, s) : launch_v3<2, 4>(a, s);
+  if (nt == 2) return r2 ? launch_v3<2, 2>(a, s) : launch_v3<1, 2>(a, s);
+  return r2 ? launch_v3<2, 4>(a, s) : launch_v3<1, 4>(a, s);
 }
 
 }  // namespace syn

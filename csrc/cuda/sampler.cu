@@ -258,3 +258,251 @@ cudaError_t launch_philox(uint64_t seed, uint64_t stream, uint64_t counter0, int
 }
 
 }  // namespace syn
+
+namespace syn {
+
+// ---------------------------------------------------------------------------------------
+// Speculative verification (reference op `VerifyAccept`, plan/rfcs/RFC-0012-execution-
+// scheduler.md :605-617; draw order plan/decisions/ADR-0107-counter-based-sampling-rng.md).
+// Point-mass drafts d_1..d_g per sequence against target logits rows 0..g:
+//   greedy rows : accept d_j while d_j == argmax_j; at the first mismatch emit argmax_j;
+//                 if all accepted emit the bonus argmax_g.  No draws.
+//   sampled rows: draw u_j; accept iff u_j < p_j(d_j) (p after temperature/top-k/top-p);
+//                 at the first rejection draw once more from p_j with d_j removed (the
+//                 residual of a point-mass draft); if all accepted draw the bonus from p_g.
+// The output distribution equals sampling from the target alone.
+
+
+// Argmax over a row (all threads participate; ties to the lower index).
+__device__ int block_argmax(const float* lg, int V, float* sb, int* si) {
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = lg[i];
+    if (v > best || (v == best && i < bi)) { best = v; bi = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) { sb[threadIdx.x >> 5] = best; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = sb[0];
+    int id = si[0];
+    for (int i = 1; i < (int)(blockDim.x >> 5); ++i)
+      if (sb[i] > b || (sb[i] == b && si[i] < id)) { b = sb[i]; id = si[i]; }
+    si[0] = id;
+  }
+  __syncthreads();
+  const int r = si[0];
+  __syncthreads();
+  return r;
+}
+
+// Fixed-point masses with temperature and top-k / top-p thresholds, as in sample_kernel.
+struct RowDist {
+  float inv_t, mx;
+  uint32_t kth_key;
+  unsigned long long floor_mass;
+};
+
+__device__ __forceinline__ unsigned long long row_mass(const float* lg, const RowDist& d, int i) {
+  const float z = lg[i] * d.inv_t;
+  if (f2key(z) < d.kth_key) return 0ull;
+  const unsigned long long m = (unsigned long long)(__expf(z - d.mx) * 4294967296.0f);
+  return m >= d.floor_mass ? m : 0ull;
+}
+
+__device__ void row_setup(const float* lg, int V, float temp, int k, float tp, RowDist& d, float* red,
+                          uint32_t* hist, unsigned long long* mhist, unsigned long long* scan) {
+  d.inv_t = 1.f / temp;
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) mx = fmaxf(mx, lg[i] * d.inv_t);
+  d.mx = block_max(mx, red);
+  d.kth_key = 0;
+  d.floor_mass = 0;
+  if (k > 0 && k < V) {
+    uint32_t prefix = 0, want = (uint32_t)k;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
+      __syncthreads();
+      const uint32_t hmask = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
+      for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const uint32_t key = f2key(lg[i] * d.inv_t);
+        if ((key & hmask) == (prefix & hmask)) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        uint32_t acc = 0;
+        int dd = 255;
+        for (; dd > 0; --dd) {
+          if (acc + hist[dd] >= want) break;
+          acc += hist[dd];
+        }
+        hist[256] = prefix | ((uint32_t)dd << shift);
+        hist[257] = want - acc;
+      }
+      __syncthreads();
+      prefix = hist[256];
+      want = hist[257];
+      __syncthreads();
+    }
+    d.kth_key = prefix;
+  }
+  if (tp < 1.f) {
+    unsigned long long tot = 0;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) tot += row_mass(lg, d, i);
+    scan[threadIdx.x] = tot;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long s = 0;
+      for (int i = 0; i < (int)blockDim.x; ++i) s += scan[i];
+      scan[0] = s;
+    }
+    __syncthreads();
+    const unsigned long long need = (unsigned long long)((double)tp * (double)scan[0]);
+    __syncthreads();
+    unsigned long long prefix = 0, acc_above = 0;
+    for (int shift = 32; shift >= 0; shift -= 8) {
+      for (int i = threadIdx.x; i < 256; i += blockDim.x) mhist[i] = 0;
+      __syncthreads();
+      const unsigned long long hmask = shift == 32 ? 0ull : (~0ull << (shift + 8));
+      for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const unsigned long long m = row_mass(lg, d, i);
+        if (m && (m & hmask) == (prefix & hmask)) atomicAdd(&mhist[(m >> shift) & 255ull], m);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        unsigned long long acc = acc_above;
+        int dd = 255;
+        for (; dd > 0; --dd) {
+          if (acc + mhist[dd] >= need) break;
+          acc += mhist[dd];
+        }
+        scan[0] = prefix | ((unsigned long long)dd << shift);
+        scan[1] = acc;
+      }
+      __syncthreads();
+      prefix = scan[0];
+      acc_above = scan[1];
+      __syncthreads();
+    }
+    d.floor_mass = prefix;
+  }
+}
+
+// Inverse-CDF draw over the row's masses with token `exclude` removed (-1: none).
+__device__ int row_draw(const float* lg, int V, const RowDist& d, int exclude, uint32_t x0,
+                        unsigned long long* scan, int* pick) {
+  const int per = (V + blockDim.x - 1) / blockDim.x;
+  const int i0 = threadIdx.x * per, i1 = min(V, i0 + per);
+  unsigned long long local = 0;
+  for (int i = i0; i < i1; ++i)
+    if (i != exclude) local += row_mass(lg, d, i);
+  scan[threadIdx.x] = local;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long s = 0;
+    for (int i = 0; i < (int)blockDim.x; ++i) {
+      const unsigned long long v = scan[i];
+      scan[i] = s;
+      s += v;
+    }
+    scan[blockDim.x] = __umul64hi((unsigned long long)x0 << 32, s);
+    *pick = -1;
+  }
+  __syncthreads();
+  const unsigned long long target = scan[blockDim.x];
+  unsigned long long run = scan[threadIdx.x];
+  if (run <= target) {
+    for (int i = i0; i < i1; ++i) {
+      if (i == exclude) continue;
+      const unsigned long long m = row_mass(lg, d, i);
+      if (m == 0) continue;
+      if (run + m > target) { *pick = i; break; }
+      run += m;
+    }
+  }
+  __syncthreads();
+  const int r = *pick >= 0 ? *pick : 0;
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(SMP_THREADS) verify_accept_kernel(VerifyArgs a) {
+  __shared__ float red[32];
+  __shared__ float sb[32];
+  __shared__ int si[32];
+  __shared__ uint32_t hist[258];
+  __shared__ unsigned long long mhist[256];
+  __shared__ unsigned long long scan[SMP_THREADS + 1];
+  __shared__ int pick;
+  __shared__ unsigned long long s_tot, s_md;
+  const int sq = blockIdx.x;
+  const int g = a.g;
+  const float temp = a.temperature[sq];
+  uint64_t ctr = (uint64_t)a.counter[sq];
+  int n_acc = g;
+  int last = 0;
+  for (int j = 0; j <= g; ++j) {
+    const float* lg = a.logits + ((int64_t)sq * (g + 1) + j) * a.V;
+    const int dj = j < g ? a.draft[sq * g + j] : -1;
+    int tok;
+    if (!(temp > 0.f)) {
+      tok = block_argmax(lg, a.V, sb, si);
+      if (j < g && tok == dj) {
+        if (threadIdx.x == 0) a.out_tokens[sq * (g + 1) + j] = dj;
+        continue;
+      }
+    } else {
+      RowDist d;
+      row_setup(lg, a.V, temp, a.top_k[sq], a.top_p[sq], d, red, hist, mhist, scan);
+      if (j < g) {
+        unsigned long long loc = 0;
+        for (int i = threadIdx.x; i < a.V; i += blockDim.x) loc += row_mass(lg, d, i);
+        scan[threadIdx.x] = loc;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+          unsigned long long s = 0;
+          for (int i = 0; i < (int)blockDim.x; ++i) s += scan[i];
+          s_tot = s;
+          s_md = (dj >= 0 && dj < a.V) ? row_mass(lg, d, dj) : 0ull;
+        }
+        __syncthreads();
+        const uint32_t u = philox_draw((uint64_t)a.seed[sq], (uint64_t)a.stream[sq], ctr++);
+        const unsigned long long thr = __umul64hi((unsigned long long)u << 32, s_tot);  // floor(u * total)
+        if (thr < s_md) {
+          if (threadIdx.x == 0) a.out_tokens[sq * (g + 1) + j] = dj;
+          __syncthreads();
+          continue;
+        }
+        tok = row_draw(lg, a.V, d, dj, philox_draw((uint64_t)a.seed[sq], (uint64_t)a.stream[sq], ctr++), scan,
+                       &pick);
+      } else {
+        tok = row_draw(lg, a.V, d, -1, philox_draw((uint64_t)a.seed[sq], (uint64_t)a.stream[sq], ctr++), scan,
+                       &pick);
+      }
+    }
+    if (threadIdx.x == 0) a.out_tokens[sq * (g + 1) + j] = tok;
+    n_acc = j < g ? j : g;
+    last = j;
+    break;
+  }
+  (void)last;
+  if (threadIdx.x == 0) {
+    a.n_accept[sq] = n_acc;
+    a.counter[sq] = (int64_t)ctr;
+  }
+}
+
+cudaError_t launch_verify_accept(const VerifyArgs& a, cudaStream_t s) {
+  if (a.S == 0) return cudaSuccess;
+  verify_accept_kernel<<<a.S, SMP_THREADS, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace syn

@@ -73,6 +73,9 @@ void tp_reduce_norm(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, i
                     torch::Tensor step_ctr, int64_t n_layers, int64_t layer, int64_t timeout_ns, torch::Tensor status,
                     int64_t off_recv, int64_t off_flag, torch::Tensor x, torch::Tensor wn, torch::Tensor hout,
                     double eps);
+void verify_accept(torch::Tensor logits, torch::Tensor draft, torch::Tensor temperature, torch::Tensor top_k,
+                   torch::Tensor top_p, torch::Tensor seed, torch::Tensor stream, torch::Tensor counter,
+                   torch::Tensor out_tokens, torch::Tensor n_accept);
 void register_all(pybind11::module& m);
 void register_runtime(pybind11::module& m);
 void register_formats(pybind11::module& m);

@@ -126,6 +126,20 @@ cudaError_t launch_argmax(const float* logits, int T, int V, int32_t* out, cudaS
 cudaError_t launch_sample(const float* logits, int T, int V, const float* temperature, const int32_t* top_k,
                           const float* top_p, const int64_t* seed, const int64_t* stream, int64_t* counter,
                           int32_t* out, cudaStream_t s);
+struct VerifyArgs {
+  const float* logits;       // [S * (g+1), V]
+  const int32_t* draft;      // [S, g]
+  int S, g, V;
+  const float* temperature;  // [S]
+  const int32_t* top_k;      // [S]
+  const float* top_p;        // [S]
+  const int64_t* seed;
+  const int64_t* stream;
+  int64_t* counter;          // [S], advanced by the number of draws taken
+  int32_t* out_tokens;       // [S, g+1]
+  int32_t* n_accept;         // [S]
+};
+cudaError_t launch_verify_accept(const VerifyArgs& a, cudaStream_t s);
 cudaError_t launch_philox(uint64_t seed, uint64_t stream, uint64_t counter0, int n, uint32_t* out, cudaStream_t s);
 
 }  // namespace syn

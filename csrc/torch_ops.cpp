@@ -516,4 +516,24 @@ void tp_reduce_norm(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, i
                                        (float)eps, (int)x.size(0), cur_stream()));
 }
 
+
+// Exact acceptance of point-mass drafts (see csrc/cuda/sampler.cu).
+void verify_accept(torch::Tensor logits, torch::Tensor draft, torch::Tensor temperature, torch::Tensor top_k,
+                   torch::Tensor top_p, torch::Tensor seed, torch::Tensor stream, torch::Tensor counter,
+                   torch::Tensor out_tokens, torch::Tensor n_accept) {
+  SYN_CHECK_INPUT(logits);
+  SYN_CHECK_INPUT(draft);
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && draft.scalar_type() == torch::kInt32 && draft.dim() == 2,
+              "logits f32, draft int32 [S, g]");
+  const int64_t S = draft.size(0), g = draft.size(1);
+  TORCH_CHECK(logits.size(0) == S * (g + 1), "logits rows must be S*(g+1)");
+  TORCH_CHECK(out_tokens.numel() >= S * (g + 1) && n_accept.numel() >= S, "outputs");
+  VerifyArgs a{logits.data_ptr<float>(), draft.data_ptr<int32_t>(), (int)S, (int)g, (int)logits.size(1),
+               temperature.data_ptr<float>(), top_k.data_ptr<int32_t>(), top_p.data_ptr<float>(),
+               seed.data_ptr<int64_t>(), stream.data_ptr<int64_t>(), counter.data_ptr<int64_t>(),
+               out_tokens.data_ptr<int32_t>(), n_accept.data_ptr<int32_t>()};
+  const at::cuda::CUDAGuard guard(logits.device());
+  SYN_CHECK_CUDA(launch_verify_accept(a, cur_stream()));
+}
+
 }  // namespace syn

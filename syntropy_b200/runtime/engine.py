@@ -62,8 +62,9 @@ class StepOutput:
 
 class LLMEngine:
     def __init__(self, runner: ModelRunner, max_prefill_tokens: int = 8192, eos_token_id: int | None = None,
-                 dist_ctx=None, prefix_cache: bool = False):
+                 dist_ctx=None, prefix_cache: bool = False, spec=None):
         self.runner = runner
+        self.spec = spec  # runtime.spec.SpecConfig or None
         self.prefix = None
         if prefix_cache:
             from ..kv.prefix import PrefixCache
@@ -79,7 +80,8 @@ class LLMEngine:
         self.finished: dict[int, Sequence] = {}
         self._ids = itertools.count()
         self._boot_seed = random.getrandbits(63)
-        self.stats = {"prefill_steps": 0, "decode_steps": 0, "decode_tokens": 0, "prefill_tokens": 0}
+        self.stats = {"prefill_steps": 0, "decode_steps": 0, "decode_tokens": 0, "prefill_tokens": 0,
+                      "spec_drafted": 0, "spec_accepted": 0}
 
     # ------------------------------------------------------------------ intake
     def add_request(self, prompt: list[int], params: SamplingParams | None = None, choice_index: int = 0) -> int:
@@ -214,6 +216,75 @@ class LLMEngine:
         return out.cpu().tolist()
 
     def _decode(self) -> list[StepOutput]:
+        if self.spec is not None and self.dist is None:
+            return self._decode_spec()
+        return self._decode_plain()
+
+    def _decode_spec(self) -> list[StepOutput]:
+        """One verify window per sequence: rows [last, d1..dg] at positions p..p+g."""
+        from .spec import verify
+        r, kv, g = self.runner, self.runner.kv, self.spec.gamma
+        seqs = self.running[: max(1, r.max_batch // (g + 1))]
+        rows = len(seqs) * (g + 1)
+        d = r.desc.h
+        drafts = []
+        for i, s in enumerate(seqs):
+            hist = s.prompt + s.output
+            dr = self.spec.drafter.propose(hist, g)
+            drafts.append(dr)
+            p = s.n_tokens - 1
+            kv.ensure(s.blocks, p + g + 1)
+            bt = torch.tensor(s.blocks, dtype=torch.int32)
+            for j, tok in enumerate([s.output[-1]] + dr):
+                row = i * (g + 1) + j
+                d["tokens"][row] = tok
+                d["pos"][row] = p + j
+                d["ctx_len"][row] = p + j + 1
+                d["slot"][row] = kv.slot(s.blocks, p + j)
+                d["block_tables"][row, : len(s.blocks)] = bt
+                d["temperature"][row] = 0.0
+        if r.use_graphs:
+            from .runner import bucket_for
+            for i in range(rows, bucket_for(rows)):
+                d["tokens"][i] = 0
+                d["pos"][i] = 0
+                d["ctx_len"][i] = 1
+                d["slot"][i] = -1
+                d["block_tables"][i, 0] = 0
+                d["temperature"][i] = 0.0
+        r.decode(rows)
+        logits = r.buf["logits"][:rows]
+        temp = torch.tensor([s.params.temperature for s in seqs], dtype=torch.float32)
+        topk = torch.tensor([s.params.top_k for s in seqs], dtype=torch.int32)
+        topp = torch.tensor([s.params.top_p for s in seqs], dtype=torch.float32)
+        seed = torch.tensor([s.seed for s in seqs], dtype=torch.int64)
+        stream = torch.tensor([s.stream for s in seqs], dtype=torch.int64)
+        ctr = torch.tensor([s.rng_counter for s in seqs], dtype=torch.int64)
+        toks, nacc = verify(logits, torch.tensor(drafts, dtype=torch.int32), temp, topk, topp, seed, stream, ctr)
+        self.stats["decode_steps"] += 1
+        outs = []
+        for i, s in enumerate(seqs):
+            s.rng_counter = int(ctr[i])
+            n = int(nacc[i])
+            self.stats["spec_drafted"] += g
+            self.stats["spec_accepted"] += n
+            new = toks[i, : n + 1].tolist()
+            emitted = []
+            for t in new:
+                o = self._append(s, t)
+                emitted.append(t)
+                if o.finished:
+                    break
+            self.stats["decode_tokens"] += len(emitted)
+            outs.append(StepOutput(s.seq_id, emitted, s.status == "finished", s.finish_reason))
+        self._reap()
+        return outs
+
+    @property
+    def acceptance_rate(self) -> float:
+        return self.stats["spec_accepted"] / max(1, self.stats["spec_drafted"])
+
+    def _decode_plain(self) -> list[StepOutput]:
         r = self.runner
         kv = r.kv
         seqs = self.running

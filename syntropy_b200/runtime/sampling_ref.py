@@ -75,3 +75,69 @@ def sample_ref(logits, temperature, top_k, top_p, seed, stream, counter) -> torc
         out[t] = tok
         counter[t] = c
     return out
+
+
+def _row_masses(lg: torch.Tensor, temperature: float, top_k: int, top_p: float) -> torch.Tensor:
+    z = lg.float() / temperature
+    V = z.numel()
+    keep = torch.ones(V, dtype=torch.bool)
+    if 0 < top_k < V:
+        keep &= z >= torch.sort(z, descending=True).values[top_k - 1]
+    mass = torch.where(keep, torch.floor(torch.exp(z - z.max()).double() * 4294967296.0),
+                       torch.zeros(V, dtype=torch.float64)).to(torch.int64)
+    if top_p < 1.0:
+        total = int(mass.sum())
+        need = int(top_p * total)
+        vals = torch.sort(mass, descending=True).values
+        idx = min(int(torch.searchsorted(torch.cumsum(vals, 0), torch.tensor(need)).item()), V - 1)
+        mass = torch.where(mass >= int(vals[idx]), mass, torch.zeros_like(mass))
+    return mass
+
+
+def _draw(mass: torch.Tensor, x0: int) -> int:
+    total = int(mass.sum())
+    target = (x0 * total) >> 32
+    tok = int(torch.searchsorted(torch.cumsum(mass, 0), torch.tensor(target), right=True).item())
+    return min(tok, mass.numel() - 1)
+
+
+def verify_ref(logits, draft, temperature, top_k, top_p, seed, stream, counter):
+    """Host oracle of the device VerifyAccept kernel (point-mass drafts).
+    logits [S*(g+1), V], draft [S, g] -> (tokens [S, g+1], n_accept [S]); counter updated."""
+    S, g = draft.shape
+    out = torch.zeros(S, g + 1, dtype=torch.int32)
+    nacc = torch.zeros(S, dtype=torch.int32)
+    for s in range(S):
+        t = float(temperature[s])
+        ctr = int(counter[s])
+        n = g
+        for j in range(g + 1):
+            lg = logits[s * (g + 1) + j]
+            dj = int(draft[s, j]) if j < g else -1
+            if not t > 0:
+                a = int(torch.argmax(lg).item())
+                if j < g and a == dj:
+                    out[s, j] = dj
+                    continue
+                out[s, j] = a
+                n = min(j, g)
+                break
+            mass = _row_masses(lg, t, int(top_k[s]), float(top_p[s]))
+            if j < g:
+                u = philox_draw(int(seed[s]), int(stream[s]), ctr)
+                ctr += 1
+                if (u * int(mass.sum())) >> 32 < int(mass[dj]):
+                    out[s, j] = dj
+                    continue
+                m2 = mass.clone()
+                m2[dj] = 0
+                out[s, j] = _draw(m2, philox_draw(int(seed[s]), int(stream[s]), ctr))
+                ctr += 1
+                n = j
+                break
+            out[s, j] = _draw(mass, philox_draw(int(seed[s]), int(stream[s]), ctr))
+            ctr += 1
+            n = g
+        nacc[s] = n
+        counter[s] = ctr
+    return out, nacc
