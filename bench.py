@@ -94,6 +94,9 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="dev only: override layer count (invalid headline)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--baseline", action="store_true", help="NCCL all-gather/reduce-scatter MoE data plane")
+    ap.add_argument("--expert-cache-frac", type=float, default=0.6,
+                    help="VRAM-resident share of each rank's experts (named config: 0.6; rest in pinned host RAM)")
+    ap.add_argument("--no-uncapped", action="store_true", help="skip the extra all-resident measurement")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -126,21 +129,26 @@ def main():
         ep = EPGroup(ctx, cfg.n_experts, cfg.top_k, cfg.hidden, cap=B, n_layers=cfg.n_layers,
                      fused=not args.baseline)
     t0 = time.time()
-    mw = prepare_weights(cfg, dev, seed=args.seed, max_pos=args.prompt + args.decode + 16,
+    mw = prepare_weights(cfg, dev, seed=args.seed, max_pos=args.prompt + max(args.decode, args.warmup + args.steps + 40) + 16,
                          expert_range=ep.expert_range if ep else None)
     torch.cuda.synchronize()
     t_weights = time.time() - t0
-    max_len = args.prompt + args.decode
+    # decode length: the config's, extended only if the requested steps need more tokens
+    decode_len = max(args.decode, args.warmup + args.steps + min(args.steps, 16) + 8)
+    max_len = args.prompt + decode_len
+    cache = None
+    if args.expert_cache_frac < 1.0 and cfg.is_moe:
+        from syntropy_b200.experts.cache import ExpertCache
+        cache = ExpertCache(mw.layers, args.expert_cache_frac, dev)
     runner = ModelRunner(mw, max_batch=B, max_seq_len=max_len + 16, ep=ep,
                          use_graphs=not (ep is not None and not ep.fused))
+    runner.expert_cache = cache
     eng = LLMEngine(runner, max_prefill_tokens=8192, dist_ctx=ctx)
     g = torch.Generator().manual_seed(1234)
     all_prompts = [torch.randint(0, cfg.vocab, (args.prompt,), generator=g).tolist() for _ in range(args.batch)]
     prompts = all_prompts[rank::world]
     # ---- prefill: TTFT of each request (all submitted at t0) ----
-    total_steps = args.warmup + args.steps
-    assert total_steps + 1 <= args.decode, "warmup + steps must fit in the decode length"
-    ids = [eng.add_request(p, SamplingParams(max_tokens=args.decode, temperature=0.0)) for p in prompts]
+    ids = [eng.add_request(p, SamplingParams(max_tokens=decode_len, temperature=0.0)) for p in prompts]
     if ctx.enabled:
         import torch.distributed as dist
         dist.barrier(group=ctx.cpu_group)
@@ -182,6 +190,20 @@ def main():
     dev_ms = max_over_ranks(ctx, dev_ms)
     e2e_s = max_over_ranks(ctx, e2e_s)
     status = ep.check_status() if ep is not None else 0
+    uncapped = None
+    if cache is not None and not args.no_uncapped:
+        # same model and batch with every expert VRAM-resident (the cap lifted)
+        cache.promote_all()
+        for _ in range(2):
+            eng.step()
+        runner.time_events = []
+        torch.cuda.synchronize()
+        for _ in range(min(args.steps, 16)):
+            eng.step()
+        torch.cuda.synchronize()
+        u_ms = max_over_ranks(ctx, sum(a.elapsed_time(b) for a, b in runner.time_events)) / len(runner.time_events)
+        uncapped = {"value": round(args.batch * 1e3 / u_ms, 2), "ms_per_step": round(u_ms, 4),
+                    "steps": len(runner.time_events), "expert_cache_frac": 1.0}
     ms_step = dev_ms / args.steps
     value = args.batch * 1e3 / ms_step          # whole-job tokens/s over all ranks
     e2e_value = args.batch * args.steps / e2e_s
@@ -192,10 +214,12 @@ def main():
         "data": "synthetic uniform-random prompts, random-init N(0,0.02) weights quantised to 4-bit",
         "p50_ttft_ms": round(p50_ttft_ms, 2),
         "config": {"model": args.model if not args.layers else f"{args.model}[layers={args.layers}] (DEV, not headline)",
-                   "global_batch": B, "seq_len": args.prompt, "decode_len": args.decode,
+                   "global_batch": args.batch, "seq_len": args.prompt, "decode_len": decode_len,
                    "parallelism": (f"ep{world}+dp-attention" + ("" if ep is None or ep.fused else " (nccl baseline)"))
                    if world > 1 else "single-gpu",
-                   "expert_cache_frac": 1.0, "l2": "inputs larger than L2 (weights 140+ GB streamed per step)",
+                   "expert_cache_frac": args.expert_cache_frac if cfg.is_moe else 1.0,
+                   "host_tier_gb": round(cache.host_bytes() / 1e9, 2) if cache is not None else 0.0,
+                   "l2": "inputs larger than L2 (weights 140+ GB streamed per step)",
                    "weights_gb": round(mw.nbytes() / 1e9, 2), "weight_build_s": round(t_weights, 1)},
         "clocks": clk.summary(),
         "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": runner.desc.nbytes,
@@ -203,6 +227,7 @@ def main():
         "gpu_launches": (n_launch * args.steps) if n_launch else None,
         "impl": "syntropy",
         "device_status": status,
+        "all_experts_resident": uncapped,
     }
     if rank == 0:
         print(json.dumps(out))

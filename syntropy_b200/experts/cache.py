@@ -57,7 +57,73 @@ class ExpertCache:
         self.hysteresis = hysteresis
         self.banks = []
         for L in self.layers:
-            self.banks.append(_TieredBank(L.experts_gu, L.experts_down, frac, device))
+            b = _TieredBank(L.experts_gu, L.experts_down, frac, device)
+            self.banks.append(b)
+            L.expert_tier = b
+        self._staging = None
+
+    def promote_all(self):
+        """Move every expert to VRAM (cap lifted) without changing the pointer-table
+        tensors, so CUDA graphs captured against them stay valid."""
+        for L, b in zip(self.layers, self.banks):
+            for bank, p in zip((L.experts_gu, L.experts_down), b.parts):
+                if p is None:
+                    continue
+                qf = torch.empty((b.E,) + tuple(p["qv"].shape[1:]), dtype=p["qv"].dtype, device=p["qv"].device)
+                sf = torch.empty((b.E,) + tuple(p["sv"].shape[1:]), dtype=p["sv"].dtype, device=p["sv"].device)
+                for e in range(b.E):
+                    s_ = b.slot_of[e]
+                    if s_ >= 0:
+                        qf[e].copy_(p["qv"][s_])
+                        sf[e].copy_(p["sv"][s_])
+                    else:
+                        qf[e].copy_(p["qh"][b.host_of[e]], non_blocking=True)
+                        sf[e].copy_(p["sh"][b.host_of[e]], non_blocking=True)
+                torch.cuda.synchronize()
+                bank.qw, bank.sm = qf, sf
+                p["qv"], p["sv"] = qf, sf
+                qs, ss = qf.stride(0) * 4, sf.stride(0) * 2
+                bank.qw_ptrs.copy_(torch.tensor([qf.data_ptr() + e * qs for e in range(b.E)], dtype=torch.int64))
+                bank.sm_ptrs.copy_(torch.tensor([sf.data_ptr() + e * ss for e in range(b.E)], dtype=torch.int64))
+                bank.bank_contiguous = True
+            b.slot_of = list(range(b.E))
+            b.host_of = [-1] * b.E
+            b.n_res = b.E
+        self.frac = 1.0
+        self._staging = None
+        torch.cuda.empty_cache()
+
+    def staged_ptrs(self, L):
+        """Pointer tables with every expert of layer L in VRAM: residents in place, host
+        experts copied (copy engine) into a staging bank shared by all layers.  Used by
+        prefill, whose GEMM streams weights with bulk copies that must read device memory."""
+        b = L.expert_tier
+        nh = b.E - b.n_res
+        if nh == 0:
+            return (L.experts_gu.qw_ptrs, L.experts_gu.sm_ptrs), (L.experts_down.qw_ptrs, L.experts_down.sm_ptrs)
+        if self._staging is None:
+            self._staging = []
+            for p in b.parts:
+                self._staging.append({"q": torch.empty_like(p["qh"], device=self.device),
+                                      "s": torch.empty_like(p["sh"], device=self.device)})
+        out = []
+        for which, p in enumerate(b.parts):
+            st = self._staging[which]
+            st["q"].copy_(p["qh"], non_blocking=True)
+            st["s"].copy_(p["sh"], non_blocking=True)
+            qp, sp = [], []
+            for e in range(b.E):
+                slot = b.slot_of[e]
+                if slot >= 0:
+                    qp.append(p["qv"].data_ptr() + slot * p["qv"].stride(0) * 4)
+                    sp.append(p["sv"].data_ptr() + slot * p["sv"].stride(0) * 2)
+                else:
+                    h = b.host_of[e]
+                    qp.append(st["q"].data_ptr() + h * st["q"].stride(0) * 4)
+                    sp.append(st["s"].data_ptr() + h * st["s"].stride(0) * 2)
+            out.append((torch.tensor(qp, dtype=torch.int64, device=self.device),
+                        torch.tensor(sp, dtype=torch.int64, device=self.device)))
+        return out[0], out[1]
 
     @property
     def n_resident(self) -> int:

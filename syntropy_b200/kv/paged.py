@@ -44,7 +44,7 @@ class BlockAllocator:
 
 class PagedKVCache:
     def __init__(self, n_layers: int, num_blocks: int, n_kv_heads: int, head_dim: int, block_size: int = 16,
-                 dtype=torch.bfloat16, device="cpu"):
+                 dtype=torch.bfloat16, device="cpu", with_v: bool = True):
         self.n_layers = n_layers
         self.num_blocks = num_blocks
         self.block_size = block_size
@@ -52,7 +52,8 @@ class PagedKVCache:
         self.head_dim = head_dim
         shape = (num_blocks, n_kv_heads, block_size, head_dim)
         self.k = [torch.zeros(shape, dtype=dtype, device=device) for _ in range(n_layers)]
-        self.v = [torch.zeros(shape, dtype=dtype, device=device) for _ in range(n_layers)]
+        # latent caches (MLA) keep one tensor per layer: V aliases K
+        self.v = [torch.zeros(shape, dtype=dtype, device=device) for _ in range(n_layers)] if with_v else self.k
         self.alloc = BlockAllocator(num_blocks)
 
     @staticmethod

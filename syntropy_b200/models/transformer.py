@@ -80,6 +80,9 @@ class LayerWeights:
     experts_gu: ExpertBank | None = None
     experts_down: ExpertBank | None = None
     is_moe: bool = False
+    mla: dict | None = None
+    shared_gu: object = None
+    shared_down: object = None
 
 
 @dataclass
@@ -92,6 +95,7 @@ class ModelWeights:
     layers: list = field(default_factory=list)
     rope_cos: torch.Tensor | None = None
     rope_sin: torch.Tensor | None = None
+    mtp: object = None
 
     def nbytes(self) -> int:
         tot = 0
@@ -117,6 +121,33 @@ class ModelWeights:
             for v in L.__dict__.values():
                 add(v)
         return tot
+
+
+class _RemapState(dict):
+    """Serves "layers.0.<x>" from "<prefix><x>" of an underlying (possibly lazy) state."""
+
+    def __init__(self, base, prefix):
+        super().__init__()
+        self.base, self.prefix = base, prefix
+
+    def __getitem__(self, name):
+        return self.base[name.replace("layers.0.", self.prefix)] if name.startswith("layers.0.") else self.base[name]
+
+    def __contains__(self, name):
+        return name.replace("layers.0.", self.prefix) in self.base
+
+
+def _prepare_mtp(cfg, get, quant, device, base_state, seed, expert_range):
+    """The multi-token-prediction head: h' = proj([enorm(emb(t+1)); hnorm(x_t)]) followed by
+    one transformer block shaped like the last layer (weights under "mtp.")."""
+    h = cfg.hidden
+    m = {"enorm": get("mtp.enorm", (h,)).float(), "hnorm": get("mtp.hnorm", (h,)).float(),
+         "proj": _linear_weight(get("mtp.proj", (h, 2 * h)), "bf16" if device.type == "cuda" else quant, device)}
+    last_moe = cfg.layer_is_moe(cfg.n_layers - 1)
+    c1 = cfg.replace(n_layers=1, first_dense_layers=0 if last_moe else 1, n_mtp=0)
+    st = _RemapState(base_state, "mtp.block.")
+    m["block"] = prepare_weights(c1, device, seed, quant, st, 8, expert_range).layers[0]
+    return m
 
 
 class _LazyState(dict):
@@ -204,15 +235,23 @@ def prepare_weights(cfg: ModelConfig, device="cpu", seed: int = 0, quant: str | 
     for i in range(cfg.n_layers):
         pre = f"layers.{i}."
         sh = layer_shapes(cfg, i)
-        qkv = torch.cat([get(pre + "q_proj", sh["q_proj"]), get(pre + "k_proj", sh["k_proj"]),
-                         get(pre + "v_proj", sh["v_proj"])], 0)
-        L = LayerWeights(
-            attn_norm=get(pre + "attn_norm", sh["attn_norm"]).float(),
-            ffn_norm=get(pre + "ffn_norm", sh["ffn_norm"]).float(),
-            qkv=_linear_weight(qkv, quant, device),
-            o=_linear_weight(get(pre + "o_proj", sh["o_proj"]), quant, device),
-        )
-        del qkv
+        if cfg.is_mla:
+            from .mla import prepare_mla
+            L = LayerWeights(attn_norm=get(pre + "attn_norm", sh["attn_norm"]).float(),
+                             ffn_norm=get(pre + "ffn_norm", sh["ffn_norm"]).float(), qkv=None,
+                             o=_linear_weight(get(pre + "o_proj", sh["o_proj"]), quant, device))
+            L.mla = prepare_mla(cfg, lambda n: get(n, sh[n.split(".")[-1]]), pre,
+                                lambda w: _linear_weight(w, quant, device))
+        else:
+            qkv = torch.cat([get(pre + "q_proj", sh["q_proj"]), get(pre + "k_proj", sh["k_proj"]),
+                             get(pre + "v_proj", sh["v_proj"])], 0)
+            L = LayerWeights(
+                attn_norm=get(pre + "attn_norm", sh["attn_norm"]).float(),
+                ffn_norm=get(pre + "ffn_norm", sh["ffn_norm"]).float(),
+                qkv=_linear_weight(qkv, quant, device),
+                o=_linear_weight(get(pre + "o_proj", sh["o_proj"]), quant, device),
+            )
+            del qkv
         if cfg.qk_norm:
             L.q_norm = get(pre + "q_norm", sh["q_norm"]).float()
             L.k_norm = get(pre + "k_norm", sh["k_norm"]).float()
@@ -258,6 +297,11 @@ def prepare_weights(cfg: ModelConfig, device="cpu", seed: int = 0, quant: str | 
             L.experts_gu, L.experts_down = gu, dn
             if "router_bias" in sh:
                 L.router_bias = get(pre + "router_bias", sh["router_bias"]).float()
+            if cfg.n_shared_experts:
+                sgu = ops.interleave_gate_up(get(pre + "shared.gate", sh["shared.gate"]),
+                                             get(pre + "shared.up", sh["shared.up"]))
+                L.shared_gu = _linear_weight(sgu, quant, device)
+                L.shared_down = _linear_weight(get(pre + "shared.down", sh["shared.down"]), quant, device)
         else:
             gu = ops.interleave_gate_up(get(pre + "gate", sh["gate"]), get(pre + "up", sh["up"]))
             L.gate_up = _linear_weight(gu, quant, device)
@@ -267,6 +311,9 @@ def prepare_weights(cfg: ModelConfig, device="cpu", seed: int = 0, quant: str | 
     for i, L in enumerate(mw.layers):
         if L.is_moe and i + 1 < cfg.n_layers and mw.layers[i + 1].is_moe:
             L.router_cat = torch.cat([L.router, mw.layers[i + 1].router], 0).contiguous()
-    cos, sin = rope_table(cfg.head_dim, cfg.rope_theta, max_pos, device)
+    if cfg.n_mtp:
+        base = state_dict if state_dict is not None else _LazyState(cfg, seed, gen_dev)
+        mw.mtp = _prepare_mtp(cfg, get, quant, device, base, seed, expert_range)
+    cos, sin = rope_table(cfg.qk_rope_dim if cfg.is_mla else cfg.head_dim, cfg.rope_theta, max_pos, device)
     mw.rope_cos, mw.rope_sin = cos.contiguous(), sin.contiguous()
     return mw

@@ -103,7 +103,7 @@ class EPGroup:
         return int(self.status.item()) if self.fused else 0
 
     # ------------------------------------------------------------------ NCCL baseline
-    def moe_baseline(self, h, topk_ids, topk_w, gu, dn, eps_unused=None) -> torch.Tensor:
+    def moe_baseline(self, h, topk_ids, topk_w, gu, dn, eps_unused=None, staged=None) -> torch.Tensor:
         """Returns f32 [T, H] MoE output for the local rows via all-gather + local experts +
         reduce-scatter.  Row counts are equalised by padding to the max over ranks."""
         ctx = self.ctx
@@ -128,14 +128,16 @@ class EPGroup:
         all_gather_rows(ga, hp, ctx.group)
         all_gather_rows(gi, ip, ctx.group)
         all_gather_rows(gw, wp, ctx.group)
-        part = _local_experts_apply(ga, gi, gw, gu, dn, self.expert_range)
+        part = _local_experts_apply(ga, gi, gw, gu, dn, self.expert_range, staged)
         out = torch.empty(Tm, H, dtype=torch.float32, device=dev)
         reduce_scatter_rows(out, part, ctx.group)
         return out[:T]
 
 
-def _local_experts_apply(rows, ids, w, gu, dn, erange) -> torch.Tensor:
-    """f32 [R, H]: sum over each row's experts that fall in erange (ascending expert order)."""
+def _local_experts_apply(rows, ids, w, gu, dn, erange, staged=None) -> torch.Tensor:
+    """f32 [R, H]: sum over each row's experts that fall in erange (ascending expert order).
+    staged: ((gu_qw_ptrs, gu_sm_ptrs), (dn_qw_ptrs, dn_sm_ptrs)) with every expert in VRAM
+    (the expert cache's staging bank) for the prefill GEMMs."""
     R, H = rows.shape[0], dn.N
     dev = rows.device
     ea, eb = erange
@@ -160,15 +162,17 @@ def _local_experts_apply(rows, ids, w, gu, dn, erange) -> torch.Tensor:
     tok_idx = tok.int().contiguous()
     P = sel.numel()
     f = gu.N // 2
-    if rows.is_cuda and gu.qw is not None and P > 256 and gu.N % 128 == 0 and dn.N % 128 == 0:
+    bk = getattr(gu, "bank_contiguous", False)
+    if rows.is_cuda and gu.qw is not None and P > 256 and gu.N % 128 == 0 and dn.N % 128 == 0 and \
+            (bk or staged is not None):
         # prefill-sized: gather rows per expert, then grouped tcgen05 GEMMs
+        (gq, gs), (dq, ds) = staged if staged is not None else ((gu.qw_ptrs, gu.sm_ptrs), (dn.qw_ptrs, dn.sm_ptrs))
         a_rows = rows.index_select(0, tok.long()).contiguous()
         mid = torch.empty(P, f, dtype=rows.dtype, device=dev)
-        bk = getattr(gu, "bank_contiguous", False)
-        ops.gemm_grouped(a_rows, gu.qw_ptrs, gu.sm_ptrs, tok_off, gu.N, gu.K, 1, None, mid, eb - ea,
+        ops.gemm_grouped(a_rows, gq, gs, tok_off, gu.N, gu.K, 1, None, mid, eb - ea,
                          gu.qw if bk else None, gu.sm if bk else None)
         yp = torch.empty(P, H, dtype=torch.float32, device=dev)
-        ops.gemm_grouped(mid, dn.qw_ptrs, dn.sm_ptrs, tok_off, dn.N, dn.K, 2, pw, yp, eb - ea,
+        ops.gemm_grouped(mid, dq, ds, tok_off, dn.N, dn.K, 2, pw, yp, eb - ea,
                          dn.qw if bk else None, dn.sm if bk else None)
     elif rows.is_cuda and gu.qw is not None and int(counts.max()) <= 256:
         mid = torch.empty(P, f, dtype=rows.dtype, device=dev)

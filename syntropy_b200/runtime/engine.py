@@ -39,6 +39,7 @@ class Sequence:
     blocks: list = field(default_factory=list)
     status: str = "waiting"  # waiting | running | finished
     cached_tokens: int = 0   # prompt tokens served from the prefix cache
+    mtp_draft: list | None = None
     finish_reason: str | None = None
     seed: int = 0
     stream: int = 0
@@ -196,6 +197,8 @@ class LLMEngine:
             s.status = "running"
             self.running.append(s)
             outs.append(self._append(s, t))
+        if self.spec is not None and hasattr(self.spec.drafter, "after_prefill"):
+            self.spec.drafter.after_prefill(batch, self.runner._prefill_x, cu)
         self._reap()
         return outs
 
@@ -228,9 +231,12 @@ class LLMEngine:
         rows = len(seqs) * (g + 1)
         d = r.desc.h
         drafts = []
+        mtp = hasattr(self.spec.drafter, "after_verify")
         for i, s in enumerate(seqs):
-            hist = s.prompt + s.output
-            dr = self.spec.drafter.propose(hist, g)
+            if mtp:
+                dr = (s.mtp_draft or [s.output[-1]])[:g]
+            else:
+                dr = self.spec.drafter.propose(s.prompt + s.output, g)
             drafts.append(dr)
             p = s.n_tokens - 1
             kv.ensure(s.blocks, p + g + 1)
@@ -263,9 +269,13 @@ class LLMEngine:
         toks, nacc = verify(logits, torch.tensor(drafts, dtype=torch.int32), temp, topk, topp, seed, stream, ctr)
         self.stats["decode_steps"] += 1
         outs = []
+        mtp_items = []
         for i, s in enumerate(seqs):
             s.rng_counter = int(ctr[i])
             n = int(nacc[i])
+            if mtp:
+                row = i * (g + 1) + n
+                mtp_items.append((s, r.buf["x"][row].clone(), int(d["pos"][row])))
             self.stats["spec_drafted"] += g
             self.stats["spec_accepted"] += n
             new = toks[i, : n + 1].tolist()
@@ -277,6 +287,8 @@ class LLMEngine:
                     break
             self.stats["decode_tokens"] += len(emitted)
             outs.append(StepOutput(s.seq_id, emitted, s.status == "finished", s.finish_reason))
+        if mtp:
+            self.spec.drafter.after_verify(mtp_items)
         self._reap()
         return outs
 

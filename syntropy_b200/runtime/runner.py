@@ -77,6 +77,7 @@ class ModelRunner:
                  kv_dtype=None, use_graphs: bool = True, kv_budget_bytes: int | None = None, ep=None, tp=None):
         cfg = mw.cfg
         self.ep = ep  # parallel.ep.EPGroup or None
+        self.expert_cache = None  # experts.cache.ExpertCache when a VRAM cap is set
         self.tp = tp  # parallel.tp.TPGroup or None
         self.mw, self.cfg = mw, cfg
         self.device = mw.device
@@ -86,15 +87,18 @@ class ModelRunner:
         self.block_size = 16
         self.max_blocks = (max_seq_len + self.block_size - 1) // self.block_size
         kv_dtype = kv_dtype or (torch.bfloat16 if self.is_cuda else torch.float32)
+        self.is_mla = cfg.is_mla
+        kv_layers = cfg.n_layers + (cfg.n_mtp if mw.mtp is not None else 0)
+        kv_heads, kv_dim = (1, cfg.kv_lora_rank + cfg.qk_rope_dim) if cfg.is_mla else (cfg.n_kv_heads, cfg.head_dim)
         if num_blocks is None:
-            per = PagedKVCache.bytes_per_block(cfg.n_layers, cfg.n_kv_heads, cfg.head_dim, self.block_size,
+            per = PagedKVCache.bytes_per_block(kv_layers, kv_heads, kv_dim, self.block_size,
                                                torch.tensor([], dtype=kv_dtype).element_size())
             if kv_budget_bytes is None:
                 num_blocks = max_batch * self.max_blocks + 1
             else:
                 num_blocks = max(2, kv_budget_bytes // per)
-        self.kv = PagedKVCache(cfg.n_layers, num_blocks, cfg.n_kv_heads, cfg.head_dim, self.block_size, kv_dtype,
-                               self.device)
+        self.kv = PagedKVCache(kv_layers, num_blocks, kv_heads, kv_dim, self.block_size, kv_dtype, self.device,
+                               with_v=not cfg.is_mla)
         self.desc = StepDesc(max_batch, self.max_blocks, self.device)
         self.use_graphs = use_graphs and self.is_cuda
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
@@ -111,9 +115,12 @@ class ModelRunner:
         b = {}
         b["x"] = torch.zeros(B, H, dtype=torch.float32, device=dev)
         b["h"] = torch.zeros(B, H, dtype=act, device=dev)
-        b["qkv"] = torch.zeros(B, qkv_dim, dtype=act, device=dev)
-        b["q"] = torch.zeros(B, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
-        b["attn"] = torch.zeros(B, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
+        if cfg.is_mla:
+            b["attn"] = torch.zeros(B, cfg.n_heads, cfg.v_head_dim, dtype=act, device=dev)
+        else:
+            b["qkv"] = torch.zeros(B, qkv_dim, dtype=act, device=dev)
+            b["q"] = torch.zeros(B, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
+            b["attn"] = torch.zeros(B, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
         b["logits"] = torch.zeros(B, cfg.vocab, dtype=torch.float32, device=dev)
         b["next"] = torch.zeros(B, dtype=torch.int32, device=dev)
         if any(not L.is_moe for L in self.mw.layers):
@@ -143,7 +150,7 @@ class ModelRunner:
         # split-KV workspace sized for the largest split count
         self.pages_per_split = 16
         n_splits = (self.max_blocks + self.pages_per_split - 1) // self.pages_per_split
-        if self.is_cuda:
+        if self.is_cuda and not cfg.is_mla:
             b["part_o"] = torch.zeros(B * cfg.n_kv_heads * n_splits * 16 * cfg.head_dim, dtype=torch.float32,
                                       device=dev)
             b["part_ml"] = torch.zeros(B * cfg.n_kv_heads * n_splits * 16 * 2, dtype=torch.float32, device=dev)
@@ -191,7 +198,30 @@ class ModelRunner:
                    d["counter"][:B], b["next"][:B])
         return logits
 
+    def _attention_decode_mla(self, L, B, i):
+        """MLA decode for B rows (absorbed form over the paged latent cache)."""
+        from ..models.mla import mla_attend, mla_qkv
+        cfg, b, d = self.cfg, self.buf, self.desc.d
+        h = b["h"][:B]
+        pos = d["pos"][:B]
+        q_lat, q_pe, lat = mla_qkv(cfg, L.mla, h, pos, self.mw.rope_cos, self.mw.rope_sin)
+        cache = self.kv.k[i].view(-1, self.kv.k[i].shape[-1])
+        sl = d["slot"][:B]
+        ok = sl >= 0
+        cache[sl[ok].long()] = lat[ok].to(cache.dtype)
+        out = b["attn"][:B].view(B, -1)
+        bs = self.block_size
+        for r in range(B):
+            n = int(d["ctx_len"][r])
+            blocks = d["block_tables"][r, : (n + bs - 1) // bs]
+            p_ = torch.arange(n, device=h.device)
+            rows = cache[blocks[p_ // bs].long() * bs + p_ % bs]
+            out[r] = mla_attend(cfg, L.mla, q_lat[r:r + 1], q_pe[r:r + 1], rows, 0)[0].to(out.dtype)
+        ops.linear(out, L.o, b["x"][:B], ops.GEMV_ADD_F32)
+
     def _attention_decode(self, L, B, i):
+        if self.is_mla:
+            return self._attention_decode_mla(L, B, i)
         cfg, b, d = self.cfg, self.buf, self.desc.d
         h = b["h"][:B]
         qkv = b["qkv"][:B]
@@ -232,11 +262,22 @@ class ModelRunner:
             return
         mid = b["moe_mid"][:B * k]
         yp = b["moe_out"][:B * k]
+        shared = self._shared_expert(L, h) if L.shared_gu is not None else None
         ops.linear_grouped(h, gu, mb["tok_off"], mb["tok_idx"], mid, ops.GEMV_SWIGLU,
                            qw_ptrs=gu.qw_ptrs, sm_ptrs=gu.sm_ptrs)
         ops.linear_grouped(mid, dn, mb["tok_off"], None, yp, ops.GEMV_SCALED_F32, route_w=mb["pair_w"],
                            qw_ptrs=dn.qw_ptrs, sm_ptrs=dn.sm_ptrs)
-        ops.moe_combine_rmsnorm(x, yp, mb["pair_of"], None, nw, h, cfg.rms_eps)
+        ops.moe_combine_rmsnorm(x, yp, mb["pair_of"], shared, nw, h, cfg.rms_eps)
+
+    def _shared_expert(self, L, h):
+        """Shared-expert FFN output (f32 [T, H]) added to the routed combine."""
+        T = h.shape[0]
+        mid = torch.empty(T, L.shared_gu.N // 2 if hasattr(L.shared_gu, "N") else L.shared_gu.shape[0] // 2,
+                          dtype=h.dtype, device=h.device)
+        ops.linear(h, L.shared_gu, mid, ops.GEMV_SWIGLU)
+        out = torch.zeros(T, self.cfg.hidden, dtype=torch.float32, device=h.device)
+        ops.linear(mid, L.shared_down, out, ops.GEMV_ADD_F32)
+        return out
 
     def _moe_decode_baseline(self, L, B, nw):
         """NCCL baseline: all-gather rows, route all rows, apply local experts, reduce-scatter."""
@@ -343,11 +384,23 @@ class ModelRunner:
         x = torch.empty(T, cfg.hidden, dtype=torch.float32, device=dev)
         ops.embed(mw.embed, tokens, x)
         h = torch.empty(T, cfg.hidden, dtype=act, device=dev)
-        qkv = torch.empty(T, cfg.q_dim + 2 * cfg.kv_dim, dtype=act, device=dev)
-        q = torch.empty(T, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
-        attn = torch.empty(T, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
+        if not self.is_mla:
+            qkv = torch.empty(T, cfg.q_dim + 2 * cfg.kv_dim, dtype=act, device=dev)
+            q = torch.empty(T, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
+            attn = torch.empty(T, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
+        self._prefill_x = x
         for i, L in enumerate(mw.layers):
             ops.rms_norm(x, L.attn_norm, cfg.rms_eps, out=h)
+            if self.is_mla:
+                self._prefill_mla(L, i, h, x, positions, slots, cu_seqlens, prefix)
+                ops.rms_norm(x, L.ffn_norm, cfg.rms_eps, out=h)
+                if L.is_moe:
+                    self._moe_prefill(L, h, x)
+                else:
+                    mid = torch.empty(T, cfg.ffn, dtype=act, device=dev)
+                    ops.linear(h, L.gate_up, mid, ops.GEMV_SWIGLU)
+                    self._row_parallel(mid, L.down, x)
+                continue
             ops.linear(h, L.qkv, qkv, ops.GEMV_STORE)
             ops.qk_rope_kv_write(qkv, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, L.q_norm, L.k_norm, cfg.rms_eps,
                                  positions, mw.rope_cos, mw.rope_sin, slots, q, self.kv.k[i], self.kv.v[i])
@@ -372,6 +425,76 @@ class ModelRunner:
         logits = torch.empty(last.numel(), cfg.vocab, dtype=torch.float32, device=dev)
         ops.linear(hl, mw.lm_head, logits, ops.GEMV_STORE)
         return logits
+
+    def _prefill_mla(self, L, i, h, x, positions, slots, cu_seqlens, prefix):
+        from ..models.mla import mla_attend, mla_qkv
+        cfg = self.cfg
+        q_lat, q_pe, lat = mla_qkv(cfg, L.mla, h, positions, self.mw.rope_cos, self.mw.rope_sin)
+        cache = self.kv.k[i].view(-1, self.kv.k[i].shape[-1])
+        ok = slots >= 0
+        cache[slots[ok].long()] = lat[ok].to(cache.dtype)
+        T = h.shape[0]
+        out = torch.empty(T, cfg.n_heads * cfg.v_head_dim, dtype=h.dtype, device=h.device)
+        bs = self.block_size
+        for s_idx in range(len(cu_seqlens) - 1):
+            a, b = cu_seqlens[s_idx], cu_seqlens[s_idx + 1]
+            start = prefix[s_idx][1] if prefix else 0
+            if start:
+                blocks = torch.tensor(prefix[s_idx][0], device=h.device)
+                p_ = torch.arange(start + b - a, device=h.device)
+                rows = cache[blocks[p_ // bs].long() * bs + p_ % bs]
+            else:
+                rows = cache[slots[a:b].long()]
+            out[a:b] = mla_attend(cfg, L.mla, q_lat[a:b], q_pe[a:b], rows, 0, causal_from=start).to(out.dtype)
+        self._row_parallel(out, L.o, x)
+
+    # ------------------------------------------------------------------ MTP drafting
+    @torch.no_grad()
+    def mtp_forward(self, x_prev: torch.Tensor, tokens: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
+                    block_tables: list) -> torch.Tensor:
+        """One MTP-head step for S rows: from the main model's final residual at position j-1
+        and the token at position j, write the MTP block's latent KV at j and return the
+        argmax draft for position j+1."""
+        from ..models.mla import mla_attend, mla_qkv
+        cfg, mw, m = self.cfg, self.mw, self.mw.mtp
+        dev = self.device
+        S = x_prev.shape[0]
+        act = torch.bfloat16 if self.is_cuda else torch.float32
+        e = torch.empty(S, cfg.hidden, dtype=torch.float32, device=dev)
+        ops.embed(mw.embed, tokens.to(dev, torch.int32), e)
+        en = ops.rms_norm(e, m["enorm"], cfg.rms_eps)
+        hn = ops.rms_norm(x_prev.to(dev), m["hnorm"], cfg.rms_eps)
+        cat = torch.cat([en.to(act), hn.to(act)], -1).contiguous()
+        x = torch.zeros(S, cfg.hidden, dtype=torch.float32, device=dev)
+        ops.linear(cat, m["proj"], x, ops.GEMV_ADD_F32)
+        L = m["block"]
+        li = cfg.n_layers  # the MTP block's cache layer
+        h = ops.rms_norm(x, L.attn_norm, cfg.rms_eps).to(act)
+        pos = positions.to(dev)
+        q_lat, q_pe, lat = mla_qkv(cfg, L.mla, h, pos, mw.rope_cos, mw.rope_sin)
+        cache = self.kv.k[li].view(-1, self.kv.k[li].shape[-1])
+        sl = slots.to(dev)
+        cache[sl.long()] = lat.to(cache.dtype)
+        out = torch.empty(S, cfg.n_heads * cfg.v_head_dim, dtype=act, device=dev)
+        bs = self.block_size
+        for r in range(S):
+            n = int(positions[r]) + 1
+            blocks = torch.tensor(block_tables[r][: (n + bs - 1) // bs], device=dev)
+            p_ = torch.arange(n, device=dev)
+            rows = cache[blocks[p_ // bs].long() * bs + p_ % bs]
+            out[r] = mla_attend(cfg, L.mla, q_lat[r:r + 1], q_pe[r:r + 1], rows, 0)[0].to(act)
+        ops.linear(out, L.o, x, ops.GEMV_ADD_F32)
+        h = ops.rms_norm(x, L.ffn_norm, cfg.rms_eps).to(act)
+        if L.is_moe:
+            self._moe_prefill(L, h.contiguous(), x)
+        else:
+            mid = torch.empty(S, cfg.ffn, dtype=act, device=dev)
+            ops.linear(h, L.gate_up, mid, ops.GEMV_SWIGLU)
+            ops.linear(mid, L.down, x, ops.GEMV_ADD_F32)
+        hl = ops.rms_norm(x, mw.final_norm, cfg.rms_eps).to(act)
+        logits = torch.empty(S, cfg.vocab, dtype=torch.float32, device=dev)
+        ops.linear(hl.contiguous(), mw.lm_head, logits, ops.GEMV_STORE)
+        return torch.argmax(logits, -1).to(torch.int32).cpu()
 
     def _prefill_attn_with_prefix(self, i, q, attn, cu_seqlens, prefix):
         """Prefill attention for chunks that continue a cached prefix: queries are the new
@@ -433,11 +556,14 @@ class ModelRunner:
             logits = h.float() @ L.router.float().t()
             _route_torch(logits, cfg, L.router_bias, mb)
         gu, dn = L.experts_gu, L.experts_down
+        if L.shared_gu is not None and T > 0:
+            x.add_(self._shared_expert(L, h))
+        staged = self.expert_cache.staged_ptrs(L) if self.expert_cache is not None else None
         if self.ep is not None:
-            x.add_(self.ep.moe_baseline(h, mb["topk_ids"], mb["topk_w"], gu, dn))
+            x.add_(self.ep.moe_baseline(h, mb["topk_ids"], mb["topk_w"], gu, dn, staged=staged))
             return
         from ..parallel.ep import _local_experts_apply
-        x.add_(_local_experts_apply(h, mb["topk_ids"], mb["topk_w"], gu, dn, (0, E)))
+        x.add_(_local_experts_apply(h, mb["topk_ids"], mb["topk_w"], gu, dn, (gu.e0, gu.e0 + gu.E), staged))
 
 
 _OFF1: dict = {}

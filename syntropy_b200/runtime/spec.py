@@ -36,6 +36,51 @@ class NgramDrafter:
         return [history[-1]] * g
 
 
+class MTPDrafter:
+    """Drafts with the model's multi-token-prediction head (DeepSeek-V3 style): one token per
+    step from the final residual of the last accepted position and the token after it.  The
+    engine calls `after_prefill` and `after_verify` to keep the MTP block's KV and the next
+    draft per sequence."""
+    gamma_max = 1
+
+    def __init__(self, runner):
+        self.runner = runner
+
+    def _run(self, rows):
+        if not rows:
+            return
+        kv = self.runner.kv
+        xs = torch.stack([r[1] for r in rows])
+        toks = torch.tensor([r[2] for r in rows], dtype=torch.int32)
+        pos = torch.tensor([r[3] for r in rows], dtype=torch.int64)
+        for s, _, _, p in rows:
+            kv.ensure(s.blocks, p + 2)
+        slots = torch.tensor([kv.slot(s.blocks, p) for s, _, _, p in rows], dtype=torch.int64)
+        drafts = self.runner.mtp_forward(xs, toks, pos, slots, [list(s.blocks) for s, _, _, _ in rows])
+        for (s, _, _, _), d in zip(rows, drafts.tolist()):
+            if s.mtp_draft is not None:
+                s.mtp_draft = [d]
+
+    def after_prefill(self, seqs, x_rows, cu):
+        rows_fill = []
+        for i, s in enumerate(seqs):
+            s.mtp_draft = []
+            a, b = cu[i], cu[i + 1]
+            st = s.cached_tokens
+            # MTP KV for prompt positions st+1..P-1 from (x_{j-1}, t_j), then the first draft
+            for j in range(max(1, st + 1), len(s.prompt)):
+                rows_fill.append((s, x_rows[a + j - 1 - st], s.prompt[j], j))
+            rows_fill.append((s, x_rows[b - 1], s.output[-1], len(s.prompt)))
+        self._run(rows_fill)
+
+    def after_verify(self, items):
+        """items: (seq, final residual of the last accepted row, its position)."""
+        self._run([(s, x, s.output[-1], p + 1) for s, x, p in items if s.status != "finished"])
+
+    def propose(self, history, g):
+        raise RuntimeError("MTPDrafter drafts per sequence state")
+
+
 @dataclass
 class SpecConfig:
     gamma: int = 2
@@ -44,6 +89,8 @@ class SpecConfig:
     def __post_init__(self):
         if self.drafter is None:
             self.drafter = NgramDrafter()
+        if isinstance(self.drafter, MTPDrafter):
+            self.gamma = 1
 
 
 def verify(logits, drafts, temperature, top_k, top_p, seed, stream, counter):
