@@ -13,6 +13,7 @@ void register_all(pybind11::module& m) {
   m.def("q4t_dequant", &q4t_dequant);
   m.def("q4_gemv", &q4_gemv);
   m.def("block_sums", &block_sums);
+  m.def("q4_gemv_dense", &q4_gemv_dense);
   m.def("rmsnorm", &rmsnorm);
   m.def("moe_combine_rmsnorm", &moe_combine_rmsnorm);
   m.def("qk_rope_kv_write", &qk_rope_kv_write);

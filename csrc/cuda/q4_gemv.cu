@@ -745,6 +745,223 @@ static cudaError_t launch_v4(const GemvArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+
+// ---------------------------------------------------------------------------------------
+// v5 (dense layers, 9..64 tokens): CTA = 4 warps = 64 output rows x one K slice.  The
+// activations of the K slice are staged once per CTA in shared memory (cp.async) and shared
+// by the 4 warps (B fragments from shared memory, not L2); each warp issues all its packed-
+// weight loads for the slice up front.  K is split over gridDim.y CTAs; partial sums go to an
+// f32 workspace and the last CTA of a row block (arrival counter) adds them in slice order
+// (deterministic) and runs the epilogue.
+template <int NT, int GMAX>
+__global__ void __launch_bounds__(128) q4_gemv5_kernel(GemvArgs a, float* __restrict__ ws,
+                                                       unsigned* __restrict__ counters) {
+  extern __shared__ __align__(16) uint8_t gsm5[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int KG = a.K >> 6;
+  const int KS = gridDim.y;
+  const int KR = KG / KS;                 // groups per slice (host guarantees divisibility)
+  const int ks = blockIdx.y;
+  const int rb = blockIdx.x;
+  const int tile = rb * 4 + warp;         // 16-row tile of this warp
+  const int T = a.tok_off[1] - a.tok_off[0];
+  const int XS = KR * 64 + 8;             // smem row stride (elements), padded against conflicts
+  __nv_bfloat16* xs_sm = reinterpret_cast<__nv_bfloat16*>(gsm5);
+  __shared__ int s_last;
+  const uint4* qw = reinterpret_cast<const uint4*>(a.qw_ptrs[0]);
+  const uint2* smw = reinterpret_cast<const uint2*>(a.sm_ptrs[0]);
+  const bool active = tile < a.N / 16;
+  const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
+
+  for (int c0 = 0; c0 < T; c0 += NT * 8) {
+    const int ccount = min(T - c0, NT * 8);
+    const int ntc = (ccount + 7) >> 3;
+    // 1) weights of this warp's slice, all loads in flight at once
+    uint4 q[GMAX];
+    uint2 slo[GMAX], shi[GMAX];
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < GMAX; ++i) {
+        if (i < KR) {
+          const int64_t tk = (int64_t)tile * KG + ks * KR + i;
+          q[i] = __ldcs(qw + tk * 32 + lane);
+          slo[i] = __ldcs(smw + tk * 16 + g);
+          shi[i] = __ldcs(smw + tk * 16 + g + 8);
+        }
+      }
+    }
+    // 2) activations of the slice into shared memory (all tokens of the chunk)
+    __syncthreads();
+    const int chunks_per_row = KR * 8;  // 16-byte chunks
+    for (int idx = threadIdx.x; idx < ntc * 8 * chunks_per_row; idx += blockDim.x) {
+      const int j = idx / chunks_per_row, c = idx % chunks_per_row;
+      const int jj = min(j, ccount - 1);
+      const int row = a.tok_idx ? a.tok_idx[c0 + jj] : c0 + jj;
+      const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.x) +
+                                                        (int64_t)row * a.ldx + ks * KR * 64) + c;
+      const uint32_t dst = (uint32_t)__cvta_generic_to_shared(xs_sm + j * XS + c * 8);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src));
+    }
+    asm volatile("cp.async.commit_group;\n" ::);
+    asm volatile("cp.async.wait_group 0;\n" ::);
+    __syncthreads();
+    float acc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
+    if (active) {
+#pragma unroll
+      for (int i = 0; i < GMAX; ++i) {
+        if (i >= KR) break;
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          const uint32_t w0 = b ? q[i].z : q[i].x;
+          const uint32_t w1 = b ? q[i].w : q[i].y;
+          uint32_t af[2][4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            af[0][j] = lop3_and_or(w0 >> (4 * j), 0x000F000Fu, 0x43004300u);
+            af[1][j] = lop3_and_or(w1 >> (4 * j), 0x000F000Fu, 0x43004300u);
+          }
+          const uint32_t vlo = b ? slo[i].y : slo[i].x, vhi = b ? shi[i].y : shi[i].x;
+          const half2 hl = *reinterpret_cast<const half2*>(&vlo);
+          const half2 hh = *reinterpret_cast<const half2*>(&vhi);
+          const float dlo = __low2float(hl), dhi = __low2float(hh);
+          const float mlo = fmaf(-128.f, dlo, __high2float(hl)), mhi = fmaf(-128.f, dhi, __high2float(hh));
+          const int kl = i * 64 + b * 32 + 2 * t;  // local k inside the slice
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            if (nt < ntc) {
+              const __nv_bfloat16* xr = xs_sm + (nt * 8 + g) * XS + kl;
+              uint32_t bf[2][2];
+              bf[0][0] = *reinterpret_cast<const uint32_t*>(xr);
+              bf[0][1] = *reinterpret_cast<const uint32_t*>(xr + 8);
+              bf[1][0] = *reinterpret_cast<const uint32_t*>(xr + 16);
+              bf[1][1] = *reinterpret_cast<const uint32_t*>(xr + 24);
+              float xs[4] = {0.f, 0.f, 0.f, 0.f}, blk[4] = {0.f, 0.f, 0.f, 0.f};
+              mma_bf16_16816(xs, ones, bf[0], xs);
+              mma_bf16_16816(xs, ones, bf[1], xs);
+              mma_bf16_16816(blk, af[0], bf[0], blk);
+              mma_bf16_16816(blk, af[1], bf[1], blk);
+              acc[nt][0] += fmaf(dlo, blk[0], mlo * xs[0]);
+              acc[nt][1] += fmaf(dlo, blk[1], mlo * xs[1]);
+              acc[nt][2] += fmaf(dhi, blk[2], mhi * xs[2]);
+              acc[nt][3] += fmaf(dhi, blk[3], mhi * xs[3]);
+            }
+          }
+        }
+      }
+    }
+    // 3) split-K partials -> workspace [ks][token][N]; the last slice CTA reduces in order
+    if (KS == 1) {
+      if (active) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const int j = nt * 8 + 2 * t + hf;
+            if (j >= ccount) continue;
+            const int p = c0 + j;
+            if (a.mode == GEMV_SWIGLU) {
+              reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)p * (a.N / 2) + tile * 8 + g] =
+                  f2bf(silu(acc[nt][hf]) * acc[nt][2 + hf]);
+            } else {
+              gemv_store(a, p, tile * 16 + g, acc[nt][hf]);
+              gemv_store(a, p, tile * 16 + g + 8, acc[nt][2 + hf]);
+            }
+          }
+      }
+      continue;
+    }
+    if (active) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int j = nt * 8 + 2 * t + hf;
+          if (j >= ccount) continue;
+          float* w = ws + ((int64_t)ks * NT * 8 + j) * a.N;
+          w[tile * 16 + g] = acc[nt][hf];
+          w[tile * 16 + g + 8] = acc[nt][2 + hf];
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned prev = atomicAdd(&counters[rb], 1u);
+      s_last = (prev == (unsigned)KS - 1);
+      if (s_last) counters[rb] = 0u;
+    }
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      // 64 rows x ccount tokens, summed over slices in order
+      for (int idx = threadIdx.x; idx < 64 * ccount; idx += blockDim.x) {
+        const int r = idx & 63, j = idx >> 6;
+        const int n = rb * 64 + r;
+        if (n >= a.N) continue;
+        float v = 0.f;
+        for (int s2 = 0; s2 < KS; ++s2) v += __ldcg(ws + ((int64_t)s2 * NT * 8 + j) * a.N + n);
+        const int p = c0 + j;
+        if (a.mode == GEMV_SWIGLU) {
+          // rows (16c + f) and (16c + 8 + f) pair up: handled by the even row of each pair
+          if ((r & 15) < 8) {
+            float u = 0.f;
+            for (int s2 = 0; s2 < KS; ++s2) u += __ldcg(ws + ((int64_t)s2 * NT * 8 + j) * a.N + n + 8);
+            reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)p * (a.N / 2) + (n >> 4) * 8 + (r & 7)] =
+                f2bf(silu(v) * u);
+          }
+        } else {
+          gemv_store(a, p, n, v);
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+template <int NT, int GMAX>
+static cudaError_t launch_v5(const GemvArgs& a, int ksplit, float* ws, unsigned* counters, cudaStream_t s) {
+  const int KG = a.K >> 6;
+  const int KR = KG / ksplit;
+  const size_t smem = (size_t)NT * 8 * (KR * 64 + 8) * 2;
+  static size_t set_for = 0;
+  if (smem > 48 * 1024 && smem > set_for) {
+    cudaError_t e = cudaFuncSetAttribute(q4_gemv5_kernel<NT, GMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    set_for = smem;
+  }
+  dim3 grid((unsigned)((a.N / 16 + 3) / 4), (unsigned)ksplit);
+  q4_gemv5_kernel<NT, GMAX><<<grid, 128, smem, s>>>(a, ws, counters);
+  return cudaGetLastError();
+}
+
+// Dense decode GEMV (one weight matrix, 9..64 rows of x).  ws: f32 workspace of
+// ksplit * NT * 8 * N floats; counters: N/64 zeroed unsigned ints (left zeroed on exit).
+cudaError_t launch_q4_gemv_dense(const GemvArgs& a, float* ws, unsigned* counters, size_t ws_floats,
+                                 cudaStream_t s) {
+  const int T = a.nt_hint * 8;
+  const int nt = T <= 16 ? 2 : 4;
+  const int KG = a.K >> 6;
+  // K slices of at most 8 groups (all of a warp's loads in flight at once), split further
+  // while the grid is below ~4 CTAs per SM
+  constexpr int GMAX = 8;
+  const int row_blocks = (a.N / 16 + 3) / 4;
+  int ksplit = 0;
+  for (int k = 1; k <= KG; ++k) {
+    if (KG % k || KG / k > GMAX) continue;
+    ksplit = k;
+    if ((long)row_blocks * k >= 148L * 4) break;
+  }
+  if (ksplit == 0) return cudaErrorInvalidValue;
+  if (ksplit > 1 && (size_t)ksplit * nt * 8 * a.N > ws_floats) return cudaErrorInvalidValue;
+  if (nt == 2) return launch_v5<2, GMAX>(a, ksplit, ws, counters, s);
+  return launch_v5<4, GMAX>(a, ksplit, ws, counters, s);
+}
+
 cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {
   // Tile shapes measured on B200 (kernel microbenchmarks at the Qwen3-235B decode shapes):
   //  * one token tile (MoE experts, token groups of dense layers): register pipeline, U=4,

@@ -80,6 +80,8 @@ cudaError_t launch_tp_reduce_norm(const EpArgs& a, int64_t off_recv, int64_t off
 cudaError_t launch_ep_combine(const EpArgs& a, float* x, const float* wn, void* hout, float eps, int T,
                               cudaStream_t s);
 cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s);
+cudaError_t launch_q4_gemv_dense(const GemvArgs& a, float* ws, unsigned* counters, size_t ws_floats,
+                                 cudaStream_t s);
 
 // ---- norms, RoPE, KV writes, embedding ----
 cudaError_t launch_rmsnorm(const void* x, bool x_bf16, const float* w, void* y, int T, int H, float eps,

@@ -536,4 +536,37 @@ void verify_accept(torch::Tensor logits, torch::Tensor draft, torch::Tensor temp
   SYN_CHECK_CUDA(launch_verify_accept(a, cur_stream()));
 }
 
+
+// Dense decode GEMV for 9..64 rows (split-K, activations staged per CTA).
+void q4_gemv_dense(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
+                   torch::Tensor out, int64_t N, int64_t K, int64_t mode, torch::Tensor ws, torch::Tensor counters) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x");
+  TORCH_CHECK(N % 64 == 0 && K % 64 == 0 && x.size(1) == K, "q4_gemv_dense shapes (N%64, K%64)");
+  TORCH_CHECK(x.size(0) <= 64, "q4_gemv_dense: at most 64 rows");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0 && (x.stride(0) * 2) % 16 == 0,
+              "x rows must be 16-byte aligned");
+  TORCH_CHECK(ws.is_cuda() && ws.scalar_type() == torch::kFloat32, "ws f32");
+  TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == torch::kInt32 && counters.numel() >= N / 64, "counters");
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.x = x.data_ptr();
+  a.qw_ptrs = qw_ptrs.data_ptr<int64_t>();
+  a.sm_ptrs = sm_ptrs.data_ptr<int64_t>();
+  a.tok_off = tok_off.data_ptr<int32_t>();
+  a.out = out.data_ptr();
+  a.N = (int)N;
+  a.K = (int)K;
+  a.ldx = (int)x.stride(0);
+  a.mode = (int)mode;
+  a.E = 1;
+  a.nt_hint = (int)((x.size(0) + 7) / 8);
+  if (mode == 0) TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.size(-1) == N, "out bf16 [T, N]");
+  if (mode == 1) TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.size(-1) == N / 2, "out bf16 [T, N/2]");
+  if (mode == 3 || mode == 5) TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.size(-1) == N, "out f32 [T, N]");
+  TORCH_CHECK(mode == 0 || mode == 1 || mode == 3 || mode == 5, "q4_gemv_dense: mode");
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_q4_gemv_dense(a, ws.data_ptr<float>(), reinterpret_cast<unsigned*>(counters.data_ptr()),
+                                      (size_t)ws.numel(), cur_stream()));
+}
+
 }  // namespace syn

@@ -96,6 +96,7 @@ class ModelWeights:
     rope_cos: torch.Tensor | None = None
     rope_sin: torch.Tensor | None = None
     mtp: object = None
+    layer_offset: int = 0
 
     def nbytes(self) -> int:
         tot = 0
@@ -195,7 +196,7 @@ def _linear_weight(w: torch.Tensor, quant: str, device):
 def prepare_weights(cfg: ModelConfig, device="cpu", seed: int = 0, quant: str | None = None,
                     state_dict: dict | None = None, max_pos: int = 8192,
                     expert_range: tuple[int, int] | None = None, dense_dtype=None,
-                    tp: tuple[int, int] | None = None) -> ModelWeights:
+                    tp: tuple[int, int] | None = None, layer_range: tuple[int, int] | None = None) -> ModelWeights:
     """Builds engine-ready weights from ``state_dict`` (canonical names) or synthetic ones
     generated directly on ``device``.  ``expert_range`` limits MoE experts to [a, b)
     (expert parallelism).  ``tp=(rank, size)`` keeps this rank's tensor-parallel shard
@@ -211,7 +212,7 @@ def prepare_weights(cfg: ModelConfig, device="cpu", seed: int = 0, quant: str | 
         sd_local = shard_state(cfg, full, tp[0], tp[1]) if not isinstance(full, _LazyState) else \
             _LazyShard(full, cfg, tp[0], tp[1])
         mw = prepare_weights(local_config(cfg, tp[1]), device, seed, quant, sd_local, max_pos, expert_range,
-                             dense_dtype, None)
+                             dense_dtype, None, layer_range)
         return mw
     quant = quant or cfg.weight_quant
     is_cuda = device.type == "cuda"
@@ -232,7 +233,9 @@ def prepare_weights(cfg: ModelConfig, device="cpu", seed: int = 0, quant: str | 
         lm_head=_linear_weight(emb if cfg.tie_embeddings else get("lm_head", shapes_g["lm_head"]), quant, device),
     )
     del emb
-    for i in range(cfg.n_layers):
+    la, lb = layer_range if layer_range is not None else (0, cfg.n_layers)
+    mw.layer_offset = la
+    for i in range(la, lb):
         pre = f"layers.{i}."
         sh = layer_shapes(cfg, i)
         if cfg.is_mla:
@@ -309,7 +312,7 @@ def prepare_weights(cfg: ModelConfig, device="cpu", seed: int = 0, quant: str | 
         mw.layers.append(L)
     # next-layer router rows appended for prediction (the last MoE layer predicts nothing)
     for i, L in enumerate(mw.layers):
-        if L.is_moe and i + 1 < cfg.n_layers and mw.layers[i + 1].is_moe:
+        if L.is_moe and i + 1 < len(mw.layers) and mw.layers[i + 1].is_moe:
             L.router_cat = torch.cat([L.router, mw.layers[i + 1].router], 0).contiguous()
     if cfg.n_mtp:
         base = state_dict if state_dict is not None else _LazyState(cfg, seed, gen_dev)

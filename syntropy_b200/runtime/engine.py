@@ -187,7 +187,18 @@ class LLMEngine:
             prefix.append((list(s.blocks), st))
         logits = self.runner.prefill(torch.tensor(toks), torch.tensor(pos), torch.tensor(slots), cu,
                                      prefix if any(p[1] for p in prefix) else None)
-        nxt = self._sample_rows(logits, batch)
+        pp = self.runner.pp
+        if pp is not None:
+            toks_t = torch.zeros(len(batch), dtype=torch.int32, device=self.runner.device)
+            if pp.last:
+                toks_t.copy_(torch.tensor(self._sample_rows(logits, batch), dtype=torch.int32))
+            else:
+                for s in batch:  # keep the draw counters in step with the sampling stage
+                    if s.params.temperature > 0:
+                        s.rng_counter += 1
+            nxt = pp.broadcast_tokens(toks_t).cpu().tolist()
+        else:
+            nxt = self._sample_rows(logits, batch)
         self.stats["prefill_steps"] += 1
         self.stats["prefill_tokens"] += cu[-1]
         now = time.perf_counter()

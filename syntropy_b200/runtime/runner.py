@@ -74,8 +74,10 @@ class StepDesc:
 
 class ModelRunner:
     def __init__(self, mw: ModelWeights, max_batch: int = 64, max_seq_len: int = 4096, num_blocks: int | None = None,
-                 kv_dtype=None, use_graphs: bool = True, kv_budget_bytes: int | None = None, ep=None, tp=None):
+                 kv_dtype=None, use_graphs: bool = True, kv_budget_bytes: int | None = None, ep=None, tp=None,
+                 pp=None):
         cfg = mw.cfg
+        self.pp = pp  # parallel.pp.PPGroup or None
         self.ep = ep  # parallel.ep.EPGroup or None
         self.expert_cache = None  # experts.cache.ExpertCache when a VRAM cap is set
         self.tp = tp  # parallel.tp.TPGroup or None
@@ -88,7 +90,7 @@ class ModelRunner:
         self.max_blocks = (max_seq_len + self.block_size - 1) // self.block_size
         kv_dtype = kv_dtype or (torch.bfloat16 if self.is_cuda else torch.float32)
         self.is_mla = cfg.is_mla
-        kv_layers = cfg.n_layers + (cfg.n_mtp if mw.mtp is not None else 0)
+        kv_layers = len(mw.layers) + (cfg.n_mtp if mw.mtp is not None else 0)
         kv_heads, kv_dim = (1, cfg.kv_lora_rank + cfg.qk_rope_dim) if cfg.is_mla else (cfg.n_kv_heads, cfg.head_dim)
         if num_blocks is None:
             per = PagedKVCache.bytes_per_block(kv_layers, kv_heads, kv_dim, self.block_size,
@@ -172,8 +174,12 @@ class ModelRunner:
             self.ep.step_begin()
         if self.tp is not None:
             self.tp.step_begin()
-        ops.embed(mw.embed, d["tokens"][:B], x)
-        n_layers = cfg.n_layers
+        pp = self.pp
+        if pp is None or pp.first:
+            ops.embed(mw.embed, d["tokens"][:B], x)
+        else:
+            pp.recv_hidden(x)
+        n_layers = len(mw.layers)
         first = mw.layers[0]
         ops.rms_norm(x, first.attn_norm, cfg.rms_eps, out=h)
         for i, L in enumerate(mw.layers):
@@ -193,9 +199,15 @@ class ModelRunner:
                     ops.linear(mid, L.down, x, ops.GEMV_ADD_F32)
                     ops.rms_norm(x, nw, cfg.rms_eps, out=h)
         logits = b["logits"][:B]
+        if pp is not None and not pp.last:
+            pp.send_hidden(x)
+            pp.broadcast_tokens(b["next"][:B])
+            return logits
         ops.linear(h, mw.lm_head, logits, ops.GEMV_STORE)
         ops.sample(logits, d["temperature"][:B], d["top_k"][:B], d["top_p"][:B], d["seed"][:B], d["stream"][:B],
                    d["counter"][:B], b["next"][:B])
+        if pp is not None:
+            pp.broadcast_tokens(b["next"][:B])
         return logits
 
     def _attention_decode_mla(self, L, B, i):
@@ -382,7 +394,11 @@ class ModelRunner:
         positions = positions.to(dev, torch.int32)
         slots = slots.to(dev, torch.int64)
         x = torch.empty(T, cfg.hidden, dtype=torch.float32, device=dev)
-        ops.embed(mw.embed, tokens, x)
+        pp = self.pp
+        if pp is None or pp.first:
+            ops.embed(mw.embed, tokens, x)
+        else:
+            pp.recv_hidden(x)
         h = torch.empty(T, cfg.hidden, dtype=act, device=dev)
         if not self.is_mla:
             qkv = torch.empty(T, cfg.q_dim + 2 * cfg.kv_dim, dtype=act, device=dev)
@@ -420,6 +436,9 @@ class ModelRunner:
                 self._row_parallel(mid, L.down, x)
         if len(cu_seqlens) == 1:
             return torch.zeros(0, cfg.vocab, dtype=torch.float32, device=dev)
+        if pp is not None and not pp.last:
+            pp.send_hidden(x)
+            return None  # the last stage produces the logits; tokens arrive by broadcast
         last = torch.tensor([c - 1 for c in cu_seqlens[1:]], device=dev, dtype=torch.long)
         hl = ops.rms_norm(x[last].contiguous(), mw.final_norm, cfg.rms_eps)
         logits = torch.empty(last.numel(), cfg.vocab, dtype=torch.float32, device=dev)
