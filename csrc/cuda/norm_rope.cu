@@ -8,6 +8,8 @@
 //  * qk_rope_kv_write: per-head RMSNorm of q and k (Qwen3 QK-norm), rotate-half RoPE from
 //    an f32 cos/sin table, q to a contiguous buffer and k/v into 16-token pages; the fused
 //    RmsNorm + Rope + KvWrite of the reference's design (RFC-0040 `KvWrite`, rope fused).
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace syn {
@@ -32,17 +34,19 @@ __global__ void rmsnorm_kernel(const TIn* __restrict__ x, const float* __restric
 cudaError_t launch_rmsnorm(const void* x, bool x_bf16, const float* w, void* y, int T, int H, float eps,
                            cudaStream_t s) {
   if (T == 0) return cudaSuccess;
+  const int threads = std::min(1024, std::max(128, ((H / 4 + 31) / 32) * 32));
   if (x_bf16)
-    rmsnorm_kernel<__nv_bfloat16><<<T, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), w,
+    rmsnorm_kernel<__nv_bfloat16><<<T, threads, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), w,
                                                       reinterpret_cast<__nv_bfloat16*>(y), H, eps);
   else
-    rmsnorm_kernel<float><<<T, 256, 0, s>>>(reinterpret_cast<const float*>(x), w,
+    rmsnorm_kernel<float><<<T, threads, 0, s>>>(reinterpret_cast<const float*>(x), w,
                                              reinterpret_cast<__nv_bfloat16*>(y), H, eps);
   return cudaGetLastError();
 }
 
 // x[t] += sum_j yp[pair_of[t][j]] (pair_of sorted by expert), then y = rmsnorm(x) * w.
-// If `shared` is given it is added first (shared-expert output, f32 [T, H]).
+// If `shared` is given it is added first (shared-expert output, f32 [T, H]).  One CTA of
+// H/4 threads per token, float4 accesses: every thread keeps top_k row loads in flight.
 __global__ void moe_combine_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ yp,
                                            const int32_t* __restrict__ pair_of, int top_k,
                                            const float* __restrict__ shared, const float* __restrict__ w,
@@ -51,13 +55,32 @@ __global__ void moe_combine_rmsnorm_kernel(float* __restrict__ x, const float* _
   const int64_t t = blockIdx.x;
   float* xr = x + t * H;
   float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    float acc = 0.f;
-    for (int j = 0; j < top_k; ++j) acc += yp[(int64_t)pair_of[t * top_k + j] * H + i];
-    if (shared) acc += shared[t * H + i];
-    const float v = xr[i] + acc;
-    xr[i] = v;
-    ss += v * v;
+  const bool vec = (H % 4) == 0;
+  if (vec) {
+    for (int i4 = threadIdx.x; i4 < H / 4; i4 += blockDim.x) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < top_k; ++j) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(yp + (int64_t)pair_of[t * top_k + j] * H) + i4);
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      }
+      if (shared) {
+        const float4 v = reinterpret_cast<const float4*>(shared + t * H)[i4];
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+      }
+      float4 xv = reinterpret_cast<float4*>(xr)[i4];
+      xv.x += acc.x; xv.y += acc.y; xv.z += acc.z; xv.w += acc.w;
+      reinterpret_cast<float4*>(xr)[i4] = xv;
+      ss += xv.x * xv.x + xv.y * xv.y + xv.z * xv.z + xv.w * xv.w;
+    }
+  } else {
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+      float acc = 0.f;
+      for (int j = 0; j < top_k; ++j) acc += yp[(int64_t)pair_of[t * top_k + j] * H + i];
+      if (shared) acc += shared[t * H + i];
+      const float v = xr[i] + acc;
+      xr[i] = v;
+      ss += v * v;
+    }
   }
   if (w == nullptr) return;
   ss = block_sum(ss, red);
@@ -69,8 +92,9 @@ cudaError_t launch_moe_combine_rmsnorm(float* x, const float* yp, const int32_t*
                                        const float* shared, const float* w, void* y, int T, int H, float eps,
                                        cudaStream_t s) {
   if (T == 0) return cudaSuccess;
-  moe_combine_rmsnorm_kernel<<<T, 256, 0, s>>>(x, yp, pair_of, top_k, shared, w,
-                                               reinterpret_cast<__nv_bfloat16*>(y), H, eps);
+  const int threads = H % 4 == 0 ? std::min(1024, std::max(128, ((H / 4 + 31) / 32) * 32)) : 256;
+  moe_combine_rmsnorm_kernel<<<T, threads, 0, s>>>(x, yp, pair_of, top_k, shared, w,
+                                                   reinterpret_cast<__nv_bfloat16*>(y), H, eps);
   return cudaGetLastError();
 }
 
