@@ -70,7 +70,7 @@ __device__ __forceinline__ void gemv_store(const GemvArgs& a, int p, int n, floa
 // 4-warp CTA is an independent tile, no shared memory).  U k-groups (64 columns each) of
 // weights and scales are loaded before any of them is used, so each warp keeps
 // U * R * 528 bytes in flight.
-template <int R, int NT, int KS, int U = 4, int MINB = 1>
+template <int R, int NT, int KS, int U = 4, int MINB = 1, bool PIPE = false>
 __global__ void __launch_bounds__(KS == 1 ? 128 : KS * 32, MINB)
 q4_gemv2_kernel(GemvArgs a) {
   constexpr int WARPS = KS == 1 ? 4 : KS;
@@ -113,21 +113,34 @@ q4_gemv2_kernel(GemvArgs a) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) acc[r][nt][i] = 0.f;
 
-      for (int kb = kw; kb < KG; kb += KS * U) {
-        uint4 q[U][R];
-        uint2 slo[U][R], shi[U][R];
+      uint4 q[U][R];
+      uint2 slo[U][R], shi[U][R];
+      auto load_batch = [&](int kb0, uint4 (&qq)[U][R], uint2 (&sl)[U][R], uint2 (&sh)[U][R]) {
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-          const int kg = kb + u * KS;
+          const int kg = kb0 + u * KS;
           if (kg < KG) {
 #pragma unroll
             for (int r = 0; r < R; ++r) {
               const int64_t tk = (int64_t)(unit * R + r) * KG + kg;
-              q[u][r] = ld_stream_v4(qw + tk * 32 + lane);
-              slo[u][r] = ld_stream_v2(sm + tk * 16 + g);
-              shi[u][r] = ld_stream_v2(sm + tk * 16 + g + 8);
+              qq[u][r] = ld_stream_v4(qw + tk * 32 + lane);
+              sl[u][r] = ld_stream_v2(sm + tk * 16 + g);
+              sh[u][r] = ld_stream_v2(sm + tk * 16 + g + 8);
             }
           }
+        }
+      };
+      if (PIPE) load_batch(kw, q, slo, shi);
+      for (int kb = kw; kb < KG; kb += KS * U) {
+        uint4 qn[PIPE ? U : 1][R];
+        uint2 sln[PIPE ? U : 1][R], shn[PIPE ? U : 1][R];
+        if (PIPE) {
+          // the next batch streams in while this one is computed
+          if (kb + KS * U < KG)
+            load_batch(kb + KS * U, reinterpret_cast<uint4(&)[U][R]>(qn), reinterpret_cast<uint2(&)[U][R]>(sln),
+                       reinterpret_cast<uint2(&)[U][R]>(shn));
+        } else {
+          load_batch(kb, q, slo, shi);
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
@@ -183,6 +196,16 @@ q4_gemv2_kernel(GemvArgs a) {
               }
             }
           }
+        }
+        if (PIPE) {
+#pragma unroll
+          for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+              q[u][r] = reinterpret_cast<uint4(&)[U][R]>(qn)[u][r];
+              slo[u][r] = reinterpret_cast<uint2(&)[U][R]>(sln)[u][r];
+              shi[u][r] = reinterpret_cast<uint2(&)[U][R]>(shn)[u][r];
+            }
         }
       }
 
@@ -254,19 +277,19 @@ q4_gemv2_kernel(GemvArgs a) {
   }
 }
 
-template <int R, int NT, int KS, int U = 4, int MINB = 1>
+template <int R, int NT, int KS, int U = 4, int MINB = 1, bool PIPE = false>
 static cudaError_t launch_v2(const GemvArgs& a, cudaStream_t s) {
   constexpr int WARPS = KS == 1 ? 4 : KS;
   const int units = a.N / (16 * R);
   const int gx = KS == 1 ? (units + WARPS - 1) / WARPS : units;
   const size_t smem = KS > 1 ? (size_t)KS * R * NT * 4 * 32 * sizeof(float) : 0;
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(q4_gemv2_kernel<R, NT, KS, U, MINB>,
+    cudaError_t e = cudaFuncSetAttribute(q4_gemv2_kernel<R, NT, KS, U, MINB, PIPE>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
   dim3 grid((unsigned)gx, (unsigned)a.E);
-  q4_gemv2_kernel<R, NT, KS, U, MINB><<<grid, WARPS * 32, smem, s>>>(a);
+  q4_gemv2_kernel<R, NT, KS, U, MINB, PIPE><<<grid, WARPS * 32, smem, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -953,6 +976,7 @@ cudaError_t launch_q4_gemv_dense(const GemvArgs& a, float* ws, unsigned* counter
   int ksplit = 0;
   for (int k = 1; k <= KG; ++k) {
     if (KG % k || KG / k > GMAX) continue;
+    if (k > 1 && (size_t)k * nt * 8 * a.N > ws_floats) break;  // no deeper split than the workspace holds
     ksplit = k;
     if ((long)row_blocks * k >= 148L * 4) break;
   }
@@ -995,6 +1019,10 @@ cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {
       case 27: return launch_v2<1, 1, 8, 4, 1>(a, s);
       case 28: return launch_v2<1, 1, 4, 4, 2>(a, s);
       case 29: return launch_v2<1, 1, 2, 4, 4>(a, s);
+      case 31: return launch_v2<1, 1, 1, 4, 4, true>(a, s);
+      case 32: return launch_v2<1, 1, 1, 4, 5, true>(a, s);
+      case 33: return launch_v2<1, 1, 1, 2, 8, true>(a, s);
+      case 34: return launch_v2<1, 1, 1, 3, 6, true>(a, s);
       default: break;
     }
     const long units = (long)(a.N / 16) * a.E_active_hint;
