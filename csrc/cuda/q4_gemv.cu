@@ -70,7 +70,7 @@ __device__ __forceinline__ void gemv_store(const GemvArgs& a, int p, int n, floa
 // 4-warp CTA is an independent tile, no shared memory).  U k-groups (64 columns each) of
 // weights and scales are loaded before any of them is used, so each warp keeps
 // U * R * 528 bytes in flight.
-template <int R, int NT, int KS, int U = 4, int MINB = 1, bool PIPE = false>
+template <int R, int NT, int KS, int U = 4, int MINB = 1>
 __global__ void __launch_bounds__(KS == 1 ? 128 : KS * 32, MINB)
 q4_gemv2_kernel(GemvArgs a) {
   constexpr int WARPS = KS == 1 ? 4 : KS;
@@ -130,18 +130,8 @@ q4_gemv2_kernel(GemvArgs a) {
           }
         }
       };
-      if (PIPE) load_batch(kw, q, slo, shi);
       for (int kb = kw; kb < KG; kb += KS * U) {
-        uint4 qn[PIPE ? U : 1][R];
-        uint2 sln[PIPE ? U : 1][R], shn[PIPE ? U : 1][R];
-        if (PIPE) {
-          // the next batch streams in while this one is computed
-          if (kb + KS * U < KG)
-            load_batch(kb + KS * U, reinterpret_cast<uint4(&)[U][R]>(qn), reinterpret_cast<uint2(&)[U][R]>(sln),
-                       reinterpret_cast<uint2(&)[U][R]>(shn));
-        } else {
-          load_batch(kb, q, slo, shi);
-        }
+        load_batch(kb, q, slo, shi);
 #pragma unroll
         for (int u = 0; u < U; ++u) {
           const int kg = kb + u * KS;
@@ -196,16 +186,6 @@ q4_gemv2_kernel(GemvArgs a) {
               }
             }
           }
-        }
-        if (PIPE) {
-#pragma unroll
-          for (int u = 0; u < U; ++u)
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-              q[u][r] = reinterpret_cast<uint4(&)[U][R]>(qn)[u][r];
-              slo[u][r] = reinterpret_cast<uint2(&)[U][R]>(sln)[u][r];
-              shi[u][r] = reinterpret_cast<uint2(&)[U][R]>(shn)[u][r];
-            }
         }
       }
 
@@ -277,19 +257,19 @@ q4_gemv2_kernel(GemvArgs a) {
   }
 }
 
-template <int R, int NT, int KS, int U = 4, int MINB = 1, bool PIPE = false>
+template <int R, int NT, int KS, int U = 4, int MINB = 1>
 static cudaError_t launch_v2(const GemvArgs& a, cudaStream_t s) {
   constexpr int WARPS = KS == 1 ? 4 : KS;
   const int units = a.N / (16 * R);
   const int gx = KS == 1 ? (units + WARPS - 1) / WARPS : units;
   const size_t smem = KS > 1 ? (size_t)KS * R * NT * 4 * 32 * sizeof(float) : 0;
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(q4_gemv2_kernel<R, NT, KS, U, MINB, PIPE>,
+    cudaError_t e = cudaFuncSetAttribute(q4_gemv2_kernel<R, NT, KS, U, MINB>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
   dim3 grid((unsigned)gx, (unsigned)a.E);
-  q4_gemv2_kernel<R, NT, KS, U, MINB, PIPE><<<grid, WARPS * 32, smem, s>>>(a);
+  q4_gemv2_kernel<R, NT, KS, U, MINB><<<grid, WARPS * 32, smem, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -777,7 +757,7 @@ static cudaError_t launch_v4(const GemvArgs& a, cudaStream_t s) {
 // f32 workspace and the last CTA of a row block (arrival counter) adds them in slice order
 // (deterministic) and runs the epilogue.
 template <int NT, int GMAX>
-__global__ void __launch_bounds__(128) q4_gemv5_kernel(GemvArgs a, float* __restrict__ ws,
+__global__ void __launch_bounds__(128, 1) q4_gemv5_kernel(GemvArgs a, float* __restrict__ ws,
                                                        unsigned* __restrict__ counters) {
   extern __shared__ __align__(16) uint8_t gsm5[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -797,8 +777,11 @@ __global__ void __launch_bounds__(128) q4_gemv5_kernel(GemvArgs a, float* __rest
   const bool active = tile < a.N / 16;
   const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
 
-  for (int c0 = 0; c0 < T; c0 += NT * 8) {
-    const int ccount = min(T - c0, NT * 8);
+  // one pass over at most NT*8 tokens (the launcher picks NT >= ceil(T/8)); a second pass in
+  // the same launch would race with the split-K reduction of the first on ws and counters
+  {
+    const int c0 = 0;
+    const int ccount = min(T, NT * 8);
     const int ntc = (ccount + 7) >> 3;
     // 1) weights of this warp's slice, all loads in flight at once
     uint4 q[GMAX];
@@ -896,7 +879,7 @@ __global__ void __launch_bounds__(128) q4_gemv5_kernel(GemvArgs a, float* __rest
             }
           }
       }
-      continue;
+      return;
     }
     if (active) {
 #pragma unroll
@@ -967,7 +950,8 @@ static cudaError_t launch_v5(const GemvArgs& a, int ksplit, float* ws, unsigned*
 cudaError_t launch_q4_gemv_dense(const GemvArgs& a, float* ws, unsigned* counters, size_t ws_floats,
                                  cudaStream_t s) {
   const int T = a.nt_hint * 8;
-  const int nt = T <= 16 ? 2 : 4;
+  if (T > 64) return cudaErrorInvalidValue;
+  const int nt = T <= 16 ? 2 : (T <= 32 ? 4 : 8);
   const int KG = a.K >> 6;
   // K slices of at most 8 groups (all of a warp's loads in flight at once), split further
   // while the grid is below ~4 CTAs per SM
@@ -983,7 +967,8 @@ cudaError_t launch_q4_gemv_dense(const GemvArgs& a, float* ws, unsigned* counter
   if (ksplit == 0) return cudaErrorInvalidValue;
   if (ksplit > 1 && (size_t)ksplit * nt * 8 * a.N > ws_floats) return cudaErrorInvalidValue;
   if (nt == 2) return launch_v5<2, GMAX>(a, ksplit, ws, counters, s);
-  return launch_v5<4, GMAX>(a, ksplit, ws, counters, s);
+  if (nt == 4) return launch_v5<4, GMAX>(a, ksplit, ws, counters, s);
+  return launch_v5<8, GMAX>(a, ksplit, ws, counters, s);
 }
 
 cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {
@@ -1019,10 +1004,6 @@ cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {
       case 27: return launch_v2<1, 1, 8, 4, 1>(a, s);
       case 28: return launch_v2<1, 1, 4, 4, 2>(a, s);
       case 29: return launch_v2<1, 1, 2, 4, 4>(a, s);
-      case 31: return launch_v2<1, 1, 1, 4, 4, true>(a, s);
-      case 32: return launch_v2<1, 1, 1, 4, 5, true>(a, s);
-      case 33: return launch_v2<1, 1, 1, 2, 8, true>(a, s);
-      case 34: return launch_v2<1, 1, 1, 3, 6, true>(a, s);
       default: break;
     }
     const long units = (long)(a.N / 16) * a.E_active_hint;
