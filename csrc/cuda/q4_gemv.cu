@@ -903,24 +903,46 @@ __global__ void __launch_bounds__(128, 1) q4_gemv5_kernel(GemvArgs a, float* __r
     __syncthreads();
     if (s_last) {
       __threadfence();
-      // 64 rows x ccount tokens, summed over slices in order
-      for (int idx = threadIdx.x; idx < 64 * ccount; idx += blockDim.x) {
-        const int r = idx & 63, j = idx >> 6;
-        const int n = rb * 64 + r;
-        if (n >= a.N) continue;
-        float v = 0.f;
-        for (int s2 = 0; s2 < KS; ++s2) v += __ldcg(ws + ((int64_t)s2 * NT * 8 + j) * a.N + n);
-        const int p = c0 + j;
-        if (a.mode == GEMV_SWIGLU) {
-          // rows (16c + f) and (16c + 8 + f) pair up: handled by the even row of each pair
-          if ((r & 15) < 8) {
-            float u = 0.f;
-            for (int s2 = 0; s2 < KS; ++s2) u += __ldcg(ws + ((int64_t)s2 * NT * 8 + j) * a.N + n + 8);
-            reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)p * (a.N / 2) + (n >> 4) * 8 + (r & 7)] =
-                f2bf(silu(v) * u);
+      // 64 rows x ccount tokens, summed over the slices in slice order (deterministic).  A
+      // thread owns 4 consecutive rows of one token (float4) and issues the loads of up to
+      // 8 slices before adding any: the reduction is bound by L2 latency, not bandwidth.
+      const bool glu = a.mode == GEMV_SWIGLU;
+      for (int idx = threadIdx.x; idx < 16 * ccount; idx += blockDim.x) {
+        const int c4 = idx & 15, j = idx >> 4;
+        if (glu && (c4 & 2)) continue;  // SwiGLU: rows 8..15 of a 16-row tile are the up halves
+        const int n = rb * 64 + c4 * 4;
+        const float* src = ws + (int64_t)j * a.N + n;
+        const int64_t sstride = (int64_t)NT * 8 * a.N;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f), u = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s0 = 0; s0 < KS; s0 += 8) {
+          float4 bv[8], bu[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if (s0 + i < KS) {
+              bv[i] = __ldcg(reinterpret_cast<const float4*>(src + (s0 + i) * sstride));
+              if (glu) bu[i] = __ldcg(reinterpret_cast<const float4*>(src + (s0 + i) * sstride + 8));
+            }
           }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if (s0 + i < KS) {
+              v.x += bv[i].x; v.y += bv[i].y; v.z += bv[i].z; v.w += bv[i].w;
+              if (glu) { u.x += bu[i].x; u.y += bu[i].y; u.z += bu[i].z; u.w += bu[i].w; }
+            }
+          }
+        }
+        const int p = c0 + j;
+        if (glu) {
+          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.out) + (int64_t)p * (a.N / 2) + (n >> 4) * 8 + (n & 7);
+          o[0] = f2bf(silu(v.x) * u.x);
+          o[1] = f2bf(silu(v.y) * u.y);
+          o[2] = f2bf(silu(v.z) * u.z);
+          o[3] = f2bf(silu(v.w) * u.w);
         } else {
-          gemv_store(a, p, n, v);
+          gemv_store(a, p, n, v.x);
+          gemv_store(a, p, n + 1, v.y);
+          gemv_store(a, p, n + 2, v.z);
+          gemv_store(a, p, n + 3, v.w);
         }
       }
     }

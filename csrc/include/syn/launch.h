@@ -120,8 +120,12 @@ struct TopkArgs {
   float* pair_w;         // [T*k]
   int32_t* pair_of;      // [T, k] pair index of each choice, choices sorted by expert
   int32_t* pred_mask;    // [E] 1 if any token is predicted to use expert e at the next layer
+  uint32_t* ws;          // zeroed workspace of TOPK_WS_WORDS words, left zeroed on exit
 };
+constexpr int TOPK_WS_WORDS = 512 * 8 + 16 + 1;
 cudaError_t launch_moe_topk(const TopkArgs& a, cudaStream_t s);
+// Any T (no next-layer prediction); ws: zeroed E * ceil(T/32) + E words (not restored).
+cudaError_t launch_moe_route_large(const TopkArgs& a, cudaStream_t s);
 
 // ---- sampling ----
 cudaError_t launch_argmax(const float* logits, int T, int V, int32_t* out, cudaStream_t s);

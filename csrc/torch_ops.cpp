@@ -241,9 +241,14 @@ void router_logits(torch::Tensor h, torch::Tensor W, torch::Tensor logits) {
 void moe_topk(torch::Tensor logits, torch::Tensor bias, int64_t E, int64_t k, int64_t scoring, int64_t n_groups,
               int64_t topk_groups, bool norm, double scaling, bool pred, torch::Tensor topk_ids, torch::Tensor topk_w,
               torch::Tensor tok_off, torch::Tensor tok_idx, torch::Tensor pair_w, torch::Tensor pair_of,
-              torch::Tensor pred_mask) {
+              torch::Tensor pred_mask, torch::Tensor ws) {
   SYN_CHECK_INPUT(logits);
   TORCH_CHECK(logits.scalar_type() == torch::kFloat32, "logits f32");
+  const bool large = logits.size(0) > 256;
+  const int64_t need = large ? E * ((logits.size(0) + 31) / 32) + E : TOPK_WS_WORDS;
+  TORCH_CHECK(ws.is_cuda() && ws.scalar_type() == torch::kInt32 && ws.numel() >= need,
+              "moe_topk workspace: zeroed int32 of at least ", need, " words");
+  TORCH_CHECK(!(large && pred), "moe_topk: next-layer prediction needs at most 256 tokens");
   const int64_t T = logits.size(0);
   TORCH_CHECK(logits.size(1) == (pred ? 2 * E : E), "logits width");
   TORCH_CHECK(topk_ids.numel() >= T * k && topk_w.numel() >= T * k && tok_idx.numel() >= T * k &&
@@ -268,8 +273,13 @@ void moe_topk(torch::Tensor logits, torch::Tensor bias, int64_t E, int64_t k, in
   a.pair_w = pair_w.data_ptr<float>();
   a.pair_of = pair_of.data_ptr<int32_t>();
   a.pred_mask = pred_mask.numel() ? pred_mask.data_ptr<int32_t>() : nullptr;
+  a.ws = reinterpret_cast<uint32_t*>(ws.data_ptr<int32_t>());
   const at::cuda::CUDAGuard guard(logits.device());
-  SYN_CHECK_CUDA(launch_moe_topk(a, cur_stream()));
+  if (large) {
+    SYN_CHECK_CUDA(launch_moe_route_large(a, cur_stream()));
+  } else {
+    SYN_CHECK_CUDA(launch_moe_topk(a, cur_stream()));
+  }
 }
 
 void argmax(torch::Tensor logits, torch::Tensor out) {

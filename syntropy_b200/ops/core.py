@@ -380,15 +380,32 @@ def router_logits(h, W, out):
     return out
 
 
+_TOPK_WS: dict = {}
+
+
+def _topk_workspace(dev) -> torch.Tensor:
+    """Zeroed int32 scratch of the routing kernel (token masks, prediction bits, arrival
+    counter); every launch leaves it zeroed again.  One per device, kept for the process."""
+    key = str(dev)
+    ws = _TOPK_WS.get(key)
+    if ws is None:
+        ws = torch.zeros(4160, dtype=torch.int32, device=dev)
+        _TOPK_WS[key] = ws
+    return ws
+
+
 def moe_topk(logits, cfg, bias, pred: bool, bufs: dict):
     """Top-k routing + CSR.  bufs: topk_ids, topk_w, tok_off, tok_idx, pair_w, pair_of, pred_mask."""
     E, k = cfg.n_experts, cfg.top_k
+    T = logits.shape[0]
     scoring = 0 if cfg.router_scoring == "softmax" else 1
     if logits.is_cuda:
         ext().moe_topk(logits, bias if bias is not None else _EMPTY_F32(logits.device), E, k, scoring, cfg.n_groups,
                        cfg.topk_groups, cfg.norm_topk_prob, cfg.routed_scaling, pred, bufs["topk_ids"],
                        bufs["topk_w"], bufs["tok_off"], bufs["tok_idx"], bufs["pair_w"], bufs["pair_of"],
-                       bufs["pred_mask"] if pred else _EMPTY_I32(logits.device))
+                       bufs["pred_mask"] if pred else _EMPTY_I32(logits.device),
+                       _topk_workspace(logits.device) if T <= 256 else
+                       torch.zeros(E * ((T + 31) // 32) + E, dtype=torch.int32, device=logits.device))
         _launched()
         return
     from ..models.reference import topk_stable
@@ -419,8 +436,6 @@ def moe_topk(logits, cfg, bias, pred: bool, bufs: dict):
     bufs["tok_off"][: E + 1] = off.int()
     fill = off[:-1].clone()
     pair_of = torch.empty(T, k, dtype=torch.int32)
-    for e in range(E):
-        pass
     for t in range(T):
         order = torch.argsort(ids[t])
         for slot, j in enumerate(order.tolist()):

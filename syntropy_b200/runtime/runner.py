@@ -567,9 +567,12 @@ class ModelRunner:
               "pair_of": torch.empty(T, k, dtype=torch.int32, device=dev), "pred_mask": None}
         if T == 0:
             pass
-        elif T <= 256 and self.is_cuda:
-            logits = torch.empty(T, E, dtype=torch.float32, device=dev)
-            ops.router_logits(h, L.router, logits)
+        elif self.is_cuda:
+            if T <= 256:
+                logits = torch.empty(T, E, dtype=torch.float32, device=dev)
+                ops.router_logits(h, L.router, logits)
+            else:  # a plain bf16 GEMM with f32 output (library); top-k and CSR are ours
+                logits = torch.mm(h, L.router.t(), out_dtype=torch.float32)
             ops.moe_topk(logits, cfg, L.router_bias, False, mb)
         else:
             logits = h.float() @ L.router.float().t()
@@ -580,6 +583,23 @@ class ModelRunner:
         staged = self.expert_cache.staged_ptrs(L) if self.expert_cache is not None else None
         if self.ep is not None:
             x.add_(self.ep.moe_baseline(h, mb["topk_ids"], mb["topk_w"], gu, dn, staged=staged))
+            return
+        bk = getattr(gu, "bank_contiguous", False)
+        if self.is_cuda and T * k > 256 and gu.qw is not None and gu.e0 == 0 and gu.E == E and \
+                gu.N % 128 == 0 and dn.N % 128 == 0 and (bk or staged is not None):
+            # every pair is local: rows gathered per expert (CSR from the routing kernel), two
+            # grouped tcgen05 GEMMs, then the ordered combine adds the pairs into x
+            (gq, gs), (dq, ds) = staged if staged is not None else ((gu.qw_ptrs, gu.sm_ptrs),
+                                                                    (dn.qw_ptrs, dn.sm_ptrs))
+            P = T * k
+            a_rows = h.index_select(0, mb["tok_idx"])
+            mid = torch.empty(P, gu.N // 2, dtype=h.dtype, device=dev)
+            ops.gemm_grouped(a_rows, gq, gs, mb["tok_off"], gu.N, gu.K, 1, None, mid, E,
+                             gu.qw if bk else None, gu.sm if bk else None)
+            yp = torch.empty(P, dn.N, dtype=torch.float32, device=dev)
+            ops.gemm_grouped(mid, dq, ds, mb["tok_off"], dn.N, dn.K, 2, mb["pair_w"], yp, E,
+                             dn.qw if bk else None, dn.sm if bk else None)
+            ops.moe_combine_rmsnorm(x, yp, mb["pair_of"], None, None, None, cfg.rms_eps)
             return
         from ..parallel.ep import _local_experts_apply
         x.add_(_local_experts_apply(h, mb["topk_ids"], mb["topk_w"], gu, dn, (gu.e0, gu.e0 + gu.E), staged))

@@ -97,11 +97,13 @@ def test_q4_gemv_grouped_swiglu_and_scaled(cuda):
     assert _rel(x, ref) < 1e-2
 
 
-def test_moe_topk_matches_cpu(cuda):
+@pytest.mark.parametrize("T", [32, 3, 256, 700])
+def test_moe_topk_matches_cpu(cuda, T):
     torch.manual_seed(2)
     cfg = get_config("qwen3-235b-a22b")
-    E, k, T = cfg.n_experts, cfg.top_k, 32
-    logits = torch.randn(T, 2 * E)
+    E, k = cfg.n_experts, cfg.top_k
+    pred_on = T <= 256  # next-layer prediction is a decode-size feature
+    logits = torch.randn(T, 2 * E if pred_on else E)
 
     def bufs(dev):
         return {"topk_ids": torch.zeros(T, k, dtype=torch.int32, device=dev),
@@ -112,10 +114,14 @@ def test_moe_topk_matches_cpu(cuda):
 
     bc, bg = bufs("cpu"), bufs(cuda)
     ops.moe_topk(logits[:, :E].contiguous(), cfg, None, False, bc)
-    ops.moe_topk(logits.to(cuda), cfg, None, True, bg)
-    for key in ("topk_ids", "tok_off", "tok_idx", "pair_of"):
-        assert torch.equal(bc[key], bg[key].cpu()), key
-    assert torch.allclose(bc["topk_w"], bg["topk_w"].cpu(), rtol=1e-5, atol=1e-6)
+    for _ in range(2):  # the second call checks that the kernel left its workspace zeroed
+        ops.moe_topk(logits.to(cuda), cfg, None, pred_on, bg)
+        for key in ("topk_ids", "tok_off", "tok_idx", "pair_of"):
+            assert torch.equal(bc[key], bg[key].cpu()), key
+        assert torch.allclose(bc["topk_w"], bg["topk_w"].cpu(), rtol=1e-5, atol=1e-6)
+        assert torch.allclose(bc["pair_w"], bg["pair_w"].cpu(), rtol=1e-5, atol=1e-6)
+    if not pred_on:
+        return
     # prediction mask = union of the next layer's top-k
     pred = torch.zeros(E, dtype=torch.int32)
     pred[torch.sort(-torch.softmax(logits[:, E:], -1), dim=-1, stable=True).indices[:, :k].reshape(-1)] = 1
