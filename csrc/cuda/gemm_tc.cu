@@ -316,15 +316,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
           const half2 dl = *reinterpret_cast<const half2*>(blk ? &slo[i].y : &slo[i].x);
           const half2 dh = *reinterpret_cast<const half2*>(blk ? &shi[i].y : &shi[i].x);
           const float dd[2] = {__low2float(dl), __low2float(dh)};
-          const float mm[2] = {__high2float(dl), __high2float(dh)};
+          // min folded with the +128 offset of the magic conversion below: m - 128 d (exact
+          // in f32 whenever d and m are within 2^13 of each other, i.e. for real blocks)
+          const float mm[2] = {fmaf(-128.f, dd[0], __high2float(dl)), fmaf(-128.f, dd[1], __high2float(dh))};
 #pragma unroll
           for (int st = 0; st < 2; ++st) {
             const uint32_t w = words[blk * 2 + st];
 #pragma unroll
             for (int reg = 0; reg < 4; ++reg) {
               const int hi_row = reg & 1, hi_col = reg >> 1;
-              const float q0 = (float)((w >> (4 * reg)) & 15u);
-              const float q1 = (float)((w >> (4 * (reg + 4))) & 15u);
+              // nibbles reg and reg+4 -> bf16 (128 + q) pair in one LOP3; bf16 -> f32 is a
+              // 16-bit shift, so no integer-to-float conversion is issued
+              const uint32_t qq = lop3_and_or(w >> (4 * reg), 0x000F000Fu, 0x43004300u);
+              const float q0 = __uint_as_float(qq << 16);
+              const float q1 = __uint_as_float(qq & 0xFFFF0000u);
               const uint32_t v = pack_bf16x2(fmaf(dd[hi_row], q0, mm[hi_row]), fmaf(dd[hi_row], q1, mm[hi_row]));
               const int row = rt * 16 + g + 8 * hi_row;
               const int chunk = (blk * 4 + st * 2 + hi_col) ^ g;

@@ -31,7 +31,9 @@ def test_tc_gemm_dense(cuda, M, N, K):
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     ref = x.float() @ wd.t()
-    assert _rel(out, ref) < 2e-3
+    # wd is the format's dequantised bf16 value: the kernel must produce exactly these
+    # weights, so only the f32 summation order differs
+    assert _rel(out, ref) < 2e-5
     ob = torch.zeros(M, N, dtype=torch.bfloat16, device=cuda)
     ext().tc_gemm_q4(x, ptrs[0], ptrs[1], off, N, K, 0, torch.empty(0, device=cuda), ob, status, (M + 127) // 128 + 1,
                      q.qw, q.sm, 0)
