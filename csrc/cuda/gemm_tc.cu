@@ -1,18 +1,22 @@
 // Prefill GEMM on the 5th-generation tensor cores: C = X * W^T with bf16 activations X
 // and 4-bit tiled weights W (syn/q4.h), grouped over experts.
 //
-// One CTA computes a 128 x BN output tile (BN = 128 or 256) with its accumulator in TMEM:
-//   warp 0      TMA producer: X tiles (128 rows x 64 bf16, SWIZZLE_128B) -> smem stage
+// One CTA computes a 256 x BN output tile (BN = 128 or 256) as two 128-row MMA subtiles
+// that share every dequantised B stage (half the dequantisation work per FLOP of a 128-row
+// tile), with both accumulators in TMEM (2 * BN columns):
+//   warp 0      TMA producer: X tiles (2 x 128 rows x 64 bf16, SWIZZLE_128B) -> smem stage
 //   warp 2      raw-weight loader: bulk async copies (cp.async.bulk) of the packed 4-bit
 //               tiles and their scales, TC_RAW stages ahead of the dequantisers
 //   warp 1      TMEM allocator and MMA issuer: one elected thread issues tcgen05.mma
 //               (kind::f16, M=128, N=BN, K=16, bf16 x bf16 -> f32) per 16 columns and
+//               subtile (the second only when the tile has rows there) and
 //               tcgen05.commit's to the stage's "empty" barrier
 //   warps 4..11 B producers during the main loop (two per scheduler, so dequantisation
 //               latency hides): 4-bit weights -> bf16 (d*q+m, f32 math, one rounding)
 //               written straight into the UMMA K-major SWIZZLE_128B layout, then
 //               fence.proxy.async; afterwards the epilogue: tcgen05.ld 32x32b of their TMEM
-//               lane quarter (warp % 4) and column half, fused epilogue, global stores
+//               lane quarter (warp % 4) and column half of each subtile, fused epilogue,
+//               global stores
 // Stages are tracked with mbarriers; every wait is bounded (the kernel records an error
 // bit and bails out instead of hanging).  Reference op: `Gemm` (crates/kernels/src/op/
 // kind.rs; f32 reference crates/kernels/src/reference/linear.rs:71).
@@ -24,9 +28,9 @@
 
 namespace syn {
 
-constexpr int TC_BM = 128;
+constexpr int TC_BM = 128;   // rows of one MMA subtile
+constexpr int TC_MSUB = 2;   // subtiles per CTA tile (CTA tile = 256 rows)
 constexpr int TC_BK = 64;
-constexpr int TC_RAW = 6;     // packed-weight stages (deep: they hide HBM latency)
 constexpr int TC_TILE_RAW = 640;  // bytes per 16-row x 64-col packed tile: 512 nibbles + 128 scales
 constexpr uint64_t TC_WAIT_NS = 2000000000ull;  // 2 s: far above any legitimate stage wait
 
@@ -149,10 +153,13 @@ struct TcGemmArgs {
 template <int BN>
 struct TcCfg {
   static constexpr int STAGES = BN == 256 ? 3 : 4;
-  static constexpr int A_BYTES = TC_BM * TC_BK * 2;  // 16 KB
-  static constexpr int B_BYTES = BN * TC_BK * 2;     // 16 / 32 KB
+  static constexpr int RAW = BN == 256 ? 3 : 6;                // packed-weight stages
+  static constexpr int A_SUB = TC_BM * TC_BK * 2;              // 16 KB per subtile
+  static constexpr int A_BYTES = TC_MSUB * A_SUB;              // 32 KB
+  static constexpr int B_BYTES = BN * TC_BK * 2;               // 16 / 32 KB
   static constexpr int RAW_BYTES = (BN / 16) * TC_TILE_RAW;
-  static constexpr size_t SMEM = 1024 + (size_t)STAGES * (A_BYTES + B_BYTES) + (size_t)TC_RAW * RAW_BYTES;
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * (A_BYTES + B_BYTES) + (size_t)RAW * RAW_BYTES;
+  static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
 constexpr int TC_THREADS = 384;
@@ -164,6 +171,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
                                                             const __grid_constant__ CUtensorMap tmap_s,
                                                             TcGemmArgs a) {
   constexpr int TC_STAGES = TcCfg<BN>::STAGES;
+  constexpr int TC_RAW = TcCfg<BN>::RAW;
+  constexpr int A_SUB = TcCfg<BN>::A_SUB;
   constexpr int A_BYTES = TcCfg<BN>::A_BYTES;
   constexpr int B_BYTES = TcCfg<BN>::B_BYTES;
   constexpr int RAW_BYTES = TcCfg<BN>::RAW_BYTES;
@@ -186,7 +195,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
     int acc = 0, grp = -1, mt = 0;
     for (int g = 0; g < a.G; ++g) {
       const int cnt = a.row_off[g + 1] - a.row_off[g];
-      const int nt = (cnt + TC_BM - 1) / TC_BM;
+      const int nt = (cnt + TC_MSUB * TC_BM - 1) / (TC_MSUB * TC_BM);
       if ((int)blockIdx.x < acc + nt) { grp = g; mt = blockIdx.x - acc; break; }
       acc += nt;
     }
@@ -197,8 +206,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
   __syncthreads();
   const int grp = s_group;
   if (grp < 0) return;  // uniform: beyond the last tile
-  const int row0 = a.row_off[grp] + s_mtile * TC_BM;
+  const int row0 = a.row_off[grp] + s_mtile * TC_MSUB * TC_BM;
   const int row_end = a.row_off[grp + 1];
+  const bool two = row0 + TC_BM < row_end;  // second subtile has rows of this group
   const int KB = a.K / TC_BK;
 
   if (threadIdx.x == 0) {
@@ -216,7 +226,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(&tmem_base)),
-                 "r"(BN));
+                 "r"(TC_MSUB * BN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
   }
   asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
@@ -231,8 +241,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
         const int s = kb % TC_STAGES;
         const uint32_t ph = (kb / TC_STAGES) & 1;
         if (kb >= TC_STAGES && !mbar_wait(&empty[s], ph ^ 1, a.status, &s_abort)) break;
-        mbar_expect_tx(&full_a[s], A_BYTES);
+        mbar_expect_tx(&full_a[s], two ? A_BYTES : A_SUB);
         tma_load_2d(sA + s * A_BYTES, &tmap_a, kb * TC_BK, row0, &full_a[s]);
+        if (two) tma_load_2d(sA + s * A_BYTES + A_SUB, &tmap_a, kb * TC_BK, row0 + TC_BM, &full_a[s]);
       }
     }
   } else if (warp == 2) {
@@ -274,8 +285,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
         asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
         const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * B_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < TC_BK / 16; ++kk)
+        for (int kk = 0; kk < TC_BK / 16; ++kk) {
           umma_bf16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), idesc, (kb | kk) != 0);
+          if (two)
+            umma_bf16(tmem + BN, sw128_desc(a0 + A_SUB + kk * 32), sw128_desc(b0 + kk * 32), idesc, (kb | kk) != 0);
+        }
         umma_commit(&empty[s]);
       }
       umma_commit(&done_bar);
@@ -346,12 +360,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
     const int quarter = warp & 3;       // TMEM lanes this warp may read
     const int half = (warp - 4) >> 2;   // which half of the columns it stores
-    const int row = row0 + quarter * 32 + lane;
-    const bool live = ok && row < row_end && row < a.M;
+#pragma unroll 1
+    for (int sub = 0; sub < (two ? 2 : 1); ++sub)
 #pragma unroll 1
     for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
+      const int row = row0 + sub * TC_BM + quarter * 32 + lane;
+      const bool live = ok && row < row_end && row < a.M;
       uint32_t r[32];
-      tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + c0, r);
+      tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + sub * BN + c0, r);
       if (!live) continue;
       const int n0 = ntile * BN + c0;
       if (a.mode == 1) {  // SwiGLU over 8-column gate/up chunks
@@ -390,7 +406,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
   asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
   __syncthreads();
   if (warp == 1) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(BN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(TC_MSUB * BN));
   }
 }
 

@@ -250,7 +250,7 @@ def gemm_grouped(x, qw_ptrs, sm_ptrs, row_off, N, K, mode, route_w, out, G, bank
     M = x.shape[0]
     if M == 0:
         return out
-    max_mtiles = (M + 127) // 128 + G
+    max_mtiles = (M + 255) // 256 + G  # CTA tiles of 256 rows, at most one partial per group
     e = _EMPTY_I32(x.device)
     ext().tc_gemm_q4(x, qw_ptrs, sm_ptrs, row_off, N, K, mode,
                      route_w if route_w is not None else _EMPTY_F32(x.device), out, gemm_status(x.device),
