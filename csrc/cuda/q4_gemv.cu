@@ -750,7 +750,7 @@ static cudaError_t launch_v4(const GemvArgs& a, cudaStream_t s) {
 
 
 // ---------------------------------------------------------------------------------------
-// v5 (dense layers, 9..64 tokens): CTA = 4 warps = 64 output rows x one K slice.  The
+// v5 (dense layers, 1..64 tokens): CTA = 4 warps = 64 output rows x one K slice.  The
 // activations of the K slice are staged once per CTA in shared memory (cp.async) and shared
 // by the 4 warps (B fragments from shared memory, not L2); each warp issues all its packed-
 // weight loads for the slice up front.  K is split over gridDim.y CTAs; partial sums go to an
@@ -771,11 +771,11 @@ __global__ void __launch_bounds__(128, 1) q4_gemv5_kernel(GemvArgs a, float* __r
   const int T = a.tok_off[1] - a.tok_off[0];
   const int XS = KR * 64 + 8;             // smem row stride (elements), padded against conflicts
   __nv_bfloat16* xs_sm = reinterpret_cast<__nv_bfloat16*>(gsm5);
+  float* xsum_sm = reinterpret_cast<float*>(gsm5 + (size_t)NT * 8 * XS * 2);  // [KR*2][NT*8]
   __shared__ int s_last;
   const uint4* qw = reinterpret_cast<const uint4*>(a.qw_ptrs[0]);
   const uint2* smw = reinterpret_cast<const uint2*>(a.sm_ptrs[0]);
   const bool active = tile < a.N / 16;
-  const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
 
   // one pass over at most NT*8 tokens (the launcher picks NT >= ceil(T/8)); a second pass in
   // the same launch would race with the split-K reduction of the first on ws and counters
@@ -812,12 +812,35 @@ __global__ void __launch_bounds__(128, 1) q4_gemv5_kernel(GemvArgs a, float* __r
     asm volatile("cp.async.commit_group;\n" ::);
     asm volatile("cp.async.wait_group 0;\n" ::);
     __syncthreads();
+    // 32-column block sums of the staged activations, once per CTA (the min term of every
+    // weight row in the CTA uses them): xsum_sm[block][token], tokens contiguous
+    for (int idx = threadIdx.x; idx < KR * 2 * ntc * 8; idx += blockDim.x) {
+      const int j = idx % (ntc * 8), blk = idx / (ntc * 8);
+      const uint4* src = reinterpret_cast<const uint4*>(xs_sm + j * XS + blk * 32);
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 v = src[c];
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_bf16x2(u[e]);
+          sum += f.x + f.y;
+        }
+      }
+      xsum_sm[blk * (NT * 8) + j] = sum;
+    }
+    __syncthreads();
     float acc[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
     if (active) {
+      // ldmatrix row address of this lane: matrix (lane / 8) = k offset 8 * (lane / 8),
+      // row (lane % 8) = token inside the 8-token tile
+      const uint32_t lds_base =
+          (uint32_t)__cvta_generic_to_shared(xs_sm + (lane & 7) * XS + (lane >> 3) * 8);
 #pragma unroll
       for (int i = 0; i < GMAX; ++i) {
         if (i >= KR) break;
@@ -836,25 +859,22 @@ __global__ void __launch_bounds__(128, 1) q4_gemv5_kernel(GemvArgs a, float* __r
           const half2 hh = *reinterpret_cast<const half2*>(&vhi);
           const float dlo = __low2float(hl), dhi = __low2float(hh);
           const float mlo = fmaf(-128.f, dlo, __high2float(hl)), mhi = fmaf(-128.f, dhi, __high2float(hh));
-          const int kl = i * 64 + b * 32 + 2 * t;  // local k inside the slice
+          const float* xsb = xsum_sm + (i * 2 + b) * (NT * 8) + 2 * t;
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             if (nt < ntc) {
-              const __nv_bfloat16* xr = xs_sm + (nt * 8 + g) * XS + kl;
               uint32_t bf[2][2];
-              bf[0][0] = *reinterpret_cast<const uint32_t*>(xr);
-              bf[0][1] = *reinterpret_cast<const uint32_t*>(xr + 8);
-              bf[1][0] = *reinterpret_cast<const uint32_t*>(xr + 16);
-              bf[1][1] = *reinterpret_cast<const uint32_t*>(xr + 24);
-              float xs[4] = {0.f, 0.f, 0.f, 0.f}, blk[4] = {0.f, 0.f, 0.f, 0.f};
-              mma_bf16_16816(xs, ones, bf[0], xs);
-              mma_bf16_16816(xs, ones, bf[1], xs);
+              asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                           : "=r"(bf[0][0]), "=r"(bf[0][1]), "=r"(bf[1][0]), "=r"(bf[1][1])
+                           : "r"(lds_base + (uint32_t)((nt * 8 * XS + i * 64 + b * 32) * 2)));
+              float blk[4] = {0.f, 0.f, 0.f, 0.f};
               mma_bf16_16816(blk, af[0], bf[0], blk);
               mma_bf16_16816(blk, af[1], bf[1], blk);
-              acc[nt][0] += fmaf(dlo, blk[0], mlo * xs[0]);
-              acc[nt][1] += fmaf(dlo, blk[1], mlo * xs[1]);
-              acc[nt][2] += fmaf(dhi, blk[2], mhi * xs[2]);
-              acc[nt][3] += fmaf(dhi, blk[3], mhi * xs[3]);
+              const float2 xs = *reinterpret_cast<const float2*>(xsb + nt * 8);
+              acc[nt][0] += fmaf(dlo, blk[0], mlo * xs.x);
+              acc[nt][1] += fmaf(dlo, blk[1], mlo * xs.y);
+              acc[nt][2] += fmaf(dhi, blk[2], mhi * xs.x);
+              acc[nt][3] += fmaf(dhi, blk[3], mhi * xs.y);
             }
           }
         }
@@ -954,7 +974,7 @@ template <int NT, int GMAX>
 static cudaError_t launch_v5(const GemvArgs& a, int ksplit, float* ws, unsigned* counters, cudaStream_t s) {
   const int KG = a.K >> 6;
   const int KR = KG / ksplit;
-  const size_t smem = (size_t)NT * 8 * (KR * 64 + 8) * 2;
+  const size_t smem = (size_t)NT * 8 * (KR * 64 + 8) * 2 + (size_t)KR * 2 * NT * 8 * 4;
   static size_t set_for = 0;
   if (smem > 48 * 1024 && smem > set_for) {
     cudaError_t e = cudaFuncSetAttribute(q4_gemv5_kernel<NT, GMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -967,13 +987,13 @@ static cudaError_t launch_v5(const GemvArgs& a, int ksplit, float* ws, unsigned*
   return cudaGetLastError();
 }
 
-// Dense decode GEMV (one weight matrix, 9..64 rows of x).  ws: f32 workspace of
+// Dense decode GEMV (one weight matrix, 1..64 rows of x).  ws: f32 workspace of
 // ksplit * NT * 8 * N floats; counters: N/64 zeroed unsigned ints (left zeroed on exit).
 cudaError_t launch_q4_gemv_dense(const GemvArgs& a, float* ws, unsigned* counters, size_t ws_floats,
                                  cudaStream_t s) {
   const int T = a.nt_hint * 8;
   if (T > 64) return cudaErrorInvalidValue;
-  const int nt = T <= 16 ? 2 : (T <= 32 ? 4 : 8);
+  const int nt = T <= 8 ? 1 : (T <= 16 ? 2 : (T <= 32 ? 4 : 8));
   const int KG = a.K >> 6;
   // K slices of at most 8 groups (all of a warp's loads in flight at once), split further
   // while the grid is below ~4 CTAs per SM
@@ -988,6 +1008,7 @@ cudaError_t launch_q4_gemv_dense(const GemvArgs& a, float* ws, unsigned* counter
   }
   if (ksplit == 0) return cudaErrorInvalidValue;
   if (ksplit > 1 && (size_t)ksplit * nt * 8 * a.N > ws_floats) return cudaErrorInvalidValue;
+  if (nt == 1) return launch_v5<1, GMAX>(a, ksplit, ws, counters, s);
   if (nt == 2) return launch_v5<2, GMAX>(a, ksplit, ws, counters, s);
   if (nt == 4) return launch_v5<4, GMAX>(a, ksplit, ws, counters, s);
   return launch_v5<8, GMAX>(a, ksplit, ws, counters, s);

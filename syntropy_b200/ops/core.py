@@ -94,7 +94,7 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
             out.copy_(y)
         return out
     T = x.shape[0]
-    if isinstance(W, Q4Weight) and 8 < T <= DECODE_ROWS_MAX and W.N % 64 == 0 and _DENSE_V5[0]:
+    if isinstance(W, Q4Weight) and _DENSE_V5[1] <= T <= DECODE_ROWS_MAX and W.N % 64 == 0 and _DENSE_V5[0]:
         kmode = {GEMV_STORE: 0, GEMV_SWIGLU: 1, GEMV_ADD_F32: 3}[mode]
         if kmode == 0 and out.dtype == torch.float32:
             kmode = 5
@@ -141,7 +141,9 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
 
 _PTR_CACHE: dict = {}
 _GROUP_CACHE: dict = {}
-_DENSE_V5 = [__import__("os").environ.get("SYN_DENSE_V5", "1") == "1"]
+# dense decode GEMV: split-K smem-staged kernel (v5) for rows in [SYN_DENSE_V5_MIN, 64]
+_DENSE_V5 = [__import__("os").environ.get("SYN_DENSE_V5", "1") == "1",
+             int(__import__("os").environ.get("SYN_DENSE_V5_MIN", "9"))]
 _DENSE_WS: dict = {}
 
 

@@ -127,3 +127,29 @@ def test_histogram_quantiles():
     c.add(5)
     c.add(7)
     assert c.get() == 12
+
+
+def test_numa_binding_from_fake_nvml():
+    """NUMA CPU set decoded from an NVML affinity bitmask (fake NVML, no GPU)."""
+    from syntropy_b200.parallel.dist import numa_cpus
+
+    class FakeNvml:
+        def nvmlInit(self):
+            pass
+
+        def nvmlDeviceGetHandleByIndex(self, i):
+            return i
+
+        def nvmlDeviceGetCpuAffinity(self, h, n):
+            return [0b1010] + [0] * (n - 1) if h == 0 else [0, 1] + [0] * max(0, n - 2)
+
+    assert numa_cpus(0, FakeNvml()) == [1, 3]
+    import os
+    if (os.cpu_count() + 63) // 64 >= 2:
+        assert numa_cpus(1, FakeNvml()) == [64]
+
+    class Broken:
+        def nvmlInit(self):
+            raise RuntimeError("no driver")
+
+    assert numa_cpus(0, Broken()) is None
