@@ -26,6 +26,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s + p50 TTFT, Qwen3-235B-A22B-shape 4-bit, 1/2/4/8 B200, max over ranks"
+# the other named configs (same measurement; --model selects them): batch, prompt, decode
+CONFIG_DEFAULTS = {"qwen3-235b-a22b": (32, 1024, 256), "llama3-8b": (64, 2048, 256),
+                   "llama3-70b": (32, 4096, 512), "deepseek-v3": (16, 2048, 256)}
 
 
 def reference_arm(args):
@@ -88,9 +91,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="syntropy", choices=["syntropy", "reference"])
     ap.add_argument("--model", default="qwen3-235b-a22b")
-    ap.add_argument("--batch", type=int, default=32)
-    ap.add_argument("--prompt", type=int, default=1024)
-    ap.add_argument("--decode", type=int, default=256)
+    ap.add_argument("--batch", type=int, default=None, help="default: the named config's")
+    ap.add_argument("--prompt", type=int, default=None)
+    ap.add_argument("--decode", type=int, default=None)
+    ap.add_argument("--pp", type=int, default=1, help="dense models: pipeline stages (TP = gpus / pp)")
     ap.add_argument("--layers", type=int, default=0, help="dev only: override layer count (invalid headline)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--baseline", action="store_true", help="NCCL all-gather/reduce-scatter MoE data plane")
@@ -100,6 +104,10 @@ def main():
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
+    db, dp, dd = CONFIG_DEFAULTS.get(args.model, (32, 1024, 256))
+    args.batch = args.batch or db
+    args.prompt = args.prompt or dp
+    args.decode = args.decode or dd
 
     import torch
 
@@ -120,17 +128,44 @@ def main():
     cfg = get_config(args.model)
     if args.layers:
         cfg = cfg.replace(n_layers=args.layers)
-    if args.batch % world:
-        raise SystemExit("global batch must divide over the GPUs")
-    B = args.batch // world  # data-parallel attention: each rank serves its share of sequences
-    ep = None
-    if world > 1:
-        from syntropy_b200.parallel.ep import EPGroup
-        ep = EPGroup(ctx, cfg.n_experts, cfg.top_k, cfg.hidden, cap=B, n_layers=cfg.n_layers,
-                     fused=not args.baseline)
-    t0 = time.time()
-    mw = prepare_weights(cfg, dev, seed=args.seed, max_pos=args.prompt + max(args.decode, args.warmup + args.steps + 40) + 16,
-                         expert_range=ep.expert_range if ep else None)
+    ep = tp = pp = None
+    tp_size = 1
+    max_pos = args.prompt + max(args.decode, args.warmup + args.steps + 40) + 16
+    if cfg.is_moe:
+        if args.batch % world:
+            raise SystemExit("global batch must divide over the GPUs")
+        B = args.batch // world  # data-parallel attention: each rank serves its share of sequences
+        if world > 1:
+            from syntropy_b200.parallel.ep import EPGroup
+            ep = EPGroup(ctx, cfg.n_experts, cfg.top_k, cfg.hidden, cap=B, n_layers=cfg.n_layers,
+                         fused=not args.baseline)
+        t0 = time.time()
+        mw = prepare_weights(cfg, dev, seed=args.seed, max_pos=max_pos, expert_range=ep.expert_range if ep else None)
+    else:
+        # dense: tensor parallel over gpus/pp ranks, pipeline over pp stages; every rank of a
+        # stage serves every sequence
+        B = args.batch
+        layer_range = None
+        t0 = time.time()
+        if world > 1:
+            from syntropy_b200.parallel.dist import split_tp_pp
+            from syntropy_b200.parallel.pp import PPGroup
+            from syntropy_b200.parallel.tp import TPGroup
+            if world % args.pp:
+                raise SystemExit("--pp must divide the GPU count")
+            tp_size = world // args.pp
+            tp_ctx, pp_group, pp_ranks, stage = split_tp_pp(ctx, tp_size, args.pp)
+            if args.pp > 1:
+                pp = PPGroup(ctx, args.pp, stage, cfg.n_layers, group=pp_group, ranks=pp_ranks)
+                layer_range = pp.layer_range
+            t0 = time.time()
+            mw = prepare_weights(cfg, dev, seed=args.seed, max_pos=max_pos,
+                                 tp=(tp_ctx.rank, tp_size) if tp_size > 1 else None, layer_range=layer_range)
+            if tp_size > 1:
+                tp = TPGroup(tp_ctx, cfg.hidden, cap=B, n_layers=len(mw.layers),
+                             fused=not args.baseline and cfg.weight_quant == "q4")
+        else:
+            mw = prepare_weights(cfg, dev, seed=args.seed, max_pos=max_pos)
     torch.cuda.synchronize()
     t_weights = time.time() - t0
     # decode length: the config's, extended only if the requested steps need more tokens
@@ -140,13 +175,13 @@ def main():
     if args.expert_cache_frac < 1.0 and cfg.is_moe:
         from syntropy_b200.experts.cache import ExpertCache
         cache = ExpertCache(mw.layers, args.expert_cache_frac, dev)
-    runner = ModelRunner(mw, max_batch=B, max_seq_len=max_len + 16, ep=ep,
-                         use_graphs=not (ep is not None and not ep.fused))
+    graphs = not ((ep is not None and not ep.fused) or (tp is not None and not tp.fused) or pp is not None)
+    runner = ModelRunner(mw, max_batch=B, max_seq_len=max_len + 16, ep=ep, tp=tp, pp=pp, use_graphs=graphs)
     runner.expert_cache = cache
     eng = LLMEngine(runner, max_prefill_tokens=8192, dist_ctx=ctx)
     g = torch.Generator().manual_seed(1234)
     all_prompts = [torch.randint(0, cfg.vocab, (args.prompt,), generator=g).tolist() for _ in range(args.batch)]
-    prompts = all_prompts[rank::world]
+    prompts = all_prompts[rank::world] if cfg.is_moe else all_prompts
     # ---- prefill: TTFT of each request (all submitted at t0) ----
     ids = [eng.add_request(p, SamplingParams(max_tokens=decode_len, temperature=0.0)) for p in prompts]
     if ctx.enabled:
@@ -166,7 +201,10 @@ def main():
         import torch.distributed as dist
         gathered = [None] * world
         dist.all_gather_object(gathered, my_ttft, group=ctx.cpu_group)
-        my_ttft = [x for part in gathered for x in part]
+        if cfg.is_moe:
+            my_ttft = [x for part in gathered for x in part]
+        else:  # every rank serves every sequence: a request's TTFT is its latest rank's
+            my_ttft = [max(part[i] for part in gathered) for i in range(len(my_ttft))]
     ttft = sorted(my_ttft)
     p50_ttft_ms = 1e3 * ttft[len(ttft) // 2]
     # ---- decode: warm-up then timed steps ----
@@ -207,19 +245,29 @@ def main():
     ms_step = dev_ms / args.steps
     value = args.batch * 1e3 / ms_step          # whole-job tokens/s over all ranks
     e2e_value = args.batch * args.steps / e2e_s
+    wq = cfg.weight_quant
+    wdesc = {"q4": "4-bit block weights (32-elem, fp16 scale+min)", "bf16": "bf16 weights",
+             "fp8": "fp8 e4m3 weights, 128x128 block scales"}.get(wq, wq)
+    if cfg.is_moe:
+        par = (f"ep{world}+dp-attention" + ("" if ep is None or ep.fused else " (nccl baseline)")) \
+            if world > 1 else "single-gpu"
+    else:
+        par = "single-gpu" if world == 1 else (f"tp{tp_size}" + (f"xpp{args.pp}" if args.pp > 1 else "") +
+                                               ("" if tp is None or tp.fused else " (nccl all-reduce baseline)"))
+    metric = METRIC if args.model == "qwen3-235b-a22b" else \
+        f"decode tok/s + p50 TTFT, {args.model}-shape {wq}, max over ranks"
     out = {
-        "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "metric": metric, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16 activations, 4-bit block weights (32-elem, fp16 scale+min)",
-        "data": "synthetic uniform-random prompts, random-init N(0,0.02) weights quantised to 4-bit",
+        "vs_baseline": None, "dtype": f"bf16 activations, {wdesc}",
+        "data": f"synthetic uniform-random prompts, random-init N(0,0.02) weights ({wq})",
         "p50_ttft_ms": round(p50_ttft_ms, 2),
         "config": {"model": args.model if not args.layers else f"{args.model}[layers={args.layers}] (DEV, not headline)",
                    "global_batch": args.batch, "seq_len": args.prompt, "decode_len": decode_len,
-                   "parallelism": (f"ep{world}+dp-attention" + ("" if ep is None or ep.fused else " (nccl baseline)"))
-                   if world > 1 else "single-gpu",
+                   "parallelism": par,
                    "expert_cache_frac": args.expert_cache_frac if cfg.is_moe else 1.0,
                    "host_tier_gb": round(cache.host_bytes() / 1e9, 2) if cache is not None else 0.0,
-                   "l2": "inputs larger than L2 (weights 140+ GB streamed per step)",
+                   "l2": f"inputs larger than L2 ({mw.nbytes() / 1e9:.0f} GB of weights streamed per step per rank)",
                    "weights_gb": round(mw.nbytes() / 1e9, 2), "weight_build_s": round(t_weights, 1)},
         "clocks": clk.summary(),
         "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": runner.desc.nbytes,

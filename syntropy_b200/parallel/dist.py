@@ -78,6 +78,29 @@ def init_distributed(backend: str | None = None, timeout_s: float = 120.0) -> Di
     return DistContext(rank, world, local, device, group, cpu_group)
 
 
+def split_tp_pp(ctx: DistContext, tp: int, pp: int):
+    """TP x PP layout over the world: global rank = stage * tp + tp_index.  Returns
+    (tp_ctx, pp_group, pp_ranks, stage): tp_ctx is a DistContext over this rank's TP group
+    (its stage), pp_group/pp_ranks link this TP index across the stages.  Every rank creates
+    every group in the same order (a torch.distributed requirement)."""
+    assert tp * pp == ctx.world, "tp * pp must equal the world size"
+    stage, t = divmod(ctx.rank, tp)
+    nccl = dist.get_backend(ctx.group) == "nccl"
+    tp_ctx = pp_group = pp_ranks = None
+    for s in range(pp):
+        ranks = [s * tp + i for i in range(tp)]
+        g = dist.new_group(ranks)
+        cg = dist.new_group(ranks, backend="gloo") if nccl else g
+        if s == stage:
+            tp_ctx = DistContext(t, tp, ctx.local_rank, ctx.device, g, cg)
+    for i in range(tp):
+        ranks = [s * tp + i for s in range(pp)]
+        g = dist.new_group(ranks)
+        if i == t:
+            pp_group, pp_ranks = g, ranks
+    return tp_ctx, pp_group, pp_ranks, stage
+
+
 def max_over_ranks(ctx: DistContext, value: float) -> float:
     if not ctx.enabled:
         return value
