@@ -84,7 +84,7 @@ torch::Tensor q4_dequant_rows_cpu(torch::Tensor rows, int64_t N, int64_t K) {
 
 // rows -> tiled (qw int32 [N*K/8], sm fp16 [N*K/16])
 std::vector<torch::Tensor> q4_rows_to_tiled_cpu(torch::Tensor rows, int64_t N, int64_t K) {
-  TORCH_CHECK(N % 16 == 0 && K % 64 == 0, "N%16, K%64");
+  TORCH_CHECK(N % 16 == 0 && K % 64 == 0, "q4 tiled layout needs N % 16 == 0 and K % 64 == 0, got N=", N, " K=", K);
   rows = rows.contiguous();
   auto qw = torch::zeros({N * K / 8}, torch::kInt32);
   auto sm = torch::empty({N * K / 16}, torch::kFloat16);

@@ -750,268 +750,264 @@ static cudaError_t launch_v4(const GemvArgs& a, cudaStream_t s) {
 
 
 // ---------------------------------------------------------------------------------------
-// v5 (dense layers, 1..64 tokens): CTA = 4 warps = 64 output rows x one K slice.  The
-// activations of the K slice are staged once per CTA in shared memory (cp.async) and shared
-// by the 4 warps (B fragments from shared memory, not L2); each warp issues all its packed-
-// weight loads for the slice up front.  K is split over gridDim.y CTAs; partial sums go to an
+// v5 (dense layers, 1..64 tokens): CTA = 4 warps = 64 output rows x one K slice of KR
+// 64-column groups.  The activations of the slice are staged once per CTA in shared memory
+// (cp.async) with their 32-column block sums, and shared by the 4 warps (B fragments by
+// ldmatrix); each warp issues all KR of its packed-weight loads up front.  NT (8-token
+// tiles) and KR are compile-time, so the main loop is straight-line code whose NT
+// independent MMA chains interleave.  K is split over gridDim.y CTAs; partial sums go to an
 // f32 workspace and the last CTA of a row block (arrival counter) adds them in slice order
 // (deterministic) and runs the epilogue.
-template <int NT, int GMAX>
-__global__ void __launch_bounds__(128, 1) q4_gemv5_kernel(GemvArgs a, float* __restrict__ ws,
+template <int NT, int KR>
+__global__ void __launch_bounds__(128, 4) q4_gemv5_kernel(GemvArgs a, float* __restrict__ ws,
                                                        unsigned* __restrict__ counters) {
   extern __shared__ __align__(16) uint8_t gsm5[];
+  constexpr int XS = KR * 64 + 8;  // smem row stride (elements), padded against bank conflicts
+  constexpr int TT = NT * 8;       // token rows staged (rows past T repeat the last token)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int KG = a.K >> 6;
   const int KS = gridDim.y;
-  const int KR = KG / KS;                 // groups per slice (host guarantees divisibility)
   const int ks = blockIdx.y;
   const int rb = blockIdx.x;
-  const int tile = rb * 4 + warp;         // 16-row tile of this warp
-  const int T = a.tok_off[1] - a.tok_off[0];
-  const int XS = KR * 64 + 8;             // smem row stride (elements), padded against conflicts
+  const int tile = rb * 4 + warp;  // 16-row tile of this warp
+  const int T = min(a.tok_off[1] - a.tok_off[0], TT);
   __nv_bfloat16* xs_sm = reinterpret_cast<__nv_bfloat16*>(gsm5);
-  float* xsum_sm = reinterpret_cast<float*>(gsm5 + (size_t)NT * 8 * XS * 2);  // [KR*2][NT*8]
+  float* xsum_sm = reinterpret_cast<float*>(gsm5 + (size_t)TT * XS * 2);  // [KR*2][TT]
   __shared__ int s_last;
   const uint4* qw = reinterpret_cast<const uint4*>(a.qw_ptrs[0]);
   const uint2* smw = reinterpret_cast<const uint2*>(a.sm_ptrs[0]);
   const bool active = tile < a.N / 16;
 
-  // one pass over at most NT*8 tokens (the launcher picks NT >= ceil(T/8)); a second pass in
-  // the same launch would race with the split-K reduction of the first on ws and counters
-  {
-    const int c0 = 0;
-    const int ccount = min(T, NT * 8);
-    const int ntc = (ccount + 7) >> 3;
-    // 1) weights of this warp's slice, all loads in flight at once
-    uint4 q[GMAX];
-    uint2 slo[GMAX], shi[GMAX];
-    if (active) {
+  // 1) weights of this warp's slice: all KR loads in flight at once
+  uint4 q[KR];
+  uint2 slo[KR], shi[KR];
+  if (active) {
+    const int64_t tk0 = (int64_t)tile * KG + ks * KR;
 #pragma unroll
-      for (int i = 0; i < GMAX; ++i) {
-        if (i < KR) {
-          const int64_t tk = (int64_t)tile * KG + ks * KR + i;
-          q[i] = __ldcs(qw + tk * 32 + lane);
-          slo[i] = __ldcs(smw + tk * 16 + g);
-          shi[i] = __ldcs(smw + tk * 16 + g + 8);
-        }
-      }
+    for (int i = 0; i < KR; ++i) {
+      q[i] = __ldcs(qw + (tk0 + i) * 32 + lane);
+      slo[i] = __ldcs(smw + (tk0 + i) * 16 + g);
+      shi[i] = __ldcs(smw + (tk0 + i) * 16 + g + 8);
     }
-    // 2) activations of the slice into shared memory (all tokens of the chunk)
-    __syncthreads();
-    const int chunks_per_row = KR * 8;  // 16-byte chunks
-    for (int idx = threadIdx.x; idx < ntc * 8 * chunks_per_row; idx += blockDim.x) {
-      const int j = idx / chunks_per_row, c = idx % chunks_per_row;
-      const int jj = min(j, ccount - 1);
-      const int row = a.tok_idx ? a.tok_idx[c0 + jj] : c0 + jj;
-      const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.x) +
-                                                        (int64_t)row * a.ldx + ks * KR * 64) + c;
+  }
+  // 2) activations of the slice into shared memory
+  {
+    const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(a.x) + (int64_t)ks * KR * 64;
+    constexpr int CPR = KR * 8;  // 16-byte chunks per row
+#pragma unroll 4
+    for (int idx = threadIdx.x; idx < TT * CPR; idx += 128) {
+      const int j = idx / CPR, c = idx % CPR;
+      const int row = min(j, T - 1);
+      const uint4* src = reinterpret_cast<const uint4*>(xb + (int64_t)row * a.ldx) + c;
       const uint32_t dst = (uint32_t)__cvta_generic_to_shared(xs_sm + j * XS + c * 8);
       asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src));
     }
     asm volatile("cp.async.commit_group;\n" ::);
     asm volatile("cp.async.wait_group 0;\n" ::);
-    __syncthreads();
-    // 32-column block sums of the staged activations, once per CTA (the min term of every
-    // weight row in the CTA uses them): xsum_sm[block][token], tokens contiguous
-    for (int idx = threadIdx.x; idx < KR * 2 * ntc * 8; idx += blockDim.x) {
-      const int j = idx % (ntc * 8), blk = idx / (ntc * 8);
-      const uint4* src = reinterpret_cast<const uint4*>(xs_sm + j * XS + blk * 32);
-      float sum = 0.f;
+  }
+  __syncthreads();
+  // 32-column block sums (the min term of every weight row uses them): xsum_sm[block][token]
+  for (int idx = threadIdx.x; idx < KR * 2 * TT; idx += 128) {
+    const int j = idx % TT, blk = idx / TT;
+    const uint4* src = reinterpret_cast<const uint4*>(xs_sm + j * XS + blk * 32);
+    float sum = 0.f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint4 v = src[c];
-        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    for (int c = 0; c < 4; ++c) {
+      const uint4 v = src[c];
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = unpack_bf16x2(u[e]);
-          sum += f.x + f.y;
-        }
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_bf16x2(u[e]);
+        sum += f.x + f.y;
       }
-      xsum_sm[blk * (NT * 8) + j] = sum;
     }
-    __syncthreads();
-    float acc[NT][4];
+    xsum_sm[blk * TT + j] = sum;
+  }
+  __syncthreads();
+  float acc[NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+  for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
-    if (active) {
-      // ldmatrix row address of this lane: matrix (lane / 8) = k offset 8 * (lane / 8),
-      // row (lane % 8) = token inside the 8-token tile
-      const uint32_t lds_base =
-          (uint32_t)__cvta_generic_to_shared(xs_sm + (lane & 7) * XS + (lane >> 3) * 8);
+    for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
+  if (active) {
+    // ldmatrix row address of this lane: matrix (lane / 8) = k offset 8 * (lane / 8),
+    // row (lane % 8) = token inside the 8-token tile
+    const uint32_t lds_base = (uint32_t)__cvta_generic_to_shared(xs_sm + (lane & 7) * XS + (lane >> 3) * 8);
 #pragma unroll
-      for (int i = 0; i < GMAX; ++i) {
-        if (i >= KR) break;
+    for (int i = 0; i < KR; ++i) {
 #pragma unroll
-        for (int b = 0; b < 2; ++b) {
-          const uint32_t w0 = b ? q[i].z : q[i].x;
-          const uint32_t w1 = b ? q[i].w : q[i].y;
-          uint32_t af[2][4];
+      for (int b = 0; b < 2; ++b) {
+        const uint32_t w0 = b ? q[i].z : q[i].x;
+        const uint32_t w1 = b ? q[i].w : q[i].y;
+        uint32_t af[2][4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            af[0][j] = lop3_and_or(w0 >> (4 * j), 0x000F000Fu, 0x43004300u);
-            af[1][j] = lop3_and_or(w1 >> (4 * j), 0x000F000Fu, 0x43004300u);
-          }
-          const uint32_t vlo = b ? slo[i].y : slo[i].x, vhi = b ? shi[i].y : shi[i].x;
-          const half2 hl = *reinterpret_cast<const half2*>(&vlo);
-          const half2 hh = *reinterpret_cast<const half2*>(&vhi);
-          const float dlo = __low2float(hl), dhi = __low2float(hh);
-          const float mlo = fmaf(-128.f, dlo, __high2float(hl)), mhi = fmaf(-128.f, dhi, __high2float(hh));
-          const float* xsb = xsum_sm + (i * 2 + b) * (NT * 8) + 2 * t;
+        for (int j = 0; j < 4; ++j) {
+          af[0][j] = lop3_and_or(w0 >> (4 * j), 0x000F000Fu, 0x43004300u);
+          af[1][j] = lop3_and_or(w1 >> (4 * j), 0x000F000Fu, 0x43004300u);
+        }
+        const uint32_t vlo = b ? slo[i].y : slo[i].x, vhi = b ? shi[i].y : shi[i].x;
+        const half2 hl = *reinterpret_cast<const half2*>(&vlo);
+        const half2 hh = *reinterpret_cast<const half2*>(&vhi);
+        const float dlo = __low2float(hl), dhi = __low2float(hh);
+        const float mlo = fmaf(-128.f, dlo, __high2float(hl)), mhi = fmaf(-128.f, dhi, __high2float(hh));
+        const float* xsb = xsum_sm + (i * 2 + b) * TT + 2 * t;
 #pragma unroll
-          for (int nt = 0; nt < NT; ++nt) {
-            if (nt < ntc) {
-              uint32_t bf[2][2];
-              asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-                           : "=r"(bf[0][0]), "=r"(bf[0][1]), "=r"(bf[1][0]), "=r"(bf[1][1])
-                           : "r"(lds_base + (uint32_t)((nt * 8 * XS + i * 64 + b * 32) * 2)));
-              float blk[4] = {0.f, 0.f, 0.f, 0.f};
-              mma_bf16_16816(blk, af[0], bf[0], blk);
-              mma_bf16_16816(blk, af[1], bf[1], blk);
-              const float2 xs = *reinterpret_cast<const float2*>(xsb + nt * 8);
-              acc[nt][0] += fmaf(dlo, blk[0], mlo * xs.x);
-              acc[nt][1] += fmaf(dlo, blk[1], mlo * xs.y);
-              acc[nt][2] += fmaf(dhi, blk[2], mhi * xs.x);
-              acc[nt][3] += fmaf(dhi, blk[3], mhi * xs.y);
-            }
-          }
+        for (int nt = 0; nt < NT; ++nt) {
+          uint32_t bf[2][2];
+          asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                       : "=r"(bf[0][0]), "=r"(bf[0][1]), "=r"(bf[1][0]), "=r"(bf[1][1])
+                       : "r"(lds_base + (uint32_t)((nt * 8 * XS + i * 64 + b * 32) * 2)));
+          float blk[4] = {0.f, 0.f, 0.f, 0.f};
+          mma_bf16_16816(blk, af[0], bf[0], blk);
+          mma_bf16_16816(blk, af[1], bf[1], blk);
+          const float2 xs = *reinterpret_cast<const float2*>(xsb + nt * 8);
+          acc[nt][0] += fmaf(dlo, blk[0], mlo * xs.x);
+          acc[nt][1] += fmaf(dlo, blk[1], mlo * xs.y);
+          acc[nt][2] += fmaf(dhi, blk[2], mhi * xs.x);
+          acc[nt][3] += fmaf(dhi, blk[3], mhi * xs.y);
         }
       }
     }
-    // 3) split-K partials -> workspace [ks][token][N]; the last slice CTA reduces in order
-    if (KS == 1) {
-      if (active) {
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
-            const int j = nt * 8 + 2 * t + hf;
-            if (j >= ccount) continue;
-            const int p = c0 + j;
-            if (a.mode == GEMV_SWIGLU) {
-              reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)p * (a.N / 2) + tile * 8 + g] =
-                  f2bf(silu(acc[nt][hf]) * acc[nt][2 + hf]);
-            } else {
-              gemv_store(a, p, tile * 16 + g, acc[nt][hf]);
-              gemv_store(a, p, tile * 16 + g + 8, acc[nt][2 + hf]);
-            }
-          }
-      }
-      return;
-    }
+  }
+  // 3) split-K partials -> workspace [ks][token][N]; the last slice CTA reduces in order
+  if (KS == 1) {
     if (active) {
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
-          const int j = nt * 8 + 2 * t + hf;
-          if (j >= ccount) continue;
-          float* w = ws + ((int64_t)ks * NT * 8 + j) * a.N;
-          w[tile * 16 + g] = acc[nt][hf];
-          w[tile * 16 + g + 8] = acc[nt][2 + hf];
-        }
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      const unsigned prev = atomicAdd(&counters[rb], 1u);
-      s_last = (prev == (unsigned)KS - 1);
-      if (s_last) counters[rb] = 0u;
-    }
-    __syncthreads();
-    if (s_last) {
-      __threadfence();
-      // 64 rows x ccount tokens, summed over the slices in slice order (deterministic).  A
-      // thread owns 4 consecutive rows of one token (float4) and issues the loads of up to
-      // 8 slices before adding any: the reduction is bound by L2 latency, not bandwidth.
-      const bool glu = a.mode == GEMV_SWIGLU;
-      for (int idx = threadIdx.x; idx < 16 * ccount; idx += blockDim.x) {
-        const int c4 = idx & 15, j = idx >> 4;
-        if (glu && (c4 & 2)) continue;  // SwiGLU: rows 8..15 of a 16-row tile are the up halves
-        const int n = rb * 64 + c4 * 4;
-        const float* src = ws + (int64_t)j * a.N + n;
-        const int64_t sstride = (int64_t)NT * 8 * a.N;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f), u = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int s0 = 0; s0 < KS; s0 += 8) {
-          float4 bv[8], bu[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            if (s0 + i < KS) {
-              bv[i] = __ldcg(reinterpret_cast<const float4*>(src + (s0 + i) * sstride));
-              if (glu) bu[i] = __ldcg(reinterpret_cast<const float4*>(src + (s0 + i) * sstride + 8));
-            }
-          }
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            if (s0 + i < KS) {
-              v.x += bv[i].x; v.y += bv[i].y; v.z += bv[i].z; v.w += bv[i].w;
-              if (glu) { u.x += bu[i].x; u.y += bu[i].y; u.z += bu[i].z; u.w += bu[i].w; }
-            }
+          const int p = nt * 8 + 2 * t + hf;
+          if (p >= T) continue;
+          if (a.mode == GEMV_SWIGLU) {
+            reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)p * (a.N / 2) + tile * 8 + g] =
+                f2bf(silu(acc[nt][hf]) * acc[nt][2 + hf]);
+          } else {
+            gemv_store(a, p, tile * 16 + g, acc[nt][hf]);
+            gemv_store(a, p, tile * 16 + g + 8, acc[nt][2 + hf]);
           }
         }
-        const int p = c0 + j;
-        if (glu) {
-          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.out) + (int64_t)p * (a.N / 2) + (n >> 4) * 8 + (n & 7);
-          o[0] = f2bf(silu(v.x) * u.x);
-          o[1] = f2bf(silu(v.y) * u.y);
-          o[2] = f2bf(silu(v.z) * u.z);
-          o[3] = f2bf(silu(v.w) * u.w);
-        } else {
-          gemv_store(a, p, n, v.x);
-          gemv_store(a, p, n + 1, v.y);
-          gemv_store(a, p, n + 2, v.z);
-          gemv_store(a, p, n + 3, v.w);
+    }
+    return;
+  }
+  if (active) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int j = nt * 8 + 2 * t + hf;
+        if (j >= T) continue;
+        float* w = ws + ((int64_t)ks * TT + j) * a.N;
+        w[tile * 16 + g] = acc[nt][hf];
+        w[tile * 16 + g + 8] = acc[nt][2 + hf];
+      }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(&counters[rb], 1u);
+    s_last = (prev == (unsigned)KS - 1);
+    if (s_last) counters[rb] = 0u;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  // 64 rows x T tokens, summed over the slices in slice order (deterministic).  A thread owns
+  // 4 consecutive rows of one token (float4) and issues the loads of up to 8 slices before
+  // adding any: the reduction is bound by L2 latency, not bandwidth.
+  const bool glu = a.mode == GEMV_SWIGLU;
+  for (int idx = threadIdx.x; idx < 16 * T; idx += 128) {
+    const int c4 = idx & 15, j = idx >> 4;
+    if (glu && (c4 & 2)) continue;  // SwiGLU: rows 8..15 of a 16-row tile are the up halves
+    const int n = rb * 64 + c4 * 4;
+    const float* src = ws + (int64_t)j * a.N + n;
+    const int64_t sstride = (int64_t)TT * a.N;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f), u = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < KS; s0 += 8) {
+      float4 bv[8], bu[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (s0 + i < KS) {
+          bv[i] = __ldcg(reinterpret_cast<const float4*>(src + (s0 + i) * sstride));
+          if (glu) bu[i] = __ldcg(reinterpret_cast<const float4*>(src + (s0 + i) * sstride + 8));
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (s0 + i < KS) {
+          v.x += bv[i].x; v.y += bv[i].y; v.z += bv[i].z; v.w += bv[i].w;
+          if (glu) { u.x += bu[i].x; u.y += bu[i].y; u.z += bu[i].z; u.w += bu[i].w; }
         }
       }
     }
-    __syncthreads();
+    if (glu) {
+      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.out) + (int64_t)j * (a.N / 2) + (n >> 4) * 8 + (n & 7);
+      o[0] = f2bf(silu(v.x) * u.x);
+      o[1] = f2bf(silu(v.y) * u.y);
+      o[2] = f2bf(silu(v.z) * u.z);
+      o[3] = f2bf(silu(v.w) * u.w);
+    } else {
+      gemv_store(a, j, n, v.x);
+      gemv_store(a, j, n + 1, v.y);
+      gemv_store(a, j, n + 2, v.z);
+      gemv_store(a, j, n + 3, v.w);
+    }
   }
 }
 
-template <int NT, int GMAX>
+template <int NT, int KR>
 static cudaError_t launch_v5(const GemvArgs& a, int ksplit, float* ws, unsigned* counters, cudaStream_t s) {
-  const int KG = a.K >> 6;
-  const int KR = KG / ksplit;
-  const size_t smem = (size_t)NT * 8 * (KR * 64 + 8) * 2 + (size_t)KR * 2 * NT * 8 * 4;
-  static size_t set_for = 0;
-  if (smem > 48 * 1024 && smem > set_for) {
-    cudaError_t e = cudaFuncSetAttribute(q4_gemv5_kernel<NT, GMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  constexpr size_t smem = (size_t)NT * 8 * (KR * 64 + 8) * 2 + (size_t)KR * 2 * NT * 8 * 4;
+  static bool set = false;
+  if (smem > 48 * 1024 && !set) {
+    cudaError_t e = cudaFuncSetAttribute(q4_gemv5_kernel<NT, KR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return e;
-    set_for = smem;
+    set = true;
   }
   dim3 grid((unsigned)((a.N / 16 + 3) / 4), (unsigned)ksplit);
-  q4_gemv5_kernel<NT, GMAX><<<grid, 128, smem, s>>>(a, ws, counters);
+  q4_gemv5_kernel<NT, KR><<<grid, 128, smem, s>>>(a, ws, counters);
   return cudaGetLastError();
 }
 
-// Dense decode GEMV (one weight matrix, 1..64 rows of x).  ws: f32 workspace of
-// ksplit * NT * 8 * N floats; counters: N/64 zeroed unsigned ints (left zeroed on exit).
+template <int NT>
+static cudaError_t launch_v5_kr(const GemvArgs& a, int kr, float* ws, unsigned* counters, cudaStream_t s) {
+  const int ksplit = (a.K >> 6) / kr;
+  if (kr == 8) return launch_v5<NT, 8>(a, ksplit, ws, counters, s);
+  if (kr == 4) return launch_v5<NT, 4>(a, ksplit, ws, counters, s);
+  return launch_v5<NT, 2>(a, ksplit, ws, counters, s);
+}
+
+// Split of the dense decode GEMV: 8-token tiles (nt), 64-column groups per K slice (kr) and
+// the workspace it needs (floats).  kr is the largest of 8/4/2 dividing K/64, halved while the
+// grid is under ~4 CTAs per SM.  Returns false when no split fits (K/64 odd, or more than 64 rows).
+bool q4_gemv_dense_plan(int N, int K, int rows, int* nt_out, int* kr_out, size_t* ws_floats_out) {
+  if (rows < 1 || rows > 64 || N % 64 || K % 128) return false;
+  const int nt = rows <= 8 ? 1 : (rows <= 16 ? 2 : (rows <= 32 ? 4 : 8));
+  const int KG = K >> 6;
+  int kr = KG % 8 == 0 ? 8 : (KG % 4 == 0 ? 4 : 2);
+  const long row_blocks = (N / 16 + 3) / 4;
+  while (kr > 2 && row_blocks * (KG / kr) < 148L * 4) kr /= 2;
+  const int ksplit = KG / kr;
+  *nt_out = nt;
+  *kr_out = kr;
+  *ws_floats_out = ksplit > 1 ? (size_t)ksplit * nt * 8 * (size_t)N : 0;
+  return true;
+}
+
+// Dense decode GEMV (one weight matrix, 1..64 rows of x).  ws: f32 workspace of at least
+// the planned size; counters: N/64 zeroed unsigned ints (left zeroed on exit).
 cudaError_t launch_q4_gemv_dense(const GemvArgs& a, float* ws, unsigned* counters, size_t ws_floats,
                                  cudaStream_t s) {
-  const int T = a.nt_hint * 8;
-  if (T > 64) return cudaErrorInvalidValue;
-  const int nt = T <= 8 ? 1 : (T <= 16 ? 2 : (T <= 32 ? 4 : 8));
-  const int KG = a.K >> 6;
-  // K slices of at most 8 groups (all of a warp's loads in flight at once), split further
-  // while the grid is below ~4 CTAs per SM
-  constexpr int GMAX = 8;
-  const int row_blocks = (a.N / 16 + 3) / 4;
-  int ksplit = 0;
-  for (int k = 1; k <= KG; ++k) {
-    if (KG % k || KG / k > GMAX) continue;
-    if (k > 1 && (size_t)k * nt * 8 * a.N > ws_floats) break;  // no deeper split than the workspace holds
-    ksplit = k;
-    if ((long)row_blocks * k >= 148L * 4) break;
-  }
-  if (ksplit == 0) return cudaErrorInvalidValue;
-  if (ksplit > 1 && (size_t)ksplit * nt * 8 * a.N > ws_floats) return cudaErrorInvalidValue;
-  if (nt == 1) return launch_v5<1, GMAX>(a, ksplit, ws, counters, s);
-  if (nt == 2) return launch_v5<2, GMAX>(a, ksplit, ws, counters, s);
-  if (nt == 4) return launch_v5<4, GMAX>(a, ksplit, ws, counters, s);
-  return launch_v5<8, GMAX>(a, ksplit, ws, counters, s);
+  int nt, kr;
+  size_t need;
+  if (!q4_gemv_dense_plan(a.N, a.K, a.nt_hint * 8 < 64 ? a.nt_hint * 8 : 64, &nt, &kr, &need))
+    return cudaErrorInvalidValue;
+  if (need > ws_floats) return cudaErrorInvalidValue;
+  if (nt == 1) return launch_v5_kr<1>(a, kr, ws, counters, s);
+  if (nt == 2) return launch_v5_kr<2>(a, kr, ws, counters, s);
+  if (nt == 4) return launch_v5_kr<4>(a, kr, ws, counters, s);
+  return launch_v5_kr<8>(a, kr, ws, counters, s);
 }
 
 cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {

@@ -58,7 +58,8 @@ extern "C" __attribute__((visibility("default"))) int syn_q4_gemv_dense_noalloc(
     cudaStream_t stream, char* err, int err_len) {
   if (!x || !qw || !sm || !out) return fail(err, err_len, -1, "null pointer argument");
   if (rows < 1 || rows > 64) return fail(err, err_len, -1, "rows must be in 1..64");
-  if (K <= 0 || N <= 0 || K % 64 || N % 64) return fail(err, err_len, -1, "N and K must be positive multiples of 64");
+  if (K <= 0 || N <= 0 || K % 128 || N % 64)
+    return fail(err, err_len, -1, "N must be a positive multiple of 64 and K of 128");
   if (ldx < K || (ldx * 2) % 16 || (reinterpret_cast<uintptr_t>(x) & 15))
     return fail(err, err_len, -1, "x rows must be 16-byte aligned with ldx >= K");
   if (mode != 0 && mode != 1 && mode != 3 && mode != 5) return fail(err, err_len, -1, "mode must be 0, 1, 3 or 5");
@@ -67,18 +68,12 @@ extern "C" __attribute__((visibility("default"))) int syn_q4_gemv_dense_noalloc(
     snprintf(m, sizeof(m), "N=%d exceeds the scratch limit of %d rows", N, SYN_NOALLOC_MAX_N);
     return fail(err, err_len, -1, m);
   }
-  // the shallowest split the kernel accepts (at most 8 column groups of 64 per slice) must fit
-  const int KG = K / 64;
-  int kmin = 0;
-  for (int k = 1; k <= KG; ++k)
-    if (KG % k == 0 && KG / k <= 8) {
-      kmin = k;
-      break;
-    }
-  const int rows8 = ((rows + 7) / 8) * 8;
-  const int nt = rows8 <= 16 ? 2 : (rows8 <= 32 ? 4 : 8);  // token tiles per CTA, as the launcher picks
-  const size_t need = kmin > 1 ? (size_t)kmin * nt * 8 * (size_t)N : 0;
-  if (kmin == 0 || need > SYN_NOALLOC_WS_FLOATS) {
+  // the split the launcher will use must fit the fixed scratch
+  int nt = 0, kr = 0;
+  size_t need = 0;
+  if (!syn::q4_gemv_dense_plan(N, K, rows, &nt, &kr, &need))
+    return fail(err, err_len, -1, "unsupported shape: K must be a multiple of 128");
+  if (need > SYN_NOALLOC_WS_FLOATS) {
     char m[200];
     snprintf(m, sizeof(m), "N=%d, K=%d, rows=%d needs %zu workspace floats; the fixed scratch holds %u", N, K, rows,
              need, (unsigned)SYN_NOALLOC_WS_FLOATS);

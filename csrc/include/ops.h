@@ -76,6 +76,7 @@ void tp_reduce_norm(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, i
 void verify_accept(torch::Tensor logits, torch::Tensor draft, torch::Tensor temperature, torch::Tensor top_k,
                    torch::Tensor top_p, torch::Tensor seed, torch::Tensor stream, torch::Tensor counter,
                    torch::Tensor out_tokens, torch::Tensor n_accept);
+int64_t q4_gemv_dense_ws(int64_t N, int64_t K, int64_t rows);
 void q4_gemv_dense(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
                    torch::Tensor out, int64_t N, int64_t K, int64_t mode, torch::Tensor ws, torch::Tensor counters);
 void register_all(pybind11::module& m);

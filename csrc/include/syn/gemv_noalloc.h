@@ -19,7 +19,7 @@ extern "C" {
 #define SYN_NOALLOC_MAX_N 262144
 
 // out = x @ W^T for one 4-bit weight matrix in the tiled device layout (qw/sm as written by
-// q4_quantize / q4_rows_to_tiled).  x: bf16 [rows, ldx] with rows in 1..64, K % 64 == 0,
+// q4_quantize / q4_rows_to_tiled).  x: bf16 [rows, ldx] with rows in 1..64, K % 128 == 0,
 // N % 64 == 0, 16-byte aligned rows.  mode: 0 bf16 store [rows, N]; 1 SwiGLU of
 // interleaved gate/up rows, bf16 [rows, N/2]; 3 f32 accumulate into out [rows, N];
 // 5 f32 store [rows, N].  Work is queued on `stream`.

@@ -80,6 +80,8 @@ cudaError_t launch_tp_reduce_norm(const EpArgs& a, int64_t off_recv, int64_t off
 cudaError_t launch_ep_combine(const EpArgs& a, float* x, const float* wn, void* hout, float eps, int T,
                               cudaStream_t s);
 cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s);
+// Split plan of the dense decode GEMV (see q4_gemv.cu); false if the shape is unsupported.
+bool q4_gemv_dense_plan(int N, int K, int rows, int* nt, int* kr, size_t* ws_floats);
 cudaError_t launch_q4_gemv_dense(const GemvArgs& a, float* ws, unsigned* counters, size_t ws_floats,
                                  cudaStream_t s);
 

@@ -551,7 +551,7 @@ void verify_accept(torch::Tensor logits, torch::Tensor draft, torch::Tensor temp
 void q4_gemv_dense(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
                    torch::Tensor out, int64_t N, int64_t K, int64_t mode, torch::Tensor ws, torch::Tensor counters) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x");
-  TORCH_CHECK(N % 64 == 0 && K % 64 == 0 && x.size(1) == K, "q4_gemv_dense shapes (N%64, K%64)");
+  TORCH_CHECK(N % 64 == 0 && K % 128 == 0 && x.size(1) == K, "q4_gemv_dense shapes (N%64, K%128)");
   TORCH_CHECK(x.size(0) <= 64, "q4_gemv_dense: at most 64 rows");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0 && (x.stride(0) * 2) % 16 == 0,
               "x rows must be 16-byte aligned");
@@ -579,4 +579,12 @@ void q4_gemv_dense(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs
                                       (size_t)ws.numel(), cur_stream()));
 }
 
+int64_t q4_gemv_dense_ws(int64_t N, int64_t K, int64_t rows) {
+  int nt, kr;
+  size_t need;
+  if (!q4_gemv_dense_plan((int)N, (int)K, (int)rows, &nt, &kr, &need)) return -1;
+  return (int64_t)need;
+}
+
 }  // namespace syn
+

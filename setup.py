@@ -25,6 +25,11 @@ def _sources():
 
 CXX_FLAGS = ["-O3", "-std=c++17", "-fno-strict-aliasing", "-Wno-unused-function"]
 LIBS = ["rt"]
+# Link the shared libstdc++ that torch itself uses.  A toolchain whose libstdc++.so dev link
+# does not resolve falls back to libstdc++.a, and a second, static copy of the C++ runtime
+# in the process breaks iostream locale facets (formatting a number in an error message
+# then crashes).
+LINK_FLAGS = ["-l:libstdc++.so.6"]
 NVCC_FLAGS = [
     "-O3",
     "-std=c++17",
@@ -47,6 +52,7 @@ setup(
             include_dirs=[os.path.join(ROOT, "csrc", "include"), os.path.join(ROOT, "csrc")],
             extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
             libraries=LIBS,
+            extra_link_args=LINK_FLAGS,
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},

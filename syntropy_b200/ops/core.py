@@ -94,11 +94,12 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
             out.copy_(y)
         return out
     T = x.shape[0]
-    if isinstance(W, Q4Weight) and _DENSE_V5[1] <= T <= DECODE_ROWS_MAX and W.N % 64 == 0 and _DENSE_V5[0]:
+    if isinstance(W, Q4Weight) and _DENSE_V5[1] <= T <= DECODE_ROWS_MAX and W.N % 64 == 0 and W.K % 128 == 0 \
+            and _DENSE_V5[0]:
         kmode = {GEMV_STORE: 0, GEMV_SWIGLU: 1, GEMV_ADD_F32: 3}[mode]
         if kmode == 0 and out.dtype == torch.float32:
             kmode = 5
-        ws, ctr = _dense_workspace(x.device, W.N, T)
+        ws, ctr = _dense_workspace(x.device, W.N, T, W.K)
         ptrs = _ptrs(W)
         ext().q4_gemv_dense(x, ptrs[0], ptrs[1], _identity_off(T, x.device), out, W.N, W.K, kmode, ws, ctr)
         _launched()
@@ -147,14 +148,14 @@ _DENSE_V5 = [__import__("os").environ.get("SYN_DENSE_V5", "1") == "1",
 _DENSE_WS: dict = {}
 
 
-def _dense_workspace(dev, N: int, T: int):
-    """Split-K workspace (f32) and arrival counters of the dense GEMV, grown on demand
-    (sized for 16 K slices x 32 tokens of the widest matrix seen)."""
+def _dense_workspace(dev, N: int, T: int, K: int):
+    """Split-K workspace (f32) and arrival counters of the dense GEMV, grown on demand to the
+    largest split planned so far on this device."""
     key = str(dev)
-    need = 16 * 32 * N
+    need = max(0, ext().q4_gemv_dense_ws(N, K, min(T, 64)))
     ws, ctr = _DENSE_WS.get(key, (None, None))
     if ws is None or ws.numel() < need or ctr.numel() < N // 64:
-        ws = torch.empty(max(need, ws.numel() if ws is not None else 0), dtype=torch.float32, device=dev)
+        ws = torch.empty(max(need, ws.numel() if ws is not None else 1), dtype=torch.float32, device=dev)
         ctr = torch.zeros(max(N // 64, ctr.numel() if ctr is not None else 0), dtype=torch.int32, device=dev)
         _DENSE_WS[key] = (ws, ctr)
     return ws, ctr

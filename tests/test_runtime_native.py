@@ -153,3 +153,13 @@ def test_numa_binding_from_fake_nvml():
             raise RuntimeError("no driver")
 
     assert numa_cpus(0, Broken()) is None
+
+
+def test_error_message_with_numbers_raises():
+    """A C++ check whose message formats numbers must raise, not crash: the extension has to
+    share the process's one C++ runtime (a second, static copy breaks iostream formatting)."""
+    import pytest
+    import torch
+    from syntropy_b200._ext import ext
+    with pytest.raises(RuntimeError, match="N=10 K=64"):
+        ext().q4_rows_to_tiled_cpu(torch.zeros(10 * 2 * 20, dtype=torch.uint8), 10, 64)

@@ -45,7 +45,7 @@ def test_noalloc_matches_torch_op(cuda, T, N, K, mode):
     ptrs = (torch.tensor([q.qw.data_ptr()], dtype=torch.int64, device=cuda),
             torch.tensor([q.sm.data_ptr()], dtype=torch.int64, device=cuda))
     off = torch.tensor([0, T], dtype=torch.int32, device=cuda)
-    ws = torch.empty(16 * 32 * N, dtype=torch.float32, device=cuda)
+    ws = torch.empty(max(1, ext().q4_gemv_dense_ws(N, K, T)), dtype=torch.float32, device=cuda)
     ctr = torch.zeros(N // 64, dtype=torch.int32, device=cuda)
     base = torch.randn(T, ncols, device=cuda).to(dt) if mode == 3 else torch.zeros(T, ncols, dtype=dt, device=cuda)
     want = base.clone()
