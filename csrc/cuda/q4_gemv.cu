@@ -992,6 +992,9 @@ bool q4_gemv_dense_plan(int N, int K, int rows, int* nt_out, int* kr_out, size_t
   *nt_out = nt;
   *kr_out = kr;
   *ws_floats_out = ksplit > 1 ? (size_t)ksplit * nt * 8 * (size_t)N : 0;
+  int nt6, ks6;
+  size_t ws6;
+  if (q4_gemv6_plan(N, K, rows, &nt6, &ks6, &ws6) && ws6 > *ws_floats_out) *ws_floats_out = ws6;  // either kernel fits
   return true;
 }
 
@@ -999,6 +1002,17 @@ bool q4_gemv_dense_plan(int N, int K, int rows, int* nt_out, int* kr_out, size_t
 // the planned size; counters: N/64 zeroed unsigned ints (left zeroed on exit).
 cudaError_t launch_q4_gemv_dense(const GemvArgs& a, float* ws, unsigned* counters, size_t ws_floats,
                                  cudaStream_t s) {
+  // Streaming v6 for large matrices (>= 64M weights: many row blocks, long K), one-slice v5
+  // otherwise (measured on B200 at the Qwen3-235B and Llama-3-70B decode shapes).
+  // SYN_DENSE_KERNEL=5/6 forces one of them.
+  static int kernel = -1;
+  if (kernel < 0) {
+    const char* v = getenv("SYN_DENSE_KERNEL");
+    kernel = v ? atoi(v) : 0;
+  }
+  const bool big = (long long)a.N * a.K >= (64ll << 20);
+  if (a.K % 256 == 0 && (kernel == 6 || (kernel == 0 && big)))
+    return launch_q4_gemv_dense6(a, ws, counters, ws_floats, s);
   int nt, kr;
   size_t need;
   if (!q4_gemv_dense_plan(a.N, a.K, a.nt_hint * 8 < 64 ? a.nt_hint * 8 : 64, &nt, &kr, &need))
@@ -1008,6 +1022,276 @@ cudaError_t launch_q4_gemv_dense(const GemvArgs& a, float* ws, unsigned* counter
   if (nt == 2) return launch_v5_kr<2>(a, kr, ws, counters, s);
   if (nt == 4) return launch_v5_kr<4>(a, kr, ws, counters, s);
   return launch_v5_kr<8>(a, kr, ws, counters, s);
+}
+
+// ---------------------------------------------------------------------------------------
+// v6 (dense layers, 1..64 tokens, large matrices): CTA = 8 warps = 128 output rows that
+// stream their K range in rounds of G 64-column groups through an ST-stage cp.async ring in
+// shared memory: each stage holds the round's activation chunk (shared by the 8 warps) and
+// the 8 warps' packed weights and scales, so ST-1 rounds of weights are always in flight
+// while one is computed.  The round's 32-column block sums are computed once per CTA.  K is
+// split over gridDim.y CTAs only when the row blocks alone do not fill the GPU; partials
+// then go through the f32 workspace and the last CTA of a row block reduces in slice order.
+template <int NT, int G, int ST>
+__global__ void __launch_bounds__(256, 1) q4_gemv6_kernel(GemvArgs a, float* __restrict__ ws,
+                                                       unsigned* __restrict__ counters, int rounds) {
+  constexpr int TT = NT * 8;
+  constexpr int XS = G * 64 + 8;          // x row stride in smem (elements), padded
+  constexpr int XB = TT * XS * 2;         // x bytes per stage
+  constexpr int WB = 8 * G * 512;         // packed nibbles per stage (8 warps)
+  constexpr int SB = 8 * G * 128;         // scale/min pairs per stage
+  constexpr int STB = XB + WB + SB;
+  extern __shared__ __align__(16) uint8_t sm6[];
+  float* xsum = reinterpret_cast<float*>(sm6 + (size_t)ST * STB);  // [G*2][TT]
+  __shared__ int s_last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int KG = a.K >> 6;
+  const int KS = gridDim.y, ks = blockIdx.y, rb = blockIdx.x;
+  const int tile = rb * 8 + warp;
+  const bool active = tile < a.N / 16;
+  const int T = min(a.tok_off[1] - a.tok_off[0], TT);
+  const int kg_first = ks * rounds * G;
+  const uint8_t* qb = reinterpret_cast<const uint8_t*>(a.qw_ptrs[0]);
+  const uint8_t* sb = reinterpret_cast<const uint8_t*>(a.sm_ptrs[0]);
+  const __nv_bfloat16* xg = reinterpret_cast<const __nv_bfloat16*>(a.x);
+
+  auto issue = [&](int r) {
+    uint8_t* st = sm6 + (size_t)(r % ST) * STB;
+    const int kg0 = kg_first + r * G;
+    for (int idx = threadIdx.x; idx < TT * G * 8; idx += 256) {
+      const int j = idx / (G * 8), c = idx % (G * 8);
+      const int row = min(j, T - 1);
+      const void* src = xg + (int64_t)row * a.ldx + kg0 * 64 + c * 8;
+      const uint32_t dst = (uint32_t)__cvta_generic_to_shared(st + (j * XS + c * 8) * 2);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src));
+    }
+    if (active) {
+      const int64_t tk = (int64_t)tile * KG + kg0;
+#pragma unroll
+      for (int i = 0; i < G; ++i) {
+        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(st + XB + (warp * G + i) * 512 + lane * 16);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(qb + (tk + i) * 512 + lane * 16));
+      }
+      if (lane < 8 * G) {
+        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(st + XB + WB + warp * G * 128 + lane * 16);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(sb + tk * 128 + lane * 16));
+      }
+    }
+    asm volatile("cp.async.commit_group;\n" ::);
+  };
+
+#pragma unroll
+  for (int r = 0; r < ST - 1; ++r) {
+    if (r < rounds) issue(r);
+    else asm volatile("cp.async.commit_group;\n" ::);
+  }
+  float acc[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
+
+  for (int r = 0; r < rounds; ++r) {
+    if (r + ST - 1 < rounds) issue(r + ST - 1);
+    else asm volatile("cp.async.commit_group;\n" ::);
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(ST - 1));
+    __syncthreads();
+    const uint8_t* st = sm6 + (size_t)(r % ST) * STB;
+    const __nv_bfloat16* xs_sm = reinterpret_cast<const __nv_bfloat16*>(st);
+    for (int idx = threadIdx.x; idx < G * 2 * TT; idx += 256) {
+      const int j = idx % TT, blk = idx / TT;
+      const uint4* src = reinterpret_cast<const uint4*>(xs_sm + j * XS + blk * 32);
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 v = src[c];
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_bf16x2(u[e]);
+          sum += f.x + f.y;
+        }
+      }
+      xsum[blk * TT + j] = sum;
+    }
+    __syncthreads();
+    if (active) {
+      const uint32_t lds_base =
+          (uint32_t)__cvta_generic_to_shared(xs_sm + (lane & 7) * XS + (lane >> 3) * 8);
+#pragma unroll
+      for (int i = 0; i < G; ++i) {
+        const uint4 q = *reinterpret_cast<const uint4*>(st + XB + (warp * G + i) * 512 + lane * 16);
+        const uint2 slo = *reinterpret_cast<const uint2*>(st + XB + WB + (warp * G + i) * 128 + g * 8);
+        const uint2 shi = *reinterpret_cast<const uint2*>(st + XB + WB + (warp * G + i) * 128 + (g + 8) * 8);
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          const uint32_t w0 = b ? q.z : q.x;
+          const uint32_t w1 = b ? q.w : q.y;
+          uint32_t af[2][4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            af[0][j] = lop3_and_or(w0 >> (4 * j), 0x000F000Fu, 0x43004300u);
+            af[1][j] = lop3_and_or(w1 >> (4 * j), 0x000F000Fu, 0x43004300u);
+          }
+          const uint32_t vlo = b ? slo.y : slo.x, vhi = b ? shi.y : shi.x;
+          const half2 hl = *reinterpret_cast<const half2*>(&vlo);
+          const half2 hh = *reinterpret_cast<const half2*>(&vhi);
+          const float dlo = __low2float(hl), dhi = __low2float(hh);
+          const float mlo = fmaf(-128.f, dlo, __high2float(hl)), mhi = fmaf(-128.f, dhi, __high2float(hh));
+          const float* xsb = xsum + (i * 2 + b) * TT + 2 * t;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            uint32_t bf[2][2];
+            asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                         : "=r"(bf[0][0]), "=r"(bf[0][1]), "=r"(bf[1][0]), "=r"(bf[1][1])
+                         : "r"(lds_base + (uint32_t)((nt * 8 * XS + i * 64 + b * 32) * 2)));
+            float blk[4] = {0.f, 0.f, 0.f, 0.f};
+            mma_bf16_16816(blk, af[0], bf[0], blk);
+            mma_bf16_16816(blk, af[1], bf[1], blk);
+            const float2 xv = *reinterpret_cast<const float2*>(xsb + nt * 8);
+            acc[nt][0] += fmaf(dlo, blk[0], mlo * xv.x);
+            acc[nt][1] += fmaf(dlo, blk[1], mlo * xv.y);
+            acc[nt][2] += fmaf(dhi, blk[2], mhi * xv.x);
+            acc[nt][3] += fmaf(dhi, blk[3], mhi * xv.y);
+          }
+        }
+      }
+    }
+    __syncthreads();  // the stage is refilled by the next round's issue
+  }
+  asm volatile("cp.async.wait_group 0;\n" ::);
+  // ---- epilogue ----
+  if (KS == 1) {
+    if (active) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int p = nt * 8 + 2 * t + hf;
+          if (p >= T) continue;
+          if (a.mode == GEMV_SWIGLU) {
+            reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)p * (a.N / 2) + tile * 8 + g] =
+                f2bf(silu(acc[nt][hf]) * acc[nt][2 + hf]);
+          } else {
+            gemv_store(a, p, tile * 16 + g, acc[nt][hf]);
+            gemv_store(a, p, tile * 16 + g + 8, acc[nt][2 + hf]);
+          }
+        }
+    }
+    return;
+  }
+  if (active) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int j = nt * 8 + 2 * t + hf;
+        if (j >= T) continue;
+        float* w = ws + ((int64_t)ks * TT + j) * a.N;
+        w[tile * 16 + g] = acc[nt][hf];
+        w[tile * 16 + g + 8] = acc[nt][2 + hf];
+      }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned prev = atomicAdd(&counters[rb], 1u);
+    s_last = (prev == (unsigned)KS - 1);
+    if (s_last) counters[rb] = 0u;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const bool glu = a.mode == GEMV_SWIGLU;
+  const int nrows = min(128, a.N - rb * 128);
+  for (int idx = threadIdx.x; idx < (nrows / 4) * T; idx += 256) {
+    const int c4 = idx % (nrows / 4), j = idx / (nrows / 4);
+    if (glu && (c4 & 2)) continue;  // SwiGLU: rows 8..15 of a 16-row tile are the up halves
+    const int n = rb * 128 + c4 * 4;
+    const float* src = ws + (int64_t)j * a.N + n;
+    const int64_t sstride = (int64_t)TT * a.N;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f), u = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < KS; s0 += 8) {
+      float4 bv[8], bu[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (s0 + i < KS) {
+          bv[i] = __ldcg(reinterpret_cast<const float4*>(src + (s0 + i) * sstride));
+          if (glu) bu[i] = __ldcg(reinterpret_cast<const float4*>(src + (s0 + i) * sstride + 8));
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (s0 + i < KS) {
+          v.x += bv[i].x; v.y += bv[i].y; v.z += bv[i].z; v.w += bv[i].w;
+          if (glu) { u.x += bu[i].x; u.y += bu[i].y; u.z += bu[i].z; u.w += bu[i].w; }
+        }
+      }
+    }
+    if (glu) {
+      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.out) + (int64_t)j * (a.N / 2) + (n >> 4) * 8 + (n & 7);
+      o[0] = f2bf(silu(v.x) * u.x);
+      o[1] = f2bf(silu(v.y) * u.y);
+      o[2] = f2bf(silu(v.z) * u.z);
+      o[3] = f2bf(silu(v.w) * u.w);
+    } else {
+      gemv_store(a, j, n, v.x);
+      gemv_store(a, j, n + 1, v.y);
+      gemv_store(a, j, n + 2, v.z);
+      gemv_store(a, j, n + 3, v.w);
+    }
+  }
+}
+
+template <int NT>
+static cudaError_t launch_v6(const GemvArgs& a, int ksplit, float* ws, unsigned* counters, cudaStream_t s) {
+  constexpr int G = 4, ST = 4;
+  constexpr size_t smem = (size_t)ST * (NT * 8 * (G * 64 + 8) * 2 + 8 * G * 512 + 8 * G * 128) +
+                          (size_t)G * 2 * NT * 8 * 4;
+  static bool set = false;
+  if (!set) {
+    cudaError_t e = cudaFuncSetAttribute(q4_gemv6_kernel<NT, G, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    set = true;
+  }
+  const int rounds = (a.K / 64) / G / ksplit;
+  dim3 grid((unsigned)((a.N / 16 + 7) / 8), (unsigned)ksplit);
+  q4_gemv6_kernel<NT, G, ST><<<grid, 256, smem, s>>>(a, ws, counters, rounds);
+  return cudaGetLastError();
+}
+
+// Split of the streaming dense GEMV: K slices (dividing the K/256 rounds) until the row
+// blocks x slices reach ~2 CTAs per SM; workspace floats as for v5.
+bool q4_gemv6_plan(int N, int K, int rows, int* nt_out, int* ksplit_out, size_t* ws_floats_out) {
+  if (rows < 1 || rows > 64 || N % 64 || K % 256) return false;
+  const int nt = rows <= 8 ? 1 : (rows <= 16 ? 2 : (rows <= 32 ? 4 : 8));
+  const int R = K / 256;
+  const long rb = (N / 16 + 7) / 8;
+  int ks = 1;
+  for (int c = 1; c <= 8; ++c) {
+    if (R % c) continue;
+    ks = c;
+    if (rb * c >= 296) break;
+  }
+  *nt_out = nt;
+  *ksplit_out = ks;
+  *ws_floats_out = ks > 1 ? (size_t)ks * nt * 8 * (size_t)N : 0;
+  return true;
+}
+
+cudaError_t launch_q4_gemv_dense6(const GemvArgs& a, float* ws, unsigned* counters, size_t ws_floats,
+                                  cudaStream_t s) {
+  int nt, ks;
+  size_t need;
+  if (!q4_gemv6_plan(a.N, a.K, a.nt_hint * 8 < 64 ? a.nt_hint * 8 : 64, &nt, &ks, &need))
+    return cudaErrorInvalidValue;
+  if (need > ws_floats) return cudaErrorInvalidValue;
+  if (nt == 1) return launch_v6<1>(a, ks, ws, counters, s);
+  if (nt == 2) return launch_v6<2>(a, ks, ws, counters, s);
+  if (nt == 4) return launch_v6<4>(a, ks, ws, counters, s);
+  return launch_v6<8>(a, ks, ws, counters, s);
 }
 
 cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s) {

@@ -82,6 +82,10 @@ cudaError_t launch_ep_combine(const EpArgs& a, float* x, const float* wn, void* 
 cudaError_t launch_q4_gemv(const GemvArgs& a, cudaStream_t s);
 // Split plan of the dense decode GEMV (see q4_gemv.cu); false if the shape is unsupported.
 bool q4_gemv_dense_plan(int N, int K, int rows, int* nt, int* kr, size_t* ws_floats);
+bool q4_gemv6_plan(int N, int K, int rows, int* nt, int* ksplit, size_t* ws_floats);
+// Streaming dense GEMV (v6): K % 256 == 0; counters: N/128 + 1 zeroed ints.
+cudaError_t launch_q4_gemv_dense6(const GemvArgs& a, float* ws, unsigned* counters, size_t ws_floats,
+                                  cudaStream_t s);
 cudaError_t launch_q4_gemv_dense(const GemvArgs& a, float* ws, unsigned* counters, size_t ws_floats,
                                  cudaStream_t s);
 

@@ -90,6 +90,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="")
     ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--dense", default="", help="extra dense GEMV shapes 'N:K,N:K' (e.g. Llama-3-70B layers)")
     args = ap.parse_args()
     only = set(x for x in args.only.split(",") if x)
     dev = torch.device("cuda:0")
@@ -135,8 +136,9 @@ def main():
                                         route_w=b["pair_w"], qw_ptrs=dn.qw_ptrs, sm_ptrs=dn.sm_ptrs)
         report("moe_down_gemv", timeit(fn), active * dn.N * dn.K * 5 // 8, extra={"active_experts": active})
         del gu, dn
-    for name, N, K in (("qkv_gemv", 9216, 4096), ("o_gemv", 4096, 8192), ("lm_head_gemv", 151936, 4096)):
-        if not want(name):
+    extra = [(f"dense_{n}x{k}", int(n), int(k)) for n, k in (x.split(":") for x in args.dense.split(",") if x)]
+    for name, N, K in [("qkv_gemv", 9216, 4096), ("o_gemv", 4096, 8192), ("lm_head_gemv", 151936, 4096)] + extra:
+        if not want(name) and not name.startswith("dense_"):
             continue
         reps = max(1, int(math.ceil(300e6 / (N * K * 5 / 8))))  # rotate copies to exceed L2
         ws = [Q4Weight.quantize(torch.randn(N, K, device=dev) * 0.02) for _ in range(reps)]

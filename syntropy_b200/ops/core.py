@@ -94,8 +94,8 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
             out.copy_(y)
         return out
     T = x.shape[0]
-    if isinstance(W, Q4Weight) and _DENSE_V5[1] <= T <= DECODE_ROWS_MAX and W.N % 64 == 0 and W.K % 128 == 0 \
-            and _DENSE_V5[0]:
+    if isinstance(W, Q4Weight) and (_DENSE_V5[1] <= T or W.N * W.K >= (64 << 20)) and T <= DECODE_ROWS_MAX \
+            and W.N % 64 == 0 and W.K % 128 == 0 and _DENSE_V5[0]:
         kmode = {GEMV_STORE: 0, GEMV_SWIGLU: 1, GEMV_ADD_F32: 3}[mode]
         if kmode == 0 and out.dtype == torch.float32:
             kmode = 5
