@@ -14,6 +14,7 @@ void register_all(pybind11::module& m) {
   m.def("q4_gemv", &q4_gemv);
   m.def("block_sums", &block_sums);
   m.def("q4_gemv_dense", &q4_gemv_dense);
+  m.def("attn_prefill", &attn_prefill, "causal prefill attention over the paged KV cache (GQA, head_dim 128)");
   m.def("q4_gemv_dense_ws", &q4_gemv_dense_ws, "split-K workspace (floats) of the dense GEMV, -1 if unsupported");
   m.def("rmsnorm", &rmsnorm);
   m.def("moe_combine_rmsnorm", &moe_combine_rmsnorm);

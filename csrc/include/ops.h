@@ -77,6 +77,8 @@ void verify_accept(torch::Tensor logits, torch::Tensor draft, torch::Tensor temp
                    torch::Tensor top_p, torch::Tensor seed, torch::Tensor stream, torch::Tensor counter,
                    torch::Tensor out_tokens, torch::Tensor n_accept);
 int64_t q4_gemv_dense_ws(int64_t N, int64_t K, int64_t rows);
+void attn_prefill(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor block_tables, torch::Tensor cu_q,
+                  torch::Tensor kv_lens, torch::Tensor out, int64_t max_q_len, double scale);
 void q4_gemv_dense(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
                    torch::Tensor out, int64_t N, int64_t K, int64_t mode, torch::Tensor ws, torch::Tensor counters);
 void register_all(pybind11::module& m);

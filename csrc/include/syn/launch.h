@@ -86,6 +86,10 @@ bool q4_gemv6_plan(int N, int K, int rows, int* nt, int* ksplit, size_t* ws_floa
 // Streaming dense GEMV (v6): K % 256 == 0; counters: N/128 + 1 zeroed ints.
 cudaError_t launch_q4_gemv_dense6(const GemvArgs& a, float* ws, unsigned* counters, size_t ws_floats,
                                   cudaStream_t s);
+// ---- causal prefill attention over the paged cache (head_dim 128) ----
+cudaError_t launch_attn_prefill(const void* q, const void* kc, const void* vc, const int32_t* block_tables,
+                                const int32_t* cu_q, const int32_t* kv_lens, void* out, int nseq, int max_q_len,
+                                int Hq, int Hkv, int D, int max_blocks, float scale, cudaStream_t s);
 cudaError_t launch_q4_gemv_dense(const GemvArgs& a, float* ws, unsigned* counters, size_t ws_floats,
                                  cudaStream_t s);
 

@@ -12,7 +12,7 @@ from ..formats.q4 import Q4Weight
 __all__ = [
     "GEMV_STORE", "GEMV_SWIGLU", "GEMV_SCALED_F32", "GEMV_ADD_F32",
     "rms_norm", "embed", "linear", "linear_grouped", "qk_rope_kv_write", "attn_decode",
-    "attn_prefill", "router_logits", "moe_topk", "moe_combine_rmsnorm", "argmax", "sample",
+    "attn_prefill", "attn_prefill_paged", "router_logits", "moe_topk", "moe_combine_rmsnorm", "argmax", "sample",
     "swiglu_interleaved_ref", "interleave_gate_up", "count_launches", "DECODE_ROWS_MAX", "moe_nt_hint", "gemm_grouped", "gemm_status", "block_sums",
 ]
 
@@ -370,6 +370,31 @@ def attn_prefill(q, k, v, cu_seqlens: list[int], out, scale):
         if not q.is_cuda:
             qq, kk, vv = qq.float(), kk.float(), vv.float()
         o = F.scaled_dot_product_attention(qq, kk, vv, is_causal=True, scale=scale, enable_gqa=(Hq != Hkv))
+        out[a:b] = o[0].transpose(0, 1).to(out.dtype)
+    return out
+
+
+def attn_prefill_paged(q, kc, vc, block_tables, cu_q, kv_lens, out, max_q_len: int, scale: float):
+    """Causal prefill attention over the paged cache: query row i of sequence s (rows
+    cu_q[s]..cu_q[s+1]) sits at position kv_lens[s] - q_len + i and attends to keys
+    0..position through block_tables[s].  q/out: [T, Hq, D]; kc/vc: [blocks, Hkv, 16, D]."""
+    if q.is_cuda and q.shape[-1] == 128:
+        ext().attn_prefill(q, kc, vc, block_tables, cu_q, kv_lens, out, max_q_len, scale)
+        _launched()
+        return out
+    Hq, Hkv, D = q.shape[1], kc.shape[1], q.shape[2]
+    cq, kl, bt = cu_q.tolist(), kv_lens.tolist(), block_tables.long()
+    kflat = kc.permute(0, 2, 1, 3).reshape(-1, Hkv, D)
+    vflat = vc.permute(0, 2, 1, 3).reshape(-1, Hkv, D)
+    for s_idx in range(len(kl)):
+        a, b, total = cq[s_idx], cq[s_idx + 1], kl[s_idx]
+        n_new = b - a
+        pos = torch.arange(total, device=q.device)
+        sl = bt[s_idx][pos // 16] * 16 + pos % 16
+        kk, vv = kflat[sl].transpose(0, 1)[None].float(), vflat[sl].transpose(0, 1)[None].float()
+        qq = q[a:b].transpose(0, 1)[None].float()
+        mask = pos[None, :] <= (torch.arange(n_new, device=q.device)[:, None] + (total - n_new))
+        o = F.scaled_dot_product_attention(qq, kk, vv, attn_mask=mask, scale=scale, enable_gqa=(Hq != Hkv))
         out[a:b] = o[0].transpose(0, 1).to(out.dtype)
     return out
 

@@ -186,7 +186,8 @@ class LLMEngine:
             cu.append(cu[-1] + len(s.prompt) - st)
             prefix.append((list(s.blocks), st))
         logits = self.runner.prefill(torch.tensor(toks), torch.tensor(pos), torch.tensor(slots), cu,
-                                     prefix if any(p[1] for p in prefix) else None)
+                                     prefix if any(p[1] for p in prefix) else None,
+                                     block_lists=[list(s.blocks) for s in batch])
         pp = self.runner.pp
         if pp is not None:
             toks_t = torch.zeros(len(batch), dtype=torch.int32, device=self.runner.device)

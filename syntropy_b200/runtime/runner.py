@@ -384,9 +384,10 @@ class ModelRunner:
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()
     def prefill(self, tokens: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor, cu_seqlens: list[int],
-                prefix: list | None = None):
-        """Eager prefill of freshly started sequences (positions from 0).  Returns the
-        last-token logits of each sequence [n_seq, vocab] (f32)."""
+                prefix: list | None = None, block_lists: list | None = None):
+        """Eager prefill of freshly started sequences (or of chunks after a cached prefix).
+        block_lists: each sequence's KV pages (the paged attention kernel reads keys through
+        them).  Returns the last-token logits of each sequence [n_seq, vocab] (f32)."""
         cfg, mw, dev = self.cfg, self.mw, self.device
         T = tokens.numel()
         act = torch.bfloat16 if self.is_cuda else torch.float32
@@ -405,6 +406,17 @@ class ModelRunner:
             q = torch.empty(T, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
             attn = torch.empty(T, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
         self._prefill_x = x
+        paged = None
+        if block_lists is not None and self.is_cuda and not self.is_mla and cfg.head_dim == 128 and T > 0:
+            nseq = len(block_lists)
+            width = max(1, max(len(b) for b in block_lists))
+            bt = torch.zeros(nseq, width, dtype=torch.int32)
+            for r, blocks in enumerate(block_lists):
+                bt[r, :len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
+            starts = [p[1] for p in prefix] if prefix is not None else [0] * nseq
+            q_lens = [cu_seqlens[r + 1] - cu_seqlens[r] for r in range(nseq)]
+            paged = (bt.to(dev), torch.tensor(cu_seqlens, dtype=torch.int32).to(dev),
+                     torch.tensor([st + n for st, n in zip(starts, q_lens)], dtype=torch.int32).to(dev), max(q_lens))
         for i, L in enumerate(mw.layers):
             ops.rms_norm(x, L.attn_norm, cfg.rms_eps, out=h)
             if self.is_mla:
@@ -420,7 +432,10 @@ class ModelRunner:
             ops.linear(h, L.qkv, qkv, ops.GEMV_STORE)
             ops.qk_rope_kv_write(qkv, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, L.q_norm, L.k_norm, cfg.rms_eps,
                                  positions, mw.rope_cos, mw.rope_sin, slots, q, self.kv.k[i], self.kv.v[i])
-            if prefix is None or not any(p[1] for p in prefix):
+            if paged is not None:
+                ops.attn_prefill_paged(q, self.kv.k[i], self.kv.v[i], paged[0], paged[1], paged[2], attn, paged[3],
+                                       self.scale)
+            elif prefix is None or not any(p[1] for p in prefix):
                 kc = self.kv.k[i].permute(0, 2, 1, 3).reshape(-1, cfg.n_kv_heads, cfg.head_dim)[slots]
                 vc = self.kv.v[i].permute(0, 2, 1, 3).reshape(-1, cfg.n_kv_heads, cfg.head_dim)[slots]
                 ops.attn_prefill(q, kc, vc, cu_seqlens, attn, self.scale)
