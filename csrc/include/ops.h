@@ -79,6 +79,12 @@ void verify_accept(torch::Tensor logits, torch::Tensor draft, torch::Tensor temp
 int64_t q4_gemv_dense_ws(int64_t N, int64_t K, int64_t rows);
 void attn_prefill(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor block_tables, torch::Tensor cu_q,
                   torch::Tensor kv_lens, torch::Tensor out, int64_t max_q_len, double scale);
+std::vector<torch::Tensor> f8_quant_act(torch::Tensor x);
+torch::Tensor f8_rows_to_tiled(torch::Tensor q, int64_t N, int64_t K);
+torch::Tensor f8_tiled_to_rows(torch::Tensor tiled, int64_t N, int64_t K);
+void f8_gemv(torch::Tensor xq, torch::Tensor xs, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
+             torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor out, int64_t N, int64_t K, int64_t mode,
+             int64_t nt_hint);
 void q4_gemv_dense(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
                    torch::Tensor out, int64_t N, int64_t K, int64_t mode, torch::Tensor ws, torch::Tensor counters);
 void register_all(pybind11::module& m);

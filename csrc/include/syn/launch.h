@@ -51,7 +51,18 @@ struct GemvArgs {
   int variant;  // 0 auto; 2 force v2 (register pipeline); 3 force v3 (cp.async ring); 4 TMA-fed
   int* status;  // error bits of bounded waits (v4), may be null
   int weights_in_vram;  // 1: every weight pointer is device memory (bulk-copy path allowed)
+  // fp8 path: activations quantised to e4m3 [rows][ldx] with f32 scales [rows][K/128]
+  const uint8_t* xq;
+  const float* xs;
 };
+// ---- fp8 (e4m3, 128x128 weight blocks, 1x128 activation blocks) ----
+// Tiled weight layout: per (16-row tile, 64-column group) 1024 bytes, lane-major in
+// mma.sync m16n8k32 A-fragment order (see fp8.cu); scales f32 [ceil(N/128)][K/128].
+cudaError_t launch_f8_quant_act(const void* x, int rows, int K, int ldx, uint8_t* xq, float* xs, cudaStream_t s);
+cudaError_t launch_f8_rows_to_tiled(const uint8_t* q, int N, int K, uint8_t* tiled, cudaStream_t s);
+cudaError_t launch_f8_tiled_to_rows(const uint8_t* tiled, int N, int K, uint8_t* q, cudaStream_t s);
+// qw_ptrs: tiled e4m3 per expert; sm_ptrs: f32 scales per expert; a.xq / a.xs: quantised x
+cudaError_t launch_f8_gemv(const GemvArgs& a, cudaStream_t s);
 cudaError_t launch_block_sums(const void* x, int rows, int K, int ldx, float* out, cudaStream_t s);
 
 // ---- prefill GEMM on tcgen05 (4-bit weights, grouped) ----

@@ -610,5 +610,71 @@ void attn_prefill(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Te
                                      (int)block_tables.size(1), (float)scale, cur_stream()));
 }
 
+
+std::vector<torch::Tensor> f8_quant_act(torch::Tensor x) {
+  SYN_CHECK_INPUT(x);
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x bf16 [T, K]");
+  const int64_t T = x.size(0), K = x.size(1);
+  TORCH_CHECK(K % 128 == 0, "K % 128 == 0 (1x128 activation blocks), got K=", K);
+  auto xq = torch::empty({T, K}, x.options().dtype(torch::kUInt8));
+  auto xs = torch::empty({T, K / 128}, x.options().dtype(torch::kFloat32));
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_f8_quant_act(x.data_ptr(), (int)T, (int)K, (int)x.stride(0), xq.data_ptr<uint8_t>(),
+                                     xs.data_ptr<float>(), cur_stream()));
+  return {xq, xs};
+}
+
+torch::Tensor f8_rows_to_tiled(torch::Tensor q, int64_t N, int64_t K) {
+  SYN_CHECK_INPUT(q);
+  TORCH_CHECK(q.scalar_type() == torch::kUInt8 && q.numel() == N * K, "e4m3 bytes [N, K]");
+  TORCH_CHECK(N % 16 == 0 && K % 128 == 0, "fp8 tiled layout needs N % 16 == 0 and K % 128 == 0, got N=", N, " K=", K);
+  auto out = torch::empty({N * K}, q.options());
+  const at::cuda::CUDAGuard guard(q.device());
+  SYN_CHECK_CUDA(launch_f8_rows_to_tiled(q.data_ptr<uint8_t>(), (int)N, (int)K, out.data_ptr<uint8_t>(), cur_stream()));
+  return out;
+}
+
+torch::Tensor f8_tiled_to_rows(torch::Tensor tiled, int64_t N, int64_t K) {
+  SYN_CHECK_INPUT(tiled);
+  TORCH_CHECK(tiled.scalar_type() == torch::kUInt8 && tiled.numel() == N * K, "tiled e4m3 bytes");
+  TORCH_CHECK(N % 16 == 0 && K % 128 == 0, "fp8 tiled layout needs N % 16 == 0 and K % 128 == 0, got N=", N, " K=", K);
+  auto out = torch::empty({N, K}, tiled.options());
+  const at::cuda::CUDAGuard guard(tiled.device());
+  SYN_CHECK_CUDA(launch_f8_tiled_to_rows(tiled.data_ptr<uint8_t>(), (int)N, (int)K, out.data_ptr<uint8_t>(), cur_stream()));
+  return out;
+}
+
+void f8_gemv(torch::Tensor xq, torch::Tensor xs, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
+             torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor out, int64_t N, int64_t K, int64_t mode,
+             int64_t nt_hint) {
+  SYN_CHECK_INPUT(xq);
+  TORCH_CHECK(xq.scalar_type() == torch::kUInt8 && xq.dim() == 2 && xq.size(1) == K && xq.stride(1) == 1, "xq");
+  TORCH_CHECK(xs.scalar_type() == torch::kFloat32 && xs.dim() == 2 && xs.size(1) == K / 128 && xs.is_contiguous(),
+              "xs f32 [rows, K/128]");
+  TORCH_CHECK(qw_ptrs.scalar_type() == torch::kInt64 && sm_ptrs.scalar_type() == torch::kInt64 &&
+                  qw_ptrs.numel() == sm_ptrs.numel() && tok_off.numel() == qw_ptrs.numel() + 1,
+              "pointer tables / CSR");
+  TORCH_CHECK(mode == 0 || mode == 1 || mode == 2 || mode == 3 || mode == 5, "f8_gemv: mode ", mode);
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.xq = xq.data_ptr<uint8_t>();
+  a.xs = xs.data_ptr<float>();
+  a.ldx = (int)xq.stride(0);
+  a.qw_ptrs = qw_ptrs.data_ptr<int64_t>();
+  a.sm_ptrs = sm_ptrs.data_ptr<int64_t>();
+  a.tok_off = tok_off.data_ptr<int32_t>();
+  a.tok_idx = tok_idx.numel() ? tok_idx.data_ptr<int32_t>() : nullptr;
+  a.route_w = route_w.numel() ? route_w.data_ptr<float>() : nullptr;
+  TORCH_CHECK(mode != 2 || a.route_w, "mode 2 needs route_w");
+  a.out = out.data_ptr();
+  a.N = (int)N;
+  a.K = (int)K;
+  a.mode = (int)mode;
+  a.E = (int)qw_ptrs.numel();
+  a.nt_hint = (int)nt_hint;
+  const at::cuda::CUDAGuard guard(xq.device());
+  SYN_CHECK_CUDA(launch_f8_gemv(a, cur_stream()));
+}
+
 }  // namespace syn
 

@@ -41,19 +41,34 @@ def quantize_act_fp8(x: torch.Tensor, group: int = BLOCK) -> tuple[torch.Tensor,
 
 @dataclass
 class FP8Weight:
+    """e4m3 weights with one f32 scale per 128x128 block.  On the device the bytes live in
+    the mma-fragment tiled layout (``tiled``, see csrc/cuda/fp8.cu) and ``q`` is None; on the
+    host ``q`` is the row-major e4m3 tensor."""
     N: int
     K: int
-    q: torch.Tensor      # e4m3 [N, K]
-    scale: torch.Tensor  # f32 [ceil(N/128), ceil(K/128)]
+    q: torch.Tensor | None   # e4m3 [N, K] (host)
+    scale: torch.Tensor      # f32 [ceil(N/128), ceil(K/128)]
+    tiled: torch.Tensor | None = None  # uint8 [N*K] (device)
 
     @classmethod
     def quantize(cls, w: torch.Tensor) -> "FP8Weight":
         q, s = quantize_fp8_block(w)
+        if w.is_cuda and w.shape[0] % 16 == 0 and w.shape[1] % 128 == 0:
+            from .._ext import ext
+            t = ext().f8_rows_to_tiled(q.view(torch.uint8).contiguous(), w.shape[0], w.shape[1])
+            return cls(w.shape[0], w.shape[1], None, s.contiguous(), t)
         return cls(w.shape[0], w.shape[1], q, s)
 
+    def rows(self) -> torch.Tensor:
+        """Row-major e4m3 [N, K]."""
+        if self.q is not None:
+            return self.q
+        from .._ext import ext
+        return ext().f8_tiled_to_rows(self.tiled, self.N, self.K).view(torch.float8_e4m3fn)
+
     def dequant(self, dtype=torch.bfloat16) -> torch.Tensor:
-        return dequant_fp8_block(self.q, self.scale).to(dtype)
+        return dequant_fp8_block(self.rows(), self.scale).to(dtype)
 
     @property
     def nbytes(self) -> int:
-        return self.q.numel() + self.scale.numel() * 4
+        return self.N * self.K + self.scale.numel() * 4

@@ -43,13 +43,29 @@ class ExpertBank:
     qw_ptrs: torch.Tensor | None = None  # int64 [E] device
     sm_ptrs: torch.Tensor | None = None
     bank_contiguous: bool = False  # qw/sm hold every expert in order (TMA-streamable bank)
+    f8: torch.Tensor | None = None   # fp8 experts: uint8 [E, N*K] in the tiled e4m3 layout
+    f8s: torch.Tensor | None = None  # f32 [E, ceil(N/128), K/128] block scales
+
+    @property
+    def is_fp8(self) -> bool:
+        return self.f8 is not None
 
     def weight(self, e: int) -> torch.Tensor:
         if self.w is not None:
             return self.w[e]
+        if self.f8 is not None:
+            from ..formats.fp8 import FP8Weight
+            return FP8Weight(self.N, self.K, None, self.f8s[e], self.f8[e]).dequant()
         return Q4Weight(self.N, self.K, self.qw[e], self.sm[e]).dequant()
 
     def build_ptrs(self):
+        if self.f8 is not None:
+            dev = self.f8.device
+            qb, sb = self.f8.data_ptr(), self.f8s.data_ptr()
+            qs, ss = self.f8.stride(0), self.f8s.stride(0) * 4
+            self.qw_ptrs = torch.tensor([qb + e * qs for e in range(self.E)], dtype=torch.int64, device=dev)
+            self.sm_ptrs = torch.tensor([sb + e * ss for e in range(self.E)], dtype=torch.int64, device=dev)
+            return
         if self.qw is None:
             return
         self.bank_contiguous = True
@@ -61,6 +77,8 @@ class ExpertBank:
 
     @property
     def expert_nbytes(self) -> int:
+        if self.f8 is not None:
+            return self.N * self.K + self.f8s[0].numel() * 4
         return self.N * self.K // 32 * 20
 
 
@@ -106,10 +124,10 @@ class ModelWeights:
             nonlocal tot
             if t is None:
                 return
-            if isinstance(t, Q4Weight):
+            if isinstance(t, Q4Weight) or type(t).__name__ == "FP8Weight":
                 tot += t.nbytes
             elif isinstance(t, ExpertBank):
-                for x in (t.qw, t.sm, t.w):
+                for x in (t.qw, t.sm, t.w, t.f8, t.f8s):
                     if x is not None and x.data_ptr() not in seen:
                         seen.add(x.data_ptr())
                         tot += x.numel() * x.element_size()
@@ -189,6 +207,9 @@ def _linear_weight(w: torch.Tensor, quant: str, device):
     if device.type == "cuda":
         if quant == "q4":
             return Q4Weight.quantize(w.to(device))
+        if quant == "fp8" and w.shape[0] % 16 == 0 and w.shape[1] % 128 == 0:
+            from ..formats.fp8 import FP8Weight
+            return FP8Weight.quantize(w.to(device))
         return w.to(device=device, dtype=torch.bfloat16)
     return w.float()
 
@@ -286,6 +307,30 @@ def prepare_weights(cfg: ModelConfig, device="cpu", seed: int = 0, quant: str | 
                     q = Q4Weight.quantize(d)
                     dn.qw[e - ea].copy_(q.qw)
                     dn.sm[e - ea].copy_(q.sm)
+                    del g, u, d, q
+                gu.build_ptrs()
+                dn.build_ptrs()
+            elif is_cuda and quant == "fp8" and H % 128 == 0 and f % 128 == 0:
+                from ..formats.fp8 import FP8Weight
+                gu.f8 = torch.empty(El, 2 * f * H, dtype=torch.uint8, device=device)
+                gu.f8s = torch.empty(El, (2 * f + 127) // 128, H // 128, dtype=torch.float32, device=device)
+                dn.f8 = torch.empty(El, H * f, dtype=torch.uint8, device=device)
+                dn.f8s = torch.empty(El, (H + 127) // 128, f // 128, dtype=torch.float32, device=device)
+                for e in range(ea, eb):
+                    if state_dict is not None:
+                        g = state_dict[pre + "experts.gate"][e].to(gen_dev).float()
+                        u = state_dict[pre + "experts.up"][e].to(gen_dev).float()
+                        d = state_dict[pre + "experts.down"][e].to(gen_dev).float()
+                    else:
+                        g = expert_tensor(cfg, pre + "experts.gate", e, (f, H), seed=seed, device=gen_dev)
+                        u = expert_tensor(cfg, pre + "experts.up", e, (f, H), seed=seed, device=gen_dev)
+                        d = expert_tensor(cfg, pre + "experts.down", e, (H, f), seed=seed, device=gen_dev)
+                    q = FP8Weight.quantize(ops.interleave_gate_up(g, u))
+                    gu.f8[e - ea].copy_(q.tiled)
+                    gu.f8s[e - ea].copy_(q.scale)
+                    q = FP8Weight.quantize(d)
+                    dn.f8[e - ea].copy_(q.tiled)
+                    dn.f8s[e - ea].copy_(q.scale)
                     del g, u, d, q
                 gu.build_ptrs()
                 dn.build_ptrs()

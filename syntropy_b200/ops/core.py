@@ -78,7 +78,33 @@ def _launched(n: int = 1):
 
 
 def _dense_weight(W) -> torch.Tensor:
-    return W.dequant() if isinstance(W, Q4Weight) else W
+    from ..formats.fp8 import FP8Weight
+    return W.dequant() if isinstance(W, (Q4Weight, FP8Weight)) else W
+
+
+def _f8_ptrs(W):
+    p = getattr(W, "_ptrs", None)
+    if p is None:
+        dev = W.tiled.device
+        p = (torch.tensor([W.tiled.data_ptr()], dtype=torch.int64, device=dev),
+             torch.tensor([W.scale.data_ptr()], dtype=torch.int64, device=dev))
+        W._ptrs = p
+    return p
+
+
+def _linear_fp8(x, W, out, mode):
+    """Block-scaled fp8 GEMV: x quantised to e4m3 with 1x128 scales, e4m3 x e4m3 tensor-core
+    products, both scales applied per 128-column block."""
+    T = x.shape[0]
+    kmode = {GEMV_STORE: 0, GEMV_SWIGLU: 1, GEMV_ADD_F32: 3}[mode]
+    if kmode == 0 and out.dtype == torch.float32:
+        kmode = 5
+    xq, xs = ext().f8_quant_act(x if x.stride(-1) == 1 else x.contiguous())
+    qp, sp = _f8_ptrs(W)
+    ext().f8_gemv(xq, xs, qp, sp, _identity_off(T, x.device), _EMPTY_I32(x.device), _EMPTY_F32(x.device), out,
+                  W.N, W.K, kmode, (T + 7) // 8)
+    _launched(2)
+    return out
 
 
 def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: torch.Tensor | None = None):
@@ -94,6 +120,8 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
             out.copy_(y)
         return out
     T = x.shape[0]
+    if getattr(W, "tiled", None) is not None and T <= DECODE_ROWS_MAX and x.dtype == torch.bfloat16:
+        return _linear_fp8(x, W, out, mode)
     if isinstance(W, Q4Weight) and (_DENSE_V5[1] <= T or W.N * W.K >= (64 << 20)) and T <= DECODE_ROWS_MAX \
             and W.N % 64 == 0 and W.K % 128 == 0 and _DENSE_V5[0]:
         kmode = {GEMV_STORE: 0, GEMV_SWIGLU: 1, GEMV_ADD_F32: 3}[mode]
@@ -273,6 +301,12 @@ def linear_grouped(x: torch.Tensor, bank, tok_off: torch.Tensor, tok_idx: torch.
         E = qw_ptrs.numel()
         if nt_hint is None:
             nt_hint = moe_nt_hint(out.shape[0], E)
+        if getattr(bank, "is_fp8", False):
+            xq, xs = e.f8_quant_act(x if x.stride(-1) == 1 else x.contiguous())
+            e.f8_gemv(xq, xs, qw_ptrs, sm_ptrs, tok_off, tok_idx if tok_idx is not None else _EMPTY_I32(x.device),
+                      route_w if route_w is not None else _EMPTY_F32(x.device), out, bank.N, bank.K, kmode, nt_hint)
+            _launched(2)
+            return out
         e.q4_gemv(x, qw_ptrs, sm_ptrs, tok_off,
                   tok_idx if tok_idx is not None else _EMPTY_I32(x.device),
                   route_w if route_w is not None else _EMPTY_F32(x.device),

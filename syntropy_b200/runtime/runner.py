@@ -256,7 +256,7 @@ class ModelRunner:
         ops.rms_norm(x, L.ffn_norm, cfg.rms_eps, out=h)
         nw = nxt.attn_norm if nxt else mw.final_norm
         ep = self.ep
-        if ep is not None and not ep.fused:
+        if ep is not None and (not ep.fused or L.experts_gu.is_fp8):  # the fused EP kernel is 4-bit only
             return self._moe_decode_baseline(L, B, nw)
         pred = L.router_cat is not None
         rw = L.router_cat if pred else L.router
