@@ -14,6 +14,7 @@ void register_all(pybind11::module& m) {
   m.def("q4_gemv", &q4_gemv);
   m.def("block_sums", &block_sums);
   m.def("q4_gemv_dense", &q4_gemv_dense);
+  m.def("mla_decode", &mla_decode, "MLA decode attention (absorbed) over the paged latent cache");
   m.def("f8_quant_act", &f8_quant_act, "bf16 [T, K] -> e4m3 [T, K] + f32 1x128 scales");
   m.def("f8_rows_to_tiled", &f8_rows_to_tiled, "row-major e4m3 bytes -> mma-fragment tiled layout");
   m.def("f8_tiled_to_rows", &f8_tiled_to_rows, "inverse of f8_rows_to_tiled");

@@ -676,5 +676,34 @@ void f8_gemv(torch::Tensor xq, torch::Tensor xs, torch::Tensor qw_ptrs, torch::T
   SYN_CHECK_CUDA(launch_f8_gemv(a, cur_stream()));
 }
 
+
+void mla_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables, torch::Tensor ctx_lens,
+                torch::Tensor out, double scale, torch::Tensor part_o, torch::Tensor part_ml, int64_t pages_per_split) {
+  SYN_CHECK_INPUT(q);
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.size(2) == 576 && q.is_contiguous(),
+              "q bf16 [B, H, 576] = [q_lat | q_pe]");
+  TORCH_CHECK(cache.scalar_type() == torch::kBFloat16 && cache.size(-1) == 576 && cache.is_contiguous() &&
+                  cache.numel() % (16 * 576) == 0,
+              "latent cache bf16 [blocks, 16, 576]");
+  const int64_t B = q.size(0), H = q.size(1);
+  TORCH_CHECK(H % 16 == 0, "heads must be a multiple of 16, got ", H);
+  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.numel() == B * H * 512 && out.is_contiguous(),
+              "out f32 [B, H, 512]");
+  TORCH_CHECK(block_tables.scalar_type() == torch::kInt32 && block_tables.dim() == 2 && block_tables.size(0) >= B &&
+                  block_tables.stride(1) == 1,
+              "block tables int32 [B, max_blocks]");
+  TORCH_CHECK(ctx_lens.scalar_type() == torch::kInt32 && ctx_lens.numel() >= B, "ctx_lens int32 [B]");
+  const int64_t max_blocks = block_tables.size(1);
+  const int64_t n_splits = (max_blocks + pages_per_split - 1) / pages_per_split;
+  TORCH_CHECK(part_o.numel() >= B * H * n_splits * 512 && part_ml.numel() >= B * H * n_splits * 2,
+              "split workspace too small");
+  if (B == 0) return;
+  const at::cuda::CUDAGuard guard(q.device());
+  SYN_CHECK_CUDA(launch_mla_decode(q.data_ptr(), cache.data_ptr(), block_tables.data_ptr<int32_t>(),
+                                   ctx_lens.data_ptr<int32_t>(), part_o.data_ptr<float>(), part_ml.data_ptr<float>(),
+                                   out.data_ptr<float>(), (int)B, (int)H, (int)block_tables.stride(0),
+                                   (int)pages_per_split, (int)n_splits, (float)scale, cur_stream()));
+}
+
 }  // namespace syn
 

@@ -133,6 +133,11 @@ _reg(ModelConfig(name="small-qwen-moe", family="qwen_moe", n_layers=4, hidden=10
                  n_experts=16, top_k=4, moe_ffn=256, weight_quant="q4"))
 _reg(ModelConfig(name="small-llama", family="llama", n_layers=4, hidden=1024, n_heads=8, n_kv_heads=2,
                  head_dim=128, ffn=2048, vocab=4096, rms_eps=1e-5, rope_theta=500000.0, weight_quant="q4"))
+_reg(ModelConfig(name="small-deepseek", family="deepseek3", n_layers=3, hidden=1024, n_heads=16, n_kv_heads=16,
+                 head_dim=192, ffn=2048, vocab=4096, rms_eps=1e-6, rope_theta=10000.0, n_experts=16, top_k=4,
+                 moe_ffn=256, n_shared_experts=1, router_scoring="sigmoid", n_groups=4, topk_groups=2,
+                 routed_scaling=2.5, first_dense_layers=1, q_lora_rank=256, kv_lora_rank=512, qk_rope_dim=64,
+                 qk_nope_dim=128, v_head_dim=128, n_mtp=1, weight_quant="fp8"))
 _reg(ModelConfig(name="tiny-deepseek", family="deepseek3", n_layers=3, hidden=256, n_heads=4, n_kv_heads=4,
                  head_dim=96, ffn=512, vocab=1024, rms_eps=1e-6, rope_theta=10000.0, n_experts=8, top_k=2,
                  moe_ffn=128, n_shared_experts=1, router_scoring="sigmoid", n_groups=4, topk_groups=2,

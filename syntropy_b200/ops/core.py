@@ -12,7 +12,7 @@ from ..formats.q4 import Q4Weight
 __all__ = [
     "GEMV_STORE", "GEMV_SWIGLU", "GEMV_SCALED_F32", "GEMV_ADD_F32",
     "rms_norm", "embed", "linear", "linear_grouped", "qk_rope_kv_write", "attn_decode",
-    "attn_prefill", "attn_prefill_paged", "router_logits", "moe_topk", "moe_combine_rmsnorm", "argmax", "sample",
+    "attn_prefill", "attn_prefill_paged", "mla_decode", "router_logits", "moe_topk", "moe_combine_rmsnorm", "argmax", "sample",
     "swiglu_interleaved_ref", "interleave_gate_up", "count_launches", "DECODE_ROWS_MAX", "moe_nt_hint", "gemm_grouped", "gemm_status", "block_sums",
 ]
 
@@ -430,6 +430,14 @@ def attn_prefill_paged(q, kc, vc, block_tables, cu_q, kv_lens, out, max_q_len: i
         mask = pos[None, :] <= (torch.arange(n_new, device=q.device)[:, None] + (total - n_new))
         o = F.scaled_dot_product_attention(qq, kk, vv, attn_mask=mask, scale=scale, enable_gqa=(Hq != Hkv))
         out[a:b] = o[0].transpose(0, 1).to(out.dtype)
+    return out
+
+
+def mla_decode(q, cache, block_tables, ctx_lens, out, scale: float, part_o, part_ml, pages_per_split: int):
+    """Absorbed MLA decode attention over the paged latent cache: q [B, H, 576] = [q_lat | q_pe]
+    (bf16), cache [blocks, 16, 576]; out f32 [B, H, 512] = softmax(q . row) weighted latent rows."""
+    ext().mla_decode(q, cache, block_tables, ctx_lens, out, scale, part_o, part_ml, pages_per_split)
+    _launched(2)
     return out
 
 

@@ -152,6 +152,16 @@ class ModelRunner:
         # split-KV workspace sized for the largest split count
         self.pages_per_split = 16
         n_splits = (self.max_blocks + self.pages_per_split - 1) // self.pages_per_split
+        if self.is_cuda and cfg.is_mla and cfg.kv_lora_rank == 512 and cfg.qk_rope_dim == 64 and cfg.n_heads % 16 == 0:
+            # MLA decode kernel: enough KV splits for ~2 CTAs per SM at the largest batch
+            per_split = B * (cfg.n_heads // 16)
+            ns = max(1, min(self.max_blocks, -(-296 // per_split)))
+            self.mla_pages_per_split = -(-self.max_blocks // ns)
+            ns = -(-self.max_blocks // self.mla_pages_per_split)
+            self.mla_scale = 1.0 / math.sqrt(cfg.qk_nope_dim + cfg.qk_rope_dim)
+            b["mla_olat"] = torch.zeros(B, cfg.n_heads, 512, dtype=torch.float32, device=dev)
+            b["mla_po"] = torch.zeros(B * cfg.n_heads * ns * 512, dtype=torch.float32, device=dev)
+            b["mla_pml"] = torch.zeros(B * cfg.n_heads * ns * 2, dtype=torch.float32, device=dev)
         if self.is_cuda and not cfg.is_mla:
             b["part_o"] = torch.zeros(B * cfg.n_kv_heads * n_splits * 16 * cfg.head_dim, dtype=torch.float32,
                                       device=dev)
@@ -218,10 +228,18 @@ class ModelRunner:
         pos = d["pos"][:B]
         q_lat, q_pe, lat = mla_qkv(cfg, L.mla, h, pos, self.mw.rope_cos, self.mw.rope_sin)
         cache = self.kv.k[i].view(-1, self.kv.k[i].shape[-1])
-        sl = d["slot"][:B]
-        ok = sl >= 0
-        cache[sl[ok].long()] = lat[ok].to(cache.dtype)
+        sl = d["slot"][:B].long()
+        # padding rows (slot -1) write into the null page: no host sync, capturable
+        cache.index_copy_(0, torch.where(sl >= 0, sl, torch.zeros_like(sl)), lat.to(cache.dtype))
         out = b["attn"][:B].view(B, -1)
+        if "mla_olat" in b:
+            qcat = torch.cat([q_lat, q_pe], -1).to(torch.bfloat16).contiguous()
+            o_lat = b["mla_olat"][:B]
+            ops.mla_decode(qcat, self.kv.k[i], d["block_tables"][:B], d["ctx_len"][:B], o_lat, self.mla_scale,
+                           b["mla_po"], b["mla_pml"], self.mla_pages_per_split)
+            out.copy_(torch.einsum("thc,hvc->thv", o_lat, L.mla["w_uv"]).reshape(B, -1))
+            ops.linear(out, L.o, b["x"][:B], ops.GEMV_ADD_F32)
+            return
         bs = self.block_size
         for r in range(B):
             n = int(d["ctx_len"][r])
