@@ -98,8 +98,9 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="dev only: override layer count (invalid headline)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--baseline", action="store_true", help="NCCL all-gather/reduce-scatter MoE data plane")
-    ap.add_argument("--expert-cache-frac", type=float, default=0.6,
-                    help="VRAM-resident share of each rank's experts (named config: 0.6; rest in pinned host RAM)")
+    ap.add_argument("--expert-cache-frac", type=float, default=None,
+                    help="VRAM-resident share of each rank's experts (Qwen3 config: 0.6, rest in pinned host RAM; "
+                         "others: 1.0)")
     ap.add_argument("--no-uncapped", action="store_true", help="skip the extra all-resident measurement")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -108,6 +109,8 @@ def main():
     args.batch = args.batch or db
     args.prompt = args.prompt or dp
     args.decode = args.decode or dd
+    if args.expert_cache_frac is None:
+        args.expert_cache_frac = 0.6 if args.model == "qwen3-235b-a22b" else 1.0
 
     import torch
 
@@ -175,7 +178,8 @@ def main():
     if args.expert_cache_frac < 1.0 and cfg.is_moe:
         from syntropy_b200.experts.cache import ExpertCache
         cache = ExpertCache(mw.layers, args.expert_cache_frac, dev)
-    graphs = not ((ep is not None and not ep.fused) or (tp is not None and not tp.fused) or pp is not None)
+    fp8_ep = ep is not None and cfg.weight_quant == "fp8"  # fp8 experts use the NCCL row exchange, eagerly
+    graphs = not ((ep is not None and not ep.fused) or fp8_ep or (tp is not None and not tp.fused) or pp is not None)
     runner = ModelRunner(mw, max_batch=B, max_seq_len=max_len + 16, ep=ep, tp=tp, pp=pp, use_graphs=graphs)
     runner.expert_cache = cache
     eng = LLMEngine(runner, max_prefill_tokens=8192, dist_ctx=ctx)
@@ -249,7 +253,7 @@ def main():
     wdesc = {"q4": "4-bit block weights (32-elem, fp16 scale+min)", "bf16": "bf16 weights",
              "fp8": "fp8 e4m3 weights, 128x128 block scales"}.get(wq, wq)
     if cfg.is_moe:
-        par = (f"ep{world}+dp-attention" + ("" if ep is None or ep.fused else " (nccl baseline)")) \
+        par = (f"ep{world}+dp-attention" + ("" if ep is None or (ep.fused and not fp8_ep) else " (nccl baseline)")) \
             if world > 1 else "single-gpu"
     else:
         par = "single-gpu" if world == 1 else (f"tp{tp_size}" + (f"xpp{args.pp}" if args.pp > 1 else "") +

@@ -130,7 +130,8 @@ class ModelRunner:
         if cfg.is_moe:
             E, k = cfg.n_experts, cfg.top_k
             ep = self.ep
-            if ep is not None and not ep.fused:
+            fp8_experts = any(L.experts_gu is not None and L.experts_gu.is_fp8 for L in self.mw.layers)
+            if ep is not None and (not ep.fused or fp8_experts):  # NCCL all-gather / reduce-scatter rows
                 B = B * ep.N  # baseline routes every rank's rows on every rank
                 b["h_all"] = torch.zeros(B, H, dtype=act, device=dev)
                 b["x_part"] = torch.zeros(B, H, dtype=torch.float32, device=dev)
