@@ -91,26 +91,70 @@ class ExpertCache:
             b.n_res = b.E
         self.frac = 1.0
         self._staging = None
+        self._issued = {}
         torch.cuda.empty_cache()
 
     def staged_ptrs(self, L):
         """Pointer tables with every expert of layer L in VRAM: residents in place, host
-        experts copied (copy engine) into a staging bank shared by all layers.  Used by
-        prefill, whose GEMM streams weights with bulk copies that must read device memory."""
+        experts copied into one of two staging banks.  Used by prefill, whose GEMM streams
+        weights with TMA copies that must read device memory.
+
+        The copies run on a side stream, double-buffered across layers: when layer i asks for
+        its tables, the copy of layer i+1's host experts is issued into the other bank, so it
+        crosses PCIe while layer i computes.  Layers are asked for in order within one prefill
+        pass; a bank is refilled only after the compute stream has passed the layer that read
+        it (events)."""
         b = L.expert_tier
-        nh = b.E - b.n_res
-        if nh == 0:
+        if b.E - b.n_res == 0:
             return (L.experts_gu.qw_ptrs, L.experts_gu.sm_ptrs), (L.experts_down.qw_ptrs, L.experts_down.sm_ptrs)
+        if not b.cuda:
+            return self._host_ptrs(L)
         if self._staging is None:
-            self._staging = []
-            for p in b.parts:
-                self._staging.append({"q": torch.empty_like(p["qh"], device=self.device),
-                                      "s": torch.empty_like(p["sh"], device=self.device)})
+            self._staging = [[{"q": torch.empty_like(p["qh"], device=self.device),
+                               "s": torch.empty_like(p["sh"], device=self.device)} for p in b.parts]
+                             for _ in range(2)]
+            self._copy_stream = torch.cuda.Stream(device=self.device)
+            self._ev_free = [None, None]
+            self._issued = {}  # layer index -> (bank, copy-done event)
+            self._last = None
+        li = next(i for i, X in enumerate(self.layers) if X is L)
+        cur = torch.cuda.current_stream(self.device)
+        if self._last is not None and self._last in self._issued:
+            # every kernel of the previously asked layer is enqueued: its bank is free after them
+            ev = torch.cuda.Event()
+            ev.record(cur)
+            self._ev_free[self._issued[self._last][0]] = ev
+        if self._last is not None and li <= self._last:  # a new prefill pass: start over
+            self._issued = {}
+        self._last = li
+        if li not in self._issued:
+            self._issue(li, li % 2)
+        buf, done = self._issued[li]
+        cur.wait_event(done)
+        nxt = self.layers[li + 1].expert_tier if li + 1 < len(self.layers) else None
+        if nxt is not None and nxt.E > nxt.n_res:
+            self._issue(li + 1, 1 - buf)
+        return self._ptrs_for(L, buf)
+
+    def _issue(self, li, buf):
+        b = self.layers[li].expert_tier
+        s = self._copy_stream
+        if self._ev_free[buf] is not None:
+            s.wait_event(self._ev_free[buf])
+        with torch.cuda.stream(s):
+            for which, p in enumerate(b.parts):
+                st = self._staging[buf][which]
+                st["q"].copy_(p["qh"], non_blocking=True)
+                st["s"].copy_(p["sh"], non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(s)
+        self._issued[li] = (buf, done)
+
+    def _ptrs_for(self, L, buf):
+        b = L.expert_tier
         out = []
         for which, p in enumerate(b.parts):
-            st = self._staging[which]
-            st["q"].copy_(p["qh"], non_blocking=True)
-            st["s"].copy_(p["sh"], non_blocking=True)
+            st = self._staging[buf][which]
             qp, sp = [], []
             for e in range(b.E):
                 slot = b.slot_of[e]
@@ -123,6 +167,20 @@ class ExpertCache:
                     sp.append(st["s"].data_ptr() + h * st["s"].stride(0) * 2)
             out.append((torch.tensor(qp, dtype=torch.int64, device=self.device),
                         torch.tensor(sp, dtype=torch.int64, device=self.device)))
+        return out[0], out[1]
+
+    def _host_ptrs(self, L):
+        """CPU banks: the tables point at the resident and host rows themselves."""
+        b = L.expert_tier
+        out = []
+        for p in b.parts:
+            qp, sp = [], []
+            for e in range(b.E):
+                slot = b.slot_of[e]
+                src_q, src_s, r = (p["qv"], p["sv"], slot) if slot >= 0 else (p["qh"], p["sh"], b.host_of[e])
+                qp.append(src_q.data_ptr() + r * src_q.stride(0) * 4)
+                sp.append(src_s.data_ptr() + r * src_s.stride(0) * 2)
+            out.append((torch.tensor(qp, dtype=torch.int64), torch.tensor(sp, dtype=torch.int64)))
         return out[0], out[1]
 
     @property
