@@ -102,6 +102,8 @@ def main():
                     help="VRAM-resident share of each rank's experts (Qwen3 config: 0.6, rest in pinned host RAM; "
                          "others: 1.0)")
     ap.add_argument("--no-uncapped", action="store_true", help="skip the extra all-resident measurement")
+    ap.add_argument("--no-mtp", action="store_true", help="models with an MTP head: plain decoding instead of "
+                    "MTP drafting + batched verification")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -180,9 +182,16 @@ def main():
         cache = ExpertCache(mw.layers, args.expert_cache_frac, dev)
     fp8_ep = ep is not None and cfg.weight_quant == "fp8"  # fp8 experts use the NCCL row exchange, eagerly
     graphs = not ((ep is not None and not ep.fused) or fp8_ep or (tp is not None and not tp.fused) or pp is not None)
-    runner = ModelRunner(mw, max_batch=B, max_seq_len=max_len + 16, ep=ep, tp=tp, pp=pp, use_graphs=graphs)
+    use_mtp = cfg.n_mtp > 0 and mw.mtp is not None and not args.no_mtp and pp is None and tp is None
+    # MTP verify windows hold 2 rows per sequence
+    runner = ModelRunner(mw, max_batch=B * (2 if use_mtp else 1), max_seq_len=max_len + 16, ep=ep, tp=tp, pp=pp,
+                         use_graphs=graphs)
     runner.expert_cache = cache
-    eng = LLMEngine(runner, max_prefill_tokens=8192, dist_ctx=ctx)
+    spec = None
+    if use_mtp:
+        from syntropy_b200.runtime.spec import MTPDrafter, SpecConfig
+        spec = SpecConfig(drafter=MTPDrafter(runner))
+    eng = LLMEngine(runner, max_prefill_tokens=8192, dist_ctx=ctx, spec=spec)
     g = torch.Generator().manual_seed(1234)
     all_prompts = [torch.randint(0, cfg.vocab, (args.prompt,), generator=g).tolist() for _ in range(args.batch)]
     prompts = all_prompts[rank::world] if cfg.is_moe else all_prompts
@@ -220,17 +229,37 @@ def main():
     # timed decode steps through the engine: device time = sum of CUDA-event-bracketed
     # graph replays; e2e = wall time of the same steps (descriptor H2D + tokens D2H)
     runner.time_events = []
+    step_events = []
+    tok0, acc0, dr0 = eng.stats["decode_tokens"], eng.stats.get("spec_accepted", 0), eng.stats.get("spec_drafted", 0)
     with ClockSampler(local) as clk:
         torch.cuda.synchronize()
         te = time.perf_counter()
         for _ in range(args.steps):
-            eng.step()
+            if spec is not None:  # a step is the verify pass plus the MTP draft pass: time both
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                eng.step()
+                e1.record()
+                step_events.append((e0, e1))
+            else:
+                eng.step()
         torch.cuda.synchronize()
         e2e_s = time.perf_counter() - te
-    dev_ms = sum(a.elapsed_time(b) for a, b in runner.time_events)
-    assert len(runner.time_events) == args.steps
+    if spec is not None:
+        dev_ms = sum(a.elapsed_time(b) for a, b in step_events)
+    else:
+        dev_ms = sum(a.elapsed_time(b) for a, b in runner.time_events)
+        assert len(runner.time_events) == args.steps
     dev_ms = max_over_ranks(ctx, dev_ms)
     e2e_s = max_over_ranks(ctx, e2e_s)
+    from syntropy_b200.parallel.dist import sum_over_ranks
+    timed_tokens = sum_over_ranks(ctx, float(eng.stats["decode_tokens"] - tok0))
+    mtp_info = None
+    if spec is not None:
+        acc = sum_over_ranks(ctx, float(eng.stats["spec_accepted"] - acc0))
+        drf = sum_over_ranks(ctx, float(eng.stats["spec_drafted"] - dr0))
+        mtp_info = {"acceptance_rate": round(acc / max(1.0, drf), 4), "drafted": int(drf), "accepted": int(acc),
+                    "tokens_per_seq_step": round(timed_tokens / (args.batch * args.steps), 4)}
     status = ep.check_status() if ep is not None else 0
     uncapped = None
     if cache is not None and not args.no_uncapped:
@@ -247,8 +276,9 @@ def main():
         uncapped = {"value": round(args.batch * 1e3 / u_ms, 2), "ms_per_step": round(u_ms, 4),
                     "steps": len(runner.time_events), "expert_cache_frac": 1.0}
     ms_step = dev_ms / args.steps
-    value = args.batch * 1e3 / ms_step          # whole-job tokens/s over all ranks
-    e2e_value = args.batch * args.steps / e2e_s
+    # whole-job tokens/s over all ranks (with MTP: the tokens actually emitted)
+    value = (timed_tokens if spec is not None else args.batch * args.steps) * 1e3 / dev_ms
+    e2e_value = (timed_tokens if spec is not None else args.batch * args.steps) / e2e_s
     wq = cfg.weight_quant
     wdesc = {"q4": "4-bit block weights (32-elem, fp16 scale+min)", "bf16": "bf16 weights",
              "fp8": "fp8 e4m3 weights, 128x128 block scales"}.get(wq, wq)
@@ -281,6 +311,8 @@ def main():
         "device_status": status,
         "all_experts_resident": uncapped,
     }
+    if mtp_info is not None:
+        out["mtp"] = mtp_info
     if rank == 0:
         print(json.dumps(out))
     runner.graphs.clear()

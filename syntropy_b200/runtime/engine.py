@@ -231,7 +231,9 @@ class LLMEngine:
         return out.cpu().tolist()
 
     def _decode(self) -> list[StepOutput]:
-        if self.spec is not None and self.dist is None:
+        # Under lockstep ranks every rank runs the same verify window shape (equal live
+        # sequence counts), so the expert-parallel exchanges inside it line up.
+        if self.spec is not None:
             return self._decode_spec()
         return self._decode_plain()
 

@@ -530,12 +530,26 @@ class ModelRunner:
         cache[sl.long()] = lat.to(cache.dtype)
         out = torch.empty(S, cfg.n_heads * cfg.v_head_dim, dtype=act, device=dev)
         bs = self.block_size
-        for r in range(S):
-            n = int(positions[r]) + 1
-            blocks = torch.tensor(block_tables[r][: (n + bs - 1) // bs], device=dev)
-            p_ = torch.arange(n, device=dev)
-            rows = cache[blocks[p_ // bs].long() * bs + p_ % bs]
-            out[r] = mla_attend(cfg, L.mla, q_lat[r:r + 1], q_pe[r:r + 1], rows, 0)[0].to(act)
+        if "mla_olat" in self.buf and S <= self.max_batch:
+            # decode-sized draft pass: the MLA decode kernel over the MTP block's latent cache
+            width = self.desc.h["block_tables"].shape[1]
+            bt = torch.zeros(S, width, dtype=torch.int32)
+            for r in range(S):
+                blk = block_tables[r][:width]
+                bt[r, :len(blk)] = torch.tensor(blk, dtype=torch.int32)
+            ctx = (positions.to(torch.int32) + 1)
+            qcat = torch.cat([q_lat, q_pe], -1).to(torch.bfloat16).contiguous()
+            o_lat = self.buf["mla_olat"][:S]
+            ops.mla_decode(qcat, self.kv.k[li], bt.to(dev), ctx.to(dev), o_lat, self.mla_scale, self.buf["mla_po"],
+                           self.buf["mla_pml"], self.mla_pages_per_split)
+            out.copy_(torch.einsum("thc,hvc->thv", o_lat, L.mla["w_uv"]).reshape(S, -1))
+        else:
+            for r in range(S):
+                n = int(positions[r]) + 1
+                blocks = torch.tensor(block_tables[r][: (n + bs - 1) // bs], device=dev)
+                p_ = torch.arange(n, device=dev)
+                rows = cache[blocks[p_ // bs].long() * bs + p_ % bs]
+                out[r] = mla_attend(cfg, L.mla, q_lat[r:r + 1], q_pe[r:r + 1], rows, 0)[0].to(act)
         ops.linear(out, L.o, x, ops.GEMV_ADD_F32)
         h = ops.rms_norm(x, L.ffn_norm, cfg.rms_eps).to(act)
         if L.is_moe:

@@ -100,3 +100,21 @@ def test_deepseek_fp8_engine(cuda):
         agree += sum(int(x == y) for x, y in zip(ref_next, o))
         total += len(o)
     assert agree / total >= 0.6, (agree, total)
+
+
+def test_deepseek_fp8_mtp_spec(cuda):
+    """MTP drafting + batched verification on the GPU: greedy tokens follow plain greedy
+    decoding (the verify windows run the same model), and acceptance is reported."""
+    from syntropy_b200.runtime.spec import MTPDrafter, SpecConfig
+    cfg = get_config("small-deepseek")
+    mw = prepare_weights(cfg, cuda, seed=9)
+    g = torch.Generator().manual_seed(12)
+    prompts = [torch.randint(0, cfg.vocab, (n,), generator=g).tolist() for n in (20, 41)]
+    sp = SamplingParams(max_tokens=8)
+    want = LLMEngine(ModelRunner(mw, max_batch=4, max_seq_len=128)).generate(prompts, sp)
+    runner = ModelRunner(mw, max_batch=4, max_seq_len=128)
+    eng = LLMEngine(runner, spec=SpecConfig(drafter=MTPDrafter(runner)))
+    got = eng.generate(prompts, sp)
+    same = sum(int(a == b) for x, y in zip(got, want) for a, b in zip(x, y))
+    assert same / sum(len(x) for x in want) >= 0.75, (got, want)
+    assert eng.stats["spec_drafted"] > 0 and 0.0 <= eng.acceptance_rate <= 1.0
