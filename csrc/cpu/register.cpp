@@ -14,6 +14,12 @@ void register_all(pybind11::module& m) {
   m.def("q4_gemv", &q4_gemv);
   m.def("block_sums", &block_sums);
   m.def("q4_gemv_dense", &q4_gemv_dense);
+  m.def("doorbell_wait", &doorbell_wait, "bounded device wait on a flag (error bit 0 on timeout)");
+  m.def("doorbell_ring", &doorbell_ring, "release store of a flag value");
+  m.def("timestamp", &timestamp, "globaltimer sample into out[slot]");
+  m.def("tap_gather", &tap_gather, "rows of a hidden state -> f32 tap buffer");
+  m.def("tap_compare", &tap_compare, "per-row max abs diff and relative L2 of two taps");
+  m.def("kv_pages", &kv_pages, "pack (true) or unpack (false) the K/V pages of a block list");
   m.def("mla_decode", &mla_decode, "MLA decode attention (absorbed) over the paged latent cache");
   m.def("f8_quant_act", &f8_quant_act, "bf16 [T, K] -> e4m3 [T, K] + f32 1x128 scales");
   m.def("f8_rows_to_tiled", &f8_rows_to_tiled, "row-major e4m3 bytes -> mma-fragment tiled layout");

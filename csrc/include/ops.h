@@ -87,6 +87,12 @@ void f8_gemv(torch::Tensor xq, torch::Tensor xs, torch::Tensor qw_ptrs, torch::T
              int64_t nt_hint);
 void mla_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables, torch::Tensor ctx_lens,
                 torch::Tensor out, double scale, torch::Tensor part_o, torch::Tensor part_ml, int64_t pages_per_split);
+void doorbell_wait(torch::Tensor flag, int64_t want, double timeout_s, torch::Tensor status, torch::Tensor waited_ns);
+void doorbell_ring(torch::Tensor flag, int64_t value);
+void timestamp(torch::Tensor out, int64_t slot);
+void tap_gather(torch::Tensor src, torch::Tensor idx, torch::Tensor dst);
+void tap_compare(torch::Tensor a, torch::Tensor b, torch::Tensor out);
+void kv_pages(torch::Tensor kc, torch::Tensor vc, torch::Tensor pages, torch::Tensor packed, bool pack);
 void q4_gemv_dense(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
                    torch::Tensor out, int64_t N, int64_t K, int64_t mode, torch::Tensor ws, torch::Tensor counters);
 void register_all(pybind11::module& m);

@@ -105,6 +105,16 @@ cudaError_t launch_attn_prefill(const void* q, const void* kc, const void* vc, c
 cudaError_t launch_mla_decode(const void* q, const void* cache, const int32_t* block_tables, const int32_t* ctx_lens,
                               float* part_o, float* part_ml, float* out, int B, int H, int max_blocks,
                               int pages_per_split, int n_splits, float scale, cudaStream_t s);
+// ---- runtime kernels: doorbells (bounded wait), timestamps, parity taps, KV page pack ----
+cudaError_t launch_doorbell_wait(const uint32_t* flag, uint32_t want, uint64_t timeout_ns, int* status,
+                                 uint64_t* waited_ns, cudaStream_t s);
+cudaError_t launch_doorbell_ring(uint32_t* flag, uint32_t value, cudaStream_t s);
+cudaError_t launch_timestamp(uint64_t* out, int slot, cudaStream_t s);
+cudaError_t launch_tap_gather(const void* src, bool src_bf16, const int32_t* idx, int n, int H, float* dst,
+                              cudaStream_t s);
+cudaError_t launch_tap_compare(const float* a, const float* b, int n, int H, float* out, cudaStream_t s);
+cudaError_t launch_kv_pages(void* kc, void* vc, const int32_t* pages, int n, int64_t page_bytes, void* packed,
+                            bool pack, cudaStream_t s);
 cudaError_t launch_q4_gemv_dense(const GemvArgs& a, float* ws, unsigned* counters, size_t ws_floats,
                                  cudaStream_t s);
 

@@ -705,5 +705,65 @@ void mla_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables
                                    (int)pages_per_split, (int)n_splits, (float)scale, cur_stream()));
 }
 
+
+void doorbell_wait(torch::Tensor flag, int64_t want, double timeout_s, torch::Tensor status, torch::Tensor waited_ns) {
+  SYN_CHECK_INPUT(flag);
+  TORCH_CHECK(flag.scalar_type() == torch::kInt32 && status.scalar_type() == torch::kInt32, "int32 flag / status");
+  TORCH_CHECK(timeout_s > 0 && timeout_s <= 60.0, "doorbell timeout must be in (0, 60] s, got ", timeout_s);
+  const at::cuda::CUDAGuard guard(flag.device());
+  SYN_CHECK_CUDA(launch_doorbell_wait(reinterpret_cast<const uint32_t*>(flag.data_ptr()), (uint32_t)want,
+                                      (uint64_t)(timeout_s * 1e9), status.data_ptr<int32_t>(),
+                                      waited_ns.numel() ? reinterpret_cast<uint64_t*>(waited_ns.data_ptr()) : nullptr,
+                                      cur_stream()));
+}
+
+void doorbell_ring(torch::Tensor flag, int64_t value) {
+  SYN_CHECK_INPUT(flag);
+  TORCH_CHECK(flag.scalar_type() == torch::kInt32, "int32 flag");
+  const at::cuda::CUDAGuard guard(flag.device());
+  SYN_CHECK_CUDA(launch_doorbell_ring(reinterpret_cast<uint32_t*>(flag.data_ptr()), (uint32_t)value, cur_stream()));
+}
+
+void timestamp(torch::Tensor out, int64_t slot) {
+  SYN_CHECK_INPUT(out);
+  TORCH_CHECK(out.scalar_type() == torch::kInt64 && slot >= 0 && slot < out.numel(), "int64 slots");
+  const at::cuda::CUDAGuard guard(out.device());
+  SYN_CHECK_CUDA(launch_timestamp(reinterpret_cast<uint64_t*>(out.data_ptr()), (int)slot, cur_stream()));
+}
+
+void tap_gather(torch::Tensor src, torch::Tensor idx, torch::Tensor dst) {
+  SYN_CHECK_INPUT(src);
+  TORCH_CHECK(src.dim() == 2 && src.is_contiguous() &&
+                  (src.scalar_type() == torch::kBFloat16 || src.scalar_type() == torch::kFloat32), "src [R, H]");
+  TORCH_CHECK(idx.scalar_type() == torch::kInt32 && dst.scalar_type() == torch::kFloat32 &&
+                  dst.size(0) == idx.numel() && dst.size(1) == src.size(1) && dst.is_contiguous(), "idx / dst");
+  const at::cuda::CUDAGuard guard(src.device());
+  SYN_CHECK_CUDA(launch_tap_gather(src.data_ptr(), src.scalar_type() == torch::kBFloat16, idx.data_ptr<int32_t>(),
+                                   (int)idx.numel(), (int)src.size(1), dst.data_ptr<float>(), cur_stream()));
+}
+
+void tap_compare(torch::Tensor a, torch::Tensor b, torch::Tensor out) {
+  SYN_CHECK_INPUT(a);
+  TORCH_CHECK(a.sizes() == b.sizes() && a.dim() == 2 && a.scalar_type() == torch::kFloat32 &&
+                  b.scalar_type() == torch::kFloat32 && a.is_contiguous() && b.is_contiguous(), "a, b f32 [n, H]");
+  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.numel() == a.size(0) * 2, "out f32 [n, 2]");
+  const at::cuda::CUDAGuard guard(a.device());
+  SYN_CHECK_CUDA(launch_tap_compare(a.data_ptr<float>(), b.data_ptr<float>(), (int)a.size(0), (int)a.size(1),
+                                    out.data_ptr<float>(), cur_stream()));
+}
+
+void kv_pages(torch::Tensor kc, torch::Tensor vc, torch::Tensor pages, torch::Tensor packed, bool pack) {
+  SYN_CHECK_INPUT(kc);
+  TORCH_CHECK(kc.sizes() == vc.sizes() && kc.is_contiguous() && vc.is_contiguous() &&
+                  kc.scalar_type() == vc.scalar_type(), "k/v caches");
+  TORCH_CHECK(pages.scalar_type() == torch::kInt32 && pages.dim() == 1, "pages int32");
+  const int64_t page_bytes = kc.numel() / kc.size(0) * kc.element_size();
+  TORCH_CHECK(packed.is_contiguous() && packed.numel() * packed.element_size() == pages.numel() * 2 * page_bytes,
+              "packed buffer must hold 2 x pages x page bytes");
+  const at::cuda::CUDAGuard guard(kc.device());
+  SYN_CHECK_CUDA(launch_kv_pages(kc.data_ptr(), vc.data_ptr(), pages.data_ptr<int32_t>(), (int)pages.numel(),
+                                 page_bytes, packed.data_ptr(), pack, cur_stream()));
+}
+
 }  // namespace syn
 

@@ -12,7 +12,8 @@ from ..formats.q4 import Q4Weight
 __all__ = [
     "GEMV_STORE", "GEMV_SWIGLU", "GEMV_SCALED_F32", "GEMV_ADD_F32",
     "rms_norm", "embed", "linear", "linear_grouped", "qk_rope_kv_write", "attn_decode",
-    "attn_prefill", "attn_prefill_paged", "mla_decode", "router_logits", "moe_topk", "moe_combine_rmsnorm", "argmax", "sample",
+    "attn_prefill", "attn_prefill_paged", "mla_decode", "router_logits", "doorbell_wait", "doorbell_ring",
+    "timestamp", "tap_rows", "tap_compare", "kv_pack", "kv_unpack", "moe_topk", "moe_combine_rmsnorm", "argmax", "sample",
     "swiglu_interleaved_ref", "interleave_gate_up", "count_launches", "DECODE_ROWS_MAX", "moe_nt_hint", "gemm_grouped", "gemm_status", "block_sums",
 ]
 
@@ -439,6 +440,70 @@ def mla_decode(q, cache, block_tables, ctx_lens, out, scale: float, part_o, part
     ext().mla_decode(q, cache, block_tables, ctx_lens, out, scale, part_o, part_ml, pages_per_split)
     _launched(2)
     return out
+
+
+def doorbell_wait(flag, want: int, timeout_s: float, status, waited_ns=None):
+    """Bounded device wait until flag[0] >= want (sequence numbers); after timeout_s it sets
+    bit 0 of status[0] and returns, leaving the context usable."""
+    ext().doorbell_wait(flag, want, timeout_s, status,
+                        waited_ns if waited_ns is not None else torch.empty(0, dtype=torch.int64, device=flag.device))
+    _launched()
+
+
+def doorbell_ring(flag, value: int):
+    ext().doorbell_ring(flag, value)
+    _launched()
+
+
+def timestamp(buf, slot: int):
+    """buf[slot] = device global timer (ns), in stream order."""
+    ext().timestamp(buf, slot)
+    _launched()
+
+
+def tap_rows(x, idx, out):
+    """Parity tap: out[i] = f32(x[idx[i]])."""
+    if x.is_cuda:
+        ext().tap_gather(x.contiguous(), idx, out)
+        _launched()
+    else:
+        out.copy_(x[idx.long()].float())
+    return out
+
+
+def tap_compare(a, b):
+    """Per-row (max |a-b|, ||a-b|| / ||b||) of two tap buffers, computed where they live."""
+    if a.is_cuda:
+        out = torch.empty(a.shape[0], 2, device=a.device)
+        ext().tap_compare(a, b, out)
+        _launched()
+        return out
+    d = (a - b).float()
+    return torch.stack([d.abs().amax(-1), d.norm(dim=-1) / b.float().norm(dim=-1).clamp_min(1e-30)], -1)
+
+
+def kv_pack(kc, vc, pages, packed=None):
+    """K/V pages of a block list -> one contiguous buffer [n, 2, page] (offload, migration)."""
+    page = kc[0].numel()
+    if packed is None:
+        packed = torch.empty(pages.numel(), 2, page, dtype=kc.dtype, device=kc.device)
+    if kc.is_cuda:
+        ext().kv_pages(kc, vc, pages, packed, True)
+        _launched()
+    else:
+        packed[:, 0] = kc[pages.long()].reshape(pages.numel(), -1)
+        packed[:, 1] = vc[pages.long()].reshape(pages.numel(), -1)
+    return packed
+
+
+def kv_unpack(packed, kc, vc, pages):
+    """Inverse of kv_pack: writes the packed pages back into the caches at `pages`."""
+    if kc.is_cuda:
+        ext().kv_pages(kc, vc, pages, packed, False)
+        _launched()
+    else:
+        kc[pages.long()] = packed[:, 0].reshape((pages.numel(),) + tuple(kc.shape[1:]))
+        vc[pages.long()] = packed[:, 1].reshape((pages.numel(),) + tuple(vc.shape[1:]))
 
 
 def router_logits(h, W, out):

@@ -163,3 +163,21 @@ def test_error_message_with_numbers_raises():
     from syntropy_b200._ext import ext
     with pytest.raises(RuntimeError, match="N=10 K=64"):
         ext().q4_rows_to_tiled_cpu(torch.zeros(10 * 2 * 20, dtype=torch.uint8), 10, 64)
+
+
+def test_cpu_taps_and_kv_pack():
+    """CPU forms of the parity taps and K/V page pack/unpack (same contracts as the kernels)."""
+    import torch
+    from syntropy_b200 import ops
+    x = torch.randn(6, 32)
+    idx = torch.tensor([5, 1], dtype=torch.int32)
+    out = torch.empty(2, 32)
+    ops.tap_rows(x, idx, out)
+    assert torch.equal(out, x[[5, 1]])
+    assert ops.tap_compare(out, out).abs().max().item() == 0
+    kc, vc = torch.randn(5, 2, 16, 8), torch.randn(5, 2, 16, 8)
+    pages = torch.tensor([4, 0], dtype=torch.int32)
+    packed = ops.kv_pack(kc, vc, pages)
+    k2, v2 = torch.zeros_like(kc), torch.zeros_like(vc)
+    ops.kv_unpack(packed, k2, v2, pages)
+    assert torch.equal(k2[[4, 0]], kc[[4, 0]]) and torch.equal(v2[[4, 0]], vc[[4, 0]])
