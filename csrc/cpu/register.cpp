@@ -53,6 +53,7 @@ void register_all(pybind11::module& m) {
   m.def("tp_reduce_norm", &tp_reduce_norm);
   register_runtime(m);
   register_formats(m);
+  register_dispatcher(m);
 }
 
 }  // namespace syn

@@ -97,5 +97,6 @@ void q4_gemv_dense(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs
                    torch::Tensor out, int64_t N, int64_t K, int64_t mode, torch::Tensor ws, torch::Tensor counters);
 void register_all(pybind11::module& m);
 void register_runtime(pybind11::module& m);
+void register_dispatcher(pybind11::module& m);
 void register_formats(pybind11::module& m);
 }  // namespace syn

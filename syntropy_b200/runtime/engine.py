@@ -15,6 +15,8 @@ from dataclasses import dataclass, field
 
 import torch
 
+from .._ext import ext
+
 from .. import ops
 from .runner import ModelRunner
 
@@ -315,32 +317,18 @@ class LLMEngine:
         kv = r.kv
         seqs = self.running
         B = len(seqs)
-        d = r.desc.h
-        for i, s in enumerate(seqs):
+        pos = []
+        for s in seqs:
             p = s.n_tokens - 1
             kv.ensure(s.blocks, p + 1)
-            d["tokens"][i] = s.output[-1]
-            d["pos"][i] = p
-            d["ctx_len"][i] = p + 1
-            d["slot"][i] = kv.slot(s.blocks, p)
-            bt = d["block_tables"][i]
-            bt[: len(s.blocks)] = torch.tensor(s.blocks, dtype=torch.int32)
-            d["temperature"][i] = s.params.temperature
-            d["top_k"][i] = s.params.top_k
-            d["top_p"][i] = s.params.top_p
-            d["seed"][i] = s.seed
-            d["stream"][i] = s.stream
-            d["counter"][i] = s.rng_counter
-        if r.use_graphs:  # padding rows of the bucket
-            from .runner import bucket_for
-            bb = bucket_for(B)
-            for i in range(B, bb):
-                d["tokens"][i] = 0
-                d["pos"][i] = 0
-                d["ctx_len"][i] = 1
-                d["slot"][i] = -1
-                d["block_tables"][i, 0] = 0
-                d["temperature"][i] = 0.0
+            pos.append(p)
+        from .runner import bucket_for
+        # one native call writes every live row and the bucket's padding rows
+        ext().step_desc_fill(r.desc.host, r.desc.rows, r.desc.max_blocks, [s.output[-1] for s in seqs], pos,
+                             [s.params.top_k for s in seqs], [kv.slot(s.blocks, p) for s, p in zip(seqs, pos)],
+                             [s.seed for s in seqs], [s.stream for s in seqs], [s.rng_counter for s in seqs],
+                             [float(s.params.temperature) for s in seqs], [float(s.params.top_p) for s in seqs],
+                             [s.blocks for s in seqs], bucket_for(B) if r.use_graphs else B)
         nxt = r.decode(B).cpu().tolist()
         # greedy rows take no draw; sampled rows take exactly one
         for s in seqs:

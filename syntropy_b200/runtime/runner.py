@@ -10,6 +10,8 @@ from __future__ import annotations
 import math
 
 import torch
+
+from .._ext import ext
 import torch.nn.functional as F
 
 from .. import ops
@@ -347,9 +349,10 @@ class ModelRunner:
             g = self.graphs.get(bb)
             if g is None:
                 g = self.capture(bb)  # uses (and restores) the host descriptor
-            self.desc.upload()
             ev = self._ev0()
-            g.replay()
+            # native: descriptor upload + graph launch on the current stream
+            ext().step_launch(self.desc.host, self.desc.dev, g.raw_cuda_graph_exec(),
+                              torch.cuda.current_stream(self.device).cuda_stream)
             self._ev1(ev)
         else:
             self.desc.upload()

@@ -181,3 +181,23 @@ def test_cpu_taps_and_kv_pack():
     k2, v2 = torch.zeros_like(kc), torch.zeros_like(vc)
     ops.kv_unpack(packed, k2, v2, pages)
     assert torch.equal(k2[[4, 0]], kc[[4, 0]]) and torch.equal(v2[[4, 0]], vc[[4, 0]])
+
+
+def test_step_desc_fill_matches_python_views():
+    """The native descriptor fill writes the layout the runner's tensor views read; padding
+    rows are inert (slot -1, null page, greedy)."""
+    import torch
+    from syntropy_b200._ext import ext
+    from syntropy_b200.runtime.runner import StepDesc
+    d = StepDesc(8, 5, torch.device("cpu"))
+    ext().step_desc_fill(d.host, 8, 5, [11, 12], [3, 40], [0, 7], [100, 205], [1, 2], [0, 1], [0, 4],
+                         [0.0, 0.7], [1.0, 0.9], [[4, 5], [1, 2, 3]], 4)
+    h = d.h
+    assert h["tokens"][:4].tolist() == [11, 12, 0, 0]
+    assert h["pos"][:4].tolist() == [3, 40, 0, 0]
+    assert h["ctx_len"][:4].tolist() == [4, 41, 1, 1]
+    assert h["slot"][:4].tolist() == [100, 205, -1, -1]
+    assert h["top_k"][:2].tolist() == [0, 7] and h["counter"][:2].tolist() == [0, 4]
+    assert abs(h["temperature"][1].item() - 0.7) < 1e-6 and abs(h["top_p"][1].item() - 0.9) < 1e-6
+    assert h["block_tables"][0, :2].tolist() == [4, 5] and h["block_tables"][1, :3].tolist() == [1, 2, 3]
+    assert h["block_tables"][2, 0].item() == 0
