@@ -102,6 +102,8 @@ def main():
                     help="VRAM-resident share of each rank's experts (Qwen3 config: 0.6, rest in pinned host RAM; "
                          "others: 1.0)")
     ap.add_argument("--no-uncapped", action="store_true", help="skip the extra all-resident measurement")
+    ap.add_argument("--expert-prefetch", type=int, default=1,
+                    help="router-predicted prefetch of host-tier experts during decode (1 on, 0 off)")
     ap.add_argument("--no-mtp", action="store_true", help="models with an MTP head: plain decoding instead of "
                     "MTP drafting + batched verification")
     args = ap.parse_args()
@@ -180,6 +182,8 @@ def main():
     if args.expert_cache_frac < 1.0 and cfg.is_moe:
         from syntropy_b200.experts.cache import ExpertCache
         cache = ExpertCache(mw.layers, args.expert_cache_frac, dev)
+        if args.expert_prefetch:
+            cache.enable_decode_prefetch(cfg.n_experts)
     fp8_ep = ep is not None and cfg.weight_quant == "fp8"  # fp8 experts use the NCCL row exchange, eagerly
     graphs = not ((ep is not None and not ep.fused) or fp8_ep or (tp is not None and not tp.fused) or pp is not None)
     use_mtp = cfg.n_mtp > 0 and mw.mtp is not None and not args.no_mtp and pp is None and tp is None
@@ -301,6 +305,7 @@ def main():
                    "parallelism": par,
                    "expert_cache_frac": args.expert_cache_frac if cfg.is_moe else 1.0,
                    "host_tier_gb": round(cache.host_bytes() / 1e9, 2) if cache is not None else 0.0,
+                   "expert_prefetch": bool(cache is not None and cache.prefetch),
                    "l2": f"inputs larger than L2 ({mw.nbytes() / 1e9:.0f} GB of weights streamed per step per rank)",
                    "weights_gb": round(mw.nbytes() / 1e9, 2), "weight_build_s": round(t_weights, 1)},
         "clocks": clk.summary(),

@@ -14,6 +14,7 @@ void register_all(pybind11::module& m) {
   m.def("q4_gemv", &q4_gemv);
   m.def("block_sums", &block_sums);
   m.def("q4_gemv_dense", &q4_gemv_dense);
+  m.def("expert_prefetch", &expert_prefetch, "router-predicted copy of next-layer host experts into VRAM staging");
   m.def("doorbell_wait", &doorbell_wait, "bounded device wait on a flag (error bit 0 on timeout)");
   m.def("doorbell_ring", &doorbell_ring, "release store of a flag value");
   m.def("timestamp", &timestamp, "globaltimer sample into out[slot]");

@@ -93,6 +93,9 @@ void timestamp(torch::Tensor out, int64_t slot);
 void tap_gather(torch::Tensor src, torch::Tensor idx, torch::Tensor dst);
 void tap_compare(torch::Tensor a, torch::Tensor b, torch::Tensor out);
 void kv_pages(torch::Tensor kc, torch::Tensor vc, torch::Tensor pages, torch::Tensor packed, bool pack);
+void expert_prefetch(torch::Tensor pred, torch::Tensor host_row, int64_t e0, std::vector<torch::Tensor> host,
+                     std::vector<torch::Tensor> stage, std::vector<torch::Tensor> live, std::vector<torch::Tensor> home,
+                     int64_t ctas);
 void q4_gemv_dense(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
                    torch::Tensor out, int64_t N, int64_t K, int64_t mode, torch::Tensor ws, torch::Tensor counters);
 void register_all(pybind11::module& m);

@@ -115,6 +115,11 @@ cudaError_t launch_tap_gather(const void* src, bool src_bf16, const int32_t* idx
 cudaError_t launch_tap_compare(const float* a, const float* b, int n, int H, float* out, cudaStream_t s);
 cudaError_t launch_kv_pages(void* kc, void* vc, const int32_t* pages, int n, int64_t page_bytes, void* packed,
                             bool pack, cudaStream_t s);
+// ---- router-predicted expert prefetch (decode) ----
+cudaError_t launch_expert_prefetch(const int32_t* pred, const int32_t* host_row, int e0, int El,
+                                   const void* const* host, void* const* stage, const int64_t* row_bytes,
+                                   int64_t* const* live, const int64_t* const* home, int n_parts, int ctas,
+                                   cudaStream_t s);
 cudaError_t launch_q4_gemv_dense(const GemvArgs& a, float* ws, unsigned* counters, size_t ws_floats,
                                  cudaStream_t s);
 

@@ -765,5 +765,37 @@ void kv_pages(torch::Tensor kc, torch::Tensor vc, torch::Tensor pages, torch::Te
                                  page_bytes, packed.data_ptr(), pack, cur_stream()));
 }
 
+
+void expert_prefetch(torch::Tensor pred, torch::Tensor host_row, int64_t e0, std::vector<torch::Tensor> host,
+                     std::vector<torch::Tensor> stage, std::vector<torch::Tensor> live, std::vector<torch::Tensor> home,
+                     int64_t ctas) {
+  SYN_CHECK_INPUT(pred);
+  TORCH_CHECK(pred.scalar_type() == torch::kInt32 && host_row.scalar_type() == torch::kInt32 && host_row.is_cuda(),
+              "int32 pred / host_row");
+  const int n = (int)host.size();
+  TORCH_CHECK(n >= 1 && n <= 4 && stage.size() == host.size() && live.size() == host.size() &&
+                  home.size() == host.size(), "1..4 parts");
+  const void* hp[4];
+  void* sp[4];
+  int64_t rb[4];
+  int64_t* lp[4];
+  const int64_t* op[4];
+  const int64_t El = host_row.numel();
+  for (int p = 0; p < n; ++p) {
+    TORCH_CHECK(host[p].is_pinned() && stage[p].is_cuda() && host[p].sizes() == stage[p].sizes() &&
+                    host[p].is_contiguous() && stage[p].is_contiguous(), "host rows pinned, staging rows on device");
+    TORCH_CHECK(live[p].scalar_type() == torch::kInt64 && home[p].scalar_type() == torch::kInt64 &&
+                    live[p].numel() == El && home[p].numel() == El, "pointer tables int64 [El]");
+    hp[p] = host[p].data_ptr();
+    sp[p] = stage[p].data_ptr();
+    rb[p] = host[p].numel() ? host[p].nbytes() / host[p].size(0) : 0;
+    lp[p] = live[p].data_ptr<int64_t>();
+    op[p] = home[p].data_ptr<int64_t>();
+  }
+  const at::cuda::CUDAGuard guard(pred.device());
+  SYN_CHECK_CUDA(launch_expert_prefetch(pred.data_ptr<int32_t>(), host_row.data_ptr<int32_t>(), (int)e0, (int)El, hp,
+                                        sp, rb, lp, op, n, (int)ctas, cur_stream()));
+}
+
 }  // namespace syn
 

@@ -61,6 +61,54 @@ class ExpertCache:
             self.banks.append(b)
             L.expert_tier = b
         self._staging = None
+        self.prefetch = False
+        # CTAs of the prefetch kernel (the rest of the GPU stays with the current layer)
+        self.prefetch_ctas = int(__import__("os").environ.get("SYN_PREFETCH_CTAS", "64"))
+
+    # ------------------------------------------------------------------ staging banks
+    def _ensure_staging(self):
+        if self._staging is not None:
+            return
+        b = next(x for x in self.banks if x.E > x.n_res)
+        self._staging = [[{"q": torch.empty_like(p["qh"], device=self.device),
+                           "s": torch.empty_like(p["sh"], device=self.device)} for p in b.parts]
+                         for _ in range(2)]
+        self._copy_stream = torch.cuda.Stream(device=self.device)
+        self._ev_free = [None, None]
+        self._issued = {}
+        self._last = None
+
+    # ------------------------------------------------------------------ decode prefetch
+    def enable_decode_prefetch(self, n_experts: int):
+        """Router-predicted prefetch for decode: after layer i routes, the experts it predicts
+        for layer i+1 that live in the host tier are copied into a VRAM staging bank on a side
+        stream, and layer i+1's pointer tables are pointed at the copies (csrc/cuda/
+        expert_prefetch.cu).  Each bank keeps its home pointer tables to fall back on."""
+        if not any(b.E > b.n_res for b in self.banks):
+            return False
+        self._ensure_staging()
+        for b in self.banks:
+            b.refresh_home()
+            b.pred = torch.zeros(n_experts, dtype=torch.int32, device=self.device)
+        self.prefetch = True
+        return True
+
+    def decode_prefetch(self, L):
+        """Launch the prefetch of layer L's predicted host experts on the current stream
+        (the caller forks a side stream); L.expert_tier.pred must hold the prediction."""
+        b = L.expert_tier
+        if b.E == b.n_res:
+            return
+        li = next(i for i, X in enumerate(self.layers) if X is L)
+        st = self._staging[li % 2]
+        host, stage, live, home = [], [], [], []
+        for which, p in enumerate(b.parts):
+            host += [p["qh"], p["sh"]]
+            stage += [st[which]["q"], st[which]["s"]]
+            live += [p["bank"].qw_ptrs, p["bank"].sm_ptrs]
+            home += [b.home[which][0], b.home[which][1]]
+        from .._ext import ext
+        ext().expert_prefetch(b.pred, b.host_row_dev, b.e0, host, stage, live, home, self.prefetch_ctas)
 
     def promote_all(self):
         """Move every expert to VRAM (cap lifted) without changing the pointer-table
@@ -90,8 +138,12 @@ class ExpertCache:
             b.host_of = [-1] * b.E
             b.n_res = b.E
         self.frac = 1.0
-        self._staging = None
         self._issued = {}
+        for b in self.banks:
+            if b.home is not None:  # every expert is home now: the prefetch kernel copies nothing
+                b.refresh_home()
+        if not self.prefetch:
+            self._staging = None
         torch.cuda.empty_cache()
 
     def staged_ptrs(self, L):
@@ -109,16 +161,13 @@ class ExpertCache:
             return (L.experts_gu.qw_ptrs, L.experts_gu.sm_ptrs), (L.experts_down.qw_ptrs, L.experts_down.sm_ptrs)
         if not b.cuda:
             return self._host_ptrs(L)
-        if self._staging is None:
-            self._staging = [[{"q": torch.empty_like(p["qh"], device=self.device),
-                               "s": torch.empty_like(p["sh"], device=self.device)} for p in b.parts]
-                             for _ in range(2)]
-            self._copy_stream = torch.cuda.Stream(device=self.device)
-            self._ev_free = [None, None]
-            self._issued = {}  # layer index -> (bank, copy-done event)
-            self._last = None
+        self._ensure_staging()
         li = next(i for i, X in enumerate(self.layers) if X is L)
         cur = torch.cuda.current_stream(self.device)
+        if self._last is None or li <= self._last:
+            # a new prefill pass: the banks may still be read by earlier work (decode-step
+            # prefetch copies included), so the copy stream starts after everything enqueued
+            self._copy_stream.wait_stream(cur)
         if self._last is not None and self._last in self._issued:
             # every kernel of the previously asked layer is enqueued: its bank is free after them
             ev = torch.cuda.Event()
@@ -218,6 +267,8 @@ class _TieredBank:
         self.gu, self.dn = gu, dn
         self.E = gu.E
         self.e0 = gu.e0
+        self.home = None
+        self.host_row_dev = None
         self.n_res = max(0, min(self.E, int(math.floor(frac * self.E + 1e-9))))
         self.slot_of = list(range(self.n_res)) + [-1] * (self.E - self.n_res)  # expert -> vram slot
         self.host_of = [-1] * self.n_res + list(range(self.E - self.n_res))    # expert -> host row
@@ -263,6 +314,22 @@ class _TieredBank:
             bank.qw_ptrs.copy_(new_q)
             bank.sm_ptrs.copy_(new_s)
 
+    def refresh_home(self):
+        """Snapshot the home pointer tables (resident slot or host row per expert) and the
+        host-row map used by the decode prefetch kernel."""
+        rows = torch.tensor([self.host_of[e] if self.slot_of[e] < 0 else -1 for e in range(self.E)],
+                            dtype=torch.int32)
+        if self.home is None:
+            self.home = [(p["bank"].qw_ptrs.clone(), p["bank"].sm_ptrs.clone()) if p is not None else None
+                         for p in self.parts]
+            self.host_row_dev = rows.to(self.parts[0]["bank"].qw_ptrs.device)
+        else:  # in place: captured decode graphs keep reading these tensors
+            for p, hm in zip(self.parts, self.home):
+                if p is not None:
+                    hm[0].copy_(p["bank"].qw_ptrs)
+                    hm[1].copy_(p["bank"].sm_ptrs)
+            self.host_row_dev.copy_(rows)
+
     def resident_mask(self) -> torch.Tensor:
         return torch.tensor([s >= 0 for s in self.slot_of])
 
@@ -289,6 +356,8 @@ class _TieredBank:
         for p in self.parts:
             if p is not None:
                 self._write_ptrs(p["bank"], p["qv"], p["sv"], p["qh"], p["sh"])
+        if self.home is not None:
+            self.refresh_home()
 
     def weight_of(self, which: int, e: int):
         """Dense view of expert e (for the CPU path / tests)."""

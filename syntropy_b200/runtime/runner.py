@@ -82,6 +82,8 @@ class ModelRunner:
         self.pp = pp  # parallel.pp.PPGroup or None
         self.ep = ep  # parallel.ep.EPGroup or None
         self.expert_cache = None  # experts.cache.ExpertCache when a VRAM cap is set
+        self._pf_stream = None    # side stream of the router-predicted expert prefetch
+        self._pf_events = {}
         self.tp = tp  # parallel.tp.TPGroup or None
         self.mw, self.cfg = mw, cfg
         self.device = mw.device
@@ -286,7 +288,26 @@ class ModelRunner:
         rl = b["rlogits"].view(-1)[: B * W].view(B, W)
         ops.router_logits(h, rw, rl)
         mb = self._moe_bufs(B)
+        cache = self.expert_cache
+        nxt_moe = pred and cache is not None and cache.prefetch and layer + 1 < len(mw.layers)
+        if nxt_moe:  # the next layer's prediction goes to its own mask (read by the side stream)
+            mb["pred_mask"] = mw.layers[layer + 1].expert_tier.pred
         ops.moe_topk(rl, cfg, L.router_bias, pred, mb)
+        if nxt_moe:
+            # router-predicted prefetch of layer+1's host experts, overlapping this layer
+            cur = torch.cuda.current_stream(self.device)
+            if self._pf_stream is None:
+                self._pf_stream = torch.cuda.Stream(device=self.device)
+            self._pf_stream.wait_stream(cur)
+            with torch.cuda.stream(self._pf_stream):
+                cache.decode_prefetch(mw.layers[layer + 1])
+                ops.core._launched()
+            ev = torch.cuda.Event()
+            ev.record(self._pf_stream)
+            self._pf_events[layer + 1] = ev
+        ev = self._pf_events.pop(layer, None)
+        if ev is not None:  # this layer's pointer tables and staged experts are ready
+            torch.cuda.current_stream(self.device).wait_event(ev)
         k = cfg.top_k
         gu, dn = L.experts_gu, L.experts_down
         if ep is not None:

@@ -1,0 +1,45 @@
+"""Router-predicted expert prefetch during decode (VRAM cap with a pinned host tier): tokens
+equal the same engine without prefetch (the GEMVs read byte-identical weights, from the
+staging copies instead of host memory), with CUDA graphs; after a step the pointer tables
+of a predicted host expert point into the VRAM staging bank."""
+import pytest
+import torch
+
+from syntropy_b200.experts.cache import ExpertCache
+from syntropy_b200.models.config import get_config
+from syntropy_b200.models.transformer import prepare_weights
+from syntropy_b200.runtime.engine import LLMEngine, SamplingParams
+from syntropy_b200.runtime.runner import ModelRunner
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(cuda, prefetch):
+    cfg = get_config("small-qwen-moe")
+    mw = prepare_weights(cfg, cuda, seed=21)
+    cache = ExpertCache(mw.layers, 0.5, cuda)
+    if prefetch:
+        assert cache.enable_decode_prefetch(cfg.n_experts)
+    runner = ModelRunner(mw, max_batch=8, max_seq_len=256, use_graphs=True)
+    runner.expert_cache = cache
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, cfg.vocab, (n,), generator=g).tolist() for n in (17, 40, 5, 64)]
+    outs = LLMEngine(runner).generate(prompts, SamplingParams(max_tokens=8))
+    return outs, cache
+
+
+def test_prefetch_matches_and_stages(cuda):
+    want, _ = _run(cuda, False)
+    got, cache = _run(cuda, True)
+    assert got == want
+    torch.cuda.synchronize()
+    # the second MoE layer's table: some predicted host expert now points into staging
+    L = cache.layers[1]
+    b = L.expert_tier
+    st = cache._staging[1][0]["q"]
+    lo, hi = st.data_ptr(), st.data_ptr() + st.numel() * st.element_size()
+    live = L.experts_gu.qw_ptrs.cpu().tolist()
+    staged = [e for e in range(b.E) if b.slot_of[e] < 0 and lo <= live[e] < hi]
+    assert staged, "no predicted host expert was staged"
+    pred = b.pred.cpu().tolist()
+    assert all(pred[b.e0 + e] for e in staged)
