@@ -185,7 +185,8 @@ def main():
         if args.expert_prefetch:
             cache.enable_decode_prefetch(cfg.n_experts)
     fp8_ep = ep is not None and cfg.weight_quant == "fp8"  # fp8 experts use the NCCL row exchange, eagerly
-    graphs = not ((ep is not None and not ep.fused) or fp8_ep or (tp is not None and not tp.fused) or pp is not None)
+    # TP's NCCL all-reduce baseline is captured into the decode graphs too (ranks step in lockstep)
+    graphs = not ((ep is not None and not ep.fused) or fp8_ep or pp is not None)
     use_mtp = cfg.n_mtp > 0 and mw.mtp is not None and not args.no_mtp and pp is None and tp is None
     # MTP verify windows hold 2 rows per sequence
     runner = ModelRunner(mw, max_batch=B * (2 if use_mtp else 1), max_seq_len=max_len + 16, ep=ep, tp=tp, pp=pp,
