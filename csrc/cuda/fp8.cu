@@ -103,6 +103,9 @@ __global__ void __launch_bounds__(128, 4) f8_gemv_kernel(GemvArgs a) {
   const int tile = blockIdx.x * 4 + warp;
   if (cnt <= 0 || tile >= a.N / 16) return;
   const int KG = a.K >> 6, KB = a.K >> 7;
+  // K slice (split-K over gridDim.z, dense only): 128-column blocks [kb_lo, kb_hi)
+  const int KS = gridDim.z, ks = blockIdx.z;
+  const int kb_lo = (int)((int64_t)KB * ks / KS), kb_hi = (int)((int64_t)KB * (ks + 1) / KS);
   const uint4* __restrict__ wq = reinterpret_cast<const uint4*>(a.qw_ptrs[e]) + (int64_t)tile * KG * 64;
   const float* __restrict__ ws = reinterpret_cast<const float*>(a.sm_ptrs[e]) + (int64_t)(tile >> 3) * KB;
   for (int c0 = 0; c0 < cnt; c0 += NT * 8) {
@@ -127,11 +130,11 @@ __global__ void __launch_bounds__(128, 4) f8_gemv_kernel(GemvArgs a) {
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
-    for (int kb0 = 0; kb0 < KG; kb0 += U) {
+    for (int kb0 = 2 * kb_lo; kb0 < 2 * kb_hi; kb0 += U) {
       uint4 wv[U][2];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        if (kb0 + u < KG) {
+        if (kb0 + u < 2 * kb_hi) {
           wv[u][0] = __ldcs(wq + (int64_t)(kb0 + u) * 64 + lane * 2);
           wv[u][1] = __ldcs(wq + (int64_t)(kb0 + u) * 64 + lane * 2 + 1);
         }
@@ -139,7 +142,7 @@ __global__ void __launch_bounds__(128, 4) f8_gemv_kernel(GemvArgs a) {
 #pragma unroll
       for (int u = 0; u < U; u += 2) {  // one 128-column scale block = two groups
         const int kg = kb0 + u;
-        if (kg >= KG) break;
+        if (kg >= 2 * kb_hi) break;
         const int kb = kg >> 1;
         const float sw = __ldg(ws + kb);
         float part[NT][4];
@@ -179,6 +182,12 @@ __global__ void __launch_bounds__(128, 4) f8_gemv_kernel(GemvArgs a) {
         const int j = nt * 8 + 2 * t + hf;
         if (j >= ccount) continue;
         const int p = p0 + c0 + j;
+        if (KS > 1) {  // raw partial sums; the reduce kernel applies the epilogue
+          float* w = a.ws_part + ((int64_t)ks * a.ws_rows + p) * a.N;
+          w[tile * 16 + g] = acc[nt][hf];
+          w[tile * 16 + g + 8] = acc[nt][2 + hf];
+          continue;
+        }
         if (a.mode == GEMV_SWIGLU) {
           reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)p * (a.N / 2) + tile * 8 + g] =
               f2bf(silu(acc[nt][hf]) * acc[nt][2 + hf]);
@@ -190,13 +199,48 @@ __global__ void __launch_bounds__(128, 4) f8_gemv_kernel(GemvArgs a) {
   }
 }
 
-cudaError_t launch_f8_gemv(const GemvArgs& a, cudaStream_t s) {
-  if (a.N % 16 || a.K % 128 || !a.xq || !a.xs || a.ldx % 4) return cudaErrorInvalidValue;
-  dim3 grid((unsigned)((a.N / 16 + 3) / 4), (unsigned)a.E);
+// Split-K reduction in slice order (deterministic) + the epilogue: thread per (row, output).
+__global__ void f8_splitk_reduce_kernel(GemvArgs a, int KS) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int rows = a.ws_rows;
+  if (i >= (int64_t)rows * a.N) return;
+  const int p = (int)(i / a.N), n = (int)(i % a.N);
+  if (a.mode == GEMV_SWIGLU && (n & 15) >= 8) return;  // up rows are read by their gate row
+  float v = 0.f, u = 0.f;
+  for (int k = 0; k < KS; ++k) {
+    const float* w = a.ws_part + ((int64_t)k * rows + p) * a.N;
+    v += w[n];
+    if (a.mode == GEMV_SWIGLU) u += w[n + 8];
+  }
+  if (a.mode == GEMV_SWIGLU)
+    reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)p * (a.N / 2) + (n >> 4) * 8 + (n & 7)] = f2bf(silu(v) * u);
+  else
+    gemv_store(a, p, n, v);
+}
+
+int f8_gemv_ksplit(int N, int K, int E, int rows, size_t ws_floats) {
+  if (E != 1 || rows <= 0) return 1;
+  const int ctas = (N / 16 + 3) / 4;
+  int ks = (2 * 148 * 4 + ctas - 1) / ctas;  // ~4 CTAs per SM
+  ks = ks < 1 ? 1 : (ks > 16 ? 16 : ks);
+  if (ks > K / 128) ks = K / 128;
+  while (ks > 1 && (size_t)ks * rows * N > ws_floats) --ks;
+  return ks;
+}
+
+cudaError_t launch_f8_gemv(const GemvArgs& a_in, cudaStream_t s) {
+  if (a_in.N % 16 || a_in.K % 128 || !a_in.xq || !a_in.xs || a_in.ldx % 4) return cudaErrorInvalidValue;
+  GemvArgs a = a_in;
+  const int ks = a.ws_part ? f8_gemv_ksplit(a.N, a.K, a.E, a.ws_rows, a.ws_floats) : 1;
+  dim3 grid((unsigned)((a.N / 16 + 3) / 4), (unsigned)a.E, (unsigned)ks);
   const int nt = a.nt_hint <= 1 ? 1 : (a.nt_hint <= 2 ? 2 : 4);
   if (nt == 1) f8_gemv_kernel<1, 4><<<grid, 128, 0, s>>>(a);
   else if (nt == 2) f8_gemv_kernel<2, 4><<<grid, 128, 0, s>>>(a);
   else f8_gemv_kernel<4, 2><<<grid, 128, 0, s>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || ks == 1) return e;
+  const int64_t n = (int64_t)a.ws_rows * a.N;
+  f8_splitk_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(a, ks);
   return cudaGetLastError();
 }
 

@@ -22,6 +22,7 @@ constexpr int MLA_ROWB = MLA_W * 2;      // 1152 bytes
 constexpr int MLA_CH = MLA_ROWB / 16;    // 72 chunks of 16 bytes
 constexpr int MLA_BN = 32;               // keys per tile
 constexpr int MLA_TILEB = MLA_BN * MLA_ROWB;
+constexpr int MLA_SS = 20;  // score row stride (16 heads + pad): bank = 8t + g, conflict-free
 
 struct MlaDecodeArgs {
   const __nv_bfloat16* q;       // [B, H, 576]: [q_lat | q_pe]
@@ -58,7 +59,7 @@ __global__ void __launch_bounds__(128) mla_decode_kernel(MlaDecodeArgs a) {
   }
   uint8_t* sQ = smem;                               // 16 rows x 1152 B
   uint8_t* sKV = smem + 16 * MLA_ROWB;              // [2][32 x 1152 B]
-  float* sS = reinterpret_cast<float*>(sKV + 2 * MLA_TILEB);  // [16][32]
+  float* sS = reinterpret_cast<float*>(sKV + 2 * MLA_TILEB);  // [32 keys][MLA_SS] (heads; padded)
   const uint32_t uQ = (uint32_t)__cvta_generic_to_shared(sQ);
   const uint32_t uKV = (uint32_t)__cvta_generic_to_shared(sKV);
   const int32_t* bt = a.block_tables + (int64_t)b * a.max_blocks;
@@ -123,7 +124,7 @@ __global__ void __launch_bounds__(128) mla_decode_kernel(MlaDecodeArgs a) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int key = k0 + warp * 8 + 2 * t + (i & 1);
-        sS[(g + 8 * (i >> 1)) * MLA_BN + warp * 8 + 2 * t + (i & 1)] =
+        sS[(warp * 8 + 2 * t + (i & 1)) * MLA_SS + g + 8 * (i >> 1)] =
             key < key_end ? sc[i] * a.scale_log2 : -INFINITY;
       }
     }
@@ -135,11 +136,11 @@ __global__ void __launch_bounds__(128) mla_decode_kernel(MlaDecodeArgs a) {
     for (int r = 0; r < 2; ++r)
 #pragma unroll
       for (int kk = 0; kk < 2; ++kk) {
-        const float* row = sS + (g + 8 * r) * MLA_BN + kk * 16 + 2 * t;
-        sv[r][kk][0] = row[0];
-        sv[r][kk][1] = row[1];
-        sv[r][kk][2] = row[8];
-        sv[r][kk][3] = row[9];
+        const float* col = sS + (kk * 16 + 2 * t) * MLA_SS + g + 8 * r;
+        sv[r][kk][0] = col[0];
+        sv[r][kk][1] = col[MLA_SS];
+        sv[r][kk][2] = col[8 * MLA_SS];
+        sv[r][kk][3] = col[9 * MLA_SS];
 #pragma unroll
         for (int i = 0; i < 4; ++i) mx[r] = fmaxf(mx[r], sv[r][kk][i]);
       }
@@ -241,7 +242,7 @@ cudaError_t launch_mla_decode(const void* q, const void* cache, const int32_t* b
                               int pages_per_split, int n_splits, float scale, cudaStream_t s) {
   if (B == 0) return cudaSuccess;
   if (H % 16 || pages_per_split <= 0) return cudaErrorInvalidValue;
-  constexpr int smem = 16 * MLA_ROWB + 2 * MLA_TILEB + 16 * MLA_BN * 4;
+  constexpr int smem = 16 * MLA_ROWB + 2 * MLA_TILEB + MLA_BN * MLA_SS * 4;
   static bool set = false;
   if (!set) {
     cudaError_t e = cudaFuncSetAttribute(mla_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

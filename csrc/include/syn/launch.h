@@ -54,6 +54,10 @@ struct GemvArgs {
   // fp8 path: activations quantised to e4m3 [rows][ldx] with f32 scales [rows][K/128]
   const uint8_t* xq;
   const float* xs;
+  // fp8 dense split-K: f32 partials [ksplit][ws_rows][N] (null: no split)
+  float* ws_part;
+  int ws_rows;
+  size_t ws_floats;
 };
 // ---- fp8 (e4m3, 128x128 weight blocks, 1x128 activation blocks) ----
 // Tiled weight layout: per (16-row tile, 64-column group) 1024 bytes, lane-major in

@@ -646,7 +646,7 @@ torch::Tensor f8_tiled_to_rows(torch::Tensor tiled, int64_t N, int64_t K) {
 
 void f8_gemv(torch::Tensor xq, torch::Tensor xs, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
              torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor out, int64_t N, int64_t K, int64_t mode,
-             int64_t nt_hint) {
+             int64_t nt_hint, torch::Tensor ws) {
   SYN_CHECK_INPUT(xq);
   TORCH_CHECK(xq.scalar_type() == torch::kUInt8 && xq.dim() == 2 && xq.size(1) == K && xq.stride(1) == 1, "xq");
   TORCH_CHECK(xs.scalar_type() == torch::kFloat32 && xs.dim() == 2 && xs.size(1) == K / 128 && xs.is_contiguous(),
@@ -672,6 +672,12 @@ void f8_gemv(torch::Tensor xq, torch::Tensor xs, torch::Tensor qw_ptrs, torch::T
   a.mode = (int)mode;
   a.E = (int)qw_ptrs.numel();
   a.nt_hint = (int)nt_hint;
+  if (ws.numel() && a.E == 1) {  // dense: split-K allowed into this f32 workspace
+    TORCH_CHECK(ws.is_cuda() && ws.scalar_type() == torch::kFloat32, "ws f32");
+    a.ws_part = ws.data_ptr<float>();
+    a.ws_rows = (int)xq.size(0);
+    a.ws_floats = (size_t)ws.numel();
+  }
   const at::cuda::CUDAGuard guard(xq.device());
   SYN_CHECK_CUDA(launch_f8_gemv(a, cur_stream()));
 }

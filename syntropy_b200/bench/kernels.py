@@ -190,6 +190,56 @@ def main():
                    extra={"status": int(st.item())})
             wd = w.dequant()
             report(f"cublas_bf16_{M}x{N}x{K}(reference)", timeit(lambda: x @ wd.t(), iters=10), flops=2 * M * N * K)
+    if want("fp8_gemv"):
+        from ..formats.fp8 import FP8Weight
+        for name, N, K, rows in (("fp8_gemv_dense_7168x18432", 7168, 18432, T), ("fp8_lm_head_129280x7168", 129280, 7168, 2)):
+            reps = max(1, int(math.ceil(300e6 / (N * K))))
+            ws = [FP8Weight.quantize(torch.randn(N, K, device=dev) * 0.02) for _ in range(reps)]
+            x = torch.randn(rows, K, device=dev).to(torch.bfloat16)
+            out = torch.empty(rows, N, dtype=torch.float32, device=dev)
+            i = [0]
+
+            def fn8():
+                ops.linear(x, ws[i[0] % reps], out, ops.GEMV_STORE)
+                i[0] += 1
+            report(name, timeit(fn8, warmup=max(3, reps)), N * K + (N // 128 + 1) * (K // 128) * 4,
+                   extra={"rows": rows})
+            del ws
+    if want("mla"):
+        B, H, ctx = 16, 128, 4096
+        nb = B * ctx // 16 + 1
+        cache = torch.randn(nb, 16, 576, device=dev).to(torch.bfloat16)
+        bt = (torch.randperm(nb - 1, device=dev)[: B * ctx // 16] + 1).int().view(B, -1)
+        cl = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+        q = torch.randn(B, H, 576, device=dev).to(torch.bfloat16)
+        pps = 32
+        ns = (bt.shape[1] + pps - 1) // pps
+        po = torch.empty(B * H * ns * 512, device=dev)
+        pml = torch.empty(B * H * ns * 2, device=dev)
+        o = torch.empty(B, H, 512, device=dev)
+        report("mla_decode_b16_ctx4096", timeit(lambda: ops.mla_decode(q, cache, bt, cl, o, 1 / math.sqrt(192), po, pml,
+                                                                       pps)), B * ctx * 1152)
+    if want("attn_prefill"):
+        nseq, L, Hq, Hkv, D = 8, 1024, 64, 4, 128
+        nb = nseq * L // 16 + 1
+        kc = torch.randn(nb, Hkv, 16, D, device=dev).to(torch.bfloat16)
+        vc = torch.randn(nb, Hkv, 16, D, device=dev).to(torch.bfloat16)
+        bt = (torch.arange(nseq * L // 16, device=dev) + 1).int().view(nseq, -1)
+        cu = torch.arange(0, nseq * L + 1, L, dtype=torch.int32, device=dev)
+        kl = torch.full((nseq,), L, dtype=torch.int32, device=dev)
+        q = torch.randn(nseq * L, Hq, D, device=dev).to(torch.bfloat16)
+        o = torch.empty_like(q)
+        flops = 4 * nseq * L * L * Hq * D / 2  # causal
+        report("attn_prefill_8x1024_h64", timeit(lambda: ops.attn_prefill_paged(q, kc, vc, bt, cu, kl, o, L,
+                                                                                1 / math.sqrt(D)), iters=10),
+               flops=flops)
+        import torch.nn.functional as F
+        qq = q.view(nseq, L, Hq, D).transpose(1, 2)
+        kk = kc[1:].permute(0, 2, 1, 3).reshape(nseq, L, Hkv, D).transpose(1, 2)
+        vv = vc[1:].permute(0, 2, 1, 3).reshape(nseq, L, Hkv, D).transpose(1, 2)
+        report("sdpa_library_8x1024_h64(reference)",
+               timeit(lambda: F.scaled_dot_product_attention(qq, kk, vv, is_causal=True, enable_gqa=True), iters=10),
+               flops=flops)
     print(json.dumps({"summary": res}))
 
 

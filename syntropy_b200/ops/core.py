@@ -93,6 +93,18 @@ def _f8_ptrs(W):
     return p
 
 
+_F8_WS: dict = {}
+
+
+def _f8_workspace(dev, floats: int) -> torch.Tensor:
+    key = str(dev)
+    ws = _F8_WS.get(key)
+    if ws is None or ws.numel() < floats:
+        ws = torch.empty(floats, dtype=torch.float32, device=dev)
+        _F8_WS[key] = ws
+    return ws
+
+
 def _linear_fp8(x, W, out, mode):
     """Block-scaled fp8 GEMV: x quantised to e4m3 with 1x128 scales, e4m3 x e4m3 tensor-core
     products, both scales applied per 128-column block."""
@@ -102,8 +114,10 @@ def _linear_fp8(x, W, out, mode):
         kmode = 5
     xq, xs = ext().f8_quant_act(x if x.stride(-1) == 1 else x.contiguous())
     qp, sp = _f8_ptrs(W)
+    # split-K workspace only where the row tiles alone underfill the GPU (< ~4 CTAs per SM)
+    ws = _f8_workspace(x.device, 16 * T * W.N) if W.N < 16 * 4 * 148 * 2 else _EMPTY_F32(x.device)
     ext().f8_gemv(xq, xs, qp, sp, _identity_off(T, x.device), _EMPTY_I32(x.device), _EMPTY_F32(x.device), out,
-                  W.N, W.K, kmode, (T + 7) // 8)
+                  W.N, W.K, kmode, (T + 7) // 8, ws)
     _launched(2)
     return out
 
@@ -305,7 +319,8 @@ def linear_grouped(x: torch.Tensor, bank, tok_off: torch.Tensor, tok_idx: torch.
         if getattr(bank, "is_fp8", False):
             xq, xs = e.f8_quant_act(x if x.stride(-1) == 1 else x.contiguous())
             e.f8_gemv(xq, xs, qw_ptrs, sm_ptrs, tok_off, tok_idx if tok_idx is not None else _EMPTY_I32(x.device),
-                      route_w if route_w is not None else _EMPTY_F32(x.device), out, bank.N, bank.K, kmode, nt_hint)
+                      route_w if route_w is not None else _EMPTY_F32(x.device), out, bank.N, bank.K, kmode, nt_hint,
+                      _EMPTY_F32(x.device))
             _launched(2)
             return out
         e.q4_gemv(x, qw_ptrs, sm_ptrs, tok_off,

@@ -38,7 +38,8 @@ def test_fp8_tiling_roundtrip_and_act_quant(cuda):
 
 
 @pytest.mark.parametrize("T,N,K,mode", [(1, 1024, 1024, "bf16"), (5, 576, 1024, "f32"), (16, 2048, 7168, "add"),
-                                         (32, 1024, 512, "swiglu"), (3, 24576 // 8, 1536, "bf16")])
+                                         (32, 1024, 512, "swiglu"), (3, 24576 // 8, 1536, "bf16"),
+                                         (2, 576, 7168, "f32"), (16, 512, 18432, "swiglu")])
 def test_fp8_gemv_dense(cuda, T, N, K, mode):
     torch.manual_seed(1)
     W = FP8Weight.quantize(torch.randn(N, K, device=cuda) * 0.02)
@@ -81,7 +82,8 @@ def test_fp8_gemv_grouped_scaled(cuda):
     x = torch.randn(T, K, device=cuda).to(torch.bfloat16)
     xq, xs = ext().f8_quant_act(x)
     out = torch.zeros(P, N, device=cuda)
-    ext().f8_gemv(xq, xs, qp, sp, torch.tensor(off, dtype=torch.int32, device=cuda), tok_idx, route_w, out, N, K, 2, 2)
+    ext().f8_gemv(xq, xs, qp, sp, torch.tensor(off, dtype=torch.int32, device=cuda), tok_idx, route_w, out, N, K, 2, 2,
+                  torch.empty(0, device=cuda))
     xa = _act_ref(xq, xs)
     ref = torch.zeros(P, N, device=cuda)
     for e in range(E):
