@@ -46,6 +46,20 @@ class ExpertStats:
         self.total.copy_(d["total"])
         self.decay = float(d["decay"])
 
+    def save(self, path: str, model: str = ""):
+        """Persist the popularity profile (next to the model pack), so a restarted instance
+        starts with the hot experts resident instead of relearning them."""
+        torch.save({"model": model, **self.state_dict()}, path)
+
+    @classmethod
+    def load(cls, path: str, model: str = "") -> "ExpertStats":
+        d = torch.load(path, map_location="cpu", weights_only=False)
+        if model and d.get("model") and d["model"] != model:
+            raise ValueError(f"expert profile is for {d['model']}, not {model}")
+        st = cls(d["score"].shape[0], d["score"].shape[1], d["decay"])
+        st.load_state_dict(d)
+        return st
+
 
 class ExpertCache:
     """Residency manager for the expert banks of a model's MoE layers on one device."""

@@ -117,6 +117,51 @@ class LLMEngine:
                 self.running.remove(s)
                 return
 
+    # ------------------------------------------------------------------ saved sessions
+    def save_session(self, seq_id: int) -> dict:
+        """Snapshot of a running sequence: its tokens, sampling state and KV pages (packed per
+        layer on the device, then copied to host memory).  `restore_session` continues it,
+        in this engine or a fresh one over the same model, without a re-prefill."""
+        s = next((x for x in self.running if x.seq_id == seq_id), None)
+        if s is None:
+            raise KeyError(f"no running sequence {seq_id}")
+        kv = self.runner.kv
+        n_pages = kv.blocks_needed(s.n_tokens - 1) if s.n_tokens > 1 else 0
+        dev = self.runner.device
+        pages = torch.tensor(s.blocks[:n_pages], dtype=torch.int32, device=dev)
+        layers = []
+        for i in range(len(kv.k)):
+            packed = ops.kv_pack(kv.k[i], kv.v[i], pages)
+            layers.append(packed.to("cpu"))
+        cfg = self.cfg
+        return {"model": cfg.name, "n_layers": len(kv.k), "kv_shape": tuple(kv.k[0].shape[1:]),
+                "prompt": list(s.prompt), "output": list(s.output), "params": s.params, "seed": s.seed,
+                "stream": s.stream, "rng_counter": s.rng_counter, "kv": layers}
+
+    def restore_session(self, state: dict) -> int:
+        """Re-admits a saved sequence as running: allocates pages, writes its KV back and
+        resumes decoding from its last token."""
+        kv = self.runner.kv
+        if state["model"] != self.cfg.name or state["n_layers"] != len(kv.k) or \
+                tuple(state["kv_shape"]) != tuple(kv.k[0].shape[1:]):
+            raise ValueError("saved session belongs to a different model or cache layout")
+        sid = next(self._ids)
+        s = Sequence(sid, list(state["prompt"]), state["params"], output=list(state["output"]),
+                     t_arrival=time.perf_counter())
+        s.seed, s.stream, s.rng_counter = state["seed"], state["stream"], state["rng_counter"]
+        n_pages = state["kv"][0].shape[0] if state["kv"] else 0
+        if kv.alloc.num_free < kv.blocks_needed(s.n_tokens + 1):
+            raise RuntimeError("not enough free KV pages to restore the session")
+        kv.ensure(s.blocks, s.n_tokens)
+        dev = self.runner.device
+        pages = torch.tensor(s.blocks[:n_pages], dtype=torch.int32, device=dev)
+        for i in range(len(kv.k)):
+            ops.kv_unpack(state["kv"][i].to(dev), kv.k[i], kv.v[i], pages)
+        s.status = "running"
+        s.t_first_token = time.perf_counter()
+        self.running.append(s)
+        return sid
+
     def has_work(self) -> bool:
         return bool(self.waiting or self.running)
 
