@@ -32,6 +32,8 @@ def main():
     ap.add_argument("--eager", action="store_true", help="no CUDA graph (one launch per op)")
     ap.add_argument("--expert-cache-frac", type=float, default=1.0)
     ap.add_argument("--kernel-table", action="store_true", help="per-kernel device time of prefill and decode")
+    ap.add_argument("--step-profile", action="store_true",
+                    help="one decode step through the timestamped graph variant: device ms per segment")
     ap.add_argument("--top", type=int, default=25)
     args = ap.parse_args()
     dev = torch.device("cuda:0")
@@ -56,6 +58,17 @@ def main():
     for _ in range(args.warmup):
         eng.step()
     torch.cuda.synchronize()
+    if args.step_profile:
+        runner.profile_next = True
+        eng.step()
+        prof = runner.step_profile()
+        agg = {}
+        for lab, ms in prof:
+            kind = lab.split(".")[-1]
+            agg[kind] = agg.get(kind, 0.0) + ms
+        print(json.dumps({"segments_ms": {k: round(v, 4) for k, v in agg.items()},
+                          "total_ms": round(sum(ms for _, ms in prof), 4)}))
+        return
     runner.time_events = []
     torch.cuda.profiler.start()
     t0 = time.perf_counter()

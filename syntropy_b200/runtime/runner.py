@@ -84,6 +84,11 @@ class ModelRunner:
         self.expert_cache = None  # experts.cache.ExpertCache when a VRAM cap is set
         self._pf_stream = None    # side stream of the router-predicted expert prefetch
         self._pf_events = {}
+        self.profile_next = False  # next decode step replays the timestamped graph variant
+        self._stamping = False
+        self._stamp_n = 0
+        self._stamp_labels: list[str] = []
+        self._stamp_buf = None
         self.tp = tp  # parallel.tp.TPGroup or None
         self.mw, self.cfg = mw, cfg
         self.device = mw.device
@@ -185,6 +190,12 @@ class ModelRunner:
         """Forward of the first B rows of the step descriptor; writes logits and next tokens."""
         cfg, mw, b, d = self.cfg, self.mw, self.buf, self.desc.d
         x, h = b["x"][:B], b["h"][:B]
+        if self._stamping:
+            if self._stamp_buf is None:
+                self._stamp_buf = torch.zeros(4 * len(mw.layers) + 8, dtype=torch.int64, device=self.device)
+            self._stamp_n = 0
+            self._stamp_labels = []
+        self._stamp("start")
         if self.ep is not None:
             self.ep.step_begin()
         if self.tp is not None:
@@ -200,6 +211,7 @@ class ModelRunner:
         for i, L in enumerate(mw.layers):
             nxt = mw.layers[i + 1] if i + 1 < n_layers else None
             self._attention_decode(L, B, i)
+            self._stamp(f"layer{i}.attention")
             if L.is_moe:
                 self._moe_decode(L, nxt, B, i)
             else:
@@ -213,14 +225,17 @@ class ModelRunner:
                 else:
                     ops.linear(mid, L.down, x, ops.GEMV_ADD_F32)
                     ops.rms_norm(x, nw, cfg.rms_eps, out=h)
+            self._stamp(f"layer{i}.{'moe' if L.is_moe else 'ffn'}")
         logits = b["logits"][:B]
         if pp is not None and not pp.last:
             pp.send_hidden(x)
             pp.broadcast_tokens(b["next"][:B])
             return logits
         ops.linear(h, mw.lm_head, logits, ops.GEMV_STORE)
+        self._stamp("lm_head")
         ops.sample(logits, d["temperature"][:B], d["top_k"][:B], d["top_p"][:B], d["seed"][:B], d["stream"][:B],
                    d["counter"][:B], b["next"][:B])
+        self._stamp("sample")
         if pp is not None:
             pp.broadcast_tokens(b["next"][:B])
         return logits
@@ -364,12 +379,18 @@ class ModelRunner:
         ops.rms_norm(x, nw, cfg.rms_eps, out=h)
 
     def decode(self, B: int):
-        """Run one decode step for the first B rows (descriptor already filled on the host)."""
+        """Run one decode step for the first B rows (descriptor already filled on the host).
+        With `profile_next` set, this step replays the profiled graph variant, which also
+        writes device timestamps at every layer boundary (see `step_profile`)."""
+        prof = self.profile_next and self.is_cuda
+        self.profile_next = False
+        self._stamping = prof
         if self.use_graphs:
             bb = bucket_for(B)
-            g = self.graphs.get(bb)
+            key = ("profiled", bb) if prof else bb
+            g = self.graphs.get(key)
             if g is None:
-                g = self.capture(bb)  # uses (and restores) the host descriptor
+                g = self.capture(bb, key)  # uses (and restores) the host descriptor
             ev = self._ev0()
             # native: descriptor upload + graph launch on the current stream
             ext().step_launch(self.desc.host, self.desc.dev, g.raw_cuda_graph_exec(),
@@ -380,7 +401,28 @@ class ModelRunner:
             ev = self._ev0()
             self.decode_forward(B)
             self._ev1(ev)
+        self._stamping = False
         return self.buf["next"][:B]
+
+    # ------------------------------------------------------------------ profiled steps
+    def _stamp(self, label: str):
+        """Device timestamp at a segment boundary (profiled steps only; captured in the
+        profiled graph variant)."""
+        if not self._stamping:
+            return
+        n = self._stamp_n
+        if self._stamp_buf is None or n >= self._stamp_buf.numel():
+            return
+        ops.timestamp(self._stamp_buf, n)
+        if len(self._stamp_labels) <= n:
+            self._stamp_labels.append(label)
+        self._stamp_n = n + 1
+
+    def step_profile(self) -> list[tuple[str, float]]:
+        """Per-segment device time (ms) of the last profiled step: (segment label, ms)."""
+        torch.cuda.synchronize(self.device)
+        t = self._stamp_buf[: len(self._stamp_labels)].cpu().tolist()
+        return [(self._stamp_labels[i], (t[i] - t[i - 1]) / 1e6) for i in range(1, len(t))]
 
     def _ev0(self):
         if self.time_events is None or not self.is_cuda:
@@ -394,7 +436,7 @@ class ModelRunner:
             ev[1].record()
             self.time_events.append(ev)
 
-    def capture(self, bb: int) -> "torch.cuda.CUDAGraph":
+    def capture(self, bb: int, key=None) -> "torch.cuda.CUDAGraph":
         """Capture the decode forward for bucket size bb (rows beyond the live batch are
         padding: null page, slot -1, greedy)."""
         d = self.desc.h
@@ -421,7 +463,7 @@ class ModelRunner:
         torch.cuda.synchronize()
         for k, v in saved.items():
             d[k].copy_(v)
-        self.graphs[bb] = g
+        self.graphs[bb if key is None else key] = g
         return g
 
     # ------------------------------------------------------------------ prefill
