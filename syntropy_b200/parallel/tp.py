@@ -25,6 +25,19 @@ def _align(n, a=256):
     return (n + a - 1) // a * a
 
 
+def gather_vocab_logits(local: torch.Tensor, out: torch.Tensor, gathered: torch.Tensor, group):
+    """out [T, V] = concatenation over ranks (rank order) of local [T, V/N] vocab slices."""
+    n = dist.get_world_size(group)
+    T, vl = local.shape
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(gathered[: n * T], local, group=group)
+    else:
+        parts = [torch.empty_like(local) for _ in range(n)]
+        dist.all_gather(parts, local.contiguous(), group=group)
+        torch.cat(parts, 0, out=gathered[: n * T])
+    out.copy_(gathered[: n * T].view(n, T, vl).permute(1, 0, 2).reshape(T, n * vl))
+
+
 class TPGroup:
     def __init__(self, ctx: DistContext, hidden: int, cap: int, n_layers: int, timeout_s: float = 2.0,
                  fused: bool = True):
@@ -101,6 +114,9 @@ def shard_state(cfg, sd: dict, rank: int, size: int) -> dict:
             out[n] = t[rank * f:(rank + 1) * f]
         elif leaf == "down":
             out[n] = t[:, rank * f:(rank + 1) * f]
+        elif n == "lm_head" and cfg.vocab % size == 0 and (cfg.vocab // size) % 16 == 0:
+            v = cfg.vocab // size  # vocab-parallel head: each rank scores its slice of the vocabulary
+            out[n] = t[rank * v:(rank + 1) * v]
         else:
             out[n] = t
     return out

@@ -133,6 +133,10 @@ class ModelRunner:
             b["q"] = torch.zeros(B, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
             b["attn"] = torch.zeros(B, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
         b["logits"] = torch.zeros(B, cfg.vocab, dtype=torch.float32, device=dev)
+        vl = self._vocab_local()
+        if self.tp is not None and vl < cfg.vocab:  # vocab-parallel head: local slice + gather space
+            b["logits_local"] = torch.zeros(B, vl, dtype=torch.float32, device=dev)
+            b["logits_gather"] = torch.zeros(self.tp.N * B, vl, dtype=torch.float32, device=dev)
         b["next"] = torch.zeros(B, dtype=torch.int32, device=dev)
         if any(not L.is_moe for L in self.mw.layers):
             b["ffn_mid"] = torch.zeros(B, cfg.ffn, dtype=act, device=dev)
@@ -231,7 +235,7 @@ class ModelRunner:
             pp.send_hidden(x)
             pp.broadcast_tokens(b["next"][:B])
             return logits
-        ops.linear(h, mw.lm_head, logits, ops.GEMV_STORE)
+        self._lm_head(h, logits, b.get("logits_local"), b.get("logits_gather"))
         self._stamp("lm_head")
         ops.sample(logits, d["temperature"][:B], d["top_k"][:B], d["top_p"][:B], d["seed"][:B], d["stream"][:B],
                    d["counter"][:B], b["next"][:B])
@@ -404,6 +408,28 @@ class ModelRunner:
         self._stamping = False
         return self.buf["next"][:B]
 
+    # ------------------------------------------------------------------ output head
+    def _vocab_local(self) -> int:
+        W = self.mw.lm_head
+        return int(getattr(W, "N", None) or W.shape[0])
+
+    def _lm_head(self, h, logits, local=None, gathered=None):
+        """logits [T, V] f32.  Under TP with a vocab-parallel head each rank scores its vocab
+        slice and the slices are all-gathered in rank order (every rank then samples alike)."""
+        vl = self._vocab_local()
+        if vl == self.cfg.vocab or self.tp is None:
+            ops.linear(h, self.mw.lm_head, logits, ops.GEMV_STORE)
+            return logits
+        from ..parallel.tp import gather_vocab_logits
+        T = h.shape[0]
+        if local is None:
+            local = torch.empty(T, vl, dtype=torch.float32, device=h.device)
+            gathered = torch.empty(self.tp.N * T, vl, dtype=torch.float32, device=h.device)
+        local = local[:T]
+        ops.linear(h, self.mw.lm_head, local, ops.GEMV_STORE)
+        gather_vocab_logits(local, logits, gathered, self.tp.ctx.group)
+        return logits
+
     # ------------------------------------------------------------------ profiled steps
     def _stamp(self, label: str):
         """Device timestamp at a segment boundary (profiled steps only; captured in the
@@ -542,7 +568,7 @@ class ModelRunner:
         last = torch.tensor([c - 1 for c in cu_seqlens[1:]], device=dev, dtype=torch.long)
         hl = ops.rms_norm(x[last].contiguous(), mw.final_norm, cfg.rms_eps)
         logits = torch.empty(last.numel(), cfg.vocab, dtype=torch.float32, device=dev)
-        ops.linear(hl, mw.lm_head, logits, ops.GEMV_STORE)
+        self._lm_head(hl, logits)
         return logits
 
     def _prefill_mla(self, L, i, h, x, positions, slots, cu_seqlens, prefix):
@@ -626,7 +652,7 @@ class ModelRunner:
             ops.linear(mid, L.down, x, ops.GEMV_ADD_F32)
         hl = ops.rms_norm(x, mw.final_norm, cfg.rms_eps).to(act)
         logits = torch.empty(S, cfg.vocab, dtype=torch.float32, device=dev)
-        ops.linear(hl.contiguous(), mw.lm_head, logits, ops.GEMV_STORE)
+        self._lm_head(hl.contiguous(), logits)
         return torch.argmax(logits, -1).to(torch.int32).cpu()
 
     def _prefill_attn_with_prefix(self, i, q, attn, cu_seqlens, prefix):
