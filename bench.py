@@ -102,6 +102,8 @@ def main():
                     help="VRAM-resident share of each rank's experts (Qwen3 config: 0.6, rest in pinned host RAM; "
                          "others: 1.0)")
     ap.add_argument("--no-uncapped", action="store_true", help="skip the extra all-resident measurement")
+    ap.add_argument("--rebalance-every", type=int, default=64,
+                    help="decode steps between expert-cache adaptations (decayed-LFU swaps; 0 = never)")
     ap.add_argument("--expert-prefetch", type=int, default=1,
                     help="router-predicted prefetch of host-tier experts during decode (1 on, 0 off)")
     ap.add_argument("--no-mtp", action="store_true", help="models with an MTP head: plain decoding instead of "
@@ -196,7 +198,7 @@ def main():
     if use_mtp:
         from syntropy_b200.runtime.spec import MTPDrafter, SpecConfig
         spec = SpecConfig(drafter=MTPDrafter(runner))
-    eng = LLMEngine(runner, max_prefill_tokens=8192, dist_ctx=ctx, spec=spec)
+    eng = LLMEngine(runner, max_prefill_tokens=8192, dist_ctx=ctx, spec=spec, rebalance_every=args.rebalance_every)
     g = torch.Generator().manual_seed(1234)
     all_prompts = [torch.randint(0, cfg.vocab, (args.prompt,), generator=g).tolist() for _ in range(args.batch)]
     prompts = all_prompts[rank::world] if cfg.is_moe else all_prompts
@@ -307,6 +309,7 @@ def main():
                    "expert_cache_frac": args.expert_cache_frac if cfg.is_moe else 1.0,
                    "host_tier_gb": round(cache.host_bytes() / 1e9, 2) if cache is not None else 0.0,
                    "expert_prefetch": bool(cache is not None and cache.prefetch),
+                   "expert_rebalance_every": args.rebalance_every if cache is not None else 0,
                    "l2": f"inputs larger than L2 ({mw.nbytes() / 1e9:.0f} GB of weights streamed per step per rank)",
                    "weights_gb": round(mw.nbytes() / 1e9, 2), "weight_build_s": round(t_weights, 1)},
         "clocks": clk.summary(),

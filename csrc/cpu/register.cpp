@@ -55,6 +55,7 @@ void register_all(pybind11::module& m) {
   register_runtime(m);
   register_formats(m);
   register_dispatcher(m);
+  register_tier(m);
 }
 
 }  // namespace syn

@@ -238,6 +238,16 @@ __global__ void __launch_bounds__(128) moe_topk_kernel(TopkArgs a) {
       }
     }
     if (lane == 31) a.tok_off[a.E] = incl;
+    if (a.counts) {  // usage statistics for the expert cache
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int e = lane * PER + i;
+        if (e < a.E) {
+          const int nxt = (i + 1 < PER) ? c[i + 1] : run;
+          a.counts[e] += nxt - c[i];
+        }
+      }
+    }
   }
   __syncthreads();
   // pair position = offset[e] + number of earlier tokens that chose e (deterministic)
@@ -297,6 +307,7 @@ __global__ void __launch_bounds__(256) moe_csr_kernel(TopkArgs a) {
     s_base = off;
     a.tok_off[e] = off;
     if (e == a.E - 1) a.tok_off[a.E] = off + (int)cnt[e];
+    if (a.counts) a.counts[e] += (int)cnt[e];
   }
   __syncthreads();
   int base = s_base;

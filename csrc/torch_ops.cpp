@@ -241,7 +241,7 @@ void router_logits(torch::Tensor h, torch::Tensor W, torch::Tensor logits) {
 void moe_topk(torch::Tensor logits, torch::Tensor bias, int64_t E, int64_t k, int64_t scoring, int64_t n_groups,
               int64_t topk_groups, bool norm, double scaling, bool pred, torch::Tensor topk_ids, torch::Tensor topk_w,
               torch::Tensor tok_off, torch::Tensor tok_idx, torch::Tensor pair_w, torch::Tensor pair_of,
-              torch::Tensor pred_mask, torch::Tensor ws) {
+              torch::Tensor pred_mask, torch::Tensor ws, torch::Tensor counts) {
   SYN_CHECK_INPUT(logits);
   TORCH_CHECK(logits.scalar_type() == torch::kFloat32, "logits f32");
   const bool large = logits.size(0) > 256;
@@ -274,6 +274,9 @@ void moe_topk(torch::Tensor logits, torch::Tensor bias, int64_t E, int64_t k, in
   a.pair_of = pair_of.data_ptr<int32_t>();
   a.pred_mask = pred_mask.numel() ? pred_mask.data_ptr<int32_t>() : nullptr;
   a.ws = reinterpret_cast<uint32_t*>(ws.data_ptr<int32_t>());
+  TORCH_CHECK(!counts.numel() || (counts.is_cuda() && counts.scalar_type() == torch::kInt32 && counts.numel() >= E &&
+                                  counts.is_contiguous()), "moe_topk counts: int32 [E] on the device");
+  a.counts = counts.numel() ? counts.data_ptr<int32_t>() : nullptr;
   const at::cuda::CUDAGuard guard(logits.device());
   if (large) {
     SYN_CHECK_CUDA(launch_moe_route_large(a, cur_stream()));

@@ -23,12 +23,16 @@ def _engine_from_config(cfg, device: str):
         from ..formats.safetensors import load_state_dict
         sd = load_state_dict(cfg.model.path)
     mw = prepare_weights(mcfg, dev, seed=cfg.model.seed, state_dict=sd, max_pos=cfg.model.max_seq_len + 16)
+    cache = None
     if cfg.tier.expert_cache_frac < 1.0 and mcfg.is_moe and dev.type == "cuda":
         from ..experts.cache import ExpertCache
-        ExpertCache(mw.layers, cfg.tier.expert_cache_frac, dev)
+        cache = ExpertCache(mw.layers, cfg.tier.expert_cache_frac, dev)
+        cache.enable_decode_prefetch(mcfg.n_experts)  # router-predicted prefetch of host experts
     runner = ModelRunner(mw, max_batch=cfg.sched.max_batch, max_seq_len=cfg.model.max_seq_len,
                          use_graphs=cfg.sched.cuda_graphs and cfg.feature("cuda_graph"))
-    return LLMEngine(runner, max_prefill_tokens=cfg.sched.max_prefill_tokens), mcfg
+    runner.expert_cache = cache
+    return LLMEngine(runner, max_prefill_tokens=cfg.sched.max_prefill_tokens,
+                     rebalance_every=cfg.tier.rebalance_every), mcfg
 
 
 def cmd_version(args, cfg):

@@ -84,9 +84,18 @@ class ExpertCache:
         if self._staging is not None:
             return
         b = next(x for x in self.banks if x.E > x.n_res)
-        self._staging = [[{"q": torch.empty_like(p["qh"], device=self.device),
-                           "s": torch.empty_like(p["sh"], device=self.device)} for p in b.parts]
-                         for _ in range(2)]
+        # both staging banks are carved out of one VRAM slab by the native arena
+        from .._ext import ext
+        sizes = [(p["qh"].nbytes, p["sh"].nbytes) for p in b.parts] * 2
+        total = sum(q + s_ + 512 for q, s_ in sizes)
+        self._arena = ext().Arena(total)
+        self._slab = torch.empty(total, dtype=torch.uint8, device=self.device)
+
+        def carve(like):
+            off = self._arena.alloc(like.nbytes, 256)
+            assert off >= 0
+            return self._slab[off: off + like.nbytes].view(like.dtype).view(like.shape)
+        self._staging = [[{"q": carve(p["qh"]), "s": carve(p["sh"])} for p in b.parts] for _ in range(2)]
         self._copy_stream = torch.cuda.Stream(device=self.device)
         self._ev_free = [None, None]
         self._issued = {}
@@ -257,18 +266,14 @@ class ExpertCache:
         return sum(b.host_bytes() for b in self.banks)
 
     def rebalance(self, stats: ExpertStats, max_swaps_per_layer: int = 2) -> int:
-        """Swap cold residents for hot host experts (decayed LFU with hysteresis)."""
+        """Swap cold residents for hot host experts (decayed LFU with hysteresis); the plan
+        comes from the native planner (`tier_plan_swaps`)."""
+        from .._ext import ext
         n = 0
         for li, b in enumerate(self.banks):
-            sc = stats.score[li, b.e0: b.e0 + b.E]
-            for _ in range(max_swaps_per_layer):
-                res = b.resident_mask()
-                if res.all() or (~res).all():
-                    break
-                cold_res = torch.where(res, sc, torch.full_like(sc, math.inf)).argmin().item()
-                hot_host = torch.where(~res, sc, torch.full_like(sc, -math.inf)).argmax().item()
-                if sc[hot_host] <= self.hysteresis * sc[cold_res] or sc[hot_host] <= 0:
-                    break
+            sc = stats.score[li, b.e0: b.e0 + b.E].tolist()
+            plan = ext().tier_plan_swaps(sc, b.resident_mask().tolist(), max_swaps_per_layer, self.hysteresis)
+            for cold_res, hot_host in plan:
                 b.swap(cold_res, hot_host)
                 n += 1
         return n

@@ -544,8 +544,9 @@ def _topk_workspace(dev) -> torch.Tensor:
     return ws
 
 
-def moe_topk(logits, cfg, bias, pred: bool, bufs: dict):
-    """Top-k routing + CSR.  bufs: topk_ids, topk_w, tok_off, tok_idx, pair_w, pair_of, pred_mask."""
+def moe_topk(logits, cfg, bias, pred: bool, bufs: dict, counts=None):
+    """Top-k routing + CSR.  bufs: topk_ids, topk_w, tok_off, tok_idx, pair_w, pair_of, pred_mask.
+    counts (int32 [E], optional) accumulates the number of pairs routed to each expert."""
     E, k = cfg.n_experts, cfg.top_k
     T = logits.shape[0]
     scoring = 0 if cfg.router_scoring == "softmax" else 1
@@ -555,7 +556,8 @@ def moe_topk(logits, cfg, bias, pred: bool, bufs: dict):
                        bufs["topk_w"], bufs["tok_off"], bufs["tok_idx"], bufs["pair_w"], bufs["pair_of"],
                        bufs["pred_mask"] if pred else _EMPTY_I32(logits.device),
                        _topk_workspace(logits.device) if T <= 256 else
-                       torch.zeros(E * ((T + 31) // 32) + E, dtype=torch.int32, device=logits.device))
+                       torch.zeros(E * ((T + 31) // 32) + E, dtype=torch.int32, device=logits.device),
+                       counts if counts is not None else _EMPTY_I32(logits.device))
         _launched()
         return
     from ..models.reference import topk_stable
@@ -580,9 +582,11 @@ def moe_topk(logits, cfg, bias, pred: bool, bufs: dict):
     w = w * cfg.routed_scaling
     bufs["topk_ids"][:T] = ids.int()
     bufs["topk_w"][:T] = w
-    counts = torch.bincount(ids.reshape(-1), minlength=E)
+    n_e = torch.bincount(ids.reshape(-1), minlength=E)
+    if counts is not None:
+        counts[:E] += n_e.to(counts.dtype)
     off = torch.zeros(E + 1, dtype=torch.int64)
-    off[1:] = torch.cumsum(counts, 0)
+    off[1:] = torch.cumsum(n_e, 0)
     bufs["tok_off"][: E + 1] = off.int()
     fill = off[:-1].clone()
     pair_of = torch.empty(T, k, dtype=torch.int32)

@@ -65,8 +65,9 @@ class StepOutput:
 
 class LLMEngine:
     def __init__(self, runner: ModelRunner, max_prefill_tokens: int = 8192, eos_token_id: int | None = None,
-                 dist_ctx=None, prefix_cache: bool = False, spec=None):
+                 dist_ctx=None, prefix_cache: bool = False, spec=None, rebalance_every: int = 64):
         self.runner = runner
+        self.rebalance_every = rebalance_every  # decode steps between expert-cache adaptations (0: never)
         self.spec = spec  # runtime.spec.SpecConfig or None
         self.prefix = None
         if prefix_cache:
@@ -280,9 +281,12 @@ class LLMEngine:
     def _decode(self) -> list[StepOutput]:
         # Under lockstep ranks every rank runs the same verify window shape (equal live
         # sequence counts), so the expert-parallel exchanges inside it line up.
-        if self.spec is not None:
-            return self._decode_spec()
-        return self._decode_plain()
+        outs = self._decode_spec() if self.spec is not None else self._decode_plain()
+        r = self.runner
+        n = self.stats["decode_steps"]
+        if r.expert_cache is not None and self.rebalance_every and n % self.rebalance_every == 0:
+            r.adapt_experts()  # lockstep ranks reach the same step count together
+        return outs
 
     def _decode_spec(self) -> list[StepOutput]:
         """One verify window per sequence: rows [last, d1..dg] at positions p..p+g."""

@@ -116,6 +116,12 @@ class ModelRunner:
         self.time_events: list | None = None  # when a list: (start, end) CUDA events per decode
         self._alloc_buffers()
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
+        # per-expert routed-pair counts of every layer, accumulated by the routing kernels
+        # (captured graphs included) and folded into the expert cache's scores between steps
+        self.route_counts = torch.zeros(len(mw.layers), cfg.n_experts, dtype=torch.int32, device=self.device) \
+            if cfg.n_experts else None
+        self._layer_index = {id(L): i for i, L in enumerate(mw.layers)}
+        self.expert_stats = None
 
     # ------------------------------------------------------------------ buffers
     def _alloc_buffers(self):
@@ -311,7 +317,7 @@ class ModelRunner:
         nxt_moe = pred and cache is not None and cache.prefetch and layer + 1 < len(mw.layers)
         if nxt_moe:  # the next layer's prediction goes to its own mask (read by the side stream)
             mb["pred_mask"] = mw.layers[layer + 1].expert_tier.pred
-        ops.moe_topk(rl, cfg, L.router_bias, pred, mb)
+        ops.moe_topk(rl, cfg, L.router_bias, pred, mb, counts=self._counts_of(layer))
         if nxt_moe:
             # router-predicted prefetch of layer+1's host experts, overlapping this layer
             cur = torch.cuda.current_stream(self.device)
@@ -342,6 +348,35 @@ class ModelRunner:
                            qw_ptrs=dn.qw_ptrs, sm_ptrs=dn.sm_ptrs)
         ops.moe_combine_rmsnorm(x, yp, mb["pair_of"], shared, nw, h, cfg.rms_eps)
 
+    def _counts_of(self, layer: int):
+        return self.route_counts[layer] if self.route_counts is not None and self.expert_cache is not None else None
+
+    def _counts_for(self, L):
+        i = self._layer_index.get(id(L))  # the MTP block's layer is not a cached layer
+        return self._counts_of(i) if i is not None else None
+
+    def adapt_experts(self, max_swaps_per_layer: int = 2) -> int:
+        """Expert-cache adaptation between steps: fold the routing counts accumulated since
+        the last call into the decayed-LFU scores and swap cold residents for hot host
+        experts.  Pointer tables change in place, so captured decode graphs stay valid.
+        Under expert parallelism the counts are summed over the group first (every rank must
+        call this at the same step).  Reference: crates/tier/src/experts/stats.rs:35-205."""
+        cache = self.expert_cache
+        if cache is None or self.route_counts is None:
+            return 0
+        from ..experts.cache import ExpertStats
+        if self.expert_stats is None:
+            self.expert_stats = ExpertStats(len(cache.layers), self.cfg.n_experts)
+        c = self.route_counts
+        if self.ep is not None:
+            import torch.distributed as dist
+            dist.all_reduce(c, group=self.ep.ctx.group)
+        host = c.cpu()
+        c.zero_()
+        for li, L in enumerate(cache.layers):
+            self.expert_stats.observe(li, host[self._layer_index[id(L)]])
+        return cache.rebalance(self.expert_stats, max_swaps_per_layer)
+
     def _shared_expert(self, L, h):
         """Shared-expert FFN output (f32 [T, H]) added to the routed combine."""
         T = h.shape[0]
@@ -364,7 +399,9 @@ class ModelRunner:
         rl = b["rlogits"].view(-1)[: R * E].view(R, E)
         ops.router_logits(ha, L.router, rl)
         mb = self._moe_bufs(R)
-        ops.moe_topk(rl, cfg, L.router_bias, False, mb)
+        # every rank routes all rows here: rank 0 alone counts them (sums over the group later)
+        ops.moe_topk(rl, cfg, L.router_bias, False, mb,
+                     counts=self._counts_for(L) if ep.rank == 0 else None)
         ea, eb = ep.expert_range
         gu, dn = L.experts_gu, L.experts_down
         mid = b["moe_mid"][: R * k]
@@ -713,10 +750,13 @@ class ModelRunner:
                 ops.router_logits(h, L.router, logits)
             else:  # a plain bf16 GEMM with f32 output (library); top-k and CSR are ours
                 logits = torch.mm(h, L.router.t(), out_dtype=torch.float32)
-            ops.moe_topk(logits, cfg, L.router_bias, False, mb)
+            ops.moe_topk(logits, cfg, L.router_bias, False, mb, counts=self._counts_for(L))
         else:
             logits = h.float() @ L.router.float().t()
             _route_torch(logits, cfg, L.router_bias, mb)
+            c = self._counts_for(L)
+            if c is not None:
+                c += torch.bincount(mb["topk_ids"].reshape(-1).long(), minlength=E).to(c.dtype)
         gu, dn = L.experts_gu, L.experts_down
         if L.shared_gu is not None and T > 0:
             x.add_(self._shared_expert(L, h))

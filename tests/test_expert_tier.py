@@ -1,0 +1,40 @@
+"""Expert cache residency on CPU tensors: the decayed-LFU planner (native) swaps the coldest
+residents for the hottest host experts, every expert's weights survive the swaps byte for
+byte, and the pointer tables point at each expert's current home."""
+from types import SimpleNamespace
+
+import torch
+
+from syntropy_b200.experts.cache import ExpertCache, ExpertStats
+
+
+def _bank(E, g):
+    return SimpleNamespace(qw=torch.randint(-2**31, 2**31 - 1, (E, 4, 32), dtype=torch.int32, generator=g),
+                           sm=torch.randn(E, 4, 8, generator=g).half(), E=E, e0=0, qw_ptrs=None, sm_ptrs=None,
+                           bank_contiguous=True)
+
+
+def test_rebalance_swaps_and_keeps_weights():
+    g = torch.Generator().manual_seed(0)
+    E = 8
+    gu, dn = _bank(E, g), _bank(E, g)
+    orig = [(gu.qw[e].clone(), gu.sm[e].clone(), dn.qw[e].clone(), dn.sm[e].clone()) for e in range(E)]
+    layer = SimpleNamespace(is_moe=True, experts_gu=gu, experts_down=dn)
+    cache = ExpertCache([layer], 0.5, torch.device("cpu"))
+    b = cache.banks[0]
+    assert b.n_res == 4 and [s >= 0 for s in b.slot_of] == [True] * 4 + [False] * 4
+    st = ExpertStats(1, E)
+    st.observe(0, torch.tensor([5, 0, 9, 1, 8, 0, 0, 7]))
+    n = cache.rebalance(st, max_swaps_per_layer=4)
+    # cold residents 1 (0), 3 (1) leave for hot host experts 4 (8), 7 (7); 0 (5) vs 5/6 (0) stays
+    assert n == 2
+    assert b.resident_mask().tolist() == [True, False, True, False, True, False, False, True]
+    for e in range(E):
+        q, s = b.weight_of(0, e)
+        assert torch.equal(q, orig[e][0]) and torch.equal(s, orig[e][1])
+        q, s = b.weight_of(1, e)
+        assert torch.equal(q, orig[e][2]) and torch.equal(s, orig[e][3])
+        assert int(gu.qw_ptrs[e]) == b.weight_of(0, e)[0].data_ptr()
+        assert int(dn.sm_ptrs[e]) == b.weight_of(1, e)[1].data_ptr()
+    # a second pass with the same scores finds nothing worth moving
+    assert cache.rebalance(st, max_swaps_per_layer=4) == 0

@@ -14,7 +14,7 @@ from syntropy_b200.runtime.runner import ModelRunner
 pytestmark = pytest.mark.gpu
 
 
-def _run(cuda, prefetch):
+def _run(cuda, prefetch, rebalance_every=64, want_runner=False):
     cfg = get_config("small-qwen-moe")
     mw = prepare_weights(cfg, cuda, seed=21)
     cache = ExpertCache(mw.layers, 0.5, cuda)
@@ -24,8 +24,8 @@ def _run(cuda, prefetch):
     runner.expert_cache = cache
     g = torch.Generator().manual_seed(3)
     prompts = [torch.randint(0, cfg.vocab, (n,), generator=g).tolist() for n in (17, 40, 5, 64)]
-    outs = LLMEngine(runner).generate(prompts, SamplingParams(max_tokens=8))
-    return outs, cache
+    outs = LLMEngine(runner, rebalance_every=rebalance_every).generate(prompts, SamplingParams(max_tokens=8))
+    return (outs, cache, runner) if want_runner else (outs, cache)
 
 
 def test_prefetch_matches_and_stages(cuda):
@@ -43,3 +43,21 @@ def test_prefetch_matches_and_stages(cuda):
     assert staged, "no predicted host expert was staged"
     pred = b.pred.cpu().tolist()
     assert all(pred[b.e0 + e] for e in staged)
+
+
+def test_adaptation_between_graph_steps(cuda):
+    """Residency adapts every 2 decode steps (weights swapped, pointer tables rewritten in
+    place under the captured graphs): tokens do not change, and the routing kernels counted
+    every routed pair (prefill rows + decode rows, top_k each)."""
+    want, _ = _run(cuda, False)
+    got, cache, runner = _run(cuda, True, rebalance_every=2, want_runner=True)
+    assert got == want
+    st = runner.expert_stats
+    assert st is not None
+    k = runner.cfg.top_k
+    n_rows = (17 + 40 + 5 + 64) + 4 * 7  # prefill rows, then 7 decode steps of 4 rows
+    left = runner.route_counts.sum(1).cpu()  # counts since the last adaptation
+    for li, L in enumerate(cache.layers):
+        i = runner._layer_index[id(L)]
+        assert int(st.total[li].sum()) + int(left[i]) == n_rows * k
+    assert any(b.slot_of != list(range(b.n_res)) + [-1] * (b.E - b.n_res) for b in cache.banks), "no swap happened"

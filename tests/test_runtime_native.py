@@ -201,3 +201,21 @@ def test_step_desc_fill_matches_python_views():
     assert abs(h["temperature"][1].item() - 0.7) < 1e-6 and abs(h["top_p"][1].item() - 0.9) < 1e-6
     assert h["block_tables"][0, :2].tolist() == [4, 5] and h["block_tables"][1, :3].tolist() == [1, 2, 3]
     assert h["block_tables"][2, 0].item() == 0
+
+
+def test_arena_and_swap_planner():
+    """Native tier pieces: the arena reuses and coalesces ranges; the swap planner pairs the
+    coldest resident with the hottest host expert under hysteresis."""
+    from syntropy_b200._ext import ext
+    a = ext().Arena(1000)
+    x = a.alloc(100, 64)
+    y = a.alloc(300, 256)
+    z = a.alloc(200, 16)
+    assert x == 0 and y == 256 and z == 560 and a.used() == 600  # [100, 256) is too small for z
+    a.release(y)
+    a.release(z)
+    assert a.largest_free() == 1000 - 100 and a.alloc(800, 16) == 112
+    assert a.alloc(200, 16) == -1
+    plan = ext().tier_plan_swaps([1.0, 9.0, 0.5, 7.0, 0.0], [True, False, True, False, True], 5, 1.25)
+    assert plan == [(4, 1), (2, 3)]
+    assert ext().tier_plan_swaps([5.0, 5.5], [True, False], 3, 1.25) == []
