@@ -170,6 +170,7 @@ __global__ void __launch_bounds__(128) moe_topk_kernel(TopkArgs a) {
   __shared__ uint32_t s_mask[TOPK_MAX_E * (TOPK_MAX_T / 32)];
   __shared__ int s_ids[TOPK_MAX_T * TOPK_MAX_K];
   __shared__ int s_off[TOPK_MAX_E];
+  __shared__ uint32_t s_valid[TOPK_MAX_T / 32];  // rows that count toward the usage statistics
   __shared__ int s_last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int TW = (a.T + 31) >> 5;
@@ -203,6 +204,15 @@ __global__ void __launch_bounds__(128) moe_topk_kernel(TopkArgs a) {
     gmask[i] = 0u;
   }
   for (int i = threadIdx.x; i < a.T * a.k; i += blockDim.x) s_ids[i] = __ldcg(a.topk_ids + i);
+  if (a.counts)
+    for (int q = threadIdx.x; q < TW; q += blockDim.x) {
+      uint32_t v = 0u;
+      for (int b = 0; b < 32; ++b) {
+        const int tt = q * 32 + b;
+        if (tt < a.T && (!a.count_rows || a.count_rows[tt] >= 0)) v |= 1u << b;
+      }
+      s_valid[q] = v;
+    }
   if (a.pred_mask)
     for (int e = threadIdx.x; e < a.E; e += blockDim.x)
       a.pred_mask[e] = a.pred ? (int)((__ldcg(gpred + (e >> 5)) >> (e & 31)) & 1u) : 0;
@@ -238,13 +248,14 @@ __global__ void __launch_bounds__(128) moe_topk_kernel(TopkArgs a) {
       }
     }
     if (lane == 31) a.tok_off[a.E] = incl;
-    if (a.counts) {  // usage statistics for the expert cache
+    if (a.counts) {  // usage statistics for the expert cache (live rows only)
 #pragma unroll
       for (int i = 0; i < PER; ++i) {
         const int e = lane * PER + i;
         if (e < a.E) {
-          const int nxt = (i + 1 < PER) ? c[i + 1] : run;
-          a.counts[e] += nxt - c[i];
+          int n = 0;
+          for (int q = 0; q < TW; ++q) n += __popc(s_mask[e * TW + q] & s_valid[q]);
+          a.counts[e] += n;
         }
       }
     }

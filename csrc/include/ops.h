@@ -33,7 +33,8 @@ void router_logits(torch::Tensor h, torch::Tensor W, torch::Tensor logits);
 void moe_topk(torch::Tensor logits, torch::Tensor bias, int64_t E, int64_t k, int64_t scoring, int64_t n_groups,
               int64_t topk_groups, bool norm, double scaling, bool pred, torch::Tensor topk_ids, torch::Tensor topk_w,
               torch::Tensor tok_off, torch::Tensor tok_idx, torch::Tensor pair_w, torch::Tensor pair_of,
-              torch::Tensor pred_mask, torch::Tensor ws, torch::Tensor counts);
+              torch::Tensor pred_mask, torch::Tensor ws, torch::Tensor counts,
+              torch::Tensor count_rows);
 void argmax(torch::Tensor logits, torch::Tensor out);
 void sample(torch::Tensor logits, torch::Tensor temperature, torch::Tensor top_k, torch::Tensor top_p,
             torch::Tensor seed, torch::Tensor stream, torch::Tensor counter, torch::Tensor out);

@@ -166,6 +166,7 @@ struct TopkArgs {
   int32_t* pred_mask;    // [E] 1 if any token is predicted to use expert e at the next layer
   uint32_t* ws;          // zeroed workspace of TOPK_WS_WORDS words, left zeroed on exit
   int32_t* counts;       // [E] or null: += the number of pairs routed to each expert (usage statistics)
+  const int64_t* count_rows;  // [T] or null: only rows t with count_rows[t] >= 0 are counted (padding rows are not)
 };
 constexpr int TOPK_WS_WORDS = 512 * 8 + 16 + 1;
 cudaError_t launch_moe_topk(const TopkArgs& a, cudaStream_t s);

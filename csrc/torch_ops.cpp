@@ -241,7 +241,7 @@ void router_logits(torch::Tensor h, torch::Tensor W, torch::Tensor logits) {
 void moe_topk(torch::Tensor logits, torch::Tensor bias, int64_t E, int64_t k, int64_t scoring, int64_t n_groups,
               int64_t topk_groups, bool norm, double scaling, bool pred, torch::Tensor topk_ids, torch::Tensor topk_w,
               torch::Tensor tok_off, torch::Tensor tok_idx, torch::Tensor pair_w, torch::Tensor pair_of,
-              torch::Tensor pred_mask, torch::Tensor ws, torch::Tensor counts) {
+              torch::Tensor pred_mask, torch::Tensor ws, torch::Tensor counts, torch::Tensor count_rows) {
   SYN_CHECK_INPUT(logits);
   TORCH_CHECK(logits.scalar_type() == torch::kFloat32, "logits f32");
   const bool large = logits.size(0) > 256;
@@ -277,6 +277,10 @@ void moe_topk(torch::Tensor logits, torch::Tensor bias, int64_t E, int64_t k, in
   TORCH_CHECK(!counts.numel() || (counts.is_cuda() && counts.scalar_type() == torch::kInt32 && counts.numel() >= E &&
                                   counts.is_contiguous()), "moe_topk counts: int32 [E] on the device");
   a.counts = counts.numel() ? counts.data_ptr<int32_t>() : nullptr;
+  TORCH_CHECK(!count_rows.numel() || (count_rows.is_cuda() && count_rows.scalar_type() == torch::kInt64 &&
+                                      count_rows.numel() >= T), "moe_topk count_rows: int64 [T] on the device (step slots)");
+  a.count_rows = count_rows.numel() ? count_rows.data_ptr<int64_t>() : nullptr;
+  TORCH_CHECK(!(large && a.count_rows), "moe_topk: count_rows is for decode batches (at most 256 rows)");
   const at::cuda::CUDAGuard guard(logits.device());
   if (large) {
     SYN_CHECK_CUDA(launch_moe_route_large(a, cur_stream()));

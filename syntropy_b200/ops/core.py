@@ -544,9 +544,10 @@ def _topk_workspace(dev) -> torch.Tensor:
     return ws
 
 
-def moe_topk(logits, cfg, bias, pred: bool, bufs: dict, counts=None):
+def moe_topk(logits, cfg, bias, pred: bool, bufs: dict, counts=None, count_rows=None):
     """Top-k routing + CSR.  bufs: topk_ids, topk_w, tok_off, tok_idx, pair_w, pair_of, pred_mask.
-    counts (int32 [E], optional) accumulates the number of pairs routed to each expert."""
+    counts (int32 [E], optional) accumulates the number of pairs routed to each expert, over
+    the rows t with count_rows[t] >= 0 when count_rows (int64 [T], e.g. the step slots) is given."""
     E, k = cfg.n_experts, cfg.top_k
     T = logits.shape[0]
     scoring = 0 if cfg.router_scoring == "softmax" else 1
@@ -557,7 +558,8 @@ def moe_topk(logits, cfg, bias, pred: bool, bufs: dict, counts=None):
                        bufs["pred_mask"] if pred else _EMPTY_I32(logits.device),
                        _topk_workspace(logits.device) if T <= 256 else
                        torch.zeros(E * ((T + 31) // 32) + E, dtype=torch.int32, device=logits.device),
-                       counts if counts is not None else _EMPTY_I32(logits.device))
+                       counts if counts is not None else _EMPTY_I32(logits.device),
+                       count_rows if count_rows is not None and counts is not None else _EMPTY_I32(logits.device))
         _launched()
         return
     from ..models.reference import topk_stable
@@ -584,7 +586,8 @@ def moe_topk(logits, cfg, bias, pred: bool, bufs: dict, counts=None):
     bufs["topk_w"][:T] = w
     n_e = torch.bincount(ids.reshape(-1), minlength=E)
     if counts is not None:
-        counts[:E] += n_e.to(counts.dtype)
+        live = ids if count_rows is None else ids[count_rows[:T].cpu() >= 0]
+        counts[:E] += torch.bincount(live.reshape(-1), minlength=E).to(counts.dtype)
     off = torch.zeros(E + 1, dtype=torch.int64)
     off[1:] = torch.cumsum(n_e, 0)
     bufs["tok_off"][: E + 1] = off.int()

@@ -317,7 +317,9 @@ class ModelRunner:
         nxt_moe = pred and cache is not None and cache.prefetch and layer + 1 < len(mw.layers)
         if nxt_moe:  # the next layer's prediction goes to its own mask (read by the side stream)
             mb["pred_mask"] = mw.layers[layer + 1].expert_tier.pred
-        ops.moe_topk(rl, cfg, L.router_bias, pred, mb, counts=self._counts_of(layer))
+        # padding rows of the bucket (slot -1) route too, but are not counted
+        ops.moe_topk(rl, cfg, L.router_bias, pred, mb, counts=self._counts_of(layer),
+                     count_rows=self.desc.d["slot"][:B])
         if nxt_moe:
             # router-predicted prefetch of layer+1's host experts, overlapping this layer
             cur = torch.cuda.current_stream(self.device)

@@ -114,12 +114,18 @@ def test_moe_topk_matches_cpu(cuda, T):
 
     bc, bg = bufs("cpu"), bufs(cuda)
     ops.moe_topk(logits[:, :E].contiguous(), cfg, None, False, bc)
+    counts = torch.zeros(E, dtype=torch.int32, device=cuda)
+    # usage counts: decode batches skip rows marked -1 (bucket padding); prefill counts all
+    rows = torch.where(torch.arange(T) % 5 == 4, -1, 1) if pred_on else None
     for _ in range(2):  # the second call checks that the kernel left its workspace zeroed
-        ops.moe_topk(logits.to(cuda), cfg, None, pred_on, bg)
+        ops.moe_topk(logits.to(cuda), cfg, None, pred_on, bg, counts=counts,
+                     count_rows=rows.to(cuda) if rows is not None else None)
         for key in ("topk_ids", "tok_off", "tok_idx", "pair_of"):
             assert torch.equal(bc[key], bg[key].cpu()), key
         assert torch.allclose(bc["topk_w"], bg["topk_w"].cpu(), rtol=1e-5, atol=1e-6)
         assert torch.allclose(bc["pair_w"], bg["pair_w"].cpu(), rtol=1e-5, atol=1e-6)
+    live = bc["topk_ids"] if rows is None else bc["topk_ids"][rows >= 0]
+    assert torch.equal(counts.cpu(), 2 * torch.bincount(live.reshape(-1).long(), minlength=E).int())
     if not pred_on:
         return
     # prediction mask = union of the next layer's top-k
