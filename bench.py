@@ -106,6 +106,11 @@ def main():
                     help="decode steps between expert-cache adaptations (decayed-LFU swaps; 0 = never)")
     ap.add_argument("--expert-prefetch", type=int, default=1,
                     help="router-predicted prefetch of host-tier experts during decode (1 on, 0 off)")
+    ap.add_argument("--cpu-experts", type=float, default=None,
+                    help="share of each layer's host-tier experts computed by host CPU threads during decode "
+                         "(the rest is read over PCIe by the GPU); 0 = off (default 0.75 on one GPU with a VRAM "
+                         "cap, else 0)")
+    ap.add_argument("--cpu-threads", type=int, default=None, help="CPU expert threads (default: all but two cores)")
     ap.add_argument("--no-mtp", action="store_true", help="models with an MTP head: plain decoding instead of "
                     "MTP drafting + batched verification")
     args = ap.parse_args()
@@ -117,6 +122,8 @@ def main():
     args.decode = args.decode or dd
     if args.expert_cache_frac is None:
         args.expert_cache_frac = 0.6 if args.model == "qwen3-235b-a22b" else 1.0
+    if args.cpu_experts is None:
+        args.cpu_experts = 0.75 if args.expert_cache_frac < 1.0 else 0.0
 
     import torch
 
@@ -194,6 +201,11 @@ def main():
     runner = ModelRunner(mw, max_batch=B * (2 if use_mtp else 1), max_seq_len=max_len + 16, ep=ep, tp=tp, pp=pp,
                          use_graphs=graphs)
     runner.expert_cache = cache
+    tier = None
+    if cache is not None and args.cpu_experts > 0 and ep is None and tp is None and pp is None:
+        from syntropy_b200.experts.cpu_tier import CpuExpertTier
+        tier = CpuExpertTier(cache, cfg, max_rows=runner.max_batch, cpu_share=args.cpu_experts,
+                             threads=args.cpu_threads)
     spec = None
     if use_mtp:
         from syntropy_b200.runtime.spec import MTPDrafter, SpecConfig
@@ -268,6 +280,7 @@ def main():
         mtp_info = {"acceptance_rate": round(acc / max(1.0, drf), 4), "drafted": int(drf), "accepted": int(acc),
                     "tokens_per_seq_step": round(timed_tokens / (args.batch * args.steps), 4)}
     status = ep.check_status() if ep is not None else 0
+    tier_stats = tier.stats() if tier is not None else None
     uncapped = None
     if cache is not None and not args.no_uncapped:
         # same model and batch with every expert VRAM-resident (the cap lifted)
@@ -310,6 +323,8 @@ def main():
                    "host_tier_gb": round(cache.host_bytes() / 1e9, 2) if cache is not None else 0.0,
                    "expert_prefetch": bool(cache is not None and cache.prefetch),
                    "expert_rebalance_every": args.rebalance_every if cache is not None else 0,
+                   "cpu_expert_share": args.cpu_experts if tier is not None else 0.0,
+                   "cpu_expert_threads": tier.threads if tier is not None else 0,
                    "l2": f"inputs larger than L2 ({mw.nbytes() / 1e9:.0f} GB of weights streamed per step per rank)",
                    "weights_gb": round(mw.nbytes() / 1e9, 2), "weight_build_s": round(t_weights, 1)},
         "clocks": clk.summary(),
@@ -317,6 +332,7 @@ def main():
                 "d2h_bytes_per_step": 4 * B},
         "gpu_launches": (n_launch * args.steps) if n_launch else None,
         "impl": "syntropy",
+        "cpu_tier": tier_stats,
         "device_status": status,
         "all_experts_resident": uncapped,
     }
@@ -325,6 +341,8 @@ def main():
     if rank == 0:
         print(json.dumps(out))
     runner.graphs.clear()
+    if tier is not None:
+        tier.close()
     shutdown(ctx)
 
 

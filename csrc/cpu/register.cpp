@@ -35,6 +35,8 @@ void register_all(pybind11::module& m) {
   m.def("attn_decode", &attn_decode);
   m.def("router_logits", &router_logits);
   m.def("moe_topk", &moe_topk);
+  m.def("cpu_handoff", &cpu_handoff);
+  m.def("cpu_collect", &cpu_collect);
   m.def("argmax", &argmax);
   m.def("sample", &sample);
   m.def("philox", &philox);
@@ -56,6 +58,7 @@ void register_all(pybind11::module& m) {
   register_formats(m);
   register_dispatcher(m);
   register_tier(m);
+  register_cpu_experts(m);
 }
 
 }  // namespace syn

@@ -38,7 +38,8 @@ q4_gemv2_kernel(GemvArgs a) {
   const int g = lane >> 2, t = lane & 3;
   const int e = blockIdx.y;
   const int p0 = a.tok_off[e];
-  const int cnt = a.tok_off[e + 1] - p0;
+  // a null weight pointer marks an expert computed elsewhere (the host CPU): its pairs are skipped
+  const int cnt = a.qw_ptrs[e] ? a.tok_off[e + 1] - p0 : 0;
   const int n_units = a.N / (16 * R);
   const int unit = KS == 1 ? blockIdx.x * WARPS + warp : blockIdx.x;
   const int kw = KS == 1 ? 0 : warp;
@@ -269,7 +270,8 @@ __global__ void __launch_bounds__(128) q4_gemv3_kernel(GemvArgs a) {
   const int g = lane >> 2, t = lane & 3;
   const int e = blockIdx.y;
   const int p0 = a.tok_off[e];
-  const int cnt = a.tok_off[e + 1] - p0;
+  // a null weight pointer marks an expert computed elsewhere (the host CPU): its pairs are skipped
+  const int cnt = a.qw_ptrs[e] ? a.tok_off[e + 1] - p0 : 0;
   const int n_units = a.N / (16 * R);
   const int unit = blockIdx.x * C::WARPS + warp;
   const int KG = a.K >> 6, KB32 = a.K >> 5;
@@ -527,7 +529,8 @@ __global__ void __launch_bounds__(128) q4_gemv4_kernel(GemvArgs a) {
   const int g = lane >> 2, t = lane & 3;
   const int e = blockIdx.y;
   const int p0 = a.tok_off[e];
-  const int cnt = a.tok_off[e + 1] - p0;
+  // a null weight pointer marks an expert computed elsewhere (the host CPU): its pairs are skipped
+  const int cnt = a.qw_ptrs[e] ? a.tok_off[e + 1] - p0 : 0;
   const int n_units = a.N / 16;
   const int unit = blockIdx.x * C::WARPS + warp;
   const int KG = a.K >> 6;

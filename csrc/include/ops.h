@@ -101,7 +101,12 @@ void q4_gemv_dense(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs
                    torch::Tensor out, int64_t N, int64_t K, int64_t mode, torch::Tensor ws, torch::Tensor counters);
 void register_all(pybind11::module& m);
 void register_runtime(pybind11::module& m);
+void cpu_handoff(torch::Tensor h, torch::Tensor tok_off, torch::Tensor tok_idx, torch::Tensor pair_w, int64_t E,
+                 int64_t k, int64_t max_rows, int64_t mailbox, int64_t layer, torch::Tensor ctr);
+void cpu_collect(int64_t mailbox, int64_t E, int64_t k, int64_t max_rows, torch::Tensor ctr, torch::Tensor yp,
+                 double timeout_s, torch::Tensor status);
 void register_dispatcher(pybind11::module& m);
 void register_tier(pybind11::module& m);
+void register_cpu_experts(pybind11::module& m);
 void register_formats(pybind11::module& m);
 }  // namespace syn

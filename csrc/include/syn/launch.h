@@ -173,6 +173,27 @@ cudaError_t launch_moe_topk(const TopkArgs& a, cudaStream_t s);
 // Any T (no next-layer prediction); ws: zeroed E * ceil(T/32) + E words (not restored).
 cudaError_t launch_moe_route_large(const TopkArgs& a, cudaStream_t s);
 
+// ---- CPU expert hand-off (mailbox layout: syn/cpu_mailbox.h) ----
+struct CpuHandoffArgs {
+  const void* h;          // [B, H] bf16 rows of this layer (device)
+  int B, H, E, k, max_rows, layer;
+  const int32_t* tok_off; // [E+1] routing CSR (device)
+  const int32_t* tok_idx; // [B*k]
+  const float* pair_w;    // [B*k]
+  uint8_t* mb;            // host-mapped mailbox
+  uint32_t* ctr;          // device [2]: last sequence number, CTA arrivals (zero between launches)
+};
+struct CpuCollectArgs {
+  const uint8_t* mb;
+  int H, E, k, max_rows;
+  const uint32_t* ctr;    // the sequence number the hand-off raised
+  float* yp;              // [B*k, H] pair outputs of the grouped GEMVs (device)
+  uint64_t timeout_ns;
+  int* status;            // bit 0: the CPU did not answer in time; bit 1: the CPU reported bad input
+};
+cudaError_t launch_cpu_handoff(const CpuHandoffArgs& a, cudaStream_t s);
+cudaError_t launch_cpu_collect(const CpuCollectArgs& a, cudaStream_t s);
+
 // ---- sampling ----
 cudaError_t launch_argmax(const float* logits, int T, int V, int32_t* out, cudaStream_t s);
 cudaError_t launch_sample(const float* logits, int T, int V, const float* temperature, const int32_t* top_k,

@@ -810,5 +810,52 @@ void expert_prefetch(torch::Tensor pred, torch::Tensor host_row, int64_t e0, std
                                         sp, rb, lp, op, n, (int)ctas, cur_stream()));
 }
 
+
+void cpu_handoff(torch::Tensor h, torch::Tensor tok_off, torch::Tensor tok_idx, torch::Tensor pair_w, int64_t E,
+                 int64_t k, int64_t max_rows, int64_t mailbox, int64_t layer, torch::Tensor ctr) {
+  SYN_CHECK_INPUT(h);
+  TORCH_CHECK(h.scalar_type() == torch::kBFloat16 && h.dim() == 2, "h bf16 [B, H]");
+  TORCH_CHECK(tok_off.is_cuda() && tok_idx.is_cuda() && pair_w.is_cuda() && ctr.is_cuda(), "device CSR / counter");
+  TORCH_CHECK(tok_off.numel() >= E + 1 && tok_idx.numel() >= h.size(0) * k && pair_w.numel() >= h.size(0) * k,
+              "CSR sizes");
+  TORCH_CHECK(ctr.scalar_type() == torch::kInt32 && ctr.numel() >= 2, "ctr int32 [2]");
+  TORCH_CHECK(h.size(0) <= max_rows, "more rows than the mailbox holds");
+  CpuHandoffArgs a;
+  a.h = h.data_ptr();
+  a.B = (int)h.size(0);
+  a.H = (int)h.size(1);
+  a.E = (int)E;
+  a.k = (int)k;
+  a.max_rows = (int)max_rows;
+  a.layer = (int)layer;
+  a.tok_off = tok_off.data_ptr<int32_t>();
+  a.tok_idx = tok_idx.data_ptr<int32_t>();
+  a.pair_w = pair_w.data_ptr<float>();
+  a.mb = reinterpret_cast<uint8_t*>(mailbox);
+  a.ctr = reinterpret_cast<uint32_t*>(ctr.data_ptr<int32_t>());
+  const at::cuda::CUDAGuard guard(h.device());
+  SYN_CHECK_CUDA(launch_cpu_handoff(a, cur_stream()));
+}
+
+void cpu_collect(int64_t mailbox, int64_t E, int64_t k, int64_t max_rows, torch::Tensor ctr, torch::Tensor yp,
+                 double timeout_s, torch::Tensor status) {
+  SYN_CHECK_INPUT(yp);
+  TORCH_CHECK(yp.scalar_type() == torch::kFloat32 && yp.dim() == 2, "yp f32 [P, H]");
+  TORCH_CHECK(ctr.is_cuda() && status.is_cuda() && status.scalar_type() == torch::kInt32, "device ctr / status");
+  TORCH_CHECK(yp.size(0) >= 1, "yp rows");
+  CpuCollectArgs a;
+  a.mb = reinterpret_cast<const uint8_t*>(mailbox);
+  a.H = (int)yp.size(1);
+  a.E = (int)E;
+  a.k = (int)k;
+  a.max_rows = (int)max_rows;
+  a.ctr = reinterpret_cast<const uint32_t*>(ctr.data_ptr<int32_t>());
+  a.yp = yp.data_ptr<float>();
+  a.timeout_ns = (uint64_t)(timeout_s * 1e9);
+  a.status = status.data_ptr<int32_t>();
+  const at::cuda::CUDAGuard guard(yp.device());
+  SYN_CHECK_CUDA(launch_cpu_collect(a, cur_stream()));
+}
+
 }  // namespace syn
 

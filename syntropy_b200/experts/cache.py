@@ -76,6 +76,7 @@ class ExpertCache:
             L.expert_tier = b
         self._staging = None
         self.prefetch = False
+        self.cpu_tier = None  # experts.cpu_tier.CpuExpertTier when host experts run on the CPU
         # CTAs of the prefetch kernel (the rest of the GPU stays with the current layer)
         self.prefetch_ctas = int(__import__("os").environ.get("SYN_PREFETCH_CTAS", "64"))
 
@@ -167,6 +168,8 @@ class ExpertCache:
                 b.refresh_home()
         if not self.prefetch:
             self._staging = None
+        if self.cpu_tier is not None:  # nothing is left on the host: the CPU owns no expert
+            self.cpu_tier.assign()
         torch.cuda.empty_cache()
 
     def staged_ptrs(self, L):
@@ -276,6 +279,8 @@ class ExpertCache:
             for cold_res, hot_host in plan:
                 b.swap(cold_res, hot_host)
                 n += 1
+        if n and getattr(self, "cpu_tier", None) is not None:
+            self.cpu_tier.assign()  # the host set changed: re-split it between the CPU and PCIe
         return n
 
 
@@ -288,6 +293,7 @@ class _TieredBank:
         self.e0 = gu.e0
         self.home = None
         self.host_row_dev = None
+        self.cpu_owned: set[int] = set()  # local experts computed by the host CPU (null pointers here)
         self.n_res = max(0, min(self.E, int(math.floor(frac * self.E + 1e-9))))
         self.slot_of = list(range(self.n_res)) + [-1] * (self.E - self.n_res)  # expert -> vram slot
         self.host_of = [-1] * self.n_res + list(range(self.E - self.n_res))    # expert -> host row
@@ -317,7 +323,10 @@ class _TieredBank:
         qp, sp = [], []
         for e in range(self.E):
             s = self.slot_of[e]
-            if s >= 0:
+            if e in self.cpu_owned:  # the GEMVs skip experts with a null weight pointer
+                qp.append(0)
+                sp.append(0)
+            elif s >= 0:
                 qp.append(qv.data_ptr() + s * qv.stride(0) * qv.element_size())
                 sp.append(sv.data_ptr() + s * sv.stride(0) * sv.element_size())
             else:
@@ -333,11 +342,20 @@ class _TieredBank:
             bank.qw_ptrs.copy_(new_q)
             bank.sm_ptrs.copy_(new_s)
 
+    def rewrite_ptrs(self):
+        """Rewrite the live pointer tables in place (after a change of ownership)."""
+        for p in self.parts:
+            if p is not None:
+                self._write_ptrs(p["bank"], p["qv"], p["sv"], p["qh"], p["sh"])
+        if self.home is not None:
+            self.refresh_home()
+
     def refresh_home(self):
         """Snapshot the home pointer tables (resident slot or host row per expert) and the
         host-row map used by the decode prefetch kernel."""
-        rows = torch.tensor([self.host_of[e] if self.slot_of[e] < 0 else -1 for e in range(self.E)],
-                            dtype=torch.int32)
+        # experts the host CPU computes are never staged (the GPU skips them)
+        rows = torch.tensor([self.host_of[e] if self.slot_of[e] < 0 and e not in self.cpu_owned else -1
+                             for e in range(self.E)], dtype=torch.int32)
         if self.home is None:
             self.home = [(p["bank"].qw_ptrs.clone(), p["bank"].sm_ptrs.clone()) if p is not None else None
                          for p in self.parts]

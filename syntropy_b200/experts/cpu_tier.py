@@ -1,0 +1,110 @@
+"""Cold experts computed on the host CPU during decode, next to the PCIe path.
+
+With a VRAM cap, every MoE layer has host experts.  The GPU can read them over PCIe in place
+(the grouped GEMV takes host pointers), which is bound by the link (~50 GB/s).  The host's own
+DRAM bandwidth is a second, independent resource: a share of the host experts
+(``cpu_share``) is computed by a pool of CPU threads (AVX-512 BF16 over the same tiled 4-bit
+rows, ``csrc/cpu/cpu_experts.cpp``) while the GPU streams the resident experts and the
+remaining host experts.  Per MoE layer of a decode step:
+
+1. routing on the GPU; ``cpu_handoff`` copies the layer's rows and routing CSR into a pinned
+   mailbox and raises its go word;
+2. the GPU runs its grouped GEMVs, which skip the CPU's experts (null weight pointers in the
+   layer's tables); the CPU threads compute theirs at the same time;
+3. ``cpu_collect`` waits for the done word (with a time limit: a missing CPU answer sets a
+   status bit instead of hanging the GPU) and copies the CPU rows into the pair outputs;
+4. the ordered combine runs as before.
+
+All of it is captured in the decode CUDA graphs (the sequence number lives on the device).
+
+Reference: crates/kernels-cpu/src/moe.rs (expert misses on the CPU), crates/kernels/src/moe/
+doorbell.rs and split.rs (host-mapped doorbell, hit / miss / CPU sites).
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from .._ext import ext
+
+
+class CpuExpertTier:
+    """Owns the mailbox, the CPU thread pool and the split of each layer's host experts."""
+
+    def __init__(self, cache, cfg, max_rows: int, cpu_share: float = 0.75, threads: int | None = None,
+                 cpus: list[int] | None = None, timeout_s: float = 2.0):
+        self.cache, self.cfg = cache, cfg
+        self.E, self.k, self.H, self.I = cfg.n_experts, cfg.top_k, cfg.hidden, cfg.moe_ffn
+        self.max_rows = max_rows
+        self.cpu_share = cpu_share
+        self.timeout_s = timeout_s
+        self.device = cache.device
+        lay = ext().cpu_mailbox_bytes(self.E, self.k, max_rows, self.H)
+        self.mailbox = torch.zeros(lay[-1], dtype=torch.uint8, pin_memory=True)
+        self.mb_ptr = self.mailbox.data_ptr()
+        self.ctr = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        if cpus is None:
+            allowed = sorted(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else []
+            # the launching thread and the driver keep the first cores
+            cpus = allowed[2:] if len(allowed) > 4 else allowed
+        if threads is None:
+            threads = int(os.environ.get("SYN_CPU_EXPERT_THREADS", max(1, len(cpus))))
+        self.threads = threads
+        self.native = ext().CpuExpertTier(len(cache.layers), self.E, self.H, self.I, self.k, max_rows,
+                                          self.mb_ptr, list(cpus), threads, True)
+        self.layer_of = {id(L): li for li, L in enumerate(cache.layers)}
+        cache.cpu_tier = self
+        self.assign()
+        self.native.start()
+
+    # ------------------------------------------------------------------ split
+    def assign(self):
+        """Give the CPU `cpu_share` of every layer's host experts (by index order, after the
+        cache's residency decisions); the GPU's pointer tables get nulls for them."""
+        for li, b in enumerate(self.cache.banks):
+            host = [e for e in range(b.E) if b.slot_of[e] < 0]
+            n_cpu = int(round(self.cpu_share * len(host)))
+            mine = set(host[:n_cpu])
+            b.cpu_owned = mine
+            for e in range(b.E):
+                eg = b.e0 + e
+                if e in mine:
+                    h = b.host_of[e]
+                    gu, dn = b.parts
+                    self.native.set_expert(li, eg, gu["qh"][h].data_ptr(), gu["sh"][h].data_ptr(),
+                                           dn["qh"][h].data_ptr(), dn["sh"][h].data_ptr())
+                else:
+                    self.native.set_expert(li, eg, 0, 0, 0, 0)
+            b.rewrite_ptrs()
+
+    def owns_layer(self, L) -> bool:
+        li = self.layer_of.get(id(L))
+        return li is not None and bool(self.cache.banks[li].cpu_owned)
+
+    # ------------------------------------------------------------------ per layer (decode)
+    def handoff(self, L, h, mb):
+        """Publish layer L's rows (bf16 [B, H]) and routing CSR to the CPU threads."""
+        ext().cpu_handoff(h, mb["tok_off"], mb["tok_idx"], mb["pair_w"], self.E, self.k, self.max_rows,
+                          self.mb_ptr, self.layer_of[id(L)], self.ctr)
+
+    def collect(self, yp):
+        """Wait for the CPU's rows and place them into the pair outputs yp (f32 [B*k, H])."""
+        ext().cpu_collect(self.mb_ptr, self.E, self.k, self.max_rows, self.ctr, yp, self.timeout_s, self.status)
+
+    def check(self):
+        """Raise if a hand-off timed out or the CPU rejected its input (device status word)."""
+        s = int(self.status.item())
+        if s:
+            from ..core.errors import KERNELS_DOORBELL_TIMEOUT, Domain, ErrorClass, SynError
+            self.status.zero_()
+            raise SynError(ErrorClass.TIMEOUT, f"CPU expert tier: status {s:#x} (1: no answer within "
+                           f"{self.timeout_s} s, 2: the CPU rejected the hand-off)", Domain.KERNELS,
+                           KERNELS_DOORBELL_TIMEOUT)
+
+    def stats(self) -> dict:
+        return dict(self.native.stats())
+
+    def close(self):
+        self.native.stop()

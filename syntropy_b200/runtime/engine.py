@@ -332,6 +332,7 @@ class LLMEngine:
         stream = torch.tensor([s.stream for s in seqs], dtype=torch.int64)
         ctr = torch.tensor([s.rng_counter for s in seqs], dtype=torch.int64)
         toks, nacc = verify(logits, torch.tensor(drafts, dtype=torch.int32), temp, topk, topp, seed, stream, ctr)
+        r.after_step()
         self.stats["decode_steps"] += 1
         outs = []
         mtp_items = []
@@ -379,6 +380,7 @@ class LLMEngine:
                              [float(s.params.temperature) for s in seqs], [float(s.params.top_p) for s in seqs],
                              [s.blocks for s in seqs], bucket_for(B) if r.use_graphs else B)
         nxt = r.decode(B).cpu().tolist()
+        r.after_step()
         # greedy rows take no draw; sampled rows take exactly one
         for s in seqs:
             if s.params.temperature > 0:

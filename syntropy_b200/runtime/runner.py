@@ -343,12 +343,26 @@ class ModelRunner:
             return
         mid = b["moe_mid"][:B * k]
         yp = b["moe_out"][:B * k]
+        tier = cache.cpu_tier if cache is not None else None
+        if tier is not None:  # the host CPU computes its share of the cold experts meanwhile
+            tier.handoff(L, h, mb)
+            ops.core._launched()
         shared = self._shared_expert(L, h) if L.shared_gu is not None else None
         ops.linear_grouped(h, gu, mb["tok_off"], mb["tok_idx"], mid, ops.GEMV_SWIGLU,
                            qw_ptrs=gu.qw_ptrs, sm_ptrs=gu.sm_ptrs)
         ops.linear_grouped(mid, dn, mb["tok_off"], None, yp, ops.GEMV_SCALED_F32, route_w=mb["pair_w"],
                            qw_ptrs=dn.qw_ptrs, sm_ptrs=dn.sm_ptrs)
+        if tier is not None:
+            tier.collect(yp)
+            ops.core._launched()
         ops.moe_combine_rmsnorm(x, yp, mb["pair_of"], shared, nw, h, cfg.rms_eps)
+
+    def after_step(self):
+        """Host-side checks after a decode step has been synchronised (device status words of
+        the CPU expert hand-off)."""
+        tier = self.expert_cache.cpu_tier if self.expert_cache is not None else None
+        if tier is not None:
+            tier.check()
 
     def _counts_of(self, layer: int):
         return self.route_counts[layer] if self.route_counts is not None and self.expert_cache is not None else None
