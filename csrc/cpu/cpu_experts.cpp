@@ -7,13 +7,16 @@
 // no copy.  In that layout the 64 bytes of lanes 4g..4g+3 of one (16-row tile, 64-column group)
 // hold rows g and g+8 over all 64 columns, and ((word >> 4j) & 0x000F000F) is a pair of
 // consecutive columns of one row (j = 0, 2: row g; j = 1, 3: row g+8; j = 2, 3 are 8 columns
-// further).  OR-ing 0x4300 into a nibble gives the bf16 number 128 + q exactly, so one
-// `vdpbf16ps` multiplies 16 weight pairs by the matching bf16 activation pairs exactly and adds
-// them in f32.  Per 32-column block with scale d and min m:
-//     sum_k (d q_k + m) x_k = d * sum_k (128 + q_k) x_k + (m - 128 d) * sum_k x_k.
-// Each activation row is packed once per layer into the pair order of the layout, with its
-// per-block sums.  Products are exact, sums are f32: the result differs from the GPU kernels
-// only by the order of f32 additions.
+// further).  Two kernel families consume these pairs (each activation row is packed once per
+// layer into the same pair order, with its per-block sums):
+//  * BF16 (default): OR-ing 0x4300 into a nibble gives the bf16 number 128 + q exactly, so
+//    `vdpbf16ps` multiplies bf16 pairs exactly and
+//        sum_k (d q_k + m) x_k = d * sum_k (128 + q_k) x_k + (m - 128 d) * sum_k x_k;
+//  * VNNI (hosts with AVX-512 VNNI but no BF16): the activation's 32-column block is scaled to
+//    int16 (s = max|x| / 32767, rounding error at most s / 2 per element), `vpdpwssd` sums
+//    q * v exactly in int32, and y ~= d * s * sum_k q_k v_k + m * sum_k x_k (sum x exact).
+// Both agree with the f32 product to ~1e-5 relative and ran at the same speed on a B200 node's
+// host (the pool is bound by the per-row work around the dot products, not by them).
 //
 // Threads: a fixed pool pinned to the given CPUs.  Thread 0 polls the mailbox's go word; on a
 // new sequence it lists the routed pairs of the experts this tier owns for that layer and
@@ -30,6 +33,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <thread>
 #include <vector>
@@ -97,67 +101,207 @@ void pack_row(const uint16_t* x, int K, uint32_t* ab, float* sx4) {
   }
 }
 
-// y[r][n] = scale[r] * sum_k W[n][k] x_r[k] for the rows of tiles [tile0, tile1), NR rows.
-template <int NR>
-__attribute__((target("avx512f,avx512bw,avx512vl,avx512bf16,f16c,fma"))) void tiles_avx512(
+// Integer form of a row for the VNNI kernel: per 32-column block b, s_b = max|x| / 32767 and
+// v_k = round(x_k / s_b) as int16 (|x_k - s_b v_k| <= s_b / 2), packed in the same pair order
+// as `pack_row`; sxs holds, per 64-column group, s_b at the 16 dword lanes (block of lane i is
+// (i & 3) >> 1); sx4 the exact block sums of x as (s0, 0, s1, 0).
+void pack_row_i16(const uint16_t* x, int K, uint32_t* ab, float* sxs, float* sx4) {
+  const int KG = K >> 6;
+  for (int kg = 0; kg < KG; ++kg) {
+    float sc[2];
+    int16_t v[64];
+    for (int b = 0; b < 2; ++b) {
+      float amax = 0.f, sum = 0.f;
+      for (int j = 0; j < 32; ++j) {
+        const float f = bf2f_h(x[64 * kg + 32 * b + j]);
+        amax = std::max(amax, std::fabs(f));
+        sum += f;
+      }
+      sc[b] = amax > 0.f ? amax / 32767.f : 1.f;
+      const float inv = 1.f / sc[b];
+      for (int j = 0; j < 32; ++j) {
+        const float q = std::nearbyint(bf2f_h(x[64 * kg + 32 * b + j]) * inv);
+        v[32 * b + j] = (int16_t)std::max(-32767.f, std::min(32767.f, q));
+      }
+      sx4[kg * 4 + 2 * b] = sum;
+      sx4[kg * 4 + 2 * b + 1] = 0.f;
+    }
+    for (int i = 0; i < 16; ++i) {
+      const int t = i >> 2, w = i & 3;
+      const int k = 32 * (w >> 1) + 16 * (w & 1) + 2 * t;
+      ab[kg * 32 + i] = (uint32_t)(uint16_t)v[k] | ((uint32_t)(uint16_t)v[k + 1] << 16);
+      ab[kg * 32 + 16 + i] = (uint32_t)(uint16_t)v[k + 8] | ((uint32_t)(uint16_t)v[k + 9] << 16);
+      sxs[kg * 16 + i] = sc[w >> 1];
+    }
+  }
+}
+
+// VNNI form of the product: nibble pairs as int16 (no magic number), activation pairs as int16,
+// vpdpwssd sums q * v exactly in int32 per block; then y += d * s * sum + m * sum(x).
+template <int NR, int GB>
+__attribute__((target("avx512f,avx512bw,avx512vl,avx512vnni,f16c,fma"))) void tiles_vnni(
+    const uint32_t* qw, const uint16_t* sm, int K, int tile0, int tile1, const uint32_t* const* ab,
+    const float* const* sxs, const float* const* sx4, float* const* y, const float* scale) {
+  const int KG = K >> 6;
+  const __m512i M = _mm512_set1_epi32(0x000F000F);
+  __m512i idx[4];
+  for (int j = 0; j < 4; ++j)
+    idx[j] = _mm512_add_epi32(_mm512_set1_epi32(4 * j), _mm512_set_epi32(2, 2, 0, 0, 2, 2, 0, 0, 2, 2, 0, 0, 2, 2, 0, 0));
+  const __m512i swap = _mm512_set_epi32(14, 15, 12, 13, 10, 11, 8, 9, 6, 7, 4, 5, 2, 3, 0, 1);
+  for (int tile = tile0; tile < tile1; ++tile) {
+    const uint32_t* wt = qw + (int64_t)tile * KG * 128;
+    const uint16_t* st = sm + (int64_t)tile * KG * 64;
+    alignas(64) float cmin[NR][64];  // m * sum(x): row r of the tile at lanes 4*(r%4) + {0, 2} of vector r/4
+    for (int r = 0; r < NR; ++r)
+      for (int i = 0; i < 64; ++i) cmin[r][i] = 0.f;
+    for (int kg = 0; kg < KG; ++kg) {
+      const uint16_t* s = st + kg * 64;
+      for (int q = 0; q < 4; ++q) {
+        const __m512 F = _mm512_cvtph_ps(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(s + 16 * q)));
+        const __m512 G = _mm512_permutexvar_ps(swap, F);  // m at the even lanes
+        for (int r = 0; r < NR; ++r) {
+          const __m512 S = _mm512_broadcast_f32x4(_mm_loadu_ps(sx4[r] + kg * 4));
+          _mm512_store_ps(&cmin[r][16 * q], _mm512_fmadd_ps(G, S, _mm512_load_ps(&cmin[r][16 * q])));
+        }
+      }
+    }
+    for (int g0 = 0; g0 < 8; g0 += GB) {
+      __m512 alo[GB][NR], ahi[GB][NR];
+      for (int gg = 0; gg < GB; ++gg)
+        for (int r = 0; r < NR; ++r) {
+          alo[gg][r] = _mm512_setzero_ps();
+          ahi[gg][r] = _mm512_setzero_ps();
+        }
+      for (int kg = 0; kg < KG; ++kg) {
+        const uint32_t* wp = wt + kg * 128 + 16 * g0;
+        for (int l = 0; l < GB; ++l) _mm_prefetch(reinterpret_cast<const char*>(wp + 4 * 128 + 16 * l), _MM_HINT_T0);
+        __m512i xa[NR], xb[NR];
+        __m512 xs[NR];
+        for (int r = 0; r < NR; ++r) {
+          xa[r] = _mm512_loadu_si512(ab[r] + kg * 32);
+          xb[r] = _mm512_loadu_si512(ab[r] + kg * 32 + 16);
+          xs[r] = _mm512_loadu_ps(sxs[r] + kg * 16);
+        }
+        const uint16_t* s = st + kg * 64;
+#pragma unroll
+        for (int gg = 0; gg < GB; ++gg) {
+          const int g = g0 + gg;
+          const __m512 Flo = _mm512_cvtph_ps(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(s + 16 * (g >> 2))));
+          const __m512 Fhi =
+              _mm512_cvtph_ps(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(s + 16 * ((g + 8) >> 2))));
+          const __m512 Dlo = _mm512_permutexvar_ps(idx[g & 3], Flo);
+          const __m512 Dhi = _mm512_permutexvar_ps(idx[g & 3], Fhi);
+          const __m512i W = _mm512_loadu_si512(wp + 16 * gg);
+          const __m512i v0 = _mm512_and_si512(W, M);
+          const __m512i v1 = _mm512_and_si512(_mm512_srli_epi32(W, 4), M);
+          const __m512i v2 = _mm512_and_si512(_mm512_srli_epi32(W, 8), M);
+          const __m512i v3 = _mm512_and_si512(_mm512_srli_epi32(W, 12), M);
+          for (int r = 0; r < NR; ++r) {
+            const __m512i t = _mm512_dpwssd_epi32(_mm512_dpwssd_epi32(_mm512_setzero_si512(), v0, xa[r]), v2, xb[r]);
+            const __m512i u = _mm512_dpwssd_epi32(_mm512_dpwssd_epi32(_mm512_setzero_si512(), v1, xa[r]), v3, xb[r]);
+            alo[gg][r] = _mm512_fmadd_ps(_mm512_cvtepi32_ps(t), _mm512_mul_ps(Dlo, xs[r]), alo[gg][r]);
+            ahi[gg][r] = _mm512_fmadd_ps(_mm512_cvtepi32_ps(u), _mm512_mul_ps(Dhi, xs[r]), ahi[gg][r]);
+          }
+        }
+      }
+      for (int gg = 0; gg < GB; ++gg)
+        for (int r = 0; r < NR; ++r) {
+          const int g = g0 + gg;
+          const float* clo = &cmin[r][16 * (g >> 2) + 4 * (g & 3)];
+          const float* chi = &cmin[r][16 * ((g + 8) >> 2) + 4 * (g & 3)];
+          const float lo = _mm512_reduce_add_ps(alo[gg][r]) + clo[0] + clo[2];
+          const float hi = _mm512_reduce_add_ps(ahi[gg][r]) + chi[0] + chi[2];
+          y[r][tile * 16 + g] = lo * scale[r];
+          y[r][tile * 16 + g + 8] = hi * scale[r];
+        }
+    }
+  }
+}
+
+// Same product with the per-k-group scale work hoisted out of the row loop: the 16 rows' (d, m)
+// pairs of a k-group are converted once (4 vcvtph2ps), each row pair's scale vectors are one
+// permute away, and the min term sum (m - 128 d) * sum(x) is accumulated for all 16 rows at
+// once into a small per-row array.  k-groups outer, GB row pairs (g) per pass.
+template <int NR, int GB>
+__attribute__((target("avx512f,avx512bw,avx512vl,avx512bf16,f16c,fma"))) void tiles_avx512_v2(
     const uint32_t* qw, const uint16_t* sm, int K, int tile0, int tile1, const uint32_t* const* ab,
     const float* const* sx4, float* const* y, const float* scale) {
   const int KG = K >> 6;
   const __m512i M = _mm512_set1_epi32(0x000F000F), C = _mm512_set1_epi32(0x43004300);
-  // dword i of a 64-byte row slice belongs to 32-column block ((i & 3) >> 1); the converted
-  // scale quad is (d0, m0, d1, m1)
-  const __m512i idx = _mm512_set_epi32(2, 2, 0, 0, 2, 2, 0, 0, 2, 2, 0, 0, 2, 2, 0, 0);
-  const __m128 c128 = _mm_set1_ps(128.f);
+  // converted scale vector q holds rows 4q..4q+3 as (d0, m0, d1, m1); row 4q+j's d pattern for
+  // dword i is element 4j + ((i & 3) >> 1) * 2
+  __m512i idx[4];
+  for (int j = 0; j < 4; ++j)
+    idx[j] = _mm512_add_epi32(_mm512_set1_epi32(4 * j), _mm512_set_epi32(2, 2, 0, 0, 2, 2, 0, 0, 2, 2, 0, 0, 2, 2, 0, 0));
+  const __m512 c128 = _mm512_set1_ps(128.f);
+  const __m512i swap = _mm512_set_epi32(14, 15, 12, 13, 10, 11, 8, 9, 6, 7, 4, 5, 2, 3, 0, 1);
   for (int tile = tile0; tile < tile1; ++tile) {
     const uint32_t* wt = qw + (int64_t)tile * KG * 128;
     const uint16_t* st = sm + (int64_t)tile * KG * 64;
-    for (int g = 0; g < 8; ++g) {
-      __m512 alo[NR], ahi[NR];
-      __m128 clo[NR], chi[NR];
-      for (int r = 0; r < NR; ++r) {
-        alo[r] = _mm512_setzero_ps();
-        ahi[r] = _mm512_setzero_ps();
-        clo[r] = _mm_setzero_ps();
-        chi[r] = _mm_setzero_ps();
-      }
-      const uint32_t* wp = wt + 16 * g;
-      for (int kg = 0; kg < KG; ++kg) {
-        _mm_prefetch(reinterpret_cast<const char*>(wp + (kg + 6) * 128), _MM_HINT_T0);
-        const __m512i W = _mm512_loadu_si512(wp + kg * 128);
-        const __m512i v0 = _mm512_ternarylogic_epi32(W, M, C, 0xEA);  // (W & M) | C
-        const __m512i v1 = _mm512_ternarylogic_epi32(_mm512_srli_epi32(W, 4), M, C, 0xEA);
-        const __m512i v2 = _mm512_ternarylogic_epi32(_mm512_srli_epi32(W, 8), M, C, 0xEA);
-        const __m512i v3 = _mm512_ternarylogic_epi32(_mm512_srli_epi32(W, 12), M, C, 0xEA);
-        const uint16_t* s = st + kg * 64;
-        const __m128 flo = _mm_cvtph_ps(_mm_loadl_epi64(reinterpret_cast<const __m128i*>(s + g * 4)));
-        const __m128 fhi = _mm_cvtph_ps(_mm_loadl_epi64(reinterpret_cast<const __m128i*>(s + (g + 8) * 4)));
-        const __m512 Dlo = _mm512_permutexvar_ps(idx, _mm512_castps128_ps512(flo));
-        const __m512 Dhi = _mm512_permutexvar_ps(idx, _mm512_castps128_ps512(fhi));
-        // (m - 128 d) in lanes 0 and 2
-        const __m128 glo = _mm_fnmadd_ps(c128, flo, _mm_permute_ps(flo, 0xB1));
-        const __m128 ghi = _mm_fnmadd_ps(c128, fhi, _mm_permute_ps(fhi, 0xB1));
+    alignas(64) float cmin[NR][64];  // per row r of the tile: lanes 4*(r%4) + {0, 2} of vector r/4
+    for (int r = 0; r < NR; ++r)
+      for (int i = 0; i < 64; ++i) cmin[r][i] = 0.f;
+    // min term for the whole tile
+    for (int kg = 0; kg < KG; ++kg) {
+      const uint16_t* s = st + kg * 64;
+      for (int q = 0; q < 4; ++q) {
+        const __m512 F = _mm512_cvtph_ps(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(s + 16 * q)));
+        const __m512 G = _mm512_fnmadd_ps(c128, F, _mm512_permutexvar_ps(swap, F));  // m - 128 d at even lanes
         for (int r = 0; r < NR; ++r) {
-          const uint32_t* xp = ab[r] + kg * 32;
-          const __m512i xa = _mm512_loadu_si512(xp), xb = _mm512_loadu_si512(xp + 16);
-          __m512 t = _mm512_dpbf16_ps(_mm512_setzero_ps(), (__m512bh)v0, (__m512bh)xa);
-          t = _mm512_dpbf16_ps(t, (__m512bh)v2, (__m512bh)xb);
-          alo[r] = _mm512_fmadd_ps(t, Dlo, alo[r]);
-          __m512 u = _mm512_dpbf16_ps(_mm512_setzero_ps(), (__m512bh)v1, (__m512bh)xa);
-          u = _mm512_dpbf16_ps(u, (__m512bh)v3, (__m512bh)xb);
-          ahi[r] = _mm512_fmadd_ps(u, Dhi, ahi[r]);
-          const __m128 sx = _mm_loadu_ps(sx4[r] + kg * 4);
-          clo[r] = _mm_fmadd_ps(glo, sx, clo[r]);
-          chi[r] = _mm_fmadd_ps(ghi, sx, chi[r]);
+          const __m512 S = _mm512_broadcast_f32x4(_mm_loadu_ps(sx4[r] + kg * 4));
+          _mm512_store_ps(&cmin[r][16 * q], _mm512_fmadd_ps(G, S, _mm512_load_ps(&cmin[r][16 * q])));
         }
       }
-      for (int r = 0; r < NR; ++r) {
-        const float lo = _mm512_reduce_add_ps(alo[r]) + _mm_cvtss_f32(clo[r]) +
-                         _mm_cvtss_f32(_mm_movehl_ps(clo[r], clo[r]));
-        const float hi = _mm512_reduce_add_ps(ahi[r]) + _mm_cvtss_f32(chi[r]) +
-                         _mm_cvtss_f32(_mm_movehl_ps(chi[r], chi[r]));
-        y[r][tile * 16 + g] = lo * scale[r];
-        y[r][tile * 16 + g + 8] = hi * scale[r];
+    }
+    for (int g0 = 0; g0 < 8; g0 += GB) {
+      __m512 alo[GB][NR], ahi[GB][NR];
+      for (int gg = 0; gg < GB; ++gg)
+        for (int r = 0; r < NR; ++r) {
+          alo[gg][r] = _mm512_setzero_ps();
+          ahi[gg][r] = _mm512_setzero_ps();
+        }
+      for (int kg = 0; kg < KG; ++kg) {
+        const uint32_t* wp = wt + kg * 128 + 16 * g0;
+        for (int l = 0; l < GB; ++l) _mm_prefetch(reinterpret_cast<const char*>(wp + 4 * 128 + 16 * l), _MM_HINT_T0);
+        __m512i xa[NR], xb[NR];
+        for (int r = 0; r < NR; ++r) {
+          xa[r] = _mm512_loadu_si512(ab[r] + kg * 32);
+          xb[r] = _mm512_loadu_si512(ab[r] + kg * 32 + 16);
+        }
+        const uint16_t* s = st + kg * 64;
+#pragma unroll
+        for (int gg = 0; gg < GB; ++gg) {
+          const int g = g0 + gg;
+          const __m512 Flo = _mm512_cvtph_ps(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(s + 16 * (g >> 2))));
+          const __m512 Fhi =
+              _mm512_cvtph_ps(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(s + 16 * ((g + 8) >> 2))));
+          const __m512 Dlo = _mm512_permutexvar_ps(idx[g & 3], Flo);
+          const __m512 Dhi = _mm512_permutexvar_ps(idx[g & 3], Fhi);
+          const __m512i W = _mm512_loadu_si512(wp + 16 * gg);
+          const __m512i v0 = _mm512_ternarylogic_epi32(W, M, C, 0xEA);
+          const __m512i v1 = _mm512_ternarylogic_epi32(_mm512_srli_epi32(W, 4), M, C, 0xEA);
+          const __m512i v2 = _mm512_ternarylogic_epi32(_mm512_srli_epi32(W, 8), M, C, 0xEA);
+          const __m512i v3 = _mm512_ternarylogic_epi32(_mm512_srli_epi32(W, 12), M, C, 0xEA);
+          for (int r = 0; r < NR; ++r) {
+            __m512 t = _mm512_dpbf16_ps(_mm512_setzero_ps(), (__m512bh)v0, (__m512bh)xa[r]);
+            t = _mm512_dpbf16_ps(t, (__m512bh)v2, (__m512bh)xb[r]);
+            alo[gg][r] = _mm512_fmadd_ps(t, Dlo, alo[gg][r]);
+            __m512 u = _mm512_dpbf16_ps(_mm512_setzero_ps(), (__m512bh)v1, (__m512bh)xa[r]);
+            u = _mm512_dpbf16_ps(u, (__m512bh)v3, (__m512bh)xb[r]);
+            ahi[gg][r] = _mm512_fmadd_ps(u, Dhi, ahi[gg][r]);
+          }
+        }
       }
+      for (int gg = 0; gg < GB; ++gg)
+        for (int r = 0; r < NR; ++r) {
+          const int g = g0 + gg;
+          const float* clo = &cmin[r][16 * (g >> 2) + 4 * (g & 3)];
+          const float* chi = &cmin[r][16 * ((g + 8) >> 2) + 4 * (g & 3)];
+          const float lo = _mm512_reduce_add_ps(alo[gg][r]) + clo[0] + clo[2];
+          const float hi = _mm512_reduce_add_ps(ahi[gg][r]) + chi[0] + chi[2];
+          y[r][tile * 16 + g] = lo * scale[r];
+          y[r][tile * 16 + g + 8] = hi * scale[r];
+        }
     }
   }
 }
@@ -189,28 +333,62 @@ void tiles_scalar(const uint32_t* qw, const uint16_t* sm, int K, int tile0, int 
     }
 }
 
-bool simd_ok() {
+// Kernel family: 0 plain C++, 1 AVX-512 BF16 (bf16 magic-number pairs, exact products; the
+// default), 2 AVX-512 VNNI (int16 activations, vpdpwssd; hosts without AVX-512 BF16).
+bool has_bf16() {
   static const bool ok = __builtin_cpu_supports("avx512f") && __builtin_cpu_supports("avx512bw") &&
                          __builtin_cpu_supports("avx512vl") && __builtin_cpu_supports("avx512bf16");
   return ok;
 }
+bool has_vnni() {
+  static const bool ok = __builtin_cpu_supports("avx512f") && __builtin_cpu_supports("avx512bw") &&
+                         __builtin_cpu_supports("avx512vl") && __builtin_cpu_supports("avx512vnni");
+  return ok;
+}
+bool simd_ok() { return has_bf16() || has_vnni(); }
 
-// Rows of one expert against one weight matrix: SIMD in groups of up to 4 rows.
-void expert_tiles(bool simd, const uint32_t* qw, const uint16_t* sm, int K, int t0, int t1, int nr,
-                  const uint32_t* const* ab, const float* const* sx4, const uint16_t* const* xr, float* const* y,
-                  const float* scale) {
-  if (!simd) {
+int pick_mode(int want) {
+  if (want < 0) {
+    const char* e = getenv("SYN_CPU_GEMV_MODE");
+    want = e ? atoi(e) : 1;
+  }
+  if (want == 1 && !has_bf16()) want = has_vnni() ? 2 : 0;
+  if (want == 2 && !has_vnni()) want = has_bf16() ? 1 : 0;
+  return want;
+}
+
+// Packs one activation row for `mode` (ab: [K/64][32] pairs, sxs: [K/64][16] VNNI scales,
+// sx4: [K/64][4] block sums).
+void pack_for(int mode, const uint16_t* x, int K, uint32_t* ab, float* sxs, float* sx4) {
+  if (mode == 2)
+    pack_row_i16(x, K, ab, sxs, sx4);
+  else if (mode == 1)
+    pack_row(x, K, ab, sx4);
+}
+
+// Rows of one expert against one weight matrix.
+void expert_tiles(int mode, const uint32_t* qw, const uint16_t* sm, int K, int t0, int t1, int nr,
+                  const uint32_t* const* ab, const float* const* sxs, const float* const* sx4,
+                  const uint16_t* const* xr, float* const* y, const float* scale) {
+  if (mode == 0) {
     tiles_scalar(qw, sm, K, t0, t1, xr, nr, y, scale);
     return;
   }
-  for (int r0 = 0; r0 < nr; r0 += 4) {
-    const int n = std::min(4, nr - r0);
-    switch (n) {
-      case 1: tiles_avx512<1>(qw, sm, K, t0, t1, ab + r0, sx4 + r0, y + r0, scale + r0); break;
-      case 2: tiles_avx512<2>(qw, sm, K, t0, t1, ab + r0, sx4 + r0, y + r0, scale + r0); break;
-      case 3: tiles_avx512<3>(qw, sm, K, t0, t1, ab + r0, sx4 + r0, y + r0, scale + r0); break;
-      default: tiles_avx512<4>(qw, sm, K, t0, t1, ab + r0, sx4 + r0, y + r0, scale + r0); break;
+  for (int r0 = 0; r0 < nr;) {
+    const int n = nr - r0;
+    const int take = n >= 2 ? 2 : 1;
+    if (mode == 2) {
+      if (take == 2)
+        tiles_vnni<2, 4>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0);
+      else
+        tiles_vnni<1, 4>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0);
+    } else {
+      if (take == 2)
+        tiles_avx512_v2<2, 4>(qw, sm, K, t0, t1, ab + r0, sx4 + r0, y + r0, scale + r0);
+      else
+        tiles_avx512_v2<1, 4>(qw, sm, K, t0, t1, ab + r0, sx4 + r0, y + r0, scale + r0);
     }
+    r0 += take;
   }
 }
 
@@ -220,19 +398,21 @@ void expert_tiles(bool simd, const uint32_t* qw, const uint16_t* sm, int K, int 
 class CpuExpertTier {
  public:
   CpuExpertTier(int64_t n_layers, int64_t E, int64_t H, int64_t I, int64_t k, int64_t max_rows, int64_t mailbox,
-                std::vector<int64_t> cpus, int64_t n_threads, bool simd)
+                std::vector<int64_t> cpus, int64_t n_threads, int64_t mode)
       : L_(n_layers), E_(E), H_(H), I_(I), k_(k), R_(max_rows), cpus_(std::move(cpus)),
-        nt_((int)std::max<int64_t>(1, n_threads)), simd_(simd && simd_ok()),
+        nt_((int)std::max<int64_t>(1, n_threads)), mode_(pick_mode((int)mode)),
         mb_(reinterpret_cast<uint8_t*>(mailbox)), lay_(cpu_mailbox_layout(E, k, max_rows, H)),
         own_(n_layers * E * 4, 0) {
     TORCH_CHECK(H % 64 == 0 && I % 64 == 0 && (2 * I) % 16 == 0, "cpu experts: H, I multiples of 64");
     const int64_t P = max_rows * k;
     hab_.resize(R_ * (H_ / 64) * 32);
     hsx_.resize(R_ * (H_ / 64) * 4);
+    hss_.resize(R_ * (H_ / 64) * 16);
     ygu_.resize(P * 2 * I_);
     mid_.resize(P * I_);
     mab_.resize(P * (I_ / 64) * 32);
     msx_.resize(P * (I_ / 64) * 4);
+    mss_.resize(P * (I_ / 64) * 16);
     row_used_.resize(R_);
   }
   ~CpuExpertTier() { stop(); }
@@ -252,7 +432,10 @@ class CpuExpertTier {
     if (!th_.empty()) return;
     stop_.store(false);
     seen_ = load_acquire(word(MB_GO));
-    for (int t = 0; t < nt_; ++t) th_.emplace_back([this, t] { loop(t); });
+    // every thread starts from the same job generation, read before any of them runs (a thread
+    // that read it after thread 0 published the first job would skip that job)
+    const uint32_t gen0 = job_gen_.load(std::memory_order_acquire);
+    for (int t = 0; t < nt_; ++t) th_.emplace_back([this, t, gen0] { loop(t, gen0); });
   }
 
   void stop() {
@@ -267,7 +450,10 @@ class CpuExpertTier {
     d["busy_ms"] = busy_ns_.load() / 1e6;
     d["pairs"] = pairs_.load();
     d["threads"] = nt_;
-    d["simd"] = simd_;
+    d["mode"] = mode_;  // 0 plain C++, 1 AVX-512 BF16, 2 AVX-512 VNNI
+    pybind11::list ph;
+    for (int i = 0; i < 4; ++i) ph.append(phase_ns_[i].load() / 1e6 / nt_);
+    d["phase_ms"] = ph;  // per thread, averaged: pack, gate/up, SiLU + pack, down
     return d;
   }
 
@@ -401,18 +587,26 @@ class CpuExpertTier {
     float* out = reinterpret_cast<float*>(mb_ + lay_.out);
     const int KGH = (int)(H_ / 64), KGI = (int)(I_ / 64);
     // 1. pack the activation rows
-    if (simd_)
+    if (mode_)
       run_phase((int)pack_rows_.size(), [&](int i) {
         const int r = pack_rows_[i];
-        pack_row(h + (int64_t)r * H_, (int)H_, &hab_[(int64_t)r * KGH * 32], &hsx_[(int64_t)r * KGH * 4]);
+        pack_for(mode_, h + (int64_t)r * H_, (int)H_, &hab_[(int64_t)r * KGH * 32], &hss_[(int64_t)r * KGH * 16],
+                 &hsx_[(int64_t)r * KGH * 4]);
       });
+    uint64_t tp = now_ns();
+    auto lap = [&](int ph) {
+      const uint64_t t = now_ns();
+      phase_ns_[ph].fetch_add(t - tp, std::memory_order_relaxed);
+      tp = t;
+    };
+    lap(0);
     // 2. gate / up blocks of every owned expert
     run_phase((int)gu_tasks_.size(), [&](int i) {
       const Task& t = gu_tasks_[i];
       const Expert& x = experts_[t.j];
       const int64_t* o = &own_[((int64_t)layer_ * E_ + x.e) * 4];
       std::vector<const uint32_t*> ab(x.n);
-      std::vector<const float*> sx(x.n);
+      std::vector<const float*> sx(x.n), ss(x.n);
       std::vector<const uint16_t*> xr(x.n);
       std::vector<float*> y(x.n);
       std::vector<float> one(x.n, 1.f);
@@ -420,12 +614,14 @@ class CpuExpertTier {
         const int tok = tidx[x.p0 + r];
         ab[r] = &hab_[(int64_t)tok * KGH * 32];
         sx[r] = &hsx_[(int64_t)tok * KGH * 4];
+        ss[r] = &hss_[(int64_t)tok * KGH * 16];
         xr[r] = h + (int64_t)tok * H_;
         y[r] = &ygu_[(int64_t)(x.q0 + r) * 2 * I_];
       }
-      expert_tiles(simd_, reinterpret_cast<const uint32_t*>(o[0]), reinterpret_cast<const uint16_t*>(o[1]), (int)H_,
-                   t.t0, t.t1, x.n, ab.data(), sx.data(), xr.data(), y.data(), one.data());
+      expert_tiles(mode_, reinterpret_cast<const uint32_t*>(o[0]), reinterpret_cast<const uint16_t*>(o[1]), (int)H_,
+                   t.t0, t.t1, x.n, ab.data(), ss.data(), sx.data(), xr.data(), y.data(), one.data());
     });
+    lap(1);
     // 3. SiLU gate (rows interleaved in 8-row gate / up chunks), bf16 rounding, packing
     run_phase(n_out_, [&](int q) {
       const float* g = &ygu_[(int64_t)q * 2 * I_];
@@ -435,15 +631,18 @@ class CpuExpertTier {
           const float gv = g[16 * c + i], uv = g[16 * c + 8 + i];
           m[8 * c + i] = f2bf_h(gv / (1.f + std::exp(-gv)) * uv);
         }
-      if (simd_) pack_row(m, (int)I_, &mab_[(int64_t)q * KGI * 32], &msx_[(int64_t)q * KGI * 4]);
+      if (mode_)
+        pack_for(mode_, m, (int)I_, &mab_[(int64_t)q * KGI * 32], &mss_[(int64_t)q * KGI * 16],
+                 &msx_[(int64_t)q * KGI * 4]);
     });
+    lap(2);
     // 4. down blocks, scaled by the routing weight, straight into the mailbox
     run_phase((int)dn_tasks_.size(), [&](int i) {
       const Task& t = dn_tasks_[i];
       const Expert& x = experts_[t.j];
       const int64_t* o = &own_[((int64_t)layer_ * E_ + x.e) * 4];
       std::vector<const uint32_t*> ab(x.n);
-      std::vector<const float*> sx(x.n);
+      std::vector<const float*> sx(x.n), ss(x.n);
       std::vector<const uint16_t*> xr(x.n);
       std::vector<float*> y(x.n);
       std::vector<float> sc(x.n);
@@ -451,18 +650,20 @@ class CpuExpertTier {
         const int q = x.q0 + r;
         ab[r] = &mab_[(int64_t)q * KGI * 32];
         sx[r] = &msx_[(int64_t)q * KGI * 4];
+        ss[r] = &mss_[(int64_t)q * KGI * 16];
         xr[r] = &mid_[(int64_t)q * I_];
         y[r] = out + (int64_t)q * H_;
         sc[r] = pw[x.p0 + r];
       }
-      expert_tiles(simd_, reinterpret_cast<const uint32_t*>(o[2]), reinterpret_cast<const uint16_t*>(o[3]), (int)I_,
-                   t.t0, t.t1, x.n, ab.data(), sx.data(), xr.data(), y.data(), sc.data());
+      expert_tiles(mode_, reinterpret_cast<const uint32_t*>(o[2]), reinterpret_cast<const uint16_t*>(o[3]), (int)I_,
+                   t.t0, t.t1, x.n, ab.data(), ss.data(), sx.data(), xr.data(), y.data(), sc.data());
     });
+    lap(3);
   }
 
-  void loop(int t) {
+  void loop(int t, uint32_t gen0) {
     pin(t);
-    uint32_t my_gen = job_gen_.load(std::memory_order_acquire);
+    uint32_t my_gen = gen0;
     while (true) {
       if (t == 0) {
         uint32_t go = 0;
@@ -491,12 +692,12 @@ class CpuExpertTier {
   const int64_t L_, E_, H_, I_, k_, R_;
   std::vector<int64_t> cpus_;
   const int nt_;
-  const bool simd_;
+  const int mode_;
   uint8_t* mb_;
   CpuMailboxLayout lay_;
   std::vector<int64_t> own_;
   std::vector<uint32_t> hab_, mab_;
-  std::vector<float> hsx_, msx_, ygu_;
+  std::vector<float> hsx_, msx_, hss_, mss_, ygu_;
   std::vector<uint16_t> mid_;
   std::vector<char> row_used_;
   std::vector<int> pack_rows_;
@@ -512,10 +713,12 @@ class CpuExpertTier {
   std::atomic<int> bar_count_{0}, bar_reset_{0}, next_{0};
   std::atomic<int64_t> jobs_{0}, pairs_{0};
   std::atomic<uint64_t> busy_ns_{0};
+  std::atomic<uint64_t> phase_ns_[4] = {};  // summed over threads: pack, gate/up, SiLU, down
 };
 
-// y [R, N] f32 = x [R, K] (bf16) @ W^T for a tiled 4-bit matrix held in host memory.
-torch::Tensor cpu_q4t_gemv(torch::Tensor qw, torch::Tensor sm, torch::Tensor x, int64_t N, bool simd) {
+// y [R, N] f32 = x [R, K] (bf16) @ W^T for a tiled 4-bit matrix held in host memory, with
+// kernel family `mode` (0 plain C++, 1 AVX-512 BF16, 2 AVX-512 VNNI, -1 the default).
+torch::Tensor cpu_q4t_gemv(torch::Tensor qw, torch::Tensor sm, torch::Tensor x, int64_t N, int64_t mode) {
   TORCH_CHECK(!qw.is_cuda() && !sm.is_cuda() && !x.is_cuda(), "cpu_q4t_gemv: host tensors");
   TORCH_CHECK(qw.is_contiguous() && sm.is_contiguous() && x.is_contiguous(), "contiguous inputs");
   TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && x.dim() == 2, "x bf16 [R, K]");
@@ -523,39 +726,77 @@ torch::Tensor cpu_q4t_gemv(torch::Tensor qw, torch::Tensor sm, torch::Tensor x, 
   TORCH_CHECK(N % 16 == 0 && K % 64 == 0, "N % 16, K % 64");
   TORCH_CHECK(qw.numel() * qw.element_size() >= N * K / 2 && sm.numel() * sm.element_size() >= N * K / 32 * 4,
               "weight sizes");
+  const int md = mode == 0 ? 0 : pick_mode((int)mode);
   auto y = torch::zeros({R, N}, torch::kFloat32);
-  const bool use_simd = simd && simd_ok();
   const uint16_t* xp = reinterpret_cast<const uint16_t*>(x.data_ptr());
-  std::vector<uint32_t> ab(R * (K / 64) * 32);
-  std::vector<float> sx(R * (K / 64) * 4);
+  const int64_t KG = K / 64;
+  std::vector<uint32_t> ab(R * KG * 32);
+  std::vector<float> sx(R * KG * 4), ss(R * KG * 16);
   std::vector<const uint32_t*> abp(R);
-  std::vector<const float*> sxp(R);
+  std::vector<const float*> sxp(R), ssp(R);
   std::vector<const uint16_t*> xr(R);
   std::vector<float*> yp(R);
   std::vector<float> one(R, 1.f);
   for (int64_t r = 0; r < R; ++r) {
-    if (use_simd) pack_row(xp + r * K, (int)K, &ab[r * (K / 64) * 32], &sx[r * (K / 64) * 4]);
-    abp[r] = &ab[r * (K / 64) * 32];
-    sxp[r] = &sx[r * (K / 64) * 4];
+    pack_for(md, xp + r * K, (int)K, &ab[r * KG * 32], &ss[r * KG * 16], &sx[r * KG * 4]);
+    abp[r] = &ab[r * KG * 32];
+    sxp[r] = &sx[r * KG * 4];
+    ssp[r] = &ss[r * KG * 16];
     xr[r] = xp + r * K;
     yp[r] = y.data_ptr<float>() + r * N;
   }
-  expert_tiles(use_simd, reinterpret_cast<const uint32_t*>(qw.data_ptr()),
-               reinterpret_cast<const uint16_t*>(sm.data_ptr()), (int)K, 0, (int)(N / 16), (int)R, abp.data(),
-               sxp.data(), xr.data(), yp.data(), one.data());
+  expert_tiles(md, reinterpret_cast<const uint32_t*>(qw.data_ptr()), reinterpret_cast<const uint16_t*>(sm.data_ptr()),
+               (int)K, 0, (int)(N / 16), (int)R, abp.data(), ssp.data(), sxp.data(), xr.data(), yp.data(), one.data());
   return y;
 }
 
+namespace {
+__attribute__((target("avx512f"))) double read_chunk(const uint8_t* p, int64_t n) {
+  __m512 acc = _mm512_setzero_ps();
+  for (int64_t i = 0; i + 256 <= n; i += 256) {
+    const __m512 a = _mm512_loadu_ps(reinterpret_cast<const float*>(p + i));
+    const __m512 b = _mm512_loadu_ps(reinterpret_cast<const float*>(p + i + 64));
+    const __m512 c = _mm512_loadu_ps(reinterpret_cast<const float*>(p + i + 128));
+    const __m512 d = _mm512_loadu_ps(reinterpret_cast<const float*>(p + i + 192));
+    acc = _mm512_add_ps(acc, _mm512_add_ps(_mm512_add_ps(a, b), _mm512_add_ps(c, d)));
+  }
+  return _mm512_reduce_add_ps(acc);
+}
+}  // namespace
+
+// Host read bandwidth (GB/s) of `threads` threads streaming disjoint parts of one buffer
+// (a probe for sizing the CPU share of the cold experts).
+double cpu_read_gbs(int64_t nbytes, int64_t threads, int64_t reps) {
+  TORCH_CHECK(simd_ok(), "cpu_read_gbs: needs AVX-512");
+  std::vector<uint8_t> buf(nbytes, 1);
+  const int64_t per = (nbytes / threads) & ~int64_t(255);
+  std::vector<double> sink(threads);
+  double best = 0.0;
+  for (int64_t r = 0; r < reps; ++r) {
+    const uint64_t t0 = now_ns();
+    std::vector<std::thread> th;
+    for (int64_t t = 0; t < threads; ++t)
+      th.emplace_back([&, t] { sink[t] = read_chunk(buf.data() + t * per, per); });
+    for (auto& x : th) x.join();
+    const double s = (now_ns() - t0) * 1e-9;
+    best = std::max(best, (double)(per * threads) / s / 1e9);
+  }
+  return best;
+}
+
 void register_cpu_experts(pybind11::module& m) {
-  m.def("cpu_q4t_gemv", &cpu_q4t_gemv, "host GEMV over the tiled 4-bit layout (AVX-512 BF16 or plain C++)");
+  m.def("cpu_read_gbs", &cpu_read_gbs, pybind11::call_guard<pybind11::gil_scoped_release>());
+  m.def("cpu_q4t_gemv", &cpu_q4t_gemv, "host GEMV over the tiled 4-bit layout (AVX-512 BF16 or plain C++)",
+        pybind11::call_guard<pybind11::gil_scoped_release>());
   m.def("cpu_simd_available", [] { return simd_ok(); });
+  m.def("cpu_gemv_mode", [] { return pick_mode(-1); }, "default kernel family: 0 C++, 1 AVX-512 BF16, 2 VNNI");
   m.def("cpu_mailbox_bytes", [](int64_t E, int64_t k, int64_t R, int64_t H) {
     const CpuMailboxLayout l = cpu_mailbox_layout(E, k, R, H);
     return std::vector<int64_t>{l.tok_off, l.tok_idx, l.pair_w, l.h, l.out_pairs, l.out, l.bytes};
   });
   pybind11::class_<CpuExpertTier>(m, "CpuExpertTier")
       .def(pybind11::init<int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t, std::vector<int64_t>, int64_t,
-                          bool>())
+                          int64_t>())
       .def("set_expert", &CpuExpertTier::set_expert)
       .def("start", &CpuExpertTier::start)
       .def("stop", &CpuExpertTier::stop, pybind11::call_guard<pybind11::gil_scoped_release>())

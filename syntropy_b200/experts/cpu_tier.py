@@ -53,7 +53,7 @@ class CpuExpertTier:
             threads = int(os.environ.get("SYN_CPU_EXPERT_THREADS", max(1, len(cpus))))
         self.threads = threads
         self.native = ext().CpuExpertTier(len(cache.layers), self.E, self.H, self.I, self.k, max_rows,
-                                          self.mb_ptr, list(cpus), threads, True)
+                                          self.mb_ptr, list(cpus), threads, -1)
         self.layer_of = {id(L): li for li, L in enumerate(cache.layers)}
         cache.cpu_tier = self
         self.assign()

@@ -19,17 +19,18 @@ def _q4(w):
     return qw, sm, ext().q4_dequant_rows_cpu(rows, N, K).float()
 
 
-@pytest.mark.parametrize("simd", [False, True])
-def test_cpu_q4t_gemv(simd):
-    if simd and not ext().cpu_simd_available():
-        pytest.skip("no AVX-512 BF16 on this CPU")
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_cpu_q4t_gemv(mode):
+    """mode 0: plain C++, 1: AVX-512 BF16, 2: AVX-512 VNNI (falls back where the ISA is missing)."""
+    if mode and not ext().cpu_simd_available():
+        pytest.skip("no AVX-512 on this CPU")
     torch.manual_seed(0)
     N, K = 256, 512
     qw, sm, wd = _q4(torch.randn(N, K) * 0.05)
     for R in (1, 3, 6):
         x = torch.randn(R, K).bfloat16()
         ref = x.float() @ wd.t()
-        y = ext().cpu_q4t_gemv(qw, sm, x, N, simd)
+        y = ext().cpu_q4t_gemv(qw, sm, x, N, mode)
         assert torch.allclose(y, ref, rtol=1e-4, atol=2e-4 * ref.abs().max().item())
 
 
@@ -46,7 +47,7 @@ def test_worker_pool_through_mailbox():
     mb = torch.zeros(nbytes, dtype=torch.uint8)
     w32 = mb.view(torch.int32)
     owned = [1, 4, 6]
-    tier = ext().CpuExpertTier(n_layers, E, H, I, k, R, mb.data_ptr(), [], 3, True)
+    tier = ext().CpuExpertTier(n_layers, E, H, I, k, R, mb.data_ptr(), [], 3, -1)
     for e in owned:
         (qg, sg, _), (qd, sd, _) = experts[e]
         tier.set_expert(layer, e, qg.data_ptr(), sg.data_ptr(), qd.data_ptr(), sd.data_ptr())
