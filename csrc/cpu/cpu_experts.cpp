@@ -218,90 +218,68 @@ __attribute__((target("avx512f,avx512bw,avx512vl,avx512vnni,f16c,fma"))) void ti
   }
 }
 
-// Same product with the per-k-group scale work hoisted out of the row loop: the 16 rows' (d, m)
-// pairs of a k-group are converted once (4 vcvtph2ps), each row pair's scale vectors are one
-// permute away, and the min term sum (m - 128 d) * sum(x) is accumulated for all 16 rows at
-// once into a small per-row array.  k-groups outer, GB row pairs (g) per pass.
-template <int NR, int GB>
-__attribute__((target("avx512f,avx512bw,avx512vl,avx512bf16,f16c,fma"))) void tiles_avx512_v2(
+// BF16 family: y[r][n] = scale[r] * sum_k W[n][k] x_r[k] for the rows of tiles [tile0, tile1),
+// NR rows; row pairs (g) outer, k-groups inner (the fastest order measured on a B200 node's host).
+template <int NR>
+__attribute__((target("avx512f,avx512bw,avx512vl,avx512bf16,f16c,fma"))) void tiles_avx512(
     const uint32_t* qw, const uint16_t* sm, int K, int tile0, int tile1, const uint32_t* const* ab,
     const float* const* sx4, float* const* y, const float* scale) {
   const int KG = K >> 6;
   const __m512i M = _mm512_set1_epi32(0x000F000F), C = _mm512_set1_epi32(0x43004300);
-  // converted scale vector q holds rows 4q..4q+3 as (d0, m0, d1, m1); row 4q+j's d pattern for
-  // dword i is element 4j + ((i & 3) >> 1) * 2
-  __m512i idx[4];
-  for (int j = 0; j < 4; ++j)
-    idx[j] = _mm512_add_epi32(_mm512_set1_epi32(4 * j), _mm512_set_epi32(2, 2, 0, 0, 2, 2, 0, 0, 2, 2, 0, 0, 2, 2, 0, 0));
-  const __m512 c128 = _mm512_set1_ps(128.f);
-  const __m512i swap = _mm512_set_epi32(14, 15, 12, 13, 10, 11, 8, 9, 6, 7, 4, 5, 2, 3, 0, 1);
+  // dword i of a 64-byte row slice belongs to 32-column block ((i & 3) >> 1); the converted
+  // scale quad is (d0, m0, d1, m1)
+  const __m512i idx = _mm512_set_epi32(2, 2, 0, 0, 2, 2, 0, 0, 2, 2, 0, 0, 2, 2, 0, 0);
+  const __m128 c128 = _mm_set1_ps(128.f);
   for (int tile = tile0; tile < tile1; ++tile) {
     const uint32_t* wt = qw + (int64_t)tile * KG * 128;
     const uint16_t* st = sm + (int64_t)tile * KG * 64;
-    alignas(64) float cmin[NR][64];  // per row r of the tile: lanes 4*(r%4) + {0, 2} of vector r/4
-    for (int r = 0; r < NR; ++r)
-      for (int i = 0; i < 64; ++i) cmin[r][i] = 0.f;
-    // min term for the whole tile
-    for (int kg = 0; kg < KG; ++kg) {
-      const uint16_t* s = st + kg * 64;
-      for (int q = 0; q < 4; ++q) {
-        const __m512 F = _mm512_cvtph_ps(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(s + 16 * q)));
-        const __m512 G = _mm512_fnmadd_ps(c128, F, _mm512_permutexvar_ps(swap, F));  // m - 128 d at even lanes
-        for (int r = 0; r < NR; ++r) {
-          const __m512 S = _mm512_broadcast_f32x4(_mm_loadu_ps(sx4[r] + kg * 4));
-          _mm512_store_ps(&cmin[r][16 * q], _mm512_fmadd_ps(G, S, _mm512_load_ps(&cmin[r][16 * q])));
-        }
+    for (int g = 0; g < 8; ++g) {
+      __m512 alo[NR], ahi[NR];
+      __m128 clo[NR], chi[NR];
+      for (int r = 0; r < NR; ++r) {
+        alo[r] = _mm512_setzero_ps();
+        ahi[r] = _mm512_setzero_ps();
+        clo[r] = _mm_setzero_ps();
+        chi[r] = _mm_setzero_ps();
       }
-    }
-    for (int g0 = 0; g0 < 8; g0 += GB) {
-      __m512 alo[GB][NR], ahi[GB][NR];
-      for (int gg = 0; gg < GB; ++gg)
-        for (int r = 0; r < NR; ++r) {
-          alo[gg][r] = _mm512_setzero_ps();
-          ahi[gg][r] = _mm512_setzero_ps();
-        }
+      const uint32_t* wp = wt + 16 * g;
       for (int kg = 0; kg < KG; ++kg) {
-        const uint32_t* wp = wt + kg * 128 + 16 * g0;
-        for (int l = 0; l < GB; ++l) _mm_prefetch(reinterpret_cast<const char*>(wp + 4 * 128 + 16 * l), _MM_HINT_T0);
-        __m512i xa[NR], xb[NR];
-        for (int r = 0; r < NR; ++r) {
-          xa[r] = _mm512_loadu_si512(ab[r] + kg * 32);
-          xb[r] = _mm512_loadu_si512(ab[r] + kg * 32 + 16);
-        }
+        _mm_prefetch(reinterpret_cast<const char*>(wp + (kg + 6) * 128), _MM_HINT_T0);
+        const __m512i W = _mm512_loadu_si512(wp + kg * 128);
+        const __m512i v0 = _mm512_ternarylogic_epi32(W, M, C, 0xEA);  // (W & M) | C
+        const __m512i v1 = _mm512_ternarylogic_epi32(_mm512_srli_epi32(W, 4), M, C, 0xEA);
+        const __m512i v2 = _mm512_ternarylogic_epi32(_mm512_srli_epi32(W, 8), M, C, 0xEA);
+        const __m512i v3 = _mm512_ternarylogic_epi32(_mm512_srli_epi32(W, 12), M, C, 0xEA);
         const uint16_t* s = st + kg * 64;
-#pragma unroll
-        for (int gg = 0; gg < GB; ++gg) {
-          const int g = g0 + gg;
-          const __m512 Flo = _mm512_cvtph_ps(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(s + 16 * (g >> 2))));
-          const __m512 Fhi =
-              _mm512_cvtph_ps(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(s + 16 * ((g + 8) >> 2))));
-          const __m512 Dlo = _mm512_permutexvar_ps(idx[g & 3], Flo);
-          const __m512 Dhi = _mm512_permutexvar_ps(idx[g & 3], Fhi);
-          const __m512i W = _mm512_loadu_si512(wp + 16 * gg);
-          const __m512i v0 = _mm512_ternarylogic_epi32(W, M, C, 0xEA);
-          const __m512i v1 = _mm512_ternarylogic_epi32(_mm512_srli_epi32(W, 4), M, C, 0xEA);
-          const __m512i v2 = _mm512_ternarylogic_epi32(_mm512_srli_epi32(W, 8), M, C, 0xEA);
-          const __m512i v3 = _mm512_ternarylogic_epi32(_mm512_srli_epi32(W, 12), M, C, 0xEA);
-          for (int r = 0; r < NR; ++r) {
-            __m512 t = _mm512_dpbf16_ps(_mm512_setzero_ps(), (__m512bh)v0, (__m512bh)xa[r]);
-            t = _mm512_dpbf16_ps(t, (__m512bh)v2, (__m512bh)xb[r]);
-            alo[gg][r] = _mm512_fmadd_ps(t, Dlo, alo[gg][r]);
-            __m512 u = _mm512_dpbf16_ps(_mm512_setzero_ps(), (__m512bh)v1, (__m512bh)xa[r]);
-            u = _mm512_dpbf16_ps(u, (__m512bh)v3, (__m512bh)xb[r]);
-            ahi[gg][r] = _mm512_fmadd_ps(u, Dhi, ahi[gg][r]);
-          }
+        const __m128 flo = _mm_cvtph_ps(_mm_loadl_epi64(reinterpret_cast<const __m128i*>(s + g * 4)));
+        const __m128 fhi = _mm_cvtph_ps(_mm_loadl_epi64(reinterpret_cast<const __m128i*>(s + (g + 8) * 4)));
+        const __m512 Dlo = _mm512_permutexvar_ps(idx, _mm512_castps128_ps512(flo));
+        const __m512 Dhi = _mm512_permutexvar_ps(idx, _mm512_castps128_ps512(fhi));
+        // (m - 128 d) in lanes 0 and 2
+        const __m128 glo = _mm_fnmadd_ps(c128, flo, _mm_permute_ps(flo, 0xB1));
+        const __m128 ghi = _mm_fnmadd_ps(c128, fhi, _mm_permute_ps(fhi, 0xB1));
+        for (int r = 0; r < NR; ++r) {
+          const uint32_t* xp = ab[r] + kg * 32;
+          const __m512i xa = _mm512_loadu_si512(xp), xb = _mm512_loadu_si512(xp + 16);
+          __m512 t = _mm512_dpbf16_ps(_mm512_setzero_ps(), (__m512bh)v0, (__m512bh)xa);
+          t = _mm512_dpbf16_ps(t, (__m512bh)v2, (__m512bh)xb);
+          alo[r] = _mm512_fmadd_ps(t, Dlo, alo[r]);
+          __m512 u = _mm512_dpbf16_ps(_mm512_setzero_ps(), (__m512bh)v1, (__m512bh)xa);
+          u = _mm512_dpbf16_ps(u, (__m512bh)v3, (__m512bh)xb);
+          ahi[r] = _mm512_fmadd_ps(u, Dhi, ahi[r]);
+          const __m128 sx = _mm_loadu_ps(sx4[r] + kg * 4);
+          clo[r] = _mm_fmadd_ps(glo, sx, clo[r]);
+          chi[r] = _mm_fmadd_ps(ghi, sx, chi[r]);
         }
       }
-      for (int gg = 0; gg < GB; ++gg)
-        for (int r = 0; r < NR; ++r) {
-          const int g = g0 + gg;
-          const float* clo = &cmin[r][16 * (g >> 2) + 4 * (g & 3)];
-          const float* chi = &cmin[r][16 * ((g + 8) >> 2) + 4 * (g & 3)];
-          const float lo = _mm512_reduce_add_ps(alo[gg][r]) + clo[0] + clo[2];
-          const float hi = _mm512_reduce_add_ps(ahi[gg][r]) + chi[0] + chi[2];
-          y[r][tile * 16 + g] = lo * scale[r];
-          y[r][tile * 16 + g + 8] = hi * scale[r];
-        }
+      for (int r = 0; r < NR; ++r) {
+        const float lo = _mm512_reduce_add_ps(alo[r]) + _mm_cvtss_f32(clo[r]) +
+                         _mm_cvtss_f32(_mm_movehl_ps(clo[r], clo[r]));
+        const float hi = _mm512_reduce_add_ps(ahi[r]) + _mm_cvtss_f32(chi[r]) +
+                         _mm_cvtss_f32(_mm_movehl_ps(chi[r], chi[r]));
+        y[r][tile * 16 + g] = lo * scale[r];
+        y[r][tile * 16 + g + 8] = hi * scale[r];
+      }
     }
   }
 }
@@ -376,19 +354,23 @@ void expert_tiles(int mode, const uint32_t* qw, const uint16_t* sm, int K, int t
   }
   for (int r0 = 0; r0 < nr;) {
     const int n = nr - r0;
-    const int take = n >= 2 ? 2 : 1;
     if (mode == 2) {
+      const int take = n >= 2 ? 2 : 1;
       if (take == 2)
         tiles_vnni<2, 4>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0);
       else
         tiles_vnni<1, 4>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0);
+      r0 += take;
     } else {
-      if (take == 2)
-        tiles_avx512_v2<2, 4>(qw, sm, K, t0, t1, ab + r0, sx4 + r0, y + r0, scale + r0);
-      else
-        tiles_avx512_v2<1, 4>(qw, sm, K, t0, t1, ab + r0, sx4 + r0, y + r0, scale + r0);
+      const int nb = std::min(4, n);
+      switch (nb) {
+        case 1: tiles_avx512<1>(qw, sm, K, t0, t1, ab + r0, sx4 + r0, y + r0, scale + r0); break;
+        case 2: tiles_avx512<2>(qw, sm, K, t0, t1, ab + r0, sx4 + r0, y + r0, scale + r0); break;
+        case 3: tiles_avx512<3>(qw, sm, K, t0, t1, ab + r0, sx4 + r0, y + r0, scale + r0); break;
+        default: tiles_avx512<4>(qw, sm, K, t0, t1, ab + r0, sx4 + r0, y + r0, scale + r0); break;
+      }
+      r0 += nb;
     }
-    r0 += take;
   }
 }
 
