@@ -106,5 +106,15 @@ class CpuExpertTier:
     def stats(self) -> dict:
         return dict(self.native.stats())
 
+    def detach(self):
+        """Hand every expert back to the GPU and stop the threads.  Decode graphs captured with
+        the hand-off must be captured again (the caller clears them)."""
+        for b in self.cache.banks:
+            b.cpu_owned = set()
+            b.rewrite_ptrs()
+        if self.cache.cpu_tier is self:
+            self.cache.cpu_tier = None
+        self.native.stop()
+
     def close(self):
         self.native.stop()
