@@ -41,7 +41,7 @@ class CpuExpertTier:
         self.timeout_s = timeout_s
         self.device = cache.device
         lay = ext().cpu_mailbox_bytes(self.E, self.k, max_rows, self.H)
-        self.mailbox = torch.zeros(lay[-1], dtype=torch.uint8, pin_memory=True)
+        self.mailbox = torch.zeros(lay[-1], dtype=torch.uint8, pin_memory=torch.cuda.is_available())
         self.mb_ptr = self.mailbox.data_ptr()
         self.ctr = torch.zeros(2, dtype=torch.int32, device=self.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)

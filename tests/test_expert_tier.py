@@ -38,3 +38,31 @@ def test_rebalance_swaps_and_keeps_weights():
         assert int(dn.sm_ptrs[e]) == b.weight_of(1, e)[1].data_ptr()
     # a second pass with the same scores finds nothing worth moving
     assert cache.rebalance(st, max_swaps_per_layer=4) == 0
+
+
+def test_cpu_tier_split_and_detach():
+    """The CPU tier takes its share of each layer's host experts (null GPU pointers for them),
+    follows residency changes, and hands everything back on detach."""
+    from syntropy_b200.experts.cpu_tier import CpuExpertTier
+    g = torch.Generator().manual_seed(1)
+    E = 8
+    gu, dn = _bank(E, g), _bank(E, g)
+    layer = SimpleNamespace(is_moe=True, experts_gu=gu, experts_down=dn)
+    cache = ExpertCache([layer], 0.5, torch.device("cpu"))
+    cfg = SimpleNamespace(n_experts=E, top_k=2, hidden=256, moe_ffn=128)
+    tier = CpuExpertTier(cache, cfg, max_rows=4, cpu_share=0.5, threads=2, cpus=[])
+    try:
+        b = cache.banks[0]
+        assert cache.cpu_tier is tier and b.cpu_owned == {4, 5}  # half of host experts 4..7
+        ptrs = gu.qw_ptrs.tolist()
+        assert [p == 0 for p in ptrs] == [False] * 4 + [True, True, False, False]
+        st = ExpertStats(1, E)
+        st.observe(0, torch.tensor([0, 9, 9, 9, 9, 0, 0, 0]))
+        assert cache.rebalance(st, max_swaps_per_layer=1) == 1  # expert 4 comes in for expert 0
+        assert b.slot_of[4] >= 0 and b.cpu_owned == {0, 5}
+        assert int(gu.qw_ptrs[4]) != 0 and int(gu.qw_ptrs[0]) == 0
+        tier.detach()
+        assert cache.cpu_tier is None and not b.cpu_owned
+        assert all(int(p) != 0 for p in gu.qw_ptrs) and all(int(p) != 0 for p in dn.sm_ptrs)
+    finally:
+        tier.close()
