@@ -59,6 +59,7 @@ void register_all(pybind11::module& m) {
   register_dispatcher(m);
   register_tier(m);
   register_cpu_experts(m);
+  register_constrain(m);
 }
 
 }  // namespace syn

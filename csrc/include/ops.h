@@ -108,5 +108,6 @@ void cpu_collect(int64_t mailbox, int64_t E, int64_t k, int64_t max_rows, torch:
 void register_dispatcher(pybind11::module& m);
 void register_tier(pybind11::module& m);
 void register_cpu_experts(pybind11::module& m);
+void register_constrain(pybind11::module& m);
 void register_formats(pybind11::module& m);
 }  // namespace syn

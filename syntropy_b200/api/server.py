@@ -30,7 +30,18 @@ def _params(body: dict, default_max: int = 16) -> SamplingParams:
                           temperature=float(body.get("temperature", 1.0 if "temperature" not in body else
                                                      body["temperature"])),
                           top_k=int(body.get("top_k", 0)), top_p=float(body.get("top_p", 1.0)),
-                          seed=body.get("seed"), stop_token_ids=tuple(stop))
+                          seed=body.get("seed"), stop_token_ids=tuple(stop), constraint=_constraint(body))
+
+
+def _constraint(body: dict):
+    """OpenAI `response_format` json_object / json_schema (any JSON object; the schema itself
+    is not enforced) and the `guided_choice` list extension -> a decoding constraint."""
+    rf = body.get("response_format") or {}
+    if isinstance(rf, dict) and rf.get("type") in ("json_object", "json_schema"):
+        return {"type": "json"}
+    if body.get("guided_choice"):
+        return {"choices": [str(c) for c in body["guided_choice"]]}
+    return body.get("constraint")
 
 
 def build_app(aeng, tokenizer, model_id: str = "syntropy", bench_api: bool = True):
@@ -39,6 +50,7 @@ def build_app(aeng, tokenizer, model_id: str = "syntropy", bench_api: bool = Tru
 
     app = FastAPI(title="syntropy_b200")
     vocab = aeng.engine.cfg.vocab
+    aeng.engine.set_tokenizer(tokenizer)  # vocabulary bytes for constrained requests
 
     async def _body(req: Request):
         raw = await req.body()
@@ -86,7 +98,7 @@ def build_app(aeng, tokenizer, model_id: str = "syntropy", bench_api: bool = Tru
         body, err = await _body(req)
         if err:
             return err
-        allowed = {"model", "tokens", "sampling", "stream", "return_tokens", "prompt", "messages"}
+        allowed = {"model", "tokens", "sampling", "stream", "return_tokens", "prompt", "messages", "constraint"}
         unknown = set(body) - allowed
         if unknown:
             return _err(400, "invalid_request", f"unknown fields {sorted(unknown)}")
@@ -103,7 +115,8 @@ def build_app(aeng, tokenizer, model_id: str = "syntropy", bench_api: bool = Tru
             return e
         sp = body.get("sampling") or {}
         params = SamplingParams(max_tokens=int(sp.get("max_tokens", 16)), temperature=float(sp.get("temperature", 0.0)),
-                                top_k=int(sp.get("top_k", 0)), top_p=float(sp.get("top_p", 1.0)), seed=sp.get("seed"))
+                                top_k=int(sp.get("top_k", 0)), top_p=float(sp.get("top_p", 1.0)), seed=sp.get("seed"),
+                                constraint=body.get("constraint"))
         ret_tokens = bool(body.get("return_tokens", False))
         seq = uuid.uuid4().hex[:16]
 

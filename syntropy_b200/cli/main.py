@@ -60,8 +60,11 @@ def cmd_run(args, cfg):
     eng, mcfg = _engine_from_config(cfg, args.device)
     tok = load_tokenizer(cfg.model.path or None, mcfg.vocab)
     ids = [int(x) for x in args.tokens.split(",")] if args.tokens else tok.encode(args.prompt)
+    eng.set_tokenizer(tok)
+    constraint = {"type": "json"} if getattr(args, "json", False) else (
+        {"choices": args.choices.split("|")} if getattr(args, "choices", None) else None)
     out = eng.generate([ids], SamplingParams(max_tokens=args.max_tokens, temperature=args.temperature,
-                                             seed=args.seed))[0]
+                                             seed=args.seed, constraint=constraint))[0]
     print(json.dumps({"tokens": out, "text": tok.decode(out)}))
 
 
@@ -114,6 +117,8 @@ def main(argv=None):
     p.add_argument("--max-tokens", type=int, default=16)
     p.add_argument("--temperature", type=float, default=0.0)
     p.add_argument("--seed", type=int, default=None)
+    p.add_argument("--json", action="store_true", help="constrain the output to one JSON object")
+    p.add_argument("--choices", default=None, help="constrain the output to one of these '|'-separated strings")
     p.add_argument("--device", default="cuda:0")
     p = sub.add_parser("serve")
     p.add_argument("--device", default="cuda:0")

@@ -30,6 +30,7 @@ class SamplingParams:
     seed: int | None = None
     stop_token_ids: tuple = ()
     ignore_eos: bool = True
+    constraint: object = None  # {"type": "json"} or {"choices": [...]} (text/constrain.py)
 
 
 @dataclass
@@ -48,6 +49,7 @@ class Sequence:
     rng_counter: int = 0
     t_arrival: float = 0.0
     t_first_token: float | None = None
+    constraint: object = None  # native automaton state of a constrained request
     t_finished: float | None = None
 
     @property
@@ -86,6 +88,21 @@ class LLMEngine:
         self._boot_seed = random.getrandbits(63)
         self.stats = {"prefill_steps": 0, "decode_steps": 0, "decode_tokens": 0, "prefill_tokens": 0,
                       "spec_drafted": 0, "spec_accepted": 0}
+        self._vocab_bytes = None  # token byte strings for constrained decoding (set_tokenizer)
+        self._trie = None
+
+    def set_tokenizer(self, tokenizer):
+        """Vocabulary of the tokenizer in use, for grammar-constrained requests."""
+        from ..text.constrain import vocab_bytes
+        self._vocab_bytes = vocab_bytes(tokenizer, self.cfg.vocab)
+        self._trie = None
+
+    def _token_trie(self):
+        if self._trie is None:
+            from ..text.constrain import vocab_bytes
+            vb = self._vocab_bytes if self._vocab_bytes is not None else vocab_bytes(None, self.cfg.vocab)
+            self._trie = ext().TokenTrie(vb)
+        return self._trie
 
     # ------------------------------------------------------------------ intake
     def add_request(self, prompt: list[int], params: SamplingParams | None = None, choice_index: int = 0) -> int:
@@ -99,6 +116,9 @@ class LLMEngine:
             raise ValueError("prompt + max_tokens exceeds max_seq_len")
         sid = next(self._ids)
         s = Sequence(sid, list(prompt), params, t_arrival=time.perf_counter())
+        if params.constraint is not None:
+            from ..text.constrain import make_constraint
+            s.constraint = make_constraint(self._token_trie(), self.eos, params.constraint)
         if params.seed is not None:  # client seed: key (seed, choice index)
             s.seed, s.stream = params.seed, choice_index
         else:  # generated seed: key (seed, sequence id)
@@ -265,6 +285,12 @@ class LLMEngine:
     def _sample_rows(self, logits: torch.Tensor, seqs: list[Sequence]) -> list[int]:
         n = len(seqs)
         dev = logits.device
+        if any(s.constraint is not None for s in seqs):  # forbidden tokens of constrained rows at -inf
+            from ..text.constrain import allowed
+            logits = logits.clone()
+            for i, s in enumerate(seqs):
+                if s.constraint is not None:
+                    logits[i].masked_fill_(~allowed(s.constraint.mask(), logits.shape[1]).to(dev), float("-inf"))
         temp = torch.tensor([s.params.temperature for s in seqs], dtype=torch.float32, device=dev)
         topk = torch.tensor([s.params.top_k for s in seqs], dtype=torch.int32, device=dev)
         topp = torch.tensor([s.params.top_p for s in seqs], dtype=torch.float32, device=dev)
@@ -281,7 +307,9 @@ class LLMEngine:
     def _decode(self) -> list[StepOutput]:
         # Under lockstep ranks every rank runs the same verify window shape (equal live
         # sequence counts), so the expert-parallel exchanges inside it line up.
-        outs = self._decode_spec() if self.spec is not None else self._decode_plain()
+        # constrained sequences take plain steps (their rows are re-drawn from masked logits)
+        plain = self.spec is None or any(s.constraint is not None for s in self.running)
+        outs = self._decode_plain() if plain else self._decode_spec()
         r = self.runner
         n = self.stats["decode_steps"]
         if r.expert_cache is not None and self.rebalance_every and n % self.rebalance_every == 0:
@@ -381,9 +409,14 @@ class LLMEngine:
                              [s.blocks for s in seqs], bucket_for(B) if r.use_graphs else B)
         nxt = r.decode(B).cpu().tolist()
         r.after_step()
-        # greedy rows take no draw; sampled rows take exactly one
+        cons = [i for i, s in enumerate(seqs) if s.constraint is not None]
+        if cons:  # constrained rows draw again from their masked logits, with the same counter
+            redo = self._sample_rows(r.buf["logits"][:B][cons], [seqs[i] for i in cons])
+            for i, t in zip(cons, redo):
+                nxt[i] = t
+        # greedy rows take no draw; sampled rows take exactly one (constrained rows took theirs)
         for s in seqs:
-            if s.params.temperature > 0:
+            if s.params.temperature > 0 and s.constraint is None:
                 s.rng_counter += 1
         self.stats["decode_steps"] += 1
         self.stats["decode_tokens"] += B
@@ -394,9 +427,17 @@ class LLMEngine:
     def _append(self, s: Sequence, tok: int) -> StepOutput:
         s.output.append(int(tok))
         reason = None
-        if len(s.output) >= s.params.max_tokens:
+        if s.constraint is not None:  # the masked sampler only picks tokens the grammar allows
+            if self.eos is not None and tok == self.eos:
+                reason = "stop"
+            else:
+                s.constraint.advance(int(tok))
+                if s.constraint.finished():
+                    reason = "stop"
+        if reason is None and len(s.output) >= s.params.max_tokens:
             reason = "length"
-        elif tok in s.params.stop_token_ids or (not s.params.ignore_eos and self.eos is not None and tok == self.eos):
+        elif reason is None and (tok in s.params.stop_token_ids or
+                                 (not s.params.ignore_eos and self.eos is not None and tok == self.eos)):
             reason = "stop"
         if reason:
             s.finish_reason = reason

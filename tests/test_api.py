@@ -83,3 +83,20 @@ def test_metrics_exposed(client):
     client.post("/v1/completions", json={"model": "tiny", "prompt": [1, 2, 3], "max_tokens": 2})
     m = client.get("/metrics").text
     assert "syntropy_requests_total" in m and "syntropy_generated_tokens_total" in m
+
+
+def test_constrained_requests(client):
+    """OpenAI guided_choice and response_format json_object; native constraint field."""
+    r = client.post("/v1/completions", json={"model": "tiny", "prompt": "answer:", "max_tokens": 8,
+                                             "temperature": 0, "guided_choice": ["red", "green"]})
+    assert r.status_code == 200, r.text
+    assert r.json()["choices"][0]["text"] in ("red", "green")
+    r = client.post("/v1/chat/completions", json={"model": "tiny", "max_tokens": 12, "temperature": 0,
+                                                  "response_format": {"type": "json_object"},
+                                                  "messages": [{"role": "user", "content": "json please"}]})
+    assert r.status_code == 200, r.text
+    text = r.json()["choices"][0]["message"]["content"]
+    assert text.lstrip().startswith("{")
+    r = client.post("/v1/syntropy/generate", json={"prompt": "x", "sampling": {"max_tokens": 6},
+                                                   "constraint": {"choices": ["ab", "cd"]}})
+    assert r.status_code == 200, r.text
