@@ -30,7 +30,11 @@ def _params(body: dict, default_max: int = 16) -> SamplingParams:
                           temperature=float(body.get("temperature", 1.0 if "temperature" not in body else
                                                      body["temperature"])),
                           top_k=int(body.get("top_k", 0)), top_p=float(body.get("top_p", 1.0)),
-                          seed=body.get("seed"), stop_token_ids=tuple(stop), constraint=_constraint(body))
+                          seed=body.get("seed"), stop_token_ids=tuple(stop), constraint=_constraint(body),
+                          repetition_penalty=float(body.get("repetition_penalty", 1.0)),
+                          frequency_penalty=float(body.get("frequency_penalty", 0.0)),
+                          presence_penalty=float(body.get("presence_penalty", 0.0)),
+                          logit_bias={int(k): float(v) for k, v in (body.get("logit_bias") or {}).items()} or None)
 
 
 def _constraint(body: dict):

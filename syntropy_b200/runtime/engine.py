@@ -31,6 +31,16 @@ class SamplingParams:
     stop_token_ids: tuple = ()
     ignore_eos: bool = True
     constraint: object = None  # {"type": "json"} or {"choices": [...]} (text/constrain.py)
+    repetition_penalty: float = 1.0  # > 1 discourages every token of the prompt and output
+    frequency_penalty: float = 0.0   # subtracted once per earlier occurrence in the output
+    presence_penalty: float = 0.0    # subtracted once if the token occurred in the output
+    logit_bias: dict | None = None   # {token id: added logit}
+
+    @property
+    def processed(self) -> bool:
+        """Whether logits need processing before the draw (penalties or bias)."""
+        return (self.repetition_penalty != 1.0 or self.frequency_penalty != 0.0 or self.presence_penalty != 0.0
+                or bool(self.logit_bias))
 
 
 @dataclass
@@ -114,6 +124,10 @@ class LLMEngine:
                 raise ValueError(f"token id {t} out of range [0, {self.cfg.vocab})")
         if len(prompt) + params.max_tokens > self.runner.max_seq_len:
             raise ValueError("prompt + max_tokens exceeds max_seq_len")
+        if params.logit_bias and not all(0 <= int(t) < self.cfg.vocab for t in params.logit_bias):
+            raise ValueError(f"logit_bias token ids must be in [0, {self.cfg.vocab})")
+        if params.repetition_penalty <= 0:
+            raise ValueError("repetition_penalty must be > 0")
         sid = next(self._ids)
         s = Sequence(sid, list(prompt), params, t_arrival=time.perf_counter())
         if params.constraint is not None:
@@ -282,13 +296,37 @@ class LLMEngine:
         self._reap()
         return outs
 
+    @staticmethod
+    def _redraw(s: Sequence) -> bool:
+        return s.constraint is not None or s.params.processed
+
+    @staticmethod
+    def _process_logits(row: torch.Tensor, s: Sequence):
+        """In place on one row: penalties over the tokens seen so far, then logit bias
+        (OpenAI / HF semantics; reference LogitsProcess, crates/kernels/src/op/kind.rs)."""
+        p = s.params
+        dev = row.device
+        if p.repetition_penalty != 1.0:
+            seen = torch.tensor(sorted(set(s.prompt) | set(s.output)), dtype=torch.long, device=dev)
+            v = row[seen]
+            row[seen] = torch.where(v > 0, v / p.repetition_penalty, v * p.repetition_penalty)
+        if (p.frequency_penalty or p.presence_penalty) and s.output:
+            ids, cnt = torch.unique(torch.tensor(s.output, dtype=torch.long), return_counts=True)
+            row[ids.to(dev)] -= (p.frequency_penalty * cnt.float() + p.presence_penalty).to(dev)
+        if p.logit_bias:
+            ids = torch.tensor([int(k) for k in p.logit_bias], dtype=torch.long, device=dev)
+            row[ids] += torch.tensor([float(v) for v in p.logit_bias.values()], device=dev)
+
     def _sample_rows(self, logits: torch.Tensor, seqs: list[Sequence]) -> list[int]:
         n = len(seqs)
         dev = logits.device
-        if any(s.constraint is not None for s in seqs):  # forbidden tokens of constrained rows at -inf
+        if any(self._redraw(s) for s in seqs):
+            # penalties / bias, then the grammar: forbidden tokens of constrained rows at -inf
             from ..text.constrain import allowed
             logits = logits.clone()
             for i, s in enumerate(seqs):
+                if s.params.processed:
+                    self._process_logits(logits[i], s)
                 if s.constraint is not None:
                     logits[i].masked_fill_(~allowed(s.constraint.mask(), logits.shape[1]).to(dev), float("-inf"))
         temp = torch.tensor([s.params.temperature for s in seqs], dtype=torch.float32, device=dev)
@@ -308,7 +346,7 @@ class LLMEngine:
         # Under lockstep ranks every rank runs the same verify window shape (equal live
         # sequence counts), so the expert-parallel exchanges inside it line up.
         # constrained sequences take plain steps (their rows are re-drawn from masked logits)
-        plain = self.spec is None or any(s.constraint is not None for s in self.running)
+        plain = self.spec is None or any(self._redraw(s) for s in self.running)
         outs = self._decode_plain() if plain else self._decode_spec()
         r = self.runner
         n = self.stats["decode_steps"]
@@ -409,14 +447,14 @@ class LLMEngine:
                              [s.blocks for s in seqs], bucket_for(B) if r.use_graphs else B)
         nxt = r.decode(B).cpu().tolist()
         r.after_step()
-        cons = [i for i, s in enumerate(seqs) if s.constraint is not None]
-        if cons:  # constrained rows draw again from their masked logits, with the same counter
+        cons = [i for i, s in enumerate(seqs) if self._redraw(s)]
+        if cons:  # constrained / processed rows draw again from their processed logits, same counter
             redo = self._sample_rows(r.buf["logits"][:B][cons], [seqs[i] for i in cons])
             for i, t in zip(cons, redo):
                 nxt[i] = t
-        # greedy rows take no draw; sampled rows take exactly one (constrained rows took theirs)
+        # greedy rows take no draw; sampled rows take exactly one (re-drawn rows took theirs)
         for s in seqs:
-            if s.params.temperature > 0 and s.constraint is None:
+            if s.params.temperature > 0 and not self._redraw(s):
                 s.rng_counter += 1
         self.stats["decode_steps"] += 1
         self.stats["decode_tokens"] += B
