@@ -98,13 +98,32 @@ class TPGroup:
 
 
 def shard_state(cfg, sd: dict, rank: int, size: int) -> dict:
-    """Slices a canonical (llama-family) state dict for TP rank `rank` of `size`."""
+    """Slices a canonical state dict for TP rank `rank` of `size`: attention by whole heads,
+    dense FFNs by columns; in MoE layers every expert (and the shared expert) is split the same
+    way along its FFN width (`TpSplit::experts`, reference crates/core/src/plan/stage.rs:103-109),
+    the router stays whole."""
     hq, hk, d = cfg.n_heads // size, cfg.n_kv_heads // size, cfg.head_dim
     f = cfg.ffn // size
+    fe = cfg.moe_ffn // size if cfg.n_experts else 0
+    fs = fe * cfg.n_shared_experts if cfg.n_experts else 0
     out = {}
     for n, t in sd.items():
         leaf = n.split(".")[-1]
-        if leaf == "q_proj":
+        if ".experts." in n or n.startswith("experts."):
+            if leaf in ("gate", "up"):    # [E, f, h]
+                out[n] = t[:, rank * fe:(rank + 1) * fe]
+            elif leaf == "down":          # [E, h, f]
+                out[n] = t[:, :, rank * fe:(rank + 1) * fe]
+            else:
+                out[n] = t
+        elif ".shared." in n or n.startswith("shared."):
+            if leaf in ("gate", "up"):
+                out[n] = t[rank * fs:(rank + 1) * fs]
+            elif leaf == "down":
+                out[n] = t[:, rank * fs:(rank + 1) * fs]
+            else:
+                out[n] = t
+        elif leaf == "q_proj":
             out[n] = t[rank * hq * d:(rank + 1) * hq * d]
         elif leaf in ("k_proj", "v_proj"):
             out[n] = t[rank * hk * d:(rank + 1) * hk * d]
@@ -125,4 +144,9 @@ def shard_state(cfg, sd: dict, rank: int, size: int) -> dict:
 def local_config(cfg, size: int):
     assert cfg.n_heads % size == 0 and cfg.n_kv_heads % size == 0 and cfg.ffn % size == 0, \
         "heads, KV heads and FFN width must divide by the TP size"
-    return cfg.replace(n_heads=cfg.n_heads // size, n_kv_heads=cfg.n_kv_heads // size, ffn=cfg.ffn // size)
+    assert not cfg.is_mla, "tensor parallelism covers GQA attention (MLA models use expert parallelism)"
+    kw = {}
+    if cfg.n_experts:
+        assert cfg.moe_ffn % (64 * size) == 0, "expert FFN width / TP size must be a multiple of 64"
+        kw["moe_ffn"] = cfg.moe_ffn // size
+    return cfg.replace(n_heads=cfg.n_heads // size, n_kv_heads=cfg.n_kv_heads // size, ffn=cfg.ffn // size, **kw)

@@ -155,6 +155,8 @@ class ModelRunner:
                 b["h_all"] = torch.zeros(B, H, dtype=act, device=dev)
                 b["x_part"] = torch.zeros(B, H, dtype=torch.float32, device=dev)
                 b["moe_red"] = torch.zeros(self.max_batch, H, dtype=torch.float32, device=dev)
+            if self.tp is not None:  # experts split along their FFN width: partial MoE outputs
+                b["tp_moe_part"] = torch.zeros(self.max_batch, H, dtype=torch.float32, device=dev)
             b["rlogits"] = torch.zeros(B, 2 * E, dtype=torch.float32, device=dev)
             b["topk_ids"] = torch.zeros(B, k, dtype=torch.int32, device=dev)
             b["topk_w"] = torch.zeros(B, k, dtype=torch.float32, device=dev)
@@ -355,6 +357,17 @@ class ModelRunner:
         if tier is not None:
             tier.collect(yp)
             ops.core._launched()
+        if self.tp is not None:
+            # every expert holds 1/N of its FFN width here: combine the partial outputs, sum them
+            # over the TP group (NCCL, captured in the decode graphs), then residual + next norm
+            import torch.distributed as dist
+            part = b["tp_moe_part"][:B]
+            part.zero_()
+            ops.moe_combine_rmsnorm(part, yp, mb["pair_of"], shared, None, None, cfg.rms_eps)
+            dist.all_reduce(part, group=self.tp.ctx.group)
+            x.add_(part)
+            ops.rms_norm(x, nw, cfg.rms_eps, out=h)
+            return
         ops.moe_combine_rmsnorm(x, yp, mb["pair_of"], shared, nw, h, cfg.rms_eps)
 
     def after_step(self):
@@ -747,7 +760,19 @@ class ModelRunner:
     def _moe_prefill(self, L, h, x):
         """MoE FFN for a prefill chunk: routing on the device, then the local experts over
         their gathered rows (one weight read per active expert), combined in ascending
-        expert order; under expert parallelism the NCCL all-gather/reduce-scatter path."""
+        expert order; under expert parallelism the NCCL all-gather/reduce-scatter path; under
+        tensor parallelism (experts split along their width) the partial outputs are summed
+        over the group with NCCL."""
+        if self.tp is not None:
+            import torch.distributed as dist
+            part = torch.zeros_like(x)
+            self._moe_prefill_local(L, h, part)
+            dist.all_reduce(part, group=self.tp.ctx.group)
+            x.add_(part)
+            return
+        self._moe_prefill_local(L, h, x)
+
+    def _moe_prefill_local(self, L, h, x):
         cfg = self.cfg
         T = h.shape[0]
         E, k = cfg.n_experts, cfg.top_k
