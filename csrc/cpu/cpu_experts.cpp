@@ -23,7 +23,16 @@
 // releases the pool through four phases separated by barriers: pack the activation rows; gate
 // and up tasks; SiLU-gate + pack; down tasks.  Then it writes the outputs' pair indices and
 // release-stores the done word, which the GPU waits on with a time limit.
+#ifdef SYN_NO_TORCH  // standalone build (the ThreadSanitizer test of the worker pool)
+#include <stdexcept>
+#define SYN_REQUIRE(c, msg) \
+  do {                      \
+    if (!(c)) throw std::runtime_error(msg); \
+  } while (0)
+#else
 #include <torch/extension.h>
+#define SYN_REQUIRE(c, msg) TORCH_CHECK(c, msg)
+#endif
 
 #include <immintrin.h>
 #include <pthread.h>
@@ -385,7 +394,7 @@ class CpuExpertTier {
         nt_((int)std::max<int64_t>(1, n_threads)), mode_(pick_mode((int)mode)),
         mb_(reinterpret_cast<uint8_t*>(mailbox)), lay_(cpu_mailbox_layout(E, k, max_rows, H)),
         own_(n_layers * E * 4, 0) {
-    TORCH_CHECK(H % 64 == 0 && I % 64 == 0 && (2 * I) % 16 == 0, "cpu experts: H, I multiples of 64");
+    SYN_REQUIRE(H % 64 == 0 && I % 64 == 0 && (2 * I) % 16 == 0, "cpu experts: H, I multiples of 64");
     const int64_t P = max_rows * k;
     hab_.resize(R_ * (H_ / 64) * 32);
     hsx_.resize(R_ * (H_ / 64) * 4);
@@ -402,7 +411,7 @@ class CpuExpertTier {
   // Expert e of layer l is computed here when its gate_up / down weight pointers are given
   // (host addresses of its tiled rows); zeros hand it back to the GPU.
   void set_expert(int64_t l, int64_t e, int64_t qgu, int64_t sgu, int64_t qdn, int64_t sdn) {
-    TORCH_CHECK(l >= 0 && l < L_ && e >= 0 && e < E_, "set_expert: layer/expert out of range");
+    SYN_REQUIRE(l >= 0 && l < L_ && e >= 0 && e < E_, "set_expert: layer/expert out of range");
     int64_t* o = &own_[(l * E_ + e) * 4];
     o[0] = qgu;
     o[1] = sgu;
@@ -426,17 +435,20 @@ class CpuExpertTier {
     th_.clear();
   }
 
-  pybind11::dict stats() const {
-    pybind11::dict d;
-    d["jobs"] = jobs_.load();
-    d["busy_ms"] = busy_ns_.load() / 1e6;
-    d["pairs"] = pairs_.load();
-    d["threads"] = nt_;
-    d["mode"] = mode_;  // 0 plain C++, 1 AVX-512 BF16, 2 AVX-512 VNNI
-    pybind11::list ph;
-    for (int i = 0; i < 4; ++i) ph.append(phase_ns_[i].load() / 1e6 / nt_);
-    d["phase_ms"] = ph;  // per thread, averaged: pack, gate/up, SiLU + pack, down
-    return d;
+  struct Stats {
+    int64_t jobs, pairs;
+    double busy_ms, phase_ms[4];  // phases per thread, averaged: pack, gate/up, SiLU + pack, down
+    int threads, mode;             // mode: 0 plain C++, 1 AVX-512 BF16, 2 AVX-512 VNNI
+  };
+  Stats stats() const {
+    Stats st;
+    st.jobs = jobs_.load();
+    st.pairs = pairs_.load();
+    st.busy_ms = busy_ns_.load() / 1e6;
+    for (int i = 0; i < 4; ++i) st.phase_ms[i] = phase_ns_[i].load() / 1e6 / nt_;
+    st.threads = nt_;
+    st.mode = mode_;
+    return st;
   }
 
  private:
@@ -698,6 +710,7 @@ class CpuExpertTier {
   std::atomic<uint64_t> phase_ns_[4] = {};  // summed over threads: pack, gate/up, SiLU, down
 };
 
+#ifndef SYN_NO_TORCH
 // y [R, N] f32 = x [R, K] (bf16) @ W^T for a tiled 4-bit matrix held in host memory, with
 // kernel family `mode` (0 plain C++, 1 AVX-512 BF16, 2 AVX-512 VNNI, -1 the default).
 torch::Tensor cpu_q4t_gemv(torch::Tensor qw, torch::Tensor sm, torch::Tensor x, int64_t N, int64_t mode) {
@@ -732,6 +745,8 @@ torch::Tensor cpu_q4t_gemv(torch::Tensor qw, torch::Tensor sm, torch::Tensor x, 
   return y;
 }
 
+#endif  // SYN_NO_TORCH
+
 namespace {
 __attribute__((target("avx512f"))) double read_chunk(const uint8_t* p, int64_t n) {
   __m512 acc = _mm512_setzero_ps();
@@ -749,7 +764,7 @@ __attribute__((target("avx512f"))) double read_chunk(const uint8_t* p, int64_t n
 // Host read bandwidth (GB/s) of `threads` threads streaming disjoint parts of one buffer
 // (a probe for sizing the CPU share of the cold experts).
 double cpu_read_gbs(int64_t nbytes, int64_t threads, int64_t reps) {
-  TORCH_CHECK(simd_ok(), "cpu_read_gbs: needs AVX-512");
+  SYN_REQUIRE(simd_ok(), "cpu_read_gbs: needs AVX-512");
   std::vector<uint8_t> buf(nbytes, 1);
   const int64_t per = (nbytes / threads) & ~int64_t(255);
   std::vector<double> sink(threads);
@@ -766,6 +781,7 @@ double cpu_read_gbs(int64_t nbytes, int64_t threads, int64_t reps) {
   return best;
 }
 
+#ifndef SYN_NO_TORCH
 void register_cpu_experts(pybind11::module& m) {
   m.def("cpu_read_gbs", &cpu_read_gbs, pybind11::call_guard<pybind11::gil_scoped_release>());
   m.def("cpu_q4t_gemv", &cpu_q4t_gemv, "host GEMV over the tiled 4-bit layout (AVX-512 BF16 or plain C++)",
@@ -782,7 +798,19 @@ void register_cpu_experts(pybind11::module& m) {
       .def("set_expert", &CpuExpertTier::set_expert)
       .def("start", &CpuExpertTier::start)
       .def("stop", &CpuExpertTier::stop, pybind11::call_guard<pybind11::gil_scoped_release>())
-      .def("stats", &CpuExpertTier::stats);
+      .def("stats", [](const CpuExpertTier& t) {
+        const auto st = t.stats();
+        pybind11::dict d;
+        d["jobs"] = st.jobs;
+        d["busy_ms"] = st.busy_ms;
+        d["pairs"] = st.pairs;
+        d["threads"] = st.threads;
+        d["mode"] = st.mode;
+        d["phase_ms"] = std::vector<double>(st.phase_ms, st.phase_ms + 4);
+        return d;
+      });
 }
+
+#endif  // SYN_NO_TORCH
 
 }  // namespace syn
