@@ -93,11 +93,13 @@ class LLMEngine:
         self.eos = eos_token_id
         self.waiting: deque[Sequence] = deque()
         self.running: list[Sequence] = []
+        # preempted sequences whose KV pages wait in host memory: (sequence, packed layers)
+        self.swapped: deque = deque()
         self.finished: dict[int, Sequence] = {}
         self._ids = itertools.count()
         self._boot_seed = random.getrandbits(63)
         self.stats = {"prefill_steps": 0, "decode_steps": 0, "decode_tokens": 0, "prefill_tokens": 0,
-                      "spec_drafted": 0, "spec_accepted": 0}
+                      "spec_drafted": 0, "spec_accepted": 0, "swapped_out": 0, "swapped_in": 0}
         self._vocab_bytes = None  # token byte strings for constrained decoding (set_tokenizer)
         self._trie = None
 
@@ -141,6 +143,11 @@ class LLMEngine:
         return sid
 
     def abort(self, seq_id: int):
+        for item in list(self.swapped):
+            if item[0].seq_id == seq_id:
+                self.swapped.remove(item)
+                self._finish(item[0], "cancelled")
+                return
         for s in list(self.waiting):
             if s.seq_id == seq_id:
                 self.waiting.remove(s)
@@ -161,17 +168,62 @@ class LLMEngine:
         if s is None:
             raise KeyError(f"no running sequence {seq_id}")
         kv = self.runner.kv
-        n_pages = kv.blocks_needed(s.n_tokens - 1) if s.n_tokens > 1 else 0
-        dev = self.runner.device
-        pages = torch.tensor(s.blocks[:n_pages], dtype=torch.int32, device=dev)
-        layers = []
-        for i in range(len(kv.k)):
-            packed = ops.kv_pack(kv.k[i], kv.v[i], pages)
-            layers.append(packed.to("cpu"))
+        layers = self._pack_kv(s)
         cfg = self.cfg
         return {"model": cfg.name, "n_layers": len(kv.k), "kv_shape": tuple(kv.k[0].shape[1:]),
                 "prompt": list(s.prompt), "output": list(s.output), "params": s.params, "seed": s.seed,
                 "stream": s.stream, "rng_counter": s.rng_counter, "kv": layers}
+
+    def _pack_kv(self, s: Sequence) -> list:
+        """The KV pages of s (every token but the last sampled one), packed per layer on the
+        device and copied to host memory."""
+        kv = self.runner.kv
+        n_pages = kv.blocks_needed(s.n_tokens - 1) if s.n_tokens > 1 else 0
+        pages = torch.tensor(s.blocks[:n_pages], dtype=torch.int32, device=self.runner.device)
+        return [ops.kv_pack(kv.k[i], kv.v[i], pages).to("cpu") for i in range(len(kv.k))]
+
+    def _unpack_kv(self, s: Sequence, layers: list):
+        kv = self.runner.kv
+        n_pages = layers[0].shape[0] if layers else 0
+        kv.ensure(s.blocks, s.n_tokens)
+        dev = self.runner.device
+        pages = torch.tensor(s.blocks[:n_pages], dtype=torch.int32, device=dev)
+        for i in range(len(kv.k)):
+            ops.kv_unpack(layers[i].to(dev), kv.k[i], kv.v[i], pages)
+
+    # ------------------------------------------------------------------ preemption (KV tiering)
+    def _pages_short(self) -> int:
+        """KV pages the next decode step needs beyond the free pool."""
+        kv = self.runner.kv
+        w = 1 + (self.spec.gamma if self.spec is not None and hasattr(self.spec, "gamma") else 0)
+        need = sum(max(0, kv.blocks_needed(s.n_tokens + w - 1) - len(s.blocks)) for s in self.running)
+        return need - kv.alloc.num_free
+
+    def _swap_out(self, s: Sequence):
+        """Preempt s: its KV pages go to host memory and back to the pool; it resumes later
+        from exactly where it stopped (no recompute)."""
+        layers = self._pack_kv(s)
+        self.runner.kv.release(s.blocks)
+        s.blocks = []
+        s.status = "swapped"
+        self.running.remove(s)
+        self.swapped.append((s, layers))
+        self.stats["swapped_out"] += 1
+
+    def _swap_in(self) -> bool:
+        """Resume the oldest preempted sequence if its pages fit (before any new admission)."""
+        if not self.swapped or len(self.running) >= self.runner.max_batch:
+            return False
+        s, layers = self.swapped[0]
+        kv = self.runner.kv
+        if kv.alloc.num_free < kv.blocks_needed(s.n_tokens + 1):
+            return False
+        self.swapped.popleft()
+        self._unpack_kv(s, layers)
+        s.status = "running"
+        self.running.append(s)
+        self.stats["swapped_in"] += 1
+        return True
 
     def restore_session(self, state: dict) -> int:
         """Re-admits a saved sequence as running: allocates pages, writes its KV back and
@@ -184,27 +236,29 @@ class LLMEngine:
         s = Sequence(sid, list(state["prompt"]), state["params"], output=list(state["output"]),
                      t_arrival=time.perf_counter())
         s.seed, s.stream, s.rng_counter = state["seed"], state["stream"], state["rng_counter"]
-        n_pages = state["kv"][0].shape[0] if state["kv"] else 0
         if kv.alloc.num_free < kv.blocks_needed(s.n_tokens + 1):
             raise RuntimeError("not enough free KV pages to restore the session")
-        kv.ensure(s.blocks, s.n_tokens)
-        dev = self.runner.device
-        pages = torch.tensor(s.blocks[:n_pages], dtype=torch.int32, device=dev)
-        for i in range(len(kv.k)):
-            ops.kv_unpack(state["kv"][i].to(dev), kv.k[i], kv.v[i], pages)
+        self._unpack_kv(s, state["kv"])
         s.status = "running"
         s.t_first_token = time.perf_counter()
         self.running.append(s)
         return sid
 
     def has_work(self) -> bool:
-        return bool(self.waiting or self.running)
+        return bool(self.waiting or self.running or self.swapped)
 
     # ------------------------------------------------------------------ steps
     def step(self) -> list[StepOutput]:
         if self.dist is not None:
             return self._step_lockstep()
-        batch = self._admit()
+        while self._swap_in():
+            pass
+        if self.running and self._pages_short() > 0:
+            # the KV pool cannot hold the next step: preempt the newest sequences to host memory
+            while len(self.running) > 1 and self._pages_short() > 0:
+                self._swap_out(self.running[-1])
+            return self._decode()
+        batch = self._admit() if not self.swapped else []
         if batch:
             return self._prefill(batch)
         if self.running:
