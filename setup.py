@@ -29,7 +29,9 @@ LIBS = ["rt"]
 # does not resolve falls back to libstdc++.a, and a second, static copy of the C++ runtime
 # in the process breaks iostream locale facets (formatting a number in an error message
 # then crashes).
-LINK_FLAGS = ["-l:libstdc++.so.6"]
+LINK_FLAGS = ["-l:libstdc++.so.6",
+              # export only the module entry point and the C entry points (syn_*)
+              "-Wl,--version-script=" + os.path.join(ROOT, "csrc", "exports.map")]
 NVCC_FLAGS = [
     "-O3",
     "-std=c++17",
