@@ -420,6 +420,8 @@ class LLMEngine:
         for i, s in enumerate(seqs):
             if mtp:
                 dr = (s.mtp_draft or [s.output[-1]])[:g]
+            elif getattr(self.spec.drafter, "stateful", False):
+                dr = self.spec.drafter.propose(s.prompt + s.output, g, key=s.seq_id)
             else:
                 dr = self.spec.drafter.propose(s.prompt + s.output, g)
             drafts.append(dr)
@@ -544,6 +546,8 @@ class LLMEngine:
             # KV holds every token but the last sampled one
             self.prefix.insert((s.prompt + s.output)[: s.n_tokens - 1], s.blocks)
         self.runner.kv.release(s.blocks)
+        if self.spec is not None and hasattr(self.spec.drafter, "release"):
+            self.spec.drafter.release(s.seq_id)
         self.finished[s.seq_id] = s
 
     def _reap(self):

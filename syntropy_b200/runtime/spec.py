@@ -36,6 +36,54 @@ class NgramDrafter:
         return [history[-1]] * g
 
 
+class DraftModelDrafter:
+    """Drafts with a smaller model of the same vocabulary (reference `DraftSource::DraftModel`,
+    crates/core/src/plan/speculative.rs): its own runner and paged KV cache.  Per sequence it
+    remembers the tokens its cache holds; on each window it keeps the longest prefix that still
+    matches the sequence (rejected drafts are overwritten), feeds the rest as one prefill chunk
+    after that prefix, then extends greedily one token at a time for the remaining drafts."""
+    stateful = True
+
+    def __init__(self, runner):
+        self.r = runner
+        self.fed: dict = {}     # key -> tokens whose K/V the draft cache holds, in order
+        self.blocks: dict = {}  # key -> the sequence's pages in the draft cache
+
+    def _feed(self, key, toks: list[int], start: int) -> int:
+        """K/V for toks at positions start.. (after the cached prefix); returns the greedy next token."""
+        r, kv = self.r, self.r.kv
+        blocks = self.blocks.setdefault(key, [])
+        kv.ensure(blocks, start + len(toks))
+        pos = list(range(start, start + len(toks)))
+        slots = [kv.slot(blocks, p) for p in pos]
+        logits = r.prefill(torch.tensor(toks), torch.tensor(pos), torch.tensor(slots, dtype=torch.int64),
+                           [0, len(toks)], [(list(blocks), start)] if start else None, block_lists=[list(blocks)])
+        return int(logits[0].argmax())
+
+    def propose(self, history: list[int], g: int, key=None) -> list[int]:
+        fed = self.fed.get(key, [])
+        c = 0
+        lim = min(len(fed), len(history) - 1)  # the last token is always fed again (its logits)
+        while c < lim and fed[c] == history[c]:
+            c += 1
+        nxt = self._feed(key, history[c:], c)
+        drafts = [nxt]
+        fed = list(history)
+        for _ in range(g - 1):
+            nxt = self._feed(key, [drafts[-1]], len(fed))
+            fed.append(drafts[-1])
+            drafts.append(nxt)
+        self.fed[key] = fed
+        return drafts
+
+    def release(self, key):
+        """Forget a finished sequence and return its draft pages."""
+        self.fed.pop(key, None)
+        blocks = self.blocks.pop(key, None)
+        if blocks:
+            self.r.kv.release(blocks)
+
+
 class MTPDrafter:
     """Drafts with the model's multi-token-prediction head (DeepSeek-V3 style): one token per
     step from the final residual of the last accepted position and the token after it.  The
