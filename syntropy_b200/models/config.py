@@ -24,6 +24,7 @@ class ModelConfig:
     rms_eps: float = 1e-5
     rope_theta: float = 10000.0
     qk_norm: bool = False
+    qkv_bias: bool = False  # bias on the Q, K and V projections (Qwen2)
     tie_embeddings: bool = False
     # MoE
     n_experts: int = 0
@@ -82,6 +83,7 @@ class ModelConfig:
                 attn += self.n_heads * self.v_head_dim * h
             else:
                 attn = h * (self.q_dim + 2 * self.kv_dim) + self.q_dim * h
+                attn += (self.q_dim + 2 * self.kv_dim) if self.qkv_bias else 0
             if self.layer_is_moe(i):
                 ffn = self.n_experts * 3 * h * self.moe_ffn + h * self.n_experts
                 ffn += self.n_shared_experts * 3 * h * self.moe_ffn
@@ -125,6 +127,12 @@ _reg(ModelConfig(name="deepseek-v3", family="deepseek3", n_layers=61, hidden=716
                  q_lora_rank=1536, kv_lora_rank=512, qk_rope_dim=64, qk_nope_dim=128, v_head_dim=128, n_mtp=1,
                  weight_quant="fp8"))
 # Small same-family configs for tests (same code paths, fewer/smaller layers).
+_reg(ModelConfig(name="tiny-qwen2", family="llama", n_layers=2, hidden=256, n_heads=4, n_kv_heads=2,
+                 head_dim=64, ffn=512, vocab=1024, rms_eps=1e-6, rope_theta=1000000.0, qkv_bias=True,
+                 tie_embeddings=True, weight_quant="fp32"))
+_reg(ModelConfig(name="qwen2.5-7b", family="llama", n_layers=28, hidden=3584, n_heads=28, n_kv_heads=4,
+                 head_dim=128, ffn=18944, vocab=152064, rms_eps=1e-6, rope_theta=1000000.0, qkv_bias=True,
+                 weight_quant="bf16"))
 _reg(ModelConfig(name="tiny-qwen-moe", family="qwen_moe", n_layers=2, hidden=256, n_heads=4, n_kv_heads=2,
                  head_dim=64, ffn=512, vocab=1024, rms_eps=1e-6, rope_theta=1000000.0, qk_norm=True,
                  n_experts=8, top_k=2, moe_ffn=128, weight_quant="fp32"))

@@ -122,9 +122,14 @@ def dense_ffn(h, W, pre):
 
 def gqa_attention_block(h, W, cfg: ModelConfig, pre: str, pos: torch.Tensor, kv_prefix=None):
     T = h.shape[0]
-    q = (h @ W[pre + "q_proj"].float().t()).view(T, cfg.n_heads, cfg.head_dim)
-    k = (h @ W[pre + "k_proj"].float().t()).view(T, cfg.n_kv_heads, cfg.head_dim)
-    v = (h @ W[pre + "v_proj"].float().t()).view(T, cfg.n_kv_heads, cfg.head_dim)
+    q = h @ W[pre + "q_proj"].float().t()
+    k = h @ W[pre + "k_proj"].float().t()
+    v = h @ W[pre + "v_proj"].float().t()
+    if cfg.qkv_bias:
+        q, k, v = q + W[pre + "q_bias"].float(), k + W[pre + "k_bias"].float(), v + W[pre + "v_bias"].float()
+    q = q.view(T, cfg.n_heads, cfg.head_dim)
+    k = k.view(T, cfg.n_kv_heads, cfg.head_dim)
+    v = v.view(T, cfg.n_kv_heads, cfg.head_dim)
     if cfg.qk_norm:
         q = rms_norm(q, W[pre + "q_norm"], cfg.rms_eps)
         k = rms_norm(k, W[pre + "k_norm"], cfg.rms_eps)

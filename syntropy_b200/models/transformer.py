@@ -90,6 +90,7 @@ class LayerWeights:
     o: object
     q_norm: torch.Tensor | None = None
     k_norm: torch.Tensor | None = None
+    qkv_bias: torch.Tensor | None = None  # [q_dim + 2 kv_dim] in the activation dtype (Qwen2)
     gate_up: object = None
     down: object = None
     router: torch.Tensor | None = None      # [E, H] (bf16 on CUDA)
@@ -279,6 +280,10 @@ def prepare_weights(cfg: ModelConfig, device="cpu", seed: int = 0, quant: str | 
         if cfg.qk_norm:
             L.q_norm = get(pre + "q_norm", sh["q_norm"]).float()
             L.k_norm = get(pre + "k_norm", sh["k_norm"]).float()
+        if cfg.qkv_bias and not cfg.is_mla:
+            b = torch.cat([get(pre + "q_bias", sh["q_bias"]), get(pre + "k_bias", sh["k_bias"]),
+                           get(pre + "v_bias", sh["v_bias"])]).float()
+            L.qkv_bias = b.to(device, torch.bfloat16 if is_cuda else torch.float32)
         if cfg.layer_is_moe(i):
             L.is_moe = True
             r = get(pre + "router", sh["router"])

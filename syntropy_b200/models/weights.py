@@ -49,6 +49,10 @@ def layer_shapes(cfg: ModelConfig, i: int) -> dict[str, tuple]:
         s["k_proj"] = (cfg.kv_dim, h)
         s["v_proj"] = (cfg.kv_dim, h)
         s["o_proj"] = (h, cfg.q_dim)
+        if cfg.qkv_bias:
+            s["q_bias"] = (cfg.q_dim,)
+            s["k_bias"] = (cfg.kv_dim,)
+            s["v_bias"] = (cfg.kv_dim,)
         if cfg.qk_norm:
             s["q_norm"] = (cfg.head_dim,)
             s["k_norm"] = (cfg.head_dim,)

@@ -123,9 +123,9 @@ def shard_state(cfg, sd: dict, rank: int, size: int) -> dict:
                 out[n] = t[:, rank * fs:(rank + 1) * fs]
             else:
                 out[n] = t
-        elif leaf == "q_proj":
+        elif leaf in ("q_proj", "q_bias"):
             out[n] = t[rank * hq * d:(rank + 1) * hq * d]
-        elif leaf in ("k_proj", "v_proj"):
+        elif leaf in ("k_proj", "v_proj", "k_bias", "v_bias"):
             out[n] = t[rank * hk * d:(rank + 1) * hk * d]
         elif leaf == "o_proj":
             out[n] = t[:, rank * hq * d:(rank + 1) * hq * d]

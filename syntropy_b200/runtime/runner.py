@@ -288,6 +288,8 @@ class ModelRunner:
         h = b["h"][:B]
         qkv = b["qkv"][:B]
         ops.linear(h, L.qkv, qkv, ops.GEMV_STORE)
+        if L.qkv_bias is not None:
+            qkv.add_(L.qkv_bias)
         q = b["q"][:B]
         ops.qk_rope_kv_write(qkv, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, L.q_norm, L.k_norm, cfg.rms_eps,
                              d["pos"][:B], self.mw.rope_cos, self.mw.rope_sin, d["slot"][:B], q, self.kv.k[i],
@@ -607,6 +609,8 @@ class ModelRunner:
                     self._row_parallel(mid, L.down, x)
                 continue
             ops.linear(h, L.qkv, qkv, ops.GEMV_STORE)
+            if L.qkv_bias is not None:
+                qkv.add_(L.qkv_bias)
             ops.qk_rope_kv_write(qkv, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, L.q_norm, L.k_norm, cfg.rms_eps,
                                  positions, mw.rope_cos, mw.rope_sin, slots, q, self.kv.k[i], self.kv.v[i])
             if paged is not None:
