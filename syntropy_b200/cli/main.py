@@ -27,12 +27,43 @@ def _engine_from_config(cfg, device: str):
     if cfg.tier.expert_cache_frac < 1.0 and mcfg.is_moe and dev.type == "cuda":
         from ..experts.cache import ExpertCache
         cache = ExpertCache(mw.layers, cfg.tier.expert_cache_frac, dev)
-        cache.enable_decode_prefetch(mcfg.n_experts)  # router-predicted prefetch of host experts
+        if cfg.tier.expert_prefetch:
+            cache.enable_decode_prefetch(mcfg.n_experts)  # router-predicted prefetch of host experts
+    kv_budget = cfg.tier.kv_budget or None
     runner = ModelRunner(mw, max_batch=cfg.sched.max_batch, max_seq_len=cfg.model.max_seq_len,
-                         use_graphs=cfg.sched.cuda_graphs and cfg.feature("cuda_graph"))
+                         use_graphs=cfg.sched.cuda_graphs and cfg.feature("cuda_graph"), kv_budget_bytes=kv_budget)
     runner.expert_cache = cache
+    if cache is not None and cfg.tier.cpu_expert_share > 0:
+        from ..experts.cpu_tier import CpuExpertTier
+        CpuExpertTier(cache, mcfg, max_rows=runner.max_batch, cpu_share=cfg.tier.cpu_expert_share,
+                      threads=cfg.tier.cpu_threads or None, timeout_s=cfg.kernels.spin_timeout,
+                      mode=cfg.kernels.cpu_gemv_mode)
     return LLMEngine(runner, max_prefill_tokens=cfg.sched.max_prefill_tokens,
-                     rebalance_every=cfg.tier.rebalance_every), mcfg
+                     rebalance_every=cfg.tier.rebalance_every, spec=_spec_from_config(cfg, mcfg, runner, dev)), mcfg
+
+
+def _spec_from_config(cfg, mcfg, runner, dev):
+    """Speculative decoding from the `spec` section (none | ngram | mtp | draft)."""
+    from ..runtime.spec import DraftModelDrafter, MTPDrafter, NgramDrafter, SpecConfig
+    kind = cfg.spec.drafter
+    if kind == "none":
+        return None
+    if kind == "ngram":
+        return SpecConfig(gamma=cfg.spec.gamma, drafter=NgramDrafter())
+    if kind == "mtp":
+        if not mcfg.n_mtp:
+            raise ValueError(f"spec.drafter = mtp: {mcfg.name} has no MTP head")
+        return SpecConfig(drafter=MTPDrafter(runner))
+    from ..models.config import get_config
+    from ..models.transformer import prepare_weights
+    from ..runtime.runner import ModelRunner
+    dcfg = get_config(cfg.spec.draft_model)
+    if dcfg.vocab != mcfg.vocab:
+        raise ValueError(f"draft model {dcfg.name} has vocabulary {dcfg.vocab}, the target {mcfg.vocab}")
+    dmw = prepare_weights(dcfg, dev, seed=cfg.model.seed, max_pos=cfg.model.max_seq_len + 16 + cfg.spec.gamma)
+    drunner = ModelRunner(dmw, max_batch=cfg.sched.max_batch, max_seq_len=cfg.model.max_seq_len + cfg.spec.gamma + 1,
+                          use_graphs=False)
+    return SpecConfig(gamma=cfg.spec.gamma, drafter=DraftModelDrafter(drunner))
 
 
 def cmd_version(args, cfg):

@@ -33,7 +33,7 @@ class CpuExpertTier:
     """Owns the mailbox, the CPU thread pool and the split of each layer's host experts."""
 
     def __init__(self, cache, cfg, max_rows: int, cpu_share: float = 0.75, threads: int | None = None,
-                 cpus: list[int] | None = None, timeout_s: float = 2.0):
+                 cpus: list[int] | None = None, timeout_s: float = 2.0, mode: int = -1):
         self.cache, self.cfg = cache, cfg
         self.E, self.k, self.H, self.I = cfg.n_experts, cfg.top_k, cfg.hidden, cfg.moe_ffn
         self.max_rows = max_rows
@@ -53,7 +53,7 @@ class CpuExpertTier:
             threads = int(os.environ.get("SYN_CPU_EXPERT_THREADS", max(1, len(cpus))))
         self.threads = threads
         self.native = ext().CpuExpertTier(len(cache.layers), self.E, self.H, self.I, self.k, max_rows,
-                                          self.mb_ptr, list(cpus), threads, -1)
+                                          self.mb_ptr, list(cpus), threads, mode)
         self.layer_of = {id(L): li for li, L in enumerate(cache.layers)}
         cache.cpu_tier = self
         self.assign()
