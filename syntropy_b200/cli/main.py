@@ -100,6 +100,10 @@ def cmd_run(args, cfg):
 
 
 def cmd_serve(args, cfg):
+    from ..daemon.bundle import install_crash_handler
+    from ..obs.log import install as install_log_suppression
+    install_crash_handler(os.path.expanduser("~/.cache/syntropy_b200/crashes"))
+    install_log_suppression()
     import uvicorn
 
     from ..api import build_app
@@ -122,6 +126,13 @@ def cmd_doctor(args, cfg):
     rep = doctor()
     print(json.dumps(rep, indent=2))
     sys.exit(0 if all(c["ok"] for c in rep["checks"]) else 1)
+
+
+def cmd_bundle(args, cfg):
+    """Redacted diagnostic bundle (config with origins, versions, metrics, flight recorder,
+    crash records, the doctor report)."""
+    from ..daemon.bundle import make_bundle
+    print(make_bundle(args.out, cfg, crash_dir=args.crash_dir, include_probe=args.probe))
 
 
 def cmd_bench(args, cfg):
@@ -156,13 +167,17 @@ def main(argv=None):
     p = sub.add_parser("probe")
     p.add_argument("--full", action="store_true")
     sub.add_parser("doctor")
+    p = sub.add_parser("bundle")
+    p.add_argument("--out", default="syntropy-bundle.tar.gz")
+    p.add_argument("--crash-dir", default=os.path.expanduser("~/.cache/syntropy_b200/crashes"))
+    p.add_argument("--probe", action="store_true", help="include the doctor report (touches the GPU)")
     p = sub.add_parser("bench")
     p.add_argument("rest", nargs=argparse.REMAINDER)
     args = ap.parse_args(argv)
     from ..config import load_config
     cfg = load_config(args.config, overrides=args.set)
     {"version": cmd_version, "config": cmd_config, "plan": cmd_plan, "run": cmd_run, "serve": cmd_serve,
-     "probe": cmd_probe, "doctor": cmd_doctor, "bench": cmd_bench}[args.cmd](args, cfg)
+     "probe": cmd_probe, "doctor": cmd_doctor, "bundle": cmd_bundle, "bench": cmd_bench}[args.cmd](args, cfg)
 
 
 if __name__ == "__main__":
