@@ -31,6 +31,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--eager", action="store_true", help="no CUDA graph (one launch per op)")
     ap.add_argument("--expert-cache-frac", type=float, default=1.0)
+    ap.add_argument("--cpu-experts", type=float, default=0.0,
+                    help="share of the host-tier experts computed by host CPU threads (with a VRAM cap)")
     ap.add_argument("--kernel-table", action="store_true", help="per-kernel device time of prefill and decode")
     ap.add_argument("--step-profile", action="store_true",
                     help="one decode step through the timestamped graph variant: device ms per segment")
@@ -44,7 +46,10 @@ def main():
     runner = ModelRunner(mw, max_batch=args.batch, max_seq_len=args.prompt + 64, use_graphs=not args.eager)
     if args.expert_cache_frac < 1.0:
         from ..experts.cache import ExpertCache
-        ExpertCache(mw.layers, args.expert_cache_frac, dev)
+        runner.expert_cache = ExpertCache(mw.layers, args.expert_cache_frac, dev)
+        if args.cpu_experts > 0:
+            from ..experts.cpu_tier import CpuExpertTier
+            CpuExpertTier(runner.expert_cache, cfg, max_rows=runner.max_batch, cpu_share=args.cpu_experts)
     eng = LLMEngine(runner)
     g = torch.Generator().manual_seed(0)
     for _ in range(args.batch):
