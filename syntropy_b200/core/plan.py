@@ -82,6 +82,7 @@ class PlacementPlan:
     speculative: SpeculativeConfig | None = None
     predicted_step_ms: float | None = None
     cost_terms: dict = field(default_factory=dict)
+    cpu_expert_share: float = 0.0    # share of the host experts computed by host CPU threads
 
     @property
     def n_devices(self) -> int:
@@ -94,6 +95,9 @@ class PlacementPlan:
                          f"collective={s.collective.value}")
         if self.expert_cache_frac < 1.0:
             lines.append(f"  expert cache: {self.expert_cache_frac:.0%} of experts VRAM-resident, rest in pinned host RAM")
+            if self.cpu_expert_share > 0:
+                lines.append(f"  host tier: {self.cpu_expert_share:.0%} of the host experts computed by host CPU "
+                             f"threads, the rest read over PCIe (concurrently)")
         if self.predicted_step_ms is not None:
             lines.append(f"  predicted decode step: {self.predicted_step_ms:.2f} ms")
             for k, v in sorted(self.cost_terms.items()):

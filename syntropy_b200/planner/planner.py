@@ -5,7 +5,10 @@ bandwidths.
 Decode is priced term by term (the reference's CostTerm idea, crates/obs/src/cost_term.rs):
   weights  = bytes streamed per step / (HBM bandwidth * kernel efficiency)
   kv       = KV bytes read per step / HBM bandwidth
-  host     = cold-expert bytes read over PCIe / PCIe bandwidth
+  host     = cold-expert bytes split between the GPU's PCIe reads and the host CPU threads,
+             which run concurrently: max(PCIe part / PCIe rate, CPU part / CPU rate) plus the
+             per-layer hand-off cost; the planner picks the CPU share that balances the two
+             paths (one GPU per host slice)
   collect  = per-layer collective latency (alpha) + bytes / NVLink bandwidth (beta)
   launch   = kernels per step * graph-launch gap
 The collective model follows crates/solver/src/collective.rs:236-333 (one-shot vs ring).
@@ -29,6 +32,12 @@ class HardwareModel:
     nvlink_alpha_us: float = 6.0   # one fused flag round trip
     nccl_alpha_us: float = 18.0    # small NCCL collective latency
     pcie_gbs: float = 55.5         # pinned H2D (measured on the B200 box)
+    # host tier with the CPU expert pool: fitted to capped Qwen3 decode at CPU shares 0.5 / 0.75 / 1.0
+    # on one B200 node slice (715 / 602 / 711 ms per step), per-layer time = fixed + max(PCIe
+    # part, CPU part)
+    pcie_read_gbs: float = 50.0    # GPU reading host experts in place while the CPU also reads DRAM
+    cpu_expert_gbs: float = 100.0  # host CPU expert pool, 14 threads
+    cpu_tier_layer_ms: float = 2.7  # per MoE layer: hand-off, collect and the serial part around them
     vram_gb: float = 178.0
     launch_gap_us: float = 1.2     # per kernel inside a CUDA graph
     tflops: float = 1422.0         # sustained bf16
@@ -57,8 +66,13 @@ def _weight_bytes(cfg: ModelConfig) -> tuple[float, float, float]:
     return attn, expert, head
 
 
+def best_cpu_share(hw: HardwareModel) -> float:
+    """CPU share of the host experts that equalises the two concurrent paths."""
+    return hw.cpu_expert_gbs / (hw.cpu_expert_gbs + hw.pcie_read_gbs)
+
+
 def price_decode(cfg: ModelConfig, n_gpu: int, batch: int, ctx: int, mode: ParallelismMode, cache_frac: float,
-                 hw: HardwareModel, fused: bool = True) -> dict:
+                 hw: HardwareModel, fused: bool = True, cpu_share: float = 0.0) -> dict:
     attn_b, exp_b, head_b = _weight_bytes(cfg)
     L = cfg.n_layers
     terms = {}
@@ -73,7 +87,12 @@ def price_decode(cfg: ModelConfig, n_gpu: int, batch: int, ctx: int, mode: Paral
         cold = active_local * (1.0 - cache_frac)
         attn_rank = attn_b / (n_gpu if mode == ParallelismMode.INTRA_NODE_TP else 1)
         terms["weights"] = L * (hot * exp_b + attn_rank) / (hw.hbm_gbs * 1e9 * hw.hbm_eff) * 1e3
-        terms["host_tier"] = L * cold * exp_b / (hw.pcie_gbs * 1e9) * 1e3
+        if cpu_share > 0:
+            terms["host_tier"] = L * cold * exp_b * max((1 - cpu_share) / (hw.pcie_read_gbs * 1e9),
+                                                        cpu_share / (hw.cpu_expert_gbs * 1e9)) * 1e3
+            terms["cpu_handoff"] = L * hw.cpu_tier_layer_ms
+        else:
+            terms["host_tier"] = L * cold * exp_b / (hw.pcie_gbs * 1e9) * 1e3
         kv_tok = 2 * cfg.kv_dim * 2 * L
         terms["kv"] = per_rank_tokens * ctx * kv_tok / (hw.hbm_gbs * 1e9 * 0.45) * 1e3
         if n_gpu > 1:
@@ -114,8 +133,10 @@ def fits(cfg: ModelConfig, n_gpu: int, mode: ParallelismMode, cache_frac: float,
 
 def plan_placement(cfg: ModelConfig, n_gpu: int, batch: int = 32, ctx: int = 2048,
                    cache_frac: float | None = None, hw: HardwareModel | None = None,
-                   fused: bool = True) -> PlacementPlan:
+                   fused: bool = True, cpu_tier: bool = True) -> PlacementPlan:
     hw = hw or HardwareModel.from_measured()
+    # the host CPU tier serves one GPU (under expert parallelism each rank reads over PCIe)
+    share = best_cpu_share(hw) if cpu_tier and n_gpu == 1 and cfg.is_moe else 0.0
     cands = []
     modes = [ParallelismMode.LOCAL] if n_gpu == 1 else [ParallelismMode.EP, ParallelismMode.INTRA_NODE_TP,
                                                        ParallelismMode.DP]
@@ -129,7 +150,7 @@ def plan_placement(cfg: ModelConfig, n_gpu: int, batch: int = 32, ctx: int = 204
             if mode == ParallelismMode.DP:
                 t = price_decode(cfg, 1, max(1, batch // n_gpu), ctx, ParallelismMode.LOCAL, fr, hw)
             else:
-                t = price_decode(cfg, n_gpu, batch, ctx, mode, fr, hw, fused)
+                t = price_decode(cfg, n_gpu, batch, ctx, mode, fr, hw, fused, cpu_share=share if fr < 1 else 0.0)
             cands.append((t["total"], mode, fr, t))
     if not cands:
         raise ValueError(f"{cfg.name} does not fit on {n_gpu} GPU(s) at batch {batch}, ctx {ctx}")
@@ -143,4 +164,5 @@ def plan_placement(cfg: ModelConfig, n_gpu: int, batch: int = 32, ctx: int = 204
     if mode == ParallelismMode.INTRA_NODE_TP:
         stage.tp = TpSplit([1.0 / n_gpu] * n_gpu)
     return PlacementPlan(model=cfg.name, stages=[stage], expert_cache_frac=fr, max_batch=batch,
-                         predicted_step_ms=total, cost_terms={k: v for k, v in terms.items() if k != "total"})
+                         predicted_step_ms=total, cost_terms={k: v for k, v in terms.items() if k != "total"},
+                         cpu_expert_share=share if fr < 1 else 0.0)
