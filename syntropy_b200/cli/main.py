@@ -82,6 +82,7 @@ def cmd_plan(args, cfg):
                        cache_frac=args.expert_cache_frac, fused=cfg.parallel.fused_collectives)
     print(p.describe() if args.explain else json.dumps({"mode": p.stages[0].mode.value,
                                                         "expert_cache_frac": p.expert_cache_frac,
+                                                        "cpu_expert_share": round(p.cpu_expert_share, 3),
                                                         "predicted_step_ms": p.predicted_step_ms}))
 
 
