@@ -216,7 +216,10 @@ class LLMEngine:
             return False
         s, layers = self.swapped[0]
         kv = self.runner.kv
-        if kv.alloc.num_free < kv.blocks_needed(s.n_tokens + 1):
+        need = kv.blocks_needed(s.n_tokens + 1)
+        if kv.alloc.num_free < need and self.prefix is not None:
+            self.prefix.evict(need - kv.alloc.num_free)  # cached prefixes give way to a preempted sequence
+        if kv.alloc.num_free < need:
             return False
         self.swapped.popleft()
         self._unpack_kv(s, layers)
@@ -253,6 +256,13 @@ class LLMEngine:
             return self._step_lockstep()
         while self._swap_in():
             pass
+        if self.swapped and not self.running:  # it cannot wait for pages nobody will return
+            s0 = self.swapped[0][0]
+            kv = self.runner.kv
+            raise MemoryError(f"preempted sequence {s0.seq_id} needs {kv.blocks_needed(s0.n_tokens + 1)} KV pages; "
+                              f"{kv.alloc.num_free} are free and nothing is running")
+        if self.running and self._pages_short() > 0 and self.prefix is not None:
+            self.prefix.evict(self._pages_short())  # unreferenced cached prefixes go first
         if self.running and self._pages_short() > 0:
             # the KV pool cannot hold the next step: preempt the newest sequences to host memory
             while len(self.running) > 1 and self._pages_short() > 0:
