@@ -126,6 +126,12 @@ class LLMEngine:
                 raise ValueError(f"token id {t} out of range [0, {self.cfg.vocab})")
         if len(prompt) + params.max_tokens > self.runner.max_seq_len:
             raise ValueError("prompt + max_tokens exceeds max_seq_len")
+        kv = self.runner.kv
+        pool = kv.alloc.num_blocks - kv.alloc.reserved
+        if kv.blocks_needed(len(prompt) + params.max_tokens) > pool:
+            # a request must be able to finish alone (preemption makes room for it, never more)
+            raise ValueError(f"prompt + max_tokens needs {kv.blocks_needed(len(prompt) + params.max_tokens)} KV "
+                             f"pages; the cache has {pool}")
         if params.logit_bias and not all(0 <= int(t) < self.cfg.vocab for t in params.logit_bias):
             raise ValueError(f"logit_bias token ids must be in [0, {self.cfg.vocab})")
         if params.repetition_penalty <= 0:

@@ -1,6 +1,7 @@
 """KV tiering by preemption on CPU: with a page pool too small for every running sequence to
 grow, the engine swaps the newest sequences' KV pages out to host memory and back in later;
 the tokens equal a run with an ample pool."""
+import pytest
 import torch
 
 from syntropy_b200.models.config import get_config
@@ -47,3 +48,14 @@ def test_swap_with_prefix_cache():
         got = [eng.finished[i].output for i in sorted(eng.finished)]
         assert got == want, nb
         assert eng.stats["swapped_out"] == eng.stats["swapped_in"]
+
+
+def test_request_larger_than_the_pool_is_rejected():
+    cfg = get_config("tiny-llama")
+    mw = prepare_weights(cfg, torch.device("cpu"), seed=2)
+    eng = LLMEngine(ModelRunner(mw, max_batch=4, max_seq_len=128, num_blocks=3))
+    with pytest.raises(ValueError, match="KV pages"):
+        eng.add_request(list(range(5, 65)), SamplingParams(max_tokens=4))
+    eng.add_request(list(range(5, 20)), SamplingParams(max_tokens=4))  # fits: served
+    while eng.has_work():
+        eng.step()
