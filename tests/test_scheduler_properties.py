@@ -1,0 +1,56 @@
+"""Scheduling properties (hypothesis, CPU): for random mixes of requests on a tight KV page
+pool — with or without the prefix cache and n-gram speculation — every request finishes within
+a bounded number of steps and greedy outputs equal those of the same request served alone with
+an ample pool (preemption, prefix sharing and batching never change tokens)."""
+import pytest
+import torch
+
+hypothesis = pytest.importorskip("hypothesis")
+from hypothesis import HealthCheck, given, settings  # noqa: E402
+from hypothesis import strategies as st  # noqa: E402
+
+from syntropy_b200.models.config import get_config  # noqa: E402
+from syntropy_b200.models.transformer import prepare_weights  # noqa: E402
+from syntropy_b200.runtime.engine import LLMEngine, SamplingParams  # noqa: E402
+from syntropy_b200.runtime.runner import ModelRunner  # noqa: E402
+from syntropy_b200.runtime.spec import SpecConfig  # noqa: E402
+
+_MW = {}
+
+
+def _mw():
+    if "mw" not in _MW:
+        cfg = get_config("tiny-llama")
+        _MW["cfg"], _MW["mw"] = cfg, prepare_weights(cfg, torch.device("cpu"), seed=6)
+        _MW["alone"] = LLMEngine(ModelRunner(_MW["mw"], max_batch=1, max_seq_len=96))
+    return _MW["cfg"], _MW["mw"]
+
+
+def _alone(prompt, n):
+    _mw()
+    return _MW["alone"].generate([prompt], SamplingParams(max_tokens=n))[0]
+
+
+@settings(max_examples=25, deadline=None, derandomize=True, suppress_health_check=[HealthCheck.too_slow])
+@given(reqs=st.lists(st.tuples(st.integers(0, 2), st.integers(1, 30), st.integers(1, 24)), min_size=1, max_size=5),
+       pool=st.integers(7, 14), prefix=st.booleans(), spec=st.booleans())
+def test_every_request_finishes_with_its_own_tokens(reqs, pool, prefix, spec):
+    cfg, mw = _mw()
+    bases = [[11, 12, 13, 14, 15, 16, 17, 18, 19, 20, 21, 22, 23, 24, 25, 26, 27], [40, 41], [90]]
+    prompts = [bases[b] + list(range(100, 100 + n)) for b, n, _ in reqs]
+    eng = LLMEngine(ModelRunner(mw, max_batch=4, max_seq_len=96, num_blocks=pool), prefix_cache=prefix,
+                    spec=SpecConfig(gamma=2) if spec else None)
+    ids = []
+    for p, (_, _, m) in zip(prompts, reqs):
+        try:
+            ids.append(eng.add_request(p, SamplingParams(max_tokens=m)))
+        except ValueError:  # larger than the whole pool: rejected up front
+            ids.append(None)
+    for _ in range(400):
+        if not eng.has_work():
+            break
+        eng.step()
+    assert not eng.has_work(), (len(eng.running), len(eng.waiting), len(eng.swapped))
+    for i, p, (_, _, m) in zip(ids, prompts, reqs):
+        if i is not None:
+            assert eng.finished[i].output == _alone(p, m)
