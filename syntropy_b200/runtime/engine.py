@@ -415,9 +415,7 @@ class LLMEngine:
     def _decode(self) -> list[StepOutput]:
         # Under lockstep ranks every rank runs the same verify window shape (equal live
         # sequence counts), so the expert-parallel exchanges inside it line up.
-        # constrained sequences take plain steps (their rows are re-drawn from masked logits)
-        plain = self.spec is None or any(self._redraw(s) for s in self.running)
-        outs = self._decode_plain() if plain else self._decode_spec()
+        outs = self._decode_plain() if self.spec is None else self._decode_spec()
         r = self.runner
         n = self.stats["decode_steps"]
         if r.expert_cache is not None and self.rebalance_every and n % self.rebalance_every == 0:
@@ -471,6 +469,14 @@ class LLMEngine:
         ctr = torch.tensor([s.rng_counter for s in seqs], dtype=torch.int64)
         toks, nacc = verify(logits, torch.tensor(drafts, dtype=torch.int32), temp, topk, topp, seed, stream, ctr)
         r.after_step()
+        redo = [i for i, s in enumerate(seqs) if self._redraw(s)]
+        if redo:
+            # penalised / constrained rows take one token per step, drawn from their processed
+            # logits at the window's first row with their own counter (exactly a plain step), so
+            # what the others in the batch do never changes their draws; their drafts are dropped
+            t1 = self._sample_rows(logits[[i * (g + 1) for i in redo]], [seqs[i] for i in redo])
+            for i, t in zip(redo, t1):
+                toks[i, 0], nacc[i], ctr[i] = t, 0, seqs[i].rng_counter
         self.stats["decode_steps"] += 1
         outs = []
         mtp_items = []
@@ -480,8 +486,9 @@ class LLMEngine:
             if mtp:
                 row = i * (g + 1) + n
                 mtp_items.append((s, r.buf["x"][row].clone(), int(d["pos"][row])))
-            self.stats["spec_drafted"] += g
-            self.stats["spec_accepted"] += n
+            if i not in redo:
+                self.stats["spec_drafted"] += g
+                self.stats["spec_accepted"] += n
             new = toks[i, : n + 1].tolist()
             emitted = []
             for t in new:
