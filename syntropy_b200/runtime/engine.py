@@ -245,6 +245,12 @@ class LLMEngine:
         s = Sequence(sid, list(state["prompt"]), state["params"], output=list(state["output"]),
                      t_arrival=time.perf_counter())
         s.seed, s.stream, s.rng_counter = state["seed"], state["stream"], state["rng_counter"]
+        if s.params.constraint is not None:  # the grammar state: replay what was emitted
+            from ..text.constrain import make_constraint
+            s.constraint = make_constraint(self._token_trie(), self.eos, s.params.constraint)
+            for t in s.output:
+                if not s.constraint.advance(int(t)):
+                    raise ValueError("saved session's output does not follow its constraint")
         if kv.alloc.num_free < kv.blocks_needed(s.n_tokens + 1):
             raise RuntimeError("not enough free KV pages to restore the session")
         self._unpack_kv(s, state["kv"])

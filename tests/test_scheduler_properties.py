@@ -71,3 +71,31 @@ def test_every_request_finishes_with_its_own_tokens(reqs, pool, prefix, spec):
     for i, p, sp in zip(ids, prompts, params):
         if i is not None:
             assert eng.finished[i].output == _alone(p, sp, spec)
+
+
+@settings(max_examples=15, deadline=None, derandomize=True, suppress_health_check=[HealthCheck.too_slow])
+@given(n=st.integers(1, 30), m=st.integers(2, 20), cut=st.integers(0, 19), kind=st.integers(0, 3),
+       seed=st.integers(0, 99))
+def test_saved_session_resumes_exactly(n, m, cut, kind, seed):
+    """A sequence saved at any step and restored into a fresh engine (with other traffic there)
+    finishes with the tokens of an uninterrupted run (a constrained one with its grammar state)."""
+    cfg, mw = _mw()
+    prompt = [5, 6, 7] + list(range(200, 200 + n))
+    sp = _params(kind, m, seed)
+    want = _alone(prompt, sp, False)
+    a = LLMEngine(ModelRunner(mw, max_batch=2, max_seq_len=96))
+    sid = a.add_request(prompt, sp)
+    a.step()  # prefill: first token
+    for _ in range(min(cut, m - 2)):
+        a.step()
+    if sid in a.finished:
+        assert a.finished[sid].output == want
+        return
+    state = a.save_session(sid)
+    b = LLMEngine(ModelRunner(mw, max_batch=3, max_seq_len=96))
+    other = b.add_request([9, 9, 9, 9], SamplingParams(max_tokens=5))
+    rid = b.restore_session(state)
+    while b.has_work():
+        b.step()
+    assert b.finished[rid].output == want
+    assert len(b.finished[other].output) == 5
