@@ -1,5 +1,6 @@
 """Tensor x pipeline parallelism on CPU ranks (gloo, TP=2 x PP=2 over 4 ranks): each stage
-holds half the layers, sharded over its two TP ranks; tokens equal a single process."""
+holds half the layers, sharded over its two TP ranks; tokens equal a single process, for the
+dense tiny Llama and for the tiny Qwen3-MoE (TP inside the experts)."""
 import os
 import socket
 
@@ -26,14 +27,14 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, model="tiny-llama"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
     from syntropy_b200.parallel.dist import init_distributed, shutdown, split_tp_pp
     from syntropy_b200.parallel.pp import PPGroup
     from syntropy_b200.parallel.tp import TPGroup
     ctx = init_distributed(backend="gloo", timeout_s=60)
-    cfg = get_config("tiny-llama").replace(n_layers=4)
+    cfg = get_config(model).replace(n_layers=4)
     sd = synthetic_state_dict(cfg, seed=13)
     tp_ctx, pp_group, pp_ranks, stage = split_tp_pp(ctx, 2, 2)
     pp = PPGroup(ctx, 2, stage, cfg.n_layers, group=pp_group, ranks=pp_ranks)
@@ -45,8 +46,8 @@ def _worker(rank, world, port, q):
     shutdown(ctx)
 
 
-def test_tp2_pp2_match_single_process():
-    cfg = get_config("tiny-llama").replace(n_layers=4)
+def test_tp2_pp2_match_single_process(model="tiny-llama"):
+    cfg = get_config(model).replace(n_layers=4)
     sd = synthetic_state_dict(cfg, seed=13)
     want = LLMEngine(ModelRunner(prepare_weights(cfg, "cpu", state_dict=sd), max_batch=4, max_seq_len=128)).generate(
         _prompts(), SamplingParams(max_tokens=5, temperature=0.7, seed=9))
@@ -54,10 +55,15 @@ def test_tp2_pp2_match_single_process():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, model)) for r in range(world)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=300) for _ in range(world))
     for p in procs:
         p.join(timeout=60)
     assert got[0] == got[1] == got[2] == got[3] == want
+
+
+def test_tp2_pp2_moe_match_single_process():
+    """The same with the tiny Qwen3-MoE: experts split along their width inside each stage."""
+    test_tp2_pp2_match_single_process("tiny-qwen-moe")
