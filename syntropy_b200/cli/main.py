@@ -14,14 +14,18 @@ def _engine_from_config(cfg, device: str):
     from ..models.transformer import prepare_weights
     from ..runtime.engine import LLMEngine
     from ..runtime.runner import ModelRunner
-    mcfg = get_config(cfg.model.name)
-    if cfg.model.quant:
-        mcfg = mcfg.replace(weight_quant=cfg.model.quant)
     dev = torch.device(device)
     sd = None
-    if cfg.model.path:
-        from ..formats.safetensors import load_state_dict
-        sd = load_state_dict(cfg.model.path)
+    if cfg.model.path and os.path.exists(os.path.join(cfg.model.path, "config.json")):
+        from ..models.hf import load_hf  # a Hugging Face checkpoint directory
+        mcfg, sd = load_hf(cfg.model.path, weight_quant=cfg.model.quant or ("bf16" if dev.type == "cuda" else "fp32"))
+    else:
+        mcfg = get_config(cfg.model.name)
+        if cfg.model.quant:
+            mcfg = mcfg.replace(weight_quant=cfg.model.quant)
+        if cfg.model.path:
+            from ..formats.safetensors import load_state_dict
+            sd = load_state_dict(cfg.model.path)
     mw = prepare_weights(mcfg, dev, seed=cfg.model.seed, state_dict=sd, max_pos=cfg.model.max_seq_len + 16)
     cache = None
     if cfg.tier.expert_cache_frac < 1.0 and mcfg.is_moe and dev.type == "cuda":

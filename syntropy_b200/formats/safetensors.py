@@ -37,7 +37,7 @@ class SafetensorsFile:
         dt, shape, b, e = self.tensors[name]
         dtype = _DT[dt]
         buf = memoryview(self._mm)[self.data_start + b: self.data_start + e]
-        t = torch.frombuffer(buf, dtype=torch.uint8).clone()
+        t = torch.frombuffer(bytearray(buf), dtype=torch.uint8)
         return t.view(dtype).reshape(shape) if dtype != torch.uint8 else t.reshape(shape)
 
     def close(self):

@@ -1,0 +1,85 @@
+"""Hugging Face checkpoints on CPU: tiny random Llama, Qwen2, Qwen3 and Qwen3-MoE models built
+and saved with the `transformers` library load through `models/hf.py`, and the engine's greedy
+tokens equal `transformers`' own greedy continuation (an independent implementation)."""
+import pytest
+import torch
+
+transformers = pytest.importorskip("transformers")
+
+from syntropy_b200.models.hf import config_from_hf, load_hf  # noqa: E402
+from syntropy_b200.models.transformer import prepare_weights  # noqa: E402
+from syntropy_b200.runtime.engine import LLMEngine, SamplingParams  # noqa: E402
+from syntropy_b200.runtime.runner import ModelRunner  # noqa: E402
+
+COMMON = dict(vocab_size=512, hidden_size=128, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+              rms_norm_eps=1e-6, max_position_embeddings=256)
+
+
+def _models():
+    yield "llama", transformers.LlamaForCausalLM(transformers.LlamaConfig(intermediate_size=256, **COMMON))
+    yield "qwen2", transformers.Qwen2ForCausalLM(transformers.Qwen2Config(intermediate_size=256,
+                                                                          tie_word_embeddings=True, **COMMON))
+    yield "qwen3", transformers.Qwen3ForCausalLM(transformers.Qwen3Config(intermediate_size=256, head_dim=32,
+                                                                          **COMMON))
+    yield "qwen3moe", transformers.Qwen3MoeForCausalLM(transformers.Qwen3MoeConfig(
+        intermediate_size=256, moe_intermediate_size=64, head_dim=32, num_experts=8, num_experts_per_tok=2,
+        norm_topk_prob=True, **COMMON))
+
+
+def _hf_greedy(model, prompt, n):
+    ids = torch.tensor([prompt])
+    out = []
+    with torch.no_grad():
+        for _ in range(n):
+            nxt = int(model(ids).logits[0, -1].argmax())
+            out.append(nxt)
+            ids = torch.cat([ids, torch.tensor([[nxt]])], 1)
+    return out
+
+
+def test_engine_matches_transformers(tmp_path):
+    torch.manual_seed(0)
+    prompt = [5, 17, 99, 250, 3, 42, 77]
+    for name, model in _models():
+        model = model.float().eval()
+        with torch.no_grad():  # larger weights than the default init, so argmaxes are not near ties
+            for p in model.parameters():
+                if p.dim() > 1:
+                    p.normal_(0, 0.08)
+        d = tmp_path / name
+        model.save_pretrained(str(d))
+        cfg, sd = load_hf(str(d), weight_quant="fp32")
+        assert cfg.qkv_bias == (name == "qwen2") and cfg.qk_norm == name.startswith("qwen3")
+        assert cfg.is_moe == (name == "qwen3moe")
+        want = _hf_greedy(model, prompt, 10)
+        mw = prepare_weights(cfg, "cpu", state_dict=sd, max_pos=64)
+        got = LLMEngine(ModelRunner(mw, max_batch=2, max_seq_len=48)).generate([prompt], SamplingParams(max_tokens=10))
+        assert got[0] == want, name
+
+
+def test_unsupported_configs_are_rejected():
+    base = dict(architectures=["LlamaForCausalLM"], hidden_size=64, num_attention_heads=4, num_hidden_layers=1,
+                vocab_size=100, intermediate_size=128)
+    with pytest.raises(ValueError, match="rotary scaling"):
+        config_from_hf(dict(base, rope_scaling={"rope_type": "yarn", "factor": 4.0}))
+    with pytest.raises(ValueError, match="sliding"):
+        config_from_hf(dict(base, architectures=["MistralForCausalLM"], sliding_window=4096))
+    with pytest.raises(ValueError, match="not supported"):
+        config_from_hf(dict(base, architectures=["GPT2LMHeadModel"]))
+
+
+def test_cli_serves_a_checkpoint_directory(tmp_path):
+    import json
+    import os
+    import subprocess
+    import sys
+    torch.manual_seed(1)
+    m = transformers.Qwen3ForCausalLM(transformers.Qwen3Config(intermediate_size=256, head_dim=32, **COMMON)).float()
+    m.save_pretrained(str(tmp_path / "ckpt"))
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-m", "syntropy_b200", "-o", f"model.path={tmp_path / 'ckpt'}",
+                        "-o", "model.max_seq_len=64", "-o", "sched.max_batch=2", "run", "--tokens", "5,6,7",
+                        "--max-tokens", "4", "--device", "cpu"], capture_output=True, text=True, timeout=300,
+                       env=dict(os.environ, PYTHONPATH=root), cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert json.loads(r.stdout)["tokens"] == _hf_greedy(m.eval(), [5, 6, 7], 4)
