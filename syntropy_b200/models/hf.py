@@ -2,9 +2,12 @@
 this package's canonical state dict.
 
 Accepted architectures (the reference's `llama` and `qwen_moe` families, crates/graph/src/
-families/{llama.rs,qwen_moe.rs}): LlamaForCausalLM and MistralForCausalLM (no projection bias,
-no sliding window), Qwen2ForCausalLM (bias on the Q, K and V projections), Qwen3ForCausalLM
-(QK-norm), Qwen3MoeForCausalLM (QK-norm, every layer MoE).  Rotary scaling other than the
+families/{llama.rs,qwen_moe.rs}, and the DeepSeek-V3 family of the target configs):
+LlamaForCausalLM and MistralForCausalLM (no projection bias, no sliding window),
+Qwen2ForCausalLM (bias on the Q, K and V projections), Qwen3ForCausalLM (QK-norm),
+Qwen3MoeForCausalLM (QK-norm, every layer MoE), DeepseekV3ForCausalLM (MLA, sigmoid
+group-limited routing with a selection bias, shared experts, leading dense layers; its rotary
+dimensions, stored interleaved, are reordered to the rotate-half layout used here).  Rotary scaling other than the
 plain one, a sliding window in effect, or an O-projection / MLP bias are rejected with a
 message instead of being served wrongly.  Experts may be stored per expert (the Hub layout:
 `mlp.experts.{e}.{gate,up,down}_proj.weight`) or fused (`mlp.experts.gate_up_proj`, `down_proj`).
@@ -20,7 +23,7 @@ import torch
 from .config import ModelConfig
 
 FAMILY = {"LlamaForCausalLM": "llama", "MistralForCausalLM": "llama", "Qwen2ForCausalLM": "llama",
-          "Qwen3ForCausalLM": "llama", "Qwen3MoeForCausalLM": "qwen_moe"}
+          "Qwen3ForCausalLM": "llama", "Qwen3MoeForCausalLM": "qwen_moe", "DeepseekV3ForCausalLM": "deepseek3"}
 
 
 def config_from_hf(d: dict, name: str = "hf", weight_quant: str = "bf16") -> ModelConfig:
@@ -42,6 +45,16 @@ def config_from_hf(d: dict, name: str = "hf", weight_quant: str = "bf16") -> Mod
               ffn=d.get("intermediate_size") or 0, vocab=d["vocab_size"], rms_eps=d.get("rms_norm_eps", 1e-6),
               rope_theta=float(theta), qk_norm=arch.startswith("Qwen3"), qkv_bias=arch == "Qwen2ForCausalLM",
               tie_embeddings=bool(d.get("tie_word_embeddings", False)), weight_quant=weight_quant)
+    if arch == "DeepseekV3ForCausalLM":
+        dn, dr, dv = d["qk_nope_head_dim"], d["qk_rope_head_dim"], d["v_head_dim"]
+        kw.update(n_kv_heads=nh, head_dim=dn + dr, qk_norm=False, q_lora_rank=d.get("q_lora_rank") or 0,
+                  kv_lora_rank=d["kv_lora_rank"], qk_rope_dim=dr, qk_nope_dim=dn, v_head_dim=dv,
+                  n_experts=d["n_routed_experts"], top_k=d["num_experts_per_tok"],
+                  moe_ffn=d["moe_intermediate_size"], n_shared_experts=d.get("n_shared_experts") or 0,
+                  router_scoring="sigmoid", n_groups=d.get("n_group") or 1, topk_groups=d.get("topk_group") or 1,
+                  routed_scaling=float(d.get("routed_scaling_factor", 1.0)),
+                  norm_topk_prob=bool(d.get("norm_topk_prob", True)),
+                  first_dense_layers=d.get("first_k_dense_replace") or 0)
     if arch == "Qwen3MoeForCausalLM":
         if d.get("mlp_only_layers") or d.get("decoder_sparse_step", 1) != 1:
             raise ValueError("dense layers between the MoE layers are not supported")
@@ -57,11 +70,32 @@ _LAYER = {"input_layernorm.weight": "attn_norm", "post_attention_layernorm.weigh
           "self_attn.q_proj.bias": "q_bias", "self_attn.k_proj.bias": "k_bias", "self_attn.v_proj.bias": "v_bias",
           "self_attn.q_norm.weight": "q_norm", "self_attn.k_norm.weight": "k_norm",
           "mlp.gate_proj.weight": "gate", "mlp.up_proj.weight": "up", "mlp.down_proj.weight": "down",
-          "mlp.gate.weight": "router"}
+          "mlp.gate.weight": "router", "mlp.gate.e_score_correction_bias": "router_bias",
+          "mlp.shared_experts.gate_proj.weight": "shared.gate", "mlp.shared_experts.up_proj.weight": "shared.up",
+          "mlp.shared_experts.down_proj.weight": "shared.down",
+          "self_attn.q_a_proj.weight": "q_a", "self_attn.q_a_layernorm.weight": "q_a_norm",
+          "self_attn.q_b_proj.weight": "q_b", "self_attn.kv_a_proj_with_mqa.weight": "kv_a",
+          "self_attn.kv_a_layernorm.weight": "kv_a_norm", "self_attn.kv_b_proj.weight": "kv_b"}
 
 
-def canonical_from_hf(sd: dict) -> dict:
-    """Hugging Face tensor names -> canonical names (experts stacked [E, ...])."""
+def _deinterleave_rope(sd: dict, cfg: ModelConfig):
+    """Rotary dimensions stored as interleaved pairs (0,1), (2,3), ... -> rotate-half order
+    (evens, then odds) in the rows of the Q projection (per head) and of the shared K rope."""
+    dn, dr, H, c = cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.n_heads, cfg.kv_lora_rank
+    perm = torch.cat([torch.arange(0, dr, 2), torch.arange(1, dr, 2)])
+    for n in list(sd):
+        leaf = n.split(".")[-1]
+        if leaf in ("q_b", "q_proj"):
+            w = sd[n].view(H, dn + dr, -1)
+            sd[n] = torch.cat([w[:, :dn], w[:, dn:][:, perm]], 1).reshape(H * (dn + dr), -1).contiguous()
+        elif leaf == "kv_a":
+            w = sd[n]
+            sd[n] = torch.cat([w[:c], w[c:][perm]], 0).contiguous()
+
+
+def canonical_from_hf(sd: dict, cfg: ModelConfig | None = None, rope_interleave: bool = True) -> dict:
+    """Hugging Face tensor names -> canonical names (experts stacked [E, ...]; MLA rotary rows
+    reordered when `cfg` is an MLA model stored with interleaved rotary dimensions)."""
     out, experts = {}, {}
     for n, t in sd.items():
         if n == "model.embed_tokens.weight":
@@ -91,6 +125,8 @@ def canonical_from_hf(sd: dict) -> dict:
                 raise KeyError(f"unmapped tensor {n}")
     for (i, kind), d in experts.items():
         out[f"layers.{i}.experts.{kind}"] = torch.stack([d[e] for e in sorted(d)])
+    if cfg is not None and cfg.is_mla and rope_interleave:
+        _deinterleave_rope(out, cfg)
     return out
 
 
@@ -98,5 +134,6 @@ def load_hf(path: str, weight_quant: str = "bf16", name: str | None = None) -> t
     """(config, canonical state dict) of a Hugging Face checkpoint directory."""
     from ..formats.safetensors import load_state_dict
     with open(os.path.join(path, "config.json")) as f:
-        cfg = config_from_hf(json.load(f), name or os.path.basename(os.path.normpath(path)), weight_quant)
-    return cfg, canonical_from_hf(load_state_dict(path))
+        d = json.load(f)
+    cfg = config_from_hf(d, name or os.path.basename(os.path.normpath(path)), weight_quant)
+    return cfg, canonical_from_hf(load_state_dict(path), cfg, bool(d.get("rope_interleave", True)))

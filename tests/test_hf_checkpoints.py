@@ -83,3 +83,32 @@ def test_cli_serves_a_checkpoint_directory(tmp_path):
                        env=dict(os.environ, PYTHONPATH=root), cwd=root)
     assert r.returncode == 0, r.stderr[-2000:]
     assert json.loads(r.stdout)["tokens"] == _hf_greedy(m.eval(), [5, 6, 7], 4)
+
+
+def test_deepseek_v3_matches_transformers(tmp_path):
+    """MLA, sigmoid group-limited routing with a selection bias, shared experts and a leading
+    dense layer, against transformers' DeepseekV3 forward."""
+    torch.manual_seed(2)
+    c = transformers.DeepseekV3Config(
+        vocab_size=512, hidden_size=128, intermediate_size=256, moe_intermediate_size=64, num_hidden_layers=3,
+        num_attention_heads=4, num_key_value_heads=4, n_routed_experts=8, num_experts_per_tok=2, n_shared_experts=1,
+        n_group=2, topk_group=1, first_k_dense_replace=1, q_lora_rank=64, kv_lora_rank=32, qk_rope_head_dim=16,
+        qk_nope_head_dim=32, v_head_dim=32, rope_scaling=None, max_position_embeddings=256, rms_norm_eps=1e-6)
+    m = transformers.DeepseekV3ForCausalLM(c).float().eval()
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if p.dim() > 1:
+                p.normal_(0, 0.08)
+        for mod in m.modules():  # a non-zero selection bias exercises it
+            if hasattr(mod, "e_score_correction_bias"):
+                mod.e_score_correction_bias.normal_(0, 0.05)
+    m.save_pretrained(str(tmp_path / "ds"))
+    cfg, sd = load_hf(str(tmp_path / "ds"), weight_quant="fp32")
+    assert cfg.is_mla and cfg.first_dense_layers == 1 and "layers.1.router_bias" in sd
+    prompt = [5, 17, 99, 250, 3, 42, 77]
+    want = _hf_greedy(m, prompt, 10)
+    from syntropy_b200.models import reference
+    assert reference.greedy_generate(torch.tensor(prompt), sd, cfg, 10) == want
+    mw = prepare_weights(cfg, "cpu", state_dict=sd, max_pos=64)
+    got = LLMEngine(ModelRunner(mw, max_batch=2, max_seq_len=48)).generate([prompt], SamplingParams(max_tokens=10))
+    assert got[0] == want
