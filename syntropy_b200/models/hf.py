@@ -7,10 +7,11 @@ LlamaForCausalLM and MistralForCausalLM (no projection bias, no sliding window),
 Qwen2ForCausalLM (bias on the Q, K and V projections), Qwen3ForCausalLM (QK-norm),
 Qwen3MoeForCausalLM (QK-norm, every layer MoE), DeepseekV3ForCausalLM (MLA, sigmoid
 group-limited routing with a selection bias, shared experts, leading dense layers; its rotary
-dimensions, stored interleaved, are reordered to the rotate-half layout used here).  Rotary scaling other than the
-plain one, a sliding window in effect, or an O-projection / MLP bias are rejected with a
-message instead of being served wrongly.  Experts may be stored per expert (the Hub layout:
-`mlp.experts.{e}.{gate,up,down}_proj.weight`) or fused (`mlp.experts.gate_up_proj`, `down_proj`).
+dimensions, stored interleaved, are reordered to the rotate-half layout used here).  Rotary
+scaling other than the plain one and Llama 3.1's "llama3" rule, a sliding window in effect,
+or an O-projection / MLP bias are rejected with a message instead of being served wrongly.
+Experts may be stored per expert (the Hub layout: `mlp.experts.{e}.{gate,up,down}_proj.weight`)
+or fused (`mlp.experts.gate_up_proj`, `down_proj`).
 """
 from __future__ import annotations
 
@@ -32,7 +33,11 @@ def config_from_hf(d: dict, name: str = "hf", weight_quant: str = "bf16") -> Mod
         raise ValueError(f"architecture {arch} is not supported (supported: {sorted(FAMILY)})")
     rope = d.get("rope_scaling") or d.get("rope_parameters") or {}
     rtype = rope.get("rope_type", rope.get("type", "default")) if isinstance(rope, dict) else "default"
-    if rtype not in (None, "default"):
+    scaling = ()
+    if rtype == "llama3" and arch != "DeepseekV3ForCausalLM":
+        scaling = ("llama3", float(rope["factor"]), float(rope.get("low_freq_factor", 1.0)),
+                   float(rope.get("high_freq_factor", 4.0)), float(rope["original_max_position_embeddings"]))
+    elif rtype not in (None, "default"):
         raise ValueError(f"rotary scaling {rtype!r} is not supported")
     theta = d.get("rope_theta") or (rope.get("rope_theta") if isinstance(rope, dict) else None) or 10000.0
     if d.get("use_sliding_window") or (arch == "MistralForCausalLM" and d.get("sliding_window")):
@@ -44,7 +49,8 @@ def config_from_hf(d: dict, name: str = "hf", weight_quant: str = "bf16") -> Mod
               n_kv_heads=d.get("num_key_value_heads") or nh, head_dim=d.get("head_dim") or H // nh,
               ffn=d.get("intermediate_size") or 0, vocab=d["vocab_size"], rms_eps=d.get("rms_norm_eps", 1e-6),
               rope_theta=float(theta), qk_norm=arch.startswith("Qwen3"), qkv_bias=arch == "Qwen2ForCausalLM",
-              tie_embeddings=bool(d.get("tie_word_embeddings", False)), weight_quant=weight_quant)
+              tie_embeddings=bool(d.get("tie_word_embeddings", False)), weight_quant=weight_quant,
+              rope_scaling=scaling)
     if arch == "DeepseekV3ForCausalLM":
         dn, dr, dv = d["qk_nope_head_dim"], d["qk_rope_head_dim"], d["v_head_dim"]
         kw.update(n_kv_heads=nh, head_dim=dn + dr, qk_norm=False, q_lora_rank=d.get("q_lora_rank") or 0,

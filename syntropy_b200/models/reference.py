@@ -22,22 +22,40 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 _ROPE_CACHE: dict = {}
 
 
-def rope_table(dim: int, theta: float, max_pos: int, device="cpu") -> tuple[torch.Tensor, torch.Tensor]:
+def rope_frequencies(dim: int, theta: float, scaling: tuple = ()) -> torch.Tensor:
+    """Inverse frequencies (f64).  With ("llama3", factor, low, high, original_max_positions),
+    the Llama 3.1 rule: wavelengths shorter than original/high keep their frequency, longer
+    than original/low are divided by `factor`, and the band between is interpolated linearly
+    in original/wavelength between the two."""
+    inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.float64) / dim))
+    if not scaling:
+        return inv
+    kind, factor, low, high, orig = scaling
+    if kind != "llama3":
+        raise ValueError(f"rotary scaling {kind!r} is not supported")
+    wavelen = 2 * math.pi / inv
+    smooth = ((orig / wavelen) - low) / (high - low)
+    scaled = torch.where(wavelen > orig / low, inv / factor, inv)
+    mid = (wavelen <= orig / low) & (wavelen >= orig / high)
+    return torch.where(mid, (1 - smooth) * inv / factor + smooth * inv, scaled)
+
+
+def rope_table(dim: int, theta: float, max_pos: int, device="cpu", scaling: tuple = ()) -> tuple[torch.Tensor, torch.Tensor]:
     """cos/sin [max_pos, dim/2] in f32, computed in f64 (exact table shared with the kernels)."""
-    key = (dim, theta, max_pos, str(device))
+    key = (dim, theta, max_pos, str(device), tuple(scaling))
     t = _ROPE_CACHE.get(key)
     if t is None:
-        inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.float64) / dim))
+        inv = rope_frequencies(dim, theta, scaling)
         ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
         t = (torch.cos(ang).float().to(device), torch.sin(ang).float().to(device))
         _ROPE_CACHE[key] = t
     return t
 
 
-def apply_rope(x: torch.Tensor, pos: torch.Tensor, theta: float) -> torch.Tensor:
+def apply_rope(x: torch.Tensor, pos: torch.Tensor, theta: float, scaling: tuple = ()) -> torch.Tensor:
     """Rotate-half RoPE on the last dim. x: [T, H, D], pos: [T]."""
     D = x.shape[-1]
-    cos, sin = rope_table(D, theta, int(pos.max().item()) + 1, x.device)
+    cos, sin = rope_table(D, theta, int(pos.max().item()) + 1, x.device, scaling)
     c = cos[pos][:, None, :]
     s = sin[pos][:, None, :]
     x1, x2 = x[..., : D // 2].float(), x[..., D // 2:].float()
@@ -133,8 +151,8 @@ def gqa_attention_block(h, W, cfg: ModelConfig, pre: str, pos: torch.Tensor, kv_
     if cfg.qk_norm:
         q = rms_norm(q, W[pre + "q_norm"], cfg.rms_eps)
         k = rms_norm(k, W[pre + "k_norm"], cfg.rms_eps)
-    q = apply_rope(q, pos, cfg.rope_theta)
-    k = apply_rope(k, pos, cfg.rope_theta)
+    q = apply_rope(q, pos, cfg.rope_theta, cfg.rope_scaling)
+    k = apply_rope(k, pos, cfg.rope_theta, cfg.rope_scaling)
     o = attention(q, k, v)
     return o.reshape(T, -1) @ W[pre + "o_proj"].float().t()
 

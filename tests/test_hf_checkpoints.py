@@ -112,3 +112,29 @@ def test_deepseek_v3_matches_transformers(tmp_path):
     mw = prepare_weights(cfg, "cpu", state_dict=sd, max_pos=64)
     got = LLMEngine(ModelRunner(mw, max_batch=2, max_seq_len=48)).generate([prompt], SamplingParams(max_tokens=10))
     assert got[0] == want
+
+
+def test_llama3_rotary_scaling_matches_transformers(tmp_path):
+    """Llama 3.1's rotary frequency rule (factor, low / high frequency bands) in the reference
+    and the engine, against transformers."""
+    torch.manual_seed(3)
+    rp = {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+          "original_max_position_embeddings": 16, "rope_theta": 10000.0}
+    c = transformers.LlamaConfig(intermediate_size=256, rope_parameters=rp, **COMMON)
+    m = transformers.LlamaForCausalLM(c).float().eval()
+    with torch.no_grad():
+        for p in m.parameters():
+            if p.dim() > 1:
+                p.normal_(0, 0.08)
+    m.save_pretrained(str(tmp_path / "l31"))
+    cfg, sd = load_hf(str(tmp_path / "l31"), weight_quant="fp32")
+    assert cfg.rope_scaling and cfg.rope_scaling[0] == "llama3"
+    prompt = list(range(3, 40))  # past the original 16 positions
+    want = _hf_greedy(m, prompt, 8)
+    mw = prepare_weights(cfg, "cpu", state_dict=sd, max_pos=64)
+    got = LLMEngine(ModelRunner(mw, max_batch=2, max_seq_len=60)).generate([prompt], SamplingParams(max_tokens=8))
+    assert got[0] == want
+    unscaled = cfg.replace(rope_scaling=())
+    mw0 = prepare_weights(unscaled, "cpu", state_dict=sd, max_pos=64)
+    plain = LLMEngine(ModelRunner(mw0, max_batch=2, max_seq_len=60)).generate([prompt], SamplingParams(max_tokens=8))
+    assert plain[0] != want  # the scaling matters for this model
