@@ -23,7 +23,8 @@ class ModelConfig:
     vocab: int
     rms_eps: float = 1e-5
     rope_theta: float = 10000.0
-    # ("llama3", factor, low_freq_factor, high_freq_factor, original_max_positions) or () for plain RoPE
+    # ("llama3", factor, low_freq_factor, high_freq_factor, original_max_positions),
+    # ("yarn", factor, original_max_positions, beta_fast, beta_slow, mscale, mscale_all_dim) or () (plain)
     rope_scaling: tuple = ()
     qk_norm: bool = False
     qkv_bias: bool = False  # bias on the Q, K and V projections (Qwen2)

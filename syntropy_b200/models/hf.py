@@ -8,8 +8,9 @@ Qwen2ForCausalLM (bias on the Q, K and V projections), Qwen3ForCausalLM (QK-norm
 Qwen3MoeForCausalLM (QK-norm, every layer MoE), DeepseekV3ForCausalLM (MLA, sigmoid
 group-limited routing with a selection bias, shared experts, leading dense layers; its rotary
 dimensions, stored interleaved, are reordered to the rotate-half layout used here).  Rotary
-scaling other than the plain one and Llama 3.1's "llama3" rule, a sliding window in effect,
-or an O-projection / MLP bias are rejected with a message instead of being served wrongly.
+scaling other than the plain one, Llama 3.1's "llama3" rule and DeepSeek-V3's YaRN, a sliding
+window in effect, or an O-projection / MLP bias are rejected with a message instead of being
+served wrongly.
 Experts may be stored per expert (the Hub layout: `mlp.experts.{e}.{gate,up,down}_proj.weight`)
 or fused (`mlp.experts.gate_up_proj`, `down_proj`).
 """
@@ -34,7 +35,12 @@ def config_from_hf(d: dict, name: str = "hf", weight_quant: str = "bf16") -> Mod
     rope = d.get("rope_scaling") or d.get("rope_parameters") or {}
     rtype = rope.get("rope_type", rope.get("type", "default")) if isinstance(rope, dict) else "default"
     scaling = ()
-    if rtype == "llama3" and arch != "DeepseekV3ForCausalLM":
+    if rtype == "yarn" and arch == "DeepseekV3ForCausalLM":
+        scaling = ("yarn", float(rope["factor"]),
+                   float(rope.get("original_max_position_embeddings") or d.get("max_position_embeddings")),
+                   float(rope.get("beta_fast", 32.0)), float(rope.get("beta_slow", 1.0)),
+                   float(rope.get("mscale", 1.0) or 0.0), float(rope.get("mscale_all_dim", 0.0) or 0.0))
+    elif rtype == "llama3" and arch != "DeepseekV3ForCausalLM":
         scaling = ("llama3", float(rope["factor"]), float(rope.get("low_freq_factor", 1.0)),
                    float(rope.get("high_freq_factor", 4.0)), float(rope["original_max_position_embeddings"]))
     elif rtype not in (None, "default"):

@@ -8,13 +8,12 @@ models/reference.py (mla_attention_block).
 """
 from __future__ import annotations
 
-import math
 
 import torch
 import torch.nn.functional as F
 
 from .. import ops
-from .reference import rope_table
+from .reference import mla_softmax_scale, rope_table
 
 
 def prepare_mla(cfg, get, pre, linear_weight):
@@ -74,7 +73,7 @@ def mla_qkv(cfg, m, h, pos, cos_t, sin_t):
 def mla_attend(cfg, m, q_lat, q_pe, lat, ctx_start: int, causal_from: int | None = None):
     """Attention of queries (rows at positions causal_from.. ) over latent rows lat [S, C+dr]."""
     C = cfg.kv_lora_rank
-    scale = 1.0 / math.sqrt(cfg.qk_nope_dim + cfg.qk_rope_dim)
+    scale = mla_softmax_scale(cfg)
     lat = lat.float()
     s = (torch.einsum("thc,sc->ths", q_lat, lat[:, :C]) + torch.einsum("thr,sr->ths", q_pe, lat[:, C:])) * scale
     if causal_from is not None:

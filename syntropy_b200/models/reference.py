@@ -30,6 +30,8 @@ def rope_frequencies(dim: int, theta: float, scaling: tuple = ()) -> torch.Tenso
     inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.float64) / dim))
     if not scaling:
         return inv
+    if scaling[0] == "yarn":
+        return _yarn_frequencies(dim, theta, *scaling[1:5])
     kind, factor, low, high, orig = scaling
     if kind != "llama3":
         raise ValueError(f"rotary scaling {kind!r} is not supported")
@@ -40,6 +42,47 @@ def rope_frequencies(dim: int, theta: float, scaling: tuple = ()) -> torch.Tenso
     return torch.where(mid, (1 - smooth) * inv / factor + smooth * inv, scaled)
 
 
+def _yarn_frequencies(dim, theta, factor, orig, beta_fast, beta_slow) -> torch.Tensor:
+    """YaRN (Peng et al. 2023): dimensions that rotate more than `beta_fast` times over the
+    original context keep their frequency, those that rotate fewer than `beta_slow` times are
+    interpolated by `factor`, with a linear ramp over the dimensions in between."""
+    base = theta ** (torch.arange(0, dim, 2, dtype=torch.float64) / dim)
+    keep, interp = 1.0 / base, 1.0 / (factor * base)
+
+    def dim_for(rotations):  # the dimension index that completes `rotations` turns in `orig` positions
+        return dim * math.log(orig / (rotations * 2 * math.pi)) / (2 * math.log(theta))
+    lo = max(math.floor(dim_for(beta_fast)), 0)
+    hi = min(math.ceil(dim_for(beta_slow)), dim - 1)
+    if lo == hi:
+        hi += 0.001
+    ramp = ((torch.arange(dim // 2, dtype=torch.float64) - lo) / (hi - lo)).clamp(0, 1)
+    return interp * ramp + keep * (1 - ramp)
+
+
+def yarn_mscale(factor: float, m: float = 1.0) -> float:
+    return 1.0 if factor <= 1 else 0.1 * m * math.log(factor) + 1.0
+
+
+def rope_magnitude(scaling: tuple = ()) -> float:
+    """Factor on cos/sin: YaRN's attention temperature (mscale / mscale_all_dim), else 1."""
+    if not scaling or scaling[0] != "yarn":
+        return 1.0
+    factor, mscale, mscale_all = scaling[1], scaling[5], scaling[6]
+    if mscale and mscale_all:
+        return yarn_mscale(factor, mscale) / yarn_mscale(factor, mscale_all)
+    return yarn_mscale(factor)
+
+
+def mla_softmax_scale(cfg: ModelConfig) -> float:
+    """1/sqrt(q-k head dim), times mscale(mscale_all_dim)^2 under YaRN (DeepSeek-V3)."""
+    s = 1.0 / math.sqrt(cfg.qk_nope_dim + cfg.qk_rope_dim)
+    sc = cfg.rope_scaling
+    if sc and sc[0] == "yarn" and sc[6]:
+        m = yarn_mscale(sc[1], sc[6])
+        s *= m * m
+    return s
+
+
 def rope_table(dim: int, theta: float, max_pos: int, device="cpu", scaling: tuple = ()) -> tuple[torch.Tensor, torch.Tensor]:
     """cos/sin [max_pos, dim/2] in f32, computed in f64 (exact table shared with the kernels)."""
     key = (dim, theta, max_pos, str(device), tuple(scaling))
@@ -47,7 +90,8 @@ def rope_table(dim: int, theta: float, max_pos: int, device="cpu", scaling: tupl
     if t is None:
         inv = rope_frequencies(dim, theta, scaling)
         ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
-        t = (torch.cos(ang).float().to(device), torch.sin(ang).float().to(device))
+        mag = rope_magnitude(scaling)
+        t = ((torch.cos(ang) * mag).float().to(device), (torch.sin(ang) * mag).float().to(device))
         _ROPE_CACHE[key] = t
     return t
 
@@ -173,11 +217,11 @@ def mla_attention_block(h, W, cfg: ModelConfig, pre: str, pos: torch.Tensor):
     c = rms_norm(c, W[pre + "kv_a_norm"], cfg.rms_eps)
     kv = (c @ W[pre + "kv_b"].float().t()).view(T, H, dn + dv)
     k_nope, v = kv[..., :dn], kv[..., dn:]
-    q_rope = apply_rope(q_rope, pos, cfg.rope_theta)
-    k_rope = apply_rope(k_rope.view(T, 1, dr), pos, cfg.rope_theta).expand(T, H, dr)
+    q_rope = apply_rope(q_rope, pos, cfg.rope_theta, cfg.rope_scaling)
+    k_rope = apply_rope(k_rope.view(T, 1, dr), pos, cfg.rope_theta, cfg.rope_scaling).expand(T, H, dr)
     qf = torch.cat([q_nope, q_rope], -1)
     kf = torch.cat([k_nope, k_rope], -1)
-    s = torch.einsum("qhd,khd->hqk", qf, kf) / math.sqrt(dn + dr)
+    s = torch.einsum("qhd,khd->hqk", qf, kf) * mla_softmax_scale(cfg)
     mask = torch.arange(T)[None, :] > torch.arange(T)[:, None]
     s = s.masked_fill(mask[None], float("-inf"))
     o = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v)

@@ -368,6 +368,6 @@ def prepare_weights(cfg: ModelConfig, device="cpu", seed: int = 0, quant: str | 
         base = state_dict if state_dict is not None else _LazyState(cfg, seed, gen_dev)
         mw.mtp = _prepare_mtp(cfg, get, quant, device, base, seed, expert_range)
     cos, sin = rope_table(cfg.qk_rope_dim if cfg.is_mla else cfg.head_dim, cfg.rope_theta, max_pos, device,
-                          () if cfg.is_mla else cfg.rope_scaling)
+                          cfg.rope_scaling)
     mw.rope_cos, mw.rope_sin = cos.contiguous(), sin.contiguous()
     return mw

@@ -180,7 +180,8 @@ class ModelRunner:
             ns = max(1, min(self.max_blocks, -(-296 // per_split)))
             self.mla_pages_per_split = -(-self.max_blocks // ns)
             ns = -(-self.max_blocks // self.mla_pages_per_split)
-            self.mla_scale = 1.0 / math.sqrt(cfg.qk_nope_dim + cfg.qk_rope_dim)
+            from ..models.reference import mla_softmax_scale
+            self.mla_scale = mla_softmax_scale(cfg)
             b["mla_olat"] = torch.zeros(B, cfg.n_heads, 512, dtype=torch.float32, device=dev)
             b["mla_po"] = torch.zeros(B * cfg.n_heads * ns * 512, dtype=torch.float32, device=dev)
             b["mla_pml"] = torch.zeros(B * cfg.n_heads * ns * 2, dtype=torch.float32, device=dev)

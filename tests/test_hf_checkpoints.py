@@ -138,3 +138,33 @@ def test_llama3_rotary_scaling_matches_transformers(tmp_path):
     mw0 = prepare_weights(unscaled, "cpu", state_dict=sd, max_pos=64)
     plain = LLMEngine(ModelRunner(mw0, max_batch=2, max_seq_len=60)).generate([prompt], SamplingParams(max_tokens=8))
     assert plain[0] != want  # the scaling matters for this model
+
+
+def test_deepseek_v3_yarn_matches_transformers(tmp_path):
+    """YaRN rotary scaling (frequencies, cos/sin magnitude, MLA softmax temperature) against
+    transformers' DeepseekV3."""
+    torch.manual_seed(4)
+    rp = {"rope_type": "yarn", "factor": 4.0, "original_max_position_embeddings": 64, "beta_fast": 32.0,
+          "beta_slow": 1.0, "mscale": 1.0, "mscale_all_dim": 1.0, "rope_theta": 10000.0}
+    c = transformers.DeepseekV3Config(
+        vocab_size=512, hidden_size=128, intermediate_size=256, moe_intermediate_size=64, num_hidden_layers=2,
+        num_attention_heads=4, num_key_value_heads=4, n_routed_experts=8, num_experts_per_tok=2, n_shared_experts=1,
+        n_group=2, topk_group=1, first_k_dense_replace=1, q_lora_rank=64, kv_lora_rank=32, qk_rope_head_dim=16,
+        qk_nope_head_dim=32, v_head_dim=32, rope_parameters=rp, max_position_embeddings=256, rms_norm_eps=1e-6)
+    m = transformers.DeepseekV3ForCausalLM(c).float().eval()
+    with torch.no_grad():
+        for p in m.parameters():
+            if p.dim() > 1:
+                p.normal_(0, 0.08)
+    m.save_pretrained(str(tmp_path / "dsy"))
+    cfg, sd = load_hf(str(tmp_path / "dsy"), weight_quant="fp32")
+    assert cfg.rope_scaling[0] == "yarn"
+    prompt = list(range(3, 30))
+    want = _hf_greedy(m, prompt, 8)
+    from syntropy_b200.models import reference
+    assert reference.greedy_generate(torch.tensor(prompt), sd, cfg, 8) == want
+    mw = prepare_weights(cfg, "cpu", state_dict=sd, max_pos=64)
+    got = LLMEngine(ModelRunner(mw, max_batch=2, max_seq_len=48)).generate([prompt], SamplingParams(max_tokens=8))
+    assert got[0] == want
+    # the scaling matters for this model (frequencies and the softmax temperature)
+    assert reference.greedy_generate(torch.tensor(prompt), sd, cfg.replace(rope_scaling=()), 8) != want
