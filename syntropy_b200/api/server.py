@@ -19,13 +19,20 @@ except ImportError:  # pragma: no cover
     Request = None
 
 
+def _chat(tokenizer):
+    """The tokenizer's own chat template when it has one (checkpoint directories), else ChatML."""
+    return getattr(tokenizer, "apply_chat_template", apply_chat_template)
+
+
 def _err(status: int, typ: str, msg: str):
     from fastapi.responses import JSONResponse
     return JSONResponse(status_code=status, content={"error": {"type": typ, "message": msg}})
 
 
-def _params(body: dict, default_max: int = 16) -> SamplingParams:
-    stop = body.get("stop_token_ids") or ()
+def _params(body: dict, default_max: int = 16, stop_ids: tuple = ()) -> SamplingParams:
+    """OpenAI / Anthropic request fields -> SamplingParams; generation stops at the tokenizer's
+    stop ids (end of sequence / end of turn) unless the request sets `ignore_eos`."""
+    stop = tuple(body.get("stop_token_ids") or ()) + (() if body.get("ignore_eos") else tuple(stop_ids))
     return SamplingParams(max_tokens=int(body.get("max_tokens", body.get("max_completion_tokens", default_max))),
                           temperature=float(body.get("temperature", 1.0 if "temperature" not in body else
                                                      body["temperature"])),
@@ -110,7 +117,7 @@ def build_app(aeng, tokenizer, model_id: str = "syntropy", bench_api: bool = Tru
         if ids is None:
             text = body.get("prompt")
             if text is None and body.get("messages"):
-                text = apply_chat_template(body["messages"])
+                text = _chat(tokenizer)(body["messages"])
             if text is None:
                 return _err(400, "invalid_request", "one of tokens, prompt or messages is required")
             ids = tokenizer.encode(text)
@@ -154,7 +161,7 @@ def build_app(aeng, tokenizer, model_id: str = "syntropy", bench_api: bool = Tru
             msgs = body.get("messages")
             if not isinstance(msgs, list) or not msgs:
                 return _err(400, "invalid_request", "messages must be a non-empty list")
-            ids = tokenizer.encode(apply_chat_template(msgs))
+            ids = tokenizer.encode(_chat(tokenizer)(msgs))
         else:
             p = body.get("prompt")
             if isinstance(p, list) and p and isinstance(p[0], int):
@@ -166,7 +173,7 @@ def build_app(aeng, tokenizer, model_id: str = "syntropy", bench_api: bool = Tru
         e = _check_ids(ids, "prompt")
         if e:
             return e
-        params = _params(body)
+        params = _params(body, stop_ids=tuple(getattr(tokenizer, "stop_token_ids", ()) or ()))
         rid = ("chatcmpl-" if chat else "cmpl-") + uuid.uuid4().hex[:24]
         created = int(time.time())
         obj = "chat.completion" if chat else "text_completion"
@@ -227,8 +234,8 @@ def build_app(aeng, tokenizer, model_id: str = "syntropy", bench_api: bool = Tru
         sysm = body.get("system")
         if isinstance(sysm, list):
             sysm = "".join(b.get("text", "") for b in sysm)
-        ids = tokenizer.encode(apply_chat_template(msgs, system=sysm))
-        params = _params(body)
+        ids = tokenizer.encode(_chat(tokenizer)(msgs, system=sysm))
+        params = _params(body, stop_ids=tuple(getattr(tokenizer, "stop_token_ids", ()) or ()))
         mid = "msg_" + uuid.uuid4().hex[:24]
         stop_map = {"length": "max_tokens", "stop": "end_turn", "cancelled": "end_turn"}
         if body.get("stream"):

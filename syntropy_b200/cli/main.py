@@ -97,10 +97,11 @@ def cmd_run(args, cfg):
     tok = load_tokenizer(cfg.model.path or None, mcfg.vocab)
     ids = [int(x) for x in args.tokens.split(",")] if args.tokens else tok.encode(args.prompt)
     eng.set_tokenizer(tok)
+    stop = tuple(getattr(tok, "stop_token_ids", ()) or ())  # a checkpoint's end-of-sequence / end-of-turn ids
     constraint = {"type": "json"} if getattr(args, "json", False) else (
         {"choices": args.choices.split("|")} if getattr(args, "choices", None) else None)
     out = eng.generate([ids], SamplingParams(max_tokens=args.max_tokens, temperature=args.temperature,
-                                             seed=args.seed, constraint=constraint))[0]
+                                             seed=args.seed, constraint=constraint, stop_token_ids=stop))[0]
     print(json.dumps({"tokens": out, "text": tok.decode(out)}))
 
 

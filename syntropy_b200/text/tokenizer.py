@@ -44,23 +44,79 @@ class IncrementalDecoder:
 
 
 class HFTokenizer:
+    """`tokenizer.json` through the `tokenizers` library, plus what a checkpoint directory says
+    about it: the chat template (Jinja, `tokenizer_config.json`), BOS/EOS tokens and the stop
+    ids of `generation_config.json` (a list: chat models stop on end-of-turn too)."""
+
     def __init__(self, path: str):
         from tokenizers import Tokenizer
         self.tk = Tokenizer.from_file(path)
         self.vocab_size = self.tk.get_vocab_size()
-        self.eos_token_id = None
-        self.bos_token_id = None
-        for name in ("<|endoftext|>", "</s>", "<|im_end|>", "<｜end▁of▁sentence｜>"):
-            i = self.tk.token_to_id(name)
-            if i is not None:
-                self.eos_token_id = i
-                break
+        d = os.path.dirname(path)
+        conf = _read_json(os.path.join(d, "tokenizer_config.json"))
+        gen = _read_json(os.path.join(d, "generation_config.json"))
+        self.chat_template = conf.get("chat_template")
+        if isinstance(self.chat_template, list):  # named templates: take the default one
+            self.chat_template = next((t["template"] for t in self.chat_template if t.get("name") == "default"),
+                                      self.chat_template[0]["template"])
+        self.bos_token = _tok_str(conf.get("bos_token"))
+        self.eos_token = _tok_str(conf.get("eos_token"))
+        self.bos_token_id = self.tk.token_to_id(self.bos_token) if self.bos_token else None
+        stop = gen.get("eos_token_id")
+        stop = stop if isinstance(stop, list) else ([stop] if stop is not None else [])
+        if self.eos_token and self.tk.token_to_id(self.eos_token) is not None:
+            stop = [self.tk.token_to_id(self.eos_token)] + [i for i in stop if i != self.tk.token_to_id(self.eos_token)]
+        if not stop:
+            for name in ("<|endoftext|>", "</s>", "<|im_end|>", "<｜end▁of▁sentence｜>"):
+                i = self.tk.token_to_id(name)
+                if i is not None:
+                    stop = [i]
+                    break
+        self.stop_token_ids = stop
+        self.eos_token_id = stop[0] if stop else None
 
     def encode(self, text: str, add_bos: bool = False) -> list[int]:
         return self.tk.encode(text, add_special_tokens=add_bos).ids
 
     def decode(self, ids) -> str:
         return self.tk.decode(list(ids))
+
+    def apply_chat_template(self, messages: list[dict], system: str | None = None,
+                            add_generation_prompt: bool = True) -> str:
+        """The checkpoint's own template (sandboxed Jinja), else ChatML."""
+        from .chat import apply_chat_template as chatml
+        if not self.chat_template:
+            return chatml(messages, system, add_generation_prompt)
+        msgs = ([{"role": "system", "content": system}] if system else []) + [
+            dict(m, content=_text(m.get("content", ""))) for m in messages]
+        from jinja2.sandbox import ImmutableSandboxedEnvironment
+        env = ImmutableSandboxedEnvironment(trim_blocks=True, lstrip_blocks=True)
+
+        def raise_exception(msg):
+            raise ValueError(msg)
+        env.globals["raise_exception"] = raise_exception
+        return env.from_string(self.chat_template).render(
+            messages=msgs, add_generation_prompt=add_generation_prompt, bos_token=self.bos_token or "",
+            eos_token=self.eos_token or "")
+
+
+def _read_json(p: str) -> dict:
+    import json
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def _tok_str(v):
+    return v.get("content") if isinstance(v, dict) else v
+
+
+def _text(content) -> str:
+    if isinstance(content, list):  # OpenAI / Anthropic content blocks
+        return "".join(b.get("text", "") for b in content if isinstance(b, dict))
+    return content
 
 
 def load_tokenizer(model_dir: str | None, vocab_size: int):

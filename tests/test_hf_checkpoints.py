@@ -168,3 +168,34 @@ def test_deepseek_v3_yarn_matches_transformers(tmp_path):
     assert got[0] == want
     # the scaling matters for this model (frequencies and the softmax temperature)
     assert reference.greedy_generate(torch.tensor(prompt), sd, cfg.replace(rope_scaling=()), 8) != want
+
+
+def test_tokenizer_files_chat_template_and_stops(tmp_path):
+    """A checkpoint's tokenizer files: its Jinja chat template renders like transformers'
+    AutoTokenizer, and its end-of-turn ids become stop ids."""
+    tokenizers = pytest.importorskip("tokenizers")
+    from tokenizers import Tokenizer, models, pre_tokenizers, trainers
+    from syntropy_b200.text.tokenizer import load_tokenizer
+    tk = Tokenizer(models.BPE(unk_token="<unk>"))
+    tk.pre_tokenizer = pre_tokenizers.ByteLevel()
+    specials = ["<unk>", "<|begin_of_text|>", "<|eot_id|>", "<|end_of_text|>", "<|start_header_id|>",
+                "<|end_header_id|>"]
+    tk.train_from_iterator(["hello world, the quick brown fox jumps over the lazy dog"] * 20,
+                           trainers.BpeTrainer(vocab_size=300, special_tokens=specials))
+    d = tmp_path / "tok"
+    d.mkdir()
+    tk.save(str(d / "tokenizer.json"))
+    template = ("{{ bos_token }}{% for m in messages %}<|start_header_id|>{{ m['role'] }}<|end_header_id|>\n\n"
+                "{{ m['content'] | trim }}<|eot_id|>{% endfor %}"
+                "{% if add_generation_prompt %}<|start_header_id|>assistant<|end_header_id|>\n\n{% endif %}")
+    import json
+    (d / "tokenizer_config.json").write_text(json.dumps({"chat_template": template, "bos_token": "<|begin_of_text|>",
+                                                         "eos_token": "<|eot_id|>"}))
+    (d / "generation_config.json").write_text(json.dumps({"eos_token_id": [tk.token_to_id("<|end_of_text|>"),
+                                                                           tk.token_to_id("<|eot_id|>")]}))
+    ours = load_tokenizer(str(d), 300)
+    msgs = [{"role": "system", "content": "be brief"}, {"role": "user", "content": " hello "}]
+    auto = transformers.AutoTokenizer.from_pretrained(str(d))
+    assert ours.apply_chat_template(msgs) == auto.apply_chat_template(msgs, tokenize=False, add_generation_prompt=True)
+    assert ours.eos_token_id == tk.token_to_id("<|eot_id|>")
+    assert set(ours.stop_token_ids) == {tk.token_to_id("<|eot_id|>"), tk.token_to_id("<|end_of_text|>")}
