@@ -16,7 +16,10 @@ def _engine_from_config(cfg, device: str):
     from ..runtime.runner import ModelRunner
     dev = torch.device(device)
     sd = None
-    if cfg.model.path and os.path.exists(os.path.join(cfg.model.path, "config.json")):
+    if cfg.model.path and cfg.model.path.endswith(".gguf"):
+        from ..models.hf import load_gguf  # a llama.cpp GGUF file (blocks dequantised, then requantised)
+        mcfg, sd = load_gguf(cfg.model.path, weight_quant=cfg.model.quant or ("bf16" if dev.type == "cuda" else "fp32"))
+    elif cfg.model.path and os.path.exists(os.path.join(cfg.model.path, "config.json")):
         from ..models.hf import load_hf  # a Hugging Face checkpoint directory
         mcfg, sd = load_hf(cfg.model.path, weight_quant=cfg.model.quant or ("bf16" if dev.type == "cuda" else "fp32"))
     else:

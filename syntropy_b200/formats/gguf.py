@@ -1,5 +1,6 @@
-"""GGUF reading (native header parser): metadata, tensor infos, and Q4_1 / F16 / F32 / BF16
-tensor data.  Q4_1 blocks map 1:1 onto this framework's 4-bit interchange layout.
+"""GGUF reading (native header parser): metadata, tensor infos, and tensor data in F32 / F16 /
+BF16 and the Q8_0 / Q4_0 / Q4_1 / Q4_K / Q6_K block formats (dequantised to f32).  Q4_1 blocks
+map 1:1 onto this framework's 4-bit interchange layout.
 Reference: crates/manifest/src/gguf.rs:75-335."""
 from __future__ import annotations
 
@@ -10,9 +11,10 @@ import torch
 
 from .._ext import ext
 
+from .ggml_blocks import BLOCKS, DEQUANT, GGML_TYPE
+
 GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q4_1, GGML_Q8_0, GGML_BF16 = 0, 1, 2, 3, 8, 30
-_BLOCK = {GGML_F32: (1, 4), GGML_F16: (1, 2), GGML_Q4_0: (32, 18), GGML_Q4_1: (32, 20), GGML_Q8_0: (32, 34),
-          GGML_BF16: (1, 2)}
+_BLOCK = {t: BLOCKS[n] for t, n in GGML_TYPE.items()}
 
 
 class GGUFFile:
@@ -50,6 +52,8 @@ class GGUFFile:
             from .q4 import dequant_rows_ref
             N = int(np.prod(shape[:-1]))
             return dequant_rows_ref(r, N, shape[-1]).reshape(shape)
+        if GGML_TYPE.get(t) in DEQUANT:
+            return DEQUANT[GGML_TYPE[t]](r).reshape(shape)
         raise NotImplementedError(f"GGML type {t} for {name}")
 
     def close(self):

@@ -149,3 +149,73 @@ def load_hf(path: str, weight_quant: str = "bf16", name: str | None = None) -> t
         d = json.load(f)
     cfg = config_from_hf(d, name or os.path.basename(os.path.normpath(path)), weight_quant)
     return cfg, canonical_from_hf(load_state_dict(path), cfg, bool(d.get("rope_interleave", True)))
+
+
+# ---------------------------------------------------------------------- GGUF checkpoints
+_GGUF_ARCH = {"llama": "LlamaForCausalLM", "qwen2": "Qwen2ForCausalLM", "qwen3": "Qwen3ForCausalLM",
+              "qwen3moe": "Qwen3MoeForCausalLM"}
+_GGUF_LAYER = {"attn_norm": "attn_norm", "ffn_norm": "ffn_norm", "attn_q": "q_proj", "attn_k": "k_proj",
+               "attn_v": "v_proj", "attn_output": "o_proj", "attn_q_norm": "q_norm", "attn_k_norm": "k_norm",
+               "ffn_gate": "gate", "ffn_up": "up", "ffn_down": "down", "ffn_gate_inp": "router",
+               "ffn_gate_exps": "experts.gate", "ffn_up_exps": "experts.up", "ffn_down_exps": "experts.down"}
+
+
+def _rows_to_rotate_half(w: torch.Tensor, n_heads: int) -> torch.Tensor:
+    """llama.cpp stores the Q / K rows of `llama` models with rotary pairs interleaved; per head
+    put the even rows first, then the odd ones (the rotate-half order used here)."""
+    rows = w.shape[0]
+    hd = rows // n_heads
+    perm = torch.cat([torch.arange(0, hd, 2), torch.arange(1, hd, 2)])
+    return w.reshape(n_heads, hd, *w.shape[1:])[:, perm].reshape(w.shape).contiguous()
+
+
+def load_gguf(path: str, weight_quant: str = "bf16", name: str | None = None) -> tuple[ModelConfig, dict]:
+    """(config, canonical state dict) of a GGUF file (llama / qwen2 / qwen3 / qwen3moe; the
+    quantised blocks are dequantised, then requantised by `prepare_weights` as configured)."""
+    from ..formats.gguf import GGUFFile
+    f = GGUFFile(path)
+    try:
+        m = f.meta
+        arch = m["general.architecture"]
+        if arch not in _GGUF_ARCH:
+            raise ValueError(f"GGUF architecture {arch!r} is not supported (supported: {sorted(_GGUF_ARCH)})")
+        if "rope_freqs.weight" in f.tensors or m.get(f"{arch}.rope.scaling.type", "none") not in ("none", None):
+            raise ValueError("rotary scaling in a GGUF file is not supported")
+        k = lambda key, default=None: m.get(f"{arch}.{key}", default)  # noqa: E731
+        emb_dims = f.tensors["token_embd.weight"][1]
+        d = {"architectures": [_GGUF_ARCH[arch]], "hidden_size": int(k("embedding_length")),
+             "num_hidden_layers": int(k("block_count")), "num_attention_heads": int(k("attention.head_count")),
+             "num_key_value_heads": int(k("attention.head_count_kv", k("attention.head_count"))),
+             "intermediate_size": int(k("feed_forward_length", 0) or 0), "vocab_size": int(emb_dims[1]),
+             "rms_norm_eps": float(k("attention.layer_norm_rms_epsilon", 1e-6)),
+             "rope_theta": float(k("rope.freq_base", 10000.0)),
+             "tie_word_embeddings": "output.weight" not in f.tensors}
+        if k("attention.key_length"):
+            d["head_dim"] = int(k("attention.key_length"))
+        if arch == "qwen3moe":
+            d.update(num_experts=int(k("expert_count")), num_experts_per_tok=int(k("expert_used_count")),
+                     moe_intermediate_size=int(k("expert_feed_forward_length")), norm_topk_prob=True)
+        cfg = config_from_hf(d, name or os.path.splitext(os.path.basename(path))[0], weight_quant)
+        sd = {}
+        for n in f.tensors:
+            t = f.get(n)
+            if n == "token_embd.weight":
+                sd["embed"] = t
+            elif n == "output_norm.weight":
+                sd["final_norm"] = t
+            elif n == "output.weight":
+                sd["lm_head"] = t
+            else:
+                mm = re.fullmatch(r"blk\.(\d+)\.(\w+)\.(weight|bias)", n)
+                if not mm or mm.group(2) not in _GGUF_LAYER:
+                    raise KeyError(f"unmapped GGUF tensor {n}")
+                i, part, kind = mm.groups()
+                leaf = _GGUF_LAYER[part]
+                if kind == "bias":
+                    leaf = {"q_proj": "q_bias", "k_proj": "k_bias", "v_proj": "v_bias"}[leaf]
+                elif arch == "llama" and leaf in ("q_proj", "k_proj"):
+                    t = _rows_to_rotate_half(t, cfg.n_heads if leaf == "q_proj" else cfg.n_kv_heads)
+                sd[f"layers.{i}.{leaf}"] = t
+        return cfg, sd
+    finally:
+        f.close()

@@ -199,3 +199,115 @@ def test_tokenizer_files_chat_template_and_stops(tmp_path):
     assert ours.apply_chat_template(msgs) == auto.apply_chat_template(msgs, tokenize=False, add_generation_prompt=True)
     assert ours.eos_token_id == tk.token_to_id("<|eot_id|>")
     assert set(ours.stop_token_ids) == {tk.token_to_id("<|eot_id|>"), tk.token_to_id("<|end_of_text|>")}
+
+
+def _gguf_from_hf(model, arch, path, quant=None):
+    """A GGUF file in llama.cpp's naming from a transformers model (Q/K rotary rows interleaved
+    for `llama`, as llama.cpp's converter stores them)."""
+    import numpy as np
+    from gguf import GGMLQuantizationType as T
+    from gguf import GGUFWriter, quants
+    c = model.config
+    w = GGUFWriter(str(path), arch)
+    w.add_block_count(c.num_hidden_layers)
+    w.add_embedding_length(c.hidden_size)
+    w.add_feed_forward_length(c.intermediate_size)
+    w.add_head_count(c.num_attention_heads)
+    w.add_head_count_kv(c.num_key_value_heads)
+    w.add_layer_norm_rms_eps(c.rms_norm_eps)
+    w.add_rope_freq_base(10000.0)
+    hd = getattr(c, "head_dim", None) or c.hidden_size // c.num_attention_heads
+    if arch.startswith("qwen3"):
+        w.add_key_length(hd)
+        w.add_value_length(hd)
+    if arch == "qwen3moe":
+        w.add_expert_count(c.num_experts if hasattr(c, "num_experts") else c.num_local_experts)
+        w.add_expert_used_count(c.num_experts_per_tok)
+        w.add_expert_feed_forward_length(c.moe_intermediate_size)
+    names = {"input_layernorm.weight": "attn_norm", "post_attention_layernorm.weight": "ffn_norm",
+             "self_attn.q_proj.weight": "attn_q", "self_attn.k_proj.weight": "attn_k",
+             "self_attn.v_proj.weight": "attn_v", "self_attn.o_proj.weight": "attn_output",
+             "self_attn.q_norm.weight": "attn_q_norm", "self_attn.k_norm.weight": "attn_k_norm",
+             "mlp.gate_proj.weight": "ffn_gate", "mlp.up_proj.weight": "ffn_up", "mlp.down_proj.weight": "ffn_down",
+             "mlp.gate.weight": "ffn_gate_inp"}
+    sd = {k: v.detach().float() for k, v in model.state_dict().items()}
+    out, experts = {}, {}
+    for n, t in sd.items():
+        if n == "model.embed_tokens.weight":
+            out["token_embd.weight"] = t
+        elif n == "model.norm.weight":
+            out["output_norm.weight"] = t
+        elif n == "lm_head.weight":
+            out["output.weight"] = t
+        else:
+            i, rest = n.split(".", 3)[2], n.split(".", 3)[3]
+            if rest == "mlp.experts.gate_up_proj":  # in memory the library fuses experts: [E, 2f, h]
+                f = t.shape[1] // 2
+                out[f"blk.{i}.ffn_gate_exps.weight"], out[f"blk.{i}.ffn_up_exps.weight"] = t[:, :f], t[:, f:]
+                continue
+            if rest == "mlp.experts.down_proj":
+                out[f"blk.{i}.ffn_down_exps.weight"] = t
+                continue
+            if rest.startswith("mlp.experts."):
+                _, _, e, kind, _ = rest.split(".")
+                experts.setdefault((i, kind), {})[int(e)] = t
+                continue
+            if rest in ("self_attn.q_proj.weight", "self_attn.k_proj.weight") and arch == "llama":
+                heads = c.num_attention_heads if "q_proj" in rest else c.num_key_value_heads
+                r = t.reshape(heads, 2, hd // 2, -1).transpose(1, 2)  # rotate-half -> interleaved pairs
+                t = r.reshape(t.shape)
+            out[f"blk.{i}.{names[rest]}.weight"] = t
+    for (i, kind), dd in experts.items():
+        out[f"blk.{i}.ffn_{kind.replace('_proj', '')}_exps.weight"] = torch.stack([dd[e] for e in sorted(dd)])
+    for n, t in out.items():
+        a = t.numpy().astype(np.float32)
+        if quant is not None and a.ndim == 2 and n != "token_embd.weight":
+            w.add_tensor(n, quants.quantize(a, quant), raw_dtype=quant)
+        else:
+            w.add_tensor(n, a)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+
+
+def test_gguf_checkpoints_match_transformers(tmp_path):
+    from syntropy_b200.models.hf import load_gguf
+    torch.manual_seed(5)
+    cases = [("llama", transformers.LlamaForCausalLM(transformers.LlamaConfig(intermediate_size=256, **COMMON))),
+             ("qwen3moe", transformers.Qwen3MoeForCausalLM(transformers.Qwen3MoeConfig(
+                 intermediate_size=256, moe_intermediate_size=64, head_dim=32, num_experts=8, num_experts_per_tok=2,
+                 norm_topk_prob=True, **COMMON)))]
+    prompt = [5, 17, 99, 250, 3, 42, 77]
+    for arch, m in cases:
+        m = m.float().eval()
+        with torch.no_grad():
+            for p in m.parameters():
+                if p.dim() > 1:
+                    p.normal_(0, 0.08)
+        path = tmp_path / f"{arch}.gguf"
+        _gguf_from_hf(m, arch, path)
+        cfg, sd = load_gguf(str(path), weight_quant="fp32")
+        assert cfg.is_moe == (arch == "qwen3moe")
+        mw = prepare_weights(cfg, "cpu", state_dict=sd, max_pos=64)
+        got = LLMEngine(ModelRunner(mw, max_batch=2, max_seq_len=48)).generate([prompt], SamplingParams(max_tokens=10))
+        assert got[0] == _hf_greedy(m, prompt, 10), arch
+
+
+def test_gguf_q8_0_blocks_load(tmp_path):
+    """Q8_0-quantised matrices load (dequantised exactly as the gguf package does) and the engine
+    serves them like the f32 oracle on the same dequantised weights."""
+    from gguf import GGMLQuantizationType as T
+    from syntropy_b200.models import reference
+    from syntropy_b200.models.hf import load_gguf
+    torch.manual_seed(6)
+    m = transformers.LlamaForCausalLM(transformers.LlamaConfig(intermediate_size=256, **COMMON)).float().eval()
+    _gguf_from_hf(m, "llama", tmp_path / "q8.gguf", quant=T.Q8_0)
+    cfg, sd = load_gguf(str(tmp_path / "q8.gguf"), weight_quant="fp32")
+    prompt = [5, 17, 99, 250, 3, 42, 77]
+    want = reference.greedy_generate(torch.tensor(prompt), sd, cfg, 8)
+    mw = prepare_weights(cfg, "cpu", state_dict=sd, max_pos=64)
+    got = LLMEngine(ModelRunner(mw, max_batch=2, max_seq_len=48)).generate([prompt], SamplingParams(max_tokens=8))
+    assert got[0] == want
+    w0 = m.model.layers[0].mlp.down_proj.weight.detach()
+    assert torch.allclose(sd["layers.0.down"], w0, atol=float(w0.abs().max()) / 100)  # 8-bit blocks
