@@ -24,6 +24,14 @@ def _chat(tokenizer):
     return getattr(tokenizer, "apply_chat_template", apply_chat_template)
 
 
+def _chat_ids(tokenizer, msgs, system=None) -> list[int]:
+    """Chat prompt ids; with span-aware encoding where the tokenizer has it (message content
+    cannot inject special tokens)."""
+    if hasattr(tokenizer, "encode_chat"):
+        return tokenizer.encode_chat(msgs, system)
+    return tokenizer.encode(_chat(tokenizer)(msgs, system=system) if system else _chat(tokenizer)(msgs))
+
+
 def _err(status: int, typ: str, msg: str):
     from fastapi.responses import JSONResponse
     return JSONResponse(status_code=status, content={"error": {"type": typ, "message": msg}})
@@ -114,10 +122,10 @@ def build_app(aeng, tokenizer, model_id: str = "syntropy", bench_api: bool = Tru
         if unknown:
             return _err(400, "invalid_request", f"unknown fields {sorted(unknown)}")
         ids = body.get("tokens")
+        if ids is None and body.get("prompt") is None and body.get("messages"):
+            ids = _chat_ids(tokenizer, body["messages"])
         if ids is None:
             text = body.get("prompt")
-            if text is None and body.get("messages"):
-                text = _chat(tokenizer)(body["messages"])
             if text is None:
                 return _err(400, "invalid_request", "one of tokens, prompt or messages is required")
             ids = tokenizer.encode(text)
@@ -161,7 +169,7 @@ def build_app(aeng, tokenizer, model_id: str = "syntropy", bench_api: bool = Tru
             msgs = body.get("messages")
             if not isinstance(msgs, list) or not msgs:
                 return _err(400, "invalid_request", "messages must be a non-empty list")
-            ids = tokenizer.encode(_chat(tokenizer)(msgs))
+            ids = _chat_ids(tokenizer, msgs)
         else:
             p = body.get("prompt")
             if isinstance(p, list) and p and isinstance(p[0], int):
@@ -234,7 +242,7 @@ def build_app(aeng, tokenizer, model_id: str = "syntropy", bench_api: bool = Tru
         sysm = body.get("system")
         if isinstance(sysm, list):
             sysm = "".join(b.get("text", "") for b in sysm)
-        ids = tokenizer.encode(_chat(tokenizer)(msgs, system=sysm))
+        ids = _chat_ids(tokenizer, msgs, system=sysm)
         params = _params(body, stop_ids=tuple(getattr(tokenizer, "stop_token_ids", ()) or ()))
         mid = "msg_" + uuid.uuid4().hex[:24]
         stop_map = {"length": "max_tokens", "stop": "end_turn", "cancelled": "end_turn"}

@@ -5,6 +5,7 @@ larger ids (present in big vocabularies) decode to nothing."""
 from __future__ import annotations
 
 import os
+import re
 
 
 class ByteTokenizer:
@@ -80,6 +81,42 @@ class HFTokenizer:
 
     def decode(self, ids) -> str:
         return self.tk.decode(list(ids))
+
+    def encode_literal(self, text: str) -> list[int]:
+        """Text as plain text: special-token strings inside it stay text."""
+        self.tk.encode_special_tokens = True
+        try:
+            return self.tk.encode(text, add_special_tokens=False).ids
+        finally:
+            self.tk.encode_special_tokens = False
+
+    def encode_chat(self, messages: list[dict], system: str | None = None,
+                    add_generation_prompt: bool = True) -> list[int]:
+        """Token ids of a chat with span-aware encoding (the injection guard of reference
+        crates/text/src/tokenizer/spans.rs): the template's own text may produce special
+        tokens, message content is encoded literally, so a user who types "<|im_end|>" gets
+        those characters, not the end-of-turn token.  Spans are encoded one by one, which
+        gives the ids of the whole rendered prompt for tokenizers whose pre-tokenizer splits
+        at those boundaries anyway and adds no prefix space (Llama 3, Qwen)."""
+        marks = [f"\x00\x01span{i}\x01\x00" for i in range(len(messages) + 1)]
+        sys_mark = marks[-1] if system else None
+        masked = [dict(m, content=marks[i]) for i, m in enumerate(messages)]
+        text = self.apply_chat_template(masked, sys_mark, add_generation_prompt)
+        trim = bool(self.chat_template) and "trim" in self.chat_template  # the template strips content
+        spans = {marks[i]: (_text(m.get("content", "")).strip() if trim else _text(m.get("content", "")))
+                 for i, m in enumerate(messages)}
+        if system:
+            spans[sys_mark] = system
+        ids, pos = [], 0
+        pattern = re.compile("|".join(re.escape(k) for k in spans))
+        for mt in pattern.finditer(text):
+            if mt.start() > pos:
+                ids += self.tk.encode(text[pos:mt.start()], add_special_tokens=False).ids
+            ids += self.encode_literal(spans[mt.group(0)])
+            pos = mt.end()
+        if pos < len(text):
+            ids += self.tk.encode(text[pos:], add_special_tokens=False).ids
+        return ids
 
     def apply_chat_template(self, messages: list[dict], system: str | None = None,
                             add_generation_prompt: bool = True) -> str:
