@@ -320,3 +320,66 @@ def test_gguf_q8_0_blocks_load(tmp_path):
     assert got[0] == want
     w0 = m.model.layers[0].mlp.down_proj.weight.detach()
     assert torch.allclose(sd["layers.0.down"], w0, atol=float(w0.abs().max()) / 100)  # 8-bit blocks
+
+
+def test_serving_a_checkpoint_directory(tmp_path):
+    """model + tokenizer files in one directory -> config-built engine -> HTTP chat completion:
+    the prompt is the checkpoint's template (span-encoded), generation stops at its end-of-turn
+    id, and the reply equals transformers' greedy continuation of the same prompt ids."""
+    pytest.importorskip("fastapi")
+    import json
+    from fastapi.testclient import TestClient
+    from tokenizers import Tokenizer, models, pre_tokenizers, trainers, decoders
+    from syntropy_b200.api import build_app
+    from syntropy_b200.cli.main import _engine_from_config
+    from syntropy_b200.config.schema import load_config
+    from syntropy_b200.runtime.async_engine import AsyncEngine
+    from syntropy_b200.text.tokenizer import load_tokenizer
+    d = tmp_path / "ckpt"
+    tk = Tokenizer(models.BPE(unk_token="<unk>"))
+    tk.pre_tokenizer = pre_tokenizers.ByteLevel(add_prefix_space=False)
+    tk.decoder = decoders.ByteLevel()
+    specials = ["<unk>", "<|im_start|>", "<|im_end|>"]
+    tk.train_from_iterator(["hello there, how are you today? fine thanks"] * 20,
+                           trainers.BpeTrainer(vocab_size=200, special_tokens=specials,
+                                               initial_alphabet=pre_tokenizers.ByteLevel.alphabet()))
+    torch.manual_seed(9)
+    cfg_t = transformers.Qwen3Config(intermediate_size=256, head_dim=32, **dict(COMMON, vocab_size=512))
+    m = transformers.Qwen3ForCausalLM(cfg_t).float().eval()
+    with torch.no_grad():
+        for p in m.parameters():
+            if p.dim() > 1:
+                p.normal_(0, 0.08)
+        m.lm_head.weight[tk.token_to_id("<|im_end|>")] += 0.5  # make the end of turn likely
+    m.save_pretrained(str(d))
+    tk.save(str(d / "tokenizer.json"))
+    tmpl = ("{% for m in messages %}<|im_start|>{{ m['role'] }}\n{{ m['content'] }}<|im_end|>\n{% endfor %}"
+            "{% if add_generation_prompt %}<|im_start|>assistant\n{% endif %}")
+    (d / "tokenizer_config.json").write_text(json.dumps({"chat_template": tmpl, "eos_token": "<|im_end|>"}))
+    cfg = load_config(env={}, overrides=[f"model.path={d}", "model.max_seq_len=128", "sched.max_batch=2"])
+    eng, mcfg = _engine_from_config(cfg, "cpu")
+    tok = load_tokenizer(str(d), mcfg.vocab)
+    msgs = [{"role": "user", "content": "hello there"}]
+    ids = tok.encode_chat(msgs)
+    want = []
+    x = torch.tensor([ids])
+    with torch.no_grad():
+        for _ in range(20):
+            nxt = int(m(x).logits[0, -1].argmax())
+            want.append(nxt)
+            if nxt == tok.eos_token_id:
+                break
+            x = torch.cat([x, torch.tensor([[nxt]])], 1)
+    aeng = AsyncEngine(eng)
+    try:
+        with TestClient(build_app(aeng, tok, model_id="ckpt")) as c:
+            r = c.post("/v1/chat/completions", json={"model": "ckpt", "messages": msgs, "max_tokens": 20,
+                                                     "temperature": 0})
+    finally:
+        aeng.close()
+    assert r.status_code == 200, r.text
+    j = r.json()
+    text_want = tok.decode([t for t in want if t != tok.eos_token_id])
+    assert j["choices"][0]["message"]["content"] == text_want
+    assert want[-1] == tok.eos_token_id and len(want) < 20  # the reply ends with the end of turn
+    assert j["choices"][0]["finish_reason"] == "stop"
