@@ -40,6 +40,17 @@ class SafetensorsFile:
         t = torch.frombuffer(bytearray(buf), dtype=torch.uint8)
         return t.view(dtype).reshape(shape) if dtype != torch.uint8 else t.reshape(shape)
 
+    def get_row(self, name: str, i: int) -> torch.Tensor:
+        """Row `i` of the first dimension, read alone (one expert of a stacked tensor)."""
+        dt, shape, b, e = self.tensors[name]
+        dtype = _DT[dt]
+        n = (e - b) // shape[0]
+        if not 0 <= i < shape[0]:
+            raise IndexError(f"{name}: row {i} of {shape[0]}")
+        buf = memoryview(self._mm)[self.data_start + b + i * n: self.data_start + b + (i + 1) * n]
+        t = torch.frombuffer(bytearray(buf), dtype=torch.uint8)
+        return t.view(dtype).reshape(shape[1:]) if dtype != torch.uint8 else t.reshape(shape[1:])
+
     def close(self):
         self._mm.close()
         self._f.close()

@@ -219,3 +219,134 @@ def load_gguf(path: str, weight_quant: str = "bf16", name: str | None = None) ->
         return cfg, sd
     finally:
         f.close()
+
+
+# ---------------------------------------------------------------------- lazy loading
+class _ExpertStack:
+    """Stacked expert tensor [E, ...] read one expert at a time.  A leading-`:` slice (a
+    tensor-parallel shard, `t[:, a:b]` or `t[:, :, a:b]`) is kept and applied to each expert."""
+
+    def __init__(self, fetch, n: int, shape: tuple, index: tuple = ()):
+        self.fetch, self.n, self._shape, self.index = fetch, n, tuple(shape), index
+
+    @property
+    def shape(self):
+        return (self.n,) + self._shape
+
+    def __len__(self):
+        return self.n
+
+    def __getitem__(self, idx):
+        if isinstance(idx, int):
+            t = self.fetch(idx)
+            return t[self.index] if self.index else t
+        if isinstance(idx, tuple) and len(idx) > 1 and idx[0] == slice(None) and not self.index:
+            rest = idx[1:]
+            shape = list(self._shape)
+            for d, s in enumerate(rest):
+                shape[d] = len(range(*s.indices(shape[d])))
+            return _ExpertStack(self.fetch, self.n, tuple(shape), rest)
+        raise TypeError(f"unsupported expert-stack index {idx!r}")
+
+
+class LazyCheckpoint(dict):
+    """Canonical-name view of a Hugging Face safetensors checkpoint whose tensors are read from
+    the memory-mapped files when asked for (experts one at a time), so preparing a model larger
+    than host memory holds about one tensor at a time.  `lazy` tells `prepare_weights` to shard
+    tensor-parallel slices on access instead of slicing the whole dict up front."""
+
+    lazy = True
+
+    def __init__(self, path: str, cfg: ModelConfig, rope_interleave: bool = True):
+        super().__init__()
+        from ..formats.safetensors import SafetensorsFile
+        self.cfg = cfg
+        files = sorted(os.path.join(path, f) for f in os.listdir(path) if f.endswith(".safetensors"))
+        self._files = [SafetensorsFile(p) for p in files]
+        self._where = {n: f for f in self._files for n in f.keys()}
+        self._map, self._experts, self._fused = {}, {}, {}
+        for n in self._where:
+            if n == "model.embed_tokens.weight":
+                self._map["embed"] = n
+            elif n == "model.norm.weight":
+                self._map["final_norm"] = n
+            elif n == "lm_head.weight":
+                self._map["lm_head"] = n
+            else:
+                m = re.fullmatch(r"model\.layers\.(\d+)\.(.+)", n)
+                if not m:
+                    raise KeyError(f"unmapped tensor {n}")
+                i, rest = m.groups()
+                if rest in _LAYER:
+                    self._map[f"layers.{i}.{_LAYER[rest]}"] = n
+                    continue
+                e = re.fullmatch(r"mlp\.experts\.(\d+)\.(gate|up|down)_proj\.weight", rest)
+                if e:
+                    self._experts.setdefault(f"layers.{i}.experts.{e.group(2)}", {})[int(e.group(1))] = n
+                elif rest == "mlp.experts.gate_up_proj":   # fused [E, 2f, h]: gate rows, then up rows
+                    self._fused[f"layers.{i}.experts.gate"] = (n, 0)
+                    self._fused[f"layers.{i}.experts.up"] = (n, 1)
+                elif rest == "mlp.experts.down_proj":      # fused [E, h, f]
+                    self._fused[f"layers.{i}.experts.down"] = (n, None)
+                else:
+                    raise KeyError(f"unmapped tensor {n}")
+        for name, ids in self._experts.items():
+            if sorted(ids) != list(range(len(ids))):
+                raise KeyError(f"{name}: experts {sorted(set(range(max(ids) + 1)) - set(ids))} missing")
+        self._rope = cfg.is_mla and rope_interleave
+
+    def _read(self, hf_name: str) -> torch.Tensor:
+        return self._where[hf_name].get(hf_name)
+
+    def _fused_row(self, hf_name: str, half, e: int) -> torch.Tensor:
+        t = self._where[hf_name].get_row(hf_name, e)
+        if half is None:
+            return t
+        f = t.shape[0] // 2
+        return t[half * f:(half + 1) * f]
+
+    def __getitem__(self, name):
+        if name in self._experts:
+            ids = self._experts[name]
+            shape = tuple(self._where[ids[0]].tensors[ids[0]][1])
+            return _ExpertStack(lambda e, ids=ids: self._read(ids[e]), len(ids), shape)
+        if name in self._fused:
+            n, half = self._fused[name]
+            shape = list(self._where[n].tensors[n][1])
+            if half is not None:
+                shape[1] //= 2
+            return _ExpertStack(lambda e, n=n, half=half: self._fused_row(n, half, e), shape[0], tuple(shape[1:]))
+        t = self._read(self._map[name])
+        if self._rope and name.split(".")[-1] in ("q_b", "q_proj", "kv_a"):
+            d = {name: t}
+            _deinterleave_rope(d, self.cfg)
+            t = d[name]
+        return t
+
+    def __contains__(self, name):
+        return name in self._map or name in self._experts or name in self._fused
+
+    def __len__(self):
+        return len(self._map) + len(self._experts) + len(self._fused)
+
+    def __iter__(self):
+        return iter(self.keys())
+
+    def keys(self):
+        return list(self._map) + list(self._experts) + list(self._fused)
+
+    def items(self):
+        return ((n, self[n]) for n in self.keys())
+
+    def close(self):
+        for f in self._files:
+            f.close()
+
+
+def load_hf_lazy(path: str, weight_quant: str = "bf16", name: str | None = None) -> tuple[ModelConfig, LazyCheckpoint]:
+    """(config, lazy canonical view) of a checkpoint directory; `prepare_weights` reads it
+    tensor by tensor and expert by expert (per-expert or fused expert tensors alike)."""
+    with open(os.path.join(path, "config.json")) as f:
+        d = json.load(f)
+    cfg = config_from_hf(d, name or os.path.basename(os.path.normpath(path)), weight_quant)
+    return cfg, LazyCheckpoint(path, cfg, bool(d.get("rope_interleave", True)))

@@ -231,8 +231,8 @@ def prepare_weights(cfg: ModelConfig, device="cpu", seed: int = 0, quant: str | 
         if full is None:
             # generate each tensor on the device, then keep this rank's slice
             full = _LazyState(cfg, seed, device if device.type == "cuda" else "cpu")
-        sd_local = shard_state(cfg, full, tp[0], tp[1]) if not isinstance(full, _LazyState) else \
-            _LazyShard(full, cfg, tp[0], tp[1])
+        lazy = isinstance(full, _LazyState) or getattr(full, "lazy", False)
+        sd_local = _LazyShard(full, cfg, tp[0], tp[1]) if lazy else shard_state(cfg, full, tp[0], tp[1])
         mw = prepare_weights(local_config(cfg, tp[1]), device, seed, quant, sd_local, max_pos, expert_range,
                              dense_dtype, None, layer_range)
         return mw
@@ -339,6 +339,14 @@ def prepare_weights(cfg: ModelConfig, device="cpu", seed: int = 0, quant: str | 
                     del g, u, d, q
                 gu.build_ptrs()
                 dn.build_ptrs()
+            elif state_dict is not None:  # expert by expert (a lazy checkpoint reads one at a time)
+                G, U, D = (state_dict[pre + "experts." + k] for k in ("gate", "up", "down"))
+                gu.w = torch.stack([ops.interleave_gate_up(G[e].to(gen_dev).float(), U[e].to(gen_dev).float())
+                                    for e in range(ea, eb)])
+                dn.w = torch.stack([D[e].to(gen_dev).float() for e in range(ea, eb)])
+                if is_cuda:
+                    gu.w = gu.w.to(device=device, dtype=torch.bfloat16)
+                    dn.w = dn.w.to(device=device, dtype=torch.bfloat16)
             else:
                 g = get(pre + "experts.gate", sh["experts.gate"])
                 u = get(pre + "experts.up", sh["experts.up"])

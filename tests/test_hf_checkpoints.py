@@ -383,3 +383,83 @@ def test_serving_a_checkpoint_directory(tmp_path):
     assert j["choices"][0]["message"]["content"] == text_want
     assert want[-1] == tok.eos_token_id and len(want) < 20  # the reply ends with the end of turn
     assert j["choices"][0]["finish_reason"] == "stop"
+
+
+def _dense(v):
+    return torch.stack([v[e] for e in range(len(v))]) if not isinstance(v, torch.Tensor) else v
+
+
+def test_lazy_checkpoint_equals_eager(tmp_path):
+    """The lazy view reads tensors on demand (experts one at a time, fused or per-expert) and
+    holds the same canonical tensors as the eager loader; weights prepared from it, whole or as
+    a tensor-parallel shard, serve the same tokens."""
+    from syntropy_b200.formats.safetensors import load_state_dict, save_file
+    from syntropy_b200.models.hf import load_hf_lazy
+    torch.manual_seed(3)
+    m = transformers.Qwen3MoeForCausalLM(transformers.Qwen3MoeConfig(
+        intermediate_size=256, moe_intermediate_size=128, head_dim=32, num_experts=8, num_experts_per_tok=2,
+        norm_topk_prob=True, **COMMON)).float().eval()
+    with torch.no_grad():
+        for p in m.parameters():
+            if p.dim() > 1:
+                p.normal_(0, 0.08)
+    d = tmp_path / "moe"
+    m.save_pretrained(str(d))
+    # the same weights with fused expert tensors ([E, 2f, h] gate|up and [E, h, f] down)
+    raw = load_state_dict(str(d))
+    fused, per = {}, {}
+    for n, t in raw.items():
+        if ".mlp.experts." in n and n.endswith("_proj.weight"):
+            lay, e, kind = n.split(".mlp.experts.")[0], int(n.split(".")[5]), n.split(".")[6]
+            per.setdefault((lay, kind), {})[e] = t
+        else:
+            fused[n] = t
+    for (lay, kind), ex in per.items():
+        stack = torch.stack([ex[e] for e in sorted(ex)])
+        if kind == "down_proj":
+            fused[f"{lay}.mlp.experts.down_proj"] = stack
+        elif kind == "gate_proj":
+            up = torch.stack([per[(lay, "up_proj")][e] for e in sorted(ex)])
+            fused[f"{lay}.mlp.experts.gate_up_proj"] = torch.cat([stack, up], 1)
+    f = tmp_path / "fused"
+    f.mkdir()
+    (f / "config.json").write_text((d / "config.json").read_text())
+    save_file(fused if per else raw, str(f / "model.safetensors"))
+
+    prompt = [5, 17, 99, 250, 3, 42, 77]
+    want = _hf_greedy(m, prompt, 8)
+    for path in (d, f):
+        cfg, eager = load_hf(str(path), weight_quant="fp32")
+        cfg2, lazy = load_hf_lazy(str(path), weight_quant="fp32")
+        assert cfg2 == cfg and sorted(lazy.keys()) == sorted(eager.keys())
+        for n in eager:
+            assert torch.equal(_dense(lazy[n]), eager[n]), n
+        mw = prepare_weights(cfg, "cpu", state_dict=lazy, max_pos=64)
+        got = LLMEngine(ModelRunner(mw, max_batch=2, max_seq_len=48)).generate([prompt], SamplingParams(max_tokens=8))
+        assert got[0] == want, path.name
+        for r in range(2):  # a TP shard sliced on access equals the eagerly sliced shard
+            a = prepare_weights(cfg, "cpu", state_dict=eager, max_pos=64, tp=(r, 2))
+            b = prepare_weights(cfg, "cpu", state_dict=lazy, max_pos=64, tp=(r, 2))
+            for La, Lb in zip(a.layers, b.layers):
+                assert torch.equal(La.experts_gu.w, Lb.experts_gu.w) and torch.equal(La.experts_down.w,
+                                                                                     Lb.experts_down.w)
+                assert torch.equal(La.qkv, Lb.qkv) and torch.equal(La.o, Lb.o)
+        lazy.close()
+
+
+def test_lazy_checkpoint_mla_rotary_rows(tmp_path):
+    """DeepseekV3 (interleaved rotary rows reordered per tensor on access) through the lazy view."""
+    from syntropy_b200.models.hf import load_hf_lazy
+    torch.manual_seed(4)
+    c = transformers.DeepseekV3Config(
+        vocab_size=512, hidden_size=128, intermediate_size=256, moe_intermediate_size=64, num_hidden_layers=2,
+        num_attention_heads=4, num_key_value_heads=4, n_routed_experts=8, num_experts_per_tok=2, n_shared_experts=1,
+        n_group=2, topk_group=1, first_k_dense_replace=1, q_lora_rank=64, kv_lora_rank=32, qk_rope_head_dim=16,
+        qk_nope_head_dim=32, v_head_dim=32, rope_scaling=None, max_position_embeddings=256, rms_norm_eps=1e-6)
+    m = transformers.DeepseekV3ForCausalLM(c).float().eval()
+    m.save_pretrained(str(tmp_path / "ds"))
+    _, eager = load_hf(str(tmp_path / "ds"), weight_quant="fp32")
+    _, lazy = load_hf_lazy(str(tmp_path / "ds"), weight_quant="fp32")
+    for n in eager:
+        assert torch.equal(_dense(lazy[n]), eager[n]), n
+    lazy.close()
