@@ -18,7 +18,8 @@ def _engine_from_config(cfg, device: str):
     sd = None
     if cfg.model.path and cfg.model.path.endswith(".gguf"):
         from ..models.hf import load_gguf  # a llama.cpp GGUF file (blocks dequantised, then requantised)
-        mcfg, sd = load_gguf(cfg.model.path, weight_quant=cfg.model.quant or ("bf16" if dev.type == "cuda" else "fp32"))
+        mcfg, sd = load_gguf(cfg.model.path, weight_quant=cfg.model.quant or ("bf16" if dev.type == "cuda" else "fp32"),
+                             lazy=True)
     elif cfg.model.path and os.path.exists(os.path.join(cfg.model.path, "config.json")):
         from ..models.hf import load_hf_lazy  # a Hugging Face checkpoint directory, read tensor by tensor
         mcfg, sd = load_hf_lazy(cfg.model.path,

@@ -40,8 +40,22 @@ class GGUFFile:
     def get(self, name: str) -> torch.Tensor:
         """Dense f32 tensor with torch shape (GGUF dims are innermost-first)."""
         t, dims, _ = self.tensors[name]
+        return self._decode(name, t, self.raw(name), tuple(reversed(dims)))
+
+    def get_row(self, name: str, i: int) -> torch.Tensor:
+        """Row `i` of the outermost dimension (one expert of a stacked tensor), read and
+        dequantised alone; a row is a whole number of blocks, so it starts on a block."""
+        t, dims, off = self.tensors[name]
         shape = tuple(reversed(dims))
-        r = self.raw(name)
+        if not 0 <= i < shape[0]:
+            raise IndexError(f"{name}: row {i} of {shape[0]}")
+        per = self.nbytes(name) // shape[0]
+        b = self.data_start + off + i * per
+        r = torch.frombuffer(memoryview(self._mm)[b: b + per], dtype=torch.uint8).clone()
+        return self._decode(name, t, r, shape[1:])
+
+    @staticmethod
+    def _decode(name: str, t: int, r: torch.Tensor, shape: tuple) -> torch.Tensor:
         if t == GGML_F32:
             return r.view(torch.float32).reshape(shape)
         if t == GGML_F16:

@@ -169,56 +169,103 @@ def _rows_to_rotate_half(w: torch.Tensor, n_heads: int) -> torch.Tensor:
     return w.reshape(n_heads, hd, *w.shape[1:])[:, perm].reshape(w.shape).contiguous()
 
 
-def load_gguf(path: str, weight_quant: str = "bf16", name: str | None = None) -> tuple[ModelConfig, dict]:
-    """(config, canonical state dict) of a GGUF file (llama / qwen2 / qwen3 / qwen3moe; the
-    quantised blocks are dequantised, then requantised by `prepare_weights` as configured)."""
-    from ..formats.gguf import GGUFFile
-    f = GGUFFile(path)
-    try:
-        m = f.meta
-        arch = m["general.architecture"]
-        if arch not in _GGUF_ARCH:
-            raise ValueError(f"GGUF architecture {arch!r} is not supported (supported: {sorted(_GGUF_ARCH)})")
-        if "rope_freqs.weight" in f.tensors or m.get(f"{arch}.rope.scaling.type", "none") not in ("none", None):
-            raise ValueError("rotary scaling in a GGUF file is not supported")
-        k = lambda key, default=None: m.get(f"{arch}.{key}", default)  # noqa: E731
-        emb_dims = f.tensors["token_embd.weight"][1]
-        d = {"architectures": [_GGUF_ARCH[arch]], "hidden_size": int(k("embedding_length")),
-             "num_hidden_layers": int(k("block_count")), "num_attention_heads": int(k("attention.head_count")),
-             "num_key_value_heads": int(k("attention.head_count_kv", k("attention.head_count"))),
-             "intermediate_size": int(k("feed_forward_length", 0) or 0), "vocab_size": int(emb_dims[1]),
-             "rms_norm_eps": float(k("attention.layer_norm_rms_epsilon", 1e-6)),
-             "rope_theta": float(k("rope.freq_base", 10000.0)),
-             "tie_word_embeddings": "output.weight" not in f.tensors}
-        if k("attention.key_length"):
-            d["head_dim"] = int(k("attention.key_length"))
-        if arch == "qwen3moe":
-            d.update(num_experts=int(k("expert_count")), num_experts_per_tok=int(k("expert_used_count")),
-                     moe_intermediate_size=int(k("expert_feed_forward_length")), norm_topk_prob=True)
-        cfg = config_from_hf(d, name or os.path.splitext(os.path.basename(path))[0], weight_quant)
-        sd = {}
-        for n in f.tensors:
-            t = f.get(n)
-            if n == "token_embd.weight":
-                sd["embed"] = t
-            elif n == "output_norm.weight":
-                sd["final_norm"] = t
-            elif n == "output.weight":
-                sd["lm_head"] = t
-            else:
+def _gguf_config(f, name: str, weight_quant: str) -> tuple[str, ModelConfig]:
+    m = f.meta
+    arch = m["general.architecture"]
+    if arch not in _GGUF_ARCH:
+        raise ValueError(f"GGUF architecture {arch!r} is not supported (supported: {sorted(_GGUF_ARCH)})")
+    if "rope_freqs.weight" in f.tensors or m.get(f"{arch}.rope.scaling.type", "none") not in ("none", None):
+        raise ValueError("rotary scaling in a GGUF file is not supported")
+    k = lambda key, default=None: m.get(f"{arch}.{key}", default)  # noqa: E731
+    emb_dims = f.tensors["token_embd.weight"][1]
+    d = {"architectures": [_GGUF_ARCH[arch]], "hidden_size": int(k("embedding_length")),
+         "num_hidden_layers": int(k("block_count")), "num_attention_heads": int(k("attention.head_count")),
+         "num_key_value_heads": int(k("attention.head_count_kv", k("attention.head_count"))),
+         "intermediate_size": int(k("feed_forward_length", 0) or 0), "vocab_size": int(emb_dims[1]),
+         "rms_norm_eps": float(k("attention.layer_norm_rms_epsilon", 1e-6)),
+         "rope_theta": float(k("rope.freq_base", 10000.0)),
+         "tie_word_embeddings": "output.weight" not in f.tensors}
+    if k("attention.key_length"):
+        d["head_dim"] = int(k("attention.key_length"))
+    if arch == "qwen3moe":
+        d.update(num_experts=int(k("expert_count")), num_experts_per_tok=int(k("expert_used_count")),
+                 moe_intermediate_size=int(k("expert_feed_forward_length")), norm_topk_prob=True)
+    return arch, config_from_hf(d, name, weight_quant)
+
+
+class GGUFCheckpoint(dict):
+    """Canonical-name view of a GGUF file (llama / qwen2 / qwen3 / qwen3moe) whose tensors are
+    dequantised when asked for (stacked experts one expert at a time), so weights are prepared
+    without the whole f32 model in host memory; `prepare_weights` requantises them as configured.
+    llama.cpp's interleaved Q / K rotary rows of `llama` models are put back in rotate-half order."""
+
+    lazy = True
+
+    def __init__(self, path: str, weight_quant: str = "bf16", name: str | None = None):
+        super().__init__()
+        from ..formats.gguf import GGUFFile
+        self.file = f = GGUFFile(path)
+        try:
+            self.arch, self.cfg = _gguf_config(f, name or os.path.splitext(os.path.basename(path))[0], weight_quant)
+            self._map = {}
+            for n in f.tensors:
+                if n in ("token_embd.weight", "output_norm.weight", "output.weight"):
+                    self._map[{"token_embd.weight": "embed", "output_norm.weight": "final_norm",
+                               "output.weight": "lm_head"}[n]] = (n, None)
+                    continue
                 mm = re.fullmatch(r"blk\.(\d+)\.(\w+)\.(weight|bias)", n)
                 if not mm or mm.group(2) not in _GGUF_LAYER:
                     raise KeyError(f"unmapped GGUF tensor {n}")
                 i, part, kind = mm.groups()
-                leaf = _GGUF_LAYER[part]
+                leaf, rot = _GGUF_LAYER[part], None
                 if kind == "bias":
                     leaf = {"q_proj": "q_bias", "k_proj": "k_bias", "v_proj": "v_bias"}[leaf]
-                elif arch == "llama" and leaf in ("q_proj", "k_proj"):
-                    t = _rows_to_rotate_half(t, cfg.n_heads if leaf == "q_proj" else cfg.n_kv_heads)
-                sd[f"layers.{i}.{leaf}"] = t
-        return cfg, sd
+                elif self.arch == "llama" and leaf in ("q_proj", "k_proj"):
+                    rot = self.cfg.n_heads if leaf == "q_proj" else self.cfg.n_kv_heads
+                self._map[f"layers.{i}.{leaf}"] = (n, rot)
+        except Exception:
+            f.close()
+            raise
+
+    def __getitem__(self, name):
+        n, rot = self._map[name]
+        if name.split(".")[-2:-1] == ["experts"]:
+            shape = tuple(reversed(self.file.tensors[n][1]))
+            return _ExpertStack(lambda e, n=n: self.file.get_row(n, e), shape[0], shape[1:])
+        t = self.file.get(n)
+        return _rows_to_rotate_half(t, rot) if rot else t
+
+    def __contains__(self, name):
+        return name in self._map
+
+    def __len__(self):
+        return len(self._map)
+
+    def __iter__(self):
+        return iter(self._map)
+
+    def keys(self):
+        return list(self._map)
+
+    def items(self):
+        return ((n, self[n]) for n in self._map)
+
+    def close(self):
+        self.file.close()
+
+
+def load_gguf(path: str, weight_quant: str = "bf16", name: str | None = None,
+              lazy: bool = False) -> tuple[ModelConfig, dict]:
+    """(config, canonical state dict) of a GGUF file: dequantised in full, or with `lazy` the
+    `GGUFCheckpoint` view that dequantises tensor by tensor (close it when done)."""
+    ck = GGUFCheckpoint(path, weight_quant, name)
+    if lazy:
+        return ck.cfg, ck
+    try:
+        return ck.cfg, {n: ck.file.get(ck._map[n][0]) if n.split(".")[-2:-1] == ["experts"] else ck[n]
+                        for n in ck.keys()}
     finally:
-        f.close()
+        ck.close()
 
 
 # ---------------------------------------------------------------------- lazy loading

@@ -270,7 +270,7 @@ def _gguf_from_hf(model, arch, path, quant=None):
         out[f"blk.{i}.ffn_{kind.replace('_proj', '')}_exps.weight"] = torch.stack([dd[e] for e in sorted(dd)])
     for n, t in out.items():
         a = t.numpy().astype(np.float32)
-        if quant is not None and a.ndim == 2 and n != "token_embd.weight":
+        if quant is not None and a.ndim >= 2 and n != "token_embd.weight":
             w.add_tensor(n, quants.quantize(a, quant), raw_dtype=quant)
         else:
             w.add_tensor(n, a)
@@ -298,9 +298,38 @@ def test_gguf_checkpoints_match_transformers(tmp_path):
         _gguf_from_hf(m, arch, path)
         cfg, sd = load_gguf(str(path), weight_quant="fp32")
         assert cfg.is_moe == (arch == "qwen3moe")
+        want = _hf_greedy(m, prompt, 10)
         mw = prepare_weights(cfg, "cpu", state_dict=sd, max_pos=64)
         got = LLMEngine(ModelRunner(mw, max_batch=2, max_seq_len=48)).generate([prompt], SamplingParams(max_tokens=10))
-        assert got[0] == _hf_greedy(m, prompt, 10), arch
+        assert got[0] == want, arch
+        _, lazy = load_gguf(str(path), weight_quant="fp32", lazy=True)  # tensor by tensor, same tokens
+        mw = prepare_weights(cfg, "cpu", state_dict=lazy, max_pos=64)
+        got = LLMEngine(ModelRunner(mw, max_batch=2, max_seq_len=48)).generate([prompt], SamplingParams(max_tokens=10))
+        assert got[0] == want, arch
+        lazy.close()
+
+
+def test_gguf_lazy_quantised_experts(tmp_path):
+    """Q8_0 / Q4_0 expert stacks dequantised one expert at a time equal the whole-tensor
+    dequantisation, and the lazy view holds the eager loader's tensors."""
+    from gguf import GGMLQuantizationType as T
+    from syntropy_b200.models.hf import load_gguf
+    torch.manual_seed(8)
+    m = transformers.Qwen3MoeForCausalLM(transformers.Qwen3MoeConfig(
+        intermediate_size=256, moe_intermediate_size=64, head_dim=32, num_experts=8, num_experts_per_tok=2,
+        norm_topk_prob=True, **COMMON)).float().eval()
+    for q in (T.Q8_0, T.Q4_0):
+        path = tmp_path / f"moe_{q.name}.gguf"
+        _gguf_from_hf(m, "qwen3moe", path, quant=q)
+        cfg, eager = load_gguf(str(path), weight_quant="fp32")
+        _, lazy = load_gguf(str(path), weight_quant="fp32", lazy=True)
+        assert sorted(lazy.keys()) == sorted(eager.keys())
+        for n in eager:
+            v = lazy[n]
+            v = torch.stack([v[e] for e in range(len(v))]) if not isinstance(v, torch.Tensor) else v
+            assert torch.equal(v, eager[n]), (q.name, n)
+        assert lazy.file.tensors["blk.0.ffn_down_exps.weight"][0] == int(q)
+        lazy.close()
 
 
 def test_gguf_q8_0_blocks_load(tmp_path):
