@@ -33,10 +33,10 @@ CONFIG_DEFAULTS = {"qwen3-235b-a22b": (32, 1024, 256), "llama3-8b": (64, 2048, 2
 
 def reference_arm(args):
     # The reference is a Rust workspace with no Python package, no GPU kernels and no
-    # end-to-end forward; it cannot be installed or run here.
+    # end-to-end forward; it cannot be installed as a Python package or run on this image.
     print(json.dumps({"impl": "reference", "unavailable":
                       "reference is a pre-alpha Rust workspace (no GPU kernels, no end-to-end forward, no cargo "
-                      "toolchain on the box); pip install of /root/reference fails: no setup.py/pyproject.toml"}))
+                      "toolchain on the box); pip install of the reference source tree fails: no setup.py/pyproject.toml"}))
 
 
 class ClockSampler:
