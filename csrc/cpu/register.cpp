@@ -60,6 +60,7 @@ void register_all(pybind11::module& m) {
   register_tier(m);
   register_cpu_experts(m);
   register_constrain(m);
+  register_ggml(m);
 }
 
 }  // namespace syn

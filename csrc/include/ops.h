@@ -110,4 +110,5 @@ void register_tier(pybind11::module& m);
 void register_cpu_experts(pybind11::module& m);
 void register_constrain(pybind11::module& m);
 void register_formats(pybind11::module& m);
+void register_ggml(pybind11::module& m);
 }  // namespace syn

@@ -184,7 +184,12 @@ def main(argv=None):
     p.add_argument("--probe", action="store_true", help="include the doctor report (touches the GPU)")
     p = sub.add_parser("bench")
     p.add_argument("rest", nargs=argparse.REMAINDER)
+    p = sub.add_parser("netprobe", help="network probe between two machines (listen | run | check)")
+    p.add_argument("rest", nargs=argparse.REMAINDER)
     args = ap.parse_args(argv)
+    if args.cmd == "netprobe":
+        from ..net.probe import main as netprobe_main
+        raise SystemExit(netprobe_main(args.rest))
     from ..config import load_config
     cfg = load_config(args.config, overrides=args.set)
     {"version": cmd_version, "config": cmd_config, "plan": cmd_plan, "run": cmd_run, "serve": cmd_serve,

@@ -62,12 +62,8 @@ class GGUFFile:
             return r.view(torch.float16).float().reshape(shape)
         if t == GGML_BF16:
             return r.view(torch.bfloat16).float().reshape(shape)
-        if t == GGML_Q4_1:
-            from .q4 import dequant_rows_ref
-            N = int(np.prod(shape[:-1]))
-            return dequant_rows_ref(r, N, shape[-1]).reshape(shape)
-        if GGML_TYPE.get(t) in DEQUANT:
-            return DEQUANT[GGML_TYPE[t]](r).reshape(shape)
+        if GGML_TYPE.get(t) in DEQUANT:  # native, multi-threaded over blocks
+            return ext().ggml_dequant(r.contiguous(), GGML_TYPE[t]).reshape(shape)
         raise NotImplementedError(f"GGML type {t} for {name}")
 
     def close(self):
