@@ -35,14 +35,21 @@ def config_from_hf(d: dict, name: str = "hf", weight_quant: str = "bf16") -> Mod
     rope = d.get("rope_scaling") or d.get("rope_parameters") or {}
     rtype = rope.get("rope_type", rope.get("type", "default")) if isinstance(rope, dict) else "default"
     scaling = ()
-    if rtype == "yarn" and arch == "DeepseekV3ForCausalLM":
+    if rtype == "yarn":  # DeepSeek-V3 (also scales the MLA softmax) and GQA models (cos/sin only)
+        if rope.get("truncate", True) is False:
+            raise ValueError("YaRN without truncated correction bounds is not supported")
+        if not (rope.get("original_max_position_embeddings") or d.get("max_position_embeddings")):
+            raise ValueError("YaRN rotary scaling needs original_max_position_embeddings")
         scaling = ("yarn", float(rope["factor"]),
                    float(rope.get("original_max_position_embeddings") or d.get("max_position_embeddings")),
-                   float(rope.get("beta_fast", 32.0)), float(rope.get("beta_slow", 1.0)),
-                   float(rope.get("mscale", 1.0) or 0.0), float(rope.get("mscale_all_dim", 0.0) or 0.0))
+                   float(rope.get("beta_fast") or 32.0), float(rope.get("beta_slow") or 1.0),
+                   float(rope.get("mscale", 1.0) or 0.0), float(rope.get("mscale_all_dim", 0.0) or 0.0),
+                   float(rope.get("attention_factor") or 0.0))
     elif rtype == "llama3" and arch != "DeepseekV3ForCausalLM":
         scaling = ("llama3", float(rope["factor"]), float(rope.get("low_freq_factor", 1.0)),
                    float(rope.get("high_freq_factor", 4.0)), float(rope["original_max_position_embeddings"]))
+    elif rtype == "linear":
+        scaling = ("linear", float(rope["factor"]))
     elif rtype not in (None, "default"):
         raise ValueError(f"rotary scaling {rtype!r} is not supported")
     theta = d.get("rope_theta") or (rope.get("rope_theta") if isinstance(rope, dict) else None) or 10000.0

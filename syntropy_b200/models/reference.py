@@ -23,7 +23,8 @@ _ROPE_CACHE: dict = {}
 
 
 def rope_frequencies(dim: int, theta: float, scaling: tuple = ()) -> torch.Tensor:
-    """Inverse frequencies (f64).  With ("llama3", factor, low, high, original_max_positions),
+    """Inverse frequencies (f64).  ("linear", factor) divides every frequency by `factor`.
+    With ("llama3", factor, low, high, original_max_positions),
     the Llama 3.1 rule: wavelengths shorter than original/high keep their frequency, longer
     than original/low are divided by `factor`, and the band between is interpolated linearly
     in original/wavelength between the two."""
@@ -32,6 +33,8 @@ def rope_frequencies(dim: int, theta: float, scaling: tuple = ()) -> torch.Tenso
         return inv
     if scaling[0] == "yarn":
         return _yarn_frequencies(dim, theta, *scaling[1:5])
+    if scaling[0] == "linear":  # position interpolation: every frequency divided by the factor
+        return inv / scaling[1]
     kind, factor, low, high, orig = scaling
     if kind != "llama3":
         raise ValueError(f"rotary scaling {kind!r} is not supported")
@@ -64,9 +67,12 @@ def yarn_mscale(factor: float, m: float = 1.0) -> float:
 
 
 def rope_magnitude(scaling: tuple = ()) -> float:
-    """Factor on cos/sin: YaRN's attention temperature (mscale / mscale_all_dim), else 1."""
+    """Factor on cos/sin: YaRN's attention temperature (given, or from mscale / mscale_all_dim),
+    else 1."""
     if not scaling or scaling[0] != "yarn":
         return 1.0
+    if len(scaling) > 7 and scaling[7]:  # given explicitly
+        return scaling[7]
     factor, mscale, mscale_all = scaling[1], scaling[5], scaling[6]
     if mscale and mscale_all:
         return yarn_mscale(factor, mscale) / yarn_mscale(factor, mscale_all)

@@ -61,7 +61,12 @@ def test_unsupported_configs_are_rejected():
     base = dict(architectures=["LlamaForCausalLM"], hidden_size=64, num_attention_heads=4, num_hidden_layers=1,
                 vocab_size=100, intermediate_size=128)
     with pytest.raises(ValueError, match="rotary scaling"):
+        config_from_hf(dict(base, rope_scaling={"rope_type": "dynamic", "factor": 4.0}))
+    with pytest.raises(ValueError, match="original_max_position_embeddings"):
         config_from_hf(dict(base, rope_scaling={"rope_type": "yarn", "factor": 4.0}))
+    with pytest.raises(ValueError, match="truncated"):
+        config_from_hf(dict(base, rope_scaling={"rope_type": "yarn", "factor": 4.0, "truncate": False,
+                                                "original_max_position_embeddings": 64}))
     with pytest.raises(ValueError, match="sliding"):
         config_from_hf(dict(base, architectures=["MistralForCausalLM"], sliding_window=4096))
     with pytest.raises(ValueError, match="not supported"):
@@ -138,6 +143,40 @@ def test_llama3_rotary_scaling_matches_transformers(tmp_path):
     mw0 = prepare_weights(unscaled, "cpu", state_dict=sd, max_pos=64)
     plain = LLMEngine(ModelRunner(mw0, max_batch=2, max_seq_len=60)).generate([prompt], SamplingParams(max_tokens=8))
     assert plain[0] != want  # the scaling matters for this model
+
+
+@pytest.mark.parametrize("kind", ["linear", "yarn", "yarn_attention_factor"])
+def test_gqa_rotary_scalings_match_transformers(tmp_path, kind):
+    """Linear position interpolation (Llama) and YaRN (Qwen3's long-context setting; the
+    attention temperature scales cos / sin) against transformers, past the original context."""
+    torch.manual_seed(9)
+    if kind == "linear":
+        rp = {"rope_type": "linear", "factor": 4.0, "rope_theta": 10000.0}
+        c = transformers.LlamaConfig(intermediate_size=256, rope_parameters=rp, **COMMON)
+        m = transformers.LlamaForCausalLM(c)
+    else:
+        rp = {"rope_type": "yarn", "factor": 4.0, "original_max_position_embeddings": 16, "rope_theta": 10000.0}
+        if kind == "yarn_attention_factor":
+            rp["attention_factor"] = 1.3
+        c = transformers.Qwen3Config(intermediate_size=256, head_dim=32, rope_parameters=rp, **COMMON)
+        m = transformers.Qwen3ForCausalLM(c)
+    m = m.float().eval()
+    with torch.no_grad():
+        for p in m.parameters():
+            if p.dim() > 1:
+                p.normal_(0, 0.08)
+    m.save_pretrained(str(tmp_path / kind))
+    cfg, sd = load_hf(str(tmp_path / kind), weight_quant="fp32")
+    assert cfg.rope_scaling[0] == kind.split("_")[0]
+    prompt = list(range(3, 40))
+    want = _hf_greedy(m, prompt, 8)
+    from syntropy_b200.models import reference
+    assert reference.greedy_generate(torch.tensor(prompt), sd, cfg, 8) == want
+    mw = prepare_weights(cfg, "cpu", state_dict=sd, max_pos=64)
+    got = LLMEngine(ModelRunner(mw, max_batch=2, max_seq_len=60)).generate([prompt], SamplingParams(max_tokens=8))
+    assert got[0] == want
+    plain = reference.greedy_generate(torch.tensor(prompt), sd, cfg.replace(rope_scaling=()), 8)
+    assert plain != want  # the scaling matters for this model
 
 
 def test_deepseek_v3_yarn_matches_transformers(tmp_path):
