@@ -61,6 +61,7 @@ void register_all(pybind11::module& m) {
   register_cpu_experts(m);
   register_constrain(m);
   register_ggml(m);
+  register_blake3(m);
 }
 
 }  // namespace syn

@@ -111,4 +111,5 @@ void register_cpu_experts(pybind11::module& m);
 void register_constrain(pybind11::module& m);
 void register_formats(pybind11::module& m);
 void register_ggml(pybind11::module& m);
+void register_blake3(pybind11::module& m);
 }  // namespace syn
