@@ -23,18 +23,13 @@ def _time_cuda(fn, iters=5):
 
 
 def probe_host() -> dict:
+    """CPU, ISA level, memory, NUMA host tiers and GPU NUMA affinity (`probe.host`)."""
+    from .host import host_report
     info = {"platform": platform.platform(), "cpus": os.cpu_count()}
     try:
-        with open("/proc/meminfo") as f:
-            for line in f:
-                if line.startswith("MemTotal"):
-                    info["mem_gb"] = round(int(line.split()[1]) / 1e6, 1)
-        with open("/proc/cpuinfo") as f:
-            flags = next((ln for ln in f if ln.startswith("flags")), "")
-        info["avx512"] = "avx512f" in flags
-        info["amx"] = "amx_tile" in flags
-    except OSError:
-        pass
+        info.update(host_report("/"))
+    except OSError as e:
+        info["error"] = str(e)
     return info
 
 
