@@ -81,7 +81,20 @@ def cmd_version(args, cfg):
 
 
 def cmd_config(args, cfg):
-    print(json.dumps({"config": cfg.to_dict(), "origin": cfg.origin}, indent=2))
+    """`config` shows the resolved values and their origins; `config get KEY`, `config set KEY
+    VALUE --file F` (a format-preserving edit of the TOML file)."""
+    action = getattr(args, "action", None)
+    if action == "get":
+        sec, _, key = args.key.rpartition(".")
+        print(json.dumps({"key": args.key, "value": getattr(getattr(cfg, sec), key),
+                          "origin": cfg.origin.get(args.key, "default")}))
+    elif action == "set":
+        from ..config.write import set_value
+        path = args.file or args.config or "syntropy.toml"
+        set_value(path, args.key, args.value)
+        print(json.dumps({"file": path, "key": args.key, "value": args.value}))
+    else:
+        print(json.dumps({"config": cfg.to_dict(), "origin": cfg.origin}, indent=2))
 
 
 def cmd_plan(args, cfg):
@@ -157,7 +170,11 @@ def main(argv=None):
     ap.add_argument("-o", "--set", action="append", default=[], help="section.key=value override")
     sub = ap.add_subparsers(dest="cmd", required=True)
     sub.add_parser("version")
-    sub.add_parser("config")
+    p = sub.add_parser("config")
+    p.add_argument("action", nargs="?", choices=["show", "get", "set"], default="show")
+    p.add_argument("key", nargs="?")
+    p.add_argument("value", nargs="?")
+    p.add_argument("--file", default=None, help="TOML file that `set` edits (default: --config)")
     p = sub.add_parser("plan")
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--batch", type=int, default=32)
