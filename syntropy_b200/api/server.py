@@ -49,7 +49,29 @@ def _params(body: dict, default_max: int = 16, stop_ids: tuple = ()) -> Sampling
                           repetition_penalty=float(body.get("repetition_penalty", 1.0)),
                           frequency_penalty=float(body.get("frequency_penalty", 0.0)),
                           presence_penalty=float(body.get("presence_penalty", 0.0)),
-                          logit_bias={int(k): float(v) for k, v in (body.get("logit_bias") or {}).items()} or None)
+                          logit_bias={int(k): float(v) for k, v in (body.get("logit_bias") or {}).items()} or None,
+                          logprobs=_logprobs_k(body))
+
+
+def _logprobs_k(body: dict):
+    """Chat `logprobs: true` (+ `top_logprobs: n`) or completions `logprobs: n` -> alternatives
+    per token (None when not asked)."""
+    lp = body.get("logprobs")
+    if lp is True:
+        return int(body.get("top_logprobs") or 0)
+    if isinstance(lp, int) and not isinstance(lp, bool):
+        return lp
+    return None
+
+
+def _render_logprobs(tokenizer, recs: list, chat: bool) -> dict:
+    def tok(t):
+        return tokenizer.decode([t])
+    if chat:
+        return {"content": [{"token": tok(r["token"]), "logprob": r["logprob"],
+                             "top_logprobs": [{"token": tok(t), "logprob": v} for t, v in r["top"]]} for r in recs]}
+    return {"tokens": [tok(r["token"]) for r in recs], "token_logprobs": [r["logprob"] for r in recs],
+            "top_logprobs": [{tok(t): v for t, v in r["top"]} for r in recs]}
 
 
 def _constraint(body: dict):
@@ -205,17 +227,19 @@ def build_app(aeng, tokenizer, model_id: str = "syntropy", bench_api: bool = Tru
                         yield "data: " + json.dumps({"error": {"message": ev.error}}) + "\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(sse(), media_type="text/event-stream")
-        toks, usage, reason = [], None, None
+        toks, usage, reason, lps = [], None, None, None
         async for ev in aeng.generate(list(ids), params):
             if ev.kind == "tokens":
                 toks += ev.tokens
             elif ev.kind == "done":
-                usage, reason = ev.usage, ev.finish_reason
+                usage, reason, lps = ev.usage, ev.finish_reason, ev.logprobs
             elif ev.kind == "error":
                 return _err(500, "internal", ev.error)
         text = tokenizer.decode(toks)
         choice = ({"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason} if chat
                   else {"index": 0, "text": text, "finish_reason": reason})
+        if lps is not None:
+            choice["logprobs"] = _render_logprobs(tokenizer, lps, chat)
         if usage:
             usage["total_tokens"] = usage["prompt_tokens"] + usage["completion_tokens"]
         return {"id": rid, "object": obj, "created": created, "model": model_id, "choices": [choice], "usage": usage}

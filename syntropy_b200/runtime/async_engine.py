@@ -25,6 +25,7 @@ class GenEvent:
     error: str | None = None
     usage: dict | None = None
     timings: dict | None = None
+    logprobs: list | None = None  # on "done": per emitted token, when the request asked for them
 
 
 class AsyncEngine:
@@ -121,5 +122,7 @@ class AsyncEngine:
                     self._emit(loop, q, GenEvent("done", finish_reason=o.finish_reason,
                                                  usage={"prompt_tokens": n_prompt, "completion_tokens": n_out},
                                                  timings={"ttft_ms": None if ttft is None else ttft * 1e3,
-                                                          "total_ms": (time.perf_counter() - t_arr) * 1e3}))
+                                                          "total_ms": (time.perf_counter() - t_arr) * 1e3},
+                                                 logprobs=(s.logprobs if s and s.params.logprobs is not None
+                                                           else None)))
                     self._subs.pop(o.seq_id, None)

@@ -35,6 +35,8 @@ class SamplingParams:
     frequency_penalty: float = 0.0   # subtracted once per earlier occurrence in the output
     presence_penalty: float = 0.0    # subtracted once if the token occurred in the output
     logit_bias: dict | None = None   # {token id: added logit}
+    logprobs: int | None = None      # record each emitted token's log-probability under the model's
+    #                                  own distribution and the `logprobs` most likely alternatives
 
     @property
     def processed(self) -> bool:
@@ -49,6 +51,7 @@ class Sequence:
     prompt: list
     params: SamplingParams
     output: list = field(default_factory=list)
+    logprobs: list = field(default_factory=list)  # per emitted token, when params.logprobs is set
     blocks: list = field(default_factory=list)
     status: str = "waiting"  # waiting | running | finished
     cached_tokens: int = 0   # prompt tokens served from the prefix cache
@@ -126,6 +129,8 @@ class LLMEngine:
                 raise ValueError(f"token id {t} out of range [0, {self.cfg.vocab})")
         if len(prompt) + params.max_tokens > self.runner.max_seq_len:
             raise ValueError("prompt + max_tokens exceeds max_seq_len")
+        if params.logprobs is not None and (self.spec is not None or params.logprobs < 0):
+            raise ValueError("logprobs: a count >= 0, and not with speculative decoding")
         kv = self.runner.kv
         pool = kv.alloc.num_blocks - kv.alloc.reserved
         if kv.blocks_needed(len(prompt) + params.max_tokens) > pool:
@@ -358,6 +363,7 @@ class LLMEngine:
             nxt = pp.broadcast_tokens(toks_t).cpu().tolist()
         else:
             nxt = self._sample_rows(logits, batch)
+            self._record_logprobs(logits, batch, nxt)
         self.stats["prefill_steps"] += 1
         self.stats["prefill_tokens"] += cu[-1]
         now = time.perf_counter()
@@ -371,6 +377,23 @@ class LLMEngine:
             self.spec.drafter.after_prefill(batch, self.runner._prefill_x, cu)
         self._reap()
         return outs
+
+    @staticmethod
+    def _record_logprobs(logits: torch.Tensor, seqs: list[Sequence], toks: list[int]):
+        """Log-softmax (f32) of the rows that asked for logprobs: the emitted token's value and
+        the top alternatives.  Rows that did not ask cost nothing."""
+        rows = [i for i, s in enumerate(seqs) if s.params.logprobs is not None]
+        if not rows:
+            return
+        lp = torch.log_softmax(logits[rows].float(), -1)
+        chosen = lp.gather(1, torch.tensor([toks[i] for i in rows], device=lp.device)[:, None])[:, 0].cpu().tolist()
+        k = max(seqs[i].params.logprobs for i in rows)
+        tv, ti = lp.topk(k, -1) if k else (None, None)
+        tv, ti = (tv.cpu().tolist(), ti.cpu().tolist()) if k else ([], [])
+        for j, i in enumerate(rows):
+            n = seqs[i].params.logprobs
+            seqs[i].logprobs.append({"token": int(toks[i]), "logprob": chosen[j],
+                                     "top": [(int(t), v) for t, v in zip(ti[j][:n], tv[j][:n])] if n else []})
 
     @staticmethod
     def _redraw(s: Sequence) -> bool:
@@ -537,6 +560,7 @@ class LLMEngine:
             redo = self._sample_rows(r.buf["logits"][:B][cons], [seqs[i] for i in cons])
             for i, t in zip(cons, redo):
                 nxt[i] = t
+        self._record_logprobs(r.buf["logits"][:B], seqs, nxt)
         # greedy rows take no draw; sampled rows take exactly one (re-drawn rows took theirs)
         for s in seqs:
             if s.params.temperature > 0 and not self._redraw(s):

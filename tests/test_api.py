@@ -100,3 +100,23 @@ def test_constrained_requests(client):
     r = client.post("/v1/syntropy/generate", json={"prompt": "x", "sampling": {"max_tokens": 6},
                                                    "constraint": {"choices": ["ab", "cd"]}})
     assert r.status_code == 200, r.text
+
+
+def test_openai_logprobs(client):
+    """Chat `logprobs` / `top_logprobs` and completions `logprobs: n`: one record per emitted
+    token; greedy tokens are their own top alternative; log-probabilities are <= 0."""
+    r = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 4,
+                                                  "temperature": 0, "logprobs": True, "top_logprobs": 2,
+                                                  "ignore_eos": True}).json()
+    content = r["choices"][0]["logprobs"]["content"]
+    assert len(content) == r["usage"]["completion_tokens"] == 4
+    for c in content:
+        assert c["logprob"] <= 0 and len(c["top_logprobs"]) == 2
+        assert c["top_logprobs"][0]["token"] == c["token"]
+        assert abs(c["top_logprobs"][0]["logprob"] - c["logprob"]) < 1e-6
+    r = client.post("/v1/completions", json={"prompt": "abc", "max_tokens": 3, "temperature": 0, "logprobs": 1,
+                                             "ignore_eos": True}).json()
+    lp = r["choices"][0]["logprobs"]
+    assert len(lp["tokens"]) == len(lp["token_logprobs"]) == len(lp["top_logprobs"]) == 3
+    r = client.post("/v1/completions", json={"prompt": "abc", "max_tokens": 2, "temperature": 0}).json()
+    assert "logprobs" not in r["choices"][0]
