@@ -68,10 +68,13 @@ extern "C" __attribute__((visibility("default"))) int syn_q4_gemv_dense_noalloc(
     snprintf(m, sizeof(m), "N=%d exceeds the scratch limit of %d rows", N, SYN_NOALLOC_MAX_N);
     return fail(err, err_len, -1, m);
   }
-  // the split the launcher will use must fit the fixed scratch
+  // the split the launcher will use must fit the fixed scratch: plan with the same
+  // 8-row-rounded token count the launcher plans with (a.nt_hint * 8 below)
+  const int nt_hint = (rows + 7) / 8;
+  const int plan_rows = nt_hint * 8 < 64 ? nt_hint * 8 : 64;
   int nt = 0, kr = 0;
   size_t need = 0;
-  if (!syn::q4_gemv_dense_plan(N, K, rows, &nt, &kr, &need))
+  if (!syn::q4_gemv_dense_plan(N, K, plan_rows, &nt, &kr, &need))
     return fail(err, err_len, -1, "unsupported shape: K must be a multiple of 128");
   if (need > SYN_NOALLOC_WS_FLOATS) {
     char m[200];
@@ -114,7 +117,7 @@ extern "C" __attribute__((visibility("default"))) int syn_q4_gemv_dense_noalloc(
   a.ldx = ldx;
   a.mode = mode;
   a.E = 1;
-  a.nt_hint = (rows + 7) / 8;
+  a.nt_hint = nt_hint;
   e = syn::launch_q4_gemv_dense(a, reinterpret_cast<float*>(base), reinterpret_cast<unsigned*>(base + kWsBytes),
                                 (size_t)SYN_NOALLOC_WS_FLOATS, stream);
   if (e != cudaSuccess) return fail(err, err_len, (int)e, cudaGetErrorString(e));

@@ -31,7 +31,10 @@ extern "C" {
 // The first call on a device looks up the scratch address with cudaGetSymbolAddress while
 // that device is current; make that first call before any stream capture begins.  The
 // scratch is shared by every call on a device: calls that overlap in time (two streams,
-// two host threads) race on it and must be serialised by the caller.
+// two host threads) race on it and must be serialised by the caller.  The looked-up address
+// is kept per device ordinal for the life of the process: after cudaDeviceReset (which
+// unloads the module and creates a new primary context on next use) it is stale, so a
+// process that resets a device must not call this entry point on it again.
 int syn_q4_gemv_dense_noalloc(const void* x, int rows, int ldx, const void* qw, const void* sm, void* out,
                               int N, int K, int mode, cudaStream_t stream, char* err, int err_len);
 

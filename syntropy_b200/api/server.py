@@ -58,7 +58,8 @@ def _logprobs_k(body: dict):
     per token (None when not asked)."""
     lp = body.get("logprobs")
     if lp is True:
-        return int(body.get("top_logprobs") or 0)
+        n = body.get("top_logprobs") or 0
+        return n if isinstance(n, int) and not isinstance(n, bool) else -1  # -1: rejected by the engine
     if isinstance(lp, int) and not isinstance(lp, bool):
         return lp
     return None
@@ -175,7 +176,8 @@ def build_app(aeng, tokenizer, model_id: str = "syntropy", bench_api: bool = Tru
                     line = {"event": "done", "finish_reason": ev.finish_reason, "usage": ev.usage,
                             "timings": ev.timings}
                 else:
-                    line = {"event": "error", "error": {"type": "internal", "message": ev.error}}
+                    line = {"event": "error", "error": {"type": "invalid_request" if ev.status == 400 else "internal",
+                                                        "message": ev.error}}
                 line["id"] = f"{seq}:{n}"
                 n += 1
                 yield json.dumps(line) + "\n"
@@ -215,6 +217,8 @@ def build_app(aeng, tokenizer, model_id: str = "syntropy", bench_api: bool = Tru
                         t = dec.push(ev.tokens)
                         choice = ({"index": 0, "delta": {"content": t}, "finish_reason": None} if chat else
                                   {"index": 0, "text": t, "finish_reason": None})
+                        if ev.logprobs:
+                            choice["logprobs"] = _render_logprobs(tokenizer, ev.logprobs, chat)
                         yield "data: " + json.dumps({"id": rid, "object": obj + ".chunk", "created": created,
                                                      "model": model_id, "choices": [choice]}) + "\n\n"
                     elif ev.kind == "done":
@@ -234,7 +238,7 @@ def build_app(aeng, tokenizer, model_id: str = "syntropy", bench_api: bool = Tru
             elif ev.kind == "done":
                 usage, reason, lps = ev.usage, ev.finish_reason, ev.logprobs
             elif ev.kind == "error":
-                return _err(500, "internal", ev.error)
+                return _err(ev.status, "invalid_request" if ev.status == 400 else "internal", ev.error)
         text = tokenizer.decode(toks)
         choice = ({"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason} if chat
                   else {"index": 0, "text": text, "finish_reason": reason})
@@ -302,7 +306,7 @@ def build_app(aeng, tokenizer, model_id: str = "syntropy", bench_api: bool = Tru
             elif ev.kind == "done":
                 usage, reason = ev.usage, ev.finish_reason
             elif ev.kind == "error":
-                return _err(500, "api_error", ev.error)
+                return _err(ev.status, "invalid_request_error" if ev.status == 400 else "api_error", ev.error)
         return {"id": mid, "type": "message", "role": "assistant", "model": model_id,
                 "content": [{"type": "text", "text": tokenizer.decode(toks)}],
                 "stop_reason": stop_map.get(reason, "end_turn"), "stop_sequence": None,

@@ -25,7 +25,9 @@ class GenEvent:
     error: str | None = None
     usage: dict | None = None
     timings: dict | None = None
-    logprobs: list | None = None  # on "done": per emitted token, when the request asked for them
+    status: int = 500  # "error": 400 for a request the engine rejected, 500 for a failed step
+    logprobs: list | None = None  # per emitted token, when the request asked for them: on "tokens"
+    #                               the records of that event's tokens, on "done" all of them
 
 
 class AsyncEngine:
@@ -80,7 +82,7 @@ class AsyncEngine:
                         try:
                             sid = eng.add_request(prompt, params)
                         except Exception as e:  # invalid request
-                            self._emit(loop, q, GenEvent("error", error=str(e)))
+                            self._emit(loop, q, GenEvent("error", error=str(e), status=400))
                             continue
                         ticket_to_seq[ticket] = sid
                         self._subs[sid] = (loop, q, time.perf_counter(), len(prompt))
@@ -103,6 +105,10 @@ class AsyncEngine:
             except Exception as e:  # device or internal failure: fail every live request
                 for sid, (loop, q, _, _) in list(self._subs.items()):
                     self._emit(loop, q, GenEvent("error", error=f"engine step failed: {e}"))
+                    try:  # the failed sequences leave the engine, so later requests are served
+                        eng.abort(sid)
+                    except Exception:  # noqa: BLE001
+                        pass
                 self._subs.clear()
                 continue
             METRICS.histogram("step_us").record(int((time.perf_counter() - t0) * 1e6))
@@ -111,7 +117,7 @@ class AsyncEngine:
                 if sub is None:
                     continue
                 loop, q, t_arr, n_prompt = sub
-                self._emit(loop, q, GenEvent("tokens", tokens=o.new_tokens))
+                self._emit(loop, q, GenEvent("tokens", tokens=o.new_tokens, logprobs=o.logprobs))
                 METRICS.counter("generated_tokens_total").add(len(o.new_tokens))
                 if o.finished:
                     s = eng.finished.get(o.seq_id)

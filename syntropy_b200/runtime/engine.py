@@ -21,6 +21,9 @@ from .. import ops
 from .runner import ModelRunner
 
 
+MAX_LOGPROBS = 20  # most alternatives per token a request may ask for
+
+
 @dataclass
 class SamplingParams:
     max_tokens: int = 16
@@ -76,6 +79,7 @@ class StepOutput:
     new_tokens: list
     finished: bool
     finish_reason: str | None = None
+    logprobs: list | None = None  # records of new_tokens, when the request asked for them
 
 
 class LLMEngine:
@@ -129,8 +133,16 @@ class LLMEngine:
                 raise ValueError(f"token id {t} out of range [0, {self.cfg.vocab})")
         if len(prompt) + params.max_tokens > self.runner.max_seq_len:
             raise ValueError("prompt + max_tokens exceeds max_seq_len")
-        if params.logprobs is not None and (self.spec is not None or params.logprobs < 0):
-            raise ValueError("logprobs: a count >= 0, and not with speculative decoding")
+        if params.logprobs is not None:
+            # the alternatives per token are capped like the OpenAI API's (0..20) and never
+            # beyond the vocabulary; speculative steps and pipeline stages do not record them
+            n = params.logprobs
+            if isinstance(n, bool) or not isinstance(n, int) or not 0 <= n <= min(MAX_LOGPROBS, self.cfg.vocab):
+                raise ValueError(f"logprobs: an integer count in 0..{min(MAX_LOGPROBS, self.cfg.vocab)}")
+            if self.spec is not None:
+                raise ValueError("logprobs are not recorded with speculative decoding")
+            if self.runner.pp is not None:
+                raise ValueError("logprobs are not recorded under pipeline parallelism")
         kv = self.runner.kv
         pool = kv.alloc.num_blocks - kv.alloc.reserved
         if kv.blocks_needed(len(prompt) + params.max_tokens) > pool:
@@ -387,7 +399,7 @@ class LLMEngine:
             return
         lp = torch.log_softmax(logits[rows].float(), -1)
         chosen = lp.gather(1, torch.tensor([toks[i] for i in rows], device=lp.device)[:, None])[:, 0].cpu().tolist()
-        k = max(seqs[i].params.logprobs for i in rows)
+        k = min(max(seqs[i].params.logprobs for i in rows), lp.shape[-1])
         tv, ti = lp.topk(k, -1) if k else (None, None)
         tv, ti = (tv.cpu().tolist(), ti.cpu().tolist()) if k else ([], [])
         for j, i in enumerate(rows):
@@ -589,7 +601,8 @@ class LLMEngine:
         if reason:
             s.finish_reason = reason
             s.status = "finished"
-        return StepOutput(s.seq_id, [int(tok)], reason is not None, reason)
+        lp = s.logprobs[-1:] if s.params.logprobs is not None and len(s.logprobs) == len(s.output) else None
+        return StepOutput(s.seq_id, [int(tok)], reason is not None, reason, lp)
 
     def _finish(self, s: Sequence, reason: str):
         s.status = "finished"

@@ -120,3 +120,32 @@ def test_openai_logprobs(client):
     assert len(lp["tokens"]) == len(lp["token_logprobs"]) == len(lp["top_logprobs"]) == 3
     r = client.post("/v1/completions", json={"prompt": "abc", "max_tokens": 2, "temperature": 0}).json()
     assert "logprobs" not in r["choices"][0]
+
+
+def test_oversized_logprobs_rejected_and_server_keeps_serving(client):
+    """A logprobs count beyond the cap (20) or the vocabulary is a 400 for that request only;
+    the engine keeps serving the next one."""
+    r = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 2,
+                                                  "logprobs": True, "top_logprobs": 5000})
+    assert r.status_code == 400, r.text
+    r = client.post("/v1/completions", json={"prompt": "abc", "max_tokens": 2, "logprobs": 21})
+    assert r.status_code == 400, r.text
+    r = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 3,
+                                                  "temperature": 0, "ignore_eos": True, "logprobs": True,
+                                                  "top_logprobs": 20})
+    assert r.status_code == 200, r.text
+    assert all(len(c["top_logprobs"]) == 20 for c in r.json()["choices"][0]["logprobs"]["content"])
+
+
+def test_streamed_logprobs(client):
+    """With stream=true every token chunk carries its logprobs record."""
+    r = client.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 3,
+                                                  "temperature": 0, "logprobs": True, "top_logprobs": 1,
+                                                  "ignore_eos": True, "stream": True})
+    assert r.status_code == 200
+    chunks = [json.loads(line[6:]) for line in r.text.splitlines() if line.startswith("data: {")]
+    recs = [c["choices"][0]["logprobs"]["content"] for c in chunks if "logprobs" in c["choices"][0]]
+    assert sum(len(x) for x in recs) == 3
+    for x in recs:
+        for c in x:
+            assert c["logprob"] <= 0 and c["top_logprobs"][0]["token"] == c["token"]

@@ -48,3 +48,27 @@ def test_logprobs_rejected_with_speculation():
     eng = LLMEngine(ModelRunner(mw, max_batch=2, max_seq_len=48), spec=SpecConfig(gamma=2, drafter=NgramDrafter()))
     with pytest.raises(ValueError, match="logprobs"):
         eng.add_request([1, 2, 3], SamplingParams(max_tokens=4, logprobs=1))
+
+
+def test_logprobs_count_is_capped():
+    """Counts outside 0..20 (or above the vocabulary) are refused at intake; the cap itself works."""
+    cfg = get_config("tiny-llama")
+    mw = prepare_weights(cfg, "cpu", max_pos=64)
+    eng = LLMEngine(ModelRunner(mw, max_batch=2, max_seq_len=48))
+    for bad in (-1, 21, 10 ** 6, True, 1.5):
+        with pytest.raises(ValueError, match="logprobs"):
+            eng.add_request([1, 2, 3], SamplingParams(max_tokens=2, logprobs=bad))
+    sid = eng.add_request([1, 2, 3], SamplingParams(max_tokens=2, logprobs=20))
+    while eng.has_work():
+        eng.step()
+    assert all(len(r["top"]) == 20 for r in eng.finished[sid].logprobs)
+
+
+def test_logprobs_rejected_under_pipeline_parallelism():
+    cfg = get_config("tiny-llama")
+    mw = prepare_weights(cfg, "cpu", max_pos=64)
+    runner = ModelRunner(mw, max_batch=2, max_seq_len=48)
+    runner.pp = object()  # any pipeline group: the intake check only looks for its presence
+    eng = LLMEngine(runner)
+    with pytest.raises(ValueError, match="pipeline"):
+        eng.add_request([1, 2, 3], SamplingParams(max_tokens=2, logprobs=1))
