@@ -110,7 +110,11 @@ def main():
                     help="share of each layer's host-tier experts computed by host CPU threads during decode "
                          "(the rest is read over PCIe by the GPU); 0 = off (default 0.75 on one GPU with a VRAM "
                          "cap, else 0)")
-    ap.add_argument("--cpu-threads", type=int, default=None, help="CPU expert threads (default: all but two cores)")
+    ap.add_argument("--cpu-threads", type=int, default=None,
+                    help="CPU expert threads per rank (default: the rank's share of the node's cores, less one)")
+    ap.add_argument("--step-profile", action="store_true",
+                    help="after the timed steps, replay one decode step through the timestamped graph variant and "
+                         "report device ms per segment kind (max over ranks)")
     ap.add_argument("--no-mtp", action="store_true", help="models with an MTP head: plain decoding instead of "
                     "MTP drafting + batched verification")
     args = ap.parse_args()
@@ -122,8 +126,6 @@ def main():
     args.decode = args.decode or dd
     if args.expert_cache_frac is None:
         args.expert_cache_frac = 0.6 if args.model == "qwen3-235b-a22b" else 1.0
-    if args.cpu_experts is None:
-        args.cpu_experts = 0.75 if args.expert_cache_frac < 1.0 else 0.0
 
     import torch
 
@@ -202,10 +204,20 @@ def main():
                          use_graphs=graphs)
     runner.expert_cache = cache
     tier = None
-    if cache is not None and args.cpu_experts > 0 and ep is None and tp is None and pp is None:
-        from syntropy_b200.experts.cpu_tier import CpuExpertTier
-        tier = CpuExpertTier(cache, cfg, max_rows=runner.max_batch, cpu_share=args.cpu_experts,
-                             threads=args.cpu_threads)
+    if cache is not None and tp is None and pp is None and (ep is None or ep.fused) and cfg.weight_quant == "q4":
+        # the host CPU computes a share of each rank's cold experts; the node's cores are split
+        # over its ranks (each rank's slice, less its launching thread's core)
+        from syntropy_b200.experts.cpu_tier import CpuExpertTier, balanced_share, rank_cpus
+        local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+        cpus, _ = rank_cpus(local, local_world)
+        threads = args.cpu_threads or len(cpus)
+        if args.cpu_experts is None:  # one GPU: the measured best share; else the balanced one
+            args.cpu_experts = 0.75 if world == 1 else balanced_share(threads, local_world)
+        if args.cpu_experts > 0 and threads > 0:
+            tier = CpuExpertTier(cache, cfg, max_rows=runner.max_batch, cpu_share=args.cpu_experts,
+                                 threads=threads, cpus=cpus, ep=ep)
+    if args.cpu_experts is None:
+        args.cpu_experts = 0.0
     spec = None
     if use_mtp:
         from syntropy_b200.runtime.spec import MTPDrafter, SpecConfig
@@ -279,6 +291,29 @@ def main():
         drf = sum_over_ranks(ctx, float(eng.stats["spec_drafted"] - dr0))
         mtp_info = {"acceptance_rate": round(acc / max(1.0, drf), 4), "drafted": int(drf), "accepted": int(acc),
                     "tokens_per_seq_step": round(timed_tokens / (args.batch * args.steps), 4)}
+    step_prof = None
+    if args.step_profile and runner.use_graphs:
+        # one decode step through the timestamped graph variant (same kernels plus one
+        # %globaltimer write per segment): device ms per segment kind, max over ranks
+        runner.profile_next = True
+        eng.step()
+        agg = {}
+        for lab, ms in runner.step_profile():
+            kind = lab.split(".")[-1]
+            agg[kind] = agg.get(kind, 0.0) + ms
+        kinds = sorted(agg)
+        if ctx.enabled:
+            import torch.distributed as dist
+            allk = [None] * world
+            dist.all_gather_object(allk, agg, group=ctx.cpu_group)
+            kinds = sorted({k for a in allk for k in a})
+            step_prof = {k: round(max(a.get(k, 0.0) for a in allk), 4) for k in kinds}
+            step_prof["rank0"] = {k: round(allk[0].get(k, 0.0), 4) for k in kinds}
+        else:
+            step_prof = {k: round(agg[k], 4) for k in kinds}
+        step_prof["host_lockstep_ms_per_step"] = round(1e3 * eng.stats.get("lockstep_s", 0.0) /
+                                                       max(1, eng.stats["decode_steps"] + eng.stats["prefill_steps"]),
+                                                       4)
     status = ep.check_status() if ep is not None else 0
     tier_stats = tier.stats() if tier is not None else None
     uncapped = None
@@ -331,7 +366,8 @@ def main():
                    "expert_prefetch": bool(cache is not None and cache.prefetch),
                    "expert_rebalance_every": args.rebalance_every if cache is not None else 0,
                    "cpu_expert_share": args.cpu_experts if tier is not None else 0.0,
-                   "cpu_expert_threads": tier.threads if tier is not None else 0,
+                   "cpu_expert_threads": tier.threads if tier is not None else 0,  # per rank
+                   "host_cores": len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else None,
                    "l2": f"inputs larger than L2 ({mw.nbytes() / 1e9:.0f} GB of weights streamed per step per rank)",
                    "weights_gb": round(mw.nbytes() / 1e9, 2), "weight_build_s": round(t_weights, 1)},
         "clocks": clk.summary(),
@@ -345,6 +381,8 @@ def main():
     }
     if mtp_info is not None:
         out["mtp"] = mtp_info
+    if step_prof is not None:
+        out["step_profile_ms"] = step_prof
     if rank == 0:
         print(json.dumps(out))
     runner.graphs.clear()

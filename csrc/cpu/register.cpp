@@ -37,6 +37,7 @@ void register_all(pybind11::module& m) {
   m.def("moe_topk", &moe_topk);
   m.def("cpu_handoff", &cpu_handoff);
   m.def("cpu_collect", &cpu_collect);
+  m.def("cpu_collect_ep", &cpu_collect_ep);
   m.def("argmax", &argmax);
   m.def("sample", &sample);
   m.def("philox", &philox);

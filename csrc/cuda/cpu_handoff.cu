@@ -73,8 +73,26 @@ __global__ void __launch_bounds__(256) cpu_collect_kernel(CpuCollectArgs a) {
   for (int i = blockIdx.x; i < n_out; i += gridDim.x) {
     const int p = __ldcv(pairs + i);
     if (p < 0 || p >= a.max_rows * a.k) continue;
-    float4* y = reinterpret_cast<float4*>(a.yp + (int64_t)p * a.H);
+    float4* y = a.pair_dst ? reinterpret_cast<float4*>(a.pair_dst[p])
+                           : reinterpret_cast<float4*>(a.yp + (int64_t)p * a.H);
+    if (y == nullptr) continue;
     for (int c = threadIdx.x; c < H4; c += blockDim.x) y[c] = __ldcv(out + (int64_t)i * H4 + c);
+  }
+  if (a.sig_n > 0) {
+    // the GEMV of this layer left the flags to this kernel: every CTA publishes its stores,
+    // the last one to arrive raises every rank's flag (counter reset before the release)
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned prev = atomicAdd(a.done_ctr, 1u);
+      if (prev == gridDim.x - 1) {
+        *a.done_ctr = 0u;
+        __threadfence_system();
+        const uint32_t seq = (*a.step_ctr) * (uint32_t)a.n_layers + (uint32_t)a.layer + 1u;
+        for (int q = 0; q < a.sig_n; ++q)
+          st_release_sys(reinterpret_cast<uint32_t*>(a.sig_peers[q] + a.sig_off) + a.sig_rank, seq);
+      }
+    }
   }
 }
 

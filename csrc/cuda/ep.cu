@@ -105,61 +105,83 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(EpArgs a, const __nv_b
   }
 }
 
-// 1 CTA x 1024 threads on the owner rank.
+// 1 CTA x 1024 threads on the owner rank.  Every source's routing metadata is staged in
+// shared memory once (coalesced loads after the bounded flag waits); then one warp per local
+// expert scans the (source, slot, choice) entries in order with ballots: a first pass counts
+// the expert's pairs, warp 0 scans the counts into the CSR offsets, a second pass writes each
+// pair at its ordered position.  The order, and so the output, is deterministic.
 __global__ void __launch_bounds__(1024) ep_build_kernel(EpArgs a, int32_t* __restrict__ tok_off,
                                                         int32_t* __restrict__ tok_idx, float* __restrict__ pair_w,
                                                         int64_t* __restrict__ pair_dst) {
+  extern __shared__ int32_t s_meta[];  // [N * cap][MS]
   __shared__ int s_cnt[512];
+  __shared__ int s_base[512];
   __shared__ int s_src_cnt[64];
   uint8_t* mine = reinterpret_cast<uint8_t*>(a.peers[a.rank]);
   const uint32_t seq = ep_seq(a.step_ctr, a.n_layers, a.layer);
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, n_warps = blockDim.x >> 5;
   if (tid < a.N) {
     const uint32_t* f = reinterpret_cast<const uint32_t*>(mine + a.off_flag_disp) + tid;
     const bool ok = wait_flag(f, seq, a.timeout_ns, a.status, 0);
-    s_src_cnt[tid] = ok ? reinterpret_cast<volatile int32_t*>(mine + a.off_cnt)[tid] : 0;
+    const int c = ok ? __ldcg(reinterpret_cast<const int32_t*>(mine + a.off_cnt) + tid) : 0;
+    s_src_cnt[tid] = c < 0 ? 0 : (c > a.cap ? a.cap : c);
   }
-  for (int e = tid; e < a.E_loc; e += blockDim.x) s_cnt[e] = 0;
   __syncthreads();
   const int MS = 1 + 3 * a.k;
+  const int rows = a.N * a.cap;
   const int32_t* meta = reinterpret_cast<const int32_t*>(mine + a.off_meta);
-  // counts per local expert
-  for (int s = 0; s < a.N; ++s) {
-    const int n = min(s_src_cnt[s], a.cap);
-    for (int idx = tid; idx < n * a.k; idx += blockDim.x) {
-      const int slot = idx / a.k, j = idx % a.k;
-      const int el = meta[((int64_t)s * a.cap + slot) * MS + 1 + 3 * j];
-      if (el >= 0) atomicAdd(&s_cnt[el], 1);
-    }
+  for (int i = tid; i < rows * MS; i += blockDim.x) {
+    const int row = i / MS;
+    const bool valid = (row % a.cap) < s_src_cnt[row / a.cap];
+    s_meta[i] = valid ? __ldcg(meta + i) : -1;  // an invalid slot routes to no expert
   }
   __syncthreads();
-  if (tid == 0) {
-    int acc = 0;
-    for (int e = 0; e < a.E_loc; ++e) {
-      tok_off[e] = acc;
-      const int c = s_cnt[e];
-      s_cnt[e] = acc;
-      acc += c;
+  const int n_ent = rows * a.k;
+  for (int e = warp; e < a.E_loc; e += n_warps) {
+    int c = 0;
+    for (int b = 0; b < n_ent; b += 32) {
+      const int idx = b + lane;
+      const int el = idx < n_ent ? s_meta[(idx / a.k) * MS + 1 + 3 * (idx % a.k)] : -1;
+      c += __popc(__ballot_sync(0xffffffffu, el == e));
     }
-    tok_off[a.E_loc] = acc;
+    if (lane == 0) s_cnt[e] = c;
   }
   __syncthreads();
-  // fill in (source, slot) order per expert: deterministic
-  for (int e = tid; e < a.E_loc; e += blockDim.x) {
-    int p = s_cnt[e];
-    for (int s = 0; s < a.N; ++s) {
-      const int n = min(s_src_cnt[s], a.cap);
-      for (int slot = 0; slot < n; ++slot) {
-        const int32_t* mrow = meta + ((int64_t)s * a.cap + slot) * MS;
-        for (int j = 0; j < a.k; ++j) {
-          if (mrow[1 + 3 * j] == e) {
-            tok_idx[p] = s * a.cap + slot;
-            pair_w[p] = __int_as_float(mrow[2 + 3 * j]);
-            pair_dst[p] = a.peers[s] + a.off_comb + (int64_t)mrow[3 + 3 * j] * a.H * 4;
-            ++p;
-          }
-        }
+  if (warp == 0) {
+    int carry = 0;
+    for (int e0 = 0; e0 < a.E_loc; e0 += 32) {
+      const int e = e0 + lane;
+      const int c = e < a.E_loc ? s_cnt[e] : 0;
+      int v = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
       }
+      if (e < a.E_loc) {
+        s_base[e] = carry + v - c;
+        tok_off[e] = carry + v - c;
+      }
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) tok_off[a.E_loc] = carry;
+  }
+  __syncthreads();
+  for (int e = warp; e < a.E_loc; e += n_warps) {
+    int p = s_base[e];
+    for (int b = 0; b < n_ent; b += 32) {
+      const int idx = b + lane;
+      const int row = idx / a.k, j = idx % a.k;
+      const int el = idx < n_ent ? s_meta[row * MS + 1 + 3 * j] : -1;
+      const unsigned m = __ballot_sync(0xffffffffu, el == e);
+      if (el == e) {
+        const int q = p + __popc(m & ((1u << lane) - 1u));
+        const int32_t* mrow = s_meta + row * MS;
+        tok_idx[q] = row;  // = source * cap + slot: the received row
+        pair_w[q] = __int_as_float(mrow[2 + 3 * j]);
+        pair_dst[q] = a.peers[row / a.cap] + a.off_comb + (int64_t)mrow[3 + 3 * j] * a.H * 4;
+      }
+      p += __popc(m);
     }
   }
 }
@@ -247,7 +269,13 @@ cudaError_t launch_ep_dispatch(const EpArgs& a, const void* h, const int32_t* id
 cudaError_t launch_ep_build(const EpArgs& a, int32_t* tok_off, int32_t* tok_idx, float* pair_w, int64_t* pair_dst,
                             cudaStream_t s) {
   if (a.E_loc > 512 || a.N > 64) return cudaErrorInvalidValue;
-  ep_build_kernel<<<1, 1024, 0, s>>>(a, tok_off, tok_idx, pair_w, pair_dst);
+  const size_t smem = (size_t)a.N * a.cap * (1 + 3 * a.k) * sizeof(int32_t);
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(ep_build_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  ep_build_kernel<<<1, 1024, smem, s>>>(a, tok_off, tok_idx, pair_w, pair_dst);
   return cudaGetLastError();
 }
 

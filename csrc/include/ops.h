@@ -105,6 +105,10 @@ void cpu_handoff(torch::Tensor h, torch::Tensor tok_off, torch::Tensor tok_idx, 
                  int64_t k, int64_t max_rows, int64_t mailbox, int64_t layer, torch::Tensor ctr);
 void cpu_collect(int64_t mailbox, int64_t E, int64_t k, int64_t max_rows, torch::Tensor ctr, torch::Tensor yp,
                  double timeout_s, torch::Tensor status);
+void cpu_collect_ep(int64_t mailbox, int64_t E, int64_t k, int64_t max_rows, int64_t H, torch::Tensor ctr,
+                    torch::Tensor pair_dst, double timeout_s, torch::Tensor status, torch::Tensor peers,
+                    int64_t sig_off, int64_t sig_rank, torch::Tensor step_ctr, int64_t n_layers, int64_t layer,
+                    torch::Tensor done_ctr);
 void register_dispatcher(pybind11::module& m);
 void register_tier(pybind11::module& m);
 void register_cpu_experts(pybind11::module& m);

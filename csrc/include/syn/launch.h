@@ -190,6 +190,16 @@ struct CpuCollectArgs {
   float* yp;              // [B*k, H] pair outputs of the grouped GEMVs (device)
   uint64_t timeout_ns;
   int* status;            // bit 0: the CPU did not answer in time; bit 1: the CPU reported bad input
+  // expert parallelism: pair p's row goes to the address pair_dst[p] (a source rank's combine
+  // slot, possibly in a peer's memory) instead of yp; then, when sig_n > 0, the completion
+  // flags of this layer are release-stored into every rank's region (flag array at sig_off,
+  // slot sig_rank, value step * n_layers + layer + 1), as the down-projection GEMV does
+  const int64_t* pair_dst;
+  const int64_t* sig_peers;
+  int64_t sig_off;
+  int sig_n, sig_rank, n_layers, layer;
+  const uint32_t* step_ctr;
+  unsigned* done_ctr;     // CTA arrival counter (zero between launches)
 };
 cudaError_t launch_cpu_handoff(const CpuHandoffArgs& a, cudaStream_t s);
 cudaError_t launch_cpu_collect(const CpuCollectArgs& a, cudaStream_t s);

@@ -420,7 +420,8 @@ void q4_gemv_ep(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, t
   a.mode = 4;
   a.E = (int)qw_ptrs.numel();
   a.out_ptrs = out_ptrs.data_ptr<int64_t>();
-  a.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr());
+  // an empty done_ctr: this launch raises no flags (a later kernel of the layer does)
+  a.done_ctr = done_ctr.numel() ? reinterpret_cast<unsigned*>(done_ctr.data_ptr()) : nullptr;
   a.sig_peers = peers.data_ptr<int64_t>();
   a.sig_off = sig_off;
   a.sig_n = (int)peers.numel();
@@ -504,7 +505,8 @@ void q4_gemv_tp(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, t
   a.ldx = (int)x.stride(0);
   a.mode = 6;
   a.E = (int)qw_ptrs.numel();
-  a.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr());
+  // an empty done_ctr: this launch raises no flags (a later kernel of the layer does)
+  a.done_ctr = done_ctr.numel() ? reinterpret_cast<unsigned*>(done_ctr.data_ptr()) : nullptr;
   a.sig_peers = peers.data_ptr<int64_t>();
   a.sig_off = sig_off;
   a.sig_n = (int)peers.numel();
@@ -853,7 +855,49 @@ void cpu_collect(int64_t mailbox, int64_t E, int64_t k, int64_t max_rows, torch:
   a.yp = yp.data_ptr<float>();
   a.timeout_ns = (uint64_t)(timeout_s * 1e9);
   a.status = status.data_ptr<int32_t>();
+  a.pair_dst = nullptr;
+  a.sig_peers = nullptr;
+  a.sig_off = 0;
+  a.sig_n = a.sig_rank = a.n_layers = a.layer = 0;
+  a.step_ctr = nullptr;
+  a.done_ctr = nullptr;
   const at::cuda::CUDAGuard guard(yp.device());
+  SYN_CHECK_CUDA(launch_cpu_collect(a, cur_stream()));
+}
+
+// Expert-parallel form: the CPU's rows go to pair_dst[p] (source ranks' combine slots over
+// NVLink), then this layer's completion flags are raised in every rank's region (the
+// down-projection GEMV ran without raising them).
+void cpu_collect_ep(int64_t mailbox, int64_t E, int64_t k, int64_t max_rows, int64_t H, torch::Tensor ctr,
+                    torch::Tensor pair_dst, double timeout_s, torch::Tensor status, torch::Tensor peers,
+                    int64_t sig_off, int64_t sig_rank, torch::Tensor step_ctr, int64_t n_layers, int64_t layer,
+                    torch::Tensor done_ctr) {
+  TORCH_CHECK(ctr.is_cuda() && status.is_cuda() && status.scalar_type() == torch::kInt32, "device ctr / status");
+  TORCH_CHECK(pair_dst.is_cuda() && pair_dst.scalar_type() == torch::kInt64 && pair_dst.numel() >= max_rows * k,
+              "pair_dst int64 [max_rows * k]");
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == torch::kInt64, "peers int64");
+  TORCH_CHECK(done_ctr.is_cuda() && done_ctr.scalar_type() == torch::kInt32 && done_ctr.numel() >= 1, "done_ctr");
+  TORCH_CHECK(step_ctr.is_cuda(), "step_ctr");
+  CpuCollectArgs a;
+  a.mb = reinterpret_cast<const uint8_t*>(mailbox);
+  a.H = (int)H;
+  a.E = (int)E;
+  a.k = (int)k;
+  a.max_rows = (int)max_rows;
+  a.ctr = reinterpret_cast<const uint32_t*>(ctr.data_ptr<int32_t>());
+  a.yp = nullptr;
+  a.timeout_ns = (uint64_t)(timeout_s * 1e9);
+  a.status = status.data_ptr<int32_t>();
+  a.pair_dst = pair_dst.data_ptr<int64_t>();
+  a.sig_peers = peers.data_ptr<int64_t>();
+  a.sig_off = sig_off;
+  a.sig_n = (int)peers.numel();
+  a.sig_rank = (int)sig_rank;
+  a.n_layers = (int)n_layers;
+  a.layer = (int)layer;
+  a.step_ctr = reinterpret_cast<const uint32_t*>(step_ctr.data_ptr());
+  a.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr());
+  const at::cuda::CUDAGuard guard(pair_dst.device());
   SYN_CHECK_CUDA(launch_cpu_collect(a, cur_stream()));
 }
 

@@ -29,13 +29,50 @@ import torch
 from .._ext import ext
 
 
+# Host-tier rates used to split each rank's cold experts between its CPU workers and its PCIe
+# link (bytes of 4-bit weights per second).  Measured on the B200 node: the AVX-512 BF16 pool
+# moves ~4.8 GB/s per worker thread; one GPU reads host rows in place at ~30-40 GB/s while the
+# CPU also streams DRAM, and ~25 GB/s per GPU when the two GPUs behind one PCIe switch read at
+# once.
+CPU_GBS_PER_THREAD = 4.8
+PCIE_GBS_ALONE, PCIE_GBS_SHARED = 35.0, 25.0
+
+
+def rank_cpus(local_rank: int, local_world: int, allowed: list[int] | None = None) -> tuple[list[int], list[int]]:
+    """Disjoint host cores for the CPU expert workers of each rank on one node: the allowed
+    cores are split evenly over the node's ranks; each rank keeps its slice's first core for
+    its launching thread (one rank alone keeps two) and gives the rest to its workers.
+    Returns (worker cores, launcher cores)."""
+    if allowed is None:
+        allowed = sorted(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else []
+    if local_world <= 1:
+        return (allowed[2:] if len(allowed) > 4 else allowed), allowed[:2]
+    n = len(allowed)
+    part = allowed[local_rank * n // local_world: (local_rank + 1) * n // local_world]
+    if len(part) < 2:
+        return part, part
+    return part[1:], part[:1]
+
+
+def balanced_share(threads: int, local_world: int) -> float:
+    """CPU share of the host tier that makes the CPU workers and the PCIe reads of one rank
+    finish together (the two run at the same time during a layer)."""
+    cpu = threads * CPU_GBS_PER_THREAD
+    pcie = PCIE_GBS_ALONE if local_world <= 1 else PCIE_GBS_SHARED
+    return round(cpu / (cpu + pcie), 2)
+
+
 class CpuExpertTier:
     """Owns the mailbox, the CPU thread pool and the split of each layer's host experts."""
 
     def __init__(self, cache, cfg, max_rows: int, cpu_share: float = 0.75, threads: int | None = None,
-                 cpus: list[int] | None = None, timeout_s: float = 2.0, mode: int = -1):
+                 cpus: list[int] | None = None, timeout_s: float = 2.0, mode: int = -1, ep=None):
         self.cache, self.cfg = cache, cfg
+        self.ep = ep  # parallel.ep.EPGroup: this rank's experts for the rows every rank dispatched
         self.E, self.k, self.H, self.I = cfg.n_experts, cfg.top_k, cfg.hidden, cfg.moe_ffn
+        if ep is not None:  # the mailbox carries the owner's CSR over its local experts
+            self.E = ep.E_loc
+            max_rows = ep.N * ep.cap
         self.max_rows = max_rows
         self.cpu_share = cpu_share
         self.timeout_s = timeout_s
@@ -69,7 +106,7 @@ class CpuExpertTier:
             mine = set(host[:n_cpu])
             b.cpu_owned = mine
             for e in range(b.E):
-                eg = b.e0 + e
+                eg = e if self.ep is not None else b.e0 + e  # local ids under expert parallelism
                 if e in mine:
                     h = b.host_of[e]
                     gu, dn = b.parts
@@ -88,6 +125,21 @@ class CpuExpertTier:
         """Publish layer L's rows (bf16 [B, H]) and routing CSR to the CPU threads."""
         ext().cpu_handoff(h, mb["tok_off"], mb["tok_idx"], mb["pair_w"], self.E, self.k, self.max_rows,
                           self.mb_ptr, self.layer_of[id(L)], self.ctr)
+
+    def handoff_ep(self, layer_of_cache: int, recv_x, tok_off, tok_idx, pair_w):
+        """Expert parallelism: publish every rank's rows received for this rank's experts
+        (bf16 [N * cap, H]) and the owner CSR built by ep_build."""
+        ext().cpu_handoff(recv_x, tok_off, tok_idx, pair_w, self.E, self.k, self.max_rows, self.mb_ptr,
+                          layer_of_cache, self.ctr)
+
+    def collect_ep(self, pair_dst, layer: int):
+        """Expert parallelism: wait for the CPU's rows, store each into its source rank's
+        combine slot (pair_dst, over NVLink), then raise this layer's completion flags on every
+        rank (the down-projection GEMV of this layer left them to this kernel)."""
+        ep = self.ep
+        ext().cpu_collect_ep(self.mb_ptr, self.E, self.k, self.max_rows, self.H, self.ctr, pair_dst,
+                             self.timeout_s, self.status, ep.region.peers, ep.off_flag_comb, ep.rank, ep.step_ctr,
+                             ep.n_layers, layer, ep.collect_ctr)
 
     def collect(self, yp):
         """Wait for the CPU's rows and place them into the pair outputs yp (f32 [B*k, H])."""

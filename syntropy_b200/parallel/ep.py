@@ -66,6 +66,8 @@ class EPGroup:
             self.step_ctr = torch.zeros(1, dtype=torch.int32, device=dev)
             self.status = torch.zeros(1, dtype=torch.int32, device=dev)
             self.done_ctr = torch.zeros(n_layers, dtype=torch.int32, device=dev)
+            self.collect_ctr = torch.zeros(1, dtype=torch.int32, device=dev)  # CPU-tier collect arrivals
+            self._no_flags = torch.empty(0, dtype=torch.int32, device=dev)
             P = N * cap * k
             self.tok_off = torch.zeros(self.E_loc + 1, dtype=torch.int32, device=dev)
             self.tok_idx = torch.zeros(P, dtype=torch.int32, device=dev)
@@ -82,21 +84,42 @@ class EPGroup:
         if self.fused:
             ext().ep_step_begin(self.step_ctr)
 
-    def moe_decode_fused(self, layer: int, h, topk_ids, topk_w, x, gu, dn, mid, next_norm, h_out, eps):
-        """One MoE layer for the local rows (h: bf16 [T, H]) through NVLink dispatch/combine."""
+    def moe_decode_fused(self, layer: int, h, topk_ids, topk_w, x, gu, dn, mid, next_norm, h_out, eps,
+                         stamp=None, tier=None, L=None):
+        """One MoE layer for the local rows (h: bf16 [T, H]) through NVLink dispatch/combine.
+        stamp: device-timestamp callback of a profiled step; tier: the host CPU expert tier,
+        which computes its share of this rank's cold experts for every rank's rows while the
+        GPU runs the rest (its rows reach the sources' combine slots over NVLink); L: the
+        model layer (its expert banks tell which experts the CPU owns)."""
         e = ext()
         c = self._common(layer)
+        stamp = stamp or (lambda _lab: None)
         e.ep_dispatch(*c, h, topk_ids, topk_w)
+        stamp(f"layer{layer}.dispatch")
         e.ep_build(*c, self.tok_off, self.tok_idx, self.pair_w, self.pair_dst)
+        stamp(f"layer{layer}.build")
+        # every layer hands off when a tier exists (the CPU answers with no rows for a layer whose
+        # cold experts it does not own), so ownership changes between steps need no new capture
+        cpu = tier is not None and L is not None and id(L) in tier.layer_of
+        if cpu:
+            tier.handoff_ep(tier.layer_of[id(L)], self.recv_x, self.tok_off, self.tok_idx, self.pair_w)
+            ops.core._launched()
         P = self.N * self.cap * self.k
         ops.linear_grouped(self.recv_x, gu, self.tok_off, self.tok_idx, mid[:P], ops.GEMV_SWIGLU,
                            qw_ptrs=gu.qw_ptrs, sm_ptrs=gu.sm_ptrs)
+        stamp(f"layer{layer}.gate_up")
         e.q4_gemv_ep(mid[:P], dn.qw_ptrs, dn.sm_ptrs, self.tok_off, torch.empty(0, dtype=torch.int32, device=h.device),
-                     self.pair_w, self.pair_dst, dn.N, dn.K, self.done_ctr[layer:layer + 1], self.region.peers,
-                     self.off_flag_comb, self.rank, self.step_ctr, self.n_layers, layer,
+                     self.pair_w, self.pair_dst, dn.N, dn.K, self._no_flags if cpu else self.done_ctr[layer:layer + 1],
+                     self.region.peers, self.off_flag_comb, self.rank, self.step_ctr, self.n_layers, layer,
                      ops.moe_nt_hint(self.N * h.shape[0] * self.k // self.N, self.E_loc), self.E_loc,
                      bool(getattr(dn, "bank_contiguous", False)))
+        stamp(f"layer{layer}.down")
+        if cpu:  # the CPU's rows, then this layer's completion flags
+            tier.collect_ep(self.pair_dst, layer)
+            ops.core._launched()
+            stamp(f"layer{layer}.cpu_wait")
         e.ep_combine(*c, x, next_norm if next_norm is not None else torch.empty(0, device=h.device), h_out, eps)
+        stamp(f"layer{layer}.combine")
         ops.core._launched(5)
 
     def check_status(self) -> int:

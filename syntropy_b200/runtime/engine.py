@@ -306,8 +306,10 @@ class LLMEngine:
 
     def _step_lockstep(self) -> list[StepOutput]:
         import torch.distributed as dist
+        t0 = time.perf_counter()
         want = torch.tensor([1 if self._can_admit() else 0, 1 if self.running else 0], dtype=torch.int64)
         dist.all_reduce(want, op=dist.ReduceOp.MAX, group=self.dist.cpu_group)
+        self.stats["lockstep_s"] = self.stats.get("lockstep_s", 0.0) + time.perf_counter() - t0
         if want[0]:
             return self._prefill(self._admit())
         if want[1]:

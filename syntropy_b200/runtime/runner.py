@@ -205,7 +205,7 @@ class ModelRunner:
         x, h = b["x"][:B], b["h"][:B]
         if self._stamping:
             if self._stamp_buf is None:
-                self._stamp_buf = torch.zeros(4 * len(mw.layers) + 8, dtype=torch.int64, device=self.device)
+                self._stamp_buf = torch.zeros(12 * len(mw.layers) + 8, dtype=torch.int64, device=self.device)
             self._stamp_n = 0
             self._stamp_labels = []
         self._stamp("start")
@@ -325,6 +325,7 @@ class ModelRunner:
         # padding rows of the bucket (slot -1) route too, but are not counted
         ops.moe_topk(rl, cfg, L.router_bias, pred, mb, counts=self._counts_of(layer),
                      count_rows=self.desc.d["slot"][:B])
+        self._stamp(f"layer{layer}.route")
         if nxt_moe:
             # router-predicted prefetch of layer+1's host experts, overlapping this layer
             cur = torch.cuda.current_stream(self.device)
@@ -344,7 +345,8 @@ class ModelRunner:
         gu, dn = L.experts_gu, L.experts_down
         if ep is not None:
             ep.moe_decode_fused(layer, h, mb["topk_ids"], mb["topk_w"], x, gu, dn, b["moe_mid"], nw, h,
-                                cfg.rms_eps)
+                                cfg.rms_eps, stamp=self._stamp if self._stamping else None,
+                                tier=cache.cpu_tier if cache is not None else None, L=L)
             return
         mid = b["moe_mid"][:B * k]
         yp = b["moe_out"][:B * k]
@@ -355,11 +357,14 @@ class ModelRunner:
         shared = self._shared_expert(L, h) if L.shared_gu is not None else None
         ops.linear_grouped(h, gu, mb["tok_off"], mb["tok_idx"], mid, ops.GEMV_SWIGLU,
                            qw_ptrs=gu.qw_ptrs, sm_ptrs=gu.sm_ptrs)
+        self._stamp(f"layer{layer}.gate_up")
         ops.linear_grouped(mid, dn, mb["tok_off"], None, yp, ops.GEMV_SCALED_F32, route_w=mb["pair_w"],
                            qw_ptrs=dn.qw_ptrs, sm_ptrs=dn.sm_ptrs)
+        self._stamp(f"layer{layer}.down")
         if tier is not None:
             tier.collect(yp)
             ops.core._launched()
+            self._stamp(f"layer{layer}.cpu_wait")
         if self.tp is not None:
             # every expert holds 1/N of its FFN width here: combine the partial outputs, sum them
             # over the TP group (NCCL, captured in the decode graphs), then residual + next norm

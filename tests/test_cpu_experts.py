@@ -91,3 +91,18 @@ def test_worker_pool_through_mailbox():
         assert st["jobs"] == 2 and st["pairs"] > 0
     finally:
         tier.stop()
+
+
+def test_rank_cpus_split_is_disjoint_and_balanced_share():
+    from syntropy_b200.experts.cpu_tier import balanced_share, rank_cpus
+    allowed = list(range(32))
+    w1, l1 = rank_cpus(0, 1, allowed)
+    assert w1 == allowed[2:] and l1 == [0, 1]
+    parts = [rank_cpus(r, 8, allowed) for r in range(8)]
+    workers = [c for w, _ in parts for c in w]
+    launch = [c for _, lc in parts for c in lc]
+    assert len(set(workers)) == len(workers) == 24 and not set(workers) & set(launch)
+    assert all(len(w) == 3 for w, _ in parts)
+    # more CPU workers per rank -> a larger CPU share; bounded in (0, 1)
+    s8, s2 = balanced_share(3, 8), balanced_share(15, 2)
+    assert 0 < s8 < s2 < 1
