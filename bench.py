@@ -105,7 +105,11 @@ def main():
     ap.add_argument("--rebalance-every", type=int, default=64,
                     help="decode steps between expert-cache adaptations (decayed-LFU swaps; 0 = never)")
     ap.add_argument("--expert-prefetch", type=int, default=1,
-                    help="router-predicted prefetch of host-tier experts during decode (1 on, 0 off)")
+                    help="host-tier experts staged into VRAM during decode (1 on, 0 off: read over PCIe in place)")
+    ap.add_argument("--expert-staging", default="auto", choices=["auto", "bulk", "predicted"],
+                    help="bulk: DMA-copy every GPU-read host expert of each layer (best when most experts are "
+                         "routed to); predicted: copy the router-predicted ones; auto: bulk when a layer's "
+                         "rows are expected to reach at least half of the experts")
     ap.add_argument("--cpu-experts", type=float, default=None,
                     help="share of each layer's host-tier experts computed by host CPU threads during decode "
                          "(the rest is read over PCIe by the GPU); 0 = off (default 0.75 on one GPU with a VRAM "
@@ -194,7 +198,13 @@ def main():
         from syntropy_b200.experts.cache import ExpertCache
         cache = ExpertCache(mw.layers, args.expert_cache_frac, dev)
         if args.expert_prefetch:
-            cache.enable_decode_prefetch(cfg.n_experts)
+            # rows one MoE layer sees per step: the global batch (every rank's rows reach an owner)
+            touched = 1.0 - (1.0 - cfg.top_k / cfg.n_experts) ** args.batch
+            bulk = args.expert_staging == "bulk" or (args.expert_staging == "auto" and touched >= 0.5)
+            if bulk:
+                cache.enable_decode_staging()
+            else:
+                cache.enable_decode_prefetch(cfg.n_experts)
     fp8_ep = ep is not None and cfg.weight_quant == "fp8"  # fp8 experts use the NCCL row exchange, eagerly
     # TP's NCCL all-reduce baseline is captured into the decode graphs too (ranks step in lockstep)
     graphs = not ((ep is not None and not ep.fused) or fp8_ep or pp is not None)
@@ -323,7 +333,7 @@ def main():
         try:
             if tier is not None:  # nothing is left for the CPU: decode graphs without the hand-off
                 tier.detach()
-                runner.graphs.clear()
+            runner.graphs.clear()  # and without staging copies
             cache.promote_all()
             for _ in range(2):
                 eng.step()
@@ -364,6 +374,8 @@ def main():
                    "expert_cache_frac": args.expert_cache_frac if cfg.is_moe else 1.0,
                    "host_tier_gb": round(cache.host_bytes() / 1e9, 2) if cache is not None else 0.0,
                    "expert_prefetch": bool(cache is not None and cache.prefetch),
+                   "expert_staging": ("bulk" if cache.stage_all else "predicted" if cache.prefetch else "none")
+                   if cache is not None else "none",
                    "expert_rebalance_every": args.rebalance_every if cache is not None else 0,
                    "cpu_expert_share": args.cpu_experts if tier is not None else 0.0,
                    "cpu_expert_threads": tier.threads if tier is not None else 0,  # per rank

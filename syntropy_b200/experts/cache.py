@@ -76,6 +76,7 @@ class ExpertCache:
             L.expert_tier = b
         self._staging = None
         self.prefetch = False
+        self.stage_all = False  # decode: DMA-stage every GPU-read host expert of each layer
         self.cpu_tier = None  # experts.cpu_tier.CpuExpertTier when host experts run on the CPU
         # CTAs of the prefetch kernel (the rest of the GPU stays with the current layer)
         self.prefetch_ctas = int(__import__("os").environ.get("SYN_PREFETCH_CTAS", "64"))
@@ -116,6 +117,44 @@ class ExpertCache:
             b.pred = torch.zeros(n_experts, dtype=torch.int32, device=self.device)
         self.prefetch = True
         return True
+
+    def enable_decode_staging(self):
+        """Bulk staging for decode at large batches (when most experts of a layer are routed to
+        anyway): every host expert the GPU reads (those the host CPU does not compute) is copied
+        by the DMA engines into a VRAM staging bank, layer by layer, double-buffered across
+        layers; the live pointer tables point at the staged rows.  The CPU tier takes the lowest
+        host rows, so the copied rows of a layer are one contiguous range (4 copies per layer)
+        however residency changes.  Replaces the router-predicted prefetch (whose per-expert
+        kernel copies are slower than DMA once nearly every expert is predicted)."""
+        if not any(b.E > b.n_res for b in self.banks):
+            return False
+        self._ensure_staging()
+        self.prefetch = False
+        self.stage_all = True
+        self._stage_events = {}
+        for li, b in enumerate(self.banks):
+            b.stage = self._staging[li % 2]
+            b.rewrite_ptrs()
+        return True
+
+    def stage_rows(self, li: int) -> int:
+        """First host row of layer li that the GPU reads (rows below it belong to the CPU)."""
+        b = self.banks[li]
+        return len(b.cpu_owned)
+
+    def issue_stage_copy(self, li: int):
+        """Copies layer li's GPU-read host rows into its staging bank on the current stream."""
+        b = self.banks[li]
+        r0 = self.stage_rows(li)
+        nh = b.E - b.n_res
+        if r0 >= nh:
+            return
+        for which, p in enumerate(b.parts):
+            if p is None:
+                continue
+            st = b.stage[which]
+            st["q"][r0:nh].copy_(p["qh"][r0:nh], non_blocking=True)
+            st["s"][r0:nh].copy_(p["sh"][r0:nh], non_blocking=True)
 
     def decode_prefetch(self, L):
         """Launch the prefetch of layer L's predicted host experts on the current stream
@@ -163,6 +202,9 @@ class ExpertCache:
             b.n_res = b.E
         self.frac = 1.0
         self._issued = {}
+        self.stage_all = False  # nothing left to stage (captured decode graphs must be captured again)
+        for b in self.banks:
+            b.stage = None
         for b in self.banks:
             if b.home is not None:  # every expert is home now: the prefetch kernel copies nothing
                 b.refresh_home()
@@ -293,6 +335,7 @@ class _TieredBank:
         self.e0 = gu.e0
         self.home = None
         self.host_row_dev = None
+        self.stage = None  # decode bulk staging: [{"q", "s"} per part] this layer's GPU-read host rows live in
         self.cpu_owned: set[int] = set()  # local experts computed by the host CPU (null pointers here)
         self.n_res = max(0, min(self.E, int(math.floor(frac * self.E + 1e-9))))
         self.slot_of = list(range(self.n_res)) + [-1] * (self.E - self.n_res)  # expert -> vram slot
@@ -319,7 +362,7 @@ class _TieredBank:
         if cuda:
             torch.cuda.empty_cache()
 
-    def _write_ptrs(self, bank, qv, sv, qh, sh):
+    def _write_ptrs(self, bank, qv, sv, qh, sh, stage=None):
         qp, sp = [], []
         for e in range(self.E):
             s = self.slot_of[e]
@@ -331,8 +374,9 @@ class _TieredBank:
                 sp.append(sv.data_ptr() + s * sv.stride(0) * sv.element_size())
             else:
                 h = self.host_of[e]
-                qp.append(qh.data_ptr() + h * qh.stride(0) * qh.element_size())
-                sp.append(sh.data_ptr() + h * sh.stride(0) * sh.element_size())
+                tq, ts = (stage["q"], stage["s"]) if stage is not None else (qh, sh)
+                qp.append(tq.data_ptr() + h * tq.stride(0) * tq.element_size())
+                sp.append(ts.data_ptr() + h * ts.stride(0) * ts.element_size())
         dev = bank.qw_ptrs.device if bank.qw_ptrs is not None else qv.device
         new_q = torch.tensor(qp, dtype=torch.int64)
         new_s = torch.tensor(sp, dtype=torch.int64)
@@ -342,11 +386,14 @@ class _TieredBank:
             bank.qw_ptrs.copy_(new_q)
             bank.sm_ptrs.copy_(new_s)
 
+    def _stage_of(self, which):
+        return self.stage[which] if self.stage is not None else None
+
     def rewrite_ptrs(self):
         """Rewrite the live pointer tables in place (after a change of ownership)."""
-        for p in self.parts:
+        for which, p in enumerate(self.parts):
             if p is not None:
-                self._write_ptrs(p["bank"], p["qv"], p["sv"], p["qh"], p["sh"])
+                self._write_ptrs(p["bank"], p["qv"], p["sv"], p["qh"], p["sh"], self._stage_of(which))
         if self.home is not None:
             self.refresh_home()
 
@@ -390,9 +437,9 @@ class _TieredBank:
             p["sh"][h].copy_(ts, non_blocking=False)
         self.slot_of[e_res], self.slot_of[e_host] = -1, s
         self.host_of[e_res], self.host_of[e_host] = h, -1
-        for p in self.parts:
+        for which, p in enumerate(self.parts):
             if p is not None:
-                self._write_ptrs(p["bank"], p["qv"], p["sv"], p["qh"], p["sh"])
+                self._write_ptrs(p["bank"], p["qv"], p["sv"], p["qh"], p["sh"], self._stage_of(which))
         if self.home is not None:
             self.refresh_home()
 

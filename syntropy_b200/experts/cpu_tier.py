@@ -101,7 +101,9 @@ class CpuExpertTier:
         """Give the CPU `cpu_share` of every layer's host experts (by index order, after the
         cache's residency decisions); the GPU's pointer tables get nulls for them."""
         for li, b in enumerate(self.cache.banks):
-            host = [e for e in range(b.E) if b.slot_of[e] < 0]
+            # the CPU takes the host experts with the lowest host rows, so the rows the GPU
+            # reads stay one contiguous range (bulk DMA staging copies them in one piece)
+            host = sorted((e for e in range(b.E) if b.slot_of[e] < 0), key=lambda e: b.host_of[e])
             n_cpu = int(round(self.cpu_share * len(host)))
             mine = set(host[:n_cpu])
             b.cpu_owned = mine

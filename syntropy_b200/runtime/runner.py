@@ -213,6 +213,11 @@ class ModelRunner:
             self.ep.step_begin()
         if self.tp is not None:
             self.tp.step_begin()
+        self._stage_ev = {}
+        cache = self.expert_cache
+        if cache is not None and cache.stage_all:  # bulk staging of the first two MoE layers
+            for li in range(min(2, len(cache.layers))):
+                self._stage_issue(li)
         pp = self.pp
         if pp is None or pp.first:
             ops.embed(mw.embed, d["tokens"][:B], x)
@@ -341,12 +346,19 @@ class ModelRunner:
         ev = self._pf_events.pop(layer, None)
         if ev is not None:  # this layer's pointer tables and staged experts are ready
             torch.cuda.current_stream(self.device).wait_event(ev)
+        li = self._cache_index(L) if cache is not None and cache.stage_all else None
+        if li is not None:
+            ev = self._stage_ev.pop(li, None)
+            if ev is not None:  # this layer's GPU-read host experts are in its staging bank
+                torch.cuda.current_stream(self.device).wait_event(ev)
         k = cfg.top_k
         gu, dn = L.experts_gu, L.experts_down
         if ep is not None:
             ep.moe_decode_fused(layer, h, mb["topk_ids"], mb["topk_w"], x, gu, dn, b["moe_mid"], nw, h,
                                 cfg.rms_eps, stamp=self._stamp if self._stamping else None,
                                 tier=cache.cpu_tier if cache is not None else None, L=L)
+            if li is not None:  # this layer's staging bank is free: stage the layer after next
+                self._stage_issue(li + 2)
             return
         mid = b["moe_mid"][:B * k]
         yp = b["moe_out"][:B * k]
@@ -361,6 +373,8 @@ class ModelRunner:
         ops.linear_grouped(mid, dn, mb["tok_off"], None, yp, ops.GEMV_SCALED_F32, route_w=mb["pair_w"],
                            qw_ptrs=dn.qw_ptrs, sm_ptrs=dn.sm_ptrs)
         self._stamp(f"layer{layer}.down")
+        if li is not None:  # this layer's staging bank is free: stage the layer after next
+            self._stage_issue(li + 2)
         if tier is not None:
             tier.collect(yp)
             ops.core._launched()
@@ -377,6 +391,28 @@ class ModelRunner:
             ops.rms_norm(x, nw, cfg.rms_eps, out=h)
             return
         ops.moe_combine_rmsnorm(x, yp, mb["pair_of"], shared, nw, h, cfg.rms_eps)
+
+    def _cache_index(self, L):
+        idx = getattr(self, "_cache_idx", None)
+        if idx is None:
+            idx = self._cache_idx = {id(X): i for i, X in enumerate(self.expert_cache.layers)}
+        return idx.get(id(L))
+
+    def _stage_issue(self, li: int):
+        """Bulk staging copy of MoE layer li (cache order) on the side stream, after everything
+        enqueued so far on the compute stream (which includes the last reader of its bank)."""
+        cache = self.expert_cache
+        if li >= len(cache.layers):
+            return
+        cur = torch.cuda.current_stream(self.device)
+        if self._pf_stream is None:
+            self._pf_stream = torch.cuda.Stream(device=self.device)
+        self._pf_stream.wait_stream(cur)
+        with torch.cuda.stream(self._pf_stream):
+            cache.issue_stage_copy(li)
+        ev = torch.cuda.Event()
+        ev.record(self._pf_stream)
+        self._stage_ev[li] = ev
 
     def after_step(self):
         """Host-side checks after a decode step has been synchronised (device status words of

@@ -61,3 +61,45 @@ def test_adaptation_between_graph_steps(cuda):
         i = runner._layer_index[id(L)]
         assert int(st.total[li].sum()) + int(left[i]) == n_rows * k
     assert any(b.slot_of != list(range(b.n_res)) + [-1] * (b.E - b.n_res) for b in cache.banks), "no swap happened"
+
+
+def _run_bulk(cuda, cpu_share=0.0, rebalance_every=64):
+    from syntropy_b200.experts.cpu_tier import CpuExpertTier
+    cfg = get_config("small-qwen-moe")
+    mw = prepare_weights(cfg, cuda, seed=21)
+    cache = ExpertCache(mw.layers, 0.5, cuda)
+    runner = ModelRunner(mw, max_batch=8, max_seq_len=256, use_graphs=True)
+    runner.expert_cache = cache
+    tier = CpuExpertTier(cache, cfg, max_rows=runner.max_batch, cpu_share=cpu_share, threads=4) \
+        if cpu_share else None
+    assert cache.enable_decode_staging()
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, cfg.vocab, (n,), generator=g).tolist() for n in (17, 40, 5, 64)]
+    try:
+        outs = LLMEngine(runner, rebalance_every=rebalance_every).generate(prompts, SamplingParams(max_tokens=8))
+    finally:
+        if tier is not None:
+            tier.close()
+    return outs, cache
+
+
+@pytest.mark.parametrize("cpu_share,rebalance_every", [(0.0, 64), (0.5, 64), (0.5, 2)])
+def test_bulk_staging_matches(cuda, cpu_share, rebalance_every):
+    """Bulk DMA staging of every GPU-read host expert (double-buffered across layers, captured
+    in the decode graphs), alone, beside the CPU tier, and across residency swaps every two
+    steps: tokens equal the engine without staging; the live tables of GPU-read host experts
+    point into the layer's staging bank, the CPU's experts stay null."""
+    want, _ = _run(cuda, False)
+    got, cache = _run_bulk(cuda, cpu_share, rebalance_every)
+    assert got == want
+    for li, L in enumerate(cache.layers):
+        b = L.expert_tier
+        st = cache._staging[li % 2][0]["q"]
+        lo, hi = st.data_ptr(), st.data_ptr() + st.numel() * st.element_size()
+        live = L.experts_gu.qw_ptrs.cpu().tolist()
+        for e in range(b.E):
+            if e in b.cpu_owned:
+                assert live[e] == 0
+            elif b.slot_of[e] < 0:
+                assert lo <= live[e] < hi
+        assert sorted(b.host_of[e] for e in b.cpu_owned) == list(range(len(b.cpu_owned)))
