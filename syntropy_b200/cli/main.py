@@ -47,8 +47,10 @@ def _engine_from_config(cfg, device: str):
         CpuExpertTier(cache, mcfg, max_rows=runner.max_batch, cpu_share=cfg.tier.cpu_expert_share,
                       threads=cfg.tier.cpu_threads or None, timeout_s=cfg.kernels.spin_timeout,
                       mode=cfg.kernels.cpu_gemv_mode)
-    return LLMEngine(runner, max_prefill_tokens=cfg.sched.max_prefill_tokens,
-                     rebalance_every=cfg.tier.rebalance_every, spec=_spec_from_config(cfg, mcfg, runner, dev)), mcfg
+    spec = _spec_from_config(cfg, mcfg, runner, dev)
+    chunk = cfg.sched.chunk_tokens or None
+    return LLMEngine(runner, max_prefill_tokens=cfg.sched.max_prefill_tokens, rebalance_every=cfg.tier.rebalance_every,
+                     spec=spec, chunk_tokens=chunk if spec is None else None), mcfg
 
 
 def _spec_from_config(cfg, mcfg, runner, dev):

@@ -75,6 +75,7 @@ class SchedSection:
     max_batch: int = 64
     max_prefill_tokens: int = 8192
     cuda_graphs: bool = True
+    chunk_tokens: int = 0            # chunked prefill with decode-first steps (0 = whole prompts)
 
 
 @dataclass
@@ -174,6 +175,8 @@ class Config:
                 err(f"parallel.{k}", "must be a power of two >= 1")
         if self.sched.max_batch < 1:
             err("sched.max_batch", "must be >= 1")
+        if self.sched.chunk_tokens < 0:
+            err("sched.chunk_tokens", "must be >= 0")
         if self.spec.drafter not in ("none", "ngram", "mtp", "draft"):
             err("spec.drafter", "must be one of none, ngram, mtp, draft")
         if self.spec.drafter == "draft" and not self.spec.draft_model:

@@ -58,6 +58,7 @@ class Sequence:
     blocks: list = field(default_factory=list)
     status: str = "waiting"  # waiting | running | finished
     cached_tokens: int = 0   # prompt tokens served from the prefix cache
+    prefilled: int = 0       # prompt tokens whose K/V are written (chunked prefill)
     mtp_draft: list | None = None
     finish_reason: str | None = None
     seed: int = 0
@@ -84,8 +85,19 @@ class StepOutput:
 
 class LLMEngine:
     def __init__(self, runner: ModelRunner, max_prefill_tokens: int = 8192, eos_token_id: int | None = None,
-                 dist_ctx=None, prefix_cache: bool = False, spec=None, rebalance_every: int = 64):
+                 dist_ctx=None, prefix_cache: bool = False, spec=None, rebalance_every: int = 64,
+                 chunk_tokens: int | None = None):
         self.runner = runner
+        # Chunked prefill (reference plan/rfcs/RFC-0012-execution-scheduler.md:299-314): prompts
+        # enter the KV cache at most `chunk_tokens` tokens per step, and every step first runs
+        # the decode rows of the running sequences, so a long prompt delays them by one chunk at
+        # most.  None: whole prompts (up to max_prefill_tokens per step), prefill steps alone.
+        if chunk_tokens is not None and (chunk_tokens < 1 or spec is not None or runner.pp is not None or
+                                         (dist_ctx is not None and dist_ctx.enabled)):
+            raise ValueError("chunk_tokens: a positive count, without speculation, pipeline stages or lockstep ranks")
+        self.chunk_tokens = chunk_tokens
+        self.prefilling: list[Sequence] = []  # admitted, prompt partly in the KV cache (chunked prefill)
+        self.step_log: list | None = None     # when a list: (decode rows, prefill tokens) per step
         self.rebalance_every = rebalance_every  # decode steps between expert-cache adaptations (0: never)
         self.spec = spec  # runtime.spec.SpecConfig or None
         self.prefix = None
@@ -166,6 +178,14 @@ class LLMEngine:
         return sid
 
     def abort(self, seq_id: int):
+        for s in list(self.prefilling):
+            if s.seq_id == seq_id:
+                # its pages hold only part of the prompt: returned, never published as a prefix
+                self.prefilling.remove(s)
+                self.runner.kv.release(s.blocks)
+                s.blocks = []
+                self._finish(s, "cancelled")
+                return
         for item in list(self.swapped):
             if item[0].seq_id == seq_id:
                 self.swapped.remove(item)
@@ -277,7 +297,7 @@ class LLMEngine:
         return sid
 
     def has_work(self) -> bool:
-        return bool(self.waiting or self.running or self.swapped)
+        return bool(self.waiting or self.running or self.swapped or self.prefilling)
 
     # ------------------------------------------------------------------ steps
     def step(self) -> list[StepOutput]:
@@ -296,13 +316,96 @@ class LLMEngine:
             # the KV pool cannot hold the next step: preempt the newest sequences to host memory
             while len(self.running) > 1 and self._pages_short() > 0:
                 self._swap_out(self.running[-1])
-            return self._decode()
+            return self._log(self._decode(), len(self.running), 0)
+        if self.chunk_tokens is not None:
+            return self._step_chunked()
         batch = self._admit() if not self.swapped else []
         if batch:
             return self._prefill(batch)
         if self.running:
             return self._decode()
         return []
+
+    def _log(self, outs, decode_rows: int, prefill_tokens: int):
+        if self.step_log is not None:
+            self.step_log.append((decode_rows, prefill_tokens))
+        return outs
+
+    def _step_chunked(self) -> list[StepOutput]:
+        """Decode-first step: the running sequences' decode rows, then one prefill chunk of at
+        most chunk_tokens prompt tokens (partly prefilled prompts continue first, in arrival
+        order, then new prompts are admitted while pages and batch rows last)."""
+        outs = []
+        n_dec = len(self.running)
+        if self.running:
+            outs += self._decode()
+        budget = self.chunk_tokens
+        work = []  # (sequence, first prompt position of this chunk, tokens)
+        for s in self.prefilling:
+            if budget <= 0:
+                break
+            n = min(budget, len(s.prompt) - s.prefilled)
+            work.append((s, s.prefilled, n))
+            budget -= n
+        if budget > 0 and not self.swapped:
+            kv = self.runner.kv
+            while self.waiting and budget > 0 and \
+                    len(self.running) + len(self.prefilling) < self.runner.max_batch:
+                s = self.waiting[0]
+                need = kv.blocks_needed(len(s.prompt) + 1)
+                if kv.alloc.num_free < need and self.prefix is not None:
+                    self.prefix.evict(need - kv.alloc.num_free)
+                if kv.alloc.num_free < need:
+                    break
+                self.waiting.popleft()
+                if self.prefix is not None:
+                    s.blocks, s.cached_tokens = self.prefix.match(s.prompt)
+                    # the last prompt token is always computed (its logits give the first token)
+                    s.cached_tokens = min(s.cached_tokens, len(s.prompt) - 1)
+                kv.ensure(s.blocks, len(s.prompt))
+                s.prefilled = s.cached_tokens
+                self.prefilling.append(s)
+                n = min(budget, len(s.prompt) - s.prefilled)
+                work.append((s, s.prefilled, n))
+                budget -= n
+        n_pre = sum(n for _, _, n in work)
+        if work:
+            outs += self._prefill_chunk(work)
+        return self._log(outs, n_dec, n_pre)
+
+    def _prefill_chunk(self, work) -> list[StepOutput]:
+        kv = self.runner.kv
+        toks, pos, slots, cu, prefix = [], [], [], [0], []
+        for s, st, n in work:
+            toks += s.prompt[st:st + n]
+            pos += list(range(st, st + n))
+            slots += [kv.slot(s.blocks, p) for p in range(st, st + n)]
+            cu.append(cu[-1] + n)
+            prefix.append((list(s.blocks), st))
+        logits = self.runner.prefill(torch.tensor(toks), torch.tensor(pos), torch.tensor(slots), cu,
+                                     prefix if any(p[1] for p in prefix) else None,
+                                     block_lists=[list(s.blocks) for s, _, _ in work])
+        self.stats["prefill_steps"] += 1
+        self.stats["prefill_tokens"] += cu[-1]
+        done = [i for i, (s, st, n) in enumerate(work) if st + n == len(s.prompt)]
+        for s, st, n in work:
+            s.prefilled = st + n
+        if not done:
+            return []
+        seqs = [work[i][0] for i in done]
+        rows = logits[done]
+        nxt = self._sample_rows(rows, seqs)
+        self._record_logprobs(rows, seqs, nxt)
+        now = time.perf_counter()
+        outs = []
+        for s, t in zip(seqs, nxt):
+            self.prefilling.remove(s)
+            s.t_first_token = now
+            s.status = "running"
+            self.running.append(s)
+            outs.append(self._append(s, t))
+        self._reap()
+        return outs
 
     def _step_lockstep(self) -> list[StepOutput]:
         import torch.distributed as dist
