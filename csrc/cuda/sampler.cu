@@ -270,6 +270,12 @@ namespace syn {
 //   sampled rows: draw u_j; accept iff u_j < p_j(d_j) (p after temperature/top-k/top-p);
 //                 at the first rejection draw once more from p_j with d_j removed (the
 //                 residual of a point-mass draft); if all accepted draw the bonus from p_g.
+//   stochastic drafts (d_j sampled from a draft distribution q_j, given as f32 rows):
+//                 accept iff u_j < min(1, p_j(d_j) / q_j(d_j)); at the first rejection draw
+//                 from the residual max(0, p_j - q_j) (renormalised); same draw order.  p and q
+//                 are compared in units of 2^-32 with exact integer rules (floor(q * 2^32)
+//                 masses; r = floor((2^64-1) / total), each (m * r) >> 32), so the host oracle
+//                 reproduces every decision bit for bit.
 // The output distribution equals sampling from the target alone.
 
 
@@ -433,6 +439,63 @@ __device__ int row_draw(const float* lg, int V, const RowDist& d, int exclude, u
   return r;
 }
 
+__device__ __forceinline__ unsigned long long draft_mass(const float* q, int i) {
+  const float v = q[i];
+  return v > 0.f ? (unsigned long long)(v * 4294967296.0f) : 0ull;
+}
+
+// Residual draw max(0, pn - qn) over the row (or from pn when the residual is empty).
+__device__ int resid_draw(const float* lg, const float* q, int V, const RowDist& d, unsigned long long rp,
+                          unsigned long long rq, uint32_t x0, unsigned long long* scan, int* pick) {
+  const int per = (V + blockDim.x - 1) / blockDim.x;
+  const int i0 = threadIdx.x * per, i1 = min(V, i0 + per);
+  __shared__ int s_plain;
+  for (int pass = 0; pass < 2; ++pass) {
+    // pass 0: residual masses; pass 1 (only if the residual sums to 0): the target's own
+    unsigned long long local = 0;
+    for (int i = i0; i < i1; ++i) {
+      const unsigned long long pn = (row_mass(lg, d, i) * rp) >> 32;
+      const unsigned long long qn = (draft_mass(q, i) * rq) >> 32;
+      local += pass ? pn : (pn > qn ? pn - qn : 0ull);
+    }
+    scan[threadIdx.x] = local;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long s = 0;
+      for (int i = 0; i < (int)blockDim.x; ++i) {
+        const unsigned long long v = scan[i];
+        scan[i] = s;
+        s += v;
+      }
+      s_plain = s == 0ull;
+      scan[blockDim.x] = __umul64hi((unsigned long long)x0 << 32, s);
+      *pick = -1;
+    }
+    __syncthreads();
+    if (pass == 0 && s_plain) {
+      __syncthreads();
+      continue;
+    }
+    const unsigned long long target = scan[blockDim.x];
+    unsigned long long run = scan[threadIdx.x];
+    if (run <= target) {
+      for (int i = i0; i < i1; ++i) {
+        const unsigned long long pn = (row_mass(lg, d, i) * rp) >> 32;
+        const unsigned long long qn = (draft_mass(q, i) * rq) >> 32;
+        const unsigned long long m = pass ? pn : (pn > qn ? pn - qn : 0ull);
+        if (m == 0) continue;
+        if (run + m > target) { *pick = i; break; }
+        run += m;
+      }
+    }
+    __syncthreads();
+    break;
+  }
+  const int r = *pick >= 0 ? *pick : 0;
+  __syncthreads();
+  return r;
+}
+
 __global__ void __launch_bounds__(SMP_THREADS) verify_accept_kernel(VerifyArgs a) {
   __shared__ float red[32];
   __shared__ float sb[32];
@@ -474,6 +537,37 @@ __global__ void __launch_bounds__(SMP_THREADS) verify_accept_kernel(VerifyArgs a
         }
         __syncthreads();
         const uint32_t u = philox_draw((uint64_t)a.seed[sq], (uint64_t)a.stream[sq], ctr++);
+        if (a.draft_probs != nullptr) {
+          // stochastic draft: accept iff u * qn(d) < pn(d) * 2^32, else draw the residual
+          const float* q = a.draft_probs + ((int64_t)sq * g + j) * a.V;
+          unsigned long long ql = 0;
+          for (int i = threadIdx.x; i < a.V; i += blockDim.x) ql += draft_mass(q, i);
+          scan[threadIdx.x] = ql;
+          __syncthreads();
+          __shared__ unsigned long long s_rp, s_rq;
+          __shared__ int s_acc;
+          if (threadIdx.x == 0) {
+            unsigned long long qs = 0;
+            for (int i = 0; i < (int)blockDim.x; ++i) qs += scan[i];
+            s_rp = s_tot ? ~0ull / s_tot : 0ull;
+            s_rq = qs ? ~0ull / qs : 0ull;
+            const bool in = dj >= 0 && dj < a.V;
+            const unsigned long long pn = (s_md * s_rp) >> 32;
+            const unsigned long long qn = in ? (draft_mass(q, dj) * s_rq) >> 32 : 0ull;
+            s_acc = in && (unsigned long long)u * qn < (pn << 32);
+          }
+          __syncthreads();
+          if (s_acc) {
+            if (threadIdx.x == 0) a.out_tokens[sq * (g + 1) + j] = dj;
+            __syncthreads();
+            continue;
+          }
+          tok = resid_draw(lg, q, a.V, d, s_rp, s_rq,
+                           philox_draw((uint64_t)a.seed[sq], (uint64_t)a.stream[sq], ctr++), scan, &pick);
+          if (threadIdx.x == 0) a.out_tokens[sq * (g + 1) + j] = tok;
+          n_acc = j;
+          break;
+        }
         const unsigned long long thr = __umul64hi((unsigned long long)u << 32, s_tot);  // floor(u * total)
         if (thr < s_md) {
           if (threadIdx.x == 0) a.out_tokens[sq * (g + 1) + j] = dj;

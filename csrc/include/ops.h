@@ -76,7 +76,7 @@ void tp_reduce_norm(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, i
                     double eps);
 void verify_accept(torch::Tensor logits, torch::Tensor draft, torch::Tensor temperature, torch::Tensor top_k,
                    torch::Tensor top_p, torch::Tensor seed, torch::Tensor stream, torch::Tensor counter,
-                   torch::Tensor out_tokens, torch::Tensor n_accept);
+                   torch::Tensor out_tokens, torch::Tensor n_accept, torch::Tensor draft_probs);
 int64_t q4_gemv_dense_ws(int64_t N, int64_t K, int64_t rows);
 void attn_prefill(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor block_tables, torch::Tensor cu_q,
                   torch::Tensor kv_lens, torch::Tensor out, int64_t max_q_len, double scale);

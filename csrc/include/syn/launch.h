@@ -221,6 +221,7 @@ struct VerifyArgs {
   int64_t* counter;          // [S], advanced by the number of draws taken
   int32_t* out_tokens;       // [S, g+1]
   int32_t* n_accept;         // [S]
+  const float* draft_probs;  // [S, g, V] distributions the drafts were sampled from, or null (point masses)
 };
 cudaError_t launch_verify_accept(const VerifyArgs& a, cudaStream_t s);
 cudaError_t launch_philox(uint64_t seed, uint64_t stream, uint64_t counter0, int n, uint32_t* out, cudaStream_t s);

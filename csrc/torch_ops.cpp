@@ -536,10 +536,11 @@ void tp_reduce_norm(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, i
 }
 
 
-// Exact acceptance of point-mass drafts (see csrc/cuda/sampler.cu).
+// Exact acceptance of point-mass drafts, or of drafts sampled from the distributions
+// draft_probs [S, g, V] (f32; empty for point masses) (see csrc/cuda/sampler.cu).
 void verify_accept(torch::Tensor logits, torch::Tensor draft, torch::Tensor temperature, torch::Tensor top_k,
                    torch::Tensor top_p, torch::Tensor seed, torch::Tensor stream, torch::Tensor counter,
-                   torch::Tensor out_tokens, torch::Tensor n_accept) {
+                   torch::Tensor out_tokens, torch::Tensor n_accept, torch::Tensor draft_probs) {
   SYN_CHECK_INPUT(logits);
   SYN_CHECK_INPUT(draft);
   TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && draft.scalar_type() == torch::kInt32 && draft.dim() == 2,
@@ -550,7 +551,13 @@ void verify_accept(torch::Tensor logits, torch::Tensor draft, torch::Tensor temp
   VerifyArgs a{logits.data_ptr<float>(), draft.data_ptr<int32_t>(), (int)S, (int)g, (int)logits.size(1),
                temperature.data_ptr<float>(), top_k.data_ptr<int32_t>(), top_p.data_ptr<float>(),
                seed.data_ptr<int64_t>(), stream.data_ptr<int64_t>(), counter.data_ptr<int64_t>(),
-               out_tokens.data_ptr<int32_t>(), n_accept.data_ptr<int32_t>()};
+               out_tokens.data_ptr<int32_t>(), n_accept.data_ptr<int32_t>(), nullptr};
+  if (draft_probs.defined() && draft_probs.numel()) {
+    SYN_CHECK_INPUT(draft_probs);
+    TORCH_CHECK(draft_probs.scalar_type() == torch::kFloat32 && draft_probs.numel() == S * g * logits.size(1),
+                "draft_probs f32 [S, g, V]");
+    a.draft_probs = draft_probs.data_ptr<float>();
+  }
   const at::cuda::CUDAGuard guard(logits.device());
   SYN_CHECK_CUDA(launch_verify_accept(a, cur_stream()));
 }

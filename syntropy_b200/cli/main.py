@@ -74,7 +74,7 @@ def _spec_from_config(cfg, mcfg, runner, dev):
     dmw = prepare_weights(dcfg, dev, seed=cfg.model.seed, max_pos=cfg.model.max_seq_len + 16 + cfg.spec.gamma)
     drunner = ModelRunner(dmw, max_batch=cfg.sched.max_batch, max_seq_len=cfg.model.max_seq_len + cfg.spec.gamma + 1,
                           use_graphs=False)
-    return SpecConfig(gamma=cfg.spec.gamma, drafter=DraftModelDrafter(drunner))
+    return SpecConfig(gamma=cfg.spec.gamma, drafter=DraftModelDrafter(drunner, temperature=cfg.spec.draft_temperature))
 
 
 def cmd_version(args, cfg):

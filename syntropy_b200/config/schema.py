@@ -100,6 +100,7 @@ class SpecSection:
     drafter: str = "none"        # none | ngram | mtp | draft
     gamma: int = 2               # drafted tokens per verify window
     draft_model: str = ""        # preset name of the draft model (drafter = draft)
+    draft_temperature: float = 0.0  # > 0: drafts sampled from the draft model (stochastic-draft acceptance)
 
 
 @dataclass

@@ -577,9 +577,14 @@ class LLMEngine:
         d = r.desc.h
         drafts = []
         mtp = hasattr(self.spec.drafter, "after_verify")
+        stochastic = getattr(self.spec.drafter, "stochastic", False)
+        probs = []  # stochastic drafts: the distribution each was sampled from
         for i, s in enumerate(seqs):
             if mtp:
                 dr = (s.mtp_draft or [s.output[-1]])[:g]
+            elif stochastic:
+                dr, q = self.spec.drafter.propose(s.prompt + s.output, g, key=s.seq_id, seed=s.seed ^ s.stream)
+                probs.append(q)
             elif getattr(self.spec.drafter, "stateful", False):
                 dr = self.spec.drafter.propose(s.prompt + s.output, g, key=s.seq_id)
             else:
@@ -613,7 +618,8 @@ class LLMEngine:
         seed = torch.tensor([s.seed for s in seqs], dtype=torch.int64)
         stream = torch.tensor([s.stream for s in seqs], dtype=torch.int64)
         ctr = torch.tensor([s.rng_counter for s in seqs], dtype=torch.int64)
-        toks, nacc = verify(logits, torch.tensor(drafts, dtype=torch.int32), temp, topk, topp, seed, stream, ctr)
+        toks, nacc = verify(logits, torch.tensor(drafts, dtype=torch.int32), temp, topk, topp, seed, stream, ctr,
+                            torch.stack(probs) if stochastic else None)
         r.after_step()
         redo = [i for i, s in enumerate(seqs) if self._redraw(s)]
         if redo:

@@ -101,9 +101,42 @@ def _draw(mass: torch.Tensor, x0: int) -> int:
     return min(tok, mass.numel() - 1)
 
 
-def verify_ref(logits, draft, temperature, top_k, top_p, seed, stream, counter):
-    """Host oracle of the device VerifyAccept kernel (point-mass drafts).
-    logits [S*(g+1), V], draft [S, g] -> (tokens [S, g+1], n_accept [S]); counter updated."""
+_U64 = (1 << 64) - 1
+
+
+def _norm32(masses: list[int]) -> list[int]:
+    """Fixed-point masses -> probabilities in units of 2^-32 (the device's exact integer rule:
+    r = floor((2^64 - 1) / total), each (m * r) >> 32)."""
+    tot = sum(masses)
+    if tot == 0:
+        return [0] * len(masses)
+    r = _U64 // tot
+    return [(m * r) >> 32 for m in masses]
+
+
+def _draft_masses(q: torch.Tensor) -> list[int]:
+    """Draft probabilities (f32) -> fixed-point masses floor(q * 2^32) (negative / NaN -> 0)."""
+    qd = q.float().double()
+    return [int(math.floor(v * 4294967296.0)) if v > 0 else 0 for v in qd.tolist()]
+
+
+def _draw_list(mass: list[int], x0: int) -> int:
+    total = sum(mass)
+    target = (x0 * total) >> 32
+    run = 0
+    for i, m in enumerate(mass):
+        if m and run + m > target:
+            return i
+        run += m
+    return 0
+
+
+def verify_ref(logits, draft, temperature, top_k, top_p, seed, stream, counter, draft_probs=None):
+    """Host oracle of the device VerifyAccept kernel.
+    logits [S*(g+1), V], draft [S, g] -> (tokens [S, g+1], n_accept [S]); counter updated.
+    draft_probs None: point-mass drafts (accept iff u < p(d); residual p without d).
+    draft_probs [S, g, V]: drafts sampled from those distributions q (accept iff
+    u < min(1, p(d) / q(d)); residual norm(max(0, p - q))), in the device's exact integers."""
     S, g = draft.shape
     out = torch.zeros(S, g + 1, dtype=torch.int32)
     nacc = torch.zeros(S, dtype=torch.int32)
@@ -123,6 +156,21 @@ def verify_ref(logits, draft, temperature, top_k, top_p, seed, stream, counter):
                 n = min(j, g)
                 break
             mass = _row_masses(lg, t, int(top_k[s]), float(top_p[s]))
+            if j < g and draft_probs is not None:
+                u = philox_draw(int(seed[s]), int(stream[s]), ctr)
+                ctr += 1
+                pn = _norm32(mass.tolist())
+                qn = _norm32(_draft_masses(draft_probs[s, j]))
+                if 0 <= dj < len(pn) and u * qn[dj] < (pn[dj] << 32):
+                    out[s, j] = dj
+                    continue
+                res = [a - b if a > b else 0 for a, b in zip(pn, qn)]
+                if not any(res):  # p == q up to rounding: the residual is p itself
+                    res = pn
+                out[s, j] = _draw_list(res, philox_draw(int(seed[s]), int(stream[s]), ctr))
+                ctr += 1
+                n = j
+                break
             if j < g:
                 u = philox_draw(int(seed[s]), int(stream[s]), ctr)
                 ctr += 1

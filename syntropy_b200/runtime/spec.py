@@ -44,13 +44,23 @@ class DraftModelDrafter:
     after that prefix, then extends greedily one token at a time for the remaining drafts."""
     stateful = True
 
-    def __init__(self, runner):
+    def __init__(self, runner, temperature: float = 0.0):
         self.r = runner
         self.fed: dict = {}     # key -> tokens whose K/V the draft cache holds, in order
         self.blocks: dict = {}  # key -> the sequence's pages in the draft cache
+        # > 0: drafts are sampled from softmax(draft logits / temperature) and the verify step
+        # applies the stochastic-draft rule with those distributions; 0: greedy point masses
+        self.temperature = temperature
+        self.stochastic = temperature > 0
 
-    def _feed(self, key, toks: list[int], start: int) -> int:
-        """K/V for toks at positions start.. (after the cached prefix); returns the greedy next token."""
+    def _pick(self, logits: torch.Tensor, gen) -> tuple[int, torch.Tensor | None]:
+        if not self.stochastic:
+            return int(logits.argmax()), None
+        q = torch.softmax(logits.float() / self.temperature, -1)
+        return int(torch.multinomial(q.cpu(), 1, generator=gen)), q.cpu()
+
+    def _feed(self, key, toks: list[int], start: int) -> torch.Tensor:
+        """K/V for toks at positions start.. (after the cached prefix); returns the next-token logits."""
         r, kv = self.r, self.r.kv
         blocks = self.blocks.setdefault(key, [])
         kv.ensure(blocks, start + len(toks))
@@ -58,23 +68,30 @@ class DraftModelDrafter:
         slots = [kv.slot(blocks, p) for p in pos]
         logits = r.prefill(torch.tensor(toks), torch.tensor(pos), torch.tensor(slots, dtype=torch.int64),
                            [0, len(toks)], [(list(blocks), start)] if start else None, block_lists=[list(blocks)])
-        return int(logits[0].argmax())
+        return logits[0]
 
-    def propose(self, history: list[int], g: int, key=None) -> list[int]:
+    def propose(self, history: list[int], g: int, key=None, seed: int = 0):
+        """g drafts after history: greedy tokens, or (stochastic) tokens sampled from the
+        draft model with their distributions [g, V] (returned as (tokens, probs)); the
+        draws are keyed by (seed, position), so a window is reproducible."""
         fed = self.fed.get(key, [])
         c = 0
         lim = min(len(fed), len(history) - 1)  # the last token is always fed again (its logits)
         while c < lim and fed[c] == history[c]:
             c += 1
-        nxt = self._feed(key, history[c:], c)
-        drafts = [nxt]
+        gen = None
+        if self.stochastic:
+            gen = torch.Generator().manual_seed((seed * 1000003 + len(history)) & ((1 << 63) - 1))
+        nxt, q = self._pick(self._feed(key, history[c:], c), gen)
+        drafts, probs = [nxt], [q]
         fed = list(history)
         for _ in range(g - 1):
-            nxt = self._feed(key, [drafts[-1]], len(fed))
+            nxt, q = self._pick(self._feed(key, [drafts[-1]], len(fed)), gen)
             fed.append(drafts[-1])
             drafts.append(nxt)
+            probs.append(q)
         self.fed[key] = fed
-        return drafts
+        return (drafts, torch.stack(probs)) if self.stochastic else drafts
 
     def release(self, key):
         """Forget a finished sequence and return its draft pages."""
@@ -141,18 +158,21 @@ class SpecConfig:
             self.gamma = 1
 
 
-def verify(logits, drafts, temperature, top_k, top_p, seed, stream, counter):
+def verify(logits, drafts, temperature, top_k, top_p, seed, stream, counter, draft_probs=None):
     """Device or host acceptance; returns (tokens [S, g+1], n_accept [S]) on the host and
-    advances `counter` (host tensor) by the draws taken."""
+    advances `counter` (host tensor) by the draws taken.  draft_probs [S, g, V]: the
+    distributions stochastic drafts were sampled from (None: point-mass drafts)."""
     if logits.is_cuda:
         dev = logits.device
         S, g = drafts.shape
         out = torch.empty(S, g + 1, dtype=torch.int32, device=dev)
         nacc = torch.empty(S, dtype=torch.int32, device=dev)
         ctr = counter.to(dev)
+        dp = draft_probs.to(dev, torch.float32).contiguous() if draft_probs is not None else \
+            torch.empty(0, dtype=torch.float32, device=dev)
         ext().verify_accept(logits.contiguous(), drafts.to(dev, torch.int32).contiguous(), temperature.to(dev),
-                            top_k.to(dev), top_p.to(dev), seed.to(dev), stream.to(dev), ctr, out, nacc)
+                            top_k.to(dev), top_p.to(dev), seed.to(dev), stream.to(dev), ctr, out, nacc, dp)
         counter.copy_(ctr.cpu())
         return out.cpu(), nacc.cpu()
     from .sampling_ref import verify_ref
-    return verify_ref(logits, drafts, temperature, top_k, top_p, seed, stream, counter)
+    return verify_ref(logits, drafts, temperature, top_k, top_p, seed, stream, counter, draft_probs)

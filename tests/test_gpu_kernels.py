@@ -252,3 +252,35 @@ def test_q4_gemv_dense_splitk(cuda, T, N, K, mode):
     if mode != 3:
         ops.linear(x, q, out2, ops.GEMV_SWIGLU if mode == 1 else ops.GEMV_STORE)
         assert torch.equal(out, out2)
+
+
+@pytest.mark.parametrize("stochastic", [False, True])
+def test_verify_accept_matches_host_oracle(cuda, stochastic):
+    """Device VerifyAccept against its host oracle, bit for bit: tokens, accepted counts and
+    Philox counters, for greedy and sampled rows (top-k / top-p included), with point-mass or
+    stochastic drafts (the drafts' own distributions given)."""
+    from syntropy_b200.runtime.sampling_ref import verify_ref
+    from syntropy_b200.runtime.spec import verify
+    torch.manual_seed(5)
+    S, g, V = 12, 3, 5000
+    logits = torch.randn(S * (g + 1), V) * 3
+    q = torch.softmax(torch.randn(S, g, V) * 2, -1) if stochastic else None
+    drafts = torch.stack([torch.multinomial(q[s], 1)[:, 0] for s in range(S)]).int() if stochastic else \
+        torch.randint(0, V, (S, g), dtype=torch.int32)
+    # make some drafts the target's argmax so that acceptance paths run too
+    for s in range(0, S, 3):
+        drafts[s, 0] = int(logits[s * (g + 1)].argmax())
+    temp = torch.tensor([0.0, 0.8, 1.0, 1.3] * (S // 4))
+    top_k = torch.tensor([0, 0, 50, 0] * (S // 4), dtype=torch.int32)
+    top_p = torch.tensor([1.0, 0.9, 1.0, 1.0] * (S // 4))
+    seed = torch.arange(S, dtype=torch.int64) + 11
+    stream = torch.arange(S, dtype=torch.int64) * 3
+    c_dev = torch.arange(S, dtype=torch.int64) * 7
+    c_ref = c_dev.clone()
+    tok_d, n_d = verify(logits.to(cuda), drafts, temp, top_k, top_p, seed, stream, c_dev, q)
+    tok_r, n_r = verify_ref(logits, drafts, temp, top_k, top_p, seed, stream, c_ref, q)
+    assert torch.equal(n_d, n_r)
+    assert torch.equal(c_dev, c_ref)
+    for s in range(S):
+        k = int(n_r[s]) + 1
+        assert tok_d[s, :k].tolist() == tok_r[s, :k].tolist(), s
