@@ -6,21 +6,20 @@ prompt walks its full pages through the table and shares the hits (refcount); fi
 sequences publish their full pages; the cache holds one reference per page and evicts the
 least recently used unreferenced pages when the allocator runs low.
 Reference: plan/rfcs/RFC-0022-kv-cache-prefix-cache-and-sessions.md :17, :355-365 (chained
-page hashes; BLAKE3 there, blake2b here).
+page hashes with BLAKE3; the native BLAKE3 of csrc/cpu/blake3.cpp here).
 """
 from __future__ import annotations
 
-import hashlib
+import struct
 from collections import OrderedDict
 
+from .._ext import ext
 from .paged import BlockAllocator
 
 
 def page_hash(parent: bytes, tokens) -> bytes:
-    h = hashlib.blake2b(digest_size=16)
-    h.update(parent)
-    h.update(b"".join(int(t).to_bytes(4, "little") for t in tokens))
-    return h.digest()
+    """BLAKE3(parent digest || tokens as u32 little-endian): 32 bytes."""
+    return ext().blake3(parent + struct.pack(f"<{len(tokens)}I", *(int(t) for t in tokens)))
 
 
 class PrefixCache:

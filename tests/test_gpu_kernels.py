@@ -220,8 +220,24 @@ def test_sampler(cuda):
                out)
     ref = sample_ref(logits, temp, topk, topp, seed, stream, ctr.clone())
     assert torch.equal(out.cpu()[:4], torch.argmax(logits[:4], -1).int())
-    agree = (out.cpu() == ref).float().mean().item()
-    assert agree >= 0.9, (out.cpu(), ref)
+    # Both sides draw the same Philox number and select by the same fixed-point inverse CDF;
+    # the masses exp(z - max) * 2^32 come from the device's fast exp and the host's exp, which
+    # agree to a few ulp, not bit for bit.  So the tokens must be equal, except where the
+    # draw's target lands within that rounding distance of a cumulative boundary, where the
+    # two picks may be neighbours in the CDF.  Each such row is checked for exactly that.
+    from syntropy_b200.runtime.sampling_ref import _row_masses, philox_draw
+    dev = out.cpu()
+    for t in range(4, T):
+        if int(dev[t]) == int(ref[t]):
+            continue
+        mass = _row_masses(logits[t], float(temp[t]), int(topk[t]), float(topp[t])).double()
+        total = float(mass.sum())
+        target = (philox_draw(int(seed[t]), int(stream[t]), 0) * int(mass.sum())) >> 32
+        cum = torch.cumsum(mass, 0)
+        lo, hi = sorted((int(dev[t]), int(ref[t])))
+        boundary = float(cum[lo])  # the boundary between the two picks
+        assert float(mass[lo + 1:hi].sum()) == 0.0, (t, dev[t], ref[t])  # neighbours in the CDF
+        assert abs(target - boundary) <= 1e-5 * total, (t, dev[t], ref[t], target, boundary)
     assert torch.equal(ctr_g.cpu(), (temp > 0).long())
 
 
