@@ -185,7 +185,8 @@ def main():
                                  tp=(tp_ctx.rank, tp_size) if tp_size > 1 else None, layer_range=layer_range)
             if tp_size > 1:
                 tp = TPGroup(tp_ctx, cfg.hidden, cap=B, n_layers=len(mw.layers),
-                             fused=not args.baseline and cfg.weight_quant == "q4")
+                             fused=not args.baseline and cfg.weight_quant in ("q4", "bf16"),
+                             vocab=cfg.vocab if cfg.weight_quant == "bf16" and (pp is None or pp.last) else 0)
         else:
             mw = prepare_weights(cfg, dev, seed=args.seed, max_pos=max_pos)
     torch.cuda.synchronize()

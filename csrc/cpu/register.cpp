@@ -38,6 +38,10 @@ void register_all(pybind11::module& m) {
   m.def("cpu_handoff", &cpu_handoff);
   m.def("cpu_collect", &cpu_collect);
   m.def("cpu_collect_ep", &cpu_collect_ep);
+  m.def("gemm_bf16", &gemm_bf16);
+  m.def("gemm_bf16_ws", &gemm_bf16_ws);
+  m.def("gemm_bf16_tp", &gemm_bf16_tp);
+  m.def("flags_wait", &flags_wait);
   m.def("argmax", &argmax);
   m.def("sample", &sample);
   m.def("philox", &philox);

@@ -252,6 +252,23 @@ __global__ void tp_reduce_norm_kernel(EpArgs a, int64_t off_recv, int64_t off_fl
   for (int i = threadIdx.x; i < a.H; i += blockDim.x) hout[(int64_t)t * a.H + i] = f2bf(xr[i] * rr * wn[i]);
 }
 
+// Bounded wait of one CTA: thread q waits for rank q's flag at off_flag in this rank's region.
+__global__ void flags_wait_kernel(const int64_t* __restrict__ peers, int n, int rank, int64_t off_flag,
+                                  const uint32_t* step_ctr, int n_layers, int layer, uint64_t timeout_ns, int* status) {
+  if ((int)threadIdx.x >= n) return;
+  const uint8_t* mine = reinterpret_cast<const uint8_t*>(peers[rank]);
+  const uint32_t seq = ep_seq(step_ctr, n_layers, layer);
+  wait_flag(reinterpret_cast<const uint32_t*>(mine + off_flag) + threadIdx.x, seq, timeout_ns, status, 2);
+}
+
+cudaError_t launch_flags_wait(const int64_t* peers, int n, int rank, int64_t off_flag, const uint32_t* step_ctr,
+                              int n_layers, int layer, uint64_t timeout_ns, int* status, cudaStream_t s) {
+  if (n <= 0 || n > 1024) return cudaErrorInvalidValue;
+  flags_wait_kernel<<<1, ((n + 31) / 32) * 32, 0, s>>>(peers, n, rank, off_flag, step_ctr, n_layers, layer, timeout_ns,
+                                                       status);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_tp_reduce_norm(const EpArgs& a, int64_t off_recv, int64_t off_flag, float* x, const float* wn,
                                   void* hout, float eps, int T, cudaStream_t s) {
   if (T == 0) return cudaSuccess;

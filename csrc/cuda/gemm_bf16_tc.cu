@@ -1,0 +1,418 @@
+// bf16 GEMM on the 5th-generation tensor cores: C = X W^T with bf16 activations X [T, K] and
+// bf16 weights W [N, K], f32 accumulation in TMEM, both operands streamed by TMA
+// (SWIZZLE_128B, K-major) from this GPU's own memory.  Reference ops `Gemm` / `Gemv`
+// (crates/kernels/src/op/kind.rs; f32 reference crates/kernels/src/reference/linear.rs:62-132)
+// for bf16 weights, and the tensor-parallel call sites of plan/rfcs/RFC-0032-distributed-
+// execution.md:372-403 when the epilogue pushes to peers.
+//
+// One CTA computes a 128 x BN tile D = A_tile * B_tile^T over its K range:
+//   prefill orientation (T >= 128): A = X (128 tokens), B = W (BN outputs); D[token][output]
+//   decode orientation (T <= 256):  A = W (128 outputs), B = X (BN >= T tokens, rows past T
+//                                    are zero-filled by TMA); D[output][token].  The weight
+//                                    rows stream once; K is split over gridDim.y CTAs when the
+//                                    row tiles alone do not fill the GPU, with an ordered
+//                                    last-CTA reduction of the f32 partials (deterministic).
+// Warps: 0 TMA producer, 1 TMEM allocator + MMA issuer (one elected thread issues
+// tcgen05.mma kind::f16 M=128 N=BN K=16 and commits each stage to its "empty" barrier),
+// 2..5 epilogue (tcgen05.ld 32x32b of their TMEM lane quarter, warp % 4).
+// Epilogues: bf16 store, SwiGLU of interleaved 8-row gate/up chunks (bf16), f32 accumulate,
+// f32 store, and the peer push of tensor parallelism: every f32 output row goes over NVLink
+// into a receive slot of each peer (one-shot all-reduce) or of the row's owner rank
+// (reduce-scatter), and the grid's last CTA raises one completion flag per peer.
+// Every wait is bounded (an error bit in `status`, never a hang).
+#include "tc_common.cuh"
+
+namespace syn {
+
+struct Bf16GemmArgs {
+  int decode;               // 1: A = W, B = X; 0: A = X, B = W
+  int T, N, K;              // tokens, outputs, reduction length
+  int splits;               // K slices per row tile (decode)
+  int mode;                 // 0 bf16, 1 SwiGLU bf16 [T, N/2], 3 f32 +=, 5 f32 =, 6 peer push f32
+  void* out;
+  int ldo;                  // output row stride (elements)
+  float* ws;                // split-K partials [tiles][splits][128][BN]
+  unsigned* counters;       // [tiles] arrival counters (left zero)
+  // peer push (mode 6): row t of output column n -> peers[d] + off_recv + (rank * src_stride + t' * ldo + n) * 4
+  // with d = every rank (owner_rows == 0; t' = t) or d = t / owner_rows (t' = t % owner_rows)
+  const int64_t* peers;
+  int n_peers, rank, cap, owner_rows;
+  int64_t src_stride;
+  int64_t off_recv, off_flag;
+  unsigned* done_ctr;       // CTA arrivals of the launch (left zero)
+  const uint32_t* step_ctr;
+  int n_layers, layer;
+  int* status;
+};
+
+template <int BN>
+struct Bf16Cfg {
+  static constexpr int STAGES = BN >= 256 ? 4 : 6;
+  static constexpr int A_BYTES = 128 * 64 * 2;  // 16 KB
+  static constexpr int B_BYTES = BN * 64 * 2;
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * (A_BYTES + B_BYTES);
+  static_assert(SMEM <= 227 * 1024, "shared memory");
+};
+
+constexpr int BF_THREADS = 192;
+
+// Epilogue of one 32-column group of one TMEM lane (row r of D).
+template <int BN>
+__device__ __forceinline__ void bf16_emit(const Bf16GemmArgs& a, int tile_a, int tile_b, int r, int c0,
+                                          const float* v) {
+  if (a.decode) {
+    const int n = tile_a * 128 + r;  // output feature of this lane
+    if (a.mode == 1) {
+      // interleaved gate/up: rows 16c..16c+7 gate, 16c+8..16c+15 up; the partner is lane ^ 8
+      const bool gate = (n & 8) == 0;
+      const int m = (n >> 4) * 8 + (n & 7);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float other = __shfl_xor_sync(0xffffffffu, v[j], 8);
+        const int t = c0 + j;
+        if (gate && t < a.T && n < a.N)
+          reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)t * a.ldo + m] = f2bf(silu(v[j]) * other);
+      }
+      return;
+    }
+    if (n >= a.N) return;  // rows past N of a partial tile (zero-filled by TMA)
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int t = c0 + j;
+      if (t >= a.T) continue;
+      const int64_t o = (int64_t)t * a.ldo + n;
+      if (a.mode == 0) {
+        reinterpret_cast<__nv_bfloat16*>(a.out)[o] = f2bf(v[j]);
+      } else if (a.mode == 3) {
+        reinterpret_cast<float*>(a.out)[o] += v[j];
+      } else if (a.mode == 5) {
+        reinterpret_cast<float*>(a.out)[o] = v[j];
+      } else {  // 6: peer push
+        if (a.owner_rows > 0) {
+          const int d = t / a.owner_rows, tt = t % a.owner_rows;
+          float* dst = reinterpret_cast<float*>(a.peers[d] + a.off_recv);
+          dst[(int64_t)a.rank * a.src_stride + (int64_t)tt * a.ldo + n] = v[j];
+        } else {
+          for (int d = 0; d < a.n_peers; ++d) {
+            float* dst = reinterpret_cast<float*>(a.peers[d] + a.off_recv);
+            dst[(int64_t)a.rank * a.src_stride + (int64_t)t * a.ldo + n] = v[j];
+          }
+        }
+      }
+    }
+    return;
+  }
+  // prefill orientation: lane = token, 32 consecutive output columns
+  const int t = tile_a * 128 + r;
+  const int n0 = tile_b * BN + c0;
+  if (t >= a.T || n0 >= a.N) return;  // N % 32 == 0: a 32-column group is all in or all out
+  if (a.mode == 1) {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.out) + (int64_t)t * a.ldo + n0 / 2;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int gi = (j / 8) * 16 + (j % 8);
+      o[j] = f2bf(silu(v[gi]) * v[gi + 8]);
+    }
+  } else if (a.mode == 0) {
+    uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out) + (int64_t)t * a.ldo + n0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 w;
+      w.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+      w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+      w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+      w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+      o[j] = w;
+    }
+  } else if (a.mode == 3 || a.mode == 5) {
+    float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + (int64_t)t * a.ldo + n0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 w = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      if (a.mode == 3) {
+        const float4 p = o[j];
+        w.x += p.x;
+        w.y += p.y;
+        w.z += p.z;
+        w.w += p.w;
+      }
+      o[j] = w;
+    }
+  } else {  // 6: peer push
+    const int d0 = a.owner_rows > 0 ? t / a.owner_rows : 0;
+    const int d1 = a.owner_rows > 0 ? d0 + 1 : a.n_peers;
+    const int tt = a.owner_rows > 0 ? t % a.owner_rows : t;
+    for (int d = d0; d < d1; ++d) {
+      float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.peers[d] + a.off_recv) +
+                                            (int64_t)a.rank * a.src_stride + (int64_t)tt * a.ldo + n0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(BF_THREADS, 1) tc_gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                                                 const __grid_constant__ CUtensorMap tmap_b,
+                                                                 Bf16GemmArgs a) {
+  constexpr int STAGES = Bf16Cfg<BN>::STAGES;
+  constexpr int A_BYTES = Bf16Cfg<BN>::A_BYTES;
+  constexpr int B_BYTES = Bf16Cfg<BN>::B_BYTES;
+  constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], done_bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ volatile int s_abort;
+  __shared__ int s_last;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // decode: blockIdx.x = weight row tile, blockIdx.y = K slice; prefill: x = token tile, y = output tile
+  const int tile_a = blockIdx.x;
+  const int tile_b = a.decode ? 0 : blockIdx.y;
+  const int split = a.decode ? blockIdx.y : 0;
+  const int KB = a.K / 64;
+  const int kb0 = (int)((int64_t)KB * split / a.splits), kb1 = (int)((int64_t)KB * (split + 1) / a.splits);
+  const int a_row0 = tile_a * 128, b_row0 = tile_b * BN;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&done_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(&tmem_base)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const int i = kb - kb0, s = i % STAGES;
+        const uint32_t ph = (i / STAGES) & 1;
+        if (i >= STAGES && !mbar_wait(&empty[s], ph ^ 1, a.status, &s_abort)) break;
+        mbar_expect_tx(&full[s], A_BYTES + B_BYTES);
+        tma_load_2d(sA + s * A_BYTES, &tmap_a, kb * 64, a_row0, &full[s]);
+        tma_load_2d(sB + s * B_BYTES, &tmap_b, kb * 64, b_row0, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32<BN>();
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const int i = kb - kb0, s = i % STAGES;
+        const uint32_t ph = (i / STAGES) & 1;
+        if (!mbar_wait(&full[s], ph, a.status, &s_abort)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+        const uint32_t a0 = smem_u32(sA + s * A_BYTES), b0 = smem_u32(sB + s * B_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_bf16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b0 + kk * 32), idesc, (i | kk) != 0);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(&done_bar);
+    }
+  } else {
+    // ---------------- epilogue warps 2..5 ----------------
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // D row (TMEM lane)
+    const bool ok = mbar_wait(&done_bar, 0, a.status, &s_abort) && kb1 > kb0;
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+    if (a.splits == 1) {
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t u[32];
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + c0, u);
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = ok ? __uint_as_float(u[j]) : 0.f;
+        if (ok) bf16_emit<BN>(a, tile_a, tile_b, r, c0, v);
+      }
+    } else {
+      // split-K: every slice stores its partial tile; the last CTA of the row tile sums them
+      // in slice order (the same order whichever CTA arrives last) and runs the epilogue
+      float* mine = a.ws + (((int64_t)tile_a * a.splits + split) * 128 + r) * BN;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t u[32];
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + c0, u);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          *reinterpret_cast<float4*>(mine + c0 + j) =
+              make_float4(ok ? __uint_as_float(u[j]) : 0.f, ok ? __uint_as_float(u[j + 1]) : 0.f,
+                          ok ? __uint_as_float(u[j + 2]) : 0.f, ok ? __uint_as_float(u[j + 3]) : 0.f);
+      }
+      __threadfence();
+      asm volatile("bar.sync 1, 128;\n" ::: "memory");
+      if (threadIdx.x == 64) {
+        const unsigned prev = atomicAdd(&a.counters[tile_a], 1u);
+        s_last = prev == (unsigned)a.splits - 1;
+        if (s_last) a.counters[tile_a] = 0u;  // ready for the next launch
+      }
+      asm volatile("bar.sync 1, 128;\n" ::: "memory");
+      if (s_last) {
+        __threadfence();
+        const float* base = a.ws + ((int64_t)tile_a * a.splits * 128 + r) * BN;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          for (int sp = 0; sp < a.splits; ++sp) {
+            const float* p = base + (int64_t)sp * 128 * BN + c0;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              const float4 q = __ldcg(reinterpret_cast<const float4*>(p + j));
+              v[j] += q.x;
+              v[j + 1] += q.y;
+              v[j + 2] += q.z;
+              v[j + 3] += q.w;
+            }
+          }
+          bf16_emit<BN>(a, tile_a, tile_b, r, c0, v);
+        }
+      }
+    }
+    if (a.mode == 6) {
+      // completion of the whole grid: every CTA publishes its peer stores, the last raises
+      // one flag per peer (the arrival counter is reset before the release)
+      __threadfence_system();
+      asm volatile("bar.sync 1, 128;\n" ::: "memory");
+      if (threadIdx.x == 64) {
+        const unsigned total = gridDim.x * gridDim.y;
+        const unsigned prev = atomicAdd(a.done_ctr, 1u);
+        if (prev == total - 1) {
+          *a.done_ctr = 0u;
+          __threadfence_system();
+          const uint32_t seq = (*a.step_ctr) * (uint32_t)a.n_layers + (uint32_t)a.layer + 1u;
+          for (int q = 0; q < a.n_peers; ++q)
+            st_release_sys(reinterpret_cast<uint32_t*>(a.peers[q] + a.off_flag) + a.rank, seq);
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(TMEM_COLS));
+  }
+}
+
+static bool encode_2d(CUtensorMap* map, const void* base, int rows, int cols, int ld_elems, int box_rows) {
+  PFN_encodeTiled enc = get_encode();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld_elems * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN>
+static cudaError_t launch_bf16(const CUtensorMap& ma, const CUtensorMap& mb, const Bf16GemmArgs& a, dim3 grid,
+                               cudaStream_t s) {
+  static bool set = false;
+  constexpr size_t smem = Bf16Cfg<BN>::SMEM;
+  if (!set) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(tc_gemm_bf16_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    set = true;
+  }
+  tc_gemm_bf16_kernel<BN><<<grid, BF_THREADS, smem, s>>>(ma, mb, a);
+  return cudaGetLastError();
+}
+
+// Split-K plan of the decode orientation: the K slices per row tile so that the grid fills
+// about two waves of the SMs, with at least 4 stages of K per slice.
+int bf16_gemm_splits(int N, int K, int T) {
+  if (T >= 128) return 1;
+  const int tiles = (N + 127) / 128, kb = K / 64;
+  int s = 1;
+  while (tiles * s * 2 <= 2 * num_sms() && kb / (s * 2) >= 4) s *= 2;
+  return s;
+}
+
+size_t bf16_gemm_ws_floats(int N, int K, int T) {
+  if (T >= 128) return 0;
+  const int s = bf16_gemm_splits(N, K, T);
+  if (s == 1) return 0;
+  const int bn = T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
+  return (size_t)((N + 127) / 128) * s * 128 * bn;
+}
+
+cudaError_t launch_tc_gemm_bf16(const void* x, int T, int ldx, const void* w, int N, int K, int mode, void* out,
+                                int ldo, float* ws, size_t ws_floats, unsigned* counters, const PeerPush* pp,
+                                int* status, cudaStream_t s) {
+  // N % 32: whole 32-column epilogue groups (prefill orientation); partial 128-row weight tiles
+  // of the decode orientation read zeros past N (TMA fill) and store nothing there
+  if (T <= 0 || N % 32 || K % 64 || K < 64) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) || (ldx * 2) % 16)
+    return cudaErrorInvalidValue;
+  if (mode == 1 && N % 16) return cudaErrorInvalidValue;
+  if (mode == 6 && pp == nullptr) return cudaErrorInvalidValue;
+  Bf16GemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.T = T;
+  a.N = N;
+  a.K = K;
+  a.mode = mode;
+  a.out = out;
+  a.ldo = ldo;
+  a.status = status;
+  if (pp) {
+    a.peers = pp->peers;
+    a.n_peers = pp->n_peers;
+    a.rank = pp->rank;
+    a.cap = pp->cap;
+    a.owner_rows = pp->owner_rows;
+    a.src_stride = pp->src_stride ? pp->src_stride : (int64_t)pp->cap * ldo;
+    a.off_recv = pp->off_recv;
+    a.off_flag = pp->off_flag;
+    a.done_ctr = pp->done_ctr;
+    a.step_ctr = pp->step_ctr;
+    a.n_layers = pp->n_layers;
+    a.layer = pp->layer;
+  }
+  CUtensorMap ma, mb;
+  if (T < 128) {
+    // decode: weights are the 128-row operand, tokens the N operand (zero-filled past T)
+    const int bn = T <= 32 ? 32 : T <= 64 ? 64 : 128;
+    a.decode = 1;
+    a.splits = bf16_gemm_splits(N, K, T);
+    if (a.splits > 1) {
+      if (ws == nullptr || counters == nullptr || (size_t)((N + 127) / 128) * a.splits * 128 * bn > ws_floats)
+        return cudaErrorInvalidValue;
+      a.ws = ws;
+      a.counters = counters;
+    }
+    if (!encode_2d(&ma, w, N, K, K, 128) || !encode_2d(&mb, x, T, K, ldx, bn)) return cudaErrorInvalidValue;
+    const dim3 grid((unsigned)((N + 127) / 128), (unsigned)a.splits);
+    if (bn == 32) return launch_bf16<32>(ma, mb, a, grid, s);
+    if (bn == 64) return launch_bf16<64>(ma, mb, a, grid, s);
+    return launch_bf16<128>(ma, mb, a, grid, s);
+  }
+  // prefill: tokens are the 128-row operand, BN output columns per CTA
+  const int bn = N % 256 == 0 ? 256 : 128;
+  a.decode = 0;
+  a.splits = 1;
+  if (!encode_2d(&ma, x, T, K, ldx, 128) || !encode_2d(&mb, w, N, K, K, bn)) return cudaErrorInvalidValue;
+  const dim3 grid((unsigned)((T + 127) / 128), (unsigned)((N + bn - 1) / bn));
+  if (bn == 256) return launch_bf16<256>(ma, mb, a, grid, s);
+  return launch_bf16<128>(ma, mb, a, grid, s);
+}
+
+}  // namespace syn

@@ -116,4 +116,14 @@ void register_constrain(pybind11::module& m);
 void register_formats(pybind11::module& m);
 void register_ggml(pybind11::module& m);
 void register_blake3(pybind11::module& m);
+void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t mode, torch::Tensor ws,
+               torch::Tensor counters, torch::Tensor status);
+int64_t gemm_bf16_ws(int64_t N, int64_t K, int64_t T);
+void gemm_bf16_tp(torch::Tensor x, torch::Tensor w, torch::Tensor peers, int64_t off_recv, int64_t cap, int64_t ldo,
+                  int64_t owner_rows, int64_t off_flag, int64_t rank, torch::Tensor done_ctr, torch::Tensor step_ctr,
+                  int64_t n_layers, int64_t layer, torch::Tensor ws, torch::Tensor counters, torch::Tensor status,
+                  int64_t src_stride);
+void flags_wait(torch::Tensor peers, int64_t rank, int64_t off_flag, torch::Tensor step_ctr, int64_t n_layers,
+                int64_t layer, int64_t timeout_ns, torch::Tensor status);
+
 }  // namespace syn

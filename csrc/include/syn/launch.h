@@ -224,6 +224,36 @@ struct VerifyArgs {
   const float* draft_probs;  // [S, g, V] distributions the drafts were sampled from, or null (point masses)
 };
 cudaError_t launch_verify_accept(const VerifyArgs& a, cudaStream_t s);
+
+// ---- bf16 GEMM on tcgen05 (csrc/cuda/gemm_bf16_tc.cu) ----
+// Peer push of a tensor-parallel partial: row t, column n of the f32 product goes to
+// peers[d] + off_recv + (rank * src_stride + t' * ldo + n) * 4 (src_stride defaults to
+// cap * ldo: one receive slot per source; the column width of a vocab slice turns it into a
+// gather of column slices) for every rank d (owner_rows == 0,
+// t' = t: one-shot all-reduce) or for d = t / owner_rows (t' = t % owner_rows: reduce-scatter);
+// the grid's last CTA then release-stores step * n_layers + layer + 1 into each peer's flag
+// slot `rank` at off_flag.
+struct PeerPush {
+  const int64_t* peers;
+  int n_peers, rank, cap, owner_rows;
+  int64_t src_stride;  // elements between two source ranks' areas (0: cap * ldo, the receive slots)
+  int64_t off_recv, off_flag;
+  unsigned* done_ctr;
+  const uint32_t* step_ctr;
+  int n_layers, layer;
+};
+// out = x [T, K] (row stride ldx) @ w [N, K]^T, bf16 operands; mode 0 bf16 store, 1 SwiGLU of
+// interleaved 8-row gate/up chunks (bf16 [T, N/2]), 3 f32 +=, 5 f32 store, 6 peer push (pp).
+// T < 128 runs the decode orientation (split-K partials in ws, per-row-tile counters).
+cudaError_t launch_tc_gemm_bf16(const void* x, int T, int ldx, const void* w, int N, int K, int mode, void* out,
+                                int ldo, float* ws, size_t ws_floats, unsigned* counters, const PeerPush* pp,
+                                int* status, cudaStream_t s);
+int bf16_gemm_splits(int N, int K, int T);
+// Bounded wait (grid of one CTA) until every rank's flag slot at off_flag holds this layer's
+// sequence number; a timeout sets bit 2 of status.
+cudaError_t launch_flags_wait(const int64_t* peers, int n, int rank, int64_t off_flag, const uint32_t* step_ctr,
+                              int n_layers, int layer, uint64_t timeout_ns, int* status, cudaStream_t s);
+size_t bf16_gemm_ws_floats(int N, int K, int T);
 cudaError_t launch_philox(uint64_t seed, uint64_t stream, uint64_t counter0, int n, uint32_t* out, cudaStream_t s);
 
 }  // namespace syn

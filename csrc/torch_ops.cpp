@@ -908,5 +908,70 @@ void cpu_collect_ep(int64_t mailbox, int64_t E, int64_t k, int64_t max_rows, int
   SYN_CHECK_CUDA(launch_cpu_collect(a, cur_stream()));
 }
 
-}  // namespace syn
 
+// out = x @ w^T on tcgen05 with bf16 weights (csrc/cuda/gemm_bf16_tc.cu).  mode: 0 bf16 [T, N],
+// 1 SwiGLU bf16 [T, N/2], 3 f32 += [T, N], 5 f32 [T, N].  ws / counters: split-K workspace
+// (f32, at least gemm_bf16_ws(N, K, T) floats) and N/128 zeroed counters (decode shapes).
+void gemm_bf16(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t mode, torch::Tensor ws,
+               torch::Tensor counters, torch::Tensor status) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "gemm_bf16: cuda tensors");
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && w.scalar_type() == torch::kBFloat16 && x.dim() == 2 &&
+                  w.dim() == 2 && x.stride(1) == 1 && w.is_contiguous(),
+              "gemm_bf16: x bf16 [T, K] (unit column stride), w bf16 [N, K] contiguous");
+  const int64_t T = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K, "gemm_bf16: K mismatch");
+  TORCH_CHECK(mode == 0 || mode == 1 || mode == 3 || mode == 5, "gemm_bf16: mode 0, 1, 3 or 5");
+  const int64_t ncol = mode == 1 ? N / 2 : N;
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == T && out.size(1) == ncol && out.stride(1) == 1, "gemm_bf16: out shape");
+  TORCH_CHECK((mode <= 1 && out.scalar_type() == torch::kBFloat16) || (mode >= 3 && out.scalar_type() == torch::kFloat32),
+              "gemm_bf16: out dtype");
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_tc_gemm_bf16(x.data_ptr(), (int)T, (int)x.stride(0), w.data_ptr(), (int)N, (int)K, (int)mode,
+                                     out.data_ptr(), (int)out.stride(0), ws.numel() ? ws.data_ptr<float>() : nullptr,
+                                     (size_t)ws.numel(),
+                                     counters.numel() ? reinterpret_cast<unsigned*>(counters.data_ptr<int32_t>()) : nullptr,
+                                     nullptr, status.data_ptr<int32_t>(), cur_stream()));
+}
+
+int64_t gemm_bf16_ws(int64_t N, int64_t K, int64_t T) { return (int64_t)bf16_gemm_ws_floats((int)N, (int)K, (int)T); }
+
+// Tensor-parallel row-parallel product with the peer push epilogue: each f32 row of x @ w^T
+// goes into every peer's receive slot [rank][row] (owner_rows == 0) or into the row owner's
+// slot (owner_rows > 0), then the completion flags (see PeerPush in syn/launch.h).
+void gemm_bf16_tp(torch::Tensor x, torch::Tensor w, torch::Tensor peers, int64_t off_recv, int64_t cap, int64_t ldo,
+                  int64_t owner_rows, int64_t off_flag, int64_t rank, torch::Tensor done_ctr, torch::Tensor step_ctr,
+                  int64_t n_layers, int64_t layer, torch::Tensor ws, torch::Tensor counters, torch::Tensor status,
+                  int64_t src_stride) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == torch::kBFloat16 && w.scalar_type() == torch::kBFloat16 &&
+                  x.dim() == 2 && x.stride(1) == 1 && w.is_contiguous(),
+              "gemm_bf16_tp: bf16 x [T, K], w [N, K]");
+  const int64_t T = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K && ldo >= N, "gemm_bf16_tp: shapes");
+  TORCH_CHECK(owner_rows > 0 ? T <= owner_rows * peers.numel() && owner_rows <= cap : T <= cap,
+              "gemm_bf16_tp: rows exceed the receive slots");
+  TORCH_CHECK(src_stride == 0 || src_stride * (peers.numel() - 1) + N + (T - 1) * ldo <= cap * ldo,
+              "gemm_bf16_tp: column slices exceed the gather area");
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == torch::kInt64, "peers int64 (device)");
+  TORCH_CHECK(done_ctr.is_cuda() && done_ctr.scalar_type() == torch::kInt32, "done_ctr int32 (device)");
+  PeerPush pp{peers.data_ptr<int64_t>(), (int)peers.numel(), (int)rank, (int)cap, (int)owner_rows, src_stride,
+              off_recv, off_flag,
+              reinterpret_cast<unsigned*>(done_ctr.data_ptr<int32_t>()),
+              reinterpret_cast<const uint32_t*>(step_ctr.data_ptr()), (int)n_layers, (int)layer};
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_tc_gemm_bf16(x.data_ptr(), (int)T, (int)x.stride(0), w.data_ptr(), (int)N, (int)K, 6, nullptr,
+                                     (int)ldo, ws.numel() ? ws.data_ptr<float>() : nullptr, (size_t)ws.numel(),
+                                     counters.numel() ? reinterpret_cast<unsigned*>(counters.data_ptr<int32_t>()) : nullptr,
+                                     &pp, status.data_ptr<int32_t>(), cur_stream()));
+}
+
+
+void flags_wait(torch::Tensor peers, int64_t rank, int64_t off_flag, torch::Tensor step_ctr, int64_t n_layers,
+                int64_t layer, int64_t timeout_ns, torch::Tensor status) {
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == torch::kInt64, "peers int64 (device)");
+  const at::cuda::CUDAGuard guard(peers.device());
+  SYN_CHECK_CUDA(launch_flags_wait(peers.data_ptr<int64_t>(), (int)peers.numel(), (int)rank, off_flag,
+                                   reinterpret_cast<const uint32_t*>(step_ctr.data_ptr()), (int)n_layers, (int)layer,
+                                   (uint64_t)timeout_ns, status.data_ptr<int32_t>(), cur_stream()));
+}
+
+}  // namespace syn

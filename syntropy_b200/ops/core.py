@@ -172,6 +172,16 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
         gm = {GEMV_STORE: 0 if out.dtype == torch.bfloat16 else 5, GEMV_SWIGLU: 1, GEMV_ADD_F32: 3}[mode]
         gemm_grouped(x, ptrs[0], ptrs[1], _identity_off(T, x.device), W.N, W.K, gm, None, out, 1, W.qw, W.sm)
         return out
+    if isinstance(W, torch.Tensor) and W.dtype == torch.bfloat16 and x.dtype == torch.bfloat16 and \
+            W.shape[0] % 32 == 0 and W.shape[1] % 64 == 0 and x.stride(-1) == 1 and _BF16_TC[0] and \
+            (mode != GEMV_SWIGLU or W.shape[0] % 16 == 0):
+        # bf16 weights: tcgen05 GEMM (decode orientation with split-K below 128 rows)
+        N, K = W.shape
+        gm = {GEMV_STORE: 0 if out.dtype == torch.bfloat16 else 5, GEMV_SWIGLU: 1, GEMV_ADD_F32: 3}[mode]
+        ws, ctr = _bf16_workspace(x.device, N, K, T)
+        ext().gemm_bf16(x, W if W.is_contiguous() else W.contiguous(), out, gm, ws, ctr, gemm_status(x.device))
+        _launched()
+        return out
     Wd = _dense_weight(W)
     y = x.to(Wd.dtype) @ Wd.t()
     if mode == GEMV_SWIGLU:
@@ -181,6 +191,25 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
     else:
         out.copy_(y)
     return out
+
+
+_BF16_TC = [__import__("os").environ.get("SYN_BF16_TC", "1") == "1"]  # 0: bf16 GEMMs through the library
+_BF16_WS: dict = {}
+
+
+def _bf16_workspace(dev, N: int, K: int, T: int):
+    """Split-K workspace (f32) and per-row-tile counters of the bf16 tcgen05 GEMM, grown on
+    demand to the largest plan so far on this device (allocated outside graph capture by the
+    warm-up passes that precede it)."""
+    key = str(dev)
+    need = max(0, ext().gemm_bf16_ws(N, K, T))
+    ws, ctr = _BF16_WS.get(key, (None, None))
+    tiles = (N + 127) // 128
+    if ws is None or ws.numel() < need or ctr.numel() < tiles:
+        ws = torch.empty(max(need, ws.numel() if ws is not None else 0), dtype=torch.float32, device=dev)
+        ctr = torch.zeros(max(tiles, ctr.numel() if ctr is not None else 0), dtype=torch.int32, device=dev)
+        _BF16_WS[key] = (ws, ctr)
+    return ws, ctr
 
 
 _PTR_CACHE: dict = {}

@@ -85,12 +85,13 @@ class EPGroup:
             ext().ep_step_begin(self.step_ctr)
 
     def moe_decode_fused(self, layer: int, h, topk_ids, topk_w, x, gu, dn, mid, next_norm, h_out, eps,
-                         stamp=None, tier=None, L=None):
+                         stamp=None, tier=None, L=None, before_gemv=None):
         """One MoE layer for the local rows (h: bf16 [T, H]) through NVLink dispatch/combine.
         stamp: device-timestamp callback of a profiled step; tier: the host CPU expert tier,
         which computes its share of this rank's cold experts for every rank's rows while the
         GPU runs the rest (its rows reach the sources' combine slots over NVLink); L: the
-        model layer (its expert banks tell which experts the CPU owns)."""
+        model layer (its expert banks tell which experts the CPU owns); before_gemv: called right
+        before the expert GEMVs (after dispatch and the CPU hand-off)."""
         e = ext()
         c = self._common(layer)
         stamp = stamp or (lambda _lab: None)
@@ -105,6 +106,8 @@ class EPGroup:
             tier.handoff_ep(tier.layer_of[id(L)], self.recv_x, self.tok_off, self.tok_idx, self.pair_w)
             ops.core._launched()
         P = self.N * self.cap * self.k
+        if before_gemv is not None:  # e.g. wait for this layer's staged host experts
+            before_gemv()
         ops.linear_grouped(self.recv_x, gu, self.tok_off, self.tok_idx, mid[:P], ops.GEMV_SWIGLU,
                            qw_ptrs=gu.qw_ptrs, sm_ptrs=gu.sm_ptrs)
         stamp(f"layer{layer}.gate_up")

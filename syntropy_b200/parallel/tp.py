@@ -1,9 +1,10 @@
 """Intra-node tensor parallelism (Megatron column/row split over NVLink).
 
 Column-parallel: qkv (whole KV heads per rank) and gate/up; row-parallel: o_proj and down.
-The row-parallel products are reduced by a fused path on GPUs: the GEMV epilogue pushes its
-f32 partial rows straight into every peer's receive slot over NVLink and the last CTA raises
-a flag; the receive kernel sums the N partials in rank order (so every rank holds bitwise
+The row-parallel products are reduced by a fused path on GPUs: the GEMV (4-bit weights) or
+the tcgen05 GEMM (bf16 weights, csrc/cuda/gemm_bf16_tc.cu) pushes its f32 partial rows from
+its epilogue straight into every peer's receive slot over NVLink and the last CTA raises a
+flag; the receive kernel sums the N partials in rank order (so every rank holds bitwise
 identical residuals, the reference's member-order rule), adds the residual and applies the
 next RMSNorm.  The NCCL all-reduce path is the baseline (and the CPU/gloo path).
 
@@ -40,26 +41,53 @@ def gather_vocab_logits(local: torch.Tensor, out: torch.Tensor, gathered: torch.
 
 class TPGroup:
     def __init__(self, ctx: DistContext, hidden: int, cap: int, n_layers: int, timeout_s: float = 2.0,
-                 fused: bool = True):
+                 fused: bool = True, vocab: int = 0):
+        """vocab > 0 (a vocab-parallel head with bf16 weights): the LM-head GEMM of each rank
+        writes its column slice of the logits straight into every rank's logits buffer, which
+        lives in the symmetric region (`logits_view`)."""
         self.ctx = ctx
         self.N, self.rank, self.H, self.cap = ctx.world, ctx.rank, hidden, cap
         self.n_layers = n_layers
         self.fused = fused and ctx.device.type == "cuda"
         self.timeout_ns = int(timeout_s * 1e9)
+        self.vocab = vocab if self.fused and vocab % self.N == 0 else 0
         if self.fused:
             area = self.N * cap * hidden * 4
             self.off_recv = [0, _align(area)]
-            self.off_flag = [2 * _align(area), 2 * _align(area) + 256]
-            self.region = SymmetricRegion(ctx, 2 * _align(area) + 512)
+            self.off_flag = [2 * _align(area), 2 * _align(area) + 256, 2 * _align(area) + 512]
+            self.off_logits = 2 * _align(area) + 768
+            size = self.off_logits + (_align(cap * self.vocab * 4) if self.vocab else 0)
+            self.region = SymmetricRegion(ctx, size)
             dev = ctx.device
             self.step_ctr = torch.zeros(1, dtype=torch.int32, device=dev)
             self.status = torch.zeros(1, dtype=torch.int32, device=dev)
-            self.done_ctr = torch.zeros(2 * n_layers, dtype=torch.int32, device=dev)
+            self.done_ctr = torch.zeros(2 * n_layers + 1, dtype=torch.int32, device=dev)
             self._off1 = {}
 
     def step_begin(self):
         if self.fused:
             ext().ep_step_begin(self.step_ctr)
+
+    def logits_view(self, rows: int) -> torch.Tensor:
+        """f32 [rows, vocab] logits buffer in the symmetric region (every rank's slices land here)."""
+        return self.region.view(self.off_logits, self.cap * self.vocab, torch.float32).view(self.cap, self.vocab)[:rows]
+
+    def gather_logits(self, h, W, logits_rows: int):
+        """Vocab-parallel head, fused: this rank's slice of h @ W^T (bf16 W [V/N, H]) goes from the
+        GEMM epilogue into columns [rank * V/N, (rank + 1) * V/N) of every rank's logits buffer
+        over NVLink; then a bounded wait for every rank's slice.  Returns the logits view."""
+        from ..ops.core import _bf16_workspace, gemm_status
+        T = h.shape[0]
+        vl = W.shape[0]
+        seq = 2 * self.n_layers  # the head's flag slot: its own monotone sequence per step
+        ws, ctr = _bf16_workspace(h.device, vl, W.shape[1], T)
+        ext().gemm_bf16_tp(h, W, self.region.peers, self.off_logits, self.cap, self.vocab, 0, self.off_flag[2],
+                           self.rank, self.done_ctr[seq:seq + 1], self.step_ctr, 2 * self.n_layers, seq, ws, ctr,
+                           gemm_status(h.device), vl)
+        ext().flags_wait(self.region.peers, self.rank, self.off_flag[2], self.step_ctr, 2 * self.n_layers, seq,
+                         self.timeout_ns, self.status)
+        ops.core._launched(2)
+        return self.logits_view(T)
 
     def _tok_off(self, T, dev):
         t = self._off1.get(T)
@@ -73,12 +101,21 @@ class TPGroup:
         which: 0 = attention output projection, 1 = FFN down projection."""
         T = x_in.shape[0]
         if self.fused:
-            from ..ops.core import _ptrs
-            qp, sp = _ptrs(W)
             seq_layer = 2 * layer + which
-            ext().q4_gemv_tp(x_in, qp, sp, self._tok_off(T, x_in.device), W.N, W.K,
-                             self.done_ctr[seq_layer:seq_layer + 1], self.region.peers, self.off_recv[which],
-                             self.cap, self.off_flag[which], self.rank, self.step_ctr, 2 * self.n_layers, seq_layer)
+            if isinstance(W, torch.Tensor) and W.dtype == torch.bfloat16:
+                # bf16 weights: the tcgen05 GEMM pushes each f32 partial row to every peer
+                from ..ops.core import _bf16_workspace, gemm_status
+                ws, ctr = _bf16_workspace(x_in.device, W.shape[0], W.shape[1], T)
+                ext().gemm_bf16_tp(x_in, W, self.region.peers, self.off_recv[which], self.cap, self.H, 0,
+                                   self.off_flag[which], self.rank, self.done_ctr[seq_layer:seq_layer + 1],
+                                   self.step_ctr, 2 * self.n_layers, seq_layer, ws, ctr, gemm_status(x_in.device), 0)
+            else:
+                from ..ops.core import _ptrs
+                qp, sp = _ptrs(W)
+                ext().q4_gemv_tp(x_in, qp, sp, self._tok_off(T, x_in.device), W.N, W.K,
+                                 self.done_ctr[seq_layer:seq_layer + 1], self.region.peers, self.off_recv[which],
+                                 self.cap, self.off_flag[which], self.rank, self.step_ctr, 2 * self.n_layers,
+                                 seq_layer)
             ext().tp_reduce_norm(self.region.peers, self.N, self.rank, self.cap, self.H, [0] * 6, self.step_ctr,
                                  2 * self.n_layers, seq_layer, self.timeout_ns, self.status, self.off_recv[which],
                                  self.off_flag[which], x_res,

@@ -138,9 +138,13 @@ class ModelRunner:
             b["qkv"] = torch.zeros(B, qkv_dim, dtype=act, device=dev)
             b["q"] = torch.zeros(B, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
             b["attn"] = torch.zeros(B, cfg.n_heads, cfg.head_dim, dtype=act, device=dev)
-        b["logits"] = torch.zeros(B, cfg.vocab, dtype=torch.float32, device=dev)
         vl = self._vocab_local()
-        if self.tp is not None and vl < cfg.vocab:  # vocab-parallel head: local slice + gather space
+        if self._fused_head():
+            # every rank's logits slice lands in this buffer (symmetric region) from the head GEMM
+            b["logits"] = self.tp.logits_view(B)
+        else:
+            b["logits"] = torch.zeros(B, cfg.vocab, dtype=torch.float32, device=dev)
+        if self.tp is not None and vl < cfg.vocab and not self._fused_head():  # local slice + gather space
             b["logits_local"] = torch.zeros(B, vl, dtype=torch.float32, device=dev)
             b["logits_gather"] = torch.zeros(self.tp.N * B, vl, dtype=torch.float32, device=dev)
         b["next"] = torch.zeros(B, dtype=torch.int32, device=dev)
@@ -347,16 +351,19 @@ class ModelRunner:
         if ev is not None:  # this layer's pointer tables and staged experts are ready
             torch.cuda.current_stream(self.device).wait_event(ev)
         li = self._cache_index(L) if cache is not None and cache.stage_all else None
-        if li is not None:
-            ev = self._stage_ev.pop(li, None)
-            if ev is not None:  # this layer's GPU-read host experts are in its staging bank
+
+        def staged():
+            # the GPU-read host experts of this layer are in its staging bank (waited for only
+            # right before the GEMVs that read them: routing and the CPU hand-off go first)
+            ev = self._stage_ev.pop(li, None) if li is not None else None
+            if ev is not None:
                 torch.cuda.current_stream(self.device).wait_event(ev)
         k = cfg.top_k
         gu, dn = L.experts_gu, L.experts_down
         if ep is not None:
             ep.moe_decode_fused(layer, h, mb["topk_ids"], mb["topk_w"], x, gu, dn, b["moe_mid"], nw, h,
                                 cfg.rms_eps, stamp=self._stamp if self._stamping else None,
-                                tier=cache.cpu_tier if cache is not None else None, L=L)
+                                tier=cache.cpu_tier if cache is not None else None, L=L, before_gemv=staged)
             if li is not None:  # this layer's staging bank is free: stage the layer after next
                 self._stage_issue(li + 2)
             return
@@ -367,6 +374,7 @@ class ModelRunner:
             tier.handoff(L, h, mb)
             ops.core._launched()
         shared = self._shared_expert(L, h) if L.shared_gu is not None else None
+        staged()
         ops.linear_grouped(h, gu, mb["tok_off"], mb["tok_idx"], mid, ops.GEMV_SWIGLU,
                            qw_ptrs=gu.qw_ptrs, sm_ptrs=gu.sm_ptrs)
         self._stamp(f"layer{layer}.gate_up")
@@ -523,12 +531,23 @@ class ModelRunner:
         W = self.mw.lm_head
         return int(getattr(W, "N", None) or W.shape[0])
 
+    def _fused_head(self) -> bool:
+        """Vocab-parallel bf16 head whose GEMM writes every rank's logits buffer (no NCCL)."""
+        tp, W = self.tp, self.mw.lm_head
+        return bool(tp is not None and getattr(tp, "vocab", 0) and isinstance(W, torch.Tensor) and
+                    W.dtype == torch.bfloat16 and self._vocab_local() * tp.N == self.cfg.vocab and
+                    self._vocab_local() % 32 == 0 and tp.cap >= self.max_batch)
+
     def _lm_head(self, h, logits, local=None, gathered=None):
         """logits [T, V] f32.  Under TP with a vocab-parallel head each rank scores its vocab
-        slice and the slices are all-gathered in rank order (every rank then samples alike)."""
+        slice and the slices are all-gathered in rank order (every rank then samples alike):
+        fused into the head GEMM's epilogue over NVLink for bf16 heads, NCCL otherwise."""
         vl = self._vocab_local()
         if vl == self.cfg.vocab or self.tp is None:
             ops.linear(h, self.mw.lm_head, logits, ops.GEMV_STORE)
+            return logits
+        if self._fused_head() and logits.data_ptr() == self.buf["logits"].data_ptr():
+            self.tp.gather_logits(h, self.mw.lm_head, h.shape[0])
             return logits
         from ..parallel.tp import gather_vocab_logits
         T = h.shape[0]

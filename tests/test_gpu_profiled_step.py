@@ -30,5 +30,7 @@ def test_profiled_step(cuda):
     assert [eng.finished[i].output for i in ids] == want
     labels = [lab for lab, _ in prof]
     assert labels[0] == "layer0.attention" and labels[-1] == "sample"
-    assert len(labels) == 2 * cfg.n_layers + 2
+    # per MoE layer: attention, route, gate_up, down, moe (combine); then lm_head and sample
+    assert len(labels) == 5 * cfg.n_layers + 2
+    assert [lab.split(".")[-1] for lab in labels[:5]] == ["attention", "route", "gate_up", "down", "moe"]
     assert all(ms > 0 for _, ms in prof)
