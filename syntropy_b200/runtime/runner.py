@@ -622,24 +622,82 @@ class ModelRunner:
         return g
 
     # ------------------------------------------------------------------ prefill
+    pp_prefill_groups = 2  # pipeline parallelism: sequence groups handed between stages per prefill
+
     @torch.no_grad()
     def prefill(self, tokens: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor, cu_seqlens: list[int],
                 prefix: list | None = None, block_lists: list | None = None):
         """Eager prefill of freshly started sequences (or of chunks after a cached prefix).
         block_lists: each sequence's KV pages (the paged attention kernel reads keys through
-        them).  Returns the last-token logits of each sequence [n_seq, vocab] (f32)."""
+        them).  Returns the last-token logits of each sequence [n_seq, vocab] (f32).
+
+        Under pipeline parallelism with several sequences the prefill is pipelined
+        (reference RFC-0001 :1832-1899, chunked staggered prefill): the sequences form groups,
+        each stage computes group k while the hidden states of group k-1 are still in flight
+        to the next stage (asynchronous NCCL point-to-point), and the next stage has posted
+        its receive of group k+1 before it computes group k."""
+        pp = self.pp
+        n = len(cu_seqlens) - 1
+        G = min(self.pp_prefill_groups, n) if pp is not None else 1
+        if G <= 1:
+            return self._prefill_pass(tokens, positions, slots, cu_seqlens, prefix, block_lists)
+        # contiguous sequence groups of about equal token counts
+        bounds, total, acc = [0], cu_seqlens[-1], 0
+        for s_i in range(n):
+            acc = cu_seqlens[s_i + 1]
+            if len(bounds) < G and acc >= total * len(bounds) / G and s_i + 1 < n:
+                bounds.append(s_i + 1)
+        bounds.append(n)
+        groups = [(a, b) for a, b in zip(bounds[:-1], bounds[1:]) if b > a]
+        dev = self.device
+
+        def recv(g):
+            a, b = groups[g]
+            buf = torch.empty(cu_seqlens[b] - cu_seqlens[a], self.cfg.hidden, dtype=torch.float32, device=dev)
+            return buf, pp.irecv_hidden(buf)
+
+        pending = recv(0) if not pp.first else None
+        sends, outs = [], []
+        for g, (a, b) in enumerate(groups):
+            nxt = recv(g + 1) if not pp.first and g + 1 < len(groups) else None
+            x_in = None
+            if pending is not None:
+                x_in, work = pending
+                work.wait()
+            t0, t1 = cu_seqlens[a], cu_seqlens[b]
+            res = self._prefill_pass(tokens[t0:t1], positions[t0:t1], slots[t0:t1], [c - t0 for c in cu_seqlens[a:b + 1]],
+                                     prefix[a:b] if prefix is not None else None,
+                                     block_lists[a:b] if block_lists is not None else None, x_in=x_in, pp_io=False)
+            if pp.last:
+                outs.append(res)
+            else:
+                sends.append((res, pp.isend_hidden(res)))
+            pending = nxt
+        for _, work in sends:
+            work.wait()
+        return torch.cat(outs, 0) if pp.last else None
+
+    @torch.no_grad()
+    def _prefill_pass(self, tokens: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor, cu_seqlens: list[int],
+                      prefix: list | None = None, block_lists: list | None = None, x_in=None, pp_io: bool = True):
+        """One prefill pass of this stage's layers.  pp_io: receive / send the hidden states
+        here (blocking); otherwise x_in is the received input and the hidden states are
+        returned instead of sent (pipelined prefill)."""
         cfg, mw, dev = self.cfg, self.mw, self.device
         T = tokens.numel()
         act = torch.bfloat16 if self.is_cuda else torch.float32
         tokens = tokens.to(dev, torch.int32)
         positions = positions.to(dev, torch.int32)
         slots = slots.to(dev, torch.int64)
-        x = torch.empty(T, cfg.hidden, dtype=torch.float32, device=dev)
         pp = self.pp
-        if pp is None or pp.first:
-            ops.embed(mw.embed, tokens, x)
+        if x_in is not None:
+            x = x_in
         else:
-            pp.recv_hidden(x)
+            x = torch.empty(T, cfg.hidden, dtype=torch.float32, device=dev)
+            if pp is None or pp.first:
+                ops.embed(mw.embed, tokens, x)
+            else:
+                pp.recv_hidden(x)
         h = torch.empty(T, cfg.hidden, dtype=act, device=dev)
         if not self.is_mla:
             qkv = torch.empty(T, cfg.q_dim + 2 * cfg.kv_dim, dtype=act, device=dev)
@@ -694,6 +752,8 @@ class ModelRunner:
         if len(cu_seqlens) == 1:
             return torch.zeros(0, cfg.vocab, dtype=torch.float32, device=dev)
         if pp is not None and not pp.last:
+            if not pp_io:
+                return x  # the pipelined caller sends it
             pp.send_hidden(x)
             return None  # the last stage produces the logits; tokens arrive by broadcast
         last = torch.tensor([c - 1 for c in cu_seqlens[1:]], device=dev, dtype=torch.long)
