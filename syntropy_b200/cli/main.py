@@ -167,6 +167,15 @@ def cmd_bench(args, cfg):
 
 
 def main(argv=None):
+    argv = sys.argv[1:] if argv is None else argv
+    if argv and argv[0] == "__runner":
+        # hidden mode: the runner process a daemon's RunnerHost spawns (daemon/runner_proc.py)
+        rp = argparse.ArgumentParser(prog="syntropy_b200 __runner")
+        rp.add_argument("--ipc-fd", type=int, required=True)
+        rp.add_argument("--region", required=True)
+        ra = rp.parse_args(argv[1:])
+        from ..daemon.runner_proc import serve
+        raise SystemExit(serve(ra.ipc_fd, ra.region))
     ap = argparse.ArgumentParser(prog="syntropy_b200")
     ap.add_argument("--config", default=None, help="TOML config file")
     ap.add_argument("-o", "--set", action="append", default=[], help="section.key=value override")
