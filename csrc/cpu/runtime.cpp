@@ -20,6 +20,7 @@
 #include <torch/extension.h>
 
 #include "syn/frame.h"
+#include "syn/payload.h"
 #include "syn/moe_assign.h"
 #include "syn/spsc.h"
 
@@ -128,6 +129,116 @@ py::tuple frame_decode_py(py::bytes buf) {
   spec["step"] = s.step;
   spec["chan_seq"] = s.chan_seq;
   return py::make_tuple(0, spec, py::bytes(b.data() + eo, el), py::bytes(b.data() + po, pl));
+}
+
+// ------------------------------------------------------------------ payload codecs (syn/payload.h)
+static FrameSpec spec_from(py::dict d) {
+  FrameSpec s;
+  if (d.contains("flags")) s.flags = (uint16_t)py::cast<int64_t>(d["flags"]);
+  if (d.contains("instance")) s.instance = (uint64_t)py::cast<int64_t>(d["instance"]);
+  if (d.contains("epoch_term")) s.epoch_term = (uint64_t)py::cast<int64_t>(d["epoch_term"]);
+  if (d.contains("epoch_seq")) s.epoch_seq = (uint64_t)py::cast<int64_t>(d["epoch_seq"]);
+  if (d.contains("step")) s.step = (uint64_t)py::cast<int64_t>(d["step"]);
+  if (d.contains("chan_seq")) s.chan_seq = (uint64_t)py::cast<int64_t>(d["chan_seq"]);
+  return s;
+}
+
+static py::dict spec_to(const FrameSpec& s) {
+  py::dict d;
+  d["wire_minor"] = s.wire_minor;
+  d["ftype"] = s.ftype;
+  d["flags"] = s.flags;
+  d["instance"] = s.instance;
+  d["epoch_term"] = s.epoch_term;
+  d["epoch_seq"] = s.epoch_seq;
+  d["step"] = s.step;
+  d["chan_seq"] = s.chan_seq;
+  return d;
+}
+
+// rows: contiguous CPU tensor [n_rows, streams * hidden], f32 (dtype 1) or bf16 (dtype 2).
+py::bytes activation_encode_py(py::dict frame, py::dict hdr, std::vector<std::tuple<int64_t, int64_t, int64_t, int64_t>> spans,
+                               torch::Tensor rows) {
+  TORCH_CHECK(!rows.is_cuda() && rows.is_contiguous() && rows.dim() == 2, "rows: contiguous host tensor [n, width]");
+  ActivationHeader h;
+  h.from_stage = (uint16_t)py::cast<int64_t>(hdr["from_stage"]);
+  h.to_stage = (uint16_t)py::cast<int64_t>(hdr["to_stage"]);
+  h.kind = (uint8_t)py::cast<int64_t>(hdr["kind"]);
+  h.streams = (uint8_t)(hdr.contains("streams") ? py::cast<int64_t>(hdr["streams"]) : 1);
+  h.dtype = rows.scalar_type() == torch::kFloat32 ? 1 : rows.scalar_type() == torch::kBFloat16 ? 2 : 0;
+  TORCH_CHECK(h.dtype, "rows dtype must be f32 or bf16");
+  TORCH_CHECK(rows.size(1) % h.streams == 0, "row width must be streams * hidden");
+  h.hidden = (uint32_t)(rows.size(1) / h.streams);
+  h.n_rows = (uint32_t)rows.size(0);
+  if (hdr.contains("part_index")) h.part_index = (uint16_t)py::cast<int64_t>(hdr["part_index"]);
+  if (hdr.contains("part_count")) h.part_count = (uint16_t)py::cast<int64_t>(hdr["part_count"]);
+  if (hdr.contains("kind_arg")) h.kind_arg = (uint32_t)py::cast<int64_t>(hdr["kind_arg"]);
+  if (hdr.contains("kind_flags")) h.kind_flags = (uint32_t)py::cast<int64_t>(hdr["kind_flags"]);
+  std::vector<ActivationSpan> sp;
+  for (const auto& t : spans) {
+    ActivationSpan a;
+    a.seq = (uint64_t)std::get<0>(t);
+    a.first_position = (uint32_t)std::get<1>(t);
+    a.n_positions = (uint32_t)std::get<2>(t);
+    a.row_offset = (uint32_t)std::get<3>(t);
+    TORCH_CHECK((uint64_t)a.row_offset + a.n_positions <= h.n_rows, "span rows beyond the frame's rows");
+    sp.push_back(a);
+  }
+  return py::bytes(activation_encode(spec_from(frame), h, sp, reinterpret_cast<const uint8_t*>(rows.data_ptr())));
+}
+
+py::tuple activation_decode_py(py::bytes buf) {
+  std::string b = buf;
+  FrameSpec fs;
+  ActivationHeader h;
+  std::vector<ActivationSpan> sp;
+  std::vector<uint8_t> rows;
+  const int rc = activation_decode(reinterpret_cast<const uint8_t*>(b.data()), b.size(), &fs, &h, &sp, &rows);
+  if (rc != 0) return py::make_tuple(rc, py::none(), py::none(), py::none(), py::none());
+  py::dict hd;
+  hd["from_stage"] = h.from_stage;
+  hd["to_stage"] = h.to_stage;
+  hd["kind"] = h.kind;
+  hd["dtype"] = h.dtype;
+  hd["streams"] = h.streams;
+  hd["hidden"] = h.hidden;
+  hd["n_rows"] = h.n_rows;
+  hd["part_index"] = h.part_index;
+  hd["part_count"] = h.part_count;
+  hd["kind_arg"] = h.kind_arg;
+  hd["kind_flags"] = h.kind_flags;
+  py::list sl;
+  for (const auto& a : sp) sl.append(py::make_tuple(a.seq, a.first_position, a.n_positions, a.row_offset));
+  auto t = torch::empty({(int64_t)h.n_rows, (int64_t)h.streams * h.hidden},
+                        h.dtype == 1 ? torch::kFloat32 : torch::kBFloat16);
+  if (!rows.empty()) memcpy(t.data_ptr(), rows.data(), rows.size());
+  return py::make_tuple(0, spec_to(fs), hd, sl, t);
+}
+
+py::bytes token_encode_py(py::dict frame, std::vector<std::tuple<int64_t, std::vector<int64_t>, int64_t>> entries) {
+  std::vector<TokenEntry> es;
+  for (const auto& t : entries) {
+    TokenEntry e;
+    e.seq = (uint64_t)std::get<0>(t);
+    for (int64_t x : std::get<1>(t)) e.tokens.push_back((uint32_t)x);
+    e.flags = (uint16_t)std::get<2>(t);
+    es.push_back(std::move(e));
+  }
+  return py::bytes(token_encode(spec_from(frame), es));
+}
+
+py::tuple token_decode_py(py::bytes buf) {
+  std::string b = buf;
+  FrameSpec fs;
+  std::vector<TokenEntry> es;
+  const int rc = token_decode(reinterpret_cast<const uint8_t*>(b.data()), b.size(), &fs, &es);
+  if (rc != 0) return py::make_tuple(rc, py::none(), py::none());
+  py::list out;
+  for (const auto& e : es) {
+    std::vector<int64_t> toks(e.tokens.begin(), e.tokens.end());
+    out.append(py::make_tuple(e.seq, toks, e.flags));
+  }
+  return py::make_tuple(0, spec_to(fs), out);
 }
 
 int64_t crc32c_py(py::bytes b) {
@@ -318,6 +429,10 @@ void register_runtime(py::module& m) {
   m.def("frame_encode", &frame_encode_py);
   m.def("frame_decode", &frame_decode_py);
   m.def("crc32c", &crc32c_py);
+  m.def("activation_encode", &activation_encode_py);
+  m.def("activation_decode", &activation_decode_py);
+  m.def("token_encode", &token_encode_py);
+  m.def("token_decode", &token_decode_py);
   m.def("moe_assign", &moe_assign_py);
   py::class_<IoPool>(m, "IoPool")
       .def(py::init<int>())

@@ -47,7 +47,9 @@ struct Bf16GemmArgs {
 
 template <int BN>
 struct Bf16Cfg {
-  static constexpr int STAGES = BN >= 256 ? 4 : 6;
+  // decode tiles (BN <= 64) keep 4 stages so that two CTAs fit on an SM (no wave tail when the
+  // row tiles x K slices exceed the SM count); prefill tiles take what shared memory allows
+  static constexpr int STAGES = BN >= 256 ? 4 : (BN <= 64 ? 4 : 6);
   static constexpr int A_BYTES = 128 * 64 * 2;  // 16 KB
   static constexpr int B_BYTES = BN * 64 * 2;
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * (A_BYTES + B_BYTES);

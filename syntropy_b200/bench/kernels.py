@@ -190,6 +190,39 @@ def main():
                    extra={"status": int(st.item())})
             wd = w.dequant()
             report(f"cublas_bf16_{M}x{N}x{K}(reference)", timeit(lambda: x @ wd.t(), iters=10), flops=2 * M * N * K)
+    if want("gemm_bf16"):
+        # Llama-3-8B bf16 projections: one GPU and one TP8 rank at decode (64 rows), and a
+        # 2048-token prefill; our tcgen05 GEMM against the library GEMM on the same inputs
+        shapes = [("qkv", 6144, 4096), ("o", 4096, 4096), ("gate_up", 28672, 4096), ("down", 4096, 14336),
+                  ("tp8_qkv", 768, 4096), ("tp8_o", 4096, 512), ("tp8_gate_up", 3584, 4096),
+                  ("tp8_down", 4096, 1792)]
+        from ..ops.core import _bf16_workspace, gemm_status
+        for rows in (T, 2048):
+            for name, N, K in shapes:
+                if rows > 256 and name.startswith("tp8"):
+                    continue
+                reps = max(1, int(math.ceil(300e6 / (N * K * 2)))) if rows <= 256 else 1
+                wl = [(torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16) for _ in range(reps)]
+                x = torch.randn(rows, K, device=dev).to(torch.bfloat16)
+                out = torch.empty(rows, N, dtype=torch.bfloat16, device=dev)
+                ws, ctr = _bf16_workspace(dev, N, K, rows)
+                st = gemm_status(dev)
+                i = [0]
+
+                def fnb():
+                    ext().gemm_bf16(x, wl[i[0] % reps], out, 0, ws, ctr, st)
+                    i[0] += 1
+
+                def fnl():
+                    torch.matmul(x, wl[i[0] % reps].t(), out=out)
+                    i[0] += 1
+                nb, fl = N * K * 2, 2 * rows * N * K
+                tag = f"{name}_{rows}x{N}x{K}"
+                report(f"gemm_bf16_tc_{tag}", timeit(fnb, warmup=max(3, reps), iters=max(20, reps)), nb, fl,
+                       extra={"splits": ext().gemm_bf16_ws(N, K, rows) and None})
+                report(f"gemm_bf16_library_{tag}(reference)", timeit(fnl, warmup=max(3, reps), iters=max(20, reps)),
+                       nb, fl)
+                del wl
     if want("fp8_gemv"):
         from ..formats.fp8 import FP8Weight
         for name, N, K, rows in (("fp8_gemv_dense_7168x18432", 7168, 18432, T), ("fp8_lm_head_129280x7168", 129280, 7168, 2)):

@@ -81,7 +81,8 @@ class TcpChannel:
             hdr = _recv_exact(self.sock, 64)
             ext_len, pay_len = struct.unpack_from("<II", hdr, 48)
             body = _recv_exact(self.sock, ext_len + pay_len)
-            rc, spec, x, p = ext().frame_decode(hdr + body)
+            self.last_frame = hdr + body
+            rc, spec, x, p = ext().frame_decode(self.last_frame)
             if rc != 0:
                 raise ValueError(f"bad frame (code {rc})")
             ft = FrameType(spec["ftype"])
@@ -96,6 +97,43 @@ class TcpChannel:
                 raise ValueError(f"sequence gap: expected {self.recv_seq + 1}, got {spec['chan_seq']}")
             self.recv_seq = spec["chan_seq"]
             return ft, spec, x, p
+
+    def _send_raw(self, build, timeout: float = 30.0):
+        """Send a data frame that `build(chan_seq)` encodes in full (payload codecs)."""
+        with self._cv:
+            if not self._cv.wait_for(lambda: self.credits > 0, timeout=timeout):
+                raise TimeoutError("no credit from receiver")
+            self.credits -= 1
+            self.send_seq += 1
+            seq = self.send_seq
+        if fault_point("net.tcp.send"):
+            return seq
+        f = build(seq)
+        with self._lock:
+            self.sock.sendall(f)
+        return seq
+
+    def send_activation(self, rows, spans, kind: str = "decode", step: int = 0, **kw):
+        """Hidden-state rows of a pipeline hand-off as one Activation frame."""
+        from .frames import encode_activation
+        return self._send_raw(lambda seq: encode_activation(rows, spans, kind=kind, step=step, chan_seq=seq,
+                                                            instance=self.instance, **kw))
+
+    def send_tokens(self, entries, step: int = 0):
+        """Sampled tokens per sequence as one Token frame."""
+        from .frames import encode_tokens
+        return self._send_raw(lambda seq: encode_tokens(entries, step=step, chan_seq=seq, instance=self.instance))
+
+    def recv_payload(self):
+        """Next data frame decoded by its payload codec: ("activation", (spec, header, spans, rows)),
+        ("tokens", (spec, entries)) or (frame type, (spec, ext, payload)) for other types."""
+        from .frames import decode_activation, decode_tokens
+        ft, spec, x, p = self.recv()
+        if ft == FrameType.ACTIVATION:
+            return "activation", decode_activation(self.last_frame)
+        if ft == FrameType.TOKEN:
+            return "tokens", decode_tokens(self.last_frame)
+        return ft, (spec, x, p)
 
     def grant(self, n: int = 1):
         self._write(FrameType.CREDIT, int(n).to_bytes(4, "little"))
