@@ -9,9 +9,11 @@
 //   prefill orientation (T >= 128): A = X (128 tokens), B = W (BN outputs); D[token][output]
 //   decode orientation (T <= 256):  A = W (128 outputs), B = X (BN >= T tokens, rows past T
 //                                    are zero-filled by TMA); D[output][token].  The weight
-//                                    rows stream once; K is split over gridDim.y CTAs when the
-//                                    row tiles alone do not fill the GPU, with an ordered
-//                                    last-CTA reduction of the f32 partials (deterministic).
+//                                    rows stream once; K is split over the CTAs of a thread-
+//                                    block cluster when the row tiles alone do not fill the
+//                                    GPU; the f32 partials meet in shared memory and each CTA
+//                                    sums a column share over distributed shared memory in
+//                                    rank order (deterministic, no global workspace).
 // Warps: 0 TMA producer, 1 TMEM allocator + MMA issuer (one elected thread issues
 // tcgen05.mma kind::f16 M=128 N=BN K=16 and commits each stage to its "empty" barrier),
 // 2..5 epilogue (tcgen05.ld 32x32b of their TMEM lane quarter, warp % 4).
@@ -31,8 +33,6 @@ struct Bf16GemmArgs {
   int mode;                 // 0 bf16, 1 SwiGLU bf16 [T, N/2], 3 f32 +=, 5 f32 =, 6 peer push f32
   void* out;
   int ldo;                  // output row stride (elements)
-  float* ws;                // split-K partials [tiles][splits][128][BN]
-  unsigned* counters;       // [tiles] arrival counters (left zero)
   // peer push (mode 6): row t of output column n -> peers[d] + off_recv + (rank * src_stride + t' * ldo + n) * 4
   // with d = every rank (owner_rows == 0; t' = t) or d = t / owner_rows (t' = t % owner_rows)
   const int64_t* peers;
@@ -58,10 +58,26 @@ struct Bf16Cfg {
 
 constexpr int BF_THREADS = 192;
 
+// Thread-block cluster helpers: every thread of every CTA of the cluster passes the barrier;
+// a load from the same shared-memory offset of CTA `rank` of the cluster.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(const float* local, int rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];\n"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(remote)
+               : "memory");
+  return v;
+}
+
 // Epilogue of one 32-column group of one TMEM lane (row r of D).
 template <int BN>
 __device__ __forceinline__ void bf16_emit(const Bf16GemmArgs& a, int tile_a, int tile_b, int r, int c0,
-                                          const float* v) {
+                                          const float* v, int nc = 32) {
   if (a.decode) {
     const int n = tile_a * 128 + r;  // output feature of this lane
     if (a.mode == 1) {
@@ -72,7 +88,7 @@ __device__ __forceinline__ void bf16_emit(const Bf16GemmArgs& a, int tile_a, int
       for (int j = 0; j < 32; ++j) {
         const float other = __shfl_xor_sync(0xffffffffu, v[j], 8);
         const int t = c0 + j;
-        if (gate && t < a.T && n < a.N)
+        if (gate && j < nc && t < a.T && n < a.N)
           reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)t * a.ldo + m] = f2bf(silu(v[j]) * other);
       }
       return;
@@ -81,7 +97,7 @@ __device__ __forceinline__ void bf16_emit(const Bf16GemmArgs& a, int tile_a, int
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const int t = c0 + j;
-      if (t >= a.T) continue;
+      if (j >= nc || t >= a.T) continue;
       const int64_t o = (int64_t)t * a.ldo + n;
       if (a.mode == 0) {
         reinterpret_cast<__nv_bfloat16*>(a.out)[o] = f2bf(v[j]);
@@ -168,7 +184,6 @@ __global__ void __launch_bounds__(BF_THREADS, 1) tc_gemm_bf16_kernel(const __gri
   __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], done_bar;
   __shared__ uint32_t tmem_base;
   __shared__ volatile int s_abort;
-  __shared__ int s_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // decode: blockIdx.x = weight row tile, blockIdx.y = K slice; prefill: x = token tile, y = output tile
@@ -242,65 +257,63 @@ __global__ void __launch_bounds__(BF_THREADS, 1) tc_gemm_bf16_kernel(const __gri
         if (ok) bf16_emit<BN>(a, tile_a, tile_b, r, c0, v);
       }
     } else {
-      // split-K: every slice stores its partial tile; the last CTA of the row tile sums them
-      // in slice order (the same order whichever CTA arrives last) and runs the epilogue
-      float* mine = a.ws + (((int64_t)tile_a * a.splits + split) * 128 + r) * BN;
+      // split-K over the CTAs of a cluster: the slice's partial tile goes to this CTA's own
+      // shared memory (the pipeline stages are free once the last MMA committed)
+      float* part = reinterpret_cast<float*>(smem) + r * (BN + 4);
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t u[32];
         tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + c0, u);
 #pragma unroll
         for (int j = 0; j < 32; j += 4)
-          *reinterpret_cast<float4*>(mine + c0 + j) =
+          *reinterpret_cast<float4*>(part + c0 + j) =
               make_float4(ok ? __uint_as_float(u[j]) : 0.f, ok ? __uint_as_float(u[j + 1]) : 0.f,
                           ok ? __uint_as_float(u[j + 2]) : 0.f, ok ? __uint_as_float(u[j + 3]) : 0.f);
       }
-      __threadfence();
-      asm volatile("bar.sync 1, 128;\n" ::: "memory");
-      if (threadIdx.x == 64) {
-        const unsigned prev = atomicAdd(&a.counters[tile_a], 1u);
-        s_last = prev == (unsigned)a.splits - 1;
-        if (s_last) a.counters[tile_a] = 0u;  // ready for the next launch
-      }
-      asm volatile("bar.sync 1, 128;\n" ::: "memory");
-      if (s_last) {
-        __threadfence();
-        const float* base = a.ws + ((int64_t)tile_a * a.splits * 128 + r) * BN;
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0.f;
-          for (int sp = 0; sp < a.splits; ++sp) {
-            const float* p = base + (int64_t)sp * 128 * BN + c0;
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              const float4 q = __ldcg(reinterpret_cast<const float4*>(p + j));
-              v[j] += q.x;
-              v[j + 1] += q.y;
-              v[j + 2] += q.z;
-              v[j + 3] += q.w;
-            }
-          }
-          bf16_emit<BN>(a, tile_a, tile_b, r, c0, v);
-        }
-      }
     }
-    if (a.mode == 6) {
-      // completion of the whole grid: every CTA publishes its peer stores, the last raises
-      // one flag per peer (the arrival counter is reset before the release)
-      __threadfence_system();
-      asm volatile("bar.sync 1, 128;\n" ::: "memory");
-      if (threadIdx.x == 64) {
-        const unsigned total = gridDim.x * gridDim.y;
-        const unsigned prev = atomicAdd(a.done_ctr, 1u);
-        if (prev == total - 1) {
-          *a.done_ctr = 0u;
-          __threadfence_system();
-          const uint32_t seq = (*a.step_ctr) * (uint32_t)a.n_layers + (uint32_t)a.layer + 1u;
-          for (int q = 0; q < a.n_peers; ++q)
-            st_release_sys(reinterpret_cast<uint32_t*>(a.peers[q] + a.off_flag) + a.rank, seq);
+  }
+  if (a.splits > 1) {
+    // every slice's partial is in its CTA's shared memory: each CTA sums one column share of
+    // the tile over the cluster's CTAs in rank order (distributed shared memory; the same
+    // order on every launch: deterministic) and runs the epilogue on it
+    cluster_sync_all();
+    if (warp >= 2) {
+      const int r = (warp & 3) * 32 + lane;
+      const int w = BN / a.splits, c_lo = split * w;
+      const float* part = reinterpret_cast<const float*>(smem) + r * (BN + 4) + c_lo;
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = 0.f;
+      for (int p = 0; p < a.splits; ++p) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          if (j < w) {
+            const float4 q = ld_dsmem_f4(part + j, p);
+            v[j] += q.x;
+            v[j + 1] += q.y;
+            v[j + 2] += q.z;
+            v[j + 3] += q.w;
+          }
         }
+      }
+      bf16_emit<BN>(a, tile_a, tile_b, r, c_lo, v, w);
+    }
+    cluster_sync_all();  // no CTA leaves while a peer still reads its shared memory
+  }
+  if (warp >= 2 && a.mode == 6) {
+    // completion of the whole grid: every CTA publishes its peer stores, the last raises
+    // one flag per peer (the arrival counter is reset before the release)
+    __threadfence_system();
+    asm volatile("bar.sync 1, 128;\n" ::: "memory");
+    if (threadIdx.x == 64) {
+      const unsigned total = gridDim.x * gridDim.y;
+      const unsigned prev = atomicAdd(a.done_ctr, 1u);
+      if (prev == total - 1) {
+        *a.done_ctr = 0u;
+        __threadfence_system();
+        const uint32_t seq = (*a.step_ctr) * (uint32_t)a.n_layers + (uint32_t)a.layer + 1u;
+        for (int q = 0; q < a.n_peers; ++q)
+          st_release_sys(reinterpret_cast<uint32_t*>(a.peers[q] + a.off_flag) + a.rank, seq);
       }
     }
   }
@@ -334,8 +347,24 @@ static cudaError_t launch_bf16(const CUtensorMap& ma, const CUtensorMap& mb, con
     if (e != cudaSuccess) return e;
     set = true;
   }
-  tc_gemm_bf16_kernel<BN><<<grid, BF_THREADS, smem, s>>>(ma, mb, a);
-  return cudaGetLastError();
+  if (a.splits == 1) {
+    tc_gemm_bf16_kernel<BN><<<grid, BF_THREADS, smem, s>>>(ma, mb, a);
+    return cudaGetLastError();
+  }
+  // the K slices of one row tile form a cluster (1 x splits): partials meet in its shared memory
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(BF_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = (unsigned)a.splits;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, tc_gemm_bf16_kernel<BN>, ma, mb, a);
 }
 
 // Split-K plan of the decode orientation: the K slices per row tile so that the grid fills
@@ -344,17 +373,13 @@ int bf16_gemm_splits(int N, int K, int T) {
   if (T >= 128) return 1;
   const int tiles = (N + 127) / 128, kb = K / 64;
   int s = 1;
-  while (tiles * s * 2 <= 2 * num_sms() && kb / (s * 2) >= 4) s *= 2;
+  // K slices (a cluster of at most 8 CTAs) while the grid stays within two CTAs per SM and
+  // each slice keeps at least 4 K stages
+  while (s < 8 && tiles * s * 2 <= 2 * num_sms() && kb / (s * 2) >= 4) s *= 2;
   return s;
 }
 
-size_t bf16_gemm_ws_floats(int N, int K, int T) {
-  if (T >= 128) return 0;
-  const int s = bf16_gemm_splits(N, K, T);
-  if (s == 1) return 0;
-  const int bn = T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
-  return (size_t)((N + 127) / 128) * s * 128 * bn;
-}
+size_t bf16_gemm_ws_floats(int, int, int) { return 0; }  // split-K partials stay on chip
 
 cudaError_t launch_tc_gemm_bf16(const void* x, int T, int ldx, const void* w, int N, int K, int mode, void* out,
                                 int ldo, float* ws, size_t ws_floats, unsigned* counters, const PeerPush* pp,
@@ -395,12 +420,6 @@ cudaError_t launch_tc_gemm_bf16(const void* x, int T, int ldx, const void* w, in
     const int bn = T <= 32 ? 32 : T <= 64 ? 64 : 128;
     a.decode = 1;
     a.splits = bf16_gemm_splits(N, K, T);
-    if (a.splits > 1) {
-      if (ws == nullptr || counters == nullptr || (size_t)((N + 127) / 128) * a.splits * 128 * bn > ws_floats)
-        return cudaErrorInvalidValue;
-      a.ws = ws;
-      a.counters = counters;
-    }
     if (!encode_2d(&ma, w, N, K, K, 128) || !encode_2d(&mb, x, T, K, ldx, bn)) return cudaErrorInvalidValue;
     const dim3 grid((unsigned)((N + 127) / 128), (unsigned)a.splits);
     if (bn == 32) return launch_bf16<32>(ma, mb, a, grid, s);

@@ -27,7 +27,7 @@ LAYERS = {
     "ops": 1, "kv": 1, "experts": 1, "net": 1, "store": 1, "cluster": 1, "config": 1,
     "models": 2, "parallel": 2, "planner": 2,
     "runtime": 3,
-    "api": 4, "daemon": 4, "bench": 4,
+    "api": 4, "daemon": 4, "bench": 4, "testkit": 4,
     "cli": 5,
 }
 ORACLES = {("models", "reference"), ("runtime", "sampling_ref")}
