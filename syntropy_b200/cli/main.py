@@ -101,9 +101,13 @@ def cmd_config(args, cfg):
 
 def cmd_plan(args, cfg):
     from ..models.config import get_config
-    from ..planner import plan_placement
+    from ..planner import HardwareModel, plan_placement
+    hw = None
+    if getattr(args, "probe", None):  # price from a probe report of this machine
+        with open(args.probe) as f:
+            hw = HardwareModel.from_probe(json.load(f))
     p = plan_placement(get_config(cfg.model.name), args.gpus, args.batch, args.ctx,
-                       cache_frac=args.expert_cache_frac, fused=cfg.parallel.fused_collectives)
+                       cache_frac=args.expert_cache_frac, fused=cfg.parallel.fused_collectives, hw=hw)
     print(p.describe() if args.explain else json.dumps({"mode": p.stages[0].mode.value,
                                                         "expert_cache_frac": p.expert_cache_frac,
                                                         "cpu_expert_share": round(p.cpu_expert_share, 3),
@@ -144,7 +148,11 @@ def cmd_serve(args, cfg):
 
 def cmd_probe(args, cfg):
     from ..probe import probe_all
-    print(json.dumps(probe_all(quick=not args.full), indent=2))
+    rep = probe_all(quick=not args.full)
+    if getattr(args, "out", None):
+        with open(args.out, "w") as f:
+            json.dump(rep, f, indent=2)
+    print(json.dumps(rep, indent=2))
 
 
 def cmd_doctor(args, cfg):
@@ -192,6 +200,7 @@ def main(argv=None):
     p.add_argument("--ctx", type=int, default=2048)
     p.add_argument("--expert-cache-frac", type=float, default=None)
     p.add_argument("--explain", action="store_true")
+    p.add_argument("--probe", default=None, help="probe report (JSON) to price the plan with")
     p = sub.add_parser("run")
     p.add_argument("--prompt", default="Hello")
     p.add_argument("--tokens", default="")
@@ -205,6 +214,7 @@ def main(argv=None):
     p.add_argument("--device", default="cuda:0")
     p = sub.add_parser("probe")
     p.add_argument("--full", action="store_true")
+    p.add_argument("--out", default=None, help="also write the report to this file")
     sub.add_parser("doctor")
     p = sub.add_parser("bundle")
     p.add_argument("--out", default="syntropy-bundle.tar.gz")

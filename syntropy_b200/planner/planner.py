@@ -43,6 +43,33 @@ class HardwareModel:
     tflops: float = 1422.0         # sustained bf16
 
     @classmethod
+    def from_probe(cls, probe: dict, base: "HardwareModel | None" = None) -> "HardwareModel":
+        """Prices from a probe report (`python -m syntropy_b200 probe --full --out FILE`): HBM copy,
+        pinned host-to-device and peer copy bandwidths, peer round-trip latency, the CUDA-graph
+        kernel gap, and the host CPU expert pool's rate.  Missing probes keep the base value
+        (the defaults above, measured on a B200 node)."""
+        hw = base or cls()
+        g = probe.get("gpu", {}) or {}
+        h = probe.get("host", {}) or {}
+        if g.get("hbm_copy_gbs"):
+            hw.hbm_gbs = float(g["hbm_copy_gbs"])
+        if g.get("h2d_gbs"):
+            hw.pcie_gbs = float(g["h2d_gbs"])
+            # host experts the GPU reads are staged with the same DMA copies (bulk staging)
+            hw.pcie_read_gbs = float(g["h2d_gbs"]) * 0.9
+        if g.get("peer_copy_gbs"):
+            hw.nvlink_gbs = float(g["peer_copy_gbs"])
+        if g.get("peer_latency_us"):
+            hw.nvlink_alpha_us = float(g["peer_latency_us"])
+        if g.get("graph_kernel_gap_us"):
+            hw.launch_gap_us = float(g["graph_kernel_gap_us"])
+        if h.get("cpu_expert_gbs"):
+            hw.cpu_expert_gbs = float(h["cpu_expert_gbs"])
+        if g.get("mem_gb"):
+            hw.vram_gb = float(g["mem_gb"]) - 2.0
+        return hw
+
+    @classmethod
     def from_measured(cls, path: str | None = None) -> "HardwareModel":
         hw = cls()
         path = path or os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")

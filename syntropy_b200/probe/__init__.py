@@ -22,15 +22,53 @@ def _time_cuda(fn, iters=5):
     return best * 1e-3
 
 
-def probe_host() -> dict:
-    """CPU, ISA level, memory, NUMA host tiers and GPU NUMA affinity (`probe.host`)."""
+def probe_host(quick: bool = True) -> dict:
+    """CPU, ISA level, memory, NUMA host tiers and GPU NUMA affinity (`probe.host`); with
+    `quick` off also the host read bandwidth and the CPU expert pool's rate (4-bit expert
+    rows per second on the allowed cores, the planner's cpu_expert_gbs)."""
     from .host import host_report
     info = {"platform": platform.platform(), "cpus": os.cpu_count()}
     try:
         info.update(host_report("/"))
     except OSError as e:
         info["error"] = str(e)
+    if not quick:
+        info.update(probe_cpu_experts())
     return info
+
+
+def probe_cpu_experts(threads: int | None = None, seconds: float = 1.0) -> dict:
+    """Host read bandwidth and the CPU expert kernel's rate: one thread's GB/s of 4-bit weights
+    on an expert-sized matrix (2 rows, the decode case), times the worker count (the pool's
+    threads run independent experts)."""
+    import threading
+
+    import torch
+
+    from .._ext import ext
+    e = ext()
+    cpus = sorted(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else list(range(os.cpu_count() or 1))
+    threads = threads or max(1, len(cpus) - 2)
+    out = {"cpu_threads": threads}
+    if not e.cpu_simd_available():
+        return out
+    out["cpu_read_gbs"] = round(e.cpu_read_gbs(1 << 28, threads, 2), 1)
+    N, K = 3072, 4096
+    w = torch.randn(N, K) * 0.02
+    rows = e.q4_quantize_rows_cpu(w)
+    qw, sm = e.q4_rows_to_tiled_cpu(rows, N, K)
+    x = torch.randn(2, K).bfloat16()
+    nbytes = qw.numel() * 4 + sm.numel() * 2
+    e.cpu_q4t_gemv(qw, sm, x, N, -1)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds / 4:
+        e.cpu_q4t_gemv(qw, sm, x, N, -1)
+        n += 1
+    per_thread = n * nbytes / (time.perf_counter() - t0) / 1e9
+    out["cpu_expert_gbs_per_thread"] = round(per_thread, 2)
+    out["cpu_expert_gbs"] = round(min(per_thread * threads, out["cpu_read_gbs"]), 1)
+    del threading
+    return out
 
 
 def probe_gpu(quick: bool = True) -> dict:
@@ -61,13 +99,16 @@ def probe_gpu(quick: bool = True) -> dict:
             c = torch.empty(n, dtype=torch.uint8, device="cuda:1")
             t = _time_cuda(lambda: c.copy_(a))
             out["peer_copy_gbs"] = round(n / t / 1e9, 1)
+            s0, s1 = torch.empty(64, dtype=torch.uint8, device=dev), torch.empty(64, dtype=torch.uint8, device="cuda:1")
+            t = _time_cuda(lambda: s1.copy_(s0), iters=20)
+            out["peer_latency_us"] = round(t * 1e6, 2)  # a small peer copy: the alpha of a hand-off
         except Exception as e:  # pragma: no cover
             out["peer_copy_error"] = str(e)
     return out
 
 
 def probe_all(quick: bool = True) -> dict:
-    return {"host": probe_host(), "gpu": probe_gpu(quick), "time": time.time()}
+    return {"host": probe_host(quick), "gpu": probe_gpu(quick), "time": time.time()}
 
 
 def doctor() -> dict:
