@@ -112,8 +112,8 @@ def main():
                          "rows are expected to reach at least half of the experts")
     ap.add_argument("--cpu-experts", type=float, default=None,
                     help="share of each layer's host-tier experts computed by host CPU threads during decode "
-                         "(the rest is read over PCIe by the GPU); 0 = off (default 0.75 on one GPU with a VRAM "
-                         "cap, else 0)")
+                         "(the rest is read over PCIe by the GPU); 0 = off (default: the share that balances the "
+                         "rank's CPU workers against its host link)")
     ap.add_argument("--cpu-threads", type=int, default=None,
                     help="CPU expert threads per rank (default: the rank's share of the node's cores, less one)")
     ap.add_argument("--step-profile", action="store_true",
@@ -222,8 +222,8 @@ def main():
         local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
         cpus, _ = rank_cpus(local, local_world)
         threads = args.cpu_threads or len(cpus)
-        if args.cpu_experts is None:  # one GPU: the measured best share; else the balanced one
-            args.cpu_experts = 0.75 if world == 1 else balanced_share(threads, local_world)
+        if args.cpu_experts is None:  # the share that balances the CPU workers and the host link
+            args.cpu_experts = balanced_share(threads, local_world)
         if args.cpu_experts > 0 and threads > 0:
             tier = CpuExpertTier(cache, cfg, max_rows=runner.max_batch, cpu_share=args.cpu_experts,
                                  threads=threads, cpus=cpus, ep=ep)

@@ -31,11 +31,12 @@ from .._ext import ext
 
 # Host-tier rates used to split each rank's cold experts between its CPU workers and its PCIe
 # link (bytes of 4-bit weights per second).  Measured on the B200 node: the AVX-512 BF16 pool
-# moves ~4.8 GB/s per worker thread; one GPU reads host rows in place at ~30-40 GB/s while the
-# CPU also streams DRAM, and ~25 GB/s per GPU when the two GPUs behind one PCIe switch read at
-# once.
+# moves ~4.8 GB/s per worker thread; one GPU stages host rows with bulk DMA at ~45 GB/s while
+# the CPU also streams DRAM (capped Qwen3 decode on one GPU and 14 workers: shares 0.5 / 0.6 /
+# 0.75 gave 57.3 / 65.4 / 55.8 tok/s, so the balance sits near 0.6), and ~25 GB/s per GPU when
+# the two GPUs behind one PCIe switch read at once.
 CPU_GBS_PER_THREAD = 4.8
-PCIE_GBS_ALONE, PCIE_GBS_SHARED = 35.0, 25.0
+PCIE_GBS_ALONE, PCIE_GBS_SHARED = 45.0, 25.0
 
 
 def rank_cpus(local_rank: int, local_world: int, allowed: list[int] | None = None) -> tuple[list[int], list[int]]:
