@@ -1,9 +1,27 @@
+#include <string>
 // Registration of every exported function (one place, so the surface is easy to audit).
 #include "ops.h"
+
+#if __has_include("syn_build_stamp.h")
+#include "syn_build_stamp.h"  // written by setup.py: the source hash and ABI version
+#endif
+#ifndef SYN_BUILD_ID
+#define SYN_BUILD_ID "unstamped"
+#endif
+#ifndef SYN_ABI_VERSION
+#define SYN_ABI_VERSION 0
+#endif
+
+// Build identity for loaders (plain C, exported): the hash of the native sources this object
+// was built from and the ABI version of its interface.
+extern "C" __attribute__((visibility("default"))) const char* syn_build_id() { return SYN_BUILD_ID; }
+extern "C" __attribute__((visibility("default"))) int syn_abi_version() { return SYN_ABI_VERSION; }
 
 namespace syn {
 
 void register_all(pybind11::module& m) {
+  m.def("build_id", [] { return std::string(syn_build_id()); });
+  m.def("abi_version", [] { return syn_abi_version(); });
   m.def("q4_quantize_rows_cpu", &q4_quantize_rows_cpu);
   m.def("q4_dequant_rows_cpu", &q4_dequant_rows_cpu);
   m.def("q4_rows_to_tiled_cpu", &q4_rows_to_tiled_cpu);

@@ -23,6 +23,24 @@ def _sources():
     return [os.path.relpath(s, ROOT) for s in out]
 
 
+def _buildinfo():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("buildinfo", os.path.join(ROOT, "syntropy_b200", "buildinfo.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.source_hash(ROOT), mod.ABI_VERSION
+
+
+BUILD_ID, ABI_VERSION = _buildinfo()
+# the build identity the loader checks (syn_build_id / syn_abi_version), in a generated header
+# that only csrc/cpu/register.cpp includes (rewritten only when it changes)
+STAMP_DIR = os.path.join(ROOT, "build", "stamp")
+os.makedirs(STAMP_DIR, exist_ok=True)
+_stamp = f'#define SYN_BUILD_ID "{BUILD_ID}"\n#define SYN_ABI_VERSION {ABI_VERSION}\n'
+_stamp_path = os.path.join(STAMP_DIR, "syn_build_stamp.h")
+if not os.path.exists(_stamp_path) or open(_stamp_path).read() != _stamp:
+    with open(_stamp_path, "w") as f:
+        f.write(_stamp)
 CXX_FLAGS = ["-O3", "-std=c++17", "-fno-strict-aliasing", "-Wno-unused-function"]
 LIBS = ["rt"]
 # Link the shared libstdc++ that torch itself uses.  A toolchain whose libstdc++.so dev link
@@ -51,7 +69,7 @@ setup(
         CUDAExtension(
             name="syntropy_b200._C",
             sources=_sources(),
-            include_dirs=[os.path.join(ROOT, "csrc", "include"), os.path.join(ROOT, "csrc")],
+            include_dirs=[os.path.join(ROOT, "csrc", "include"), os.path.join(ROOT, "csrc"), STAMP_DIR],
             extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
             libraries=LIBS,
             extra_link_args=LINK_FLAGS,
