@@ -322,6 +322,20 @@ def main():
             step_prof["rank0"] = {k: round(allk[0].get(k, 0.0), 4) for k in kinds}
         else:
             step_prof = {k: round(agg[k], 4) for k in kinds}
+        # the same step as cost terms beside the planner's prediction for this configuration
+        try:
+            from syntropy_b200.core.plan import ParallelismMode
+            from syntropy_b200.obs.spans import step_cost_record
+            from syntropy_b200.planner.planner import HardwareModel, price_decode
+            mode = ParallelismMode.LOCAL if world == 1 else (ParallelismMode.EP if cfg.is_moe else
+                                                             ParallelismMode.INTRA_NODE_TP)
+            pred = price_decode(cfg, world, args.batch, args.prompt + args.warmup + args.steps, mode,
+                                args.expert_cache_frac if cfg.is_moe else 1.0, HardwareModel.from_measured(),
+                                fused=not args.baseline, cpu_share=args.cpu_experts)
+            rec = step_cost_record(eng.stats["decode_steps"], runner.step_profile(), pred)
+            step_prof["cost_terms"] = rec.rows()
+        except Exception as exc:  # noqa: BLE001  (informational)
+            step_prof["cost_terms"] = f"{type(exc).__name__}: {exc}"[:200]
         step_prof["host_lockstep_ms_per_step"] = round(1e3 * eng.stats.get("lockstep_s", 0.0) /
                                                        max(1, eng.stats["decode_steps"] + eng.stats["prefill_steps"]),
                                                        4)

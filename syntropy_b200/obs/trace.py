@@ -36,6 +36,7 @@ class FlightRecorder:
 
 
 FLIGHT = FlightRecorder()
+SINKS: list = []  # extra span sinks (e.g. obs.spans.SpanRing instances a daemon drains)
 _local = threading.local()
 
 
@@ -68,3 +69,5 @@ def span(name: str, **attrs):
         s.t1_ns = time.monotonic_ns()
         _local.cur = parent
         FLIGHT.record(s)
+        for sink in SINKS:
+            sink.push(s)
