@@ -173,8 +173,8 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
         gemm_grouped(x, ptrs[0], ptrs[1], _identity_off(T, x.device), W.N, W.K, gm, None, out, 1, W.qw, W.sm)
         return out
     if isinstance(W, torch.Tensor) and W.dtype == torch.bfloat16 and x.dtype == torch.bfloat16 and \
-            W.shape[0] % 32 == 0 and W.shape[1] % 64 == 0 and x.stride(-1) == 1 and _BF16_TC[0] and \
-            (mode != GEMV_SWIGLU or W.shape[0] % 16 == 0):
+            W.shape[0] % 32 == 0 and W.shape[1] % 64 == 0 and x.stride(-1) == 1 and \
+            (mode != GEMV_SWIGLU or W.shape[0] % 16 == 0) and _bf16_provider(x, W, mode) == "tcgen05":
         # bf16 weights: tcgen05 GEMM (decode orientation with split-K below 128 rows)
         N, K = W.shape
         gm = {GEMV_STORE: 0 if out.dtype == torch.bfloat16 else 5, GEMV_SWIGLU: 1, GEMV_ADD_F32: 3}[mode]
@@ -193,7 +193,44 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
     return out
 
 
-_BF16_TC = [__import__("os").environ.get("SYN_BF16_TC", "1") == "1"]  # 0: bf16 GEMMs through the library
+# bf16 GEMM provider: "1" the tcgen05 kernel, "0" the library GEMM, "auto" chosen per shape by
+# the selector (certified against the f32 reference, then timed; 3% margin for the default)
+_BF16_TC = [__import__("os").environ.get("SYN_BF16_TC", "1")]
+SELECTOR = None
+
+
+def _bf16_provider(x, W, mode) -> str:
+    choice = _BF16_TC[0]
+    if choice != "auto":
+        return "tcgen05" if choice == "1" else "library"
+    global SELECTOR
+    from .numerics import Candidate, Selector
+    if SELECTOR is None:
+        SELECTOR = Selector()
+    T = x.shape[0]
+    bucket = 1 << max(0, (T - 1).bit_length())
+    key = f"linear_bf16:{W.shape[0]}x{W.shape[1]}x{bucket}x{mode}"
+    if key in SELECTOR.decisions:
+        return SELECTOR.decisions[key]
+    if torch.cuda.is_current_stream_capturing():
+        return "tcgen05"  # decisions are made outside capture (the warm-up passes come first)
+    N, K = W.shape
+    xs = x.contiguous()
+
+    def ours(a, w):
+        o = torch.empty(a.shape[0], N, dtype=torch.float32, device=a.device)
+        ws, ctr = _bf16_workspace(a.device, N, K, a.shape[0])
+        ext().gemm_bf16(a, w, o, 5, ws, ctr, gemm_status(a.device))
+        return o
+
+    def lib(a, w):
+        return (a @ w.t()).float()
+    pick = SELECTOR.choose("linear_bf16", (N, K, bucket, mode),
+                           [Candidate("tcgen05", ours, "bf16_f32acc"), Candidate("library", lib, "bf16_out")],
+                           (xs, W if W.is_contiguous() else W.contiguous()),
+                           lambda a, w: a.float() @ w.float().t())
+    SELECTOR.decisions[key] = pick
+    return pick
 _BF16_WS: dict = {}
 
 

@@ -89,3 +89,31 @@ def test_bf16_model_matches_reference(cuda):
     out = LLMEngine(ModelRunner(mw, max_batch=4, max_seq_len=256)).generate([prompt[:9], prompt[:33]],
                                                                            SamplingParams(max_tokens=6))
     assert all(len(o) == 6 for o in out)
+
+
+def test_bf16_gemm_accumulates_in_f32_and_is_selectable(cuda):
+    """The accumulation detector sees f32 accumulation in the tcgen05 GEMM; the selector certifies
+    both providers of a decode shape against the f32 reference and picks one."""
+    from syntropy_b200.ops import core
+    from syntropy_b200.ops.numerics import Selector, accumulation_class
+
+    def dot(x, w):
+        o = torch.empty(1, 128, dtype=torch.float32, device=cuda)
+        wp = torch.zeros(128, x.shape[1], dtype=torch.bfloat16, device=cuda)
+        wp[0] = w[0]
+        ws, ctr = _bf16_workspace(cuda, 128, x.shape[1], 1)
+        ext().gemm_bf16(x, wp, o, 5, ws, ctr, gemm_status(cuda))
+        return o[:, :1]
+    assert accumulation_class(dot, device=cuda) == "f32"
+    saved, core._BF16_TC[0], core.SELECTOR = core._BF16_TC[0], "auto", Selector()
+    try:
+        x = (torch.randn(64, 4096, device=cuda) * 0.5).to(torch.bfloat16)
+        w = (torch.randn(1024, 4096, device=cuda) * 0.02).to(torch.bfloat16)
+        out = torch.empty(64, 1024, dtype=torch.bfloat16, device=cuda)
+        ops.linear(x, w, out, ops.GEMV_STORE)
+        assert _rel(out, x.float() @ w.float().t()) < 1e-2
+        certs = [r for r in core.SELECTOR.log if "certified" in r]
+        assert {r["candidate"] for r in certs} == {"tcgen05", "library"} and all(r["certified"] for r in certs)
+        assert list(core.SELECTOR.decisions.values())[0] in ("tcgen05", "library")
+    finally:
+        core._BF16_TC[0], core.SELECTOR = saved, None
