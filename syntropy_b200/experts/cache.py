@@ -214,6 +214,40 @@ class ExpertCache:
             self.cpu_tier.assign()
         torch.cuda.empty_cache()
 
+    def save_host_tier(self, path: str) -> dict:
+        """Writes every bank's host-tier rows (tiled 4-bit weights and scales) and the
+        residency map as a pack, so a restart reloads the cold experts from disk."""
+        from ..store.pack import write_pack
+        tensors = {}
+        for li, b in enumerate(self.banks):
+            for which, p in enumerate(b.parts):
+                if p is not None:
+                    tensors[f"{li}.{which}.q"] = p["qh"]
+                    tensors[f"{li}.{which}.s"] = p["sh"]
+        side = write_pack(path, tensors)
+        import json
+        with open(path + ".residency.json", "w") as f:
+            json.dump([{"slot_of": b.slot_of, "host_of": b.host_of} for b in self.banks], f)
+        return side
+
+    def load_host_tier(self, path: str, threads: int = 8) -> int:
+        """Fills the host tier from a pack written by save_host_tier (direct-I/O reads through the
+        native I/O pool).  The residency map must be the one the pack was written with."""
+        import json
+
+        from ..store.pack import read_pack_into
+        with open(path + ".residency.json") as f:
+            res = json.load(f)
+        if [(r["slot_of"], r["host_of"]) for r in res] != [(b.slot_of, b.host_of) for b in self.banks]:
+            raise ValueError("pack was written with another expert residency")
+        targets = {}
+        for li, b in enumerate(self.banks):
+            for which, p in enumerate(b.parts):
+                if p is not None:
+                    targets[f"{li}.{which}.q"] = p["qh"]
+                    targets[f"{li}.{which}.s"] = p["sh"]
+        return read_pack_into(path, targets, threads=threads)
+
     def staged_ptrs(self, L):
         """Pointer tables with every expert of layer L in VRAM: residents in place, host
         experts copied into one of two staging banks.  Used by prefill, whose GEMM streams
