@@ -159,8 +159,9 @@ def main():
         B = args.batch // world  # data-parallel attention: each rank serves its share of sequences
         if world > 1:
             from syntropy_b200.parallel.ep import EPGroup
-            ep = EPGroup(ctx, cfg.n_experts, cfg.top_k, cfg.hidden, cap=B, n_layers=cfg.n_layers,
-                         fused=not args.baseline)
+            # MTP verify windows hold 2 rows per sequence: the combine slots take them all
+            ep = EPGroup(ctx, cfg.n_experts, cfg.top_k, cfg.hidden, cap=B * (2 if cfg.n_mtp and not args.no_mtp else 1),
+                         n_layers=cfg.n_layers, fused=not args.baseline)
         t0 = time.time()
         mw = prepare_weights(cfg, dev, seed=args.seed, max_pos=max_pos, expert_range=ep.expert_range if ep else None)
     else:
@@ -206,9 +207,8 @@ def main():
                 cache.enable_decode_staging()
             else:
                 cache.enable_decode_prefetch(cfg.n_experts)
-    fp8_ep = ep is not None and cfg.weight_quant == "fp8"  # fp8 experts use the NCCL row exchange, eagerly
     # TP's NCCL all-reduce baseline is captured into the decode graphs too (ranks step in lockstep)
-    graphs = not ((ep is not None and not ep.fused) or fp8_ep or pp is not None)
+    graphs = not ((ep is not None and not ep.fused) or pp is not None)
     use_mtp = cfg.n_mtp > 0 and mw.mtp is not None and not args.no_mtp and pp is None and tp is None
     # MTP verify windows hold 2 rows per sequence
     runner = ModelRunner(mw, max_batch=B * (2 if use_mtp else 1), max_seq_len=max_len + 16, ep=ep, tp=tp, pp=pp,
@@ -370,7 +370,7 @@ def main():
     wdesc = {"q4": "4-bit block weights (32-elem, fp16 scale+min)", "bf16": "bf16 weights",
              "fp8": "fp8 e4m3 weights, 128x128 block scales"}.get(wq, wq)
     if cfg.is_moe:
-        par = (f"ep{world}+dp-attention" + ("" if ep is None or (ep.fused and not fp8_ep) else " (nccl baseline)")) \
+        par = (f"ep{world}+dp-attention" + ("" if ep is None or ep.fused else " (nccl baseline)")) \
             if world > 1 else "single-gpu"
     else:
         par = "single-gpu" if world == 1 else (f"tp{tp_size}" + (f"xpp{args.pp}" if args.pp > 1 else "") +

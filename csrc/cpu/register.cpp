@@ -44,6 +44,7 @@ void register_all(pybind11::module& m) {
   m.def("f8_rows_to_tiled", &f8_rows_to_tiled, "row-major e4m3 bytes -> mma-fragment tiled layout");
   m.def("f8_tiled_to_rows", &f8_tiled_to_rows, "inverse of f8_rows_to_tiled");
   m.def("f8_gemv", &f8_gemv, "block-scaled fp8 grouped GEMV (e4m3 x e4m3 tensor cores)");
+  m.def("f8_gemv_ep", &f8_gemv_ep, "fp8 expert down projection into source ranks' combine slots + layer flags");
   m.def("attn_prefill", &attn_prefill, "causal prefill attention over the paged KV cache (GQA, head_dim 128)");
   m.def("q4_gemv_dense_ws", &q4_gemv_dense_ws, "split-K workspace (floats) of the dense GEMV, -1 if unsupported");
   m.def("rmsnorm", &rmsnorm);

@@ -11,6 +11,7 @@
 // streaming load per lane and group; no shared-memory staging.
 #include "common.cuh"
 #include "gemv_epilogue.cuh"
+#include "sync.cuh"
 
 namespace syn {
 
@@ -101,14 +102,15 @@ __global__ void __launch_bounds__(128, 4) f8_gemv_kernel(GemvArgs a) {
   const int p0 = a.tok_off[e];
   const int cnt = a.tok_off[e + 1] - p0;
   const int tile = blockIdx.x * 4 + warp;
-  if (cnt <= 0 || tile >= a.N / 16) return;
+  // no early return: with done_ctr set every CTA must reach the completion count below
+  const bool active = cnt > 0 && tile < a.N / 16;
   const int KG = a.K >> 6, KB = a.K >> 7;
   // K slice (split-K over gridDim.z, dense only): 128-column blocks [kb_lo, kb_hi)
   const int KS = gridDim.z, ks = blockIdx.z;
   const int kb_lo = (int)((int64_t)KB * ks / KS), kb_hi = (int)((int64_t)KB * (ks + 1) / KS);
   const uint4* __restrict__ wq = reinterpret_cast<const uint4*>(a.qw_ptrs[e]) + (int64_t)tile * KG * 64;
   const float* __restrict__ ws = reinterpret_cast<const float*>(a.sm_ptrs[e]) + (int64_t)(tile >> 3) * KB;
-  for (int c0 = 0; c0 < cnt; c0 += NT * 8) {
+  for (int c0 = 0; active && c0 < cnt; c0 += NT * 8) {
     const int ccount = min(cnt - c0, NT * 8);
     // B rows (token g of each n-tile) and the two accumulator tokens (2t, 2t+1) per n-tile
     const uint8_t* xrow[NT];
@@ -197,6 +199,24 @@ __global__ void __launch_bounds__(128, 4) f8_gemv_kernel(GemvArgs a) {
         }
       }
   }
+  if (a.done_ctr != nullptr) {
+    // Expert parallelism: the rows above went to their source ranks' combine slots (mode
+    // GEMV_SCALED_F32_PTR); every CTA publishes them and the last one raises this layer's
+    // flag on every peer (the counter is reset for the next launch before the release).
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+      const unsigned prev = atomicAdd(a.done_ctr, 1u);
+      if (prev == total - 1) {
+        *a.done_ctr = 0u;
+        __threadfence_system();
+        const uint32_t seq = (*a.step_ctr) * (uint32_t)a.n_layers + (uint32_t)a.layer + 1u;
+        for (int q = 0; q < a.sig_n; ++q)
+          st_release_sys(reinterpret_cast<uint32_t*>(a.sig_peers[q] + a.sig_off) + a.sig_rank, seq);
+      }
+    }
+  }
 }
 
 // Split-K reduction in slice order (deterministic) + the epilogue: thread per (row, output).
@@ -230,6 +250,8 @@ int f8_gemv_ksplit(int N, int K, int E, int rows, size_t ws_floats) {
 
 cudaError_t launch_f8_gemv(const GemvArgs& a_in, cudaStream_t s) {
   if (a_in.N % 16 || a_in.K % 128 || !a_in.xq || !a_in.xs || a_in.ldx % 4) return cudaErrorInvalidValue;
+  // split-K finishes in a second kernel, which the completion flags would not wait for
+  if (a_in.done_ctr && a_in.ws_part) return cudaErrorInvalidValue;
   GemvArgs a = a_in;
   const int ks = a.ws_part ? f8_gemv_ksplit(a.N, a.K, a.E, a.ws_rows, a.ws_floats) : 1;
   dim3 grid((unsigned)((a.N / 16 + 3) / 4), (unsigned)a.E, (unsigned)ks);

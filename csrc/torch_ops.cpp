@@ -406,6 +406,7 @@ void q4_gemv_ep(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, t
   TORCH_CHECK(N % 16 == 0 && K % 64 == 0 && x.size(1) == K, "q4_gemv_ep shapes");
   TORCH_CHECK(done_ctr.is_cuda() && done_ctr.scalar_type() == torch::kInt32, "done_ctr cuda int32");
   GemvArgs a;
+  memset(&a, 0, sizeof(a));
   a.x = x.data_ptr();
   a.qw_ptrs = qw_ptrs.data_ptr<int64_t>();
   a.sm_ptrs = sm_ptrs.data_ptr<int64_t>();
@@ -698,6 +699,49 @@ void f8_gemv(torch::Tensor xq, torch::Tensor xs, torch::Tensor qw_ptrs, torch::T
   SYN_CHECK_CUDA(launch_f8_gemv(a, cur_stream()));
 }
 
+// Expert-parallel down projection over fp8 experts: xq/xs are the quantised SwiGLU rows of
+// every pair (contiguous, pair order), row p goes scaled by route_w[p] to the address
+// out_ptrs[p] (a source rank's combine slot, local or peer), and the last CTA raises this
+// layer's flags on every peer unless done_ctr is empty.
+void f8_gemv_ep(torch::Tensor xq, torch::Tensor xs, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs,
+                torch::Tensor tok_off, torch::Tensor route_w, torch::Tensor out_ptrs, int64_t N, int64_t K,
+                torch::Tensor done_ctr, torch::Tensor peers, int64_t sig_off, int64_t sig_rank, torch::Tensor step_ctr,
+                int64_t n_layers, int64_t layer, int64_t nt_hint) {
+  SYN_CHECK_INPUT(xq);
+  TORCH_CHECK(xq.scalar_type() == torch::kUInt8 && xq.dim() == 2 && xq.size(1) == K && xq.stride(1) == 1, "xq");
+  TORCH_CHECK(xs.scalar_type() == torch::kFloat32 && xs.dim() == 2 && xs.size(1) == K / 128 && xs.is_contiguous(),
+              "xs f32 [rows, K/128]");
+  TORCH_CHECK(qw_ptrs.scalar_type() == torch::kInt64 && sm_ptrs.scalar_type() == torch::kInt64 &&
+                  qw_ptrs.numel() == sm_ptrs.numel() && tok_off.numel() == qw_ptrs.numel() + 1,
+              "pointer tables / CSR");
+  TORCH_CHECK(out_ptrs.scalar_type() == torch::kInt64 && route_w.scalar_type() == torch::kFloat32, "out_ptrs / route_w");
+  TORCH_CHECK(done_ctr.is_cuda() && done_ctr.scalar_type() == torch::kInt32, "done_ctr cuda int32");
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.xq = xq.data_ptr<uint8_t>();
+  a.xs = xs.data_ptr<float>();
+  a.ldx = (int)xq.stride(0);
+  a.qw_ptrs = qw_ptrs.data_ptr<int64_t>();
+  a.sm_ptrs = sm_ptrs.data_ptr<int64_t>();
+  a.tok_off = tok_off.data_ptr<int32_t>();
+  a.route_w = route_w.data_ptr<float>();
+  a.out_ptrs = out_ptrs.data_ptr<int64_t>();
+  a.N = (int)N;
+  a.K = (int)K;
+  a.mode = 4;
+  a.E = (int)qw_ptrs.numel();
+  a.nt_hint = (int)nt_hint;
+  a.done_ctr = done_ctr.numel() ? reinterpret_cast<unsigned*>(done_ctr.data_ptr()) : nullptr;
+  a.sig_peers = peers.data_ptr<int64_t>();
+  a.sig_off = sig_off;
+  a.sig_n = (int)peers.numel();
+  a.sig_rank = (int)sig_rank;
+  a.step_ctr = reinterpret_cast<const uint32_t*>(step_ctr.data_ptr());
+  a.n_layers = (int)n_layers;
+  a.layer = (int)layer;
+  const at::cuda::CUDAGuard guard(xq.device());
+  SYN_CHECK_CUDA(launch_f8_gemv(a, cur_stream()));
+}
 
 void mla_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables, torch::Tensor ctx_lens,
                 torch::Tensor out, double scale, torch::Tensor part_o, torch::Tensor part_ml, int64_t pages_per_split) {

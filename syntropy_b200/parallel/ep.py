@@ -85,18 +85,24 @@ class EPGroup:
             ext().ep_step_begin(self.step_ctr)
 
     def moe_decode_fused(self, layer: int, h, topk_ids, topk_w, x, gu, dn, mid, next_norm, h_out, eps,
-                         stamp=None, tier=None, L=None, before_gemv=None):
+                         stamp=None, tier=None, L=None, before_gemv=None, after_dispatch=None):
         """One MoE layer for the local rows (h: bf16 [T, H]) through NVLink dispatch/combine.
         stamp: device-timestamp callback of a profiled step; tier: the host CPU expert tier,
         which computes its share of this rank's cold experts for every rank's rows while the
         GPU runs the rest (its rows reach the sources' combine slots over NVLink); L: the
         model layer (its expert banks tell which experts the CPU owns); before_gemv: called right
-        before the expert GEMVs (after dispatch and the CPU hand-off)."""
+        before the expert GEMVs (after dispatch and the CPU hand-off); after_dispatch: local work
+        that overlaps the rows' flight to their owners (e.g. a shared expert adding into x).
+        4-bit and block-scaled fp8 experts (gu.is_fp8): the fp8 path quantises the received rows
+        and the SwiGLU rows to e4m3 (1x128 scales) before each GEMV; the down GEMV of both stores
+        each pair's row into its source rank's combine slot and raises the layer's flags."""
         e = ext()
         c = self._common(layer)
         stamp = stamp or (lambda _lab: None)
         e.ep_dispatch(*c, h, topk_ids, topk_w)
         stamp(f"layer{layer}.dispatch")
+        if after_dispatch is not None:
+            after_dispatch()
         e.ep_build(*c, self.tok_off, self.tok_idx, self.pair_w, self.pair_dst)
         stamp(f"layer{layer}.build")
         # every layer hands off when a tier exists (the CPU answers with no rows for a layer whose
@@ -111,11 +117,18 @@ class EPGroup:
         ops.linear_grouped(self.recv_x, gu, self.tok_off, self.tok_idx, mid[:P], ops.GEMV_SWIGLU,
                            qw_ptrs=gu.qw_ptrs, sm_ptrs=gu.sm_ptrs)
         stamp(f"layer{layer}.gate_up")
-        e.q4_gemv_ep(mid[:P], dn.qw_ptrs, dn.sm_ptrs, self.tok_off, torch.empty(0, dtype=torch.int32, device=h.device),
-                     self.pair_w, self.pair_dst, dn.N, dn.K, self._no_flags if cpu else self.done_ctr[layer:layer + 1],
-                     self.region.peers, self.off_flag_comb, self.rank, self.step_ctr, self.n_layers, layer,
-                     ops.moe_nt_hint(self.N * h.shape[0] * self.k // self.N, self.E_loc), self.E_loc,
-                     bool(getattr(dn, "bank_contiguous", False)))
+        flags = self._no_flags if cpu else self.done_ctr[layer:layer + 1]
+        nt = ops.moe_nt_hint(self.N * h.shape[0] * self.k // self.N, self.E_loc)
+        if getattr(dn, "is_fp8", False):
+            xq, xs = e.f8_quant_act(mid[:P])
+            e.f8_gemv_ep(xq, xs, dn.qw_ptrs, dn.sm_ptrs, self.tok_off, self.pair_w, self.pair_dst, dn.N, dn.K, flags,
+                         self.region.peers, self.off_flag_comb, self.rank, self.step_ctr, self.n_layers, layer, nt)
+            ops.core._launched()
+        else:
+            e.q4_gemv_ep(mid[:P], dn.qw_ptrs, dn.sm_ptrs, self.tok_off,
+                         torch.empty(0, dtype=torch.int32, device=h.device), self.pair_w, self.pair_dst, dn.N, dn.K,
+                         flags, self.region.peers, self.off_flag_comb, self.rank, self.step_ctr, self.n_layers, layer,
+                         nt, self.E_loc, bool(getattr(dn, "bank_contiguous", False)))
         stamp(f"layer{layer}.down")
         if cpu:  # the CPU's rows, then this layer's completion flags
             tier.collect_ep(self.pair_dst, layer)

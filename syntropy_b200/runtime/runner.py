@@ -153,8 +153,7 @@ class ModelRunner:
         if cfg.is_moe:
             E, k = cfg.n_experts, cfg.top_k
             ep = self.ep
-            fp8_experts = any(L.experts_gu is not None and L.experts_gu.is_fp8 for L in self.mw.layers)
-            if ep is not None and (not ep.fused or fp8_experts):  # NCCL all-gather / reduce-scatter rows
+            if ep is not None and not ep.fused:  # NCCL all-gather / reduce-scatter rows
                 B = B * ep.N  # baseline routes every rank's rows on every rank
                 b["h_all"] = torch.zeros(B, H, dtype=act, device=dev)
                 b["x_part"] = torch.zeros(B, H, dtype=torch.float32, device=dev)
@@ -318,7 +317,7 @@ class ModelRunner:
         ops.rms_norm(x, L.ffn_norm, cfg.rms_eps, out=h)
         nw = nxt.attn_norm if nxt else mw.final_norm
         ep = self.ep
-        if ep is not None and (not ep.fused or L.experts_gu.is_fp8):  # the fused EP kernel is 4-bit only
+        if ep is not None and not ep.fused:
             return self._moe_decode_baseline(L, B, nw)
         pred = L.router_cat is not None
         rw = L.router_cat if pred else L.router
@@ -361,9 +360,12 @@ class ModelRunner:
         k = cfg.top_k
         gu, dn = L.experts_gu, L.experts_down
         if ep is not None:
+            # the shared expert (every rank holds it whole) adds into x while the rows fly to their owners
+            shared_into_x = (lambda: self._shared_expert(L, h, into=x)) if L.shared_gu is not None else None
             ep.moe_decode_fused(layer, h, mb["topk_ids"], mb["topk_w"], x, gu, dn, b["moe_mid"], nw, h,
                                 cfg.rms_eps, stamp=self._stamp if self._stamping else None,
-                                tier=cache.cpu_tier if cache is not None else None, L=L, before_gemv=staged)
+                                tier=cache.cpu_tier if cache is not None else None, L=L, before_gemv=staged,
+                                after_dispatch=shared_into_x)
             if li is not None:  # this layer's staging bank is free: stage the layer after next
                 self._stage_issue(li + 2)
             return
@@ -458,13 +460,14 @@ class ModelRunner:
             self.expert_stats.observe(li, host[self._layer_index[id(L)]])
         return cache.rebalance(self.expert_stats, max_swaps_per_layer)
 
-    def _shared_expert(self, L, h):
-        """Shared-expert FFN output (f32 [T, H]) added to the routed combine."""
+    def _shared_expert(self, L, h, into=None):
+        """Shared-expert FFN output (f32 [T, H]) added to the routed combine; with `into` (f32
+        [T, H]) the output is added to that tensor instead."""
         T = h.shape[0]
         mid = torch.empty(T, L.shared_gu.N // 2 if hasattr(L.shared_gu, "N") else L.shared_gu.shape[0] // 2,
                           dtype=h.dtype, device=h.device)
         ops.linear(h, L.shared_gu, mid, ops.GEMV_SWIGLU)
-        out = torch.zeros(T, self.cfg.hidden, dtype=torch.float32, device=h.device)
+        out = into if into is not None else torch.zeros(T, self.cfg.hidden, dtype=torch.float32, device=h.device)
         ops.linear(mid, L.shared_down, out, ops.GEMV_ADD_F32)
         return out
 
@@ -498,6 +501,8 @@ class ModelRunner:
         red = b["moe_red"][:B]
         reduce_scatter_rows(red, part, ep.ctx.group)
         x.add_(red)
+        if L.shared_gu is not None:  # every rank holds the shared expert whole: local rows only
+            self._shared_expert(L, h, into=x)
         ops.rms_norm(x, nw, cfg.rms_eps, out=h)
 
     def decode(self, B: int):

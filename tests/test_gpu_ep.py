@@ -23,28 +23,36 @@ from syntropy_b200.runtime.runner import ModelRunner
 from syntropy_b200.parallel.dist import init_distributed, shutdown
 from syntropy_b200.parallel.ep import EPGroup
 fused = os.environ["FUSED"] == "1"
+spec_on = os.environ.get("SPEC") == "1"
 ctx = init_distributed(timeout_s=60)
-cfg = get_config("small-qwen-moe")
-ep = EPGroup(ctx, cfg.n_experts, cfg.top_k, cfg.hidden, cap=4, n_layers=cfg.n_layers, fused=fused)
+cfg = get_config(os.environ.get("MODEL", "small-qwen-moe"))
+# MTP verify windows hold 2 rows per sequence
+ep = EPGroup(ctx, cfg.n_experts, cfg.top_k, cfg.hidden, cap=8 if spec_on else 4, n_layers=cfg.n_layers, fused=fused)
 mw = prepare_weights(cfg, ctx.device, seed=7, expert_range=ep.expert_range)
-runner = ModelRunner(mw, max_batch=4, max_seq_len=256, ep=ep, use_graphs=fused)
-eng = LLMEngine(runner, dist_ctx=ctx)
+runner = ModelRunner(mw, max_batch=8 if spec_on else 4, max_seq_len=256, ep=ep, use_graphs=fused)
+spec = None
+if spec_on:
+    from syntropy_b200.runtime.spec import MTPDrafter, SpecConfig
+    spec = SpecConfig(drafter=MTPDrafter(runner))
+eng = LLMEngine(runner, dist_ctx=ctx, spec=spec)
 g = torch.Generator().manual_seed(3)
 prompts = [torch.randint(0, cfg.vocab, (n,), generator=g).tolist() for n in (11, 30, 7, 19)]
 outs = eng.generate(prompts[ctx.rank::ctx.world], SamplingParams(max_tokens=8))
 st = ep.check_status()
 runner.graphs.clear()
-print("RESULT " + json.dumps({"rank": ctx.rank, "outs": outs, "status": st}), flush=True)
+acc = eng.stats.get("spec_accepted", 0) / max(1, eng.stats.get("spec_drafted", 0)) if spec_on else None
+print("RESULT " + json.dumps({"rank": ctx.rank, "outs": outs, "status": st, "accept": acc}), flush=True)
 shutdown(ctx)
 """
 
 
-def _run(fused: bool):
-    port = 29611 if fused else 29612
+def _run(fused: bool, model: str = "small-qwen-moe", spec: bool = False, port: int | None = None):
+    port = port or (29611 if fused else 29612)
     procs = []
     for r in range(2):
         env = dict(os.environ, ROOT=ROOT, FUSED="1" if fused else "0", RANK=str(r), WORLD_SIZE="2",
-                   LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+                   LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                   MODEL=model, SPEC="1" if spec else "0")
         procs.append(subprocess.Popen([sys.executable, "-c", WORKER], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
     res = {}
@@ -79,6 +87,30 @@ def test_ep_fused_matches_baseline_and_single_gpu():
     single = LLMEngine(ModelRunner(mw, max_batch=4, max_seq_len=256)).generate(prompts, SamplingParams(max_tokens=8))
     agree = sum(a == b for r in (0, 1) for a, b in zip(fused[r]["outs"], single[r::2]))
     assert agree >= 3  # different f32 summation association (per-rank partials) may flip a near-tie
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_fused_fp8_deepseek_with_mtp_matches_single_gpu():
+    """DeepSeek-style layers (MLA, block-scaled fp8 experts, a shared expert, group-limited
+    routing) through the fused dispatch/combine with MTP drafts verified in the same decode
+    graphs, against one GPU holding every expert without drafts."""
+    from syntropy_b200.models.config import get_config
+    from syntropy_b200.models.transformer import prepare_weights
+    from syntropy_b200.runtime.engine import LLMEngine, SamplingParams
+    from syntropy_b200.runtime.runner import ModelRunner
+    fused = _run(True, "small-deepseek", spec=True, port=29613)
+    for r in (0, 1):
+        assert fused[r]["status"] == 0
+        assert fused[r]["accept"] is not None
+    cfg = get_config("small-deepseek")
+    mw = prepare_weights(cfg, torch.device("cuda:0"), seed=7)
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, cfg.vocab, (n,), generator=g).tolist() for n in (11, 30, 7, 19)]
+    single = LLMEngine(ModelRunner(mw, max_batch=4, max_seq_len=256)).generate(prompts, SamplingParams(max_tokens=8))
+    # greedy with exact acceptance emits the target's own tokens: sequences agree up to near-tie flips
+    # (fp8 activations and a different f32 summation association)
+    agree = sum(a[:4] == b[:4] for r in (0, 1) for a, b in zip(fused[r]["outs"], single[r::2]))
+    assert agree >= 2, (fused, single)
 
 
 TP_WORKER = r"""
