@@ -341,6 +341,12 @@ def main():
                                                        4)
     status = ep.check_status() if ep is not None else 0
     tier_stats = tier.stats() if tier is not None else None
+    # the timed run's expert placement (the all-resident measurement below changes it)
+    placed = {"prefetch": bool(cache is not None and cache.prefetch),
+              "staging": ("bulk" if cache.stage_all else "predicted" if cache.prefetch else "none")
+              if cache is not None else "none",
+              "host_gb": round(cache.host_bytes() / 1e9, 2) if cache is not None else 0.0,
+              "weights_gb": mw.nbytes() / 1e9}
     uncapped = None
     if cache is not None and not args.no_uncapped:
         # same model and batch with every expert VRAM-resident (the cap lifted); informational,
@@ -387,16 +393,15 @@ def main():
                    "global_batch": args.batch, "seq_len": args.prompt, "decode_len": decode_len,
                    "parallelism": par,
                    "expert_cache_frac": args.expert_cache_frac if cfg.is_moe else 1.0,
-                   "host_tier_gb": round(cache.host_bytes() / 1e9, 2) if cache is not None else 0.0,
-                   "expert_prefetch": bool(cache is not None and cache.prefetch),
-                   "expert_staging": ("bulk" if cache.stage_all else "predicted" if cache.prefetch else "none")
-                   if cache is not None else "none",
+                   "host_tier_gb": placed["host_gb"],
+                   "expert_prefetch": placed["prefetch"],
+                   "expert_staging": placed["staging"],
                    "expert_rebalance_every": args.rebalance_every if cache is not None else 0,
                    "cpu_expert_share": args.cpu_experts if tier is not None else 0.0,
                    "cpu_expert_threads": tier.threads if tier is not None else 0,  # per rank
                    "host_cores": len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else None,
-                   "l2": f"inputs larger than L2 ({mw.nbytes() / 1e9:.0f} GB of weights streamed per step per rank)",
-                   "weights_gb": round(mw.nbytes() / 1e9, 2), "weight_build_s": round(t_weights, 1)},
+                   "l2": f"inputs larger than L2 ({placed['weights_gb']:.0f} GB of weights streamed per step per rank)",
+                   "weights_gb": round(placed["weights_gb"], 2), "weight_build_s": round(t_weights, 1)},
         "clocks": clk.summary(),
         "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": runner.desc.nbytes,
                 "d2h_bytes_per_step": 4 * B},

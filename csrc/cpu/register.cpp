@@ -46,6 +46,7 @@ void register_all(pybind11::module& m) {
   m.def("f8_gemv", &f8_gemv, "block-scaled fp8 grouped GEMV (e4m3 x e4m3 tensor cores)");
   m.def("f8_gemv_ep", &f8_gemv_ep, "fp8 expert down projection into source ranks' combine slots + layer flags");
   m.def("attn_prefill", &attn_prefill, "causal prefill attention over the paged KV cache (GQA, head_dim 128)");
+  m.def("attn_prefill_tc", &attn_prefill_tc, "causal paged prefill attention on tcgen05 (TMA, TMEM)");
   m.def("q4_gemv_dense_ws", &q4_gemv_dense_ws, "split-K workspace (floats) of the dense GEMV, -1 if unsupported");
   m.def("rmsnorm", &rmsnorm);
   m.def("moe_combine_rmsnorm", &moe_combine_rmsnorm);

@@ -75,12 +75,12 @@ __device__ __forceinline__ float4 ld_dsmem_f4(const float* local, int rank) {
 }
 
 // Epilogue of one 32-column group of one TMEM lane (row r of D).
-template <int BN>
+template <int BN, int MODE, bool DEC>
 __device__ __forceinline__ void bf16_emit(const Bf16GemmArgs& a, int tile_a, int tile_b, int r, int c0,
                                           const float* v, int nc = 32) {
-  if (a.decode) {
+  if constexpr (DEC) {
     const int n = tile_a * 128 + r;  // output feature of this lane
-    if (a.mode == 1) {
+    if constexpr (MODE == 1) {
       // interleaved gate/up: rows 16c..16c+7 gate, 16c+8..16c+15 up; the partner is lane ^ 8
       const bool gate = (n & 8) == 0;
       const int m = (n >> 4) * 8 + (n & 7);
@@ -99,11 +99,11 @@ __device__ __forceinline__ void bf16_emit(const Bf16GemmArgs& a, int tile_a, int
       const int t = c0 + j;
       if (j >= nc || t >= a.T) continue;
       const int64_t o = (int64_t)t * a.ldo + n;
-      if (a.mode == 0) {
+      if constexpr (MODE == 0) {
         reinterpret_cast<__nv_bfloat16*>(a.out)[o] = f2bf(v[j]);
-      } else if (a.mode == 3) {
+      } else if constexpr (MODE == 3) {
         reinterpret_cast<float*>(a.out)[o] += v[j];
-      } else if (a.mode == 5) {
+      } else if constexpr (MODE == 5) {
         reinterpret_cast<float*>(a.out)[o] = v[j];
       } else {  // 6: peer push
         if (a.owner_rows > 0) {
@@ -124,14 +124,14 @@ __device__ __forceinline__ void bf16_emit(const Bf16GemmArgs& a, int tile_a, int
   const int t = tile_a * 128 + r;
   const int n0 = tile_b * BN + c0;
   if (t >= a.T || n0 >= a.N) return;  // N % 32 == 0: a 32-column group is all in or all out
-  if (a.mode == 1) {
+  if constexpr (MODE == 1) {
     __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.out) + (int64_t)t * a.ldo + n0 / 2;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int gi = (j / 8) * 16 + (j % 8);
       o[j] = f2bf(silu(v[gi]) * v[gi + 8]);
     }
-  } else if (a.mode == 0) {
+  } else if constexpr (MODE == 0) {
     uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out) + (int64_t)t * a.ldo + n0);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -142,12 +142,12 @@ __device__ __forceinline__ void bf16_emit(const Bf16GemmArgs& a, int tile_a, int
       w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
       o[j] = w;
     }
-  } else if (a.mode == 3 || a.mode == 5) {
+  } else if constexpr (MODE == 3 || MODE == 5) {
     float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + (int64_t)t * a.ldo + n0);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       float4 w = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-      if (a.mode == 3) {
+      if constexpr (MODE == 3) {
         const float4 p = o[j];
         w.x += p.x;
         w.y += p.y;
@@ -169,7 +169,7 @@ __device__ __forceinline__ void bf16_emit(const Bf16GemmArgs& a, int tile_a, int
   }
 }
 
-template <int BN>
+template <int BN, int MODE, bool DEC>
 __global__ void __launch_bounds__(BF_THREADS, 1) tc_gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                                  const __grid_constant__ CUtensorMap tmap_b,
                                                                  Bf16GemmArgs a) {
@@ -188,8 +188,8 @@ __global__ void __launch_bounds__(BF_THREADS, 1) tc_gemm_bf16_kernel(const __gri
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // decode: blockIdx.x = weight row tile, blockIdx.y = K slice; prefill: x = token tile, y = output tile
   const int tile_a = blockIdx.x;
-  const int tile_b = a.decode ? 0 : blockIdx.y;
-  const int split = a.decode ? blockIdx.y : 0;
+  const int tile_b = DEC ? 0 : blockIdx.y;
+  const int split = DEC ? blockIdx.y : 0;
   const int KB = a.K / 64;
   const int kb0 = (int)((int64_t)KB * split / a.splits), kb1 = (int)((int64_t)KB * (split + 1) / a.splits);
   const int a_row0 = tile_a * 128, b_row0 = tile_b * BN;
@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(BF_THREADS, 1) tc_gemm_bf16_kernel(const __gri
     const int r = quarter * 32 + lane;  // D row (TMEM lane)
     const bool ok = mbar_wait(&done_bar, 0, a.status, &s_abort) && kb1 > kb0;
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-    if (a.splits == 1) {
+    if (!DEC || a.splits == 1) {
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t u[32];
@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(BF_THREADS, 1) tc_gemm_bf16_kernel(const __gri
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = ok ? __uint_as_float(u[j]) : 0.f;
-        if (ok) bf16_emit<BN>(a, tile_a, tile_b, r, c0, v);
+        if (ok) bf16_emit<BN, MODE, DEC>(a, tile_a, tile_b, r, c0, v);
       }
     } else {
       // split-K over the CTAs of a cluster: the slice's partial tile goes to this CTA's own
@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(BF_THREADS, 1) tc_gemm_bf16_kernel(const __gri
       }
     }
   }
-  if (a.splits > 1) {
+  if (DEC && a.splits > 1) {
     // every slice's partial is in its CTA's shared memory: each CTA sums one column share of
     // the tile over the cluster's CTAs in rank order (distributed shared memory; the same
     // order on every launch: deterministic) and runs the epilogue on it
@@ -296,11 +296,11 @@ __global__ void __launch_bounds__(BF_THREADS, 1) tc_gemm_bf16_kernel(const __gri
           }
         }
       }
-      bf16_emit<BN>(a, tile_a, tile_b, r, c_lo, v, w);
+      bf16_emit<BN, MODE, DEC>(a, tile_a, tile_b, r, c_lo, v, w);
     }
     cluster_sync_all();  // no CTA leaves while a peer still reads its shared memory
   }
-  if (warp >= 2 && a.mode == 6) {
+  if (MODE == 6 && warp >= 2) {
     // completion of the whole grid: every CTA publishes its peer stores, the last raises
     // one flag per peer (the arrival counter is reset before the release)
     __threadfence_system();
@@ -336,19 +336,19 @@ static bool encode_2d(CUtensorMap* map, const void* base, int rows, int cols, in
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN>
+template <int BN, int MODE, bool DEC>
 static cudaError_t launch_bf16(const CUtensorMap& ma, const CUtensorMap& mb, const Bf16GemmArgs& a, dim3 grid,
                                cudaStream_t s) {
   static bool set = false;
   constexpr size_t smem = Bf16Cfg<BN>::SMEM;
+  auto* kern = tc_gemm_bf16_kernel<BN, MODE, DEC>;
   if (!set) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(tc_gemm_bf16_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     set = true;
   }
   if (a.splits == 1) {
-    tc_gemm_bf16_kernel<BN><<<grid, BF_THREADS, smem, s>>>(ma, mb, a);
+    kern<<<grid, BF_THREADS, smem, s>>>(ma, mb, a);
     return cudaGetLastError();
   }
   // the K slices of one row tile form a cluster (1 x splits): partials meet in its shared memory
@@ -364,7 +364,22 @@ static cudaError_t launch_bf16(const CUtensorMap& ma, const CUtensorMap& mb, con
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, tc_gemm_bf16_kernel<BN>, ma, mb, a);
+  return cudaLaunchKernelEx(&cfg, kern, ma, mb, a);
+}
+
+// One instantiation per (tile width, epilogue, orientation): each kernel carries only its own
+// epilogue code (a small kernel's time is otherwise dominated by instruction fetch on every SM).
+template <int BN, bool DEC>
+static cudaError_t launch_mode(const CUtensorMap& ma, const CUtensorMap& mb, const Bf16GemmArgs& a, dim3 grid,
+                               cudaStream_t s) {
+  switch (a.mode) {
+    case 0: return launch_bf16<BN, 0, DEC>(ma, mb, a, grid, s);
+    case 1: return launch_bf16<BN, 1, DEC>(ma, mb, a, grid, s);
+    case 3: return launch_bf16<BN, 3, DEC>(ma, mb, a, grid, s);
+    case 5: return launch_bf16<BN, 5, DEC>(ma, mb, a, grid, s);
+    case 6: return launch_bf16<BN, 6, DEC>(ma, mb, a, grid, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 // Split-K plan of the decode orientation: the K slices per row tile so that the grid fills
@@ -422,9 +437,9 @@ cudaError_t launch_tc_gemm_bf16(const void* x, int T, int ldx, const void* w, in
     a.splits = bf16_gemm_splits(N, K, T);
     if (!encode_2d(&ma, w, N, K, K, 128) || !encode_2d(&mb, x, T, K, ldx, bn)) return cudaErrorInvalidValue;
     const dim3 grid((unsigned)((N + 127) / 128), (unsigned)a.splits);
-    if (bn == 32) return launch_bf16<32>(ma, mb, a, grid, s);
-    if (bn == 64) return launch_bf16<64>(ma, mb, a, grid, s);
-    return launch_bf16<128>(ma, mb, a, grid, s);
+    if (bn == 32) return launch_mode<32, true>(ma, mb, a, grid, s);
+    if (bn == 64) return launch_mode<64, true>(ma, mb, a, grid, s);
+    return launch_mode<128, true>(ma, mb, a, grid, s);
   }
   // prefill: tokens are the 128-row operand, BN output columns per CTA
   const int bn = N % 256 == 0 ? 256 : 128;
@@ -432,8 +447,8 @@ cudaError_t launch_tc_gemm_bf16(const void* x, int T, int ldx, const void* w, in
   a.splits = 1;
   if (!encode_2d(&ma, x, T, K, ldx, 128) || !encode_2d(&mb, w, N, K, K, bn)) return cudaErrorInvalidValue;
   const dim3 grid((unsigned)((T + 127) / 128), (unsigned)((N + bn - 1) / bn));
-  if (bn == 256) return launch_bf16<256>(ma, mb, a, grid, s);
-  return launch_bf16<128>(ma, mb, a, grid, s);
+  if (bn == 256) return launch_mode<256, false>(ma, mb, a, grid, s);
+  return launch_mode<128, false>(ma, mb, a, grid, s);
 }
 
 }  // namespace syn

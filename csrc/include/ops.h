@@ -80,6 +80,9 @@ void verify_accept(torch::Tensor logits, torch::Tensor draft, torch::Tensor temp
 int64_t q4_gemv_dense_ws(int64_t N, int64_t K, int64_t rows);
 void attn_prefill(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor block_tables, torch::Tensor cu_q,
                   torch::Tensor kv_lens, torch::Tensor out, int64_t max_q_len, double scale);
+void attn_prefill_tc(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor block_tables,
+                     torch::Tensor cu_q, torch::Tensor kv_lens, torch::Tensor out, int64_t max_q_len, double scale,
+                     torch::Tensor status);
 std::vector<torch::Tensor> f8_quant_act(torch::Tensor x);
 torch::Tensor f8_rows_to_tiled(torch::Tensor q, int64_t N, int64_t K);
 torch::Tensor f8_tiled_to_rows(torch::Tensor tiled, int64_t N, int64_t K);

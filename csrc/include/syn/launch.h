@@ -105,6 +105,12 @@ cudaError_t launch_q4_gemv_dense6(const GemvArgs& a, float* ws, unsigned* counte
 cudaError_t launch_attn_prefill(const void* q, const void* kc, const void* vc, const int32_t* block_tables,
                                 const int32_t* cu_q, const int32_t* kv_lens, void* out, int nseq, int max_q_len,
                                 int Hq, int Hkv, int D, int max_blocks, float scale, cudaStream_t s);
+// tcgen05 variant (TMA-fed, S and P V on the tensor cores, softmax warps between); Tq: rows
+// of q, n_blocks: pages of the cache; *status bit 4: a pipeline wait timed out.
+cudaError_t launch_attn_prefill_tc(const void* q, int Tq, const void* kc, const void* vc, int n_blocks,
+                                   const int32_t* block_tables, const int32_t* cu_q, const int32_t* kv_lens, void* out,
+                                   int nseq, int max_q_len, int Hq, int Hkv, int D, int max_blocks, float scale,
+                                   int* status, cudaStream_t s);
 // ---- MLA decode attention (absorbed; latent 512 + rope 64) over the paged latent cache ----
 cudaError_t launch_mla_decode(const void* q, const void* cache, const int32_t* block_tables, const int32_t* ctx_lens,
                               float* part_o, float* part_ml, float* out, int B, int H, int max_blocks,

@@ -627,6 +627,32 @@ void attn_prefill(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Te
                                      (int)block_tables.size(1), (float)scale, cur_stream()));
 }
 
+// The same contract on tcgen05 (status: int32 error word, bit 4 = a pipeline wait timed out).
+void attn_prefill_tc(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor block_tables,
+                     torch::Tensor cu_q, torch::Tensor kv_lens, torch::Tensor out, int64_t max_q_len, double scale,
+                     torch::Tensor status) {
+  SYN_CHECK_INPUT(q);
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && q.dim() == 3 && q.is_contiguous(), "q bf16 [T, Hq, D]");
+  TORCH_CHECK(kc.scalar_type() == torch::kBFloat16 && kc.dim() == 4 && kc.size(2) == 16 && kc.is_contiguous(),
+              "k cache bf16 [blocks, Hkv, 16, D]");
+  TORCH_CHECK(vc.sizes() == kc.sizes() && vc.is_contiguous() && vc.scalar_type() == torch::kBFloat16, "v cache");
+  TORCH_CHECK(out.sizes() == q.sizes() && out.scalar_type() == torch::kBFloat16 && out.is_contiguous(), "out");
+  TORCH_CHECK(block_tables.scalar_type() == torch::kInt32 && block_tables.dim() == 2 && block_tables.is_contiguous(),
+              "block tables int32 [nseq, max_blocks]");
+  const int64_t nseq = block_tables.size(0);
+  TORCH_CHECK(cu_q.scalar_type() == torch::kInt32 && cu_q.numel() == nseq + 1, "cu_q int32 [nseq + 1]");
+  TORCH_CHECK(kv_lens.scalar_type() == torch::kInt32 && kv_lens.numel() == nseq, "kv_lens int32 [nseq]");
+  TORCH_CHECK(q.size(2) == 128 && kc.size(3) == 128, "head_dim 128");
+  TORCH_CHECK(q.size(1) % kc.size(1) == 0, "query heads must be a multiple of KV heads");
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == torch::kInt32, "status int32");
+  if (nseq == 0 || q.size(0) == 0) return;
+  const at::cuda::CUDAGuard guard(q.device());
+  SYN_CHECK_CUDA(launch_attn_prefill_tc(q.data_ptr(), (int)q.size(0), kc.data_ptr(), vc.data_ptr(), (int)kc.size(0),
+                                        block_tables.data_ptr<int32_t>(), cu_q.data_ptr<int32_t>(),
+                                        kv_lens.data_ptr<int32_t>(), out.data_ptr(), (int)nseq, (int)max_q_len,
+                                        (int)q.size(1), (int)kc.size(1), (int)q.size(2), (int)block_tables.size(1),
+                                        (float)scale, status.data_ptr<int32_t>(), cur_stream()));
+}
 
 std::vector<torch::Tensor> f8_quant_act(torch::Tensor x) {
   SYN_CHECK_INPUT(x);

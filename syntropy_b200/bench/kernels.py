@@ -253,26 +253,34 @@ def main():
         report("mla_decode_b16_ctx4096", timeit(lambda: ops.mla_decode(q, cache, bt, cl, o, 1 / math.sqrt(192), po, pml,
                                                                        pps)), B * ctx * 1152)
     if want("attn_prefill"):
-        nseq, L, Hq, Hkv, D = 8, 1024, 64, 4, 128
-        nb = nseq * L // 16 + 1
-        kc = torch.randn(nb, Hkv, 16, D, device=dev).to(torch.bfloat16)
-        vc = torch.randn(nb, Hkv, 16, D, device=dev).to(torch.bfloat16)
-        bt = (torch.arange(nseq * L // 16, device=dev) + 1).int().view(nseq, -1)
-        cu = torch.arange(0, nseq * L + 1, L, dtype=torch.int32, device=dev)
-        kl = torch.full((nseq,), L, dtype=torch.int32, device=dev)
-        q = torch.randn(nseq * L, Hq, D, device=dev).to(torch.bfloat16)
-        o = torch.empty_like(q)
-        flops = 4 * nseq * L * L * Hq * D / 2  # causal
-        report("attn_prefill_8x1024_h64", timeit(lambda: ops.attn_prefill_paged(q, kc, vc, bt, cu, kl, o, L,
-                                                                                1 / math.sqrt(D)), iters=10),
-               flops=flops)
         import torch.nn.functional as F
-        qq = q.view(nseq, L, Hq, D).transpose(1, 2)
-        kk = kc[1:].permute(0, 2, 1, 3).reshape(nseq, L, Hkv, D).transpose(1, 2)
-        vv = vc[1:].permute(0, 2, 1, 3).reshape(nseq, L, Hkv, D).transpose(1, 2)
-        report("sdpa_library_8x1024_h64(reference)",
-               timeit(lambda: F.scaled_dot_product_attention(qq, kk, vv, is_causal=True, enable_gqa=True), iters=10),
-               flops=flops)
+        from syntropy_b200.ops import core as _core
+        # Qwen3-235B prompt shape (8 x 1024, 64 q / 4 kv heads) and Llama-3-8B (4 x 2048, 32 / 8)
+        for nseq, L, Hq, Hkv in ((8, 1024, 64, 4), (4, 2048, 32, 8)):
+            D = 128
+            nb = nseq * L // 16 + 1
+            kc = torch.randn(nb, Hkv, 16, D, device=dev).to(torch.bfloat16)
+            vc = torch.randn(nb, Hkv, 16, D, device=dev).to(torch.bfloat16)
+            bt = (torch.arange(nseq * L // 16, device=dev) + 1).int().view(nseq, -1)
+            cu = torch.arange(0, nseq * L + 1, L, dtype=torch.int32, device=dev)
+            kl = torch.full((nseq,), L, dtype=torch.int32, device=dev)
+            q = torch.randn(nseq * L, Hq, D, device=dev).to(torch.bfloat16)
+            o = torch.empty_like(q)
+            flops = 4 * nseq * L * L * Hq * D / 2  # causal
+            tag = f"{nseq}x{L}_h{Hq}kv{Hkv}"
+            saved = _core._ATTN_TC[0]
+            for impl, flag in (("tcgen05", "1"), ("mma_sync", "0")):
+                _core._ATTN_TC[0] = flag
+                report(f"attn_prefill_{impl}_{tag}",
+                       timeit(lambda: ops.attn_prefill_paged(q, kc, vc, bt, cu, kl, o, L, 1 / math.sqrt(D)),
+                              iters=10), flops=flops)
+            _core._ATTN_TC[0] = saved
+            qq = q.view(nseq, L, Hq, D).transpose(1, 2)
+            kk = kc[1:].permute(0, 2, 1, 3).reshape(nseq, L, Hkv, D).transpose(1, 2)
+            vv = vc[1:].permute(0, 2, 1, 3).reshape(nseq, L, Hkv, D).transpose(1, 2)
+            report(f"sdpa_library_{tag}(reference)",
+                   timeit(lambda: F.scaled_dot_product_attention(qq, kk, vv, is_causal=True, enable_gqa=True),
+                          iters=10), flops=flops)
     print(json.dumps({"summary": res}))
 
 

@@ -490,12 +490,19 @@ def attn_prefill(q, k, v, cu_seqlens: list[int], out, scale):
     return out
 
 
+# SYN_ATTN_TC: "1" (default) prefill attention on tcgen05, "0" the mma.sync kernel
+_ATTN_TC = [__import__("os").environ.get("SYN_ATTN_TC", "1")]
+
+
 def attn_prefill_paged(q, kc, vc, block_tables, cu_q, kv_lens, out, max_q_len: int, scale: float):
     """Causal prefill attention over the paged cache: query row i of sequence s (rows
     cu_q[s]..cu_q[s+1]) sits at position kv_lens[s] - q_len + i and attends to keys
     0..position through block_tables[s].  q/out: [T, Hq, D]; kc/vc: [blocks, Hkv, 16, D]."""
     if q.is_cuda and q.shape[-1] == 128:
-        ext().attn_prefill(q, kc, vc, block_tables, cu_q, kv_lens, out, max_q_len, scale)
+        if _ATTN_TC[0] == "1":  # tcgen05 kernel (TMA-fed, S and P V in TMEM)
+            ext().attn_prefill_tc(q, kc, vc, block_tables, cu_q, kv_lens, out, max_q_len, scale, gemm_status(q.device))
+        else:                   # mma.sync kernel (the earlier tensor-core path, kept for comparison)
+            ext().attn_prefill(q, kc, vc, block_tables, cu_q, kv_lens, out, max_q_len, scale)
         _launched()
         return out
     Hq, Hkv, D = q.shape[1], kc.shape[1], q.shape[2]

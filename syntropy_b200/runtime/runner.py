@@ -492,9 +492,16 @@ class ModelRunner:
         yp = b["moe_out"][: R * k]
         yp.zero_()
         off = mb["tok_off"][ea: eb + 1]
+        cache = self.expert_cache
+        li = self._cache_index(L) if cache is not None and cache.stage_all else None
+        ev = self._stage_ev.pop(li, None) if li is not None else None
+        if ev is not None:  # the GPU-read host experts of this layer are in its staging bank
+            torch.cuda.current_stream(self.device).wait_event(ev)
         ops.linear_grouped(ha, gu, off, mb["tok_idx"], mid, ops.GEMV_SWIGLU, qw_ptrs=gu.qw_ptrs, sm_ptrs=gu.sm_ptrs)
         ops.linear_grouped(mid, dn, off, None, yp, ops.GEMV_SCALED_F32, route_w=mb["pair_w"],
                            qw_ptrs=dn.qw_ptrs, sm_ptrs=dn.sm_ptrs)
+        if li is not None:  # this layer's staging bank is free: stage the layer after next
+            self._stage_issue(li + 2)
         part = b["x_part"][:R]
         part.zero_()
         ops.moe_combine_rmsnorm(part, yp, mb["pair_of"], None, None, None, cfg.rms_eps)

@@ -1,5 +1,6 @@
-"""Paged causal prefill attention kernel against a plain f32 PyTorch reference (GQA,
-head_dim 128, random page order, chunked prefill after a cached prefix)."""
+"""Paged causal prefill attention kernels (tcgen05 and mma.sync) against a plain f32 PyTorch
+reference (GQA, head_dim 128, random page order, chunked prefill after a cached prefix, query
+tiles and key tiles that straddle sequence and page boundaries)."""
 import math
 
 import pytest
@@ -30,10 +31,12 @@ def _ref(q, kc, vc, bts, q_lens, kv_lens, scale):
     return torch.cat(outs, 0)
 
 
+@pytest.mark.parametrize("impl", ["tc", "mma"])
 @pytest.mark.parametrize("Hq,Hkv,q_lens,prefix", [(64, 4, [1024, 300, 7], [0, 0, 0]),
                                                   (16, 2, [130, 64, 1], [0, 37, 500]),
-                                                  (8, 8, [200], [96])])
-def test_attn_prefill_paged(cuda, Hq, Hkv, q_lens, prefix):
+                                                  (8, 8, [200], [96]),
+                                                  (32, 8, [129, 255, 256, 17, 640], [0, 127, 128, 1000, 5])])
+def test_attn_prefill_paged(cuda, Hq, Hkv, q_lens, prefix, impl):
     torch.manual_seed(5)
     D = 128
     kv_lens = [n + p for n, p in zip(q_lens, prefix)]
@@ -57,8 +60,18 @@ def test_attn_prefill_paged(cuda, Hq, Hkv, q_lens, prefix):
         cu.append(cu[-1] + n)
     out = torch.empty_like(q)
     scale = 1 / math.sqrt(D)
-    ops.attn_prefill_paged(q, kc, vc, bt.to(cuda), torch.tensor(cu, dtype=torch.int32, device=cuda),
-                           torch.tensor(kv_lens, dtype=torch.int32, device=cuda), out, max(q_lens), scale)
+    from syntropy_b200._ext import ext
+    from syntropy_b200.ops.core import gemm_status
+    args = (q, kc, vc, bt.to(cuda), torch.tensor(cu, dtype=torch.int32, device=cuda),
+            torch.tensor(kv_lens, dtype=torch.int32, device=cuda), out, max(q_lens), scale)
+    if impl == "tc":
+        st = gemm_status(cuda)
+        st.zero_()
+        ext().attn_prefill_tc(*args, st)
+        torch.cuda.synchronize()
+        assert int(st.item()) == 0
+    else:
+        ext().attn_prefill(*args)
     ref = _ref(q, kc, vc, bts, q_lens, kv_lens, scale)
     err = ((out.float() - ref).norm() / ref.norm()).item()
     assert err < 1e-2, err

@@ -98,19 +98,29 @@ def test_ep_fused_fp8_deepseek_with_mtp_matches_single_gpu():
     from syntropy_b200.models.transformer import prepare_weights
     from syntropy_b200.runtime.engine import LLMEngine, SamplingParams
     from syntropy_b200.runtime.runner import ModelRunner
-    fused = _run(True, "small-deepseek", spec=True, port=29613)
+    plain = _run(True, "small-deepseek", spec=False, port=29613)
+    spec = _run(True, "small-deepseek", spec=True, port=29614)
     for r in (0, 1):
-        assert fused[r]["status"] == 0
-        assert fused[r]["accept"] is not None
+        assert plain[r]["status"] == 0 and spec[r]["status"] == 0
+        assert spec[r]["accept"] is not None
     cfg = get_config("small-deepseek")
     mw = prepare_weights(cfg, torch.device("cuda:0"), seed=7)
     g = torch.Generator().manual_seed(3)
     prompts = [torch.randint(0, cfg.vocab, (n,), generator=g).tolist() for n in (11, 30, 7, 19)]
     single = LLMEngine(ModelRunner(mw, max_batch=4, max_seq_len=256)).generate(prompts, SamplingParams(max_tokens=8))
-    # greedy with exact acceptance emits the target's own tokens: sequences agree up to near-tie flips
-    # (fp8 activations and a different f32 summation association)
-    agree = sum(a[:4] == b[:4] for r in (0, 1) for a, b in zip(fused[r]["outs"], single[r::2]))
-    assert agree >= 2, (fused, single)
+
+    def agree(res):
+        seqs = [(x, y) for r in (0, 1) for x, y in zip(res[r]["outs"], single[r::2])]
+        first = sum(x[0] == y[0] for x, y in seqs)
+        prefix = sum(next((i for i, (a, b) in enumerate(zip(x, y)) if a != b), len(y)) for x, y in seqs)
+        return first, prefix / sum(len(y) for _, y in seqs)
+    # greedy tokens agree up to near-tie flips (the f32 summation association differs between the
+    # EP combine and the single-GPU combine; verify windows batch 2 rows per sequence), and a flip
+    # changes the rest of its sequence: the first tokens and most of the common prefix agree
+    for res in (plain, spec):
+        first, prefix = agree(res)
+        msg = json.dumps({"ep": [res[r]["outs"] for r in (0, 1)], "single": single})
+        assert first >= 3 and prefix >= 0.5, (first, prefix, msg)
 
 
 TP_WORKER = r"""

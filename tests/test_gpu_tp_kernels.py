@@ -100,8 +100,11 @@ def test_tp_fused_paths_match_f32_reference():
     for r in (0, 1):
         d = res[r]
         assert d["status"] == 0, d
+        # bf16 operands with f32 accumulation: near f32; the 4-bit GEMV rounds each dequantised
+        # weight to bf16 for the tensor-core product (relative error about 2^-9)
+        assert d["bf16_rel"] < 1e-4, d
+        assert d["q4_rel"] < 5e-3, d
         for kind in ("bf16", "q4"):
-            assert d[kind + "_rel"] < 1e-3, d      # f32 partials of bf16 / dequantised 4-bit products
             assert d[kind + "_h_rel"] < 1e-2, d
             assert d[kind + "_bitwise_equal"], d    # rank-order reduction: identical residuals
         assert d["logits_rel"] < 1e-4, d
