@@ -121,6 +121,13 @@ def main():
                          "report device ms per segment kind (max over ranks)")
     ap.add_argument("--no-mtp", action="store_true", help="models with an MTP head: plain decoding instead of "
                     "MTP drafting + batched verification")
+    ap.add_argument("--spec", choices=["auto", "none", "ngram"], default="auto",
+                    help="speculative decoding: auto = the model's MTP head when it has one; ngram = prompt-lookup "
+                         "drafts of --spec-gamma tokens verified in one batched pass (one GPU, no TP/PP)")
+    ap.add_argument("--spec-gamma", type=int, default=3)
+    ap.add_argument("--max-prefill-tokens", type=int, default=0,
+                    help="prompt tokens per prefill step (0: 8192, or every local prompt up to 32768 tokens when "
+                         "host-tier experts stream through each prefill pass)")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -209,10 +216,13 @@ def main():
                 cache.enable_decode_prefetch(cfg.n_experts)
     # TP's NCCL all-reduce baseline is captured into the decode graphs too (ranks step in lockstep)
     graphs = not ((ep is not None and not ep.fused) or pp is not None)
-    use_mtp = cfg.n_mtp > 0 and mw.mtp is not None and not args.no_mtp and pp is None and tp is None
-    # MTP verify windows hold 2 rows per sequence
-    runner = ModelRunner(mw, max_batch=B * (2 if use_mtp else 1), max_seq_len=max_len + 16, ep=ep, tp=tp, pp=pp,
-                         use_graphs=graphs)
+    use_mtp = cfg.n_mtp > 0 and mw.mtp is not None and not args.no_mtp and pp is None and tp is None and \
+        args.spec == "auto"
+    use_ngram = args.spec == "ngram" and pp is None and tp is None and ep is None
+    # verify windows hold 1 + gamma rows per sequence (MTP: gamma 1)
+    rows_per_seq = 2 if use_mtp else (1 + args.spec_gamma if use_ngram else 1)
+    runner = ModelRunner(mw, max_batch=B * rows_per_seq, max_seq_len=max_len + 16 + args.spec_gamma, ep=ep, tp=tp,
+                         pp=pp, use_graphs=graphs)
     runner.expert_cache = cache
     tier = None
     if cache is not None and tp is None and pp is None and (ep is None or ep.fused) and cfg.weight_quant == "q4":
@@ -233,7 +243,14 @@ def main():
     if use_mtp:
         from syntropy_b200.runtime.spec import MTPDrafter, SpecConfig
         spec = SpecConfig(drafter=MTPDrafter(runner))
-    eng = LLMEngine(runner, max_prefill_tokens=8192, dist_ctx=ctx, spec=spec, rebalance_every=args.rebalance_every)
+    elif use_ngram:
+        from syntropy_b200.runtime.spec import NgramDrafter, SpecConfig
+        spec = SpecConfig(drafter=NgramDrafter(), gamma=args.spec_gamma)
+    # a prefill pass streams every host-tier expert of every layer over PCIe once, whatever its
+    # token count: with a host tier, one pass takes all local prompts (bounded for activations)
+    n_local = args.batch // world if cfg.is_moe else args.batch
+    mpt = args.max_prefill_tokens or (min(32768, max(8192, n_local * args.prompt)) if cache is not None else 8192)
+    eng = LLMEngine(runner, max_prefill_tokens=mpt, dist_ctx=ctx, spec=spec, rebalance_every=args.rebalance_every)
     g = torch.Generator().manual_seed(1234)
     all_prompts = [torch.randint(0, cfg.vocab, (args.prompt,), generator=g).tolist() for _ in range(args.batch)]
     prompts = all_prompts[rank::world] if cfg.is_moe else all_prompts
@@ -242,6 +259,8 @@ def main():
     if ctx.enabled:
         import torch.distributed as dist
         dist.barrier(group=ctx.cpu_group)
+    if args.step_profile and runner.is_cuda:
+        runner.profile_prefill_next = True  # the first prefill pass: device ms per layer segment
     t_sub = time.perf_counter()
     if ctx.enabled:
         while _any_waiting(ctx, eng):
@@ -250,6 +269,17 @@ def main():
         while eng.waiting:
             eng.step()
     torch.cuda.synchronize()
+    prefill_prof = None
+    if args.step_profile and runner.is_cuda:
+        # every rank takes the same collective steps: a fixed list of segment kinds
+        agg = dict.fromkeys(("prefill_attn", "prefill_ffn", "prefill_moe", "prefill_head"), 0.0)
+        if runner._stamp_labels[-1:] == ["prefill_head"]:
+            for lab, ms in runner.step_profile():
+                kind = lab.split(".")[-1]
+                agg[kind] = agg.get(kind, 0.0) + ms
+        prefill_prof = {k: round(max_over_ranks(ctx, agg[k]), 3) for k in
+                        ("prefill_attn", "prefill_ffn", "prefill_moe", "prefill_head")}
+        prefill_prof["tokens_in_pass"] = int(min(mpt, n_local * args.prompt))
     seqs = {s.seq_id: s for s in eng.running}
     my_ttft = [seqs[i].t_first_token - t_sub for i in ids]
     if ctx.enabled:
@@ -277,7 +307,7 @@ def main():
         torch.cuda.synchronize()
         te = time.perf_counter()
         for _ in range(args.steps):
-            if spec is not None:  # a step is the verify pass plus the MTP draft pass: time both
+            if spec is not None:  # a step is the verify pass plus the draft pass: time both
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record()
                 eng.step()
@@ -391,6 +421,7 @@ def main():
         "p50_ttft_ms": round(p50_ttft_ms, 2),
         "config": {"model": args.model if not args.layers else f"{args.model}[layers={args.layers}] (DEV, not headline)",
                    "global_batch": args.batch, "seq_len": args.prompt, "decode_len": decode_len,
+                   "max_prefill_tokens": mpt,
                    "parallelism": par,
                    "expert_cache_frac": args.expert_cache_frac if cfg.is_moe else 1.0,
                    "host_tier_gb": placed["host_gb"],
@@ -412,9 +443,11 @@ def main():
         "all_experts_resident": uncapped,
     }
     if mtp_info is not None:
-        out["mtp"] = mtp_info
+        out["mtp" if use_mtp else "spec"] = dict(mtp_info, drafter="mtp" if use_mtp else f"ngram(gamma={args.spec_gamma})")
     if step_prof is not None:
         out["step_profile_ms"] = step_prof
+    if prefill_prof is not None:
+        out["prefill_profile_ms"] = prefill_prof
     if rank == 0:
         print(json.dumps(out))
     runner.graphs.clear()

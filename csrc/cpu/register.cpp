@@ -40,9 +40,13 @@ void register_all(pybind11::module& m) {
   m.def("tap_compare", &tap_compare, "per-row max abs diff and relative L2 of two taps");
   m.def("kv_pages", &kv_pages, "pack (true) or unpack (false) the K/V pages of a block list");
   m.def("mla_decode", &mla_decode, "MLA decode attention (absorbed) over the paged latent cache");
+  m.def("mla_q_absorb", &mla_q_absorb, "MLA decode: q_nope . W_uk and rope(q_pe) into the 576-wide query rows");
+  m.def("mla_kv_write", &mla_kv_write, "MLA decode: normed latent + rope(k_pe) into the latent cache");
+  m.def("mla_o_absorb", &mla_o_absorb, "MLA decode: o_lat . W_uv^T per head (bf16 out)");
   m.def("f8_quant_act", &f8_quant_act, "bf16 [T, K] -> e4m3 [T, K] + f32 1x128 scales");
   m.def("f8_rows_to_tiled", &f8_rows_to_tiled, "row-major e4m3 bytes -> mma-fragment tiled layout");
   m.def("f8_tiled_to_rows", &f8_tiled_to_rows, "inverse of f8_rows_to_tiled");
+  m.def("f8_dequant_tiled", &f8_dequant_tiled, "tiled e4m3 + 128x128 block scales -> bf16 rows");
   m.def("f8_gemv", &f8_gemv, "block-scaled fp8 grouped GEMV (e4m3 x e4m3 tensor cores)");
   m.def("f8_gemv_ep", &f8_gemv_ep, "fp8 expert down projection into source ranks' combine slots + layer flags");
   m.def("attn_prefill", &attn_prefill, "causal prefill attention over the paged KV cache (GQA, head_dim 128)");

@@ -83,6 +83,43 @@ cudaError_t launch_f8_tiled_to_rows(const uint8_t* tiled, int N, int K, uint8_t*
   return cudaGetLastError();
 }
 
+// tiled e4m3 -> bf16 row-major with the 128x128 block scales applied (prefill operands of the
+// bf16 tensor-core GEMM): thread per tiled 4-byte word, e4m3 pairs widened by cvt to f16x2
+__global__ void f8_dequant_tiled_kernel(const uint32_t* __restrict__ tiled, const float* __restrict__ scale, int N,
+                                        int K, __nv_bfloat16* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int KG = K / 64;
+  if (i >= (int64_t)N * K / 4) return;
+  const int64_t grp = i >> 8;
+  const int w = (int)(i & 255);
+  const int lane = w >> 3, step = (w >> 2) & 1, reg = w & 3;
+  const int tile = (int)(grp / KG), kg = (int)(grp % KG);
+  const int g = lane >> 2, t = lane & 3;
+  const int row = tile * 16 + g + 8 * (reg & 1);
+  const int col = kg * 64 + step * 32 + 16 * (reg >> 1) + 4 * t;
+  const float sc = scale[(int64_t)(row >> 7) * ((K + 127) >> 7) + (col >> 7)];
+  const uint32_t v = tiled[i];
+  uint32_t h01, h23;
+  asm("{ .reg .b16 lo, hi; mov.b32 {lo, hi}, %2; cvt.rn.f16x2.e4m3x2 %0, lo; cvt.rn.f16x2.e4m3x2 %1, hi; }"
+      : "=r"(h01), "=r"(h23)
+      : "r"(v));
+  const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+  const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+  uint2 o;
+  o.x = pack_bf16x2(f01.x * sc, f01.y * sc);
+  o.y = pack_bf16x2(f23.x * sc, f23.y * sc);
+  *reinterpret_cast<uint2*>(out + (int64_t)row * K + col) = o;
+}
+
+cudaError_t launch_f8_dequant_tiled(const uint8_t* tiled, const float* scale, int N, int K, void* out_bf16,
+                                    cudaStream_t s) {
+  if (N % 16 || K % 128) return cudaErrorInvalidValue;
+  const int64_t words = (int64_t)N * K / 4;
+  f8_dequant_tiled_kernel<<<(unsigned)((words + 255) / 256), 256, 0, s>>>(
+      reinterpret_cast<const uint32_t*>(tiled), scale, N, K, reinterpret_cast<__nv_bfloat16*>(out_bf16));
+  return cudaGetLastError();
+}
+
 __device__ __forceinline__ void mma_e4m3_16832(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 "

@@ -86,6 +86,7 @@ void attn_prefill_tc(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch:
 std::vector<torch::Tensor> f8_quant_act(torch::Tensor x);
 torch::Tensor f8_rows_to_tiled(torch::Tensor q, int64_t N, int64_t K);
 torch::Tensor f8_tiled_to_rows(torch::Tensor tiled, int64_t N, int64_t K);
+torch::Tensor f8_dequant_tiled(torch::Tensor tiled, torch::Tensor scale, int64_t N, int64_t K);
 void f8_gemv(torch::Tensor xq, torch::Tensor xs, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
              torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor out, int64_t N, int64_t K, int64_t mode,
              int64_t nt_hint, torch::Tensor ws);
@@ -93,6 +94,11 @@ void f8_gemv_ep(torch::Tensor xq, torch::Tensor xs, torch::Tensor qw_ptrs, torch
                 torch::Tensor tok_off, torch::Tensor route_w, torch::Tensor out_ptrs, int64_t N, int64_t K,
                 torch::Tensor done_ctr, torch::Tensor peers, int64_t sig_off, int64_t sig_rank, torch::Tensor step_ctr,
                 int64_t n_layers, int64_t layer, int64_t nt_hint);
+void mla_q_absorb(torch::Tensor q, torch::Tensor w_uk, torch::Tensor cos_t, torch::Tensor sin_t, torch::Tensor pos,
+                  torch::Tensor qcat);
+void mla_kv_write(torch::Tensor kva, torch::Tensor norm_w, double eps, torch::Tensor cos_t, torch::Tensor sin_t,
+                  torch::Tensor pos, torch::Tensor slot, torch::Tensor cache);
+void mla_o_absorb(torch::Tensor o_lat, torch::Tensor w_uv, torch::Tensor out);
 void mla_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables, torch::Tensor ctx_lens,
                 torch::Tensor out, double scale, torch::Tensor part_o, torch::Tensor part_ml, int64_t pages_per_split);
 void doorbell_wait(torch::Tensor flag, int64_t want, double timeout_s, torch::Tensor status, torch::Tensor waited_ns);

@@ -65,6 +65,9 @@ struct GemvArgs {
 cudaError_t launch_f8_quant_act(const void* x, int rows, int K, int ldx, uint8_t* xq, float* xs, cudaStream_t s);
 cudaError_t launch_f8_rows_to_tiled(const uint8_t* q, int N, int K, uint8_t* tiled, cudaStream_t s);
 cudaError_t launch_f8_tiled_to_rows(const uint8_t* tiled, int N, int K, uint8_t* q, cudaStream_t s);
+// tiled e4m3 + block scales -> bf16 row-major [N, K]
+cudaError_t launch_f8_dequant_tiled(const uint8_t* tiled, const float* scale, int N, int K, void* out_bf16,
+                                    cudaStream_t s);
 // qw_ptrs: tiled e4m3 per expert; sm_ptrs: f32 scales per expert; a.xq / a.xs: quantised x
 cudaError_t launch_f8_gemv(const GemvArgs& a, cudaStream_t s);
 cudaError_t launch_block_sums(const void* x, int rows, int K, int ldx, float* out, cudaStream_t s);
@@ -115,6 +118,13 @@ cudaError_t launch_attn_prefill_tc(const void* q, int Tq, const void* kc, const 
 cudaError_t launch_mla_decode(const void* q, const void* cache, const int32_t* block_tables, const int32_t* ctx_lens,
                               float* part_o, float* part_ml, float* out, int B, int H, int max_blocks,
                               int pages_per_split, int n_splits, float scale, cudaStream_t s);
+// ---- MLA decode projections around the latent attention (C 512, nope 128, rope 64, v 128) ----
+cudaError_t launch_mla_q_absorb(const void* q, int T, int H, const void* w_uk, const float* cos_t, const float* sin_t,
+                                const int32_t* pos, void* qcat, cudaStream_t s);
+cudaError_t launch_mla_kv_write(const void* kva, int T, const float* norm_w, float eps, const float* cos_t,
+                                const float* sin_t, const int32_t* pos, const int64_t* slot, void* cache,
+                                cudaStream_t s);
+cudaError_t launch_mla_o_absorb(const float* o_lat, int T, int H, const void* w_uv, void* out, cudaStream_t s);
 // ---- runtime kernels: doorbells (bounded wait), timestamps, parity taps, KV page pack ----
 cudaError_t launch_doorbell_wait(const uint32_t* flag, uint32_t want, uint64_t timeout_ns, int* status,
                                  uint64_t* waited_ns, cudaStream_t s);

@@ -687,6 +687,19 @@ torch::Tensor f8_tiled_to_rows(torch::Tensor tiled, int64_t N, int64_t K) {
   return out;
 }
 
+torch::Tensor f8_dequant_tiled(torch::Tensor tiled, torch::Tensor scale, int64_t N, int64_t K) {
+  SYN_CHECK_INPUT(tiled);
+  TORCH_CHECK(tiled.scalar_type() == torch::kUInt8 && tiled.numel() == N * K, "tiled e4m3 bytes");
+  TORCH_CHECK(scale.is_cuda() && scale.scalar_type() == torch::kFloat32 && scale.is_contiguous() &&
+                  scale.numel() == ((N + 127) / 128) * ((K + 127) / 128), "scale f32 [ceil(N/128), ceil(K/128)]");
+  TORCH_CHECK(N % 16 == 0 && K % 128 == 0, "fp8 tiled layout needs N % 16 == 0 and K % 128 == 0");
+  auto out = torch::empty({N, K}, tiled.options().dtype(torch::kBFloat16));
+  const at::cuda::CUDAGuard guard(tiled.device());
+  SYN_CHECK_CUDA(launch_f8_dequant_tiled(tiled.data_ptr<uint8_t>(), scale.data_ptr<float>(), (int)N, (int)K,
+                                         out.data_ptr(), cur_stream()));
+  return out;
+}
+
 void f8_gemv(torch::Tensor xq, torch::Tensor xs, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off,
              torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor out, int64_t N, int64_t K, int64_t mode,
              int64_t nt_hint, torch::Tensor ws) {
@@ -767,6 +780,59 @@ void f8_gemv_ep(torch::Tensor xq, torch::Tensor xs, torch::Tensor qw_ptrs, torch
   a.layer = (int)layer;
   const at::cuda::CUDAGuard guard(xq.device());
   SYN_CHECK_CUDA(launch_f8_gemv(a, cur_stream()));
+}
+
+// MLA decode projections: q bf16 [T, H*(128+64)] -> qcat bf16 [T, H, 576]; kva bf16 [T, 576] ->
+// cache rows (normed latent | roped k_pe); o_lat f32 [T, H, 512] -> out bf16 [T, H*128].
+void mla_q_absorb(torch::Tensor q, torch::Tensor w_uk, torch::Tensor cos_t, torch::Tensor sin_t, torch::Tensor pos,
+                  torch::Tensor qcat) {
+  SYN_CHECK_INPUT(q);
+  const int64_t T = qcat.size(0), H = qcat.size(1);
+  TORCH_CHECK(q.scalar_type() == torch::kBFloat16 && q.is_contiguous() && q.numel() == T * H * 192, "q bf16 [T, H*192]");
+  TORCH_CHECK(w_uk.scalar_type() == torch::kBFloat16 && w_uk.is_contiguous() && w_uk.numel() == H * 128 * 512,
+              "w_uk bf16 [H, 128, 512]");
+  TORCH_CHECK(qcat.scalar_type() == torch::kBFloat16 && qcat.is_contiguous() && qcat.dim() == 3 && qcat.size(2) == 576,
+              "qcat bf16 [T, H, 576]");
+  TORCH_CHECK(cos_t.scalar_type() == torch::kFloat32 && sin_t.scalar_type() == torch::kFloat32 && cos_t.size(-1) == 32,
+              "rope tables f32 [max_pos, 32]");
+  TORCH_CHECK(pos.scalar_type() == torch::kInt32 && pos.numel() >= T, "pos int32 [T]");
+  if (T == 0) return;
+  const at::cuda::CUDAGuard guard(q.device());
+  SYN_CHECK_CUDA(launch_mla_q_absorb(q.data_ptr(), (int)T, (int)H, w_uk.data_ptr(), cos_t.data_ptr<float>(),
+                                     sin_t.data_ptr<float>(), pos.data_ptr<int32_t>(), qcat.data_ptr(), cur_stream()));
+}
+
+void mla_kv_write(torch::Tensor kva, torch::Tensor norm_w, double eps, torch::Tensor cos_t, torch::Tensor sin_t,
+                  torch::Tensor pos, torch::Tensor slot, torch::Tensor cache) {
+  SYN_CHECK_INPUT(kva);
+  TORCH_CHECK(kva.scalar_type() == torch::kBFloat16 && kva.is_contiguous() && kva.dim() == 2 && kva.size(1) == 576,
+              "kva bf16 [T, 576]");
+  TORCH_CHECK(norm_w.scalar_type() == torch::kFloat32 && norm_w.numel() == 512, "norm weight f32 [512]");
+  TORCH_CHECK(cache.scalar_type() == torch::kBFloat16 && cache.is_contiguous() && cache.size(-1) == 576,
+              "latent cache bf16 [.., 576]");
+  const int64_t T = kva.size(0);
+  TORCH_CHECK(pos.scalar_type() == torch::kInt32 && slot.scalar_type() == torch::kInt64 && pos.numel() >= T &&
+                  slot.numel() >= T, "pos int32 / slot int64 [T]");
+  if (T == 0) return;
+  const at::cuda::CUDAGuard guard(kva.device());
+  SYN_CHECK_CUDA(launch_mla_kv_write(kva.data_ptr(), (int)T, norm_w.data_ptr<float>(), (float)eps,
+                                     cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), pos.data_ptr<int32_t>(),
+                                     slot.data_ptr<int64_t>(), cache.data_ptr(), cur_stream()));
+}
+
+void mla_o_absorb(torch::Tensor o_lat, torch::Tensor w_uv, torch::Tensor out) {
+  SYN_CHECK_INPUT(o_lat);
+  TORCH_CHECK(o_lat.scalar_type() == torch::kFloat32 && o_lat.is_contiguous() && o_lat.dim() == 3 &&
+                  o_lat.size(2) == 512, "o_lat f32 [T, H, 512]");
+  const int64_t T = o_lat.size(0), H = o_lat.size(1);
+  TORCH_CHECK(w_uv.scalar_type() == torch::kBFloat16 && w_uv.is_contiguous() && w_uv.numel() == H * 128 * 512,
+              "w_uv bf16 [H, 128, 512]");
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.is_contiguous() && out.numel() == T * H * 128,
+              "out bf16 [T, H*128]");
+  if (T == 0) return;
+  const at::cuda::CUDAGuard guard(o_lat.device());
+  SYN_CHECK_CUDA(launch_mla_o_absorb(o_lat.data_ptr<float>(), (int)T, (int)H, w_uv.data_ptr(), out.data_ptr(),
+                                     cur_stream()));
 }
 
 void mla_decode(torch::Tensor q, torch::Tensor cache, torch::Tensor block_tables, torch::Tensor ctx_lens,

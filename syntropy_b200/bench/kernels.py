@@ -252,11 +252,13 @@ def main():
         o = torch.empty(B, H, 512, device=dev)
         report("mla_decode_b16_ctx4096", timeit(lambda: ops.mla_decode(q, cache, bt, cl, o, 1 / math.sqrt(192), po, pml,
                                                                        pps)), B * ctx * 1152)
-    if want("attn_prefill"):
+    if want("attn_prefill") or "attn_prefill_small" in only:
         import torch.nn.functional as F
         from syntropy_b200.ops import core as _core
-        # Qwen3-235B prompt shape (8 x 1024, 64 q / 4 kv heads) and Llama-3-8B (4 x 2048, 32 / 8)
-        for nseq, L, Hq, Hkv in ((8, 1024, 64, 4), (4, 2048, 32, 8)):
+        # Qwen3-235B prompt shape (8 x 1024, 64 q / 4 kv heads) and Llama-3-8B (4 x 2048, 32 / 8);
+        # attn_prefill_small: one 4 x 1024 (32 / 8) case, small enough for a profiler capture
+        shapes = ((4, 1024, 32, 8),) if "attn_prefill_small" in only else ((8, 1024, 64, 4), (4, 2048, 32, 8))
+        for nseq, L, Hq, Hkv in shapes:
             D = 128
             nb = nseq * L // 16 + 1
             kc = torch.randn(nb, Hkv, 16, D, device=dev).to(torch.bfloat16)

@@ -67,6 +67,9 @@ class FP8Weight:
         return ext().f8_tiled_to_rows(self.tiled, self.N, self.K).view(torch.float8_e4m3fn)
 
     def dequant(self, dtype=torch.bfloat16) -> torch.Tensor:
+        if self.tiled is not None and dtype == torch.bfloat16:
+            from .._ext import ext
+            return ext().f8_dequant_tiled(self.tiled, self.scale, self.N, self.K)
         return dequant_fp8_block(self.rows(), self.scale).to(dtype)
 
     @property

@@ -29,9 +29,36 @@ def prepare_mla(cfg, get, pre, linear_weight):
     w["kv_a"] = linear_weight(get(pre + "kv_a"))
     w["kv_a_norm"] = get(pre + "kv_a_norm").float()
     kvb = get(pre + "kv_b").float().view(H, dn + dv, C)
-    w["w_uk"] = kvb[:, :dn, :].contiguous()   # [H, dn, C]
-    w["w_uv"] = kvb[:, dn:, :].contiguous()   # [H, dv, C]
+    # [H, dn, C] / [H, dv, C]; bf16 on the GPU (the decode kernels read them once per step, the
+    # eager paths widen them to f32 where they use them)
+    wt = torch.bfloat16 if kvb.is_cuda else torch.float32
+    w["w_uk"] = kvb[:, :dn, :].to(wt).contiguous()
+    w["w_uv"] = kvb[:, dn:, :].to(wt).contiguous()
     return w
+
+
+def mla_qkv_decode(cfg, m, h, pos, slot, cos_t, sin_t, cache, qcat):
+    """GPU decode projections for T rows: the latent row (normed c | roped k_pe) goes straight
+    into the cache at `slot` (int64; -1 = padding, written to the null page) and qcat (bf16
+    [T, H, C + dr]) receives [q_nope . W_uk | roped q_pe] for the latent attention kernel."""
+    from .._ext import ext
+    T = h.shape[0]
+    H, dn, dr, C = cfg.n_heads, cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.kv_lora_rank
+    q = torch.empty(T, H * (dn + dr), dtype=torch.bfloat16, device=h.device)
+    if cfg.q_lora_rank:
+        qa = torch.empty(T, cfg.q_lora_rank, dtype=torch.bfloat16, device=h.device)
+        ops.linear(h, m["q_a"], qa, ops.GEMV_STORE)
+        qa = ops.rms_norm(qa, m["q_a_norm"], cfg.rms_eps)
+        ops.linear(qa.to(torch.bfloat16), m["q_b"], q, ops.GEMV_STORE)
+    else:
+        ops.linear(h, m["q_proj"], q, ops.GEMV_STORE)
+    kva = torch.empty(T, C + dr, dtype=torch.bfloat16, device=h.device)
+    ops.linear(h, m["kv_a"], kva, ops.GEMV_STORE)
+    e = ext()
+    e.mla_kv_write(kva, m["kv_a_norm"], cfg.rms_eps, cos_t, sin_t, pos, slot, cache)
+    e.mla_q_absorb(q, m["w_uk"], cos_t, sin_t, pos, qcat)
+    ops.core._launched(2)
+    return qcat
 
 
 def _rope(x, pos, theta, cos_t=None, sin_t=None):

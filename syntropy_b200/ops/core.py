@@ -182,6 +182,11 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
         ext().gemm_bf16(x, W if W.is_contiguous() else W.contiguous(), out, gm, ws, ctr, gemm_status(x.device))
         _launched()
         return out
+    if getattr(W, "tiled", None) is not None and x.dtype == torch.bfloat16 and W.N % 32 == 0 and \
+            (mode != GEMV_SWIGLU or W.N % 16 == 0):
+        # prefill over block-scaled fp8 weights: widened to bf16 (scales applied) in one pass,
+        # then the tcgen05 GEMM
+        return linear(x, ext().f8_dequant_tiled(W.tiled, W.scale, W.N, W.K), out, mode)
     Wd = _dense_weight(W)
     y = x.to(Wd.dtype) @ Wd.t()
     if mode == GEMV_SWIGLU:

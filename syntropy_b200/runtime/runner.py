@@ -85,6 +85,7 @@ class ModelRunner:
         self._pf_stream = None    # side stream of the router-predicted expert prefetch
         self._pf_events = {}
         self.profile_next = False  # next decode step replays the timestamped graph variant
+        self.profile_prefill_next = False  # next prefill pass records per-layer timestamps
         self._stamping = False
         self._stamp_n = 0
         self._stamp_labels: list[str] = []
@@ -186,6 +187,7 @@ class ModelRunner:
             from ..models.reference import mla_softmax_scale
             self.mla_scale = mla_softmax_scale(cfg)
             b["mla_olat"] = torch.zeros(B, cfg.n_heads, 512, dtype=torch.float32, device=dev)
+            b["mla_qcat"] = torch.zeros(B, cfg.n_heads, 512 + cfg.qk_rope_dim, dtype=torch.bfloat16, device=dev)
             b["mla_po"] = torch.zeros(B * cfg.n_heads * ns * 512, dtype=torch.float32, device=dev)
             b["mla_pml"] = torch.zeros(B * cfg.n_heads * ns * 2, dtype=torch.float32, device=dev)
         if self.is_cuda and not cfg.is_mla:
@@ -263,24 +265,28 @@ class ModelRunner:
 
     def _attention_decode_mla(self, L, B, i):
         """MLA decode for B rows (absorbed form over the paged latent cache)."""
-        from ..models.mla import mla_attend, mla_qkv
+        from ..models.mla import mla_attend, mla_qkv, mla_qkv_decode
         cfg, b, d = self.cfg, self.buf, self.desc.d
         h = b["h"][:B]
         pos = d["pos"][:B]
+        out = b["attn"][:B].view(B, -1)
+        if "mla_olat" in b and self.kv.k[i].dtype == torch.bfloat16:
+            # projections, latent write and both absorbs in four kernels around the latent
+            # attention (padding rows, slot -1, write the null page: capturable, no host sync)
+            qcat = mla_qkv_decode(cfg, L.mla, h, pos, d["slot"][:B], self.mw.rope_cos, self.mw.rope_sin,
+                                  self.kv.k[i], b["mla_qcat"][:B])
+            o_lat = b["mla_olat"][:B]
+            ops.mla_decode(qcat, self.kv.k[i], d["block_tables"][:B], d["ctx_len"][:B], o_lat, self.mla_scale,
+                           b["mla_po"], b["mla_pml"], self.mla_pages_per_split)
+            ext().mla_o_absorb(o_lat, L.mla["w_uv"], out)
+            ops.core._launched()
+            ops.linear(out, L.o, b["x"][:B], ops.GEMV_ADD_F32)
+            return
         q_lat, q_pe, lat = mla_qkv(cfg, L.mla, h, pos, self.mw.rope_cos, self.mw.rope_sin)
         cache = self.kv.k[i].view(-1, self.kv.k[i].shape[-1])
         sl = d["slot"][:B].long()
         # padding rows (slot -1) write into the null page: no host sync, capturable
         cache.index_copy_(0, torch.where(sl >= 0, sl, torch.zeros_like(sl)), lat.to(cache.dtype))
-        out = b["attn"][:B].view(B, -1)
-        if "mla_olat" in b:
-            qcat = torch.cat([q_lat, q_pe], -1).to(torch.bfloat16).contiguous()
-            o_lat = b["mla_olat"][:B]
-            ops.mla_decode(qcat, self.kv.k[i], d["block_tables"][:B], d["ctx_len"][:B], o_lat, self.mla_scale,
-                           b["mla_po"], b["mla_pml"], self.mla_pages_per_split)
-            out.copy_(torch.einsum("thc,hvc->thv", o_lat, L.mla["w_uv"]).reshape(B, -1))
-            ops.linear(out, L.o, b["x"][:B], ops.GEMV_ADD_F32)
-            return
         bs = self.block_size
         for r in range(B):
             n = int(d["ctx_len"][r])
@@ -690,14 +696,35 @@ class ModelRunner:
         return torch.cat(outs, 0) if pp.last else None
 
     @torch.no_grad()
-    def _prefill_pass(self, tokens: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor, cu_seqlens: list[int],
-                      prefix: list | None = None, block_lists: list | None = None, x_in=None, pp_io: bool = True):
+    def _prefill_pass(self, *args, **kw):
+        """One prefill pass (see `_prefill_pass_body`); with `profile_prefill_next` set, the pass
+        records device timestamps after each layer's attention and FFN (`step_profile`)."""
+        prof = self.profile_prefill_next and self.is_cuda
+        try:
+            return self._prefill_pass_body(*args, **kw)
+        finally:
+            if prof:
+                self._stamp("prefill_head")
+                self._stamping = False
+
+    def _prefill_pass_body(self, tokens: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
+                           cu_seqlens: list[int], prefix: list | None = None, block_lists: list | None = None,
+                           x_in=None, pp_io: bool = True):
         """One prefill pass of this stage's layers.  pp_io: receive / send the hidden states
         here (blocking); otherwise x_in is the received input and the hidden states are
         returned instead of sent (pipelined prefill)."""
         cfg, mw, dev = self.cfg, self.mw, self.device
         T = tokens.numel()
         act = torch.bfloat16 if self.is_cuda else torch.float32
+        prof = self.profile_prefill_next and self.is_cuda
+        if prof:  # device timestamps around each layer's attention and FFN (eager pass)
+            self.profile_prefill_next = False
+            self._stamping = True
+            if self._stamp_buf is None:
+                self._stamp_buf = torch.zeros(12 * len(mw.layers) + 8, dtype=torch.int64, device=self.device)
+            self._stamp_n = 0
+            self._stamp_labels = []
+            self._stamp("start")
         tokens = tokens.to(dev, torch.int32)
         positions = positions.to(dev, torch.int32)
         slots = slots.to(dev, torch.int64)
@@ -731,6 +758,7 @@ class ModelRunner:
             ops.rms_norm(x, L.attn_norm, cfg.rms_eps, out=h)
             if self.is_mla:
                 self._prefill_mla(L, i, h, x, positions, slots, cu_seqlens, prefix)
+                self._stamp(f"layer{i}.prefill_attn")
                 ops.rms_norm(x, L.ffn_norm, cfg.rms_eps, out=h)
                 if L.is_moe:
                     self._moe_prefill(L, h, x)
@@ -738,6 +766,7 @@ class ModelRunner:
                     mid = torch.empty(T, cfg.ffn, dtype=act, device=dev)
                     ops.linear(h, L.gate_up, mid, ops.GEMV_SWIGLU)
                     self._row_parallel(mid, L.down, x)
+                self._stamp(f"layer{i}.prefill_{'moe' if L.is_moe else 'ffn'}")
                 continue
             ops.linear(h, L.qkv, qkv, ops.GEMV_STORE)
             if L.qkv_bias is not None:
@@ -754,6 +783,7 @@ class ModelRunner:
             else:
                 self._prefill_attn_with_prefix(i, q, attn, cu_seqlens, prefix)
             self._row_parallel(attn.view(T, -1), L.o, x)
+            self._stamp(f"layer{i}.prefill_attn")
             ops.rms_norm(x, L.ffn_norm, cfg.rms_eps, out=h)
             if L.is_moe:
                 self._moe_prefill(L, h, x)
@@ -761,6 +791,7 @@ class ModelRunner:
                 mid = torch.empty(T, cfg.ffn, dtype=act, device=dev)
                 ops.linear(h, L.gate_up, mid, ops.GEMV_SWIGLU)
                 self._row_parallel(mid, L.down, x)
+            self._stamp(f"layer{i}.prefill_{'moe' if L.is_moe else 'ffn'}")
         if len(cu_seqlens) == 1:
             return torch.zeros(0, cfg.vocab, dtype=torch.float32, device=dev)
         if pp is not None and not pp.last:
@@ -837,7 +868,8 @@ class ModelRunner:
             o_lat = self.buf["mla_olat"][:S]
             ops.mla_decode(qcat, self.kv.k[li], bt.to(dev), ctx.to(dev), o_lat, self.mla_scale, self.buf["mla_po"],
                            self.buf["mla_pml"], self.mla_pages_per_split)
-            out.copy_(torch.einsum("thc,hvc->thv", o_lat, L.mla["w_uv"]).reshape(S, -1))
+            ext().mla_o_absorb(o_lat, L.mla["w_uv"], out)
+            ops.core._launched()
         else:
             for r in range(S):
                 n = int(positions[r]) + 1

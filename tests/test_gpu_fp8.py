@@ -92,3 +92,19 @@ def test_fp8_gemv_grouped_scaled(cuda):
             wf = dequant_fp8_block(Ws[e].rows(), Ws[e].scale)
             ref[a:b] = route_w[a:b, None] * (xa[tok_idx[a:b].long()] @ wf.t())
     assert _rel(out, ref) < 1e-5
+
+
+@pytest.mark.parametrize("T,N,K", [(300, 576, 1024), (1024, 2048, 7168)])
+def test_fp8_prefill_dequant_and_gemm(cuda, T, N, K):
+    """Prefill rows over fp8 weights: the tiled dequant kernel equals the block-scale dequant of
+    the row-major bytes exactly, and the prefill linear (dequant + tcgen05 bf16 GEMM) matches
+    the f32 product with the dequantised weights."""
+    torch.manual_seed(T)
+    W = FP8Weight.quantize(torch.randn(N, K, device=cuda) * 0.02)
+    wd = ext().f8_dequant_tiled(W.tiled, W.scale, N, K)
+    ref_w = dequant_fp8_block(W.rows(), W.scale).to(torch.bfloat16)
+    assert torch.equal(wd, ref_w)
+    x = (torch.randn(T, K, device=cuda) * 0.5).to(torch.bfloat16)
+    out = torch.empty(T, N, dtype=torch.float32, device=cuda)
+    ops.linear(x, W, out, ops.GEMV_STORE)
+    assert _rel(out, x.float() @ ref_w.float().t()) < 1e-4

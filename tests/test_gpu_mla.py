@@ -118,3 +118,33 @@ def test_deepseek_fp8_mtp_spec(cuda):
     same = sum(int(a == b) for x, y in zip(got, want) for a, b in zip(x, y))
     assert same / sum(len(x) for x in want) >= 0.75, (got, want)
     assert eng.stats["spec_drafted"] > 0 and 0.0 <= eng.acceptance_rate <= 1.0
+
+
+@pytest.mark.parametrize("T", [1, 5, 19])
+def test_mla_decode_projection_kernels(cuda, T):
+    """mla_kv_write / mla_q_absorb / mla_o_absorb against the f32 tensor path they replace
+    (mla_qkv's latent row and absorbed query, the W_uv einsum), on DeepSeek-V3 head shapes."""
+    from syntropy_b200._ext import ext
+    from syntropy_b200.models.mla import mla_qkv, mla_qkv_decode
+    cfg = get_config("small-deepseek")
+    mw = prepare_weights(cfg, cuda, seed=21)
+    m = mw.layers[0].mla
+    H = cfg.n_heads
+    g = torch.Generator().manual_seed(T)
+    h = torch.randn(T, cfg.hidden, generator=g).to(cuda, torch.bfloat16)
+    pos = torch.randint(0, 100, (T,), generator=g).int().to(cuda)
+    slot = torch.randperm(64, generator=g)[:T].long().to(cuda) + 16
+    slot[0] = -1  # a padding row writes the null page
+    cache = torch.zeros(8, 16, 576, dtype=torch.bfloat16, device=cuda)
+    qcat = torch.empty(T, H, 576, dtype=torch.bfloat16, device=cuda)
+    mla_qkv_decode(cfg, m, h, pos, slot, mw.rope_cos, mw.rope_sin, cache, qcat)
+    q_lat, q_pe, lat = mla_qkv(cfg, m, h, pos, mw.rope_cos, mw.rope_sin)
+    want_q = torch.cat([q_lat, q_pe], -1)
+    assert ((qcat.float() - want_q).norm() / want_q.norm()).item() < 1e-2
+    rows = cache.view(-1, 576)[torch.where(slot >= 0, slot, torch.zeros_like(slot))]
+    assert ((rows.float() - lat).norm() / lat.norm()).item() < 1e-2
+    o_lat = torch.randn(T, H, 512, generator=g).to(cuda)
+    out = torch.empty(T, H * 128, dtype=torch.bfloat16, device=cuda)
+    ext().mla_o_absorb(o_lat, m["w_uv"], out)
+    want_o = torch.einsum("thc,hvc->thv", o_lat, m["w_uv"].float()).reshape(T, -1)
+    assert ((out.float() - want_o).norm() / want_o.norm()).item() < 1e-2
