@@ -254,6 +254,11 @@ def main():
     g = torch.Generator().manual_seed(1234)
     all_prompts = [torch.randint(0, cfg.vocab, (args.prompt,), generator=g).tolist() for _ in range(args.batch)]
     prompts = all_prompts[rank::world] if cfg.is_moe else all_prompts
+    # ---- warm-up (untimed): one request of the timed prompt length through prefill and two
+    # decode steps, so the timed prefill meets loaded kernels, encoded tensor maps and live NCCL
+    # communicators (their one-time set-up is not time to first token of a serving engine) ----
+    eng.generate([all_prompts[0]], SamplingParams(max_tokens=2, temperature=0.0))
+    torch.cuda.synchronize()
     # ---- prefill: TTFT of each request (all submitted at t0) ----
     ids = [eng.add_request(p, SamplingParams(max_tokens=decode_len, temperature=0.0)) for p in prompts]
     if ctx.enabled:
@@ -272,13 +277,14 @@ def main():
     prefill_prof = None
     if args.step_profile and runner.is_cuda:
         # every rank takes the same collective steps: a fixed list of segment kinds
-        agg = dict.fromkeys(("prefill_attn", "prefill_ffn", "prefill_moe", "prefill_head"), 0.0)
+        kinds = ("prefill_qkv", "prefill_attn_core", "prefill_attn", "prefill_ffn", "prefill_moe_route",
+                 "prefill_moe_stage", "prefill_moe_experts", "prefill_moe", "prefill_head")
+        agg = dict.fromkeys(kinds, 0.0)
         if runner._stamp_labels[-1:] == ["prefill_head"]:
             for lab, ms in runner.step_profile():
                 kind = lab.split(".")[-1]
                 agg[kind] = agg.get(kind, 0.0) + ms
-        prefill_prof = {k: round(max_over_ranks(ctx, agg[k]), 3) for k in
-                        ("prefill_attn", "prefill_ffn", "prefill_moe", "prefill_head")}
+        prefill_prof = {k: round(max_over_ranks(ctx, agg[k]), 3) for k in kinds}
         prefill_prof["tokens_in_pass"] = int(min(mpt, n_local * args.prompt))
     seqs = {s.seq_id: s for s in eng.running}
     my_ttft = [seqs[i].t_first_token - t_sub for i in ids]

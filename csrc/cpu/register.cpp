@@ -66,6 +66,8 @@ void register_all(pybind11::module& m) {
   m.def("gemm_bf16_ws", &gemm_bf16_ws);
   m.def("gemm_bf16_tp", &gemm_bf16_tp);
   m.def("flags_wait", &flags_wait);
+  m.def("q4_gemm_dec", &q4_gemm_dec, "4-bit weights x 16-64 token rows on tcgen05 (decode orientation)");
+  m.def("q4_gemm_dec_tp", &q4_gemm_dec_tp, "4-bit decode GEMM on tcgen05 with the TP peer push epilogue");
   m.def("argmax", &argmax);
   m.def("sample", &sample);
   m.def("philox", &philox);

@@ -136,6 +136,11 @@ void gemm_bf16_tp(torch::Tensor x, torch::Tensor w, torch::Tensor peers, int64_t
                   int64_t owner_rows, int64_t off_flag, int64_t rank, torch::Tensor done_ctr, torch::Tensor step_ctr,
                   int64_t n_layers, int64_t layer, torch::Tensor ws, torch::Tensor counters, torch::Tensor status,
                   int64_t src_stride);
+void q4_gemm_dec(torch::Tensor x, torch::Tensor qw, torch::Tensor sm, int64_t N, int64_t K, int64_t mode,
+                 torch::Tensor out, torch::Tensor status);
+void q4_gemm_dec_tp(torch::Tensor x, torch::Tensor qw, torch::Tensor sm, int64_t N, int64_t K, torch::Tensor peers,
+                    int64_t off_recv, int64_t cap, int64_t ldo, int64_t off_flag, int64_t rank, torch::Tensor done_ctr,
+                    torch::Tensor step_ctr, int64_t n_layers, int64_t layer, torch::Tensor status);
 void flags_wait(torch::Tensor peers, int64_t rank, int64_t off_flag, torch::Tensor step_ctr, int64_t n_layers,
                 int64_t layer, int64_t timeout_ns, torch::Tensor status);
 

@@ -265,6 +265,11 @@ cudaError_t launch_tc_gemm_bf16(const void* x, int T, int ldx, const void* w, in
                                 int ldo, float* ws, size_t ws_floats, unsigned* counters, const PeerPush* pp,
                                 int* status, cudaStream_t s);
 int bf16_gemm_splits(int N, int K, int T);
+// 4-bit tiled weights (syn/q4.h), 1..64 token rows, decode orientation on tcgen05 (weights as the
+// M operand); N % 128 == 0, K % 64 == 0; modes as launch_tc_gemm_bf16.
+cudaError_t launch_tc_gemm_q4_dec(const void* x, int T, int ldx, const void* qw, const void* sm, int N, int K,
+                                  int mode, void* out, int ldo, const PeerPush* pp, int* status, cudaStream_t s);
+int q4_dec_splits(int N, int K);
 // Bounded wait (grid of one CTA) until every rank's flag slot at off_flag holds this layer's
 // sequence number; a timeout sets bit 2 of status.
 cudaError_t launch_flags_wait(const int64_t* peers, int n, int rank, int64_t off_flag, const uint32_t* step_ctr,

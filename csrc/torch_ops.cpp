@@ -1101,6 +1101,43 @@ void gemm_bf16_tp(torch::Tensor x, torch::Tensor w, torch::Tensor peers, int64_t
 }
 
 
+// 4-bit weights, 16-64 token rows, on tcgen05 (decode orientation): out = x @ W^T with the
+// epilogues of gemm_bf16 (mode 0, 1, 3, 5); q4_gemm_dec_tp: the peer push (mode 6).
+void q4_gemm_dec(torch::Tensor x, torch::Tensor qw, torch::Tensor sm, int64_t N, int64_t K, int64_t mode,
+                 torch::Tensor out, torch::Tensor status) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1 && x.size(1) == K,
+              "q4_gemm_dec: x bf16 [T, K]");
+  TORCH_CHECK(qw.is_cuda() && sm.is_cuda() && qw.numel() * 4 == N * K / 2 && sm.numel() * 2 == N * K / 8,
+              "q4_gemm_dec: tiled 4-bit weights [N, K]");
+  TORCH_CHECK(mode == 0 || mode == 1 || mode == 3 || mode == 5, "q4_gemm_dec: mode 0, 1, 3 or 5");
+  const int64_t T = x.size(0), ncol = mode == 1 ? N / 2 : N;
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == T && out.size(1) == ncol && out.stride(1) == 1, "q4_gemm_dec: out shape");
+  TORCH_CHECK((mode <= 1 && out.scalar_type() == torch::kBFloat16) || (mode >= 3 && out.scalar_type() == torch::kFloat32),
+              "q4_gemm_dec: out dtype");
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_tc_gemm_q4_dec(x.data_ptr(), (int)T, (int)x.stride(0), qw.data_ptr(), sm.data_ptr(), (int)N,
+                                       (int)K, (int)mode, out.data_ptr(), (int)out.stride(0), nullptr,
+                                       status.data_ptr<int32_t>(), cur_stream()));
+}
+
+void q4_gemm_dec_tp(torch::Tensor x, torch::Tensor qw, torch::Tensor sm, int64_t N, int64_t K, torch::Tensor peers,
+                    int64_t off_recv, int64_t cap, int64_t ldo, int64_t off_flag, int64_t rank, torch::Tensor done_ctr,
+                    torch::Tensor step_ctr, int64_t n_layers, int64_t layer, torch::Tensor status) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1 && x.size(1) == K,
+              "q4_gemm_dec_tp: x bf16 [T, K]");
+  TORCH_CHECK(qw.numel() * 4 == N * K / 2 && sm.numel() * 2 == N * K / 8, "q4_gemm_dec_tp: tiled 4-bit weights");
+  TORCH_CHECK(x.size(0) <= cap && ldo >= N, "q4_gemm_dec_tp: rows exceed the receive slots");
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == torch::kInt64, "peers int64 (device)");
+  TORCH_CHECK(done_ctr.is_cuda() && done_ctr.scalar_type() == torch::kInt32, "done_ctr int32 (device)");
+  PeerPush pp{peers.data_ptr<int64_t>(), (int)peers.numel(), (int)rank, (int)cap, 0, 0, off_recv, off_flag,
+              reinterpret_cast<unsigned*>(done_ctr.data_ptr<int32_t>()),
+              reinterpret_cast<const uint32_t*>(step_ctr.data_ptr()), (int)n_layers, (int)layer};
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_tc_gemm_q4_dec(x.data_ptr(), (int)x.size(0), (int)x.stride(0), qw.data_ptr(), sm.data_ptr(),
+                                       (int)N, (int)K, 6, nullptr, (int)ldo, &pp, status.data_ptr<int32_t>(),
+                                       cur_stream()));
+}
+
 void flags_wait(torch::Tensor peers, int64_t rank, int64_t off_flag, torch::Tensor step_ctr, int64_t n_layers,
                 int64_t layer, int64_t timeout_ns, torch::Tensor status) {
   TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == torch::kInt64, "peers int64 (device)");

@@ -190,6 +190,30 @@ def main():
                    extra={"status": int(st.item())})
             wd = w.dequant()
             report(f"cublas_bf16_{M}x{N}x{K}(reference)", timeit(lambda: x @ wd.t(), iters=10), flops=2 * M * N * K)
+    if want("q4_dec"):
+        # 4-bit weights at 16-64 decode rows (Llama-3-70B layer shapes, one GPU and one TP8 rank):
+        # the tcgen05 decode GEMM against the mma.sync GEMV on the same inputs; weights in
+        # rotated copies larger than L2
+        from syntropy_b200.ops import core as _core
+        for N, K in ((10240, 8192), (8192, 8192), (57344, 8192), (8192, 28672), (1280, 8192), (7168, 8192),
+                     (8192, 3584)):
+            ncopy = max(1, int(2 * 126e6 // (N * K // 2)) + 1)
+            ws = [Q4Weight.quantize(torch.randn(N, K, device=dev) * 0.02) for _ in range(min(ncopy, 64))]
+            for rows in (16, 32, 64):
+                x = torch.randn(rows, K, device=dev).to(torch.bfloat16)
+                out = torch.empty(rows, N, dtype=torch.float32, device=dev)
+                it = [0]
+
+                def fn():
+                    it[0] += 1
+                    ops.linear(x, ws[it[0] % len(ws)], out, ops.GEMV_STORE)
+                nbytes = N * K // 2 + N * K // 8
+                saved = _core._Q4_TC[0]
+                for impl, thr in (("tcgen05", 16), ("mma_sync_gemv", 1 << 30)):
+                    _core._Q4_TC[0] = thr
+                    report(f"q4_dec_{impl}_{rows}x{N}x{K}", timeit(fn, iters=20), nbytes=nbytes,
+                           flops=2 * rows * N * K)
+                _core._Q4_TC[0] = saved
     if want("gemm_bf16"):
         # Llama-3-8B bf16 projections: one GPU and one TP8 rank at decode (64 rows), and a
         # 2048-token prefill; our tcgen05 GEMM against the library GEMM on the same inputs

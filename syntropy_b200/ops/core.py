@@ -122,6 +122,11 @@ def _linear_fp8(x, W, out, mode):
     return out
 
 
+# SYN_Q4_TC_MIN: fewest token rows for which 4-bit decode products run on tcgen05 (default 16;
+# a value above 64 keeps every decode product on the mma.sync GEMV)
+_Q4_TC = [int(__import__("os").environ.get("SYN_Q4_TC_MIN", "16"))]
+
+
 def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: torch.Tensor | None = None):
     """out = x @ W^T with an epilogue:
     STORE: out = y; SWIGLU: out = silu(gate) * up (interleaved rows); ADD_F32: out += y (f32)."""
@@ -137,6 +142,14 @@ def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: t
     T = x.shape[0]
     if getattr(W, "tiled", None) is not None and T <= DECODE_ROWS_MAX and x.dtype == torch.bfloat16:
         return _linear_fp8(x, W, out, mode)
+    if isinstance(W, Q4Weight) and _Q4_TC[0] <= T <= DECODE_ROWS_MAX and W.N % 128 == 0 and W.K % 64 == 0 and \
+            x.dtype == torch.bfloat16 and x.stride(-1) == 1 and out.stride(-1) == 1:
+        # 16-64 rows: tcgen05 with the dequantised weights as the M operand (one dequantisation
+        # per weight whatever the row count; the mma.sync GEMV is instruction-bound here)
+        kmode = {GEMV_STORE: 0 if out.dtype == torch.bfloat16 else 5, GEMV_SWIGLU: 1, GEMV_ADD_F32: 3}[mode]
+        ext().q4_gemm_dec(x, W.qw, W.sm, W.N, W.K, kmode, out, gemm_status(x.device))
+        _launched()
+        return out
     if isinstance(W, Q4Weight) and (_DENSE_V5[1] <= T or W.N * W.K >= (64 << 20)) and T <= DECODE_ROWS_MAX \
             and W.N % 64 == 0 and W.K % 128 == 0 and _DENSE_V5[0]:
         kmode = {GEMV_STORE: 0, GEMV_SWIGLU: 1, GEMV_ADD_F32: 3}[mode]

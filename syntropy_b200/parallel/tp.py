@@ -109,6 +109,12 @@ class TPGroup:
                 ext().gemm_bf16_tp(x_in, W, self.region.peers, self.off_recv[which], self.cap, self.H, 0,
                                    self.off_flag[which], self.rank, self.done_ctr[seq_layer:seq_layer + 1],
                                    self.step_ctr, 2 * self.n_layers, seq_layer, ws, ctr, gemm_status(x_in.device), 0)
+            elif T >= ops.core._Q4_TC[0] and W.N % 128 == 0 and W.K % 64 == 0:
+                # 16-64 rows of 4-bit weights: the tcgen05 decode GEMM pushes each f32 row to every peer
+                from ..ops.core import gemm_status
+                ext().q4_gemm_dec_tp(x_in, W.qw, W.sm, W.N, W.K, self.region.peers, self.off_recv[which], self.cap,
+                                     self.H, self.off_flag[which], self.rank, self.done_ctr[seq_layer:seq_layer + 1],
+                                     self.step_ctr, 2 * self.n_layers, seq_layer, gemm_status(x_in.device))
             else:
                 from ..ops.core import _ptrs
                 qp, sp = _ptrs(W)

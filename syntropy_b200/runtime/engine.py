@@ -603,7 +603,7 @@ class LLMEngine:
                 d["temperature"][row] = 0.0
         if r.use_graphs:
             from .runner import bucket_for
-            for i in range(rows, bucket_for(rows)):
+            for i in range(rows, bucket_for(rows, cap=r.max_batch)):
                 d["tokens"][i] = 0
                 d["pos"][i] = 0
                 d["ctx_len"][i] = 1
@@ -675,7 +675,7 @@ class LLMEngine:
                              [s.params.top_k for s in seqs], [kv.slot(s.blocks, p) for s, p in zip(seqs, pos)],
                              [s.seed for s in seqs], [s.stream for s in seqs], [s.rng_counter for s in seqs],
                              [float(s.params.temperature) for s in seqs], [float(s.params.top_p) for s in seqs],
-                             [s.blocks for s in seqs], bucket_for(B) if r.use_graphs else B)
+                             [s.blocks for s in seqs], bucket_for(B, cap=r.max_batch) if r.use_graphs else B)
         nxt = r.decode(B).cpu().tolist()
         r.after_step()
         cons = [i for i, s in enumerate(seqs) if self._redraw(s)]

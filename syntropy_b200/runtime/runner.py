@@ -19,13 +19,15 @@ from ..formats.q4 import Q4Weight
 from ..kv.paged import PagedKVCache
 from ..models.transformer import ModelWeights
 
-BUCKETS = (1, 2, 4, 8, 16, 32, 48, 64)
+BUCKETS = (1, 2, 4, 8, 16, 32, 48, 64, 96, 128, 192, 256)  # rows past 64: verify windows of drafts
 
 
-def bucket_for(n: int, buckets=BUCKETS) -> int:
+def bucket_for(n: int, buckets=BUCKETS, cap: int | None = None) -> int:
+    """Graph bucket for n rows: the smallest bucket that holds them, never above `cap` (the
+    runner's row count, itself the last bucket when it is not one of BUCKETS)."""
     for b in buckets:
         if n <= b:
-            return b
+            return b if cap is None else min(b, max(cap, n))
     raise ValueError(f"batch {n} exceeds the largest bucket {buckets[-1]}")
 
 
@@ -526,7 +528,7 @@ class ModelRunner:
         self.profile_next = False
         self._stamping = prof
         if self.use_graphs:
-            bb = bucket_for(B)
+            bb = bucket_for(B, cap=self.max_batch)
             key = ("profiled", bb) if prof else bb
             g = self.graphs.get(key)
             if g is None:
@@ -773,6 +775,7 @@ class ModelRunner:
                 qkv.add_(L.qkv_bias)
             ops.qk_rope_kv_write(qkv, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, L.q_norm, L.k_norm, cfg.rms_eps,
                                  positions, mw.rope_cos, mw.rope_sin, slots, q, self.kv.k[i], self.kv.v[i])
+            self._stamp(f"layer{i}.prefill_qkv")
             if paged is not None:
                 ops.attn_prefill_paged(q, self.kv.k[i], self.kv.v[i], paged[0], paged[1], paged[2], attn, paged[3],
                                        self.scale)
@@ -782,6 +785,7 @@ class ModelRunner:
                 ops.attn_prefill(q, kc, vc, cu_seqlens, attn, self.scale)
             else:
                 self._prefill_attn_with_prefix(i, q, attn, cu_seqlens, prefix)
+            self._stamp(f"layer{i}.prefill_attn_core")
             self._row_parallel(attn.view(T, -1), L.o, x)
             self._stamp(f"layer{i}.prefill_attn")
             ops.rms_norm(x, L.ffn_norm, cfg.rms_eps, out=h)
@@ -961,6 +965,7 @@ class ModelRunner:
             else:  # a plain bf16 GEMM with f32 output (library); top-k and CSR are ours
                 logits = torch.mm(h, L.router.t(), out_dtype=torch.float32)
             ops.moe_topk(logits, cfg, L.router_bias, False, mb, counts=self._counts_for(L))
+            self._stamp("prefill_moe_route")
         else:
             logits = h.float() @ L.router.float().t()
             _route_torch(logits, cfg, L.router_bias, mb)
@@ -971,6 +976,7 @@ class ModelRunner:
         if L.shared_gu is not None and T > 0:
             x.add_(self._shared_expert(L, h))
         staged = self.expert_cache.staged_ptrs(L) if self.expert_cache is not None else None
+        self._stamp("prefill_moe_stage")  # (profiled passes) the wait for this layer's staged host experts
         if self.ep is not None:
             x.add_(self.ep.moe_baseline(h, mb["topk_ids"], mb["topk_w"], gu, dn, staged=staged))
             return
@@ -989,6 +995,7 @@ class ModelRunner:
             yp = torch.empty(P, dn.N, dtype=torch.float32, device=dev)
             ops.gemm_grouped(mid, dq, ds, mb["tok_off"], dn.N, dn.K, 2, mb["pair_w"], yp, E,
                              dn.qw if bk else None, dn.sm if bk else None)
+            self._stamp("prefill_moe_experts")
             ops.moe_combine_rmsnorm(x, yp, mb["pair_of"], None, None, None, cfg.rms_eps)
             return
         from ..parallel.ep import _local_experts_apply

@@ -28,7 +28,11 @@ ctx = init_distributed(timeout_s=60)
 cfg = get_config(os.environ.get("MODEL", "small-qwen-moe"))
 # MTP verify windows hold 2 rows per sequence
 ep = EPGroup(ctx, cfg.n_experts, cfg.top_k, cfg.hidden, cap=8 if spec_on else 4, n_layers=cfg.n_layers, fused=fused)
-mw = prepare_weights(cfg, ctx.device, seed=7, expert_range=ep.expert_range)
+if cfg.weight_quant == "fp8":  # the same synthetic weights the test's f32 reference uses
+    from syntropy_b200.models.weights import synthetic_state_dict
+    mw = prepare_weights(cfg, ctx.device, state_dict=synthetic_state_dict(cfg, seed=7), expert_range=ep.expert_range)
+else:
+    mw = prepare_weights(cfg, ctx.device, seed=7, expert_range=ep.expert_range)
 runner = ModelRunner(mw, max_batch=8 if spec_on else 4, max_seq_len=256, ep=ep, use_graphs=fused)
 spec = None
 if spec_on:
@@ -90,37 +94,34 @@ def test_ep_fused_matches_baseline_and_single_gpu():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ep_fused_fp8_deepseek_with_mtp_matches_single_gpu():
+def test_ep_fused_fp8_deepseek_with_mtp_follows_reference():
     """DeepSeek-style layers (MLA, block-scaled fp8 experts, a shared expert, group-limited
-    routing) through the fused dispatch/combine with MTP drafts verified in the same decode
-    graphs, against one GPU holding every expert without drafts."""
+    routing) through the fused dispatch/combine, with and without MTP drafts verified in the
+    same decode graphs: every emitted token is checked teacher-forced against the f32 reference
+    forward over the fp8-rounded weights (the bound of the single-GPU fp8 engine test: e4m3
+    activations flip near-ties of this random-weight model)."""
+    from syntropy_b200.models import reference
     from syntropy_b200.models.config import get_config
-    from syntropy_b200.models.transformer import prepare_weights
-    from syntropy_b200.runtime.engine import LLMEngine, SamplingParams
-    from syntropy_b200.runtime.runner import ModelRunner
+    from syntropy_b200.models.weights import synthetic_state_dict
+    from test_gpu_mla import _fp8_roundtrip_state
     plain = _run(True, "small-deepseek", spec=False, port=29613)
     spec = _run(True, "small-deepseek", spec=True, port=29614)
     for r in (0, 1):
         assert plain[r]["status"] == 0 and spec[r]["status"] == 0
         assert spec[r]["accept"] is not None
     cfg = get_config("small-deepseek")
-    mw = prepare_weights(cfg, torch.device("cuda:0"), seed=7)
+    sdq = _fp8_roundtrip_state(synthetic_state_dict(cfg, seed=7))
     g = torch.Generator().manual_seed(3)
     prompts = [torch.randint(0, cfg.vocab, (n,), generator=g).tolist() for n in (11, 30, 7, 19)]
-    single = LLMEngine(ModelRunner(mw, max_batch=4, max_seq_len=256)).generate(prompts, SamplingParams(max_tokens=8))
-
-    def agree(res):
-        seqs = [(x, y) for r in (0, 1) for x, y in zip(res[r]["outs"], single[r::2])]
-        first = sum(x[0] == y[0] for x, y in seqs)
-        prefix = sum(next((i for i, (a, b) in enumerate(zip(x, y)) if a != b), len(y)) for x, y in seqs)
-        return first, prefix / sum(len(y) for _, y in seqs)
-    # greedy tokens agree up to near-tie flips (the f32 summation association differs between the
-    # EP combine and the single-GPU combine; verify windows batch 2 rows per sequence), and a flip
-    # changes the rest of its sequence: the first tokens and most of the common prefix agree
     for res in (plain, spec):
-        first, prefix = agree(res)
-        msg = json.dumps({"ep": [res[r]["outs"] for r in (0, 1)], "single": single})
-        assert first >= 3 and prefix >= 0.5, (first, prefix, msg)
+        agree = total = 0
+        for r in (0, 1):
+            for p, o in zip(prompts[r::2], res[r]["outs"]):
+                logits = reference.forward(torch.tensor(p + o), sdq, cfg)
+                ref_next = torch.argmax(logits[len(p) - 1:-1], -1).tolist()
+                agree += sum(int(x == y) for x, y in zip(ref_next, o))
+                total += len(o)
+        assert agree / total >= 0.6, (agree, total, res)
 
 
 TP_WORKER = r"""
