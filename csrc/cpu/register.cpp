@@ -82,6 +82,7 @@ void register_all(pybind11::module& m) {
   m.def("ep_combine", &ep_combine);
   m.def("q4_gemv_ep", &q4_gemv_ep);
   m.def("tc_gemm_q4", &tc_gemm_q4);
+  m.def("tc_gemm_q4_banks", &tc_gemm_q4_banks, "grouped 4-bit tcgen05 GEMM over two weight banks (TMA)");
   m.def("verify_accept", &verify_accept);
   m.def("q4_gemv_tp", &q4_gemv_tp);
   m.def("tp_reduce_norm", &tp_reduce_norm);

@@ -15,6 +15,7 @@
 #include <mutex>
 #include <string>
 #include <thread>
+#include <algorithm>
 #include <vector>
 
 #include <torch/extension.h>
@@ -413,7 +414,39 @@ class Counter {
   std::atomic<int64_t> v_{0};
 };
 
+// Prompt-lookup drafting for a batch of sequences: for each history, the most recent earlier
+// occurrence of its last n tokens (n from max_n down to 1) and the g tokens that followed it,
+// padded with the last of them; without any match, g copies of the last token.  One linear
+// scan per (sequence, n), in native code because the host builds the drafts of every running
+// sequence each decode step.
+static std::vector<std::vector<int64_t>> ngram_propose_py(const std::vector<std::vector<int64_t>>& histories,
+                                                          int max_n, int g) {
+  std::vector<std::vector<int64_t>> out;
+  out.reserve(histories.size());
+  for (const auto& h : histories) {
+    const int64_t L = (int64_t)h.size();
+    std::vector<int64_t> d;
+    for (int n = (int)std::min<int64_t>(max_n, L - 1); n >= 1 && d.empty(); --n) {
+      const int64_t* key = h.data() + L - n;
+      for (int64_t i = L - n - 1; i >= 0; --i) {
+        if (std::equal(key, key + n, h.data() + i)) {
+          const int64_t c0 = i + n, c1 = std::min<int64_t>(L, c0 + g);
+          if (c1 > c0) {
+            d.assign(h.begin() + c0, h.begin() + c1);
+            break;
+          }
+        }
+      }
+    }
+    if (d.empty()) d.assign(g, L > 0 ? h.back() : 0);
+    while ((int)d.size() < g) d.push_back(d.back());
+    out.push_back(std::move(d));
+  }
+  return out;
+}
+
 void register_runtime(py::module& m) {
+  m.def("ngram_propose", &ngram_propose_py, "prompt-lookup drafts for a batch of token histories");
   py::class_<ShmRegion>(m, "ShmRegion")
       .def(py::init<const std::string&, int64_t, bool>())
       .def("address", &ShmRegion::address)

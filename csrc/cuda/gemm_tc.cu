@@ -44,6 +44,9 @@ struct TcGemmArgs {
   int G, M, N, K;
   int mode;                 // 0 store bf16, 1 swiglu bf16 [M, N/2], 2 scaled f32, 3 add f32, 5 store f32
   int* status;
+  // two banks (raw_tma): group g's weights are entry grp_sel[g] >> 1 of bank grp_sel[g] & 1
+  // (bank 0: tmap_q / tmap_s, bank 1: tmap_q2 / tmap_s2); null: entry group_base + g of bank 0
+  const int32_t* grp_sel;
 };
 
 template <int BN>
@@ -65,6 +68,8 @@ template <int BN>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                             const __grid_constant__ CUtensorMap tmap_q,
                                                             const __grid_constant__ CUtensorMap tmap_s,
+                                                            const __grid_constant__ CUtensorMap tmap_q2,
+                                                            const __grid_constant__ CUtensorMap tmap_s2,
                                                             TcGemmArgs a) {
   constexpr int TC_STAGES = TcCfg<BN>::STAGES;
   constexpr int TC_RAW = TcCfg<BN>::RAW;
@@ -145,10 +150,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
   } else if (warp == 2) {
     // ---------------- raw 4-bit weight loader ----------------
     if (lane == 0) {
-      const uint8_t* qw = reinterpret_cast<const uint8_t*>(a.qw_ptrs[grp]);
-      const uint8_t* sm = reinterpret_cast<const uint8_t*>(a.sm_ptrs[grp]);
+      // pointer tables are read only on the bulk-copy path (the two-bank launch passes none)
+      const uint8_t* qw = a.raw_tma ? nullptr : reinterpret_cast<const uint8_t*>(a.qw_ptrs[grp]);
+      const uint8_t* sm = a.raw_tma ? nullptr : reinterpret_cast<const uint8_t*>(a.sm_ptrs[grp]);
       const int KG = a.K >> 6;
       const int tile0 = ntile * (BN / 16);
+      const CUtensorMap* mq = &tmap_q;
+      const CUtensorMap* ms = &tmap_s;
+      int entry = a.group_base + grp;
+      if (a.raw_tma && a.grp_sel) {
+        const int sel = a.grp_sel[grp];
+        entry = sel >> 1;
+        if (sel & 1) {
+          mq = &tmap_q2;
+          ms = &tmap_s2;
+        }
+      }
       for (int kb = 0; kb < KB; ++kb) {
         const int r = kb % TC_RAW;
         const uint32_t ph = (kb / TC_RAW) & 1;
@@ -157,8 +174,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
         uint8_t* dst = sR + r * RAW_BYTES;
         if (a.raw_tma) {
           // [BN/16 tiles x 512 B] of nibbles, then [BN/16 x 128 B] of scales: two copies
-          tma_load_4d(dst, &tmap_q, 0, kb, tile0, a.group_base + grp, &raw_full[r]);
-          tma_load_4d(dst + (BN / 16) * 512, &tmap_s, 0, kb, tile0, a.group_base + grp, &raw_full[r]);
+          tma_load_4d(dst, mq, 0, kb, tile0, entry, &raw_full[r]);
+          tma_load_4d(dst + (BN / 16) * 512, ms, 0, kb, tile0, entry, &raw_full[r]);
         } else {
 #pragma unroll 4
           for (int i = 0; i < BN / 16; ++i) {
@@ -307,13 +324,37 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
 }
 
 // ---- host side ----
+// 4-D tensor maps over a contiguous bank of packed 4-bit matrices [entries][N/16][K/64]:
+// nibbles 512 B and scale/min 128 B per (16-row tile, 64-column block); one box = BN/16 tiles.
+static bool encode_raw_maps(PFN_encodeTiled enc, CUtensorMap* mq, CUtensorMap* ms, const void* bank_qw,
+                            const void* bank_sm, int entries, int N, int K, int BN) {
+  const cuuint64_t KG = (cuuint64_t)(K / 64), NT = (cuuint64_t)(N / 16);
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const cuuint64_t dq[4] = {128, KG, NT, (cuuint64_t)entries};  // [entry][tile][kg][128 x u32]
+  const cuuint64_t sq[3] = {512, 512 * KG, 512 * KG * NT};
+  const cuuint32_t bq[4] = {128, 1, (cuuint32_t)(BN / 16), 1};
+  if (enc(mq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, const_cast<void*>(bank_qw), dq, sq, bq, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  const cuuint64_t ds[4] = {32, KG, NT, (cuuint64_t)entries};    // [entry][tile][kg][32 x u32]
+  const cuuint64_t ss[3] = {128, 128 * KG, 128 * KG * NT};
+  const cuuint32_t bs[4] = {32, 1, (cuuint32_t)(BN / 16), 1};
+  return enc(ms, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, const_cast<void*>(bank_sm), ds, ss, bs, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // bank_qw/bank_sm: base of a contiguous expert bank (or of one matrix) and the number
 // of experts in it; when given (non-null), the packed weights stream with two 4-D TMA copies
-// per stage instead of 2 * BN/16 bulk copies.
+// per stage instead of 2 * BN/16 bulk copies.  bank2_* and grp_sel: a second bank (e.g. the
+// VRAM residents in bank 0 and the staged host experts in bank 1); group g reads entry
+// grp_sel[g] >> 1 of bank grp_sel[g] & 1.
 cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, const int64_t* sm_ptrs,
                               const int32_t* row_off, int G, int M, int N, int K, int mode, const float* route_w,
                               void* out, int* status, int max_mtiles, const void* bank_qw, const void* bank_sm,
-                              int bank_experts, int group_base, cudaStream_t s) {
+                              int bank_experts, int group_base, cudaStream_t s, const void* bank2_qw,
+                              const void* bank2_sm, int bank2_experts, const int32_t* grp_sel) {
   if (K % TC_BK != 0 || N % 128 != 0 || M <= 0) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || (ldx * 2) % 16 != 0) return cudaErrorInvalidValue;
   PFN_encodeTiled enc = get_encode();
@@ -333,29 +374,20 @@ cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, co
   }
   const bool wide = (N % 256 == 0);
   const int BN = wide ? 256 : 128;
-  const int raw_tma = bank_qw != nullptr && bank_sm != nullptr &&
-                      (reinterpret_cast<uintptr_t>(bank_qw) & 15) == 0 && (reinterpret_cast<uintptr_t>(bank_sm) & 15) == 0;
+  auto aligned = [](const void* p) { return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const int raw_tma = aligned(bank_qw) && aligned(bank_sm);
+  if (bank2_qw != nullptr && !(raw_tma && aligned(bank2_qw) && aligned(bank2_sm) && grp_sel != nullptr))
+    return cudaErrorInvalidValue;
+  CUtensorMap mq2, ms2;
+  memset(&mq2, 0, sizeof(mq2));
+  memset(&ms2, 0, sizeof(ms2));
   if (raw_tma) {
-    const cuuint64_t KG = (cuuint64_t)(K / 64), NT = (cuuint64_t)(N / 16);
-    const cuuint32_t estr[4] = {1, 1, 1, 1};
-    // nibbles: [expert][tile][kg][128 x u32]
-    const cuuint64_t dq[4] = {128, KG, NT, (cuuint64_t)bank_experts};
-    const cuuint64_t sq[3] = {512, 512 * KG, 512 * KG * NT};
-    const cuuint32_t bq[4] = {128, 1, (cuuint32_t)(BN / 16), 1};
-    CUresult r = enc(&mq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, const_cast<void*>(bank_qw), dq, sq, bq, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
-    // scales: [expert][tile][kg][32 x u32]
-    const cuuint64_t ds[4] = {32, KG, NT, (cuuint64_t)bank_experts};
-    const cuuint64_t ss[3] = {128, 128 * KG, 128 * KG * NT};
-    const cuuint32_t bs[4] = {32, 1, (cuuint32_t)(BN / 16), 1};
-    r = enc(&ms, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, const_cast<void*>(bank_sm), ds, ss, bs, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    if (!encode_raw_maps(enc, &mq, &ms, bank_qw, bank_sm, bank_experts, N, K, BN)) return cudaErrorInvalidValue;
+    if (bank2_qw != nullptr && !encode_raw_maps(enc, &mq2, &ms2, bank2_qw, bank2_sm, bank2_experts, N, K, BN))
+      return cudaErrorInvalidValue;
   }
-  TcGemmArgs a{raw_tma, qw_ptrs, sm_ptrs, row_off, route_w, out, group_base, G, M, N, K, mode, status};
+  TcGemmArgs a{raw_tma, qw_ptrs, sm_ptrs, row_off, route_w, out, group_base, G, M, N, K, mode, status,
+               bank2_qw != nullptr ? grp_sel : nullptr};
   const size_t smem = wide ? TcCfg<256>::SMEM : TcCfg<128>::SMEM;
   dim3 grid((unsigned)max_mtiles, (unsigned)(N / BN));
   if (wide) {
@@ -366,7 +398,7 @@ cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, co
       if (e != cudaSuccess) return e;
       set = true;
     }
-    tc_gemm_q4_kernel<256><<<grid, TC_THREADS, smem, s>>>(map, mq, ms, a);
+    tc_gemm_q4_kernel<256><<<grid, TC_THREADS, smem, s>>>(map, mq, ms, mq2, ms2, a);
   } else {
     static bool set = false;
     if (!set) {
@@ -375,7 +407,7 @@ cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, co
       if (e != cudaSuccess) return e;
       set = true;
     }
-    tc_gemm_q4_kernel<128><<<grid, TC_THREADS, smem, s>>>(map, mq, ms, a);
+    tc_gemm_q4_kernel<128><<<grid, TC_THREADS, smem, s>>>(map, mq, ms, mq2, ms2, a);
   }
   return cudaGetLastError();
 }

@@ -17,6 +17,9 @@ void q4_gemv(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torc
              torch::Tensor tok_idx, torch::Tensor route_w, torch::Tensor res, torch::Tensor out,
              int64_t N, int64_t K, int64_t mode, int64_t nt_hint, int64_t e_active, torch::Tensor xsum,
              bool in_vram);
+void tc_gemm_q4_banks(torch::Tensor x, torch::Tensor row_off, int64_t N, int64_t K, int64_t mode, torch::Tensor route_w,
+                      torch::Tensor out, torch::Tensor status, int64_t max_mtiles, torch::Tensor b0_qw,
+                      torch::Tensor b0_sm, torch::Tensor b1_qw, torch::Tensor b1_sm, torch::Tensor sel);
 void block_sums(torch::Tensor x, torch::Tensor out);
 
 void rmsnorm(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor out);

@@ -76,7 +76,8 @@ cudaError_t launch_block_sums(const void* x, int rows, int K, int ldx, float* ou
 cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, const int64_t* sm_ptrs,
                               const int32_t* row_off, int G, int M, int N, int K, int mode, const float* route_w,
                               void* out, int* status, int max_mtiles, const void* bank_qw, const void* bank_sm,
-                              int bank_experts, int group_base, cudaStream_t s);
+                              int bank_experts, int group_base, cudaStream_t s, const void* bank2_qw = nullptr,
+                              const void* bank2_sm = nullptr, int bank2_experts = 0, const int32_t* grp_sel = nullptr);
 
 // ---- expert parallelism over NVLink peer memory ----
 struct EpArgs {

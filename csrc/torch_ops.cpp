@@ -476,6 +476,41 @@ void tc_gemm_q4(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, t
 }
 
 
+// The grouped 4-bit GEMM over two contiguous banks: group g reads entry sel[g] >> 1 of bank
+// sel[g] & 1 (bank 0: b0_qw / b0_sm [entries, N*K/8 u32 / N*K/16 f16], bank 1 likewise).
+void tc_gemm_q4_banks(torch::Tensor x, torch::Tensor row_off, int64_t N, int64_t K, int64_t mode, torch::Tensor route_w,
+                      torch::Tensor out, torch::Tensor status, int64_t max_mtiles, torch::Tensor b0_qw,
+                      torch::Tensor b0_sm, torch::Tensor b1_qw, torch::Tensor b1_sm, torch::Tensor sel) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x bf16 [M, K]");
+  TORCH_CHECK(x.size(1) == K && K % 64 == 0 && N % 128 == 0, "tc_gemm_q4_banks shapes (K%64, N%128)");
+  TORCH_CHECK(row_off.is_cuda() && row_off.scalar_type() == torch::kInt32 && sel.is_cuda() &&
+                  sel.scalar_type() == torch::kInt32 && sel.numel() + 1 == row_off.numel(),
+              "row_off int32 [G+1], sel int32 [G]");
+  const int64_t per_q = N * K / 8, per_s = N * K / 16;
+  TORCH_CHECK(b0_qw.is_cuda() && b0_qw.dim() == 2 && b0_qw.size(1) == per_q && b0_sm.dim() == 2 &&
+                  b0_sm.size(1) == per_s && b0_sm.size(0) == b0_qw.size(0) && b0_qw.is_contiguous() &&
+                  b0_sm.is_contiguous(), "bank 0 [entries, words]");
+  TORCH_CHECK(b1_qw.is_cuda() && b1_qw.dim() == 2 && b1_qw.size(1) == per_q && b1_sm.dim() == 2 &&
+                  b1_sm.size(1) == per_s && b1_sm.size(0) == b1_qw.size(0) && b1_qw.is_contiguous() &&
+                  b1_sm.is_contiguous(), "bank 1 [entries, words]");
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == torch::kInt32, "status int32");
+  const int64_t M = x.size(0);
+  if (mode == 1) TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.size(-1) == N / 2 && out.size(0) >= M, "out swiglu");
+  if (mode == 0) TORCH_CHECK(out.scalar_type() == torch::kBFloat16 && out.size(-1) == N && out.size(0) >= M, "out bf16");
+  if (mode == 2 || mode == 3 || mode == 5)
+    TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.size(-1) == N && out.size(0) >= M, "out f32");
+  if (mode == 2) TORCH_CHECK(route_w.numel() >= M, "route_w");
+  TORCH_CHECK(out.is_contiguous(), "out contiguous");
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_tc_gemm_q4(x.data_ptr(), (int)x.stride(0), nullptr, nullptr, row_off.data_ptr<int32_t>(),
+                                   (int)sel.numel(), (int)M, (int)N, (int)K, (int)mode,
+                                   mode == 2 ? route_w.data_ptr<float>() : nullptr, out.data_ptr(),
+                                   status.data_ptr<int32_t>(), (int)max_mtiles, b0_qw.data_ptr(), b0_sm.data_ptr(),
+                                   (int)b0_qw.size(0), 0, cur_stream(), b1_qw.data_ptr(), b1_sm.data_ptr(),
+                                   (int)b1_qw.size(0), sel.data_ptr<int32_t>()));
+}
+
 void block_sums(torch::Tensor x, torch::Tensor out) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x bf16 [rows, K]");
   TORCH_CHECK(x.size(1) % 32 == 0, "K % 32");

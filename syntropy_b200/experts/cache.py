@@ -285,7 +285,28 @@ class ExpertCache:
         nxt = self.layers[li + 1].expert_tier if li + 1 < len(self.layers) else None
         if nxt is not None and nxt.E > nxt.n_res:
             self._issue(li + 1, 1 - buf)
+        self._staged_buf = (li, buf)
         return self._ptrs_for(L, buf)
+
+    def staged_banks(self, L):
+        """After `staged_ptrs(L)`: the two contiguous banks that hold layer L's experts for the
+        prefill GEMM's tensor maps, per matrix (gate_up, down): (resident q, resident s, staged q,
+        staged s), and the selector int32 [E]: (slot << 1) for a resident expert, (host row << 1)
+        | 1 for a staged one.  None when the layer is not staged on the device."""
+        b = L.expert_tier
+        if not b.cuda:
+            return None
+        li = next(i for i, X in enumerate(self.layers) if X is L)
+        if b.E - b.n_res == 0 or getattr(self, "_staged_buf", (None,))[0] != li:
+            return None
+        buf = self._staged_buf[1]
+        sel = [(b.slot_of[e] << 1) if b.slot_of[e] >= 0 else ((b.host_of[e] << 1) | 1) for e in range(b.E)]
+        banks = []
+        for which, p in enumerate(b.parts):
+            st = self._staging[buf][which]
+            res_q, res_s = (p["qv"], p["sv"]) if b.n_res > 0 else (st["q"], st["s"])
+            banks.append((res_q, res_s, st["q"], st["s"]))
+        return banks[0], banks[1], torch.tensor(sel, dtype=torch.int32).to(self.device, non_blocking=True)
 
     def _issue(self, li, buf):
         b = self.layers[li].expert_tier

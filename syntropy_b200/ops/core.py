@@ -389,6 +389,20 @@ def gemm_grouped(x, qw_ptrs, sm_ptrs, row_off, N, K, mode, route_w, out, G, bank
     return out
 
 
+def gemm_grouped_banks(x, row_off, N, K, mode, route_w, out, banks, sel):
+    """gemm_grouped over two contiguous weight banks streamed by TMA: banks = (q0, s0, q1, s1)
+    with [entries, words] each; group g reads entry sel[g] >> 1 of bank sel[g] & 1."""
+    M = x.shape[0]
+    if M == 0:
+        return out
+    G = sel.numel()
+    q0, s0, q1, s1 = banks
+    ext().tc_gemm_q4_banks(x, row_off, N, K, mode, route_w if route_w is not None else _EMPTY_F32(x.device), out,
+                           gemm_status(x.device), (M + 255) // 256 + G, q0, s0, q1, s1, sel)
+    _launched()
+    return out
+
+
 def linear_grouped(x: torch.Tensor, bank, tok_off: torch.Tensor, tok_idx: torch.Tensor | None,
                    out: torch.Tensor, mode: int, route_w: torch.Tensor | None = None,
                    qw_ptrs: torch.Tensor | None = None, sm_ptrs: torch.Tensor | None = None,

@@ -579,37 +579,37 @@ class LLMEngine:
         mtp = hasattr(self.spec.drafter, "after_verify")
         stochastic = getattr(self.spec.drafter, "stochastic", False)
         probs = []  # stochastic drafts: the distribution each was sampled from
-        for i, s in enumerate(seqs):
-            if mtp:
-                dr = (s.mtp_draft or [s.output[-1]])[:g]
-            elif stochastic:
-                dr, q = self.spec.drafter.propose(s.prompt + s.output, g, key=s.seq_id, seed=s.seed ^ s.stream)
-                probs.append(q)
-            elif getattr(self.spec.drafter, "stateful", False):
-                dr = self.spec.drafter.propose(s.prompt + s.output, g, key=s.seq_id)
-            else:
-                dr = self.spec.drafter.propose(s.prompt + s.output, g)
-            drafts.append(dr)
+        batch = getattr(self.spec.drafter, "propose_batch", None)
+        if batch is not None and not mtp and not stochastic:
+            drafts = batch([s.prompt + s.output for s in seqs], g)
+        else:
+            for s in seqs:
+                if mtp:
+                    dr = (s.mtp_draft or [s.output[-1]])[:g]
+                elif stochastic:
+                    dr, q = self.spec.drafter.propose(s.prompt + s.output, g, key=s.seq_id, seed=s.seed ^ s.stream)
+                    probs.append(q)
+                elif getattr(self.spec.drafter, "stateful", False):
+                    dr = self.spec.drafter.propose(s.prompt + s.output, g, key=s.seq_id)
+                else:
+                    dr = self.spec.drafter.propose(s.prompt + s.output, g)
+                drafts.append(dr)
+        # every verify row of every window in one native descriptor fill (greedy rows: the
+        # acceptance draws on the host-side verify, not in the graph's sampler)
+        tok_rows, pos_rows, slot_rows, bl_rows = [], [], [], []
+        for s, dr in zip(seqs, drafts):
             p = s.n_tokens - 1
             kv.ensure(s.blocks, p + g + 1)
-            bt = torch.tensor(s.blocks, dtype=torch.int32)
-            for j, tok in enumerate([s.output[-1]] + dr):
-                row = i * (g + 1) + j
-                d["tokens"][row] = tok
-                d["pos"][row] = p + j
-                d["ctx_len"][row] = p + j + 1
-                d["slot"][row] = kv.slot(s.blocks, p + j)
-                d["block_tables"][row, : len(s.blocks)] = bt
-                d["temperature"][row] = 0.0
-        if r.use_graphs:
-            from .runner import bucket_for
-            for i in range(rows, bucket_for(rows, cap=r.max_batch)):
-                d["tokens"][i] = 0
-                d["pos"][i] = 0
-                d["ctx_len"][i] = 1
-                d["slot"][i] = -1
-                d["block_tables"][i, 0] = 0
-                d["temperature"][i] = 0.0
+            for j, tok in enumerate([s.output[-1]] + list(dr)):
+                tok_rows.append(int(tok))
+                pos_rows.append(p + j)
+                slot_rows.append(kv.slot(s.blocks, p + j))
+                bl_rows.append(s.blocks)
+        from .runner import bucket_for
+        zeros_i, zeros_l = [0] * rows, [0] * rows
+        ext().step_desc_fill(r.desc.host, r.desc.rows, r.desc.max_blocks, tok_rows, pos_rows, zeros_i, slot_rows,
+                             zeros_l, zeros_l, zeros_l, [0.0] * rows, [1.0] * rows, bl_rows,
+                             bucket_for(rows, cap=r.max_batch) if r.use_graphs else rows)
         r.decode(rows)
         logits = r.buf["logits"][:rows]
         temp = torch.tensor([s.params.temperature for s in seqs], dtype=torch.float32)

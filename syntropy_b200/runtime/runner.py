@@ -990,11 +990,18 @@ class ModelRunner:
             P = T * k
             a_rows = h.index_select(0, mb["tok_idx"])
             mid = torch.empty(P, gu.N // 2, dtype=h.dtype, device=dev)
-            ops.gemm_grouped(a_rows, gq, gs, mb["tok_off"], gu.N, gu.K, 1, None, mid, E,
-                             gu.qw if bk else None, gu.sm if bk else None)
             yp = torch.empty(P, dn.N, dtype=torch.float32, device=dev)
-            ops.gemm_grouped(mid, dq, ds, mb["tok_off"], dn.N, dn.K, 2, mb["pair_w"], yp, E,
-                             dn.qw if bk else None, dn.sm if bk else None)
+            banks = self.expert_cache.staged_banks(L) if staged is not None and not bk else None
+            if banks is not None:
+                # residents and staged host experts in two contiguous banks: packed weights by TMA
+                gb, db, sel = banks
+                ops.core.gemm_grouped_banks(a_rows, mb["tok_off"], gu.N, gu.K, 1, None, mid, gb, sel)
+                ops.core.gemm_grouped_banks(mid, mb["tok_off"], dn.N, dn.K, 2, mb["pair_w"], yp, db, sel)
+            else:
+                ops.gemm_grouped(a_rows, gq, gs, mb["tok_off"], gu.N, gu.K, 1, None, mid, E,
+                                 gu.qw if bk else None, gu.sm if bk else None)
+                ops.gemm_grouped(mid, dq, ds, mb["tok_off"], dn.N, dn.K, 2, mb["pair_w"], yp, E,
+                                 dn.qw if bk else None, dn.sm if bk else None)
             self._stamp("prefill_moe_experts")
             ops.moe_combine_rmsnorm(x, yp, mb["pair_of"], None, None, None, cfg.rms_eps)
             return

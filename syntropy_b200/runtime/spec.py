@@ -25,6 +25,10 @@ class NgramDrafter:
     def __init__(self, n: int = 3):
         self.n = n
 
+    def propose_batch(self, histories: list[list[int]], g: int) -> list[list[int]]:
+        """Drafts of every running sequence in one native scan (same rule as `propose`)."""
+        return ext().ngram_propose(histories, self.n, g)
+
     def propose(self, history: list[int], g: int) -> list[int]:
         for n in range(min(self.n, len(history) - 1), 0, -1):
             key = history[-n:]

@@ -127,3 +127,28 @@ def test_host_tier_pack_round_trip(cuda, tmp_path):
     g = torch.Generator().manual_seed(3)
     prompts = [torch.randint(0, cfg.vocab, (n,), generator=g).tolist() for n in (17, 40, 5, 64)]
     assert LLMEngine(runner).generate(prompts, SamplingParams(max_tokens=8)) == _run(cuda, False)[0]
+
+
+def test_prefill_over_two_banks_matches_resident(cuda):
+    """Prefill with half the experts in the host tier: the grouped GEMMs stream the residents
+    and the staged host experts from two contiguous banks through TMA (per-expert bank
+    selector); the last-token logits equal those of the same model with every expert resident
+    (one contiguous bank)."""
+    cfg = get_config("small-qwen-moe")
+    g = torch.Generator().manual_seed(5)
+    prompt = torch.randint(0, cfg.vocab, (200,), generator=g)
+    blocks = list(range(1, 1 + (200 + 15) // 16))
+    slots = torch.tensor([blocks[p // 16] * 16 + p % 16 for p in range(200)])
+
+    def logits(capped):
+        mw = prepare_weights(cfg, cuda, seed=21)
+        runner = ModelRunner(mw, max_batch=4, max_seq_len=256)
+        if capped:
+            runner.expert_cache = ExpertCache(mw.layers, 0.5, cuda)
+        out = runner.prefill(prompt, torch.arange(200), slots, [0, 200], block_lists=[blocks])[0].float().cpu()
+        torch.cuda.synchronize()
+        return out, runner
+    want, _ = logits(False)
+    got, runner = logits(True)
+    assert runner.expert_cache.staged_banks(runner.mw.layers[-1]) is not None
+    assert ((got - want).norm() / want.norm()).item() < 1e-4

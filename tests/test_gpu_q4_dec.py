@@ -46,7 +46,8 @@ def test_q4_gemm_dec_modes(cuda, T, N, K, mode):
 
 
 def test_linear_routes_16_to_64_rows_to_tcgen05(cuda):
-    """ops.linear over 4-bit weights at 32 rows equals the GEMV path (SYN_Q4_TC_MIN above 64)."""
+    """ops.linear over 4-bit weights at 32 rows (tcgen05) against the GEMV path (SYN_Q4_TC_MIN
+    above 64) and the f32 reference."""
     from syntropy_b200.ops import core
     torch.manual_seed(1)
     W = Q4Weight.quantize(torch.randn(4096, 4096, device=cuda) * 0.02)
@@ -60,5 +61,8 @@ def test_linear_routes_16_to_64_rows_to_tcgen05(cuda):
         ops.linear(x, W, b, ops.GEMV_ADD_F32)
     finally:
         core._Q4_TC[0] = saved
-    assert _rel(a, b) < 1e-4
-    assert _rel(a, x.float() @ W.dequant().float().t()) < 5e-3
+    # the GEMV folds scale and min in f32; the tcgen05 path rounds each dequantised weight to
+    # bf16 once (as the prefill GEMM does): both within the bf16-weight bound of the reference
+    ref = x.float() @ W.dequant().float().t()
+    assert _rel(a, ref) < 5e-3 and _rel(b, ref) < 5e-3
+    assert _rel(a, b) < 5e-3

@@ -49,3 +49,15 @@ def test_acceptance_preserves_distribution():
     assert (freq - p).abs().max() < 0.03, (freq, p)
     # draws: accept -> 1 (u) + 1 (bonus); reject -> 1 (u) + 1 (residual)
     assert torch.all(ctr == 2)
+
+
+def test_ngram_native_batch_matches_python_rule():
+    """The native batched prompt-lookup drafts equal the per-sequence Python rule."""
+    import random as _r
+    from syntropy_b200.runtime.spec import NgramDrafter
+    rng = _r.Random(7)
+    d = NgramDrafter(n=3)
+    hist = [[rng.randrange(6) for _ in range(rng.randrange(1, 60))] for _ in range(50)]
+    hist.append([5])
+    for g in (1, 3, 4):
+        assert d.propose_batch(hist, g) == [d.propose(h, g) for h in hist]
