@@ -11,8 +11,8 @@
 // rank order: deterministic):
 //   warp 0      TMA producer of the X tiles (BT rows x 64 bf16, SWIZZLE_128B)
 //   warp 1      TMEM owner and MMA issuer (kind::f16, M = 128, N = BT, K = 16)
-//   warp 2      raw-weight loader: bulk async copies of the eight packed 16-row tiles
-//               (512 B of nibbles + 128 B of scale/min each) per 64-column block
+//   warp 2      raw-weight loader: two 4-D TMA copies per 64-column block (the eight packed
+//               16-row tiles: 8 x 512 B of nibbles, 8 x 128 B of scale/min)
 //   warps 4..11 dequantisers (one 16-row tile each): d * q + m in f32, one rounding to bf16,
 //               straight into the K-major SWIZZLE_128B A tile; then warps 4..7 run the
 //               epilogue of their TMEM lane quarter (shared with the bf16 GEMM: bf16 store,
@@ -27,26 +27,23 @@ namespace {
 constexpr int QD_THREADS = 384;
 constexpr int QD_PRODUCERS = 8;
 constexpr int QD_STAGES = 3;
-constexpr int QD_RAW = 4;
 constexpr int QD_A_BYTES = 128 * 128;           // 128 rows x 64 bf16
 constexpr int QD_RAW_BYTES = 8 * (512 + 128);   // eight 16-row packed tiles
 
 template <int BT>
 struct QdCfg {
   static constexpr int B_BYTES = BT * 128;
-  static constexpr size_t SMEM = 1024 + (size_t)QD_STAGES * (QD_A_BYTES + B_BYTES) + (size_t)QD_RAW * QD_RAW_BYTES;
+  static constexpr int RAW = BT <= 32 ? 8 : 6;  // packed-weight stages in flight (HBM latency)
+  static constexpr size_t SMEM = 1024 + (size_t)QD_STAGES * (QD_A_BYTES + B_BYTES) + (size_t)RAW * QD_RAW_BYTES;
   static_assert(SMEM <= 113 * 1024, "two CTAs per SM");
-};
-
-struct Q4DecWeights {
-  const uint8_t* qw;  // tiled nibbles [N/16][K/64][512 B]
-  const uint8_t* sm;  // tiled scale/min [N/16][K/64][128 B]
 };
 
 template <int BT, int MODE>
 __global__ void __launch_bounds__(QD_THREADS, 2)
-    tc_gemm_q4_dec_kernel(const __grid_constant__ CUtensorMap tmap_x, Q4DecWeights wq, DenseGemmArgs a) {
+    tc_gemm_q4_dec_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_q,
+                          const __grid_constant__ CUtensorMap tmap_s, DenseGemmArgs a) {
   constexpr int B_BYTES = QdCfg<BT>::B_BYTES;
+  constexpr int QD_RAW = QdCfg<BT>::RAW;
   constexpr int TMEM_COLS = BT < 32 ? 32 : BT;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -106,12 +103,8 @@ __global__ void __launch_bounds__(QD_THREADS, 2)
         if (i >= QD_RAW && !mbar_wait(&raw_empty[r], ((i / QD_RAW) & 1) ^ 1, a.status, &s_abort)) break;
         mbar_expect_tx(&raw_full[r], QD_RAW_BYTES);
         uint8_t* dst = sR + r * QD_RAW_BYTES;
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-          const int64_t tk = (int64_t)(tile * 8 + t) * KB + kb0 + i;
-          bulk_load(dst + t * 512, wq.qw + tk * 512, 512, &raw_full[r]);
-          bulk_load(dst + 8 * 512 + t * 128, wq.sm + tk * 128, 128, &raw_full[r]);
-        }
+        tma_load_4d(dst, &tmap_q, 0, kb0 + i, tile * 8, 0, &raw_full[r]);
+        tma_load_4d(dst + 8 * 512, &tmap_s, 0, kb0 + i, tile * 8, 0, &raw_full[r]);
       }
     }
   } else if (warp == 1) {
@@ -258,7 +251,8 @@ __global__ void __launch_bounds__(QD_THREADS, 2)
 }
 
 template <int BT, int MODE>
-cudaError_t launch_qd(const CUtensorMap& mx, const Q4DecWeights& wq, const DenseGemmArgs& a, cudaStream_t s) {
+cudaError_t launch_qd(const CUtensorMap& mx, const CUtensorMap& mq, const CUtensorMap& ms, const DenseGemmArgs& a,
+                      cudaStream_t s) {
   static bool set = false;
   constexpr size_t smem = QdCfg<BT>::SMEM;
   auto* kern = tc_gemm_q4_dec_kernel<BT, MODE>;
@@ -269,7 +263,7 @@ cudaError_t launch_qd(const CUtensorMap& mx, const Q4DecWeights& wq, const Dense
   }
   const dim3 grid((unsigned)(a.N / 128), (unsigned)a.splits);
   if (a.splits == 1) {
-    kern<<<grid, QD_THREADS, smem, s>>>(mx, wq, a);
+    kern<<<grid, QD_THREADS, smem, s>>>(mx, mq, ms, a);
     return cudaGetLastError();
   }
   cudaLaunchConfig_t cfg = {};
@@ -284,17 +278,18 @@ cudaError_t launch_qd(const CUtensorMap& mx, const Q4DecWeights& wq, const Dense
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, mx, wq, a);
+  return cudaLaunchKernelEx(&cfg, kern, mx, mq, ms, a);
 }
 
 template <int BT>
-cudaError_t launch_qd_mode(const CUtensorMap& mx, const Q4DecWeights& wq, const DenseGemmArgs& a, cudaStream_t s) {
+cudaError_t launch_qd_mode(const CUtensorMap& mx, const CUtensorMap& mq, const CUtensorMap& ms,
+                           const DenseGemmArgs& a, cudaStream_t s) {
   switch (a.mode) {
-    case 0: return launch_qd<BT, 0>(mx, wq, a, s);
-    case 1: return launch_qd<BT, 1>(mx, wq, a, s);
-    case 3: return launch_qd<BT, 3>(mx, wq, a, s);
-    case 5: return launch_qd<BT, 5>(mx, wq, a, s);
-    case 6: return launch_qd<BT, 6>(mx, wq, a, s);
+    case 0: return launch_qd<BT, 0>(mx, mq, ms, a, s);
+    case 1: return launch_qd<BT, 1>(mx, mq, ms, a, s);
+    case 3: return launch_qd<BT, 3>(mx, mq, ms, a, s);
+    case 5: return launch_qd<BT, 5>(mx, mq, ms, a, s);
+    case 6: return launch_qd<BT, 6>(mx, mq, ms, a, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -353,8 +348,9 @@ cudaError_t launch_tc_gemm_q4_dec(const void* x, int T, int ldx, const void* qw,
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
-  const Q4DecWeights wq{reinterpret_cast<const uint8_t*>(qw), reinterpret_cast<const uint8_t*>(sm)};
-  return bt == 32 ? launch_qd_mode<32>(mx, wq, a, s) : launch_qd_mode<64>(mx, wq, a, s);
+  CUtensorMap mq, ms;  // the matrix as a one-entry bank: one box = the eight tiles of a 128-row tile
+  if (!encode_q4_raw_maps(enc, &mq, &ms, qw, sm, 1, N, K, 128)) return cudaErrorInvalidValue;
+  return bt == 32 ? launch_qd_mode<32>(mx, mq, ms, a, s) : launch_qd_mode<64>(mx, mq, ms, a, s);
 }
 
 }  // namespace syn

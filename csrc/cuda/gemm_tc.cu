@@ -324,27 +324,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
 }
 
 // ---- host side ----
-// 4-D tensor maps over a contiguous bank of packed 4-bit matrices [entries][N/16][K/64]:
-// nibbles 512 B and scale/min 128 B per (16-row tile, 64-column block); one box = BN/16 tiles.
-static bool encode_raw_maps(PFN_encodeTiled enc, CUtensorMap* mq, CUtensorMap* ms, const void* bank_qw,
-                            const void* bank_sm, int entries, int N, int K, int BN) {
-  const cuuint64_t KG = (cuuint64_t)(K / 64), NT = (cuuint64_t)(N / 16);
-  const cuuint32_t estr[4] = {1, 1, 1, 1};
-  const cuuint64_t dq[4] = {128, KG, NT, (cuuint64_t)entries};  // [entry][tile][kg][128 x u32]
-  const cuuint64_t sq[3] = {512, 512 * KG, 512 * KG * NT};
-  const cuuint32_t bq[4] = {128, 1, (cuuint32_t)(BN / 16), 1};
-  if (enc(mq, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, const_cast<void*>(bank_qw), dq, sq, bq, estr,
-          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-    return false;
-  const cuuint64_t ds[4] = {32, KG, NT, (cuuint64_t)entries};    // [entry][tile][kg][32 x u32]
-  const cuuint64_t ss[3] = {128, 128 * KG, 128 * KG * NT};
-  const cuuint32_t bs[4] = {32, 1, (cuuint32_t)(BN / 16), 1};
-  return enc(ms, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, const_cast<void*>(bank_sm), ds, ss, bs, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 // bank_qw/bank_sm: base of a contiguous expert bank (or of one matrix) and the number
 // of experts in it; when given (non-null), the packed weights stream with two 4-D TMA copies
 // per stage instead of 2 * BN/16 bulk copies.  bank2_* and grp_sel: a second bank (e.g. the
@@ -382,8 +361,8 @@ cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, co
   memset(&mq2, 0, sizeof(mq2));
   memset(&ms2, 0, sizeof(ms2));
   if (raw_tma) {
-    if (!encode_raw_maps(enc, &mq, &ms, bank_qw, bank_sm, bank_experts, N, K, BN)) return cudaErrorInvalidValue;
-    if (bank2_qw != nullptr && !encode_raw_maps(enc, &mq2, &ms2, bank2_qw, bank2_sm, bank2_experts, N, K, BN))
+    if (!encode_q4_raw_maps(enc, &mq, &ms, bank_qw, bank_sm, bank_experts, N, K, BN)) return cudaErrorInvalidValue;
+    if (bank2_qw != nullptr && !encode_q4_raw_maps(enc, &mq2, &ms2, bank2_qw, bank2_sm, bank2_experts, N, K, BN))
       return cudaErrorInvalidValue;
   }
   TcGemmArgs a{raw_tma, qw_ptrs, sm_ptrs, row_off, route_w, out, group_base, G, M, N, K, mode, status,
