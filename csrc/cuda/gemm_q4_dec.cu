@@ -18,6 +18,8 @@
 //               epilogue of their TMEM lane quarter (shared with the bf16 GEMM: bf16 store,
 //               SwiGLU, f32 add / store, tensor-parallel peer push with completion flags).
 // Every wait is bounded (bit 4 of *status, never a hang).
+#include <cstdlib>
+
 #include "tc_emit.cuh"
 
 namespace syn {
@@ -30,20 +32,20 @@ constexpr int QD_STAGES = 3;
 constexpr int QD_A_BYTES = 128 * 128;           // 128 rows x 64 bf16
 constexpr int QD_RAW_BYTES = 8 * (512 + 128);   // eight 16-row packed tiles
 
-template <int BT>
+template <int BT, int RAW_ = (BT <= 32 ? 8 : 6)>
 struct QdCfg {
   static constexpr int B_BYTES = BT * 128;
-  static constexpr int RAW = BT <= 32 ? 8 : 6;  // packed-weight stages in flight (HBM latency)
+  static constexpr int RAW = RAW_;  // packed-weight stages in flight (HBM latency)
   static constexpr size_t SMEM = 1024 + (size_t)QD_STAGES * (QD_A_BYTES + B_BYTES) + (size_t)RAW * QD_RAW_BYTES;
   static_assert(SMEM <= 113 * 1024, "two CTAs per SM");
 };
 
-template <int BT, int MODE>
+template <int BT, int MODE, int RAWS>
 __global__ void __launch_bounds__(QD_THREADS, 2)
     tc_gemm_q4_dec_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_q,
                           const __grid_constant__ CUtensorMap tmap_s, DenseGemmArgs a) {
-  constexpr int B_BYTES = QdCfg<BT>::B_BYTES;
-  constexpr int QD_RAW = QdCfg<BT>::RAW;
+  constexpr int B_BYTES = QdCfg<BT, RAWS>::B_BYTES;
+  constexpr int QD_RAW = QdCfg<BT, RAWS>::RAW;
   constexpr int TMEM_COLS = BT < 32 ? 32 : BT;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -138,7 +140,6 @@ __global__ void __launch_bounds__(QD_THREADS, 2)
       const uint8_t* sb = R + 8 * 512 + rt * 128;
       const uint2 slo = *reinterpret_cast<const uint2*>(sb + g * 8);
       const uint2 shi = *reinterpret_cast<const uint2*>(sb + (g + 8) * 8);
-      mbar_arrive(&raw_empty[rr]);
       if (i >= QD_STAGES && !mbar_wait(&empty[s], ((i / QD_STAGES) & 1) ^ 1, a.status, &s_abort)) break;
       uint8_t* A = sA + s * QD_A_BYTES;
       const uint32_t words[4] = {q.x, q.y, q.z, q.w};
@@ -165,7 +166,11 @@ __global__ void __launch_bounds__(QD_THREADS, 2)
           }
         }
       }
+      // the packed stage is released only now: its values were consumed by the stores above,
+      // and the proxy fence orders these generic-proxy reads (and the stores) before the TMA
+      // refill of the stage and the MMA reads of the tile (async proxy)
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      mbar_arrive(&raw_empty[rr]);
       mbar_arrive(&full_a[s]);
     }
     // ---------------- epilogue (warps 4..7: one TMEM lane quarter each) ----------------
@@ -250,12 +255,12 @@ __global__ void __launch_bounds__(QD_THREADS, 2)
   }
 }
 
-template <int BT, int MODE>
+template <int BT, int MODE, int RAWS>
 cudaError_t launch_qd(const CUtensorMap& mx, const CUtensorMap& mq, const CUtensorMap& ms, const DenseGemmArgs& a,
                       cudaStream_t s) {
   static bool set = false;
-  constexpr size_t smem = QdCfg<BT>::SMEM;
-  auto* kern = tc_gemm_q4_dec_kernel<BT, MODE>;
+  constexpr size_t smem = QdCfg<BT, RAWS>::SMEM;
+  auto* kern = tc_gemm_q4_dec_kernel<BT, MODE, RAWS>;
   if (!set) {
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -284,12 +289,16 @@ cudaError_t launch_qd(const CUtensorMap& mx, const CUtensorMap& mq, const CUtens
 template <int BT>
 cudaError_t launch_qd_mode(const CUtensorMap& mx, const CUtensorMap& mq, const CUtensorMap& ms,
                            const DenseGemmArgs& a, cudaStream_t s) {
+  // SYN_Q4_DEC_RAW=4: four packed-weight stages (fault isolation / measurement)
+  static const bool raw4 = getenv("SYN_Q4_DEC_RAW") && atoi(getenv("SYN_Q4_DEC_RAW")) == 4;
+  if (raw4 && a.mode == 5) return launch_qd<BT, 5, 4>(mx, mq, ms, a, s);
+  constexpr int R = QdCfg<BT>::RAW;
   switch (a.mode) {
-    case 0: return launch_qd<BT, 0>(mx, mq, ms, a, s);
-    case 1: return launch_qd<BT, 1>(mx, mq, ms, a, s);
-    case 3: return launch_qd<BT, 3>(mx, mq, ms, a, s);
-    case 5: return launch_qd<BT, 5>(mx, mq, ms, a, s);
-    case 6: return launch_qd<BT, 6>(mx, mq, ms, a, s);
+    case 0: return launch_qd<BT, 0, R>(mx, mq, ms, a, s);
+    case 1: return launch_qd<BT, 1, R>(mx, mq, ms, a, s);
+    case 3: return launch_qd<BT, 3, R>(mx, mq, ms, a, s);
+    case 5: return launch_qd<BT, 5, R>(mx, mq, ms, a, s);
+    case 6: return launch_qd<BT, 6, R>(mx, mq, ms, a, s);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -322,6 +331,10 @@ cudaError_t launch_tc_gemm_q4_dec(const void* x, int T, int ldx, const void* qw,
   a.ldo = ldo;
   a.status = status;
   a.splits = q4_dec_splits(N, K);
+  if (const char* e = getenv("SYN_Q4_DEC_SPLITS")) {  // forced K slices (fault isolation / measurement)
+    const int f = atoi(e);
+    if (f == 1 || f == 2 || f == 4 || f == 8) a.splits = f;
+  }
   if (pp) {
     a.peers = pp->peers;
     a.n_peers = pp->n_peers;

@@ -228,7 +228,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
         slo[i] = *reinterpret_cast<const uint2*>(sb + g * 8);
         shi[i] = *reinterpret_cast<const uint2*>(sb + (g + 8) * 8);
       }
-      mbar_arrive(&raw_empty[rr]);
       if (kb >= TC_STAGES && !mbar_wait(&empty[s], ph ^ 1, a.status, &s_abort)) break;
       uint8_t* B = sB + s * B_BYTES;
       // Dequantise: value = bf16(fma(d, q, m)) in f32 (one rounding, the reference's
@@ -265,7 +264,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
           }
         }
       }
+      // the packed stage is released only now: its values were consumed by the stores above,
+      // and the proxy fence orders these generic-proxy reads (and the stores) before the TMA
+      // refill of the stage and the MMA reads of the tile (async proxy)
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      mbar_arrive(&raw_empty[rr]);
       mbar_arrive(&full_b[s]);
     }
     // ---------------- epilogue ----------------

@@ -655,6 +655,8 @@ __global__ void __launch_bounds__(128) q4_gemv4_kernel(GemvArgs a) {
             }
           }
         }
+        // the stage's generic-proxy reads are ordered before its refill by the bulk copy
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         __syncwarp();
         issue(c + C::STAGES);
       }

@@ -190,16 +190,19 @@ def main():
                    extra={"status": int(st.item())})
             wd = w.dequant()
             report(f"cublas_bf16_{M}x{N}x{K}(reference)", timeit(lambda: x @ wd.t(), iters=10), flops=2 * M * N * K)
-    if want("q4_dec"):
+    if want("q4_dec") or "q4_dec_small" in only:
         # 4-bit weights at 16-64 decode rows (Llama-3-70B layer shapes, one GPU and one TP8 rank):
         # the tcgen05 decode GEMM against the mma.sync GEMV on the same inputs; weights in
         # rotated copies larger than L2
         from syntropy_b200.ops import core as _core
-        for N, K in ((10240, 8192), (8192, 8192), (57344, 8192), (8192, 28672), (1280, 8192), (7168, 8192),
-                     (8192, 3584)):
+        # q4_dec_small: one shape at 32 rows (a profiler-sized case)
+        small = "q4_dec_small" in only
+        shapes = ((8192, 8192),) if small else ((10240, 8192), (8192, 8192), (57344, 8192), (8192, 28672),
+                                                (1280, 8192), (7168, 8192), (8192, 3584))
+        for N, K in shapes:
             ncopy = max(1, int(2 * 126e6 // (N * K // 2)) + 1)
             ws = [Q4Weight.quantize(torch.randn(N, K, device=dev) * 0.02) for _ in range(min(ncopy, 64))]
-            for rows in (16, 32, 64):
+            for rows in ((32,) if small else (16, 32, 64)):
                 x = torch.randn(rows, K, device=dev).to(torch.bfloat16)
                 out = torch.empty(rows, N, dtype=torch.float32, device=dev)
                 it = [0]

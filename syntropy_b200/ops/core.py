@@ -122,9 +122,10 @@ def _linear_fp8(x, W, out, mode):
     return out
 
 
-# SYN_Q4_TC_MIN: fewest token rows for which 4-bit decode products run on tcgen05 (default 16;
-# a value above 64 keeps every decode product on the mma.sync GEMV)
-_Q4_TC = [int(__import__("os").environ.get("SYN_Q4_TC_MIN", "16"))]
+# SYN_Q4_TC_MIN: fewest token rows for which 4-bit decode products run on tcgen05 (default 32,
+# measured: at 16 rows the mma.sync GEMV is still faster, from 32 rows the tcgen05 GEMM; a value
+# above 64 keeps every decode product on the GEMV)
+_Q4_TC = [int(__import__("os").environ.get("SYN_Q4_TC_MIN", "32"))]
 
 
 def linear(x: torch.Tensor, W, out: torch.Tensor, mode: int = GEMV_STORE, res: torch.Tensor | None = None):

@@ -1,8 +1,8 @@
 """Tensor-parallel fused paths on 2 GPUs, kernel by kernel, against f32 PyTorch references.
 
 * Row-parallel product + one-shot all-reduce: each rank's partial x_r @ W_r^T leaves the GEMV
-  (4-bit weights) or the tcgen05 GEMM (bf16 weights) epilogue straight into every peer's
-  receive slot over NVLink; tp_reduce_norm sums the partials in rank order, adds the residual
+  (4-bit weights, 24 rows), the tcgen05 4-bit decode GEMM (40 rows) or the tcgen05 bf16 GEMM
+  epilogue straight into every peer's receive slot over NVLink; tp_reduce_norm sums the partials in rank order, adds the residual
   and applies the next RMSNorm.  Checked against x + sum_r x_r @ W_r^T in f32, and the
   residuals of both ranks must be bitwise equal (member-order reduction).
 * Vocab-parallel head: each rank's bf16 head GEMM writes its column slice into both ranks'
@@ -32,8 +32,8 @@ from syntropy_b200.parallel.tp import TPGroup
 
 ctx = init_distributed(timeout_s=60)
 dev = ctx.device
-T, H, K, V = 24, 1024, 512, 4096
-tp = TPGroup(ctx, H, cap=32, n_layers=2, fused=True, vocab=V)
+T, H, K, V = 40, 1024, 512, 4096
+tp = TPGroup(ctx, H, cap=48, n_layers=3, fused=True, vocab=V)
 res = {"rank": ctx.rank}
 g = torch.Generator().manual_seed(50 + ctx.rank)
 x_in = (torch.randn(T, K, generator=g) * 0.5).to(torch.bfloat16)
@@ -43,18 +43,21 @@ g0 = torch.Generator().manual_seed(7)  # the residual and norm are the same on b
 x0 = torch.randn(T, H, generator=g0)
 nw = torch.rand(H, generator=g0) + 0.5
 eps = 1e-5
-parts = {"bf16": (x_in.float() @ w_bf.float().t()), "q4": (x_in.float() @ w_q4.dequant().float().cpu().t())}
-for layer, (kind, W) in enumerate((("bf16", w_bf.to(dev)), ("q4", w_q4))):
+q4_ref = x_in.float() @ w_q4.dequant().float().cpu().t()
+parts = {"bf16": (x_in.float() @ w_bf.float().t()), "q4": q4_ref, "q4_gemv": q4_ref[:24]}
+# 40 rows of 4-bit weights run the tcgen05 decode GEMM's push, 24 rows the GEMV's push
+for layer, (kind, W) in enumerate((("bf16", w_bf.to(dev)), ("q4", w_q4), ("q4_gemv", w_q4))):
+    rows = 24 if kind == "q4_gemv" else T
     tp.step_begin()
-    x = x0.clone().to(dev)
-    h = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
-    tp.row_parallel_reduce(0, layer, x_in.to(dev), W, x, nw.to(dev), h, eps)
+    x = x0[:rows].clone().to(dev)
+    h = torch.empty(rows, H, dtype=torch.bfloat16, device=dev)
+    tp.row_parallel_reduce(0, layer, x_in[:rows].to(dev), W, x, nw.to(dev), h, eps)
     torch.cuda.synchronize()
     allp = [None] * ctx.world
     dist.all_gather_object(allp, parts[kind], group=ctx.cpu_group)
-    ref = x0.double() + sum(p.double() for p in allp)
+    ref = x0[:rows].double() + sum(p.double() for p in allp)
     got = x.cpu()
-    res[kind + "_rel"] = ((got.double() - ref).norm() / (ref - x0.double()).norm()).item()
+    res[kind + "_rel"] = ((got.double() - ref).norm() / (ref - x0[:rows].double()).norm()).item()
     href = (ref * torch.rsqrt(ref.pow(2).mean(-1, keepdim=True) + eps) * nw.double()).float()
     res[kind + "_h_rel"] = ((h.float().cpu() - href).norm() / href.norm()).item()
     allx = [None] * ctx.world
@@ -103,8 +106,8 @@ def test_tp_fused_paths_match_f32_reference():
         # bf16 operands with f32 accumulation: near f32; the 4-bit GEMV rounds each dequantised
         # weight to bf16 for the tensor-core product (relative error about 2^-9)
         assert d["bf16_rel"] < 1e-4, d
-        assert d["q4_rel"] < 5e-3, d
-        for kind in ("bf16", "q4"):
+        assert d["q4_rel"] < 5e-3 and d["q4_gemv_rel"] < 5e-3, d
+        for kind in ("bf16", "q4", "q4_gemv"):
             assert d[kind + "_h_rel"] < 1e-2, d
             assert d[kind + "_bitwise_equal"], d    # rank-order reduction: identical residuals
         assert d["logits_rel"] < 1e-4, d
