@@ -32,11 +32,23 @@ __device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: the waiting warp sleeps until the phase completes (or
+// the hint, 64 us, runs out) instead of spinning, so waiting warps leave the issue slots to
+// the warps that work.
+__device__ __forceinline__ bool mbar_test_sleep(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity), "r"(65536u)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait on an mbarrier phase; false (with an error bit) after TC_WAIT_NS.
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int* status, volatile int* abort) {
   if (mbar_test(b, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  while (!mbar_test(b, parity)) {
+  while (!mbar_test_sleep(b, parity)) {
     if (*abort) return false;
     if (globaltimer_ns() - t0 > TC_WAIT_NS) {
       *abort = 1;
