@@ -7,21 +7,22 @@
 // chunked prefill after a cached prefix).  Reference op: `AttnPrefill(Gqa)`
 // (crates/kernels/src/op/kind.rs; f32 reference crates/kernels/src/reference/attention.rs).
 //
-// One CTA = 128 query rows of one head, 192 threads:
-//   warp 0      TMA producer: Q once (two 64-column halves), then per 128-key tile the K and V
-//               pages (16 keys x 64 columns per box, 16 boxes each) into a 2-stage ring;
-//   warp 1      TMEM owner and MMA issuer (one elected lane): S_{j+1} is issued before P_j V_j so
-//               the tensor core computes the next scores while the softmax warps work;
-//               O += P_j V_j accumulates in TMEM across the key tiles;
-//   warps 2..5  softmax: thread = query row = TMEM lane.  One read of the S_j row (128 columns)
-//               gives its max; P_j = 2^(S_j * scale - m) goes in bf16 to one of two shared-memory
-//               P buffers in the SWIZZLE_128B K-major layout the next MMA reads.  The running
-//               max m is raised lazily: only when a row's new max exceeds it by more than 2^8
-//               (P stays below 256, exact in f32 sums) are O (in TMEM) and the row sum rescaled,
-//               after the previous P V has finished.
-// TMEM: S double buffer (2 x 128 columns) + O (128 columns).  V is the MN-major B operand of
-// P V (its rows are keys, 64 head-dim columns per 128-byte row).  Every mbarrier wait is
-// bounded: a wait that runs out sets bit 4 of *status and every role leaves its loop.
+// One CTA = 256 query rows of one head (query tiles A and B of 128 rows), 320 threads:
+//   warp 0      TMA producer: both Q tiles once (two 64-column halves each), then per 128-key
+//               tile the K and V pages (16 keys x 64 columns per box, 16 boxes each) into a
+//               2-stage ring;
+//   warp 1      TMEM owner and MMA issuer (one elected lane), ping-pong over the two tiles: per
+//               key tile j it issues P_A V, S_A(j+1), P_B V, S_B(j+1), so the tensor core works on
+//               one tile while the softmax warps of the other run; O_A and O_B accumulate in TMEM;
+//   warps 2..5  softmax of tile A, warps 6..9 of tile B (thread = query row = TMEM lane): one
+//               read of the S row (its S columns are released at once), causal / length mask,
+//               row max, P = 2^(S * scale - m) in bf16 into the shared P buffer (SWIZZLE_128B
+//               K-major, as the next MMA reads it; the tiles take it in turn).  The running max
+//               is raised lazily: only when a row's new max exceeds it by more than 2^8 is its
+//               O (in TMEM) rescaled, after that tile's previous P V.
+// TMEM: S_A, S_B, O_A, O_B (128 columns each).  V is the MN-major B operand of P V (its rows are
+// keys, 64 head-dim columns per 128-byte row).  Every mbarrier wait is bounded: a wait that
+// runs out sets bit 4 of *status and every role leaves its loop.
 #include <cuda.h>
 
 #include "common.cuh"
@@ -37,8 +38,8 @@ constexpr int AT_BM = 128;                   // query rows per CTA (TMEM lanes)
 constexpr int AT_BN = 128;                   // keys per tile
 constexpr int AT_HALF = 128 * 128;           // one 64-column half of a 128-row tile: 16 KB
 constexpr int AT_TILE = 2 * AT_HALF;         // 32 KB
-constexpr int AT_SMEM = 7 * AT_TILE + 1024;  // Q, K[2], V[2], P[2] + alignment slack
-constexpr int AT_THREADS = 192;
+constexpr int AT_SMEM = 7 * AT_TILE + 1024;  // Q[2 tiles], K[2], V[2], P + alignment slack
+constexpr int AT_THREADS = 320;
 
 struct AttnTcArgs {
   const int32_t* block_tables;  // [nseq, max_blocks]
@@ -107,12 +108,12 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
                            const __grid_constant__ CUtensorMap tm_v, AttnTcArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + AT_TILE;        // [2 stages]
+  uint8_t* sQ = smem;                // [2 query tiles]
+  uint8_t* sK = sQ + 2 * AT_TILE;    // [2 stages]
   uint8_t* sV = sK + 2 * AT_TILE;    // [2 stages]
-  uint8_t* sP = sV + 2 * AT_TILE;    // [2 buffers]
-  __shared__ __align__(8) uint64_t q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], s_empty[2], p_full[2],
-      p_empty[2], o_done;
+  uint8_t* sP = sV + 2 * AT_TILE;    // one P buffer, used by the two query tiles in turn
+  __shared__ __align__(8) uint64_t q_full, k_full[2], v_full[2], kv_empty[2], s_full[2], s_free[2], p_full[2],
+      pv_done[2], p_free, o_done;
   __shared__ uint32_t tmem_base;
   __shared__ volatile int s_abort;
 
@@ -120,13 +121,19 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   const int s = blockIdx.z, h = blockIdx.y;
   const int qt = a.n_qtiles - 1 - (int)blockIdx.x;  // longest (latest) tiles first
   const int q0 = a.cu_q[s], q_len = a.cu_q[s + 1] - q0;
-  const int i0 = qt * AT_BM;
+  const int i0 = qt * 2 * AT_BM;                      // 256 query rows per CTA: tiles A and B
   if (i0 >= q_len) return;  // uniform over the CTA, before any barrier or TMEM use
   const int kv_len = a.kv_lens[s];
   const int pos0 = kv_len - q_len;
   const int hk = h / (a.Hq / a.Hkv);
-  const int p_last = pos0 + min(i0 + AT_BM, q_len) - 1;
-  const int n_tiles = p_last / AT_BN + 1;
+  // key tiles each query tile needs (0 for a tile past the sequence's rows)
+  int n_t[2];
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    const int r0 = i0 + g * AT_BM;
+    n_t[g] = r0 < q_len ? (pos0 + min(r0 + AT_BM, q_len) - 1) / AT_BN + 1 : 0;
+  }
+  const int n_max = max(n_t[0], n_t[1]);
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -136,10 +143,11 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&kv_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
+      mbar_init(&s_free[i], 128);
       mbar_init(&p_full[i], 128);
-      mbar_init(&p_empty[i], 1);
+      mbar_init(&pv_done[i], 1);
     }
+    mbar_init(&p_free, 1);
     mbar_init(&o_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
@@ -152,17 +160,20 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
   const uint32_t tmem = tmem_base;
-  const uint32_t t_s0 = tmem, t_o = tmem + 256;  // S buffers at columns 0 / 128, O at 256
+  // TMEM: S of tile g at columns 128 g, O of tile g at 256 + 128 g
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       const int32_t* bt = a.block_tables + (int64_t)s * a.max_blocks;
       const int n_pages = (kv_len + 15) >> 4;
-      mbar_expect_tx(&q_full, AT_TILE);
-      tma_load_3d(sQ, &tm_q, 0, h, q0 + i0, &q_full);
-      tma_load_3d(sQ + AT_HALF, &tm_q, 64, h, q0 + i0, &q_full);
-      for (int j = 0; j < n_tiles; ++j) {
+      mbar_expect_tx(&q_full, 2 * AT_TILE);
+#pragma unroll
+      for (int g = 0; g < 2; ++g) {  // rows past the tensor read zeros; rows of the next sequence are masked out
+        tma_load_3d(sQ + g * AT_TILE, &tm_q, 0, h, q0 + i0 + g * AT_BM, &q_full);
+        tma_load_3d(sQ + g * AT_TILE + AT_HALF, &tm_q, 64, h, q0 + i0 + g * AT_BM, &q_full);
+      }
+      for (int j = 0; j < n_max; ++j) {
         const int st = j & 1;
         if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1, a.status, &s_abort)) break;
         int blk[8];
@@ -183,66 +194,84 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+    // ---------------- MMA issuer: S_A(j+1), P_B V and S_B(j+1) overlap the softmax of the other tile ----
     if (lane == 0) {
       constexpr uint32_t id_s = at_idesc(false), id_o = at_idesc(true);
-      const uint32_t uq = smem_u32(sQ);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(&k_full[st], (j >> 1) & 1, a.status, &s_abort)) return false;
-        if (j >= 2 && !mbar_wait(&s_empty[st], ((j >> 1) - 1) & 1, a.status, &s_abort)) return false;
+      const uint32_t up = smem_u32(sP);
+      auto issue_s = [&](int g, int j) -> bool {  // S_g(j) into tile g's S columns
+        if (j >= 1 && !mbar_wait(&s_free[g], (j - 1) & 1, a.status, &s_abort)) return false;
+        if (!mbar_wait(&k_full[j & 1], (j >> 1) & 1, a.status, &s_abort)) return false;
         asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-        const uint32_t uk = smem_u32(sK + st * AT_TILE);
+        const uint32_t uq = smem_u32(sQ + g * AT_TILE), uk = smem_u32(sK + (j & 1) * AT_TILE);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * AT_HALF + (kk & 3) * 32;
-          umma_bf16(t_s0 + st * 128, sw128_desc(uq + off), sw128_desc(uk + off), id_s, kk != 0);
+          umma_bf16(tmem + g * 128, sw128_desc(uq + off), sw128_desc(uk + off), id_s, kk != 0);
         }
-        umma_commit(&s_full[st]);
+        umma_commit(&s_full[g]);
         return true;
       };
-      bool ok = mbar_wait(&q_full, 0, a.status, &s_abort) && issue_s(0);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        const int st = j & 1;
-        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-        if (!mbar_wait(&p_full[st], (j >> 1) & 1, a.status, &s_abort)) break;
-        if (!mbar_wait(&v_full[st], (j >> 1) & 1, a.status, &s_abort)) break;
+      auto issue_pv = [&](int g, int j) -> bool {  // O_g += P_g(j) V_j
+        if (!mbar_wait(&p_full[g], j & 1, a.status, &s_abort)) return false;
+        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, a.status, &s_abort)) return false;
         asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-        const uint32_t uv = smem_u32(sV + st * AT_TILE), up = smem_u32(sP + st * AT_TILE);
+        const uint32_t uv = smem_u32(sV + (j & 1) * AT_TILE);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          // A = P: K-major, 16 keys per step; B = V: MN-major, 16 key rows (2 KB) per step
           const uint32_t aoff = (kk >> 2) * AT_HALF + (kk & 3) * 32;
-          umma_bf16(t_o, sw128_desc(up + aoff), sw128_mn_desc(uv + kk * 2048, AT_HALF), id_o, (j | kk) != 0);
+          umma_bf16(tmem + 256 + g * 128, sw128_desc(up + aoff), sw128_mn_desc(uv + kk * 2048, AT_HALF), id_o,
+                    (j | kk) != 0);
         }
-        umma_commit(&p_empty[st]);
-        umma_commit(&kv_empty[st]);
+        umma_commit(&pv_done[g]);
+        return true;
+      };
+      bool ok = mbar_wait(&q_full, 0, a.status, &s_abort);
+      for (int g = 0; ok && g < 2; ++g)
+        if (n_t[g] > 0) ok = issue_s(g, 0);
+      for (int j = 0; ok && j < n_max; ++j) {
+        // the P buffer serves A(j), B(j), A(j+1), ...: one p_free phase per slot (an empty
+        // commit for a tile that has no key tile j), so each softmax waits a fixed parity
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          if (!ok) break;
+          if (j < n_t[g]) {
+            ok = issue_pv(g, j);
+            if (ok && j + 1 < n_t[g]) ok = issue_s(g, j + 1);
+          }
+          umma_commit(&p_free);
+        }
+        umma_commit(&kv_empty[j & 1]);
       }
       umma_commit(&o_done);
     }
-  } else {
-    // ---------------- softmax warps ----------------
+  } else if (warp >= 2 && warp < 10) {
+    // ---------------- softmax: warps 2..5 query tile A, 6..9 tile B ----------------
+    const int g = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;                 // query row in the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const int prow = pos0 + i0 + r;                    // absolute position of this query
-    const int pmin = pos0 + i0;                        // first query position of the tile
+    const int row0 = i0 + g * AT_BM;
+    const int prow = pos0 + row0 + r;                  // absolute position of this query
+    const int pmin = pos0 + row0;                      // first query position of the tile
     const float sl2 = a.scale_log2;
-    float m_used = -INFINITY, l_run = 0.f;             // m_used: the max the exponentials subtract
+    const uint32_t t_s = tmem + g * 128 + lane_off, t_o = tmem + 256 + g * 128 + lane_off;
+    const int nt = n_t[g];
+    float m_used = -INFINITY, l_run = 0.f;  // m_used: the max the exponentials subtract
     bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int st = j & 1;
+    for (int j = 0; j < nt; ++j) {
       // tcgen05.ld / st are warp-collective: every branch around them is decided warp-uniformly
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[st], (j >> 1) & 1, a.status, &s_abort))) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[g], j & 1, a.status, &s_abort))) {
         ok = false;
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-      const uint32_t ts = t_s0 + st * 128 + lane_off;
       uint32_t u[AT_BN];
 #pragma unroll
-      for (int c0 = 0; c0 < AT_BN; c0 += 32) tmem_ld32_async(ts + c0, u + c0);
+      for (int c0 = 0; c0 < AT_BN; c0 += 32) tmem_ld32_async(t_s + c0, u + c0);
       tmem_wait_ld();
+      // the S columns are free for S_g(j+1) as soon as the row is in registers
+      asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+      mbar_arrive(&s_free[g]);
       const int key0 = j * AT_BN;
       if (key0 + AT_BN - 1 > pmin || key0 + AT_BN > kv_len) {  // causal / length mask
 #pragma unroll
@@ -257,38 +286,36 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       mx *= sl2;
       const bool raise = mx > m_used + 8.f;  // always on the first tile (m_used = -inf)
       const float m_new = raise ? mx : m_used;
-      if (__any_sync(0xffffffffu, raise)) {
-        if (j > 0) {
-          // O holds tiles 0..j-1: wait for the last P V (P buffer of tile j-1), then rescale
-          // (alpha = 1 on the lanes that keep their max)
-          if (!__all_sync(0xffffffffu,
-                          mbar_wait(&p_empty[(j - 1) & 1], ((j - 1) >> 1) & 1, a.status, &s_abort))) {
-            ok = false;
-            break;
-          }
-          asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-          const float alpha = exp2f(m_used - m_new);
-#pragma unroll 1
-          for (int c0 = 0; c0 < AT_D; c0 += 32) {
-            uint32_t o[32];
-            tmem_ld32_async(t_o + lane_off + c0, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(t_o + lane_off + c0, o);
-          }
-          asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
-          l_run *= alpha;
+      if (__any_sync(0xffffffffu, raise) && j > 0) {
+        // O holds tiles 0..j-1: wait for P_g(j-1) V, then rescale (alpha = 1 where the max stays)
+        if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[g], (j - 1) & 1, a.status, &s_abort))) {
+          ok = false;
+          break;
         }
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+        const float alpha = exp2f(m_used - m_new);
+#pragma unroll 1
+        for (int c0 = 0; c0 < AT_D; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32_async(t_o + c0, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(t_o + c0, o);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+        l_run *= alpha;
       }
       m_used = m_new;
-      // this P buffer was last read by P_{j-2} V
-      if (j >= 2 && !__all_sync(0xffffffffu, mbar_wait(&p_empty[st], ((j >> 1) - 1) & 1, a.status, &s_abort))) {
+      // the shared P buffer: tile A's slot j follows tile B's slot j-1 (phase 2j-1), tile B's
+      // slot j follows tile A's slot j (phase 2j)
+      if ((g == 1 || j >= 1) &&
+          !__all_sync(0xffffffffu, mbar_wait(&p_free, g == 0 ? 1u : 0u, a.status, &s_abort))) {
         ok = false;
         break;
       }
       float rs = 0.f;
-      uint8_t* pbuf = sP + st * AT_TILE + r * 128;
+      uint8_t* pbuf = sP + r * 128;
 #pragma unroll
       for (int c0 = 0; c0 < AT_BN; c0 += 32) {
         uint32_t pk[16];
@@ -308,21 +335,20 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         }
       }
       l_run += rs;
-      // P visible to the tensor core (async proxy); S buffer and P handed over
+      // P visible to the tensor core (async proxy), then handed over
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
-      mbar_arrive(&s_empty[st]);
-      mbar_arrive(&p_full[st]);
+      mbar_arrive(&p_full[g]);
     }
-    if (ok && __all_sync(0xffffffffu, mbar_wait(&o_done, 0, a.status, &s_abort))) {
+    if (ok && nt > 0 && __all_sync(0xffffffffu, mbar_wait(&o_done, 0, a.status, &s_abort))) {
       asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-      const int i = i0 + r;
+      const int i = row0 + r;
       const float inv = 1.f / l_run;
       uint4* orow = reinterpret_cast<uint4*>(a.out + ((int64_t)(q0 + min(i, q_len - 1)) * a.Hq + h) * AT_D);
 #pragma unroll 1
       for (int c0 = 0; c0 < AT_D; c0 += 32) {
         uint32_t o[32];
-        tmem_ld32_async(t_o + lane_off + c0, o);
+        tmem_ld32_async(t_o + c0, o);
         tmem_wait_ld();
         if (i < q_len) {
 #pragma unroll
@@ -383,7 +409,7 @@ cudaError_t launch_attn_prefill_tc(const void* q, int Tq, const void* kc, const 
     set = true;
   }
   AttnTcArgs a{block_tables, cu_q, kv_lens, reinterpret_cast<__nv_bfloat16*>(out), Hq, Hkv, max_blocks,
-               (max_q_len + AT_BM - 1) / AT_BM, scale * 1.4426950408889634f, status};
+               (max_q_len + 2 * AT_BM - 1) / (2 * AT_BM), scale * 1.4426950408889634f, status};
   dim3 grid((unsigned)a.n_qtiles, (unsigned)Hq, (unsigned)nseq);
   attn_prefill_tc_kernel<<<grid, AT_THREADS, AT_SMEM, s>>>(mq, mk, mv, a);
   return cudaGetLastError();

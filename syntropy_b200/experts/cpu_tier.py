@@ -33,11 +33,13 @@ from .._ext import ext
 # link (bytes of 4-bit weights per second).  Measured on the B200 node: the AVX-512 BF16 pool
 # moves ~4.8 GB/s per worker thread; one GPU stages host rows with bulk DMA at ~45 GB/s while
 # the CPU also streams DRAM (capped Qwen3 decode on one GPU and 14 workers: shares 0.5 / 0.6 /
-# 0.75 gave 57.3 / 65.4 / 55.8 tok/s, so the balance sits near 0.6), and ~41 GB/s per GPU when
-# several GPUs stage at once (capped Qwen3 decode over EP2 with 11 workers per rank: shares
-# 0.68 / 0.5 gave 71.7 / 90.1 tok/s, the staging copies of a 0.5 share finishing in ~0.35 s).
+# 0.75 gave 57.3 / 65.4 / 55.8 tok/s, so the balance sits near 0.6).  With several ranks per
+# node the workers of all ranks contend for DRAM while each GPU stages over its own link; the
+# effective link rate that reproduces the measured balance is ~55 GB/s per GPU (capped Qwen3
+# decode over EP2 with 11 workers per rank: shares 0.68 / 0.56 / 0.5 gave 71.7 / 78.1 / 90.1
+# tok/s).
 CPU_GBS_PER_THREAD = 4.8
-PCIE_GBS_ALONE, PCIE_GBS_SHARED = 45.0, 41.0
+PCIE_GBS_ALONE, PCIE_GBS_SHARED = 45.0, 55.0
 
 
 def rank_cpus(local_rank: int, local_world: int, allowed: list[int] | None = None) -> tuple[list[int], list[int]]:
