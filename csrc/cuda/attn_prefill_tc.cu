@@ -83,6 +83,12 @@ __device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t* r) {
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 2^x in one MUFU operation (ex2.approx.ftz: ~2 ulp, flush-to-zero; P is rounded to bf16)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
@@ -265,11 +271,11 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+      // one read of the S row (four loads, one wait); its S columns are free for S_g(j+1) at once
       uint32_t u[AT_BN];
 #pragma unroll
       for (int c0 = 0; c0 < AT_BN; c0 += 32) tmem_ld32_async(t_s + c0, u + c0);
       tmem_wait_ld();
-      // the S columns are free for S_g(j+1) as soon as the row is in registers
       asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
       mbar_arrive(&s_free[g]);
       const int key0 = j * AT_BN;
@@ -286,26 +292,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
       mx *= sl2;
       const bool raise = mx > m_used + 8.f;  // always on the first tile (m_used = -inf)
       const float m_new = raise ? mx : m_used;
-      if (__any_sync(0xffffffffu, raise) && j > 0) {
-        // O holds tiles 0..j-1: wait for P_g(j-1) V, then rescale (alpha = 1 where the max stays)
-        if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[g], (j - 1) & 1, a.status, &s_abort))) {
-          ok = false;
-          break;
-        }
-        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-        const float alpha = exp2f(m_used - m_new);
-#pragma unroll 1
-        for (int c0 = 0; c0 < AT_D; c0 += 32) {
-          uint32_t o[32];
-          tmem_ld32_async(t_o + c0, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(t_o + c0, o);
-        }
-        asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
-        l_run *= alpha;
-      }
+      const float alpha = ex2_approx(m_used - m_new);  // 1 where the max stays, 0 on the first tile
       m_used = m_new;
       // the shared P buffer: tile A's slot j follows tile B's slot j-1 (phase 2j-1), tile B's
       // slot j follows tile A's slot j (phase 2j)
@@ -321,8 +308,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const float p0 = exp2f(fmaf(__uint_as_float(u[c0 + i]), sl2, -m_used));
-          const float p1 = exp2f(fmaf(__uint_as_float(u[c0 + i + 1]), sl2, -m_used));
+          const float p0 = ex2_approx(fmaf(__uint_as_float(u[c0 + i]), sl2, -m_used));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(u[c0 + i + 1]), sl2, -m_used));
           rs += p0 + p1;
           pk[i >> 1] = pack_bf16x2(p0, p1);
         }
@@ -334,7 +321,26 @@ __global__ void __launch_bounds__(AT_THREADS, 1)
               make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
       }
-      l_run += rs;
+      l_run = l_run * alpha + rs;
+      // a raised max: O (tiles 0..j-1) is rescaled now, with the S row out of the registers,
+      // after P_g(j-1) V has finished and before P_g(j) V is issued
+      if (__any_sync(0xffffffffu, raise) && j > 0) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[g], (j - 1) & 1, a.status, &s_abort))) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+#pragma unroll 1
+        for (int c0 = 0; c0 < AT_D; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32_async(t_o + c0, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(t_o + c0, o);
+        }
+        asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+      }
       // P visible to the tensor core (async proxy), then handed over
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
