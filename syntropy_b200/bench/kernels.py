@@ -218,6 +218,27 @@ def main():
                     report(f"q4_dec_{impl}_{rows}x{N}x{K}", timeit(fn, iters=20, warmup=len(ws) + 2), nbytes=nbytes,
                            flops=2 * rows * N * K)
                 _core._Q4_TC[0] = saved
+    if want("moe_prefill"):
+        # grouped 4-bit GEMMs of one Qwen3-235B MoE layer over a 32768-token prefill pass
+        # (top-8 of 128 experts: ~2048 rows per expert), all experts in one contiguous bank
+        G, rows_per = 128, 2048
+        off = torch.arange(0, (G + 1) * rows_per, rows_per, dtype=torch.int32, device=dev)
+        M = G * rows_per
+        for name, N, K in (("gate_up", 3072, 4096), ("down", 4096, 1536)):
+            wq = [Q4Weight.quantize(torch.randn(N, K, device=dev) * 0.02) for _ in range(4)]
+            qb = torch.stack([wq[e % 4].qw for e in range(G)])
+            sb = torch.stack([wq[e % 4].sm for e in range(G)])
+            qp = torch.tensor([qb[e].data_ptr() for e in range(G)], dtype=torch.int64, device=dev)
+            sp = torch.tensor([sb[e].data_ptr() for e in range(G)], dtype=torch.int64, device=dev)
+            x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+            out = torch.empty(M, N // 2 if name == "gate_up" else N,
+                              dtype=torch.bfloat16 if name == "gate_up" else torch.float32, device=dev)
+            rw = torch.rand(M, device=dev)
+            mode = 1 if name == "gate_up" else 2
+            report(f"moe_prefill_{name}_{G}x{rows_per}x{N}x{K}",
+                   timeit(lambda: ops.gemm_grouped(x, qp, sp, off, N, K, mode, rw, out, G, qb, sb), iters=5),
+                   flops=2 * M * N * K)
+            del qb, sb, x, out
     if want("gemm_bf16"):
         # Llama-3-8B bf16 projections: one GPU and one TP8 rank at decode (64 rows), and a
         # 2048-token prefill; our tcgen05 GEMM against the library GEMM on the same inputs
