@@ -89,20 +89,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
   __shared__ volatile int s_abort;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ntile = blockIdx.y;
+  // grid (n-tiles, m-tiles): consecutive CTAs share an activation tile (read from HBM once
+  // while its n-tiles run together) and the n-tiles of one group's weights stay in L2
+  const int ntile = blockIdx.x;
 
-  // ---- find this CTA's (group, m-tile) ----
-  if (threadIdx.x == 0) {
-    int acc = 0, grp = -1, mt = 0;
-    for (int g = 0; g < a.G; ++g) {
-      const int cnt = a.row_off[g + 1] - a.row_off[g];
-      const int nt = (cnt + TC_MSUB * TC_BM - 1) / (TC_MSUB * TC_BM);
-      if ((int)blockIdx.x < acc + nt) { grp = g; mt = blockIdx.x - acc; break; }
-      acc += nt;
+  // ---- find this CTA's (group, m-tile): warp 0 scans the groups 32 at a time (a prefix sum of
+  // the per-group tile counts over the lanes), so a CTA of a late group does not walk every
+  // earlier group's offsets one dependent load at a time ----
+  if (warp == 0) {
+    int base = 0, grp = -1, mt = 0;
+    for (int g0 = 0; g0 < a.G && grp < 0; g0 += 32) {
+      const int g = g0 + lane;
+      const int nt = g < a.G ? (a.row_off[g + 1] - a.row_off[g] + TC_MSUB * TC_BM - 1) / (TC_MSUB * TC_BM) : 0;
+      int incl = nt;  // inclusive prefix over the lanes
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const int bx = (int)blockIdx.y - base;
+      const unsigned hit = __ballot_sync(0xffffffffu, g < a.G && bx < incl && bx >= incl - nt);
+      if (hit) {
+        const int src = __ffs(hit) - 1;
+        grp = g0 + src;
+        mt = bx - __shfl_sync(0xffffffffu, incl - nt, src);
+      }
+      base += __shfl_sync(0xffffffffu, incl, 31);
     }
-    s_group = grp;
-    s_mtile = mt;
-    s_abort = 0;
+    if (lane == 0) {
+      s_group = grp;
+      s_mtile = mt;
+      s_abort = 0;
+    }
   }
   __syncthreads();
   const int grp = s_group;
@@ -371,7 +389,8 @@ cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, co
   TcGemmArgs a{raw_tma, qw_ptrs, sm_ptrs, row_off, route_w, out, group_base, G, M, N, K, mode, status,
                bank2_qw != nullptr ? grp_sel : nullptr};
   const size_t smem = wide ? TcCfg<256>::SMEM : TcCfg<128>::SMEM;
-  dim3 grid((unsigned)max_mtiles, (unsigned)(N / BN));
+  if (max_mtiles > 65535) return cudaErrorInvalidValue;  // grid y limit
+  dim3 grid((unsigned)(N / BN), (unsigned)max_mtiles);
   if (wide) {
     static bool set = false;
     if (!set) {

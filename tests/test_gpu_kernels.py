@@ -30,11 +30,14 @@ def test_q4_quantize_matches_cpu_oracle(cuda):
 
 
 @pytest.fixture
-def gemv_only(monkeypatch):
+def gemv_only():
     """Keep 32-64-row 4-bit products on the mma.sync GEMV (its exact f32 scale/min fold is what
     these tests check; the tcgen05 decode GEMM has its own tests)."""
     from syntropy_b200.ops import core
-    monkeypatch.setitem(core._Q4_TC, 0, 1 << 30)
+    saved = core._Q4_TC[0]
+    core._Q4_TC[0] = 1 << 30
+    yield
+    core._Q4_TC[0] = saved
 
 
 @pytest.mark.parametrize("T,N,K", [(1, 256, 512), (5, 512, 1024), (8, 4096, 4096), (32, 1024, 4096),
