@@ -61,3 +61,15 @@ def test_ngram_native_batch_matches_python_rule():
     hist.append([5])
     for g in (1, 3, 4):
         assert d.propose_batch(hist, g) == [d.propose(h, g) for h in hist]
+
+
+def test_graph_bucket_never_exceeds_runner_rows():
+    """A decode bucket holds the rows but never more than the runner's rows (the descriptor and
+    the per-row buffers are sized by them), and the last bucket is the runner's own row count."""
+    from syntropy_b200.runtime.runner import BUCKETS, bucket_for
+    for cap in (1, 4, 50, 64, 100, 256):
+        for n in range(1, cap + 1):
+            b = bucket_for(n, cap=cap)
+            assert n <= b <= cap
+            assert b in BUCKETS or b == cap
+    assert bucket_for(40) == 48 and bucket_for(200) == 256
