@@ -49,12 +49,10 @@ struct TcGemmArgs {
   const int32_t* grp_sel;
 };
 
-// LEAN: short K (few blocks per CTA), 128-wide tiles with two stages so that two CTAs share an
-// SM and one's epilogue overlaps the other's main loop
-template <int BN, int LEAN = 0>
+template <int BN>
 struct TcCfg {
-  static constexpr int STAGES = LEAN ? 2 : (BN == 256 ? 3 : 4);
-  static constexpr int RAW = LEAN ? 3 : (BN == 256 ? 3 : 6);   // packed-weight stages
+  static constexpr int STAGES = BN == 256 ? 3 : 4;
+  static constexpr int RAW = BN == 256 ? 3 : 6;                // packed-weight stages
   static constexpr int A_SUB = TC_BM * TC_BK * 2;              // 16 KB per subtile
   static constexpr int A_BYTES = TC_MSUB * A_SUB;              // 32 KB
   static constexpr int B_BYTES = BN * TC_BK * 2;               // 16 / 32 KB
@@ -66,19 +64,19 @@ struct TcCfg {
 constexpr int TC_THREADS = 384;
 constexpr int TC_PRODUCERS = 8;  // warps 4..11
 
-template <int BN, int LEAN>
-__global__ void __launch_bounds__(TC_THREADS, LEAN ? 2 : 1) tc_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmap_a,
+template <int BN>
+__global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                             const __grid_constant__ CUtensorMap tmap_q,
                                                             const __grid_constant__ CUtensorMap tmap_s,
                                                             const __grid_constant__ CUtensorMap tmap_q2,
                                                             const __grid_constant__ CUtensorMap tmap_s2,
                                                             TcGemmArgs a) {
-  constexpr int TC_STAGES = TcCfg<BN, LEAN>::STAGES;
-  constexpr int TC_RAW = TcCfg<BN, LEAN>::RAW;
-  constexpr int A_SUB = TcCfg<BN, LEAN>::A_SUB;
-  constexpr int A_BYTES = TcCfg<BN, LEAN>::A_BYTES;
-  constexpr int B_BYTES = TcCfg<BN, LEAN>::B_BYTES;
-  constexpr int RAW_BYTES = TcCfg<BN, LEAN>::RAW_BYTES;
+  constexpr int TC_STAGES = TcCfg<BN>::STAGES;
+  constexpr int TC_RAW = TcCfg<BN>::RAW;
+  constexpr int A_SUB = TcCfg<BN>::A_SUB;
+  constexpr int A_BYTES = TcCfg<BN>::A_BYTES;
+  constexpr int B_BYTES = TcCfg<BN>::B_BYTES;
+  constexpr int RAW_BYTES = TcCfg<BN>::RAW_BYTES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -347,19 +345,19 @@ __global__ void __launch_bounds__(TC_THREADS, LEAN ? 2 : 1) tc_gemm_q4_kernel(co
 }
 
 // ---- host side ----
-template <int BN, int LEAN>
+template <int BN>
 static cudaError_t launch_q4_tiles(dim3 grid, const CUtensorMap& map, const CUtensorMap& mq, const CUtensorMap& ms,
                                    const CUtensorMap& mq2, const CUtensorMap& ms2, const TcGemmArgs& a,
                                    cudaStream_t s) {
   static bool set = false;
-  constexpr size_t smem = TcCfg<BN, LEAN>::SMEM;
+  constexpr size_t smem = TcCfg<BN>::SMEM;
   if (!set) {
     const cudaError_t e =
-        cudaFuncSetAttribute(tc_gemm_q4_kernel<BN, LEAN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(tc_gemm_q4_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     set = true;
   }
-  tc_gemm_q4_kernel<BN, LEAN><<<grid, TC_THREADS, smem, s>>>(map, mq, ms, mq2, ms2, a);
+  tc_gemm_q4_kernel<BN><<<grid, TC_THREADS, smem, s>>>(map, mq, ms, mq2, ms2, a);
   return cudaGetLastError();
 }
 
@@ -390,9 +388,7 @@ cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, co
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
   }
-  // few K blocks per CTA: lean 128-wide tiles, two CTAs per SM; else 256-wide where N allows
-  const bool lean = K <= 2048;
-  const bool wide = !lean && (N % 256 == 0);
+  const bool wide = (N % 256 == 0);
   const int BN = wide ? 256 : 128;
   auto aligned = [](const void* p) { return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   const int raw_tma = aligned(bank_qw) && aligned(bank_sm);
@@ -410,9 +406,8 @@ cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, co
                bank2_qw != nullptr ? grp_sel : nullptr};
   if (max_mtiles > 65535) return cudaErrorInvalidValue;  // grid y limit
   dim3 grid((unsigned)(N / BN), (unsigned)max_mtiles);
-  if (wide) return launch_q4_tiles<256, 0>(grid, map, mq, ms, mq2, ms2, a, s);
-  if (lean) return launch_q4_tiles<128, 1>(grid, map, mq, ms, mq2, ms2, a, s);
-  return launch_q4_tiles<128, 0>(grid, map, mq, ms, mq2, ms2, a, s);
+  if (wide) return launch_q4_tiles<256>(grid, map, mq, ms, mq2, ms2, a, s);
+  return launch_q4_tiles<128>(grid, map, mq, ms, mq2, ms2, a, s);
 }
 
 

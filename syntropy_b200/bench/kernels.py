@@ -218,10 +218,11 @@ def main():
                     report(f"q4_dec_{impl}_{rows}x{N}x{K}", timeit(fn, iters=20, warmup=len(ws) + 2), nbytes=nbytes,
                            flops=2 * rows * N * K)
                 _core._Q4_TC[0] = saved
-    if want("moe_prefill"):
+    if want("moe_prefill") or "moe_prefill_small" in only:
         # grouped 4-bit GEMMs of one Qwen3-235B MoE layer over a 32768-token prefill pass
-        # (top-8 of 128 experts: ~2048 rows per expert), all experts in one contiguous bank
-        G, rows_per = 128, 2048
+        # (top-8 of 128 experts: ~2048 rows per expert), all experts in one contiguous bank;
+        # moe_prefill_small: 16 experts (a profiler-sized case)
+        G, rows_per = (16 if "moe_prefill_small" in only else 128), 2048
         off = torch.arange(0, (G + 1) * rows_per, rows_per, dtype=torch.int32, device=dev)
         M = G * rows_per
         for name, N, K in (("gate_up", 3072, 4096), ("down", 4096, 1536)):
