@@ -331,10 +331,13 @@ cudaError_t launch_tc_gemm_q4_dec(const void* x, int T, int ldx, const void* qw,
   a.ldo = ldo;
   a.status = status;
   a.splits = q4_dec_splits(N, K);
-  if (const char* e = getenv("SYN_Q4_DEC_SPLITS")) {  // forced K slices (fault isolation / measurement)
-    const int f = atoi(e);
-    if (f == 1 || f == 2 || f == 4 || f == 8) a.splits = f;
-  }
+  // forced K slices (fault isolation / measurement), read once
+  static const int forced = [] {
+    const char* e = getenv("SYN_Q4_DEC_SPLITS");
+    const int f = e ? atoi(e) : 0;
+    return (f == 1 || f == 2 || f == 4 || f == 8) ? f : 0;
+  }();
+  if (forced) a.splits = forced;
   if (pp) {
     a.peers = pp->peers;
     a.n_peers = pp->n_peers;
