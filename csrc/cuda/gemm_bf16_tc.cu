@@ -116,7 +116,35 @@ __global__ void __launch_bounds__(BF_THREADS, 1) tc_gemm_bf16_kernel(const __gri
     const int r = quarter * 32 + lane;  // D row (TMEM lane)
     const bool ok = mbar_wait(&done_bar, 0, a.status, &s_abort) && kb1 > kb0;
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-    if (!DEC || a.splits == 1) {
+    if (!DEC && MODE != 6 && a.vec_out) {
+      // prefill orientation (lane = token): each 32 x 32 block goes through 4 KB of the free
+      // pipeline stages and is stored row-major, 16 bytes per lane
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      uint8_t* stg = sA + (warp - 2) * 4096;
+      const int tbase = tile_a * 128 + quarter * 32;
+      const int nrows = min(32, a.T - tbase);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t u[32];
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + c0, u);
+        const int n0 = tile_b * BN + c0;
+        if (!ok || nrows <= 0 || n0 >= a.N) continue;  // warp-uniform
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(u[j]);
+        uint8_t* ob = reinterpret_cast<uint8_t*>(a.out);
+        if constexpr (MODE == 1) {
+          stg_put_swiglu(stg, lane, v);
+          stg_flush<2>(stg, lane, ob + ((int64_t)tbase * a.ldo + n0 / 2) * 2, (int64_t)a.ldo * 2, nrows);
+        } else if constexpr (MODE == 0) {
+          stg_put_bf16(stg, lane, v);
+          stg_flush<4>(stg, lane, ob + ((int64_t)tbase * a.ldo + n0) * 2, (int64_t)a.ldo * 2, nrows);
+        } else {
+          stg_put_f32(stg, lane, v, 1.f);
+          stg_flush<8, MODE == 3>(stg, lane, ob + ((int64_t)tbase * a.ldo + n0) * 4, (int64_t)a.ldo * 4, nrows);
+        }
+      }
+    } else if (!DEC || a.splits == 1) {
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t u[32];
@@ -285,6 +313,10 @@ cudaError_t launch_tc_gemm_bf16(const void* x, int T, int ldx, const void* w, in
   a.out = out;
   a.ldo = ldo;
   a.status = status;
+  {
+    const int esz = (mode == 0 || mode == 1) ? 2 : 4;
+    a.vec_out = (reinterpret_cast<uintptr_t>(out) & 15) == 0 && ((int64_t)ldo * esz) % 16 == 0;
+  }
   if (pp) {
     a.peers = pp->peers;
     a.n_peers = pp->n_peers;

@@ -292,48 +292,41 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_q4_kernel(const __grid_
     // ---------------- epilogue ----------------
     const bool ok = mbar_wait(&done_bar, 0, a.status, &s_abort);
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+    // the activation stages are free once every MMA has completed (done_bar): each epilogue
+    // warp stages its output blocks in 4 KB of them (generic writes after async-proxy use)
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    uint8_t* stg = sA + (warp - 4) * 4096;
     const int quarter = warp & 3;       // TMEM lanes this warp may read
     const int half = (warp - 4) >> 2;   // which half of the columns it stores
 #pragma unroll 1
     for (int sub = 0; sub < (two ? 2 : 1); ++sub)
 #pragma unroll 1
     for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 32) {
-      const int row = row0 + sub * TC_BM + quarter * 32 + lane;
-      const bool live = ok && row < row_end && row < a.M;
+      const int rbase = row0 + sub * TC_BM + quarter * 32;  // first row of this warp's 32 x 32 block
       uint32_t r[32];
       tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + sub * BN + c0, r);
-      if (!live) continue;
+      const int nrows = min(32, min(row_end, a.M) - rbase);  // rows of this group (warp-uniform)
+      if (!ok || nrows <= 0) continue;
       const int n0 = ntile * BN + c0;
-      if (a.mode == 1) {  // SwiGLU over 8-column gate/up chunks
-        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(a.out) + (int64_t)row * (a.N / 2) + n0 / 2;
+      // lane = row in TMEM; the block goes through this warp's staging buffer so that each
+      // global store instruction writes whole 16-byte pieces of consecutive rows
+      float v[32];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int gi = (j / 8) * 16 + (j % 8);
-          const float gv = __uint_as_float(r[gi]), uv = __uint_as_float(r[gi + 8]);
-          o[j] = f2bf(silu(gv) * uv);
-        }
-      } else if (a.mode == 0) {
-        uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.out) + (int64_t)row * a.N + n0);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4 v;
-          v.x = pack_bf16x2(__uint_as_float(r[8 * j + 0]), __uint_as_float(r[8 * j + 1]));
-          v.y = pack_bf16x2(__uint_as_float(r[8 * j + 2]), __uint_as_float(r[8 * j + 3]));
-          v.z = pack_bf16x2(__uint_as_float(r[8 * j + 4]), __uint_as_float(r[8 * j + 5]));
-          v.w = pack_bf16x2(__uint_as_float(r[8 * j + 6]), __uint_as_float(r[8 * j + 7]));
-          o[j] = v;
-        }
-      } else {
-        float* o = reinterpret_cast<float*>(a.out) + (int64_t)row * a.N + n0;
-        const float sc = a.mode == 2 ? a.route_w[row] : 1.f;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float v = __uint_as_float(r[j]);
-          if (a.mode == 3)
-            o[j] += v;
-          else
-            o[j] = sc * v;
-        }
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+      uint8_t* ob = reinterpret_cast<uint8_t*>(a.out);
+      if (a.mode == 1) {  // SwiGLU: bf16 [M, N / 2]
+        stg_put_swiglu(stg, lane, v);
+        stg_flush<2>(stg, lane, ob + ((int64_t)rbase * (a.N / 2) + n0 / 2) * 2, (int64_t)a.N, nrows);
+      } else if (a.mode == 0) {  // bf16 [M, N]
+        stg_put_bf16(stg, lane, v);
+        stg_flush<4>(stg, lane, ob + ((int64_t)rbase * a.N + n0) * 2, (int64_t)a.N * 2, nrows);
+      } else {  // f32 [M, N]; mode 2: scaled by the row's routing weight; mode 3: added
+        const float sc = (a.mode == 2 && lane < nrows) ? a.route_w[rbase + lane] : 1.f;
+        stg_put_f32(stg, lane, v, sc);
+        if (a.mode == 3)
+          stg_flush<8, true>(stg, lane, ob + ((int64_t)rbase * a.N + n0) * 4, (int64_t)a.N * 4, nrows);
+        else
+          stg_flush<8>(stg, lane, ob + ((int64_t)rbase * a.N + n0) * 4, (int64_t)a.N * 4, nrows);
       }
     }
   }
@@ -373,6 +366,7 @@ cudaError_t launch_tc_gemm_q4(const void* x, int ldx, const int64_t* qw_ptrs, co
                               const void* bank2_sm, int bank2_experts, const int32_t* grp_sel) {
   if (K % TC_BK != 0 || N % 128 != 0 || M <= 0) return cudaErrorInvalidValue;
   if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || (ldx * 2) % 16 != 0) return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(out) & 15) != 0) return cudaErrorInvalidValue;  // 16-byte epilogue stores
   PFN_encodeTiled enc = get_encode();
   if (!enc) return cudaErrorNotSupported;
   CUtensorMap map, mq, ms;

@@ -166,4 +166,82 @@ static inline bool encode_q4_raw_maps(PFN_encodeTiled enc, CUtensorMap* mq, CUte
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+
+// ---- epilogue staging: a warp's 32-row output block stored row-major ----
+// After tcgen05.ld each lane holds one output row.  Storing from there writes 32 rows per
+// instruction; instead each lane writes its row's 16-byte chunks into a 4 KB staging block
+// and the warp stores the block back row-major, 16 bytes per lane.
+// stg_off<C>: byte offset of chunk c of row `row`, rows of C chunks (C = 2, 4, 8: 32, 64, 128
+// bytes) packed 8 / C to a 128-byte line, chunk position XORed with the line index, so the
+// row-per-lane writes (8 lanes = 8 rows per phase) and the row-major reads (8 lanes = one
+// line) both touch all 32 banks.
+template <int C>
+__device__ __forceinline__ uint32_t stg_off(int row, int c) {
+  constexpr int L = 8 / C;  // rows per 128-byte line
+  const int line = row / L;
+  return (uint32_t)(line * 128 + ((((row % L) * C + c) ^ (line & 7)) << 4));
+}
+
+// Stores rows [0, nrows) of the staged block to out + row * row_bytes (16-byte aligned rows);
+// ADD: f32 elements added to what is there.  Warp-collective.
+template <int C, bool ADD = false>
+__device__ __forceinline__ void stg_flush(const uint8_t* stg, int lane, uint8_t* out, int64_t row_bytes,
+                                          int nrows) {
+  __syncwarp();
+  constexpr int RPI = 32 / C;  // rows per store instruction
+#pragma unroll
+  for (int rr = 0; rr < 32; rr += RPI) {
+    const int rw = rr + lane / C, c = lane % C;
+    if (rw < nrows) {
+      uint4* o = reinterpret_cast<uint4*>(out + rw * row_bytes + c * 16);
+      uint4 v = *reinterpret_cast<const uint4*>(stg + stg_off<C>(rw, c));
+      if constexpr (ADD) {
+        const uint4 u = *o;
+        v.x = __float_as_uint(__uint_as_float(u.x) + __uint_as_float(v.x));
+        v.y = __float_as_uint(__uint_as_float(u.y) + __uint_as_float(v.y));
+        v.z = __float_as_uint(__uint_as_float(u.z) + __uint_as_float(v.z));
+        v.w = __float_as_uint(__uint_as_float(u.w) + __uint_as_float(v.w));
+      }
+      *o = v;
+    }
+  }
+  __syncwarp();  // the block is rewritten next
+}
+
+// Row r of the staged block from 32 accumulator columns v (lane = row): SwiGLU over the
+// interleaved 8-column gate / up chunks (16 bf16 out, C = 2), bf16 (C = 4), f32 * sc (C = 8).
+__device__ __forceinline__ void stg_put_swiglu(uint8_t* stg, int lane, const float* v) {
+  uint32_t w[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float o2[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int jj = 2 * j + e, gi = (jj / 8) * 16 + (jj % 8);
+      o2[e] = silu(v[gi]) * v[gi + 8];
+    }
+    w[j] = pack_bf16x2(o2[0], o2[1]);
+  }
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
+    *reinterpret_cast<uint4*>(stg + stg_off<2>(lane, c)) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+}
+__device__ __forceinline__ void stg_put_bf16(uint8_t* stg, int lane, const float* v) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint4 w;
+    w.x = pack_bf16x2(v[8 * c + 0], v[8 * c + 1]);
+    w.y = pack_bf16x2(v[8 * c + 2], v[8 * c + 3]);
+    w.z = pack_bf16x2(v[8 * c + 4], v[8 * c + 5]);
+    w.w = pack_bf16x2(v[8 * c + 6], v[8 * c + 7]);
+    *reinterpret_cast<uint4*>(stg + stg_off<4>(lane, c)) = w;
+  }
+}
+__device__ __forceinline__ void stg_put_f32(uint8_t* stg, int lane, const float* v, float sc) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    *reinterpret_cast<float4*>(stg + stg_off<8>(lane, c)) =
+        make_float4(sc * v[4 * c], sc * v[4 * c + 1], sc * v[4 * c + 2], sc * v[4 * c + 3]);
+}
+
 }  // namespace syn

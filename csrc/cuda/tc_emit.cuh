@@ -25,6 +25,7 @@ struct DenseGemmArgs {
   const uint32_t* step_ctr;
   int n_layers, layer;
   int* status;
+  int vec_out;              // out and ldo allow 16-byte row-major epilogue stores (prefill orientation)
 };
 
 

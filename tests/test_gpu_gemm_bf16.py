@@ -18,7 +18,7 @@ def _rel(a, b):
 
 @pytest.mark.parametrize("T,N,K", [(1, 768, 4096), (7, 4096, 512), (32, 3584, 4096), (64, 4096, 1792),
                                    (100, 1024, 1024), (128, 768, 4096), (300, 4096, 1024), (1000, 2048, 512),
-                                   (64, 16032, 4096), (5, 160, 256)])
+                                   (64, 16032, 4096), (5, 160, 256), (200, 160, 256)])
 @pytest.mark.parametrize("mode", [0, 1, 3, 5])
 def test_gemm_bf16_modes(cuda, T, N, K, mode):
     if mode == 1 and N % 16:
