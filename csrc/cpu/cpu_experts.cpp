@@ -9,14 +9,15 @@
 // consecutive columns of one row (j = 0, 2: row g; j = 1, 3: row g+8; j = 2, 3 are 8 columns
 // further).  Two kernel families consume these pairs (each activation row is packed once per
 // layer into the same pair order, with its per-block sums):
-//  * BF16 (default): OR-ing 0x4300 into a nibble gives the bf16 number 128 + q exactly, so
+//  * BF16: OR-ing 0x4300 into a nibble gives the bf16 number 128 + q exactly, so
 //    `vdpbf16ps` multiplies bf16 pairs exactly and
 //        sum_k (d q_k + m) x_k = d * sum_k (128 + q_k) x_k + (m - 128 d) * sum_k x_k;
 //  * VNNI (hosts with AVX-512 VNNI but no BF16): the activation's 32-column block is scaled to
 //    int16 (s = max|x| / 32767, rounding error at most s / 2 per element), `vpdpwssd` sums
 //    q * v exactly in int32, and y ~= d * s * sum_k q_k v_k + m * sum_k x_k (sum x exact).
-// Both agree with the f32 product to ~1e-5 relative and ran at the same speed on a B200 node's
-// host (the pool is bound by the per-row work around the dot products, not by them).
+// Both agree with the f32 product to ~1e-5 relative.  Which one is faster depends on the host's
+// `vdpbf16ps` rate, so the default is the faster of the two, timed once per process
+// (`calibrate_mode`).
 //
 // Threads: a fixed pool pinned to the given CPUs.  Thread 0 polls the mailbox's go word; on a
 // new sequence it lists the routed pairs of the experts this tier owns for that layer and
@@ -183,7 +184,8 @@ __attribute__((target("avx512f,avx512bw,avx512vl,avx512vnni,f16c,fma"))) void ti
         }
       for (int kg = 0; kg < KG; ++kg) {
         const uint32_t* wp = wt + kg * 128 + 16 * g0;
-        for (int l = 0; l < GB; ++l) _mm_prefetch(reinterpret_cast<const char*>(wp + 4 * 128 + 16 * l), _MM_HINT_T0);
+        // 8 groups (4 KB of the tile) ahead: one thread streams from DRAM at its miss latency
+        for (int l = 0; l < GB; ++l) _mm_prefetch(reinterpret_cast<const char*>(wp + 8 * 128 + 16 * l), _MM_HINT_T0);
         __m512i xa[NR], xb[NR];
         __m512 xs[NR];
         for (int r = 0; r < NR; ++r) {
@@ -320,8 +322,8 @@ void tiles_scalar(const uint32_t* qw, const uint16_t* sm, int K, int tile0, int 
     }
 }
 
-// Kernel family: 0 plain C++, 1 AVX-512 BF16 (bf16 magic-number pairs, exact products; the
-// default), 2 AVX-512 VNNI (int16 activations, vpdpwssd; hosts without AVX-512 BF16).
+// Kernel family: 0 plain C++, 1 AVX-512 BF16 (bf16 magic-number pairs, exact products),
+// 2 AVX-512 VNNI (int16 activations, vpdpwssd); the default is the faster SIMD family.
 bool has_bf16() {
   static const bool ok = __builtin_cpu_supports("avx512f") && __builtin_cpu_supports("avx512bw") &&
                          __builtin_cpu_supports("avx512vl") && __builtin_cpu_supports("avx512bf16");
@@ -334,10 +336,59 @@ bool has_vnni() {
 }
 bool simd_ok() { return has_bf16() || has_vnni(); }
 
+// Which SIMD family is faster depends on the host: on some Xeons `vdpbf16ps` issues at about a
+// quarter of the FMA rate, so the int16 VNNI form (two `vpdpwssd` per pair of columns, exact
+// integer sums) wins by ~1.4x; where bf16 dot products are cheap the BF16 form saves the
+// activation scaling.  Both families are timed once per process on a synthetic, cache-resident
+// slice (4 tiles x 1024 columns, 2 rows: the common row count of an expert at decode) and the
+// faster one is the default.  A few milliseconds on the calling thread.
+int calibrate_mode() {
+  if (!(has_bf16() && has_vnni())) return has_bf16() ? 1 : (has_vnni() ? 2 : 0);
+  constexpr int Kc = 1024, KGc = Kc / 64, T = 4, R = 2;
+  std::vector<uint32_t> qw((size_t)T * KGc * 128);
+  std::vector<uint16_t> sm((size_t)T * KGc * 64);
+  uint32_t st = 12345u;
+  for (auto& v : qw) v = (st = st * 1664525u + 1013904223u);
+  for (size_t i = 0; i < sm.size(); ++i) sm[i] = (i & 1) ? 0xA400 : 0x2000;  // m = -1/64, d = 1/128
+  std::vector<uint16_t> x((size_t)R * Kc);
+  for (auto& v : x) v = f2bf_h((float)(int)((st = st * 1664525u + 1013904223u) >> 22) / 512.f - 1.f);
+  std::vector<uint32_t> ab(R * KGc * 32), ab16(R * KGc * 32);
+  std::vector<float> sx4(R * KGc * 4), sxs(R * KGc * 16), y(R * T * 16), one(R, 1.f);
+  const uint32_t *pa[R], *pa16[R];
+  const float *ps4[R], *pss[R];
+  float* py[R];
+  for (int r = 0; r < R; ++r) {
+    pack_row(&x[r * Kc], Kc, &ab[r * KGc * 32], &sx4[r * KGc * 4]);
+    pack_row_i16(&x[r * Kc], Kc, &ab16[r * KGc * 32], &sxs[r * KGc * 16], &sx4[r * KGc * 4]);
+    pa[r] = &ab[r * KGc * 32];
+    pa16[r] = &ab16[r * KGc * 32];
+    ps4[r] = &sx4[r * KGc * 4];
+    pss[r] = &sxs[r * KGc * 16];
+    py[r] = &y[r * T * 16];
+  }
+  auto best_of = [](auto&& f) {
+    uint64_t best = ~0ull;
+    for (int rep = 0; rep < 7; ++rep) {
+      const uint64_t t0 = now_ns();
+      for (int i = 0; i < 16; ++i) f();
+      best = std::min(best, now_ns() - t0);
+    }
+    return best;
+  };
+  const uint64_t t_bf = best_of([&] { tiles_avx512<R>(qw.data(), sm.data(), Kc, 0, T, pa, ps4, py, one.data()); });
+  const uint64_t t_i16 =
+      best_of([&] { tiles_vnni<R, 4>(qw.data(), sm.data(), Kc, 0, T, pa16, pss, ps4, py, one.data()); });
+  return t_i16 < t_bf ? 2 : 1;
+}
+
 int pick_mode(int want) {
   if (want < 0) {
-    const char* e = getenv("SYN_CPU_GEMV_MODE");
-    want = e ? atoi(e) : 1;
+    if (const char* e = getenv("SYN_CPU_GEMV_MODE")) {
+      want = atoi(e);
+    } else {
+      static const int fastest = calibrate_mode();
+      want = fastest;
+    }
   }
   if (want == 1 && !has_bf16()) want = has_vnni() ? 2 : 0;
   if (want == 2 && !has_vnni()) want = has_bf16() ? 1 : 0;
