@@ -3,8 +3,8 @@
 With a VRAM cap, every MoE layer has host experts.  The GPU can read them over PCIe in place
 (the grouped GEMV takes host pointers), which is bound by the link (~50 GB/s).  The host's own
 DRAM bandwidth is a second, independent resource: a share of the host experts
-(``cpu_share``) is computed by a pool of CPU threads (AVX-512 BF16 over the same tiled 4-bit
-rows, ``csrc/cpu/cpu_experts.cpp``) while the GPU streams the resident experts and the
+(``cpu_share``) is computed by a pool of CPU threads (AVX-512 int16 VNNI or BF16, whichever is
+faster on the host, over the same tiled 4-bit rows, ``csrc/cpu/cpu_experts.cpp``) while the GPU streams the resident experts and the
 remaining host experts.  Per MoE layer of a decode step:
 
 1. routing on the GPU; ``cpu_handoff`` copies the layer's rows and routing CSR into a pinned
@@ -30,15 +30,18 @@ from .._ext import ext
 
 
 # Host-tier rates used to split each rank's cold experts between its CPU workers and its PCIe
-# link (bytes of 4-bit weights per second).  Measured on the B200 node: the AVX-512 BF16 pool
-# moves ~4.8 GB/s per worker thread; one GPU stages host rows with bulk DMA at ~45 GB/s while
-# the CPU also streams DRAM (capped Qwen3 decode on one GPU and 14 workers: shares 0.5 / 0.6 /
-# 0.75 gave 57.3 / 65.4 / 55.8 tok/s, so the balance sits near 0.6).  With several ranks per
+# link (bytes of 4-bit weights per second), per CPU kernel family (`ext().cpu_gemv_mode()`, the
+# faster of the two on the host, timed at start-up).  Measured on the B200 node (16-core Xeon
+# slice, 14 workers, capped Qwen3 decode on one GPU): the int16 VNNI pool balances the link at a
+# share of 0.7 (shares 0.6 / 0.7 / 0.75 / 0.8 gave 68.4 / 71.4 / 67.7 / 57.8 tok/s), i.e. ~7.5
+# GB/s per worker; the BF16 pool at 0.6 (0.5 / 0.6 / 0.75 gave 57.3 / 65.4 / 55.8), ~4.8 GB/s per
+# worker (its `vdpbf16ps` issues at about a quarter of the FMA rate on that host).  One GPU stages
+# host rows with bulk DMA at ~45 GB/s while the CPU also streams DRAM.  With several ranks per
 # node the workers of all ranks contend for DRAM while each GPU stages over its own link; the
 # effective link rate that reproduces the measured balance is ~55 GB/s per GPU (capped Qwen3
-# decode over EP2 with 11 workers per rank: shares 0.68 / 0.56 / 0.5 gave 71.7 / 78.1 / 90.1
-# tok/s).
-CPU_GBS_PER_THREAD = 4.8
+# decode over EP2 with 11 BF16 workers per rank: shares 0.68 / 0.56 / 0.5 gave 71.7 / 78.1 /
+# 90.1 tok/s).
+CPU_GBS_PER_THREAD = {1: 4.8, 2: 7.5}
 PCIE_GBS_ALONE, PCIE_GBS_SHARED = 45.0, 55.0
 
 
@@ -58,10 +61,13 @@ def rank_cpus(local_rank: int, local_world: int, allowed: list[int] | None = Non
     return part[1:], part[:1]
 
 
-def balanced_share(threads: int, local_world: int) -> float:
+def balanced_share(threads: int, local_world: int, mode: int | None = None) -> float:
     """CPU share of the host tier that makes the CPU workers and the PCIe reads of one rank
-    finish together (the two run at the same time during a layer)."""
-    cpu = threads * CPU_GBS_PER_THREAD
+    finish together (the two run at the same time during a layer); `mode` is the CPU kernel
+    family (default: the one the pool will use)."""
+    if mode is None:
+        mode = ext().cpu_gemv_mode()
+    cpu = threads * CPU_GBS_PER_THREAD.get(mode, 0.5)
     pcie = PCIE_GBS_ALONE if local_world <= 1 else PCIE_GBS_SHARED
     return round(cpu / (cpu + pcie), 2)
 

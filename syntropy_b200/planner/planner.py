@@ -32,11 +32,11 @@ class HardwareModel:
     nvlink_alpha_us: float = 6.0   # one fused flag round trip
     nccl_alpha_us: float = 18.0    # small NCCL collective latency
     pcie_gbs: float = 55.5         # pinned H2D (measured on the B200 box)
-    # host tier with the CPU expert pool: fitted to capped Qwen3 decode at CPU shares 0.5 / 0.75 / 1.0
-    # on one B200 node slice (715 / 602 / 711 ms per step), per-layer time = fixed + max(PCIe
-    # part, CPU part)
+    # host tier with the CPU expert pool: per-layer time = fixed + max(PCIe part, CPU part); the
+    # PCIe rate fitted to capped Qwen3 decode on one B200 node slice, the CPU rate to the measured
+    # balance of the int16 VNNI pool (share 0.7 against the link: 0.7 / 0.3 x 50 GB/s)
     pcie_read_gbs: float = 50.0    # GPU reading host experts in place while the CPU also reads DRAM
-    cpu_expert_gbs: float = 100.0  # host CPU expert pool, 14 threads
+    cpu_expert_gbs: float = 117.0  # host CPU expert pool, 14 threads
     cpu_tier_layer_ms: float = 2.7  # per MoE layer: hand-off, collect and the serial part around them
     vram_gb: float = 178.0
     launch_gap_us: float = 1.2     # per kernel inside a CUDA graph
