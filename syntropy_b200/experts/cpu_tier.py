@@ -42,6 +42,11 @@ from .._ext import ext
 # decode over EP2 with 11 BF16 workers per rank: shares 0.68 / 0.56 / 0.5 gave 71.7 / 78.1 /
 # 90.1 tok/s).
 CPU_GBS_PER_THREAD = {1: 4.8, 2: 7.5}
+# With several ranks on a node the pools of all ranks share the host's DRAM: on the 2-GPU node
+# slice (24 cores, 11 int16 workers per rank) a rank's pool reached ~57 GB/s at share 0.6
+# (86.4 tok/s, 370 ms per step, the CPU part the longer one), below its 11 x 7.5 GB/s of
+# instruction throughput, so the model caps a rank's pool there.
+CPU_GBS_PER_RANK_SHARED = 57.0
 PCIE_GBS_ALONE, PCIE_GBS_SHARED = 45.0, 55.0
 
 
@@ -68,6 +73,8 @@ def balanced_share(threads: int, local_world: int, mode: int | None = None) -> f
     if mode is None:
         mode = ext().cpu_gemv_mode()
     cpu = threads * CPU_GBS_PER_THREAD.get(mode, 0.5)
+    if local_world > 1:
+        cpu = min(cpu, CPU_GBS_PER_RANK_SHARED)
     pcie = PCIE_GBS_ALONE if local_world <= 1 else PCIE_GBS_SHARED
     return round(cpu / (cpu + pcie), 2)
 
