@@ -50,7 +50,9 @@ def _engine_from_config(cfg, device: str):
     spec = _spec_from_config(cfg, mcfg, runner, dev)
     chunk = cfg.sched.chunk_tokens or None
     return LLMEngine(runner, max_prefill_tokens=cfg.sched.max_prefill_tokens, rebalance_every=cfg.tier.rebalance_every,
-                     spec=spec, chunk_tokens=chunk if spec is None else None), mcfg
+                     spec=spec, chunk_tokens=chunk if spec is None else None,
+                     kv_host_bytes=cfg.tier.kv_host_budget or None,
+                     kv_spill_dir=cfg.tier.kv_spill_dir or None), mcfg
 
 
 def _spec_from_config(cfg, mcfg, runner, dev):

@@ -86,6 +86,8 @@ class TierSection:
     expert_prefetch: bool = True     # router-predicted prefetch of host experts during decode
     cpu_expert_share: float = 0.0    # share of each layer's host experts computed by host threads
     cpu_threads: int = 0             # 0 = every allowed core but two
+    kv_host_budget: int = _size(0)   # host RAM for preempted sequences' KV pages; 0 = unbounded
+    kv_spill_dir: str = ""           # pack files for preempted KV past kv_host_budget ("" = none)
 
 
 @dataclass

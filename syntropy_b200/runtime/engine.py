@@ -86,7 +86,8 @@ class StepOutput:
 class LLMEngine:
     def __init__(self, runner: ModelRunner, max_prefill_tokens: int = 8192, eos_token_id: int | None = None,
                  dist_ctx=None, prefix_cache: bool = False, spec=None, rebalance_every: int = 64,
-                 chunk_tokens: int | None = None):
+                 chunk_tokens: int | None = None, kv_host_bytes: int | None = None,
+                 kv_spill_dir: str | None = None):
         self.runner = runner
         # Chunked prefill (reference plan/rfcs/RFC-0012-execution-scheduler.md:299-314): prompts
         # enter the KV cache at most `chunk_tokens` tokens per step, and every step first runs
@@ -112,8 +113,11 @@ class LLMEngine:
         self.eos = eos_token_id
         self.waiting: deque[Sequence] = deque()
         self.running: list[Sequence] = []
-        # preempted sequences whose KV pages wait in host memory: (sequence, packed layers)
+        # preempted sequences whose KV pages wait below VRAM: (sequence, SwapStore entry); the
+        # store keeps them in host RAM up to kv_host_bytes, then in pack files under kv_spill_dir
+        from ..kv.tiers import SwapStore
         self.swapped: deque = deque()
+        self.kv_store = SwapStore(kv_host_bytes, kv_spill_dir)
         self.finished: dict[int, Sequence] = {}
         self._ids = itertools.count()
         self._boot_seed = random.getrandbits(63)
@@ -189,6 +193,7 @@ class LLMEngine:
         for item in list(self.swapped):
             if item[0].seq_id == seq_id:
                 self.swapped.remove(item)
+                self.kv_store.drop(item[1])
                 self._finish(item[0], "cancelled")
                 return
         for s in list(self.waiting):
@@ -243,21 +248,21 @@ class LLMEngine:
         return need - kv.alloc.num_free
 
     def _swap_out(self, s: Sequence):
-        """Preempt s: its KV pages go to host memory and back to the pool; it resumes later
-        from exactly where it stopped (no recompute)."""
+        """Preempt s: its KV pages go to host memory (or a spill file past the host budget) and
+        back to the pool; it resumes later from exactly where it stopped (no recompute)."""
         layers = self._pack_kv(s)
         self.runner.kv.release(s.blocks)
         s.blocks = []
         s.status = "swapped"
         self.running.remove(s)
-        self.swapped.append((s, layers))
+        self.swapped.append((s, self.kv_store.put(s.seq_id, layers)))
         self.stats["swapped_out"] += 1
 
     def _swap_in(self) -> bool:
         """Resume the oldest preempted sequence if its pages fit (before any new admission)."""
         if not self.swapped or len(self.running) >= self.runner.max_batch:
             return False
-        s, layers = self.swapped[0]
+        s, entry = self.swapped[0]
         kv = self.runner.kv
         need = kv.blocks_needed(s.n_tokens + 1)
         if kv.alloc.num_free < need and self.prefix is not None:
@@ -265,7 +270,8 @@ class LLMEngine:
         if kv.alloc.num_free < need:
             return False
         self.swapped.popleft()
-        self._unpack_kv(s, layers)
+        self._unpack_kv(s, self.kv_store.take(entry))
+        self.kv_store.refill(e for _, e in self.swapped)  # the next to resume come back into RAM
         s.status = "running"
         self.running.append(s)
         self.stats["swapped_in"] += 1

@@ -59,3 +59,47 @@ def test_request_larger_than_the_pool_is_rejected():
     eng.add_request(list(range(5, 20)), SamplingParams(max_tokens=4))  # fits: served
     while eng.has_work():
         eng.step()
+
+
+@pytest.mark.parametrize("host_budget", [0, 6000])
+def test_swap_spills_to_files_past_the_host_budget(tmp_path, host_budget):
+    """A host budget below the preempted pages sends them to pack files (budget 0: all of them;
+    a small budget: the tail of the queue) and back; tokens equal the ample-pool run and no
+    file is left behind."""
+    cfg = get_config("tiny-llama")
+    mw = prepare_weights(cfg, torch.device("cpu"), seed=2)
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, cfg.vocab, (n,), generator=g).tolist() for n in (20, 14, 30, 9)]
+    params = SamplingParams(max_tokens=40)
+    want = LLMEngine(ModelRunner(mw, max_batch=4, max_seq_len=128)).generate(prompts, params)
+    eng = LLMEngine(ModelRunner(mw, max_batch=4, max_seq_len=128, num_blocks=9), kv_host_bytes=host_budget,
+                    kv_spill_dir=str(tmp_path / "kv"))
+    assert eng.generate(prompts, params) == want
+    st = eng.kv_store.stats
+    assert eng.stats["swapped_out"] > 0 and st["spilled"] > 0 and st["restored"] == st["spilled"]
+    assert eng.kv_store.host_bytes == 0 and eng.kv_store.disk_bytes == 0
+    assert not list((tmp_path / "kv").iterdir())
+
+
+def test_swap_store_tiers_and_digest(tmp_path):
+    from syntropy_b200.kv.tiers import SwapStore
+    a = [torch.randn(3, 4, 16).to(torch.bfloat16) for _ in range(2)]
+    b = [torch.randn(2, 4, 16).to(torch.bfloat16) for _ in range(2)]
+    nb_a = sum(t.numel() * 2 for t in a)
+    st = SwapStore(host_budget=nb_a, spill_dir=str(tmp_path))
+    ea, eb = st.put(1, [t.clone() for t in a]), st.put(2, [t.clone() for t in b])
+    assert st.where(ea) == "host" and st.where(eb) == "disk"
+    assert all(torch.equal(x, y) for x, y in zip(st.take(ea), a))
+    st.refill([eb])  # room again: the next to resume comes back into RAM
+    assert st.where(eb) == "host" and not list(tmp_path.glob("*.pack"))
+    assert all(torch.equal(x, y) for x, y in zip(st.take(eb), b))
+    # a damaged spill file is caught by its digest, not handed back as KV
+    st2 = SwapStore(host_budget=0, spill_dir=str(tmp_path))
+    ec = st2.put(3, [t.clone() for t in b])
+    with open(ec.path, "r+b") as f:
+        f.seek(5)
+        f.write(b"\xff\xfe")
+    with pytest.raises(ValueError, match="digest"):
+        st2.take(ec)
+    st2.drop(ec)
+    assert not list(tmp_path.glob("kv_3*"))
