@@ -86,6 +86,7 @@ void register_all(pybind11::module& m) {
   m.def("verify_accept", &verify_accept);
   m.def("q4_gemv_tp", &q4_gemv_tp);
   m.def("tp_reduce_norm", &tp_reduce_norm);
+  m.def("tp_twoshot", &tp_twoshot, "ordered two-shot all-reduce (peer-load reduce-scatter, peer-store all-gather) + residual + RMSNorm");
   register_runtime(m);
   register_formats(m);
   register_dispatcher(m);

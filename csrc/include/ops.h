@@ -73,6 +73,9 @@ void tc_gemm_q4(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, t
 void q4_gemv_tp(torch::Tensor x, torch::Tensor qw_ptrs, torch::Tensor sm_ptrs, torch::Tensor tok_off, int64_t N,
                 int64_t K, torch::Tensor done_ctr, torch::Tensor peers, int64_t peer_off, int64_t peer_cap,
                 int64_t sig_off, int64_t rank, torch::Tensor step_ctr, int64_t n_layers, int64_t layer);
+void tp_twoshot(torch::Tensor peers, int64_t rank, int64_t off_part, int64_t off_gather, int64_t off_flag_ready,
+                int64_t off_flag_done, int64_t seq, int64_t timeout_ns, torch::Tensor status, torch::Tensor done_ctr,
+                torch::Tensor x, torch::Tensor wn, torch::Tensor hout, double eps);
 void tp_reduce_norm(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, int64_t H, std::vector<int64_t> offs,
                     torch::Tensor step_ctr, int64_t n_layers, int64_t layer, int64_t timeout_ns, torch::Tensor status,
                     int64_t off_recv, int64_t off_flag, torch::Tensor x, torch::Tensor wn, torch::Tensor hout,

@@ -94,6 +94,20 @@ cudaError_t launch_ep_dispatch(const EpArgs& a, const void* h, const int32_t* id
                                cudaStream_t s);
 cudaError_t launch_ep_build(const EpArgs& a, int32_t* tok_off, int32_t* tok_idx, float* pair_w, int64_t* pair_dst,
                             cudaStream_t s);
+// Ordered two-shot all-reduce of f32 partials in symmetric regions (tensor-parallel prefill):
+// rank-order reduce-scatter by peer loads, all-gather by peer stores, then x += sum (+ RMSNorm).
+struct TwoShotArgs {
+  const int64_t* peers;  // device array [N] of symmetric-region bases (own included)
+  int N, rank, H;
+  int64_t n_elems;       // T * H
+  int64_t off_part, off_gather, off_flag_ready, off_flag_done;
+  uint32_t seq;          // monotone per use; flags compare against it
+  uint64_t timeout_ns;
+  int* status;
+  unsigned* done_ctr;    // CTA arrivals of the reduce-scatter (left zero)
+};
+cudaError_t launch_tp_twoshot(const TwoShotArgs& a, float* x, const float* wn, void* hout, float eps, int T,
+                              cudaStream_t s);
 cudaError_t launch_tp_reduce_norm(const EpArgs& a, int64_t off_recv, int64_t off_flag, float* x, const float* wn,
                                   void* hout, float eps, int T, cudaStream_t s);
 cudaError_t launch_ep_combine(const EpArgs& a, float* x, const float* wn, void* hout, float eps, int T,

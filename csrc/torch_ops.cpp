@@ -572,6 +572,36 @@ void tp_reduce_norm(torch::Tensor peers, int64_t N, int64_t rank, int64_t cap, i
 }
 
 
+// Two-shot all-reduce of this rank's f32 partial (at off_part of its symmetric region, [T, H])
+// into x [T, H] (+ RMSNorm into hout when wn is given).
+void tp_twoshot(torch::Tensor peers, int64_t rank, int64_t off_part, int64_t off_gather, int64_t off_flag_ready,
+                int64_t off_flag_done, int64_t seq, int64_t timeout_ns, torch::Tensor status, torch::Tensor done_ctr,
+                torch::Tensor x, torch::Tensor wn, torch::Tensor hout, double eps) {
+  TORCH_CHECK(peers.is_cuda() && peers.scalar_type() == torch::kInt64, "peers int64 (device)");
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kFloat32 && x.dim() == 2 && x.is_contiguous(), "x f32 [T, H]");
+  TORCH_CHECK(status.is_cuda() && status.scalar_type() == torch::kInt32, "status int32 (device)");
+  TORCH_CHECK(done_ctr.is_cuda() && done_ctr.scalar_type() == torch::kInt32 && done_ctr.numel() >= 1, "done_ctr int32");
+  TwoShotArgs a;
+  a.peers = peers.data_ptr<int64_t>();
+  a.N = (int)peers.numel();
+  a.rank = (int)rank;
+  a.H = (int)x.size(1);
+  a.n_elems = x.numel();
+  a.off_part = off_part;
+  a.off_gather = off_gather;
+  a.off_flag_ready = off_flag_ready;
+  a.off_flag_done = off_flag_done;
+  a.seq = (uint32_t)seq;
+  a.timeout_ns = (uint64_t)timeout_ns;
+  a.status = status.data_ptr<int32_t>();
+  a.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr<int32_t>());
+  const float* wp = fptr_or_null(wn);
+  if (wp) TORCH_CHECK(hout.is_cuda() && hout.scalar_type() == torch::kBFloat16 && hout.numel() >= x.numel(), "hout bf16");
+  const at::cuda::CUDAGuard guard(x.device());
+  SYN_CHECK_CUDA(launch_tp_twoshot(a, x.data_ptr<float>(), wp, wp ? hout.data_ptr() : nullptr, (float)eps,
+                                   (int)x.size(0), cur_stream()));
+}
+
 // Exact acceptance of point-mass drafts, or of drafts sampled from the distributions
 // draft_probs [S, g, V] (f32; empty for point masses) (see csrc/cuda/sampler.cu).
 void verify_accept(torch::Tensor logits, torch::Tensor draft, torch::Tensor temperature, torch::Tensor top_k,

@@ -63,6 +63,16 @@ class TPGroup:
             self.status = torch.zeros(1, dtype=torch.int32, device=dev)
             self.done_ctr = torch.zeros(2 * n_layers + 1, dtype=torch.int32, device=dev)
             self._off1 = {}
+            # prefill (MiB-scale messages): ordered two-shot all-reduce over a second region
+            # holding a partial and a gather buffer of `prefill_rows` rows, plus ready / done
+            # flags; sequence numbers come from a host counter (prefill runs eagerly)
+            self.prefill_rows = max(256, (64 << 20) // (hidden * 4) // 256 * 256)
+            part = _align(self.prefill_rows * hidden * 4)
+            self.off_part, self.off_gather = 0, part
+            self.off_ready, self.off_done = 2 * part, 2 * part + 256
+            self.region2 = SymmetricRegion(ctx, 2 * part + 512)
+            self.ts_ctr = torch.zeros(1, dtype=torch.int32, device=dev)
+            self.ts_seq = 0
 
     def step_begin(self):
         if self.fused:
@@ -135,6 +145,29 @@ class TPGroup:
         x_res.add_(part)
         if next_norm is not None:
             ops.rms_norm(x_res, next_norm, eps, out=h_out)
+
+    def part_view(self, rows: int) -> torch.Tensor:
+        """f32 [rows, H] partial buffer of the two-shot all-reduce (rows <= prefill_rows)."""
+        return self.region2.view(self.off_part, rows * self.H, torch.float32).view(rows, self.H)
+
+    def twoshot_add(self, x_rows: torch.Tensor, next_norm=None, h_out=None, eps: float = 0.0):
+        """x_rows += sum over ranks of their part_view(rows) (rank order; identical bits on every
+        rank), then h_out = rmsnorm(x_rows) * next_norm when next_norm is given."""
+        self.ts_seq += 1
+        dev = x_rows.device
+        ext().tp_twoshot(self.region2.peers, self.rank, self.off_part, self.off_gather, self.off_ready, self.off_done,
+                         self.ts_seq, self.timeout_ns, self.status, self.ts_ctr, x_rows,
+                         next_norm if next_norm is not None else torch.empty(0, device=dev),
+                         h_out if h_out is not None else torch.empty(0, device=dev), eps)
+        ops.core._launched(2)
+
+    def allreduce_rows(self, T: int, partial_fn, x: torch.Tensor):
+        """x[:T] += all_reduce(partial) in chunks of prefill_rows rows; partial_fn(r0, r1, out)
+        writes this rank's f32 partial of rows [r0, r1) into out (a view of the region)."""
+        for r0 in range(0, T, self.prefill_rows):
+            r1 = min(T, r0 + self.prefill_rows)
+            partial_fn(r0, r1, self.part_view(r1 - r0))
+            self.twoshot_add(x[r0:r1])
 
     def check_status(self) -> int:
         return int(self.status.item()) if self.fused else 0

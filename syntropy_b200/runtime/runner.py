@@ -920,9 +920,14 @@ class ModelRunner:
             attn[a:b] = o[0].transpose(0, 1).to(attn.dtype)
 
     def _row_parallel(self, a, W, x):
-        """x += a @ W^T, summed over TP ranks with NCCL (prefill)."""
+        """x += a @ W^T, summed over TP ranks (prefill): the ordered two-shot all-reduce over
+        NVLink peer memory (each chunk's f32 partial written straight into the symmetric
+        region by the GEMM), or NCCL for the baseline."""
         if self.tp is None:
             ops.linear(a, W, x, ops.GEMV_ADD_F32)
+            return
+        if self.tp.fused:
+            self.tp.allreduce_rows(a.shape[0], lambda r0, r1, out: ops.linear(a[r0:r1], W, out, ops.GEMV_STORE), x)
             return
         import torch.distributed as dist
         part = torch.zeros_like(x)
@@ -935,7 +940,13 @@ class ModelRunner:
         their gathered rows (one weight read per active expert), combined in ascending
         expert order; under expert parallelism the NCCL all-gather/reduce-scatter path; under
         tensor parallelism (experts split along their width) the partial outputs are summed
-        over the group with NCCL."""
+        over the group by the two-shot all-reduce (NCCL for the baseline)."""
+        if self.tp is not None and self.tp.fused:
+            def partial(r0, r1, out):
+                out.zero_()
+                self._moe_prefill_local(L, h[r0:r1], out)
+            self.tp.allreduce_rows(h.shape[0], partial, x)
+            return
         if self.tp is not None:
             import torch.distributed as dist
             part = torch.zeros_like(x)

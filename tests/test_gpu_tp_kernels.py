@@ -7,6 +7,8 @@
   residuals of both ranks must be bitwise equal (member-order reduction).
 * Vocab-parallel head: each rank's bf16 head GEMM writes its column slice into both ranks'
   logits buffers; checked against the f32 product with the concatenated slices.
+* Prefill all-reduce (ordered two-shot over peer memory, in chunks): the residual must equal
+  x + (p_0 + p_1) in f32 bit for bit.
 
 Runs as two child processes (one per GPU), NVLS off; skipped with fewer than 2 GPUs.
 """
@@ -73,6 +75,32 @@ alls = [None] * ctx.world
 dist.all_gather_object(alls, w_lm, group=ctx.cpu_group)
 lref = hh.float() @ torch.cat([a.float() for a in alls]).t()
 res["logits_rel"] = ((logits.cpu() - lref).norm() / lref.norm()).item()
+# ordered two-shot all-reduce of prefill partials: 250 rows in chunks of 96 (three launches of
+# the reduce-scatter / all-gather pair), then one chunk with the next RMSNorm
+tp.prefill_rows = 96
+Tp = 250
+gp = torch.Generator().manual_seed(90 + ctx.rank)
+part = torch.randn(Tp, H, generator=gp)
+xp0 = torch.randn(Tp, H, generator=g0)
+xp = xp0.clone().to(dev)
+part_d = part.to(dev)
+tp.allreduce_rows(Tp, lambda r0, r1, out: out.copy_(part_d[r0:r1]), xp)
+torch.cuda.synchronize()
+allpp = [None] * ctx.world
+dist.all_gather_object(allpp, part, group=ctx.cpu_group)
+acc = torch.zeros(Tp, H)
+for p in allpp:  # the kernel's order: rank 0 first
+    acc = acc + p
+res["twoshot_exact"] = torch.equal(xp.cpu(), xp0 + acc)
+xn = xp0[:64].clone().to(dev)
+hn = torch.empty(64, H, dtype=torch.bfloat16, device=dev)
+tp.part_view(64).copy_(part_d[:64])
+tp.twoshot_add(xn, nw.to(dev), hn, eps)
+torch.cuda.synchronize()
+rn = (xp0[:64] + acc[:64]).double()
+hr = (rn * torch.rsqrt(rn.pow(2).mean(-1, keepdim=True) + eps) * nw.double()).float()
+res["twoshot_norm_x_exact"] = torch.equal(xn.cpu(), (xp0[:64] + acc[:64]))
+res["twoshot_h_rel"] = ((hn.float().cpu() - hr).norm() / hr.norm()).item()
 res["status"] = tp.check_status()
 print("RESULT " + json.dumps(res), flush=True)
 dist.barrier(group=ctx.cpu_group)
@@ -111,3 +139,6 @@ def test_tp_fused_paths_match_f32_reference():
             assert d[kind + "_h_rel"] < 1e-2, d
             assert d[kind + "_bitwise_equal"], d    # rank-order reduction: identical residuals
         assert d["logits_rel"] < 1e-4, d
+        # two-shot: each element summed once in rank order, so x equals the f32 sum exactly
+        assert d["twoshot_exact"] and d["twoshot_norm_x_exact"], d
+        assert d["twoshot_h_rel"] < 1e-2, d
