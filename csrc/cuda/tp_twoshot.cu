@@ -44,18 +44,38 @@ __global__ void __launch_bounds__(256) tp_twoshot_rs_kernel(TwoShotArgs a) {
   const int64_t n4 = a.n_elems / 4;
   const int64_t lo = n4 * a.rank / a.N, hi = n4 * (a.rank + 1) / a.N;  // this rank's float4 slice
   if (s_ok) {
-    for (int64_t i = lo + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < hi; i += (int64_t)gridDim.x * blockDim.x) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    // four float4 per thread in flight from every rank before any add: remote loads take
+    // microseconds, so the memory-level parallelism sets the rate
+    constexpr int U = 4;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i0 = lo + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < hi; i0 += U * stride) {
+      float4 acc[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int r = 0; r < a.N; ++r) {  // rank order: identical bits on every rank
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(a.peers[r]) +
-                                                                a.off_part) + i);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+        const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const uint8_t*>(a.peers[r]) + a.off_part);
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t i = i0 + u * stride;
+          v[u] = i < hi ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          acc[u].x += v[u].x;
+          acc[u].y += v[u].y;
+          acc[u].z += v[u].z;
+          acc[u].w += v[u].w;
+        }
       }
-      for (int r = 0; r < a.N; ++r)
-        reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(a.peers[r]) + a.off_gather)[i] = acc;
+      for (int r = 0; r < a.N; ++r) {
+        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(a.peers[r]) + a.off_gather);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t i = i0 + u * stride;
+          if (i < hi) dst[i] = acc[u];
+        }
+      }
     }
   }
   // completion of this rank's slice: the last CTA raises the done flag on every rank
@@ -90,14 +110,23 @@ __global__ void __launch_bounds__(256) tp_twoshot_add_kernel(TwoShotArgs a, floa
     if (!wait_flag(f, a.seq, a.timeout_ns, a.status, 3)) s_ok = 0;
   }
   __syncthreads();
-  const float* g = reinterpret_cast<const float*>(mine + a.off_gather) + (int64_t)t * a.H;
-  float* xr = x + (int64_t)t * a.H;
+  const float4* g = reinterpret_cast<const float4*>(mine + a.off_gather) + (int64_t)t * (a.H / 4);
+  float4* xr4 = reinterpret_cast<float4*>(x + (int64_t)t * a.H);
+  const float* xr = x + (int64_t)t * a.H;
   float ss = 0.f;
-  for (int i = threadIdx.x; i < a.H; i += blockDim.x) {
-    const float v = xr[i] + (s_ok ? __ldcg(g + i) : 0.f);
-    xr[i] = v;
-    ss += v * v;
+  for (int i = threadIdx.x; i < a.H / 4; i += blockDim.x) {
+    float4 v = xr4[i];
+    if (s_ok) {
+      const float4 d = __ldcg(g + i);
+      v.x += d.x;
+      v.y += d.y;
+      v.z += d.z;
+      v.w += d.w;
+    }
+    xr4[i] = v;
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
   }
+  __syncthreads();  // x rows are re-read by other threads for the norm below
   if (wn == nullptr) return;
   ss = block_sum(ss, red);
   const float rr = rsqrtf(ss / (float)a.H + eps);
@@ -109,7 +138,8 @@ __global__ void __launch_bounds__(256) tp_twoshot_add_kernel(TwoShotArgs a, floa
 cudaError_t launch_tp_twoshot(const TwoShotArgs& a, float* x, const float* wn, void* hout, float eps, int T,
                               cudaStream_t s) {
   if (T <= 0) return cudaSuccess;
-  if (a.N < 1 || a.N > 32 || a.H % 4 != 0 || a.n_elems != (int64_t)T * a.H || (a.off_part | a.off_gather) & 15)
+  if (a.N < 1 || a.N > 32 || a.H % 4 != 0 || a.n_elems != (int64_t)T * a.H || (a.off_part | a.off_gather) & 15 ||
+      (reinterpret_cast<uintptr_t>(x) & 15))
     return cudaErrorInvalidValue;
   static int n_sm = 0;
   if (n_sm == 0) {
@@ -118,7 +148,7 @@ cudaError_t launch_tp_twoshot(const TwoShotArgs& a, float* x, const float* wn, v
     cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
   }
   const int64_t slice4 = a.n_elems / 4 / a.N + 1;
-  const int blocks = (int)std::min<int64_t>(2 * n_sm, (slice4 + 255) / 256);
+  const int blocks = (int)std::min<int64_t>(4 * n_sm, (slice4 + 255) / 256);
   tp_twoshot_rs_kernel<<<blocks, 256, 0, s>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
