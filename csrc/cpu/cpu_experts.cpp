@@ -415,11 +415,15 @@ void expert_tiles(int mode, const uint32_t* qw, const uint16_t* sm, int K, int t
   for (int r0 = 0; r0 < nr;) {
     const int n = nr - r0;
     if (mode == 2) {
-      const int take = n >= 2 ? 2 : 1;
-      if (take == 2)
-        tiles_vnni<2, 4>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0);
-      else
-        tiles_vnni<1, 4>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0);
+      // up to four rows per pass over the weights (one pass for 3 rows is ~28 % faster than 2 + 1,
+      // for 4 rows ~18 % faster than 2 + 2); fewer row pairs per pass as rows grow (registers)
+      const int take = std::min(4, n);
+      switch (take) {
+        case 1: tiles_vnni<1, 4>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0); break;
+        case 2: tiles_vnni<2, 4>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0); break;
+        case 3: tiles_vnni<3, 2>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0); break;
+        default: tiles_vnni<4, 2>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0); break;
+      }
       r0 += take;
     } else {
       const int nb = std::min(4, n);
