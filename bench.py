@@ -125,6 +125,10 @@ def main():
                     help="speculative decoding: auto = the model's MTP head when it has one; ngram = prompt-lookup "
                          "drafts of --spec-gamma tokens verified in one batched pass (one GPU, no TP/PP)")
     ap.add_argument("--spec-gamma", type=int, default=3)
+    ap.add_argument("--prompt-kind", choices=["random", "repeat"], default="random",
+                    help="random: uniform-random token ids (the named config); repeat: a random 64-token "
+                         "pattern repeated to the prompt length (text with repetition, where prompt-lookup "
+                         "drafts apply)")
     ap.add_argument("--max-prefill-tokens", type=int, default=0,
                     help="prompt tokens per prefill step (0: 8192, or every local prompt up to 32768 tokens when "
                          "host-tier experts stream through each prefill pass)")
@@ -252,7 +256,11 @@ def main():
     mpt = args.max_prefill_tokens or (min(32768, max(8192, n_local * args.prompt)) if cache is not None else 8192)
     eng = LLMEngine(runner, max_prefill_tokens=mpt, dist_ctx=ctx, spec=spec, rebalance_every=args.rebalance_every)
     g = torch.Generator().manual_seed(1234)
-    all_prompts = [torch.randint(0, cfg.vocab, (args.prompt,), generator=g).tolist() for _ in range(args.batch)]
+    if args.prompt_kind == "repeat":
+        pats = [torch.randint(0, cfg.vocab, (64,), generator=g).tolist() for _ in range(args.batch)]
+        all_prompts = [(p * (args.prompt // 64 + 1))[:args.prompt] for p in pats]
+    else:
+        all_prompts = [torch.randint(0, cfg.vocab, (args.prompt,), generator=g).tolist() for _ in range(args.batch)]
     prompts = all_prompts[rank::world] if cfg.is_moe else all_prompts
     # ---- warm-up (untimed): one request of the timed prompt length through prefill and two
     # decode steps, so the timed prefill meets loaded kernels, encoded tensor maps and live NCCL
@@ -309,6 +317,7 @@ def main():
     runner.time_events = []
     step_events = []
     tok0, acc0, dr0 = eng.stats["decode_tokens"], eng.stats.get("spec_accepted", 0), eng.stats.get("spec_drafted", 0)
+    pz0 = eng.stats.get("spec_paused_steps", 0)
     with ClockSampler(local) as clk:
         torch.cuda.synchronize()
         te = time.perf_counter()
@@ -337,7 +346,8 @@ def main():
         acc = sum_over_ranks(ctx, float(eng.stats["spec_accepted"] - acc0))
         drf = sum_over_ranks(ctx, float(eng.stats["spec_drafted"] - dr0))
         mtp_info = {"acceptance_rate": round(acc / max(1.0, drf), 4), "drafted": int(drf), "accepted": int(acc),
-                    "tokens_per_seq_step": round(timed_tokens / (args.batch * args.steps), 4)}
+                    "tokens_per_seq_step": round(timed_tokens / (args.batch * args.steps), 4),
+                    "paused_steps": int(eng.stats.get("spec_paused_steps", 0) - pz0)}
     step_prof = None
     if args.step_profile and runner.use_graphs:
         # one decode step through the timestamped graph variant (same kernels plus one
@@ -423,7 +433,8 @@ def main():
         "metric": metric, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": f"bf16 activations, {wdesc}",
-        "data": f"synthetic uniform-random prompts, random-init N(0,0.02) weights ({wq})",
+        "data": (f"synthetic {'uniform-random' if args.prompt_kind == 'random' else 'repeated 64-token-pattern'} "
+                 f"prompts, random-init N(0,0.02) weights ({wq})"),
         "p50_ttft_ms": round(p50_ttft_ms, 2),
         "config": {"model": args.model if not args.layers else f"{args.model}[layers={args.layers}] (DEV, not headline)",
                    "global_batch": args.batch, "seq_len": args.prompt, "decode_len": decode_len,

@@ -122,7 +122,10 @@ class LLMEngine:
         self._ids = itertools.count()
         self._boot_seed = random.getrandbits(63)
         self.stats = {"prefill_steps": 0, "decode_steps": 0, "decode_tokens": 0, "prefill_tokens": 0,
-                      "spec_drafted": 0, "spec_accepted": 0, "swapped_out": 0, "swapped_in": 0}
+                      "spec_drafted": 0, "spec_accepted": 0, "spec_paused_steps": 0, "swapped_out": 0,
+                      "swapped_in": 0}
+        self._spec_pause = 0           # plain decode steps left before drafting again
+        self._spec_recent: deque = deque()  # (drafted, accepted) of recent verify steps
         self._vocab_bytes = None  # token byte strings for constrained decoding (set_tokenizer)
         self._trie = None
 
@@ -567,7 +570,16 @@ class LLMEngine:
     def _decode(self) -> list[StepOutput]:
         # Under lockstep ranks every rank runs the same verify window shape (equal live
         # sequence counts), so the expert-parallel exchanges inside it line up.
-        outs = self._decode_plain() if self.spec is None else self._decode_spec()
+        if self.spec is None:
+            outs = self._decode_plain()
+        elif self._spec_pause > 0:
+            self._spec_pause -= 1
+            self.stats["spec_paused_steps"] += 1
+            outs = self._decode_plain()
+        else:
+            d0, a0 = self.stats["spec_drafted"], self.stats["spec_accepted"]
+            outs = self._decode_spec()
+            self._spec_adapt(self.stats["spec_drafted"] - d0, self.stats["spec_accepted"] - a0)
         r = self.runner
         n = self.stats["decode_steps"]
         if r.expert_cache is not None and self.rebalance_every and n % self.rebalance_every == 0:
@@ -660,6 +672,21 @@ class LLMEngine:
             self.spec.drafter.after_verify(mtp_items)
         self._reap()
         return outs
+
+    def _spec_adapt(self, drafted: int, accepted: int):
+        """Pauses drafting for a while when recent acceptance is too low to pay for the verify
+        windows (point-mass drafters on one rank only)."""
+        sp = self.spec
+        if sp.min_accept <= 0 or self.dist is not None or hasattr(sp.drafter, "after_verify") or \
+                getattr(sp.drafter, "stochastic", False):
+            return
+        self._spec_recent.append((drafted, accepted))
+        tot = sum(d for d, _ in self._spec_recent)
+        while self._spec_recent and tot - self._spec_recent[0][0] >= sp.window:
+            tot -= self._spec_recent.popleft()[0]
+        if tot >= sp.window and sum(a for _, a in self._spec_recent) < sp.min_accept * tot:
+            self._spec_pause = sp.pause_steps
+            self._spec_recent.clear()
 
     @property
     def acceptance_rate(self) -> float:

@@ -154,6 +154,13 @@ class MTPDrafter:
 class SpecConfig:
     gamma: int = 2
     drafter: object = None
+    # adaptive pause: when fewer than min_accept of the last `window` drafted tokens were
+    # accepted, the engine takes `pause_steps` plain decode steps (a verify window costs about
+    # g + 1 rows of work for one token when nothing is accepted), then drafts again.  Not for
+    # MTP (its drafts come from the verify pass) nor under lockstep ranks.  min_accept 0: off.
+    min_accept: float = 0.1
+    window: int = 256
+    pause_steps: int = 32
 
     def __post_init__(self):
         if self.drafter is None:

@@ -73,3 +73,30 @@ def test_graph_bucket_never_exceeds_runner_rows():
             assert n <= b <= cap
             assert b in BUCKETS or b == cap
     assert bucket_for(40) == 48 and bucket_for(200) == 256
+
+
+class _WrongDrafter:
+    """Drafts that are never the model's greedy token (vocab-1 - last token)."""
+
+    def propose(self, history, g):
+        return [(1023 - history[-1]) % 1024] * g
+
+
+def test_low_acceptance_pauses_drafting_and_keeps_tokens():
+    """With drafts that are always rejected the engine stops paying for verify windows: after
+    `window` drafted tokens at low acceptance it takes `pause_steps` plain steps, then probes
+    again; the greedy tokens equal plain decoding throughout."""
+    cfg = get_config("tiny-llama")
+    mw = prepare_weights(cfg, torch.device("cpu"), seed=0)
+    prompts = [[1, 2, 3, 4, 5, 6, 7, 8], [9, 10, 11]]
+    params = SamplingParams(max_tokens=60)
+    want = LLMEngine(ModelRunner(mw, max_batch=8, max_seq_len=128)).generate(prompts, params)
+    spec = SpecConfig(gamma=3, drafter=_WrongDrafter(), window=24, pause_steps=5)
+    eng = LLMEngine(ModelRunner(mw, max_batch=8, max_seq_len=128), spec=spec)
+    assert eng.generate(prompts, params) == want
+    assert eng.stats["spec_paused_steps"] >= 5
+    assert eng.stats["spec_accepted"] <= 0.1 * eng.stats["spec_drafted"] + 6
+    # min_accept 0 turns the pause off: every step drafts
+    eng2 = LLMEngine(ModelRunner(mw, max_batch=8, max_seq_len=128),
+                     spec=SpecConfig(gamma=3, drafter=_WrongDrafter(), min_accept=0.0))
+    assert eng2.generate(prompts, params) == want and eng2.stats["spec_paused_steps"] == 0
