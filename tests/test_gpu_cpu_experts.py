@@ -22,8 +22,9 @@ def _engine(cuda, share, graphs=True, timeout_s=2.0):
     cache = ExpertCache(mw.layers, 0.5, cuda)
     runner = ModelRunner(mw, max_batch=8, max_seq_len=256, use_graphs=graphs)
     runner.expert_cache = cache
+    # mode 1 (BF16, exact products): the tokens must equal the GPU-only engine
     tier = CpuExpertTier(cache, cfg, max_rows=runner.max_batch, cpu_share=share, threads=4,
-                         timeout_s=timeout_s) if share else None
+                         timeout_s=timeout_s, mode=1) if share else None
     return LLMEngine(runner), cfg, tier
 
 

@@ -70,7 +70,10 @@ def _run_bulk(cuda, cpu_share=0.0, rebalance_every=64):
     cache = ExpertCache(mw.layers, 0.5, cuda)
     runner = ModelRunner(mw, max_batch=8, max_seq_len=256, use_graphs=True)
     runner.expert_cache = cache
-    tier = CpuExpertTier(cache, cfg, max_rows=runner.max_batch, cpu_share=cpu_share, threads=4) \
+    # the BF16 family: exact products, so the tokens must equal the GPU-only engine (the int16
+    # family rounds activations to 16 bits per block and may flip a near-tie; its error is
+    # checked against the f32 product in test_cpu_experts.py)
+    tier = CpuExpertTier(cache, cfg, max_rows=runner.max_batch, cpu_share=cpu_share, threads=4, mode=1) \
         if cpu_share else None
     assert cache.enable_decode_staging()
     g = torch.Generator().manual_seed(3)
