@@ -47,6 +47,9 @@ cudaError_t launch_rmsnorm(const void* x, bool x_bf16, const float* w, void* y, 
 // x[t] += sum_j yp[pair_of[t][j]] (pair_of sorted by expert), then y = rmsnorm(x) * w.
 // If `shared` is given it is added first (shared-expert output, f32 [T, H]).  One CTA of
 // H/4 threads per token, float4 accesses: every thread keeps top_k row loads in flight.
+// KT > 0: top_k == KT known at compile time (the pair rows are read once into registers and
+// their KT row loads issued back to back; the same summation order as the generic loop).
+template <int KT>
 __global__ void moe_combine_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ yp,
                                            const int32_t* __restrict__ pair_of, int top_k,
                                            const float* __restrict__ shared, const float* __restrict__ w,
@@ -56,7 +59,30 @@ __global__ void moe_combine_rmsnorm_kernel(float* __restrict__ x, const float* _
   float* xr = x + t * H;
   float ss = 0.f;
   const bool vec = (H % 4) == 0;
-  if (vec) {
+  if (KT > 0 && vec) {
+    const float4* rows[KT > 0 ? KT : 1];
+#pragma unroll
+    for (int j = 0; j < KT; ++j)
+      rows[j] = reinterpret_cast<const float4*>(yp + (int64_t)__ldg(pair_of + t * KT + j) * H);
+    for (int i4 = threadIdx.x; i4 < H / 4; i4 += blockDim.x) {
+      float4 v[KT > 0 ? KT : 1];
+#pragma unroll
+      for (int j = 0; j < KT; ++j) v[j] = __ldg(rows[j] + i4);
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int j = 0; j < KT; ++j) {
+        acc.x += v[j].x; acc.y += v[j].y; acc.z += v[j].z; acc.w += v[j].w;
+      }
+      if (shared) {
+        const float4 u = reinterpret_cast<const float4*>(shared + t * H)[i4];
+        acc.x += u.x; acc.y += u.y; acc.z += u.z; acc.w += u.w;
+      }
+      float4 xv = reinterpret_cast<float4*>(xr)[i4];
+      xv.x += acc.x; xv.y += acc.y; xv.z += acc.z; xv.w += acc.w;
+      reinterpret_cast<float4*>(xr)[i4] = xv;
+      ss += xv.x * xv.x + xv.y * xv.y + xv.z * xv.z + xv.w * xv.w;
+    }
+  } else if (vec) {
     for (int i4 = threadIdx.x; i4 < H / 4; i4 += blockDim.x) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int j = 0; j < top_k; ++j) {
@@ -93,8 +119,12 @@ cudaError_t launch_moe_combine_rmsnorm(float* x, const float* yp, const int32_t*
                                        cudaStream_t s) {
   if (T == 0) return cudaSuccess;
   const int threads = H % 4 == 0 ? std::min(1024, std::max(128, ((H / 4 + 31) / 32) * 32)) : 256;
-  moe_combine_rmsnorm_kernel<<<T, threads, 0, s>>>(x, yp, pair_of, top_k, shared, w,
-                                                   reinterpret_cast<__nv_bfloat16*>(y), H, eps);
+  if (top_k == 8)
+    moe_combine_rmsnorm_kernel<8><<<T, threads, 0, s>>>(x, yp, pair_of, top_k, shared, w,
+                                                        reinterpret_cast<__nv_bfloat16*>(y), H, eps);
+  else
+    moe_combine_rmsnorm_kernel<0><<<T, threads, 0, s>>>(x, yp, pair_of, top_k, shared, w,
+                                                        reinterpret_cast<__nv_bfloat16*>(y), H, eps);
   return cudaGetLastError();
 }
 
@@ -108,7 +138,7 @@ __global__ void qk_rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, i
                                         const float* __restrict__ sin_t, const int64_t* __restrict__ slot,
                                         __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_cache,
                                         __nv_bfloat16* __restrict__ v_cache, int block_size) {
-  constexpr int PER = D / 64;  // elements per lane per half
+  constexpr int PER = D / 64;  // elements per lane per half (1 or 2: one 2- or 4-byte access)
   const int t = blockIdx.x;
   const int lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
@@ -116,18 +146,32 @@ __global__ void qk_rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, i
   const int p = pos[t];
   const int64_t sl = slot[t];
   const int64_t blk = sl / block_size, off = sl % block_size;
+  // per-lane constants of the token, loaded once for all its heads: rotation and norm weights
+  float cs[PER], sn[PER], wq_lo[PER], wq_hi[PER], wk_lo[PER], wk_hi[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int j = lane * PER + i;
+    cs[i] = cos_t[(int64_t)p * (D / 2) + j];
+    sn[i] = sin_t[(int64_t)p * (D / 2) + j];
+    wq_lo[i] = qn ? qn[j] : 1.f;
+    wq_hi[i] = qn ? qn[D / 2 + j] : 1.f;
+    wk_lo[i] = kn ? kn[j] : 1.f;
+    wk_hi[i] = kn ? kn[D / 2 + j] : 1.f;
+  }
   for (int h = threadIdx.x >> 5; h < nh; h += nwarps) {
     const __nv_bfloat16* src = qkv + ((int64_t)t * nh + h) * D;
     float lo[PER], hi[PER];
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      lo[i] = bf2f(src[lane * PER + i]);
-      hi[i] = bf2f(src[D / 2 + lane * PER + i]);
+    if constexpr (PER == 2) {
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + lane * 2));
+      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src + D / 2 + lane * 2));
+      lo[0] = a.x, lo[1] = a.y, hi[0] = b.x, hi[1] = b.y;
+    } else {
+      lo[0] = bf2f(src[lane]);
+      hi[0] = bf2f(src[D / 2 + lane]);
     }
     const bool is_q = h < Hq, is_k = !is_q && h < Hq + Hkv;
     if (is_q || is_k) {
-      const float* nw = is_q ? qn : kn;
-      if (nw) {
+      if (is_q ? qn != nullptr : kn != nullptr) {
         float ss = 0.f;
 #pragma unroll
         for (int i = 0; i < PER; ++i) ss += lo[i] * lo[i] + hi[i] * hi[i];
@@ -135,17 +179,15 @@ __global__ void qk_rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, i
         const float r = rsqrtf(ss / (float)D + eps);
 #pragma unroll
         for (int i = 0; i < PER; ++i) {
-          lo[i] = lo[i] * r * nw[lane * PER + i];
-          hi[i] = hi[i] * r * nw[D / 2 + lane * PER + i];
+          lo[i] = lo[i] * r * (is_q ? wq_lo[i] : wk_lo[i]);
+          hi[i] = hi[i] * r * (is_q ? wq_hi[i] : wk_hi[i]);
         }
       }
 #pragma unroll
       for (int i = 0; i < PER; ++i) {
-        const int j = lane * PER + i;
-        const float c = cos_t[(int64_t)p * (D / 2) + j], s = sin_t[(int64_t)p * (D / 2) + j];
         const float a = lo[i], b = hi[i];
-        lo[i] = a * c - b * s;
-        hi[i] = b * c + a * s;
+        lo[i] = a * cs[i] - b * sn[i];
+        hi[i] = b * cs[i] + a * sn[i];
       }
     }
     __nv_bfloat16* dst;
@@ -157,10 +199,12 @@ __global__ void qk_rope_kv_write_kernel(const __nv_bfloat16* __restrict__ qkv, i
       if (sl < 0) continue;  // padded row: no cache write
       dst = cache + (((blk * Hkv + kh) * block_size) + off) * D;
     }
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      dst[lane * PER + i] = f2bf(lo[i]);
-      dst[D / 2 + lane * PER + i] = f2bf(hi[i]);
+    if constexpr (PER == 2) {
+      *reinterpret_cast<__nv_bfloat162*>(dst + lane * 2) = __floats2bfloat162_rn(lo[0], lo[1]);
+      *reinterpret_cast<__nv_bfloat162*>(dst + D / 2 + lane * 2) = __floats2bfloat162_rn(hi[0], hi[1]);
+    } else {
+      dst[lane] = f2bf(lo[0]);
+      dst[D / 2 + lane] = f2bf(hi[0]);
     }
   }
 }

@@ -311,3 +311,23 @@ def test_verify_accept_matches_host_oracle(cuda, stochastic):
     for s in range(S):
         k = int(n_r[s]) + 1
         assert tok_d[s, :k].tolist() == tok_r[s, :k].tolist(), s
+
+
+@pytest.mark.parametrize("k", [8, 6])
+def test_moe_combine_rmsnorm_matches_reference(cuda, k):
+    """Ordered combine of the top-k pair rows (+ shared expert) into the residual, then the next
+    RMSNorm: top-8 (indices read once, the eight row loads issued together) and the generic
+    loop; the residual equals the host's same-order f32 sum bit for bit."""
+    torch.manual_seed(k)
+    T, H = 37, 4096
+    yp = torch.randn(T * k, H)
+    pair_of = torch.randperm(T * k).view(T, k).to(torch.int32)
+    shared = torch.randn(T, H)
+    w = torch.rand(H) + 0.5
+    x = torch.randn(T, H)
+    xd, out = x.clone().to(cuda), torch.empty(T, H, dtype=torch.bfloat16, device=cuda)
+    ops.moe_combine_rmsnorm(xd, yp.to(cuda), pair_of.to(cuda), shared.to(cuda), w.to(cuda), out, 1e-6)
+    xr, outr = x.clone(), torch.empty(T, H)
+    ops.moe_combine_rmsnorm(xr, yp, pair_of, shared, w, outr, 1e-6)
+    assert torch.equal(xd.cpu(), xr)
+    assert _rel(out.float().cpu(), outr) < 1e-2
