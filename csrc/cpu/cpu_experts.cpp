@@ -346,6 +346,59 @@ bool has_vnni() {
 }
 bool simd_ok() { return has_bf16() || has_vnni(); }
 
+// Issue cost of the dot-product instructions the two families rest on (ns per instruction, eight
+// independent accumulator chains, zmm forms): vdpbf16ps, vfmadd231ps, vpdpwssd, vpdpbusd.
+// A probe of the host (the figures behind the family choice); -1 where the ISA is missing.
+__attribute__((target("avx512f,avx512bw,avx512vl,avx512bf16,avx512vnni"))) static double time_bf16(long n) {
+  __m512 a[8];
+  for (int i = 0; i < 8; ++i) a[i] = _mm512_set1_ps((float)i);
+  __m512i x = _mm512_set1_epi32(0x3f803f80), w = _mm512_set1_epi32(0x3f003f00);
+  const uint64_t t0 = now_ns();
+  for (long i = 0; i < n; ++i) {
+#pragma GCC unroll 8
+    for (int j = 0; j < 8; ++j) a[j] = _mm512_dpbf16_ps(a[j], (__m512bh)x, (__m512bh)w);
+    asm volatile("" : "+v"(x));
+  }
+  const uint64_t t1 = now_ns();
+  float s = 0.f;
+  for (int i = 0; i < 8; ++i) s += _mm512_reduce_add_ps(a[i]);
+  asm volatile("" ::"x"(s));
+  return (double)(t1 - t0) / (8.0 * n);
+}
+__attribute__((target("avx512f,fma"))) static double time_fma(long n) {
+  __m512 a[8];
+  for (int i = 0; i < 8; ++i) a[i] = _mm512_set1_ps((float)i);
+  __m512 y = _mm512_set1_ps(0.999f), z = _mm512_set1_ps(0.5f);
+  const uint64_t t0 = now_ns();
+  for (long i = 0; i < n; ++i) {
+#pragma GCC unroll 8
+    for (int j = 0; j < 8; ++j) a[j] = _mm512_fmadd_ps(a[j], y, z);
+    asm volatile("" : "+v"(y));
+  }
+  const uint64_t t1 = now_ns();
+  float s = 0.f;
+  for (int i = 0; i < 8; ++i) s += _mm512_reduce_add_ps(a[i]);
+  asm volatile("" ::"x"(s));
+  return (double)(t1 - t0) / (8.0 * n);
+}
+template <bool BYTES>
+__attribute__((target("avx512f,avx512bw,avx512vnni"))) static double time_vnni(long n) {
+  __m512i a[8];
+  for (int i = 0; i < 8; ++i) a[i] = _mm512_set1_epi32(i);
+  __m512i u = _mm512_set1_epi32(0x01010101), v = _mm512_set1_epi32(0x02020202);
+  const uint64_t t0 = now_ns();
+  for (long i = 0; i < n; ++i) {
+#pragma GCC unroll 8
+    for (int j = 0; j < 8; ++j) a[j] = BYTES ? _mm512_dpbusd_epi32(a[j], u, v) : _mm512_dpwssd_epi32(a[j], u, v);
+    asm volatile("" : "+v"(u));
+  }
+  const uint64_t t1 = now_ns();
+  long s = 0;
+  for (int i = 0; i < 8; ++i) s += _mm512_reduce_add_epi32(a[i]);
+  asm volatile("" ::"r"(s));
+  return (double)(t1 - t0) / (8.0 * n);
+}
+
 // Which SIMD family is faster depends on the host: on some Xeons `vdpbf16ps` issues at about a
 // quarter of the FMA rate, so the int16 VNNI form (two `vpdpwssd` per pair of columns, exact
 // integer sums) wins by ~1.4x; where bf16 dot products are cheap the BF16 form saves the
@@ -403,6 +456,17 @@ int pick_mode(int want) {
   if (want == 1 && !has_bf16()) want = has_vnni() ? 2 : 0;
   if (want == 2 && !has_vnni()) want = has_bf16() ? 1 : 0;
   return want;
+}
+
+std::vector<double> isa_rates(long n) {
+  std::vector<double> r(4, -1.0);
+  if (has_bf16()) r[0] = time_bf16(n);
+  if (__builtin_cpu_supports("avx512f") && __builtin_cpu_supports("fma")) r[1] = time_fma(n);
+  if (has_vnni()) {
+    r[2] = time_vnni<false>(n);
+    r[3] = time_vnni<true>(n);
+  }
+  return r;
 }
 
 // Packs one activation row for `mode` (ab: [K/64][32] pairs, sxs: [K/64][16] VNNI scales,
@@ -863,6 +927,9 @@ void register_cpu_experts(pybind11::module& m) {
         pybind11::call_guard<pybind11::gil_scoped_release>());
   m.def("cpu_simd_available", [] { return simd_ok(); });
   m.def("cpu_gemv_mode", [] { return pick_mode(-1); }, "default kernel family: 0 C++, 1 AVX-512 BF16, 2 VNNI");
+  m.def("cpu_isa_rates", [](int64_t n) { return isa_rates((long)n); }, pybind11::arg("n") = 20000000,
+        "ns per instruction (8 chains): vdpbf16ps, vfmadd231ps, vpdpwssd, vpdpbusd (-1: not supported)",
+        pybind11::call_guard<pybind11::gil_scoped_release>());
   m.def("cpu_mailbox_bytes", [](int64_t E, int64_t k, int64_t R, int64_t H) {
     const CpuMailboxLayout l = cpu_mailbox_layout(E, k, R, H);
     return std::vector<int64_t>{l.tok_off, l.tok_idx, l.pair_w, l.h, l.out_pairs, l.out, l.bytes};

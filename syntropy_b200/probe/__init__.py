@@ -66,6 +66,10 @@ def probe_cpu_experts(threads: int | None = None, seconds: float = 1.0) -> dict:
         n += 1
     per_thread = n * nbytes / (time.perf_counter() - t0) / 1e9
     out["cpu_expert_gbs_per_thread"] = round(per_thread, 2)
+    out["cpu_gemv_mode"] = e.cpu_gemv_mode()
+    rates = e.cpu_isa_rates(5_000_000)
+    out["isa_ns_per_instr"] = {k: round(v, 3) for k, v in
+                               zip(("vdpbf16ps", "vfmadd231ps", "vpdpwssd", "vpdpbusd"), rates) if v >= 0}
     out["cpu_expert_gbs"] = round(min(per_thread * threads, out["cpu_read_gbs"]), 1)
     del threading
     return out
