@@ -147,6 +147,12 @@ void pack_row_i16(const uint16_t* x, int K, uint32_t* ab, float* sxs, float* sx4
   }
 }
 
+// narrower int16 passes (4 / 2 row pairs) instead of 8 / 4: SYN_CPU_NARROW=1 (measurement)
+const bool g_narrow_passes = [] {
+  const char* e = getenv("SYN_CPU_NARROW");
+  return e && atoi(e) == 1;
+}();
+
 // 64-column groups the int16 kernel prefetches ahead: 16 (8 KB of the tile) measured best with
 // 14 workers streaming from DRAM (SYN_CPU_PREFETCH overrides, measurement)
 const int g_prefetch_groups = [] {
@@ -491,12 +497,23 @@ void expert_tiles(int mode, const uint32_t* qw, const uint16_t* sm, int K, int t
     if (mode == 2) {
       // up to four rows per pass over the weights (one pass for 3 rows is ~28 % faster than 2 + 1,
       // for 4 rows ~18 % faster than 2 + 2); fewer row pairs per pass as rows grow (registers)
+      // row pairs per pass: all 8 for 1-2 rows (each 512-byte group of the tile streamed whole),
+      // 4 for 3-4 rows (registers); SYN_CPU_NARROW=1 keeps the narrower passes (measurement)
       const int take = std::min(4, n);
-      switch (take) {
-        case 1: tiles_vnni<1, 4>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0); break;
-        case 2: tiles_vnni<2, 4>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0); break;
-        case 3: tiles_vnni<3, 2>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0); break;
-        default: tiles_vnni<4, 2>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0); break;
+      if (g_narrow_passes) {
+        switch (take) {
+          case 1: tiles_vnni<1, 4>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0); break;
+          case 2: tiles_vnni<2, 4>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0); break;
+          case 3: tiles_vnni<3, 2>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0); break;
+          default: tiles_vnni<4, 2>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0); break;
+        }
+      } else {
+        switch (take) {
+          case 1: tiles_vnni<1, 8>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0); break;
+          case 2: tiles_vnni<2, 8>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0); break;
+          case 3: tiles_vnni<3, 4>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0); break;
+          default: tiles_vnni<4, 4>(qw, sm, K, t0, t1, ab + r0, sxs + r0, sx4 + r0, y + r0, scale + r0); break;
+        }
       }
       r0 += take;
     } else {
