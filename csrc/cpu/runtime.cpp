@@ -242,6 +242,130 @@ py::tuple token_decode_py(py::bytes buf) {
   return py::make_tuple(0, spec_to(fs), out);
 }
 
+static uint8_t rows_dtype(const torch::Tensor& rows) {
+  TORCH_CHECK(!rows.is_cuda() && rows.is_contiguous() && rows.dim() == 2, "rows: contiguous host tensor [n, width]");
+  const uint8_t d = rows.scalar_type() == torch::kFloat32 ? 1 : rows.scalar_type() == torch::kBFloat16 ? 2 : 0;
+  TORCH_CHECK(d, "rows dtype must be f32 or bf16");
+  return d;
+}
+static torch::Tensor rows_tensor(const std::vector<uint8_t>& rows, uint32_t n, uint32_t width, uint8_t dtype) {
+  auto t = torch::empty({(int64_t)n, (int64_t)width}, dtype == 1 ? torch::kFloat32 : torch::kBFloat16);
+  if (!rows.empty()) memcpy(t.data_ptr(), rows.data(), rows.size());
+  return t;
+}
+
+// Collective: hdr {phase, member, n_members, layer, row_offset, epoch}; rows [n, width]
+py::bytes collective_encode_py(py::dict frame, py::dict hdr, torch::Tensor rows) {
+  CollectiveHeader h;
+  h.dtype = rows_dtype(rows);
+  h.phase = (uint8_t)py::cast<int64_t>(hdr["phase"]);
+  h.member = (uint16_t)py::cast<int64_t>(hdr["member"]);
+  h.n_members = (uint16_t)py::cast<int64_t>(hdr["n_members"]);
+  TORCH_CHECK(h.n_members > 0 && h.member < h.n_members, "member outside the group");
+  h.layer = (uint32_t)py::cast<int64_t>(hdr["layer"]);
+  h.row_offset = hdr.contains("row_offset") ? (uint32_t)py::cast<int64_t>(hdr["row_offset"]) : 0;
+  h.epoch = hdr.contains("epoch") ? (uint32_t)py::cast<int64_t>(hdr["epoch"]) : 0;
+  h.n_rows = (uint32_t)rows.size(0);
+  h.width = (uint32_t)rows.size(1);
+  return py::bytes(collective_encode(spec_from(frame), h, reinterpret_cast<const uint8_t*>(rows.data_ptr())));
+}
+
+py::tuple collective_decode_py(py::bytes buf) {
+  std::string b = buf;
+  FrameSpec fs;
+  CollectiveHeader h;
+  std::vector<uint8_t> rows;
+  const int rc = collective_decode(reinterpret_cast<const uint8_t*>(b.data()), b.size(), &fs, &h, &rows);
+  if (rc != 0) return py::make_tuple(rc, py::none(), py::none(), py::none());
+  py::dict hd;
+  hd["phase"] = h.phase;
+  hd["member"] = h.member;
+  hd["n_members"] = h.n_members;
+  hd["layer"] = h.layer;
+  hd["row_offset"] = h.row_offset;
+  hd["epoch"] = h.epoch;
+  return py::make_tuple(0, spec_to(fs), hd, rows_tensor(rows, h.n_rows, h.width, h.dtype));
+}
+
+static EpHeader ep_header_from(py::dict hdr, const torch::Tensor& rows) {
+  EpHeader h;
+  h.src_rank = (uint16_t)py::cast<int64_t>(hdr["src_rank"]);
+  h.dst_rank = (uint16_t)py::cast<int64_t>(hdr["dst_rank"]);
+  h.layer = (uint32_t)py::cast<int64_t>(hdr["layer"]);
+  h.epoch = hdr.contains("epoch") ? (uint32_t)py::cast<int64_t>(hdr["epoch"]) : 0;
+  h.n_rows = (uint32_t)rows.size(0);
+  h.hidden = (uint32_t)rows.size(1);
+  return h;
+}
+static py::dict ep_header_to(const EpHeader& h) {
+  py::dict hd;
+  hd["src_rank"] = h.src_rank;
+  hd["dst_rank"] = h.dst_rank;
+  hd["layer"] = h.layer;
+  hd["epoch"] = h.epoch;
+  hd["top_k"] = h.top_k;
+  return hd;
+}
+
+// routes: per row (source row, [(expert, weight)...]) with at most top_k routes
+py::bytes ep_dispatch_encode_py(py::dict frame, py::dict hdr,
+                                std::vector<std::tuple<int64_t, std::vector<std::tuple<int64_t, double>>>> routes,
+                                torch::Tensor rows) {
+  EpHeader h = ep_header_from(hdr, rows);
+  h.dtype = rows_dtype(rows);
+  h.top_k = (uint8_t)py::cast<int64_t>(hdr["top_k"]);
+  TORCH_CHECK(h.top_k > 0 && routes.size() == h.n_rows, "one route record per row, top_k > 0");
+  std::vector<EpRoute> rs;
+  for (const auto& t : routes) {
+    EpRoute e;
+    e.row = (uint32_t)std::get<0>(t);
+    TORCH_CHECK(!std::get<1>(t).empty() && std::get<1>(t).size() <= h.top_k, "1..top_k routes per row");
+    for (const auto& r : std::get<1>(t)) {
+      e.experts.push_back((uint16_t)std::get<0>(r));
+      e.weights.push_back((float)std::get<1>(r));
+    }
+    rs.push_back(std::move(e));
+  }
+  return py::bytes(ep_dispatch_encode(spec_from(frame), h, rs, reinterpret_cast<const uint8_t*>(rows.data_ptr())));
+}
+
+py::tuple ep_dispatch_decode_py(py::bytes buf) {
+  std::string b = buf;
+  FrameSpec fs;
+  EpHeader h;
+  std::vector<EpRoute> rs;
+  std::vector<uint8_t> rows;
+  const int rc = ep_dispatch_decode(reinterpret_cast<const uint8_t*>(b.data()), b.size(), &fs, &h, &rs, &rows);
+  if (rc != 0) return py::make_tuple(rc, py::none(), py::none(), py::none(), py::none());
+  py::list rl;
+  for (const auto& e : rs) {
+    py::list r;
+    for (size_t j = 0; j < e.experts.size(); ++j) r.append(py::make_tuple(e.experts[j], e.weights[j]));
+    rl.append(py::make_tuple(e.row, r));
+  }
+  return py::make_tuple(0, spec_to(fs), ep_header_to(h), rl, rows_tensor(rows, h.n_rows, h.hidden, h.dtype));
+}
+
+py::bytes ep_combine_encode_py(py::dict frame, py::dict hdr, std::vector<int64_t> row_ids, torch::Tensor rows) {
+  TORCH_CHECK(rows_dtype(rows) == 1, "combine rows are f32");
+  EpHeader h = ep_header_from(hdr, rows);
+  TORCH_CHECK(row_ids.size() == h.n_rows, "one source row id per row");
+  std::vector<uint32_t> ids(row_ids.begin(), row_ids.end());
+  return py::bytes(ep_combine_encode(spec_from(frame), h, ids, reinterpret_cast<const uint8_t*>(rows.data_ptr())));
+}
+
+py::tuple ep_combine_decode_py(py::bytes buf) {
+  std::string b = buf;
+  FrameSpec fs;
+  EpHeader h;
+  std::vector<uint32_t> ids;
+  std::vector<uint8_t> rows;
+  const int rc = ep_combine_decode(reinterpret_cast<const uint8_t*>(b.data()), b.size(), &fs, &h, &ids, &rows);
+  if (rc != 0) return py::make_tuple(rc, py::none(), py::none(), py::none(), py::none());
+  std::vector<int64_t> out(ids.begin(), ids.end());
+  return py::make_tuple(0, spec_to(fs), ep_header_to(h), out, rows_tensor(rows, h.n_rows, h.hidden, 1));
+}
+
 int64_t crc32c_py(py::bytes b) {
   std::string s = b;
   return crc32c(reinterpret_cast<const uint8_t*>(s.data()), s.size());
@@ -463,6 +587,12 @@ void register_runtime(py::module& m) {
   m.def("frame_decode", &frame_decode_py);
   m.def("crc32c", &crc32c_py);
   m.def("activation_encode", &activation_encode_py);
+  m.def("collective_encode", &collective_encode_py);
+  m.def("collective_decode", &collective_decode_py);
+  m.def("ep_dispatch_encode", &ep_dispatch_encode_py);
+  m.def("ep_dispatch_decode", &ep_dispatch_decode_py);
+  m.def("ep_combine_encode", &ep_combine_encode_py);
+  m.def("ep_combine_decode", &ep_combine_decode_py);
   m.def("activation_decode", &activation_decode_py);
   m.def("token_encode", &token_encode_py);
   m.def("token_decode", &token_decode_py);

@@ -1,12 +1,17 @@
-"""Activation and Token frames (data-plane payloads on the 64-byte frame header): the native
-codecs of csrc/include/syn/payload.h, with Python-side conveniences.
+"""Data-plane payloads on the 64-byte frame header: the native codecs of
+csrc/include/syn/payload.h, with Python-side conveniences.
 
 * Activation: hidden-state rows passed from one pipeline stage to the next (kind prefill /
   decode / verify / replay / canary), the spans of sequences they belong to, and a chunk split
   into parts at row boundaries when it exceeds a frame size limit.
 * Token: sampled tokens per sequence, with a finished flag and a finish-reason code.
+* Collective: one member's part of a group reduction or gather (phase, layer, member, rows).
+* EP dispatch / combine: rows sent to the owner of some of their experts with a route record
+  per row (source row, experts, weights), and the owner's weighted f32 sums sent back.
 
-Reference: crates/net/src/frame/activation.rs:82-482, crates/net/src/frame/token.rs.
+Reference: crates/net/src/frame/activation.rs:82-482, crates/net/src/frame/token.rs,
+crates/net/src/frame/collective.rs:1-40, crates/net/src/frame/ep.rs:1-50 (semantics; the
+extension and payload layouts here are this framework's own).
 """
 from __future__ import annotations
 
@@ -98,3 +103,71 @@ def decode_tokens(buf: bytes) -> tuple[dict, list]:
         raise FrameError(rc)
     inv = {v: k for k, v in REASONS.items()}
     return spec, [(seq, toks, bool(fl & FINISHED), inv.get(fl >> 8)) for seq, toks, fl in entries]
+
+
+PHASES = {"attn_allreduce": 1, "ffn_allreduce": 2, "exit_gather": 3, "logits_gather": 4}
+
+
+def encode_collective(rows: torch.Tensor, phase: str, member: int, n_members: int, layer: int,
+                      row_offset: int = 0, epoch: int = 0, step: int = 0, chan_seq: int = 0,
+                      instance: int = 0) -> bytes:
+    """rows: [n, width] f32 or bf16, this member's part (rows from row_offset)."""
+    return ext().collective_encode({"instance": instance, "step": step, "chan_seq": chan_seq},
+                                   {"phase": PHASES[phase], "member": member, "n_members": n_members,
+                                    "layer": layer, "row_offset": row_offset, "epoch": epoch},
+                                   rows.detach().to("cpu").contiguous())
+
+
+def decode_collective(buf: bytes) -> tuple[dict, dict, torch.Tensor]:
+    rc, spec, hdr, rows = ext().collective_decode(buf)
+    if rc:
+        raise FrameError(rc)
+    inv = {v: k for k, v in PHASES.items()}
+    hdr["phase"] = inv.get(hdr["phase"], hdr["phase"])
+    return spec, hdr, rows
+
+
+def reduce_collective(frames: list[bytes]) -> torch.Tensor:
+    """Sum of the members' rows of one reduction in member order (identical bits whatever
+    order the frames arrived in)."""
+    dec = sorted((decode_collective(f) for f in frames), key=lambda d: d[1]["member"])
+    n = dec[0][1]["n_members"] if dec else 0
+    if [d[1]["member"] for d in dec] != list(range(n)) or len({d[1]["layer"] for d in dec}) != 1:
+        raise FrameError(13)
+    acc = dec[0][2].float().clone()
+    for _, _, r in dec[1:]:
+        acc += r.float()
+    return acc
+
+
+def encode_ep_dispatch(rows: torch.Tensor, routes: list[tuple[int, list[tuple[int, float]]]], src_rank: int,
+                       dst_rank: int, layer: int, top_k: int, epoch: int = 0, step: int = 0, chan_seq: int = 0,
+                       instance: int = 0) -> bytes:
+    """rows [n, hidden] (bf16 or f32); routes: per row (source row, [(expert, weight)])."""
+    return ext().ep_dispatch_encode({"instance": instance, "step": step, "chan_seq": chan_seq},
+                                    {"src_rank": src_rank, "dst_rank": dst_rank, "layer": layer, "top_k": top_k,
+                                     "epoch": epoch},
+                                    [(int(r), [(int(e), float(w)) for e, w in rt]) for r, rt in routes],
+                                    rows.detach().to("cpu").contiguous())
+
+
+def decode_ep_dispatch(buf: bytes) -> tuple[dict, dict, list, torch.Tensor]:
+    rc, spec, hdr, routes, rows = ext().ep_dispatch_decode(buf)
+    if rc:
+        raise FrameError(rc)
+    return spec, hdr, [(r, [tuple(x) for x in rt]) for r, rt in routes], rows
+
+
+def encode_ep_combine(rows: torch.Tensor, row_ids: list[int], src_rank: int, dst_rank: int, layer: int,
+                      epoch: int = 0, step: int = 0, chan_seq: int = 0, instance: int = 0) -> bytes:
+    """rows [n, hidden] f32: the owner's weighted sum over its experts for each source row."""
+    return ext().ep_combine_encode({"instance": instance, "step": step, "chan_seq": chan_seq},
+                                   {"src_rank": src_rank, "dst_rank": dst_rank, "layer": layer, "epoch": epoch},
+                                   [int(i) for i in row_ids], rows.detach().to("cpu").float().contiguous())
+
+
+def decode_ep_combine(buf: bytes) -> tuple[dict, dict, list, torch.Tensor]:
+    rc, spec, hdr, ids, rows = ext().ep_combine_decode(buf)
+    if rc:
+        raise FrameError(rc)
+    return spec, hdr, list(ids), rows

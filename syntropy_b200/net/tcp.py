@@ -124,15 +124,39 @@ class TcpChannel:
         from .frames import encode_tokens
         return self._send_raw(lambda seq: encode_tokens(entries, step=step, chan_seq=seq, instance=self.instance))
 
+    def send_collective(self, rows, phase: str, member: int, n_members: int, layer: int, step: int = 0, **kw):
+        """This member's part of a group reduction or gather as one Collective frame."""
+        from .frames import encode_collective
+        return self._send_raw(lambda seq: encode_collective(rows, phase, member, n_members, layer, step=step,
+                                                            chan_seq=seq, instance=self.instance, **kw))
+
+    def send_ep_dispatch(self, rows, routes, src_rank: int, dst_rank: int, layer: int, top_k: int, step: int = 0):
+        """Rows for the owner of some of their experts, with their route records."""
+        from .frames import encode_ep_dispatch
+        return self._send_raw(lambda seq: encode_ep_dispatch(rows, routes, src_rank, dst_rank, layer, top_k,
+                                                             step=step, chan_seq=seq, instance=self.instance))
+
+    def send_ep_combine(self, rows, row_ids, src_rank: int, dst_rank: int, layer: int, step: int = 0):
+        """The owner's weighted f32 sums, back to the rows' source rank."""
+        from .frames import encode_ep_combine
+        return self._send_raw(lambda seq: encode_ep_combine(rows, row_ids, src_rank, dst_rank, layer, step=step,
+                                                            chan_seq=seq, instance=self.instance))
+
     def recv_payload(self):
         """Next data frame decoded by its payload codec: ("activation", (spec, header, spans, rows)),
-        ("tokens", (spec, entries)) or (frame type, (spec, ext, payload)) for other types."""
-        from .frames import decode_activation, decode_tokens
+        ("tokens", (spec, entries)), ("collective", (spec, header, rows)), ("ep_dispatch", (spec,
+        header, routes, rows)), ("ep_combine", (spec, header, row ids, rows)), or (frame type,
+        (spec, ext, payload)) for other types."""
+        from . import frames
         ft, spec, x, p = self.recv()
-        if ft == FrameType.ACTIVATION:
-            return "activation", decode_activation(self.last_frame)
-        if ft == FrameType.TOKEN:
-            return "tokens", decode_tokens(self.last_frame)
+        decoders = {FrameType.ACTIVATION: ("activation", frames.decode_activation),
+                    FrameType.TOKEN: ("tokens", frames.decode_tokens),
+                    FrameType.COLLECTIVE: ("collective", frames.decode_collective),
+                    FrameType.EP_DISPATCH: ("ep_dispatch", frames.decode_ep_dispatch),
+                    FrameType.EP_COMBINE: ("ep_combine", frames.decode_ep_combine)}
+        if ft in decoders:
+            name, dec = decoders[ft]
+            return name, dec(self.last_frame)
         return ft, (spec, x, p)
 
     def grant(self, n: int = 1):
