@@ -48,6 +48,10 @@ CPU_GBS_PER_THREAD = {1: 4.8, 2: 7.5}
 # instruction throughput, so the model caps a rank's pool there.
 CPU_GBS_PER_RANK_SHARED = 57.0
 PCIE_GBS_ALONE, PCIE_GBS_SHARED = 45.0, 55.0
+# Eight ranks per node: GPU pairs share a host link; EP8 staged 7.76 GB per rank in 305 ms
+# (~25 GB/s per rank) on the B200 node.  (Four ranks balanced at the EP2 rate: share 0.49 gave
+# 93.2 tok/s against 88.1 / 90.0 at 0.62 / 0.75.)
+PCIE_GBS_PAIRED = 25.0
 
 
 def rank_cpus(local_rank: int, local_world: int, allowed: list[int] | None = None) -> tuple[list[int], list[int]]:
@@ -75,7 +79,7 @@ def balanced_share(threads: int, local_world: int, mode: int | None = None) -> f
     cpu = threads * CPU_GBS_PER_THREAD.get(mode, 0.5)
     if local_world > 1:
         cpu = min(cpu, CPU_GBS_PER_RANK_SHARED)
-    pcie = PCIE_GBS_ALONE if local_world <= 1 else PCIE_GBS_SHARED
+    pcie = PCIE_GBS_ALONE if local_world <= 1 else PCIE_GBS_SHARED if local_world <= 4 else PCIE_GBS_PAIRED
     return round(cpu / (cpu + pcie), 2)
 
 
