@@ -53,7 +53,8 @@ class SwapStore:
 
     def _spill(self, e: SwapEntry):
         from ..store.pack import write_pack
-        path = os.path.join(self.spill_dir, f"kv_{e.key}.pack")
+        # unique per process and store: several engines may share one spill directory
+        path = os.path.join(self.spill_dir, f"kv_{os.getpid()}_{id(self):x}_{e.key}.pack")
         write_pack(path, {f"l{i}": t for i, t in enumerate(e.layers)})
         self.host_bytes -= e.nbytes
         self.disk_bytes += e.nbytes

@@ -102,4 +102,4 @@ def test_swap_store_tiers_and_digest(tmp_path):
     with pytest.raises(ValueError, match="digest"):
         st2.take(ec)
     st2.drop(ec)
-    assert not list(tmp_path.glob("kv_3*"))
+    assert not list(tmp_path.glob("*.pack*"))
