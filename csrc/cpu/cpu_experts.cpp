@@ -210,7 +210,7 @@ __attribute__((target("avx512f,avx512bw,avx512vl,avx512vnni,f16c,fma"))) void ti
           xs[r] = _mm512_loadu_ps(sxs[r] + kg * 16);
         }
         const uint16_t* s = st + kg * 64;
-#pragma unroll
+#pragma GCC unroll 8
         for (int gg = 0; gg < GB; ++gg) {
           const int g = g0 + gg;
           const __m512 Flo = _mm512_cvtph_ps(_mm256_loadu_si256(reinterpret_cast<const __m256i*>(s + 16 * (g >> 2))));
