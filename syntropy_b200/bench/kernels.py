@@ -169,12 +169,12 @@ def main():
         cl = torch.full((T,), ctx, dtype=torch.int32, device=dev)
         q = torch.randn(T, Hq, D, device=dev).to(torch.bfloat16)
         out = torch.empty_like(q)
-        pps = 16
-        ns = (bt.shape[1] + pps - 1) // pps
-        po = torch.empty(T * Hkv * ns * 16 * D, device=dev)
-        pml = torch.empty(T * Hkv * ns * 16 * 2, device=dev)
-        fn = lambda: ops.attn_decode(q, kc, vc, bt, cl, out, 1 / math.sqrt(D), po, pml, pps)  # noqa: E731
-        report("attn_decode", timeit(fn), T * ctx * Hkv * D * 2 * 2)
+        for pps in (16, 8, 4):  # pages per KV split: CTAs = T x Hkv x splits (16: the runner's default)
+            ns = (bt.shape[1] + pps - 1) // pps
+            po = torch.empty(T * Hkv * ns * 16 * D, device=dev)
+            pml = torch.empty(T * Hkv * ns * 16 * 2, device=dev)
+            fn = lambda: ops.attn_decode(q, kc, vc, bt, cl, out, 1 / math.sqrt(D), po, pml, pps)  # noqa: E731
+            report("attn_decode" if pps == 16 else f"attn_decode_pps{pps}", timeit(fn), T * ctx * Hkv * D * 2 * 2)
     if want("gemm_tc"):
         for M, N, K in ((8192, 9216, 4096), (8192, 4096, 8192)):
             w = Q4Weight.quantize(torch.randn(N, K, device=dev) * 0.02)
