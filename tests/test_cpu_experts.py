@@ -106,3 +106,27 @@ def test_rank_cpus_split_is_disjoint_and_balanced_share():
     # more CPU workers per rank -> a larger CPU share; bounded in (0, 1)
     s8, s2 = balanced_share(3, 8), balanced_share(15, 2)
     assert 0 < s8 < s2 < 1
+
+
+def test_isa_rates_and_calibrated_family():
+    """The host probe of the dot-product instructions and the family the pool uses: a SIMD
+    family whenever the host has one (the faster of BF16 and int16 VNNI)."""
+    r = ext().cpu_isa_rates(200000)
+    assert len(r) == 4 and all(x == -1.0 or x > 0 for x in r)
+    mode = ext().cpu_gemv_mode()
+    assert mode in (0, 1, 2) and (mode != 0 or not ext().cpu_simd_available())
+
+
+def test_cpu_pool_bench_runs(monkeypatch, capsys):
+    """The pool benchmark drives the mailbox end to end at Qwen3 layer size (two owned
+    experts, one layer) and prints one JSON line."""
+    import json
+    import sys
+
+    from syntropy_b200.bench import cpu_pool
+    monkeypatch.setattr(sys, "argv", ["cpu_pool", "--layers", "1", "--threads", "2", "--owned", "2",
+                                      "--repeats", "1"])
+    cpu_pool.main()
+    line = capsys.readouterr().out.strip().splitlines()[-1]
+    d = json.loads(line)
+    assert d["bench"] == "cpu_expert_pool" and d["threads"] == 2 and d["layer_ms"] > 0
