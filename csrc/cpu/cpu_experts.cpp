@@ -12,9 +12,9 @@
 //  * BF16: OR-ing 0x4300 into a nibble gives the bf16 number 128 + q exactly, so
 //    `vdpbf16ps` multiplies bf16 pairs exactly and
 //        sum_k (d q_k + m) x_k = d * sum_k (128 + q_k) x_k + (m - 128 d) * sum_k x_k;
-//  * VNNI (hosts with AVX-512 VNNI but no BF16): the activation's 32-column block is scaled to
-//    int16 (s = max|x| / 32767, rounding error at most s / 2 per element), `vpdpwssd` sums
-//    q * v exactly in int32, and y ~= d * s * sum_k q_k v_k + m * sum_k x_k (sum x exact).
+//  * VNNI int16: the activation row is scaled to int16 (s = max|x| / 32767, rounding error at
+//    most s / 2 per element), `vpdpwssd` sums q * v exactly in int32 per block, and
+//    y ~= s * sum_b d_b * sum_k q_k v_k + sum_b m_b * sum_k x_k (sum x exact).
 // Both agree with the f32 product to ~1e-5 relative.  Which one is faster depends on the host's
 // `vdpbf16ps` rate, so the default is the faster of the two, timed once per process
 // (`calibrate_mode`).
@@ -112,26 +112,24 @@ void pack_row(const uint16_t* x, int K, uint32_t* ab, float* sx4) {
   }
 }
 
-// Integer form of a row for the VNNI kernel: per 32-column block b, s_b = max|x| / 32767 and
-// v_k = round(x_k / s_b) as int16 (|x_k - s_b v_k| <= s_b / 2), packed in the same pair order
-// as `pack_row`; sxs holds, per 64-column group, s_b at the 16 dword lanes (block of lane i is
-// (i & 3) >> 1); sx4 the exact block sums of x as (s0, 0, s1, 0).
+// Integer form of a row for the VNNI kernel: one scale per row, s = max|x| / 32767, and
+// v_k = round(x_k / s) as int16 (|x_k - s v_k| <= s / 2: about 1e-4 of the row's largest
+// element, far below the bf16 rounding the GPU path applies to the same activations), packed
+// in the same pair order as `pack_row`; sxs holds s at every lane of every 64-column group (the
+// kernel applies it once per output); sx4 the exact block sums of x as (s0, 0, s1, 0).
 void pack_row_i16(const uint16_t* x, int K, uint32_t* ab, float* sxs, float* sx4) {
   const int KG = K >> 6;
+  float amax = 0.f;
+  for (int k = 0; k < K; ++k) amax = std::max(amax, std::fabs(bf2f_h(x[k])));
+  const float sc = amax > 0.f ? amax / 32767.f : 1.f, inv = 1.f / sc;
   for (int kg = 0; kg < KG; ++kg) {
-    float sc[2];
     int16_t v[64];
     for (int b = 0; b < 2; ++b) {
-      float amax = 0.f, sum = 0.f;
+      float sum = 0.f;
       for (int j = 0; j < 32; ++j) {
         const float f = bf2f_h(x[64 * kg + 32 * b + j]);
-        amax = std::max(amax, std::fabs(f));
         sum += f;
-      }
-      sc[b] = amax > 0.f ? amax / 32767.f : 1.f;
-      const float inv = 1.f / sc[b];
-      for (int j = 0; j < 32; ++j) {
-        const float q = std::nearbyint(bf2f_h(x[64 * kg + 32 * b + j]) * inv);
+        const float q = std::nearbyint(f * inv);
         v[32 * b + j] = (int16_t)std::max(-32767.f, std::min(32767.f, q));
       }
       sx4[kg * 4 + 2 * b] = sum;
@@ -142,7 +140,7 @@ void pack_row_i16(const uint16_t* x, int K, uint32_t* ab, float* sxs, float* sx4
       const int k = 32 * (w >> 1) + 16 * (w & 1) + 2 * t;
       ab[kg * 32 + i] = (uint32_t)(uint16_t)v[k] | ((uint32_t)(uint16_t)v[k + 1] << 16);
       ab[kg * 32 + 16 + i] = (uint32_t)(uint16_t)v[k + 8] | ((uint32_t)(uint16_t)v[k + 9] << 16);
-      sxs[kg * 16 + i] = sc[w >> 1];
+      sxs[kg * 16 + i] = sc;
     }
   }
 }
@@ -162,7 +160,8 @@ const int g_prefetch_groups = [] {
 }();
 
 // VNNI form of the product: nibble pairs as int16 (no magic number), activation pairs as int16,
-// vpdpwssd sums q * v exactly in int32 per block; then y += d * s * sum + m * sum(x).
+// vpdpwssd sums q * v exactly in int32 per block; y = s * sum_b d_b * sum(q v) + sum_b m_b * sum(x)
+// (s: the row's activation scale, applied once per output).
 template <int NR, int GB>
 __attribute__((target("avx512f,avx512bw,avx512vl,avx512vnni,f16c,fma"))) void tiles_vnni(
     const uint32_t* qw, const uint16_t* sm, int K, int tile0, int tile1, const uint32_t* const* ab,
@@ -203,11 +202,9 @@ __attribute__((target("avx512f,avx512bw,avx512vl,avx512vnni,f16c,fma"))) void ti
         for (int l = 0; l < GB; ++l)
           _mm_prefetch(reinterpret_cast<const char*>(wp + g_prefetch_groups * 128 + 16 * l), _MM_HINT_T0);
         __m512i xa[NR], xb[NR];
-        __m512 xs[NR];
         for (int r = 0; r < NR; ++r) {
           xa[r] = _mm512_loadu_si512(ab[r] + kg * 32);
           xb[r] = _mm512_loadu_si512(ab[r] + kg * 32 + 16);
-          xs[r] = _mm512_loadu_ps(sxs[r] + kg * 16);
         }
         const uint16_t* s = st + kg * 64;
 #pragma GCC unroll 8
@@ -226,8 +223,8 @@ __attribute__((target("avx512f,avx512bw,avx512vl,avx512vnni,f16c,fma"))) void ti
           for (int r = 0; r < NR; ++r) {
             const __m512i t = _mm512_dpwssd_epi32(_mm512_dpwssd_epi32(_mm512_setzero_si512(), v0, xa[r]), v2, xb[r]);
             const __m512i u = _mm512_dpwssd_epi32(_mm512_dpwssd_epi32(_mm512_setzero_si512(), v1, xa[r]), v3, xb[r]);
-            alo[gg][r] = _mm512_fmadd_ps(_mm512_cvtepi32_ps(t), _mm512_mul_ps(Dlo, xs[r]), alo[gg][r]);
-            ahi[gg][r] = _mm512_fmadd_ps(_mm512_cvtepi32_ps(u), _mm512_mul_ps(Dhi, xs[r]), ahi[gg][r]);
+            alo[gg][r] = _mm512_fmadd_ps(_mm512_cvtepi32_ps(t), Dlo, alo[gg][r]);
+            ahi[gg][r] = _mm512_fmadd_ps(_mm512_cvtepi32_ps(u), Dhi, ahi[gg][r]);
           }
         }
       }
@@ -236,8 +233,10 @@ __attribute__((target("avx512f,avx512bw,avx512vl,avx512vnni,f16c,fma"))) void ti
           const int g = g0 + gg;
           const float* clo = &cmin[r][16 * (g >> 2) + 4 * (g & 3)];
           const float* chi = &cmin[r][16 * ((g + 8) >> 2) + 4 * (g & 3)];
-          const float lo = _mm512_reduce_add_ps(alo[gg][r]) + clo[0] + clo[2];
-          const float hi = _mm512_reduce_add_ps(ahi[gg][r]) + chi[0] + chi[2];
+          // the row's activation scale, once per output (the same at every lane and group)
+          const float sr = sxs[r][0];
+          const float lo = _mm512_reduce_add_ps(alo[gg][r]) * sr + clo[0] + clo[2];
+          const float hi = _mm512_reduce_add_ps(ahi[gg][r]) * sr + chi[0] + chi[2];
           y[r][tile * 16 + g] = lo * scale[r];
           y[r][tile * 16 + g + 8] = hi * scale[r];
         }
