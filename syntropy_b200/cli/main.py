@@ -15,6 +15,11 @@ def _engine_from_config(cfg, device: str):
     from ..runtime.engine import LLMEngine
     from ..runtime.runner import ModelRunner
     dev = torch.device(device)
+    from .. import ops
+    if not cfg.feature("tcgen05_attention"):
+        ops.core._ATTN_TC[0] = "0"   # the mma.sync prefill attention kernel
+    if not cfg.feature("tcgen05_bf16_gemm"):
+        ops.core._BF16_TC[0] = "0"   # the library GEMM for bf16 weights
     sd = None
     if cfg.model.path and cfg.model.path.endswith(".gguf"):
         from ..models.hf import load_gguf  # a llama.cpp GGUF file (blocks dequantised, then requantised)
@@ -36,18 +41,18 @@ def _engine_from_config(cfg, device: str):
     if cfg.tier.expert_cache_frac < 1.0 and mcfg.is_moe and dev.type == "cuda":
         from ..experts.cache import ExpertCache
         cache = ExpertCache(mw.layers, cfg.tier.expert_cache_frac, dev)
-        if cfg.tier.expert_prefetch:
+        if cfg.tier.expert_prefetch and cfg.feature("expert_prefetch"):
             cache.enable_decode_prefetch(mcfg.n_experts)  # router-predicted prefetch of host experts
     kv_budget = cfg.tier.kv_budget or None
     runner = ModelRunner(mw, max_batch=cfg.sched.max_batch, max_seq_len=cfg.model.max_seq_len,
                          use_graphs=cfg.sched.cuda_graphs and cfg.feature("cuda_graph"), kv_budget_bytes=kv_budget)
     runner.expert_cache = cache
-    if cache is not None and cfg.tier.cpu_expert_share > 0:
+    if cache is not None and cfg.tier.cpu_expert_share > 0 and cfg.feature("cpu_tier"):
         from ..experts.cpu_tier import CpuExpertTier
         CpuExpertTier(cache, mcfg, max_rows=runner.max_batch, cpu_share=cfg.tier.cpu_expert_share,
                       threads=cfg.tier.cpu_threads or None, timeout_s=cfg.kernels.spin_timeout,
                       mode=cfg.kernels.cpu_gemv_mode)
-    spec = _spec_from_config(cfg, mcfg, runner, dev)
+    spec = _spec_from_config(cfg, mcfg, runner, dev) if cfg.feature("speculative") else None
     chunk = cfg.sched.chunk_tokens or None
     return LLMEngine(runner, max_prefill_tokens=cfg.sched.max_prefill_tokens, rebalance_every=cfg.tier.rebalance_every,
                      spec=spec, chunk_tokens=chunk if spec is None else None,

@@ -121,7 +121,14 @@ class DebugSection:
 
 @dataclass
 class FeaturesSection:
-    disable: list = field(default_factory=list)  # kill switches: "cuda_graph", "fused_collectives", ...
+    # kill switches, each falling back to a plainer path that stays correct: cuda_graph (eager
+    # decode steps), expert_prefetch (host experts read in place), cpu_tier (no host CPU experts),
+    # speculative (plain decode), tcgen05_attention (the mma.sync prefill attention kernel),
+    # tcgen05_bf16_gemm (the library GEMM for bf16 weights)
+    disable: list = field(default_factory=list)
+
+
+FEATURES = ("cuda_graph", "expert_prefetch", "cpu_tier", "speculative", "tcgen05_attention", "tcgen05_bf16_gemm")
 
 
 @dataclass
@@ -180,6 +187,9 @@ class Config:
             err("sched.max_batch", "must be >= 1")
         if self.sched.chunk_tokens < 0:
             err("sched.chunk_tokens", "must be >= 0")
+        unknown = [f for f in self.features.disable if f not in FEATURES]
+        if unknown:
+            err("features.disable", f"names unknown switches {unknown} (known: {', '.join(FEATURES)})")
         if self.spec.drafter not in ("none", "ngram", "mtp", "draft"):
             err("spec.drafter", "must be one of none, ngram, mtp, draft")
         if self.spec.drafter == "draft" and not self.spec.draft_model:

@@ -50,3 +50,16 @@ def test_cli_engine_spec_section():
     assert isinstance(eng.spec.drafter, DraftModelDrafter)
     assert eng.generate([[3, 4, 5, 6]], SamplingParams(max_tokens=10)) == want
     assert eng.acceptance_rate > 0.9  # the same model drafts for itself
+
+
+def test_feature_kill_switches():
+    """features.disable names switches from a closed set (a typo is an error, not a no-op);
+    disabling `speculative` serves without drafts even when spec.drafter asks for them."""
+    from syntropy_b200.cli.main import _engine_from_config
+    with pytest.raises(ValueError, match="unknown switches"):
+        load_config(env={}, overrides=["features.disable=cuda_graphs"])
+    base = ["model.name=tiny-llama", "model.max_seq_len=96", "sched.max_batch=4", "spec.drafter=ngram"]
+    cfg = load_config(env={}, overrides=base + ["features.disable=speculative,cuda_graph"])
+    assert not cfg.feature("speculative") and not cfg.feature("cuda_graph") and cfg.feature("cpu_tier")
+    eng, _ = _engine_from_config(cfg, "cpu")
+    assert eng.spec is None and not eng.runner.use_graphs
