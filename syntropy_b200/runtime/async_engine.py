@@ -112,6 +112,7 @@ class AsyncEngine:
                 self._subs.clear()
                 continue
             METRICS.histogram("step_us").record(int((time.perf_counter() - t0) * 1e6))
+            _engine_gauges(eng)
             for o in outs:
                 sub = self._subs.get(o.seq_id)
                 if sub is None:
@@ -132,3 +133,24 @@ class AsyncEngine:
                                                  logprobs=(s.logprobs if s and s.params.logprobs is not None
                                                            else None)))
                     self._subs.pop(o.seq_id, None)
+
+
+def _engine_gauges(eng):
+    """Engine state after a step, as gauges: queues, free KV pages, preemption and spill to host
+    memory / files, speculative acceptance and the expert cache's VRAM hit rate."""
+    st = eng.stats
+    METRICS.gauge("running_sequences", len(eng.running))
+    METRICS.gauge("waiting_sequences", len(eng.waiting))
+    METRICS.gauge("swapped_sequences", len(eng.swapped))
+    METRICS.gauge("kv_pages_free", eng.runner.kv.alloc.num_free)
+    METRICS.gauge("kv_swapped_out_total", st.get("swapped_out", 0))
+    store = getattr(eng, "kv_store", None)
+    if store is not None:
+        METRICS.gauge("kv_host_swap_bytes", store.host_bytes)
+        METRICS.gauge("kv_spill_file_bytes", store.disk_bytes)
+    if eng.spec is not None:
+        METRICS.gauge("spec_acceptance_rate", round(eng.acceptance_rate, 4))
+        METRICS.gauge("spec_paused_steps_total", st.get("spec_paused_steps", 0))
+    hr = getattr(eng.runner, "expert_hit_rate", None)
+    if hr is not None:
+        METRICS.gauge("expert_vram_hit_rate", round(hr, 4))

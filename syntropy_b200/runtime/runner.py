@@ -125,6 +125,7 @@ class ModelRunner:
             if cfg.n_experts else None
         self._layer_index = {id(L): i for i, L in enumerate(mw.layers)}
         self.expert_stats = None
+        self.expert_hit_rate = None  # VRAM hit rate of the last expert-cache rebalance window
 
     # ------------------------------------------------------------------ buffers
     def _alloc_buffers(self):
@@ -462,10 +463,19 @@ class ModelRunner:
         if self.ep is not None:
             import torch.distributed as dist
             dist.all_reduce(c, group=self.ep.ctx.group)
-        host = c.cpu()
+        host = c.to("cpu", copy=True)  # a copy also on CPU runners: the counters are zeroed next
         c.zero_()
+        hits = total = 0
         for li, L in enumerate(cache.layers):
-            self.expert_stats.observe(li, host[self._layer_index[id(L)]])
+            cnt = host[self._layer_index[id(L)]]
+            self.expert_stats.observe(li, cnt)
+            b = getattr(L, "expert_tier", None)
+            if b is not None:
+                resident = b.resident_mask()
+                hits += int(cnt[:b.E][resident].sum())
+                total += int(cnt[:b.E].sum())
+        # share of the window's routed pairs whose expert was in VRAM (before this rebalance)
+        self.expert_hit_rate = hits / total if total else None
         return cache.rebalance(self.expert_stats, max_swaps_per_layer)
 
     def _shared_expert(self, L, h, into=None):

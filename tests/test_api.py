@@ -83,6 +83,10 @@ def test_metrics_exposed(client):
     client.post("/v1/completions", json={"model": "tiny", "prompt": [1, 2, 3], "max_tokens": 2})
     m = client.get("/metrics").text
     assert "syntropy_requests_total" in m and "syntropy_generated_tokens_total" in m
+    # engine state after each step, as gauges
+    for g in ("running_sequences", "waiting_sequences", "kv_pages_free", "kv_swapped_out_total",
+              "kv_host_swap_bytes"):
+        assert f"# TYPE syntropy_{g} gauge" in m, g
 
 
 def test_constrained_requests(client):

@@ -66,3 +66,19 @@ def test_cpu_tier_split_and_detach():
         assert all(int(p) != 0 for p in gu.qw_ptrs) and all(int(p) != 0 for p in dn.sm_ptrs)
     finally:
         tier.close()
+
+
+def test_adapt_experts_reports_the_window_hit_rate():
+    """The runner's rebalance folds the window's routing counts into the scores and records the
+    share of routed pairs whose expert was in VRAM during that window."""
+    from syntropy_b200.runtime.runner import ModelRunner
+    g = torch.Generator().manual_seed(0)
+    E = 8
+    layer = SimpleNamespace(is_moe=True, experts_gu=_bank(E, g), experts_down=_bank(E, g))
+    cache = ExpertCache([layer], 0.5, torch.device("cpu"))
+    counts = torch.tensor([[5, 0, 9, 1, 8, 0, 0, 7]], dtype=torch.int32)  # residents: experts 0-3
+    fake = SimpleNamespace(expert_cache=cache, route_counts=counts.clone(), expert_stats=None, ep=None,
+                           cfg=SimpleNamespace(n_experts=E), _layer_index={id(layer): 0}, expert_hit_rate=None)
+    assert ModelRunner.adapt_experts(fake, max_swaps_per_layer=4) == 2
+    assert abs(fake.expert_hit_rate - 15 / 30) < 1e-9
+    assert int(fake.route_counts.sum()) == 0  # the window's counts were consumed
