@@ -471,9 +471,10 @@ class ModelRunner:
             self.expert_stats.observe(li, cnt)
             b = getattr(L, "expert_tier", None)
             if b is not None:
-                resident = b.resident_mask()
-                hits += int(cnt[:b.E][resident].sum())
-                total += int(cnt[:b.E].sum())
+                resident = b.resident_mask()  # this rank's experts e0 .. e0 + E
+                mine = cnt[b.e0: b.e0 + b.E]
+                hits += int(mine[resident].sum())
+                total += int(mine.sum())
         # share of the window's routed pairs whose expert was in VRAM (before this rebalance)
         self.expert_hit_rate = hits / total if total else None
         return cache.rebalance(self.expert_stats, max_swaps_per_layer)
