@@ -91,7 +91,11 @@ class SwapStore:
                       dtype=layers[0].dtype if layers else torch.bfloat16)
         self.host_bytes += n
         if not self._fits(0) and self.spill_dir is not None:
-            self._spill(e)
+            try:
+                self._spill(e)
+            except OSError:
+                self.host_bytes -= n  # nothing was stored: the caller keeps the pages
+                raise
         return e
 
     def take(self, e: SwapEntry) -> list:

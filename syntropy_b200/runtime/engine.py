@@ -254,11 +254,14 @@ class LLMEngine:
         """Preempt s: its KV pages go to host memory (or a spill file past the host budget) and
         back to the pool; it resumes later from exactly where it stopped (no recompute)."""
         layers = self._pack_kv(s)
+        # stored first: if the store fails (a spill file that cannot be written), the sequence
+        # keeps its pages and stays running
+        entry = self.kv_store.put(s.seq_id, layers)
         self.runner.kv.release(s.blocks)
         s.blocks = []
         s.status = "swapped"
         self.running.remove(s)
-        self.swapped.append((s, self.kv_store.put(s.seq_id, layers)))
+        self.swapped.append((s, entry))
         self.stats["swapped_out"] += 1
 
     def _swap_in(self) -> bool:

@@ -103,3 +103,28 @@ def test_swap_store_tiers_and_digest(tmp_path):
         st2.take(ec)
     st2.drop(ec)
     assert not list(tmp_path.glob("*.pack*"))
+
+
+def test_failed_spill_keeps_the_sequence_running(tmp_path, monkeypatch):
+    """A spill that cannot be written raises from the step, and the sequence it was preempting
+    still holds its pages and runs (nothing is lost)."""
+    from syntropy_b200.kv import tiers
+    cfg = get_config("tiny-llama")
+    mw = prepare_weights(cfg, torch.device("cpu"), seed=2)
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, cfg.vocab, (n,), generator=g).tolist() for n in (20, 14, 30, 9)]
+    eng = LLMEngine(ModelRunner(mw, max_batch=4, max_seq_len=128, num_blocks=9), kv_host_bytes=0,
+                    kv_spill_dir=str(tmp_path / "kv"))
+
+    def broken(*a, **k):
+        raise OSError(28, "No space left on device")
+    monkeypatch.setattr(tiers.SwapStore, "_spill", broken)
+    for p in prompts:
+        eng.add_request(p, SamplingParams(max_tokens=40))
+    with pytest.raises(OSError):
+        for _ in range(200):
+            if not eng.has_work():
+                break
+            eng.step()
+    assert not eng.swapped and eng.kv_store.host_bytes == 0
+    assert all(s.blocks for s in eng.running)  # every running sequence still holds its pages
