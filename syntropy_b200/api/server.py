@@ -8,7 +8,7 @@ import uuid
 from .. import __version__
 from ..obs.metrics import METRICS
 from ..runtime.engine import SamplingParams
-from ..text.chat import apply_chat_template
+from ..text.chat import apply_chat_template, chat_ids
 from ..text.tokenizer import IncrementalDecoder
 
 MAX_BODY = 32 << 20
@@ -25,11 +25,7 @@ def _chat(tokenizer):
 
 
 def _chat_ids(tokenizer, msgs, system=None) -> list[int]:
-    """Chat prompt ids; with span-aware encoding where the tokenizer has it (message content
-    cannot inject special tokens)."""
-    if hasattr(tokenizer, "encode_chat"):
-        return tokenizer.encode_chat(msgs, system)
-    return tokenizer.encode(_chat(tokenizer)(msgs, system=system) if system else _chat(tokenizer)(msgs))
+    return chat_ids(tokenizer, msgs, system)
 
 
 def _err(status: int, typ: str, msg: str):

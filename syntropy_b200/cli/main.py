@@ -136,6 +136,54 @@ def cmd_run(args, cfg):
     print(json.dumps({"tokens": out, "text": tok.decode(out)}))
 
 
+def cmd_chat(args, cfg):
+    """Interactive chat over the engine: each line typed is a user turn, the reply is generated
+    with the model's chat template and stop tokens and printed; the conversation is kept as
+    context.  `/exit` (or end of input) ends it, `/reset` starts a new conversation."""
+    from ..runtime.engine import SamplingParams
+    from ..text.chat import chat_ids
+    from ..text.tokenizer import load_tokenizer
+    eng, mcfg = _engine_from_config(cfg, args.device)
+    tok = load_tokenizer(cfg.model.path or None, mcfg.vocab)
+    eng.set_tokenizer(tok)
+    stop = tuple(getattr(tok, "stop_token_ids", ()) or ())
+    src = open(args.input) if args.input else sys.stdin
+    messages = []
+    try:
+        for line in src:
+            text = line.rstrip("\n")
+            if text == "/exit":
+                break
+            if text == "/reset":
+                messages = []
+                continue
+            if not text:
+                continue
+            messages.append({"role": "user", "content": text})
+            ids = chat_ids(tok, messages, args.system)
+            out = eng.generate([ids], SamplingParams(max_tokens=args.max_tokens, temperature=args.temperature,
+                                                     seed=args.seed, stop_token_ids=stop))[0]
+            reply = tok.decode([t for t in out if t not in stop])
+            messages.append({"role": "assistant", "content": reply})
+            print(json.dumps({"reply": reply, "tokens": len(out)}) if args.json else reply, flush=True)
+    finally:
+        if src is not sys.stdin:
+            src.close()
+
+
+def cmd_ls(args, cfg):
+    """Models in the local store (name, id, files, bytes); --verify re-checks every file's digest."""
+    from ..store.local import ModelStore
+    st = ModelStore(args.store)
+    for name in st.list():
+        e = st.index[name]
+        line = {"name": name, "model_id": e["model_id"], "files": len(e["files"]),
+                "bytes": sum(f["bytes"] for f in e["files"].values())}
+        if args.verify:
+            line["damaged"] = st.verify(name)
+        print(json.dumps(line))
+
+
 def cmd_serve(args, cfg):
     from ..daemon.bundle import install_crash_handler
     from ..obs.log import install as install_log_suppression
@@ -217,6 +265,17 @@ def main(argv=None):
     p.add_argument("--json", action="store_true", help="constrain the output to one JSON object")
     p.add_argument("--choices", default=None, help="constrain the output to one of these '|'-separated strings")
     p.add_argument("--device", default="cuda:0")
+    p = sub.add_parser("chat", help="interactive chat (one user turn per input line)")
+    p.add_argument("--system", default=None)
+    p.add_argument("--max-tokens", type=int, default=256)
+    p.add_argument("--temperature", type=float, default=0.7)
+    p.add_argument("--seed", type=int, default=None)
+    p.add_argument("--input", default=None, help="read the turns from this file instead of stdin")
+    p.add_argument("--json", action="store_true", help="print each reply as a JSON line")
+    p.add_argument("--device", default="cuda:0")
+    p = sub.add_parser("ls", help="models in the local store")
+    p.add_argument("--store", default=os.path.expanduser("~/.cache/syntropy_b200/store"))
+    p.add_argument("--verify", action="store_true", help="re-check every file's SHA-256")
     p = sub.add_parser("serve")
     p.add_argument("--device", default="cuda:0")
     p = sub.add_parser("probe")
@@ -237,7 +296,8 @@ def main(argv=None):
         raise SystemExit(netprobe_main(args.rest))
     from ..config import load_config
     cfg = load_config(args.config, overrides=args.set)
-    {"version": cmd_version, "config": cmd_config, "plan": cmd_plan, "run": cmd_run, "serve": cmd_serve,
+    {"version": cmd_version, "config": cmd_config, "plan": cmd_plan, "run": cmd_run, "chat": cmd_chat, "ls": cmd_ls,
+     "serve": cmd_serve,
      "probe": cmd_probe, "doctor": cmd_doctor, "bundle": cmd_bundle, "bench": cmd_bench}[args.cmd](args, cfg)
 
 
