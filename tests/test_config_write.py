@@ -35,11 +35,11 @@ def test_insert_key_and_section(tmp_path):
     assert out.splitlines()[4] == "seed = 7" and out.startswith(TEXT.split("\n# scheduling")[0])
     out = set_value(str(p), "tier.kv_budget", "8GiB")
     assert out.endswith('\n[tier]\nkv_budget = "8GiB"\n')
-    out = set_value(str(p), "features.disable", "cuda_graph,fused_collectives")
-    assert 'disable = ["cuda_graph", "fused_collectives"]' in out
+    out = set_value(str(p), "features.disable", "cuda_graph,expert_prefetch")
+    assert 'disable = ["cuda_graph", "expert_prefetch"]' in out
     cfg = load_config(str(p), env={})
     assert cfg.model.seed == 7 and cfg.tier.kv_budget == 8 << 30 and cfg.features.disable == ["cuda_graph",
-                                                                                               "fused_collectives"]
+                                                                                               "expert_prefetch"]
     new = tmp_path / "new.toml"
     set_value(str(new), "sched.cuda_graphs", "off")
     assert new.read_text() == "[sched]\ncuda_graphs = false\n"
