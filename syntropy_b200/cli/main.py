@@ -184,6 +184,48 @@ def cmd_ls(args, cfg):
         print(json.dumps(line))
 
 
+def runner_table(shm_dir: str = "/dev/shm") -> list[dict]:
+    """Runner processes on this host, from the shared-memory status regions their daemons
+    created (`/syn-runner-<daemon pid>-<id>`): pid, lifecycle state, seconds since the last
+    heartbeat, step counter, pending work, error code, and whether the pid is alive."""
+    import time
+
+    from .._ext import ext
+    from ..net.ipc import HEADER_BYTES, StatusHeader
+    rows = []
+    try:
+        names = sorted(n for n in os.listdir(shm_dir) if n.startswith("syn-runner-"))
+    except OSError:
+        return rows
+    now = time.monotonic_ns()
+    for n in names:
+        try:
+            reg = ext().ShmRegion("/" + n, HEADER_BYTES, False)
+        except RuntimeError:
+            continue  # gone since the listing, or not ours to read
+        h = StatusHeader(reg.address())
+        if not h.valid():
+            continue
+        pid = h.pid
+        try:
+            os.kill(pid, 0)
+            alive = pid > 0
+        except OSError:
+            alive = False
+        hb = h.heartbeat_ns
+        rows.append({"region": "/" + n, "daemon_pid": int(n.split("-")[2]), "pid": pid, "state": h.state,
+                     "heartbeat_age_s": round((now - hb) / 1e9, 3) if hb else None, "step": h.step,
+                     "pending": h.pending, "error": h.error, "alive": alive})
+        del h, reg
+    return rows
+
+
+def cmd_ps(args, cfg):
+    """Runner processes on this host (one JSON line each)."""
+    for r in runner_table():
+        print(json.dumps(r))
+
+
 def cmd_serve(args, cfg):
     from ..daemon.bundle import install_crash_handler
     from ..obs.log import install as install_log_suppression
@@ -273,6 +315,7 @@ def main(argv=None):
     p.add_argument("--input", default=None, help="read the turns from this file instead of stdin")
     p.add_argument("--json", action="store_true", help="print each reply as a JSON line")
     p.add_argument("--device", default="cuda:0")
+    sub.add_parser("ps", help="runner processes on this host (from their shared-memory status headers)")
     p = sub.add_parser("ls", help="models in the local store")
     p.add_argument("--store", default=os.path.expanduser("~/.cache/syntropy_b200/store"))
     p.add_argument("--verify", action="store_true", help="re-check every file's SHA-256")
@@ -296,7 +339,7 @@ def main(argv=None):
         raise SystemExit(netprobe_main(args.rest))
     from ..config import load_config
     cfg = load_config(args.config, overrides=args.set)
-    {"version": cmd_version, "config": cmd_config, "plan": cmd_plan, "run": cmd_run, "chat": cmd_chat, "ls": cmd_ls,
+    {"version": cmd_version, "config": cmd_config, "plan": cmd_plan, "run": cmd_run, "chat": cmd_chat, "ls": cmd_ls, "ps": cmd_ps,
      "serve": cmd_serve,
      "probe": cmd_probe, "doctor": cmd_doctor, "bundle": cmd_bundle, "bench": cmd_bench}[args.cmd](args, cfg)
 

@@ -90,6 +90,9 @@ class RunnerHost:
             except subprocess.TimeoutExpired:
                 self._kill()
         self._close()
+        # the status region goes with the instance (its owner unlinks it): the header view first
+        self.hdr = None
+        self.region = None
 
     # ------------------------------------------------------------------ supervision
     def poll(self) -> str | None:

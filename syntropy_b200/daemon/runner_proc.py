@@ -54,6 +54,7 @@ def serve(fd: int, region: str) -> int:
         return 2
     shm = ext().ShmRegion(region, int(init.get("region_bytes", HEADER_BYTES)), False)
     hdr = StatusHeader(shm.address())
+    hdr.set_pid(os.getpid())  # the header names its runner (read by `ps` and by the daemon)
     stop_beats = threading.Event()
     done = threading.Event()
     period = float(init.get("heartbeat_ms", 100)) / 1e3

@@ -124,6 +124,9 @@ class StatusHeader:
         return self._u32(OFF_MAGIC).value == MAGIC and self._u32(OFF_PROTOCOL).value == PROTOCOL
 
     # runner side
+    def set_pid(self, pid: int):
+        self._u32(OFF_PID).value = pid
+
     def beat(self):
         self._u64(OFF_HEARTBEAT).value = time.monotonic_ns()
 

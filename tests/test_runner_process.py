@@ -105,3 +105,21 @@ def test_runner_exits_when_the_daemon_goes_away():
     assert proc.returncode == 0
     host.proc = None
     host.stop()
+
+
+def test_ps_lists_the_runner():
+    """`ps` reads each runner's shared-memory status header: the spawned runner appears with
+    its pid, state and heartbeat; after the daemon side stops it, its region is gone."""
+    from syntropy_b200.cli.main import runner_table
+    sup = SupervisorConfig(liveness_timeout_s=2.0, backoff_initial_s=0.05, backoff_max_s=0.2, restart_budget=3)
+    host = RunnerHost(INIT, sup)
+    host.start()
+    try:
+        _pump(host, lambda a: host.sup.state == RunnerHealth.HEALTHY)
+        rows = [r for r in runner_table() if r["pid"] == host.pid]
+        assert len(rows) == 1 and rows[0]["state"] == "ready" and rows[0]["alive"]
+        assert rows[0]["daemon_pid"] == os.getpid() and rows[0]["heartbeat_age_s"] < 2.0
+        region = rows[0]["region"]
+    finally:
+        host.stop()
+    assert all(r["region"] != region for r in runner_table())
