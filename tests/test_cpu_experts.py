@@ -130,3 +130,17 @@ def test_cpu_pool_bench_runs(monkeypatch, capsys):
     line = capsys.readouterr().out.strip().splitlines()[-1]
     d = json.loads(line)
     assert d["bench"] == "cpu_expert_pool" and d["threads"] == 2 and d["layer_ms"] > 0
+
+
+def test_balanced_share_tiers():
+    """The CPU share of the host tier balances the pool's rate (per kernel family) against the
+    link: one rank alone, 2-4 ranks with the pools capped by shared DRAM, 8 ranks with GPU pairs
+    sharing a host link (measured balances: 0.7 on one GPU with 14 int16 workers, ~0.5 at EP2
+    with 11 workers)."""
+    from syntropy_b200.experts.cpu_tier import balanced_share
+    assert balanced_share(14, 1, mode=2) == 0.7
+    assert balanced_share(14, 1, mode=1) == 0.6            # the BF16 family is slower per worker
+    assert abs(balanced_share(11, 2, mode=2) - 0.51) < 0.01  # DRAM cap, not 11 x 7.5 GB/s
+    assert balanced_share(7, 4, mode=2) == balanced_share(7, 2, mode=2)
+    assert balanced_share(7, 8, mode=2) > balanced_share(7, 4, mode=2)  # paired links: more to the CPU
+    assert 0 < balanced_share(1, 8, mode=2) < balanced_share(15, 1, mode=2) < 1
