@@ -18,6 +18,7 @@ from .. import ops
 from ..formats.q4 import Q4Weight
 from ..kv.paged import PagedKVCache
 from ..models.transformer import ModelWeights
+from ..obs.nvtx import nvtx_ranged
 
 BUCKETS = (1, 2, 4, 8, 16, 32, 48, 64, 96, 128, 192, 256)  # rows past 64: verify windows of drafts
 
@@ -531,6 +532,7 @@ class ModelRunner:
             self._shared_expert(L, h, into=x)
         ops.rms_norm(x, nw, cfg.rms_eps, out=h)
 
+    @nvtx_ranged("syn.decode")
     def decode(self, B: int):
         """Run one decode step for the first B rows (descriptor already filled on the host).
         With `profile_next` set, this step replays the profiled graph variant, which also
@@ -656,6 +658,7 @@ class ModelRunner:
     pp_prefill_groups = 2  # pipeline parallelism: sequence groups handed between stages per prefill
 
     @torch.no_grad()
+    @nvtx_ranged("syn.prefill")
     def prefill(self, tokens: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor, cu_seqlens: list[int],
                 prefix: list | None = None, block_lists: list | None = None):
         """Eager prefill of freshly started sequences (or of chunks after a cached prefix).

@@ -66,3 +66,26 @@ def test_repeat_suppression():
     finally:
         lg.removeHandler(h)
     assert seen == ["queue full", "drained (previous message repeated 49 times)"]
+
+
+def test_nvtx_ranges_are_opt_in():
+    """SYN_NVTX off: the decorator hands back the function itself; on: a wrapper that still
+    returns the function's result (on a host without CUDA it only calls through)."""
+    import importlib
+
+    from syntropy_b200.obs import nvtx
+    f = lambda x: x + 1  # noqa: E731
+    assert nvtx.nvtx_ranged("a")(f) is f or nvtx.ENABLED
+    import os
+    old = os.environ.get("SYN_NVTX")
+    os.environ["SYN_NVTX"] = "1"
+    try:
+        mod = importlib.reload(nvtx)
+        g = mod.nvtx_ranged("a")(f)
+        assert g is not f and g(2) == 3
+    finally:
+        if old is None:
+            del os.environ["SYN_NVTX"]
+        else:
+            os.environ["SYN_NVTX"] = old
+        importlib.reload(nvtx)
